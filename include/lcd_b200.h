@@ -1,0 +1,239 @@
+/*
+ * lcd_b200 -- C ABI of the B200 (sm_100a) dependence-DAG kernels.
+ *
+ * Every entry point is extern "C", takes raw device pointers, sizes and a CUDA
+ * stream handle (cudaStream_t passed as void*), allocates no device memory and
+ * returns an LCD_* code (0 = success).  Index arrays are int32, values are
+ * float64.  Functions whose last parameter is `int *status_host` enqueue their
+ * work on `stream`; when `status_host` is non-NULL they also synchronise the
+ * stream and report the device-side status there (and as the return value),
+ * when it is NULL they return right after enqueueing and the caller reads the
+ * status later with lcd_read_status().
+ *
+ * Each declaration names the part of the reference (SwiftWare-Lab/lcd, paths
+ * inside that project) whose work it replaces.
+ */
+#ifndef LCD_B200_H
+#define LCD_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return / status codes -------------------------------------------- */
+enum {
+    LCD_OK = 0,
+    LCD_ERR_INVALID_ARGUMENT = 1,
+    LCD_ERR_CUDA = 2,             /* a CUDA runtime call failed (see lcd_last_cuda_error) */
+    LCD_ERR_WORKSPACE = 3,        /* caller-provided workspace too small */
+    LCD_ERR_TIMEOUT = 4,          /* a bounded device wait expired: dependency never satisfied */
+    LCD_ERR_UNSORTED = 5,         /* a segment violates the sorted-segment property */
+    LCD_ERR_BAD_POINTERS = 6,     /* pointer array not monotone / out of range */
+    LCD_ERR_INDEX_RANGE = 7,      /* an index lies outside [0, n) or on the wrong side of the diagonal */
+    LCD_ERR_CYCLE = 8,            /* the dependence graph is not acyclic */
+    LCD_ERR_MISSING_DIAGONAL = 9, /* a row needs a diagonal entry that is not stored */
+    LCD_ERR_TOO_LARGE = 10        /* a size exceeds a documented limit */
+};
+
+/* Operators: which edge rule the inspector applies.  The numbering is shared by
+ * the DAG build and the solvers.  Upper-triangular operators use reversed node
+ * ids v = n-1-i, i.e. "upper = lower on the index-reversed matrix". */
+enum {
+    LCD_OP_CSR_LOWER = 0, /* rows, diagonal last   (compiler/demo/sptrsv.py:26-34)  */
+    LCD_OP_CSC_LOWER = 1, /* cols, diagonal first  (compiler/demo/sptrsv.py:37-43)  */
+    LCD_OP_ILU0_CSR = 2,  /* full rows, sorted     (compiler/demo/spilu0.py:21-47)  */
+    LCD_OP_CSR_UPPER = 3, /* rows, diagonal first, visited last to first            */
+    LCD_OP_CSC_UPPER = 4  /* cols, diagonal last,  visited last to first            */
+};
+
+/* Flags of the CSR solvers. */
+enum {
+    LCD_SOLVE_UPPER = 1,      /* backward substitution (rows n-1 .. 0) */
+    LCD_SOLVE_UNIT_DIAG = 2,  /* implicit unit diagonal, no division (needs OF_FULL) */
+    LCD_SOLVE_OF_FULL = 4,    /* the triangle is the part of a full sorted CSR row before
+                                 (lower) / after (upper) diag_pos[row]; used on ILU0 factors */
+    LCD_SOLVE_EXACT = 8       /* one lane per row, unfused multiply/subtract in storage order
+                                 and a true division: bit-identical to the sequential loop */
+};
+
+/* Device-side status block every solver uses: 8 int32 words in device memory,
+ * owned by the caller, zeroed by the entry point before the launch.
+ * word 0: LCD_* code (also read as "abort" by all waiting threads),
+ * word 1: node / row at which the error was detected, word 2: ticket counter. */
+#define LCD_STATUS_WORDS 8
+
+const char *lcd_error_string(int code);
+const char *lcd_last_cuda_error(void);
+int lcd_version(void);
+
+/* Reads status word 0 after synchronising `stream`; *node gets word 1. */
+int lcd_read_status(const int32_t *status_dev, void *stream, int32_t *node);
+
+/* ---- DAG build ---------------------------------------------------------- */
+/*
+ * Replaces the generated Python inspector `extract_dag` (compiler/dag_codegen.py:
+ * 1164-1196 edge rule, :1391-1402 edge multiplicity, :1421-1482 dep_count) and
+ * compiler/dag_preprocessing.py:115-143 (compact_successors), :146-163
+ * (wavefronts_from_dag) and :166-204 (preprocess_wavefront).  All outputs are
+ * element-wise identical to those functions' outputs.
+ *
+ *   dep_count[n]      distinct predecessors of each node
+ *   edge_count[n]     predecessors counted with repetition (push protocol)
+ *   dag_ptr[n+1], dag_index[>= edge capacity]  successors, ascending and distinct
+ *   level[n]          level(v) = 0 without predecessors, else 1 + max over predecessors
+ *   wavefronts[n]     nodes ordered by (level, node id)
+ *   wavefront_ptr[n+1]   first n_levels+1 entries are valid
+ *
+ * lcd_dag_workspace_bytes gives the scratch size for a matrix with `nnz` stored
+ * entries.  The call synchronises `stream` (sizes are read back between phases).
+ * `timeout_ms` bounds the level propagation's device-side waits (0 = default).
+ */
+int lcd_dag_workspace_bytes(int op, int32_t n, int64_t nnz, int64_t *bytes);
+int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_t *idx, int64_t nnz,
+                  int32_t *dep_count, int32_t *edge_count, int32_t *dag_ptr,
+                  int32_t *dag_index, int64_t *n_edges_host, int32_t *level,
+                  int32_t *wavefronts, int32_t *wavefront_ptr, int32_t *n_levels_host,
+                  void *workspace, int64_t workspace_bytes, int32_t timeout_ms,
+                  void *stream);
+
+/*
+ * Diagonal-position table: pos[s] = first p in [ptr[s], ptr[s+1]) with idx[p] == s,
+ * else -1.  Replaces compiler/structural_lookups.py:279-333 (_materialize_lookup)
+ * including its validation: returns LCD_ERR_BAD_POINTERS / LCD_ERR_UNSORTED where
+ * that function raises StructuralLookupError.  `status_dev`: LCD_STATUS_WORDS ints.
+ */
+int lcd_diag_positions(int32_t n, const int32_t *ptr, const int32_t *idx, int64_t nnz,
+                       int32_t *pos, int32_t *status_dev, void *stream, int *status_host);
+
+/* ---- sync-free SpTRSV ----------------------------------------------------- */
+/*
+ * CSR triangular solve with one dependency hand-off per operand and no counters:
+ * x is pre-filled with a reserved NaN pattern, a consumer polls the operand
+ * itself.  Replaces the generated sync-free kernels and launchers of
+ * compiler/cuda_lowering.py (:519-541 plain, :1343-1410 warp/counter, :1362-1370
+ * pull; launchers :673-735, :1070-1119) for the SpTRSV-CSR loop nest.
+ *
+ *   flags            LCD_SOLVE_* bits
+ *   diag_pos         needed with LCD_SOLVE_OF_FULL, else NULL
+ *   lanes_per_row    1,2,4,8,16,32 (0 = choose from nnz/n)
+ *   threads_per_block  256, 512 or 1024 (0 = 1024); a block owns threads/lanes rows
+ *   nnz              number of stored entries (bounds the pointer checks)
+ *   x                n doubles, overwritten (must not alias b)
+ *   timeout_ms       bound of every device wait (0 = default 4000)
+ */
+int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, const double *Ax,
+                            const int32_t *diag_pos, const double *b, double *x, int flags,
+                            int lanes_per_row, int threads_per_block, int32_t *status_dev,
+                            int32_t timeout_ms, void *stream, int *status_host);
+
+/*
+ * Multi-RHS variant: B and X are row-major n x nrhs blocks (leading dimension
+ * ld >= nrhs, in doubles); lanes run over right-hand sides.
+ * lcd_transpose_f64 converts between column-major and row-major blocks.
+ */
+int lcd_sptrsv_csr_syncfree_multi(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap, const int32_t *Ai,
+                                  const double *Ax, const int32_t *diag_pos, const double *B,
+                                  double *X, int64_t ld, int flags, int32_t *status_dev,
+                                  int32_t timeout_ms, void *stream, int *status_host);
+int lcd_transpose_f64(int64_t rows, int64_t cols, const double *in, int64_t ld_in, double *out,
+                      int64_t ld_out, void *stream);
+
+/*
+ * CSC triangular solve, push protocol: a column waits until its counter of
+ * pending contributions reaches zero, then scatters.  `dep_count` must hold the
+ * edge multiplicities (edge_count of lcd_dag_build, or lcd_csc_edge_count) and
+ * is consumed by the solve.  x doubles as the accumulator and is zeroed by the
+ * call.  Replaces the push-protocol kernel of compiler/cuda_lowering.py:2031-2059.
+ * flags: LCD_SOLVE_UPPER only.
+ */
+int lcd_sptrsv_csc_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, const double *Ax,
+                            const double *b, double *x, int32_t *dep_count, int flags,
+                            int lanes_per_col, int32_t *status_dev, int32_t timeout_ms,
+                            void *stream, int *status_host);
+int lcd_csc_edge_count(int32_t n, const int32_t *Ap, const int32_t *Ai, int flags,
+                       int32_t *edge_count, void *stream);
+
+/* ---- wavefront SpTRSV ------------------------------------------------------- */
+/*
+ * Level-by-level solve over `wavefronts` / `wavefront_ptr` (device arrays as built
+ * by lcd_dag_build).  mode 0: one launch per level on `stream`; mode 1: a single
+ * cooperative launch with a grid-wide barrier between levels, runs of levels that
+ * fit one thread block being handled by one block with block-level barriers.
+ * Replaces the generated wavefront kernels and launchers of
+ * compiler/cuda_lowering.py:1233-1291, :855-1016 (CSR and CSC loop nests).
+ * op: LCD_OP_CSR_LOWER / CSR_UPPER / CSC_LOWER / CSC_UPPER.  For CSC x is zeroed
+ * by the call and accumulates with atomics.
+ */
+enum { LCD_WAVEFRONT_PER_LEVEL = 0, LCD_WAVEFRONT_COOPERATIVE = 1 };
+int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                         const double *Ax, const int32_t *diag_pos, const double *b, double *x,
+                         int flags, const int32_t *wavefronts, const int32_t *wavefront_ptr_dev,
+                         const int32_t *wavefront_ptr_host, int32_t n_levels, int mode,
+                         int lanes_per_row, int32_t *status_dev, int32_t timeout_ms, void *stream,
+                         int *status_host);
+
+/* ---- SpILU0 (CSR, in place) -------------------------------------------------- */
+/*
+ * In-place ILU(0) of a CSR matrix with sorted rows; arithmetic identical to the
+ * sequential loop nest of compiler/demo/spilu0.py:21-47 (pivots in ascending
+ * order, unfused multiply/subtract).  Replaces the nested-thread-map kernel of
+ * compiler/cuda_lowering.py:1572-1989.  mode: 0 = sync-free (per-row done flags in
+ * `done`, n ints, zeroed by the call), 1 = per-level launches over wavefronts.
+ */
+int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, double *Ax,
+                   const int32_t *diag_pos, int mode, int32_t *done,
+                   const int32_t *wavefronts, const int32_t *wavefront_ptr_host,
+                   int32_t n_levels, int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
+                   void *stream, int *status_host);
+
+/* ---- supernodal SpTRSV ------------------------------------------------------- */
+/*
+ * Lower-triangular solve on the supernodal layout of
+ * utils/symbolic_cholesky_csc.py:950-1021 (column-major panels, own columns
+ * first in each row list), in place on x (x holds b on entry).  Replaces
+ * benchmark/sptrsv_supernodal.py:12-28 / :55-94 and the dense helpers
+ * utils/dense_blas.py:19-33, :228-242.  Lp is 64-bit.
+ *   pending[n_super]  number of panel-row updates each supernode still waits for
+ *                     (lcd_supernodal_pending computes it; consumed by the solve)
+ */
+int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const int32_t *Lip,
+                           const int32_t *Li, const int32_t *col_to_super, int32_t *pending,
+                           void *stream);
+/*
+ * Tasks: the solve is cut into tasks listed in supernode order; task t works on
+ * supernode task_super[t]; task_strip[t] == 0 solves the diagonal block and then,
+ * like every other strip, multiplies lcd_supernodal_strip_rows() rows of the
+ * off-diagonal panel starting at row task_strip[t] * strip_rows.  Every supernode
+ * needs its strip-0 task even when it has no off-diagonal rows.
+ *   solved[n_super]   scratch flags (zeroed by the call)
+ *   supernode widths are limited to 1024 columns (LCD_ERR_TOO_LARGE)
+ */
+int lcd_supernodal_strip_rows(void);
+int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
+                          const int32_t *task_super, const int32_t *task_strip,
+                          const int32_t *sn, const int32_t *Lip, const int32_t *Li,
+                          const int64_t *Lp, const double *Lx, const int32_t *col_to_super,
+                          int32_t *pending, int32_t *solved, double *x, int32_t *status_dev,
+                          int32_t timeout_ms, void *stream, int *status_host);
+
+/* Scheduling knobs of the one-lane-per-row sync-free kernel (process-wide).  They
+ * change waiting behaviour only, never results.  The reference's counterpart is the
+ * schedule search of compiler/scheduler.py:172-303 (block size / unroll / protocol). */
+enum {
+    LCD_TUNE_SLEEP_LOCAL_NS = 0,  /* pause after a failed poll inside the own chunk */
+    LCD_TUNE_SLEEP_GLOBAL_NS = 1, /* pause after a failed poll of another chunk's row */
+    LCD_TUNE_GAP_NS = 2,          /* extra pause per row the producer's warp still owes */
+    LCD_TUNE_ROW_VARIANT = 3      /* 0: thread-per-row kernel, 1: generic lane-group kernel */
+};
+int lcd_set_tuning(int key, int value);
+
+/* ---- small device utilities used by the host layer ---------------------------- */
+int lcd_fill_u64(uint64_t *dst, int64_t count, uint64_t value, void *stream);
+int lcd_device_sm_count(int *sm_count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LCD_B200_H */

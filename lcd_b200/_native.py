@@ -1,0 +1,113 @@
+"""ctypes binding of ``liblcd_b200.so`` (the C ABI declared in ``include/lcd_b200.h``).
+
+There is no CPU fallback: if the CUDA library has not been built, or a call
+returns a non-zero code, this module raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_double, c_int, c_int32, c_int64, c_uint64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblcd_b200.so")
+
+# LCD_* codes of include/lcd_b200.h
+OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
+    ERR_BAD_POINTERS, ERR_INDEX_RANGE, ERR_CYCLE, ERR_MISSING_DIAGONAL, ERR_TOO_LARGE = range(11)
+OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER = range(5)
+SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
+WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
+STATUS_WORDS = 8
+TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT = range(4)
+
+
+class NativeLibraryMissing(RuntimeError):
+    """The CUDA library is not built; there is no other implementation."""
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned a non-zero LCD_* code."""
+
+    def __init__(self, code, where, detail=""):
+        self.code = int(code)
+        self.where = where
+        super().__init__(f"{where}: LCD error {code} ({detail})")
+
+
+_P = c_void_p
+_SIGNATURES = {
+    # name: (restype, argtypes)
+    "lcd_error_string": (ctypes.c_char_p, [c_int]),
+    "lcd_last_cuda_error": (ctypes.c_char_p, []),
+    "lcd_version": (c_int, []),
+    "lcd_read_status": (c_int, [_P, _P, ctypes.POINTER(c_int32)]),
+    "lcd_dag_workspace_bytes": (c_int, [c_int, c_int32, c_int64, ctypes.POINTER(c_int64)]),
+    "lcd_dag_build": (c_int, [c_int, c_int32, _P, _P, c_int64, _P, _P, _P, _P,
+                              ctypes.POINTER(c_int64), _P, _P, _P, ctypes.POINTER(c_int32),
+                              _P, c_int64, c_int32, _P]),
+    "lcd_diag_positions": (c_int, [c_int32, _P, _P, c_int64, _P, _P, _P, ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_csr_syncfree": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, c_int,
+                                        c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_csr_syncfree_multi": (c_int, [c_int32, c_int64, c_int32, _P, _P, _P, _P, _P, _P,
+                                              c_int64, c_int, _P, c_int32, _P,
+                                              ctypes.POINTER(c_int)]),
+    "lcd_transpose_f64": (c_int, [c_int64, c_int64, _P, c_int64, _P, c_int64, _P]),
+    "lcd_sptrsv_csc_syncfree": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, c_int,
+                                        _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_csc_edge_count": (c_int, [c_int32, _P, _P, c_int, _P, _P]),
+    "lcd_sptrsv_wavefront": (c_int, [c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P,
+                                     _P, _P, c_int32, c_int, c_int, _P, c_int32, _P,
+                                     ctypes.POINTER(c_int)]),
+    "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
+                               c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_supernodal_pending": (c_int, [c_int32, _P, _P, _P, _P, _P, _P]),
+    "lcd_supernodal_strip_rows": (c_int, []),
+    "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
+                                      _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_set_tuning": (c_int, [c_int, c_int]),
+    "lcd_fill_u64": (c_int, [_P, c_int64, c_uint64, _P]),
+    "lcd_device_sm_count": (c_int, [ctypes.POINTER(c_int)]),
+}
+EXPORTED_SYMBOLS = tuple(_SIGNATURES)
+
+_lib = None
+
+
+def load():
+    """Load the shared library (once) and attach the prototypes."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise NativeLibraryMissing(
+            f"{LIB_PATH} is missing. Build it with `python -m lcd_b200.build` "
+            "(needs nvcc); lcd_b200 has no CPU or interpreter fallback.")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def error_string(code):
+    return load().lcd_error_string(int(code)).decode()
+
+
+def check(code, where):
+    """Raise NativeError for a non-zero return code."""
+    if code != OK:
+        detail = error_string(code)
+        if code == ERR_CUDA:
+            detail += ": " + load().lcd_last_cuda_error().decode()
+        raise NativeError(code, where, detail)
+
+
+def ptr(tensor):
+    """Device address of a torch tensor (or None)."""
+    if tensor is None:
+        return None
+    return c_void_p(tensor.data_ptr())

@@ -1,0 +1,81 @@
+// Host-side helpers shared by every entry point: error text, status block I/O.
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace lcd {
+
+static thread_local char g_cuda_error[512] = "";
+
+void set_cuda_error(cudaError_t e, const char *where) {
+    snprintf(g_cuda_error, sizeof g_cuda_error, "%s: %s (%s)", cudaGetErrorName(e),
+             cudaGetErrorString(e), where);
+}
+
+int reset_status(int32_t *status_dev, cudaStream_t stream) {
+    LCD_CUDA_TRY(cudaMemsetAsync(status_dev, 0, LCD_STATUS_WORDS * sizeof(int32_t), stream));
+    return LCD_OK;
+}
+
+int finish(int32_t *status_dev, cudaStream_t stream, int *status_host) {
+    if (!status_host) return LCD_OK;
+    int32_t node = -1;
+    const int rc = lcd_read_status(status_dev, stream, &node);
+    *status_host = rc;
+    return rc;
+}
+
+int sm_count() {
+    static int cached = 0;
+    if (!cached) {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+            cached = sms;
+        else
+            return 148;
+    }
+    return cached;
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" const char *lcd_error_string(int code) {
+    switch (code) {
+        case LCD_OK: return "success";
+        case LCD_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case LCD_ERR_CUDA: return "CUDA runtime error";
+        case LCD_ERR_WORKSPACE: return "workspace too small";
+        case LCD_ERR_TIMEOUT: return "a bounded device wait expired (dependency never satisfied)";
+        case LCD_ERR_UNSORTED: return "segment violates the sorted-segment property";
+        case LCD_ERR_BAD_POINTERS: return "pointer array is not monotone or out of range";
+        case LCD_ERR_INDEX_RANGE: return "index out of range or on the wrong side of the diagonal";
+        case LCD_ERR_CYCLE: return "dependence graph is not acyclic";
+        case LCD_ERR_MISSING_DIAGONAL: return "a required diagonal entry is not stored";
+        case LCD_ERR_TOO_LARGE: return "size exceeds a documented limit";
+        default: return "unknown lcd_b200 error";
+    }
+}
+
+extern "C" const char *lcd_last_cuda_error(void) { return g_cuda_error; }
+
+extern "C" int lcd_version(void) { return 100; }
+
+extern "C" int lcd_read_status(const int32_t *status_dev, void *stream, int32_t *node) {
+    if (!status_dev) return LCD_ERR_INVALID_ARGUMENT;
+    int32_t words[2] = {0, -1};
+    cudaStream_t st = (cudaStream_t)stream;
+    LCD_CUDA_TRY(cudaMemcpyAsync(words, status_dev, sizeof words, cudaMemcpyDeviceToHost, st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    if (node) *node = words[1];
+    return words[0];
+}
+
+extern "C" int lcd_device_sm_count(int *count) {
+    if (!count) return LCD_ERR_INVALID_ARGUMENT;
+    *count = sm_count();
+    return LCD_OK;
+}

@@ -1,0 +1,583 @@
+// On-device construction of the dependence DAG and its level sets (sm_100a).
+//
+// Output arrays are element-wise identical to what the reference's generated
+// inspector plus dag_preprocessing produce:
+//   1. every node counts and then emits the edge instances of its segment in
+//      the order the inspector visits them                    (count / scan / emit)
+//   2. edges are brought into (source, destination) order by stable LSD radix
+//      passes over 8-bit digits                               (sort)
+//   3. repeated edges are dropped, successors compacted       (flag / scan / compact)
+//   4. the distinct edges are regrouped by destination        (sort) and levels are
+//      propagated with a pull scheme that polls the predecessor's level word
+//      itself (-1 = not known yet), own-chunk levels mirrored in shared memory
+//   5. nodes are ordered by (level, id) with stable radix passes on the level.
+// All primitives (scan, radix pass) are written here; nothing is allocated.
+#include "common.cuh"
+
+namespace lcd {
+
+// ---------------------------------------------------------------- scan ----
+constexpr int kScanThreads = 512;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ int block_exclusive_scan(int value, int *warp_sums, int &block_total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = value;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    const int nwarps = blockDim.x >> 5;
+    if (warp == 0) {
+        int w = lane < nwarps ? warp_sums[lane] : 0;
+        int wi = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, wi, off);
+            if (lane >= off) wi += t;
+        }
+        if (lane < nwarps) warp_sums[lane] = wi - w;  // exclusive
+        if (lane == 31) warp_sums[32] = wi;           // block total
+    }
+    __syncthreads();
+    block_total = warp_sums[32];
+    const int result = warp_sums[warp] + incl - value;
+    __syncthreads();
+    return result;
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_reduce_kernel(const int *__restrict__ in, long long n, int *__restrict__ block_sums) {
+    __shared__ int warp_sums[33];
+    const long long base = (long long)blockIdx.x * kScanTile + (long long)threadIdx.x * kScanItems;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n) s += in[base + k];
+    int total;
+    block_exclusive_scan(s, warp_sums, total);
+    if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// One block: exclusive scan of block_sums in place; total (64-bit) to *total_out.
+__global__ void __launch_bounds__(kScanThreads)
+scan_sums_kernel(int *block_sums, int nb, long long *total_out) {
+    __shared__ int warp_sums[33];
+    long long carry = 0;
+    for (int base = 0; base < nb; base += kScanThreads) {
+        const int k = base + threadIdx.x;
+        const int v = k < nb ? block_sums[k] : 0;
+        int total;
+        const int ex = block_exclusive_scan(v, warp_sums, total);
+        if (k < nb) block_sums[k] = (int)(carry + ex);
+        carry += total;
+    }
+    if (threadIdx.x == 0) *total_out = carry;
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_apply_kernel(const int *in, long long n, const int *__restrict__ block_offsets,
+                  const long long *__restrict__ total, int *out) {
+    __shared__ int warp_sums[33];
+    const long long base = (long long)blockIdx.x * kScanTile + (long long)threadIdx.x * kScanItems;
+    int v[kScanItems];
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        v[k] = base + k < n ? in[base + k] : 0;
+        s += v[k];
+    }
+    int block_total;
+    int run = block_exclusive_scan(s, warp_sums, block_total) + block_offsets[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        if (base + k < n) out[base + k] = run;
+        run += v[k];
+    }
+    // entry n receives the grand total (out has n+1 entries)
+    if (blockIdx.x == 0 && threadIdx.x == 0) out[n] = (int)*total;
+}
+
+static inline int scan_blocks(long long n) { return (int)((n + kScanTile - 1) / kScanTile); }
+
+// out[0..n] = exclusive prefix sums of in[0..n) (out[n] = total).  `block_sums`
+// needs scan_blocks(n)+1 ints, `total_dev` one 64-bit word.  In-place is allowed.
+static cudaError_t exclusive_scan(const int *in, long long n, int *out, int *block_sums,
+                                  long long *total_dev, cudaStream_t st) {
+    const int nb = n > 0 ? scan_blocks(n) : 1;
+    scan_reduce_kernel<<<nb, kScanThreads, 0, st>>>(in, n, block_sums);
+    scan_sums_kernel<<<1, kScanThreads, 0, st>>>(block_sums, nb, total_dev);
+    scan_apply_kernel<<<nb, kScanThreads, 0, st>>>(in, n, block_sums, total_dev, out);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------- radix pass ----
+constexpr int kSortThreads = 256;
+constexpr int kSortRounds = 16;
+constexpr int kSortTile = kSortThreads * kSortRounds;
+
+__global__ void __launch_bounds__(kSortThreads)
+radix_hist_kernel(const unsigned *__restrict__ keys, long long m, int shift, int nb,
+                  int *__restrict__ hist) {
+    __shared__ int h[256];
+    h[threadIdx.x] = 0;
+    __syncthreads();
+    const long long base = (long long)blockIdx.x * kSortTile;
+    for (int r = 0; r < kSortRounds; ++r) {
+        const long long k = base + (long long)r * kSortThreads + threadIdx.x;
+        if (k < m) atomicAdd(&h[(keys[k] >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    hist[(long long)threadIdx.x * nb + blockIdx.x] = h[threadIdx.x];  // digit-major
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+radix_scatter_kernel(const unsigned *__restrict__ keys_in, const unsigned *__restrict__ vals_in,
+                     long long m, int shift, int nb, const int *__restrict__ offsets,
+                     unsigned *__restrict__ keys_out, unsigned *__restrict__ vals_out) {
+    constexpr int kWarps = kSortThreads / 32;
+    __shared__ int running[256];
+    __shared__ int warp_cnt[kWarps][256];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    running[threadIdx.x] = offsets[(long long)threadIdx.x * nb + blockIdx.x];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) warp_cnt[w][threadIdx.x] = 0;
+    __syncthreads();
+    const long long base = (long long)blockIdx.x * kSortTile;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int r = 0; r < kSortRounds; ++r) {
+        const long long k = base + (long long)r * kSortThreads + threadIdx.x;
+        const bool valid = k < m;
+        unsigned key = 0, val = 0;
+        if (valid) { key = keys_in[k]; val = vals_in[k]; }
+        const int dg = valid ? (int)((key >> shift) & 255u) : 256;
+        const unsigned peers = __match_any_sync(0xffffffffu, dg);
+        const int rank = __popc(peers & lt_mask);
+        const int cnt = __popc(peers);
+        if (valid && rank == 0) warp_cnt[warp][dg] = cnt;
+        __syncthreads();
+        if (valid) {
+            int off = running[dg] + rank;
+            for (int w = 0; w < warp; ++w) off += warp_cnt[w][dg];
+            keys_out[off] = key;
+            vals_out[off] = val;
+        }
+        __syncthreads();
+        if (valid && rank == 0) {
+            atomicAdd(&running[dg], cnt);
+            warp_cnt[warp][dg] = 0;
+        }
+        __syncthreads();
+    }
+}
+
+static inline int sort_blocks(long long m) { return (int)((m + kSortTile - 1) / kSortTile); }
+static inline int bits_for(long long max_value) {
+    int b = 1;
+    while (b < 32 && (1ll << b) <= max_value) ++b;
+    return b;
+}
+
+struct SortScratch {
+    int *hist;          // 256 * sort_blocks(m) + 1
+    int *block_sums;    // scan_blocks(256 * sort_blocks) + 1
+    long long *total;
+};
+
+// Stable sort of (keys, vals) on the low `bits` bits of keys.  Ping-pongs between
+// (k0,v0) and (k1,v1); *result_in_first tells where the sorted data ended up.
+static cudaError_t radix_sort_pairs(unsigned *k0, unsigned *v0, unsigned *k1, unsigned *v1,
+                                    long long m, int bits, const SortScratch &s,
+                                    cudaStream_t st, bool *result_in_first) {
+    bool first = true;
+    if (m > 0) {
+        const int nb = sort_blocks(m);
+        for (int shift = 0; shift < bits; shift += 8) {
+            unsigned *ki = first ? k0 : k1, *vi = first ? v0 : v1;
+            unsigned *ko = first ? k1 : k0, *vo = first ? v1 : v0;
+            radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, m, shift, nb, s.hist);
+            cudaError_t e = exclusive_scan(s.hist, 256ll * nb, s.hist, s.block_sums, s.total, st);
+            if (e != cudaSuccess) return e;
+            radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, m, shift, nb, s.hist, ko, vo);
+            first = !first;
+        }
+    }
+    *result_in_first = first;
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------- edge rule ----
+struct EdgeRule {
+    int op;
+    int n;
+    long long nnz;
+    const int *__restrict__ ptr;
+    const int *__restrict__ idx;
+};
+
+__device__ __forceinline__ bool src_major(int op) {
+    return op == LCD_OP_CSC_LOWER || op == LCD_OP_CSC_UPPER;
+}
+
+// Visits the edge instances of node v in inspector order; f(src, dst) per edge.
+// Returns an LCD_* code for malformed input.
+template <typename F>
+__device__ __forceinline__ int visit_edges(const EdgeRule &q, int v, F f) {
+    const bool upper = q.op == LCD_OP_CSR_UPPER || q.op == LCD_OP_CSC_UPPER;
+    const int i = upper ? q.n - 1 - v : v;
+    const int s = q.ptr[i], e = q.ptr[i + 1];
+    if (s < 0 || e < s || (long long)e > q.nnz) return LCD_ERR_BAD_POINTERS;
+    int lo = s, hi = e;
+    if (q.op == LCD_OP_CSR_LOWER || q.op == LCD_OP_CSC_UPPER) hi = e - 1;
+    if (q.op == LCD_OP_CSC_LOWER || q.op == LCD_OP_CSR_UPPER) lo = s + 1;
+    int rc = LCD_OK;
+    for (int j = lo; j < hi; ++j) {
+        const int c = q.idx[j];
+        if (c < 0 || c >= q.n) { rc = LCD_ERR_INDEX_RANGE; continue; }
+        switch (q.op) {
+            case LCD_OP_CSR_LOWER: if (i > c) f(c, i); break;
+            case LCD_OP_CSC_LOWER: if (c > i) f(i, c); break;
+            case LCD_OP_ILU0_CSR:
+                if (c >= i) return rc;
+                f(c, i);
+                break;
+            case LCD_OP_CSR_UPPER: if (c > i) f(q.n - 1 - c, v); break;
+            default: if (c < i) f(v, q.n - 1 - c); break;  // LCD_OP_CSC_UPPER
+        }
+    }
+    return rc;
+}
+
+__global__ void count_edges_kernel(const EdgeRule q, int *__restrict__ cnt, int32_t *status) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= q.n) return;
+    int c = 0;
+    const int rc = visit_edges(q, v, [&](int, int) { ++c; });
+    if (rc) raise_error(status, rc, v);
+    cnt[v] = c;
+}
+
+__global__ void emit_edges_kernel(const EdgeRule q, const int *__restrict__ offs,
+                                  unsigned *__restrict__ src_out, unsigned *__restrict__ dst_out,
+                                  int *edge_count) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= q.n) return;
+    int pos = offs[v];
+    const bool by_src = src_major(q.op);
+    visit_edges(q, v, [&](int src, int dst) {
+        src_out[pos] = (unsigned)src;
+        dst_out[pos] = (unsigned)dst;
+        ++pos;
+        if (by_src) atomicAdd(edge_count + dst, 1);
+    });
+}
+
+// head[p] = 1 for the first instance of each distinct (src, dst) pair.
+__global__ void flag_heads_kernel(const unsigned *__restrict__ src, const unsigned *__restrict__ dst,
+                                  long long m, int *__restrict__ head) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += stride)
+        head[p] = (p == 0 || src[p] != src[p - 1] || dst[p] != dst[p - 1]) ? 1 : 0;
+}
+
+__global__ void compact_edges_kernel(const unsigned *__restrict__ src, const unsigned *__restrict__ dst,
+                                     long long m, const int *__restrict__ pos,
+                                     int *__restrict__ dag_index, unsigned *__restrict__ usrc,
+                                     unsigned *__restrict__ udst, int *out_degree, int *dep_count) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += stride) {
+        if (pos[p + 1] == pos[p]) continue;  // not a head
+        const int o = pos[p];
+        dag_index[o] = (int)dst[p];
+        usrc[o] = src[p];
+        udst[o] = dst[p];
+        atomicAdd(out_degree + src[p], 1);
+        atomicAdd(dep_count + dst[p], 1);
+    }
+}
+
+// ------------------------------------------------------- level kernel ----
+constexpr int kLevelThreads = 512;
+
+__global__ void __launch_bounds__(kLevelThreads)
+level_kernel(int n, const int *__restrict__ pred_ptr, const unsigned *__restrict__ pred,
+             int *level, int *max_level, int32_t *status, unsigned long long budget_ns) {
+    __shared__ int sl[kLevelThreads];
+    __shared__ int s_chunk;
+    __shared__ int s_max;
+    const int tid = threadIdx.x;
+    if (tid == 0) { s_chunk = atomicAdd(&status[kStatusTicket], 1); s_max = -1; }
+    sl[tid] = -1;
+    __syncthreads();
+    volatile int *slv = sl;
+    const int row0 = s_chunk * kLevelThreads;
+    const int v = row0 + tid;
+    if (v < n) {
+        int p = pred_ptr[v];
+        const int pe = pred_ptr[v + 1];
+        int lvl = 0;
+        bool have = p < pe;
+        int u = have ? (int)pred[p] : 0;
+        Deadline dl;
+        dl.start(budget_ns);
+        for (;;) {
+            if (have) {
+                if ((unsigned)u >= (unsigned)v) {  // an edge must come from an earlier node
+                    raise_error(status, LCD_ERR_CYCLE, v);
+                    have = false;
+                } else {
+                    const int lu = (u >= row0) ? slv[u - row0] : ld_relaxed_s32(level + u);
+                    if (lu >= 0) {
+                        lvl = max(lvl, lu + 1);
+                        ++p;
+                        have = p < pe;
+                        if (have) u = (int)pred[p];
+                    } else if (dl.tick(status, v)) {
+                        have = false;
+                    }
+                }
+            } else {
+                asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(level + v), "r"(lvl) : "memory");
+                slv[tid] = lvl;
+                atomicMax(&s_max, lvl);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0 && s_max >= 0) atomicMax(max_level, s_max);
+}
+
+__global__ void level_hist_kernel(int n, const int *__restrict__ level, int *hist) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v < n) atomicAdd(hist + level[v], 1);
+}
+
+__global__ void iota_levels_kernel(int n, const int *__restrict__ level, unsigned *keys,
+                                   unsigned *vals) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v < n) { keys[v] = (unsigned)level[v]; vals[v] = (unsigned)v; }
+}
+
+__global__ void copy_u32_to_i32_kernel(long long m, const unsigned *__restrict__ in, int *out) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += stride)
+        out[p] = (int)in[p];
+}
+
+__global__ void adjacent_diff_kernel(int n, const int *__restrict__ offs, int *out) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v < n) out[v] = offs[v + 1] - offs[v];
+}
+
+// ---------------------------------------------------- diagonal table ----
+__global__ void diag_positions_kernel(int n, const int *__restrict__ ptr,
+                                      const int *__restrict__ idx, long long nnz, int *pos,
+                                      int32_t *status) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const long long start = ptr[s], end = ptr[s + 1];
+    if (start < 0 || end < start || end > nnz) {
+        raise_error(status, LCD_ERR_BAD_POINTERS, s);
+        pos[s] = -1;
+        return;
+    }
+    for (long long p = start + 1; p < end; ++p)
+        if (idx[p] < idx[p - 1]) { raise_error(status, LCD_ERR_UNSORTED, s); break; }
+    long long lo = start, hi = end;  // leftmost entry >= s
+    while (lo < hi) {
+        const long long mid = (lo + hi) >> 1;
+        if (idx[mid] < s) lo = mid + 1; else hi = mid;
+    }
+    pos[s] = (lo < end && idx[lo] == s) ? (int)lo : -1;
+}
+
+// ------------------------------------------------------ workspace plan ----
+struct Bump {
+    char *base;
+    size_t used;
+    template <typename T> T *take(size_t count) {
+        used = (used + 255) & ~(size_t)255;
+        T *p = base ? reinterpret_cast<T *>(base + used) : nullptr;
+        used += count * sizeof(T);
+        return p;
+    }
+};
+
+struct DagScratch {
+    unsigned *k0, *v0, *k1, *v1;  // cap entries each
+    int *flags;                   // cap + 1
+    int *cnt;                     // n + 1
+    int *pred_ptr;                // n + 1
+    int *out_degree;              // n + 1
+    int *max_level;               // 1 (+ padding)
+    SortScratch sort;
+    int *scan_sums;
+    long long *scan_total;
+};
+
+static DagScratch plan_scratch(Bump &b, int n, long long cap) {
+    DagScratch s;
+    const long long big = cap > n ? cap : n;
+    s.k0 = b.take<unsigned>(big + 1);
+    s.v0 = b.take<unsigned>(big + 1);
+    s.k1 = b.take<unsigned>(big + 1);
+    s.v1 = b.take<unsigned>(big + 1);
+    s.flags = b.take<int>(big + 2);
+    s.cnt = b.take<int>((size_t)n + 2);
+    s.pred_ptr = b.take<int>((size_t)n + 2);
+    s.out_degree = b.take<int>((size_t)n + 2);
+    s.max_level = b.take<int>(64);
+    const long long hist_len = 256ll * sort_blocks(big + 1) + 1;
+    s.sort.hist = b.take<int>(hist_len + 1);
+    s.sort.block_sums = b.take<int>(scan_blocks(hist_len) + 2);
+    s.sort.total = b.take<long long>(8);
+    s.scan_sums = b.take<int>(scan_blocks(big + 2) + 2);
+    s.scan_total = b.take<long long>(8);
+    return s;
+}
+
+static inline int grid_for(long long m, int threads) {
+    long long g = (m + threads - 1) / threads;
+    const long long cap = 148ll * 32;
+    return (int)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" int lcd_dag_workspace_bytes(int op, int32_t n, int64_t nnz, int64_t *bytes) {
+    if (op < 0 || op > LCD_OP_CSC_UPPER || n < 0 || nnz < 0 || !bytes)
+        return LCD_ERR_INVALID_ARGUMENT;
+    Bump b{nullptr, 0};
+    b.take<int32_t>(LCD_STATUS_WORDS);
+    plan_scratch(b, n, nnz);
+    *bytes = (int64_t)b.used + 256;
+    return LCD_OK;
+}
+
+extern "C" int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_t *idx,
+                             int64_t nnz, int32_t *dep_count, int32_t *edge_count,
+                             int32_t *dag_ptr, int32_t *dag_index, int64_t *n_edges_host,
+                             int32_t *level, int32_t *wavefronts, int32_t *wavefront_ptr,
+                             int32_t *n_levels_host, void *workspace, int64_t workspace_bytes,
+                             int32_t timeout_ms, void *stream) {
+    if (op < 0 || op > LCD_OP_CSC_UPPER || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
+        return LCD_ERR_INVALID_ARGUMENT;
+    *n_edges_host = 0;
+    *n_levels_host = 0;
+    if (n == 0) return LCD_OK;
+    if (!ptr || (nnz > 0 && !idx) || !dep_count || !edge_count || !dag_ptr || !dag_index ||
+        !level || !wavefronts || !wavefront_ptr || !workspace)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (nnz > 0x7fffffffll - 4096) return LCD_ERR_TOO_LARGE;
+    int64_t need = 0;
+    lcd_dag_workspace_bytes(op, n, nnz, &need);
+    if (workspace_bytes < need) return LCD_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    Bump bump{reinterpret_cast<char *>(workspace), 0};
+    int32_t *status = bump.take<int32_t>(LCD_STATUS_WORDS);
+    DagScratch s = plan_scratch(bump, n, nnz);
+    int rc = reset_status(status, st);
+    if (rc) return rc;
+    const EdgeRule q{op, n, nnz, ptr, idx};
+    const int nblk = (n + 255) / 256;
+    const bool by_src = (op == LCD_OP_CSC_LOWER || op == LCD_OP_CSC_UPPER);
+
+    // 1. count, scan, emit
+    count_edges_kernel<<<nblk, 256, 0, st>>>(q, s.cnt, status);
+    LCD_CUDA_TRY(exclusive_scan(s.cnt, n, s.cnt, s.scan_sums, s.scan_total, st));
+    long long n_inst = 0;
+    LCD_CUDA_TRY(cudaMemcpyAsync(&n_inst, s.scan_total, sizeof n_inst, cudaMemcpyDeviceToHost, st));
+    LCD_CUDA_TRY(cudaMemsetAsync(edge_count, 0, (size_t)n * sizeof(int32_t), st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    rc = lcd_read_status(status, st, nullptr);
+    if (rc) return rc;
+    if (n_inst > nnz) return LCD_ERR_TOO_LARGE;  // cannot happen: one edge per stored entry at most
+    emit_edges_kernel<<<nblk, 256, 0, st>>>(q, s.cnt, s.k0, s.v0, edge_count);
+    // destination-major rules: the per-node instance count is the edge multiplicity
+    if (!by_src) adjacent_diff_kernel<<<nblk, 256, 0, st>>>(n, s.cnt, edge_count);
+    LCD_CUDA_TRY(cudaGetLastError());
+
+    // 2. (src, dst) order.  keys = src in k*, vals = dst in v*.
+    const int node_bits = bits_for(n > 1 ? n - 1 : 1);
+    unsigned *src = s.k0, *dst = s.v0, *src_alt = s.k1, *dst_alt = s.v1;
+    bool in_first = true;
+    if (by_src) {
+        // emission is source-major but destinations inside a segment may be unsorted:
+        // sort by destination first (dst as key), then by source.
+        LCD_CUDA_TRY(radix_sort_pairs(dst, src, dst_alt, src_alt, n_inst, node_bits, s.sort, st,
+                                      &in_first));
+        if (!in_first) { unsigned *t = src; src = src_alt; src_alt = t; t = dst; dst = dst_alt; dst_alt = t; }
+    }
+    LCD_CUDA_TRY(radix_sort_pairs(src, dst, src_alt, dst_alt, n_inst, node_bits, s.sort, st,
+                                  &in_first));
+    if (!in_first) { unsigned *t = src; src = src_alt; src_alt = t; t = dst; dst = dst_alt; dst_alt = t; }
+
+    // 3. distinct edges
+    LCD_CUDA_TRY(cudaMemsetAsync(dep_count, 0, (size_t)n * sizeof(int32_t), st));
+    LCD_CUDA_TRY(cudaMemsetAsync(s.out_degree, 0, ((size_t)n + 1) * sizeof(int), st));
+    long long n_uniq = 0;
+    if (n_inst > 0) {
+        flag_heads_kernel<<<grid_for(n_inst, 256), 256, 0, st>>>(src, dst, n_inst, s.flags);
+        LCD_CUDA_TRY(exclusive_scan(s.flags, n_inst, s.flags, s.scan_sums, s.scan_total, st));
+        compact_edges_kernel<<<grid_for(n_inst, 256), 256, 0, st>>>(
+            src, dst, n_inst, s.flags, dag_index, src_alt, dst_alt, s.out_degree, dep_count);
+        LCD_CUDA_TRY(cudaMemcpyAsync(&n_uniq, s.scan_total, sizeof n_uniq, cudaMemcpyDeviceToHost, st));
+    }
+    LCD_CUDA_TRY(exclusive_scan(s.out_degree, n, dag_ptr, s.scan_sums, s.scan_total, st));
+    LCD_CUDA_TRY(exclusive_scan(dep_count, n, s.pred_ptr, s.scan_sums, s.scan_total, st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    *n_edges_host = n_uniq;
+
+    // 4. predecessor lists (distinct edges regrouped by destination), levels
+    //    distinct edges live in (src_alt, dst_alt); (src, dst) is free now.
+    LCD_CUDA_TRY(radix_sort_pairs(dst_alt, src_alt, dst, src, n_uniq, node_bits, s.sort, st, &in_first));
+    const unsigned *pred = in_first ? src_alt : src;
+    LCD_CUDA_TRY(cudaMemsetAsync(level, 0xFF, (size_t)n * sizeof(int32_t), st));
+    LCD_CUDA_TRY(cudaMemsetAsync(s.max_level, 0xFF, sizeof(int), st));
+    rc = reset_status(status, st);
+    if (rc) return rc;
+    level_kernel<<<(n + kLevelThreads - 1) / kLevelThreads, kLevelThreads, 0, st>>>(
+        n, s.pred_ptr, pred, level, s.max_level, status, timeout_ns(timeout_ms));
+    LCD_CUDA_TRY(cudaGetLastError());
+    int max_level = -1;
+    LCD_CUDA_TRY(cudaMemcpyAsync(&max_level, s.max_level, sizeof max_level, cudaMemcpyDeviceToHost, st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    rc = lcd_read_status(status, st, nullptr);
+    if (rc) return rc;
+    const int n_levels = max_level + 1;
+    *n_levels_host = n_levels;
+
+    // 5. nodes by (level, id); level offsets
+    LCD_CUDA_TRY(cudaMemsetAsync(s.cnt, 0, ((size_t)n + 1) * sizeof(int), st));
+    level_hist_kernel<<<nblk, 256, 0, st>>>(n, level, s.cnt);
+    LCD_CUDA_TRY(exclusive_scan(s.cnt, n_levels, wavefront_ptr, s.scan_sums, s.scan_total, st));
+    iota_levels_kernel<<<nblk, 256, 0, st>>>(n, level, s.k0, s.v0);
+    LCD_CUDA_TRY(radix_sort_pairs(s.k0, s.v0, s.k1, s.v1, n, bits_for(n_levels > 1 ? n_levels - 1 : 1),
+                                  s.sort, st, &in_first));
+    copy_u32_to_i32_kernel<<<grid_for(n, 256), 256, 0, st>>>(n, in_first ? s.v0 : s.v1, wavefronts);
+    LCD_CUDA_TRY(cudaGetLastError());
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    return LCD_OK;
+}
+
+extern "C" int lcd_diag_positions(int32_t n, const int32_t *ptr, const int32_t *idx, int64_t nnz,
+                                  int32_t *pos, int32_t *status_dev, void *stream,
+                                  int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev || (n > 0 && (!ptr || !pos)))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        diag_positions_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, ptr, idx, nnz, pos, status_dev);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    return finish(status_dev, st, status_host);
+}

@@ -1,0 +1,196 @@
+// In-place ILU(0) of a CSR matrix with sorted rows (sm_100a).
+//
+// Arithmetic follows the sequential loop nest exactly: for each row the pivots
+// k < i are applied in ascending order, l_ik = a_ik / a_kk, then
+// a_ij <- a_ij - l_ik * a_kj for the stored j > k of row i that row k also
+// stores, with the product and the difference rounded separately.  The result
+// is therefore bit-identical to the sequential factorisation.
+//
+// Sync-free mode: rows are handed out by ticket in index order; a lane group
+// owns a row and keeps a fixed owner lane per stored entry, a finished row is
+// announced with a release store to done[row]; a row polls done[k] of its next
+// pivot without blocking (one poll per loop trip), so groups that share a warp
+// never wait on each other inside a convergence region.
+// Wavefront mode: one launch per level over the same row code.
+#include "common.cuh"
+
+namespace lcd {
+
+struct Ilu0Params {
+    int n;
+    long long nnz;
+    const int *__restrict__ Ap;
+    const int *__restrict__ Ai;
+    double *Ax;
+    const int *__restrict__ dpos;
+    int *done;
+    const int *__restrict__ wavefronts;
+    int32_t *status;
+    unsigned long long budget_ns;
+};
+
+// Applies pivot row k (position kp in row i) with the lanes of one group.
+// owner(jp) = (jp - row_start) % G keeps every entry of row i with one lane.
+template <int G>
+__device__ __forceinline__ void apply_pivot(const Ilu0Params &p, int i, int row_start, int row_end,
+                                            int kp, int k, int lane, unsigned gmask) {
+    const int dk = __ldg(p.dpos + k);
+    double diag = 0.0;
+    if (dk >= 0) diag = ld_relaxed_f64(p.Ax + dk);
+    if (diag == 0.0) return;  // group-uniform: every lane read the same value
+    const int owner = (kp - row_start) % G;
+    double lik = 0.0;
+    if (lane == owner) {
+        lik = p.Ax[kp] / diag;
+        p.Ax[kp] = lik;
+    }
+    if (G > 1) lik = __shfl_sync(gmask, lik, owner, G);
+    const int ks = __ldg(p.Ap + k), ke = __ldg(p.Ap + k + 1);
+    // first own position after kp
+    int jp = kp + 1 + ((lane - (kp + 1 - row_start)) % G + G) % G;
+    for (; jp < row_end; jp += G) {
+        const int j = __ldg(p.Ai + jp);
+        int lo = ks, hi = ke;  // leftmost entry of row k that is >= j
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (__ldg(p.Ai + mid) < j) lo = mid + 1; else hi = mid;
+        }
+        if (lo < ke && __ldg(p.Ai + lo) == j)
+            p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ld_relaxed_f64(p.Ax + lo)));
+    }
+}
+
+template <int G, int TPB>
+__global__ void __launch_bounds__(TPB) ilu0_syncfree_kernel(const Ilu0Params p) {
+    constexpr int R = TPB / G;
+    __shared__ int s_chunk;
+    if (threadIdx.x == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    __syncthreads();
+    const int local = threadIdx.x / G, lane = threadIdx.x % G;
+    const int i = s_chunk * R + local;
+    if (i >= p.n) return;
+    const unsigned gmask =
+        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+    const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
+    bool bad = s < 0 || e < s || (long long)e > p.nnz;
+    if (bad && lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
+    int kp = s;
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        int k = -1;
+        if (!bad && kp < e) {
+            k = __ldg(p.Ai + kp);
+            if (k < 0 || k >= p.n) {
+                if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, i);
+                bad = true;
+                k = -1;
+            } else if (k >= i) {
+                k = -1;  // reached the diagonal / upper part: the row is complete
+            }
+        }
+        if (k >= 0) {
+            int ready = 0;  // 0 not yet, 1 go, 2 give up
+            if (lane == 0) {
+                if (ld_acquire_s32(p.done + k) != 0) ready = 1;
+                else if (dl.tick(p.status, i)) ready = 2;
+            }
+            if (G > 1) ready = __shfl_sync(gmask, ready, 0, G);
+            if (ready == 1) {
+                apply_pivot<G>(p, i, s, e, kp, k, lane, gmask);
+                ++kp;
+            } else if (ready == 2) {
+                bad = true;
+            }
+        } else {
+            // all stores of the group happen before the flag becomes visible
+            if (G > 1) __syncwarp(gmask);
+            if (lane == 0) {
+                __threadfence();
+                st_release_s32(p.done + i, 1);
+            }
+            break;
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int wave_start,
+                                                        int wave_end) {
+    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int t = wave_start + gtid / G, lane = gtid % G;
+    if (t >= wave_end) return;
+    const int i = __ldg(p.wavefronts + t);
+    if ((unsigned)i >= (unsigned)p.n) return;
+    const unsigned gmask =
+        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+    const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
+    if (s < 0 || e < s || (long long)e > p.nnz) {
+        if (lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
+        return;
+    }
+    for (int kp = s; kp < e; ++kp) {
+        const int k = __ldg(p.Ai + kp);
+        if (k >= i) break;
+        if (k < 0) { if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, i); break; }
+        apply_pivot<G>(p, i, s, e, kp, k, lane, gmask);
+    }
+}
+
+template <int G>
+static cudaError_t launch_ilu0(const Ilu0Params &p, int mode, const int32_t *wptr_host,
+                               int n_levels, cudaStream_t st) {
+    if (mode == 0) {
+        constexpr int TPB = 256, R = TPB / G;
+        ilu0_syncfree_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
+    } else {
+        for (int l = 0; l < n_levels; ++l) {
+            const int ws = wptr_host[l], we = wptr_host[l + 1];
+            if (we <= ws) continue;
+            const long long threads = (long long)(we - ws) * G;
+            ilu0_level_kernel<G><<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(p, ws, we);
+        }
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                              double *Ax, const int32_t *diag_pos, int mode, int32_t *done,
+                              const int32_t *wavefronts, const int32_t *wavefront_ptr_host,
+                              int32_t n_levels, int lanes_per_row, int32_t *status_dev,
+                              int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev || (mode != 0 && mode != 1)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !Ai || !Ax || !diag_pos)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && mode == 0 && !done) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && mode == 1 && (!wavefronts || !wavefront_ptr_host || n_levels < 0))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int G = lanes_per_row;
+    if (G <= 0) {
+        const double avg = n > 0 ? (double)nnz / n : 0.0;
+        G = avg <= 12 ? 4 : (avg <= 40 ? 8 : (avg <= 96 ? 16 : 32));
+    }
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        if (mode == 0) LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
+        Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, wavefronts, status_dev,
+                     timeout_ns(timeout_ms)};
+        cudaError_t e;
+        switch (G) {
+            case 1: e = launch_ilu0<1>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            case 2: e = launch_ilu0<2>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            case 4: e = launch_ilu0<4>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            case 8: e = launch_ilu0<8>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            case 16: e = launch_ilu0<16>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            case 32: e = launch_ilu0<32>(p, mode, wavefront_ptr_host, n_levels, st); break;
+            default: return LCD_ERR_INVALID_ARGUMENT;
+        }
+        LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}

@@ -1,0 +1,629 @@
+// Sync-free sparse triangular solves (CSR pull, CSC push, multi-RHS) for sm_100a.
+//
+// Scheduling.  Rows are handed out in node order through a ticket taken by each
+// thread block when it starts running, so a block only ever waits for rows that
+// belong to blocks already resident or finished: the waits cannot deadlock.
+// A block owns a contiguous chunk of rows; one lane group (1..32 lanes) owns a row.
+//
+// Hand-off (CSR).  The solution vector is pre-filled with a reserved NaN bit
+// pattern.  A consumer polls the operand x[c] itself: an aligned 8-byte store is
+// single-copy atomic, so no flag, counter or fence is needed.  Rows of the own
+// chunk are mirrored in shared memory, which turns dependences between nearby
+// rows (the critical chain of banded / grid matrices) into shared-memory polls.
+//
+// Every wait is bounded by a wall-clock budget; on expiry the kernel records
+// LCD_ERR_TIMEOUT in the status block, all other waiters observe it and drain.
+#include "common.cuh"
+
+namespace lcd {
+
+template <int G, int TPB, int MINB>
+__global__ void __launch_bounds__(TPB, MINB) csr_syncfree_kernel(const CsrSolveParams p) {
+    constexpr int R = TPB / G;
+    __shared__ double sx[R];
+    __shared__ int s_chunk;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    if (tid < R) reinterpret_cast<unsigned long long *>(sx)[tid] = kPendingBits;
+    __syncthreads();
+    volatile double *sxv = sx;
+    const int row0 = s_chunk * R;  // node id of the chunk's first row
+    const int local = tid / G;
+    const int lane = tid % G;
+    const int task = row0 + local;
+    if (task >= p.n) return;
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const bool exact = p.flags & LCD_SOLVE_EXACT;
+    const int r = upper ? p.n - 1 - task : task;
+    const unsigned gmask =
+        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+
+    int lo = 0, hi = 0, d = -1;
+    bool failed = false;
+    if (!csr_row_range(p, r, lo, hi, d)) {
+        if (lane == 0)
+            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                               : LCD_ERR_BAD_POINTERS, r);
+        failed = true;
+        lo = hi = 0;
+        d = -1;
+    }
+    double acc = 0.0, dv = 1.0, rinv = 1.0;
+    if (lane == 0) {
+        acc = __ldg(p.b + r);
+        if (d >= 0) dv = __ldg(p.Ax + d);
+        if (!exact) rinv = 1.0 / dv;  // off the critical path: computed before any wait
+    }
+    int j = lo + lane;
+    bool have = j < hi;
+    int c = 0;
+    double a = 0.0;
+    if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        if (have) {
+            const int tc = upper ? p.n - 1 - c : c;
+            if ((unsigned)tc >= (unsigned)task) {  // not strictly before this row
+                raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                failed = true;
+                have = false;
+            } else {
+                const double xv = (tc >= row0) ? sxv[tc - row0] : ld_relaxed_f64(p.x + c);
+                if (!is_pending(xv)) {
+                    acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
+                    j += G;
+                    have = j < hi;
+                    if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
+                } else if (dl.tick(p.status, r)) {
+                    failed = true;
+                    have = false;
+                }
+            }
+        }
+        const bool group_done = (G == 1) ? !have : (__all_sync(gmask, !have) != 0);
+        if (group_done) {
+            if (G > 1) {
+#pragma unroll
+                for (int off = G / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(gmask, acc, off, G);
+                failed = __any_sync(gmask, failed) != 0;
+            }
+            if (lane == 0) {
+                double val = (d < 0) ? acc : (exact ? acc / dv : acc * rinv);
+                if (failed) val = __longlong_as_double(kCanonicalNaN);
+                val = publishable(val);
+                st_relaxed_f64(p.x + r, val);
+                sxv[local] = val;
+            }
+            break;
+        }
+    }
+}
+
+// Tunables of the thread-per-row kernel (set through lcd_set_tuning).
+struct RowTuning {
+    int sleep_local_ns;   // pause after a failed poll of the shared-memory mirror
+    int sleep_global_ns;  // pause after a failed poll of x in global memory
+    int gap_ns;           // pause per row of distance between the awaited row and the
+                          // progress of the warp that owns it (0 = off)
+    int variant;          // 0: thread-per-row kernel for one lane per row, 1: generic kernel
+};
+static RowTuning g_row_tuning = {0, 200, 40, 0};
+
+// Thread per row.  Leading operands that live before the chunk and are already
+// available are consumed first without waiting; everything else goes through a
+// single try-advance loop (shared-memory mirror for rows of the own chunk, global
+// memory otherwise).  Rows complete roughly in index order inside a warp, so a
+// per-warp completion count tells a waiting thread how far the producer's warp is
+// from the row it needs; distant waiters pause instead of burning issue slots that
+// the threads on the critical chain need.
+template <int TPB, int MINB>
+__global__ void __launch_bounds__(TPB, MINB)
+csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
+    constexpr int kWarps = TPB / 32;
+    __shared__ double sx[TPB];
+    __shared__ int s_wdone[kWarps];
+    __shared__ int s_chunk;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    reinterpret_cast<unsigned long long *>(sx)[tid] = kPendingBits;
+    if (tid < kWarps) s_wdone[tid] = 0;
+    __syncthreads();
+    volatile double *sxv = sx;
+    volatile int *wdone = s_wdone;
+    const int row0 = s_chunk * TPB;
+    const int task = row0 + tid;
+    if (task >= p.n) return;
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const bool exact = p.flags & LCD_SOLVE_EXACT;
+    const int r = upper ? p.n - 1 - task : task;
+    int lo = 0, hi = 0, d = -1;
+    bool failed = false;
+    if (!csr_row_range(p, r, lo, hi, d)) {
+        raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                           : LCD_ERR_BAD_POINTERS, r);
+        failed = true;
+        lo = hi = 0;
+        d = -1;
+    }
+    double acc = __ldg(p.b + r);
+    double dv = 1.0, rinv = 1.0;
+    if (d >= 0) dv = __ldg(p.Ax + d);
+    if (!exact) rinv = 1.0 / dv;
+    int j = lo;
+    int cl = 0, c = 0;  // cl: operand's position relative to the chunk (>= 0: mirrored)
+    double a = 0.0;
+    bool have = j < hi;
+#define LCD_FETCH_OPERAND()                                                  \
+    do {                                                                     \
+        c = __ldg(p.Ai + j);                                                 \
+        a = __ldg(p.Ax + j);                                                 \
+        const int tc_ = upper ? p.n - 1 - c : c;                             \
+        if ((unsigned)tc_ >= (unsigned)task) {                               \
+            raise_error(p.status, LCD_ERR_INDEX_RANGE, r);                   \
+            failed = true;                                                   \
+            have = false;                                                    \
+        }                                                                    \
+        cl = tc_ - row0;                                                     \
+    } while (0)
+    if (have) LCD_FETCH_OPERAND();
+    // fast-forward over operands outside the chunk that are already there
+    while (have && cl < 0) {
+        const double xv = ld_relaxed_f64(p.x + c);
+        if (is_pending(xv)) break;
+        acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
+        ++j;
+        have = j < hi;
+        if (have) LCD_FETCH_OPERAND();
+    }
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        if (have) {
+            const double xv = cl >= 0 ? sxv[cl] : ld_relaxed_f64(p.x + c);
+            if (!is_pending(xv)) {
+                acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
+                ++j;
+                have = j < hi;
+                if (have) LCD_FETCH_OPERAND();
+            } else {
+                if (dl.tick(p.status, r)) {
+                    failed = true;
+                    have = false;
+                } else if (cl >= 0) {
+                    int pause = tune.sleep_local_ns;
+                    if (tune.gap_ns) {
+                        const int gap = (cl & 31) - wdone[cl >> 5];  // rows the owner warp still owes
+                        if (gap > 1) pause += (gap - 1) * tune.gap_ns;
+                    }
+                    if (pause > 0) __nanosleep(pause);
+                } else if (tune.sleep_global_ns > 0) {
+                    __nanosleep(tune.sleep_global_ns);
+                }
+            }
+        } else {
+            double val = (d < 0) ? acc : (exact ? acc / dv : acc * rinv);
+            if (failed) val = __longlong_as_double(kCanonicalNaN);
+            val = publishable(val);
+            sxv[tid] = val;
+            st_relaxed_f64(p.x + r, val);
+            atomicAdd(&s_wdone[tid >> 5], 1);
+            break;
+        }
+    }
+#undef LCD_FETCH_OPERAND
+}
+
+// Multi-RHS: the block of right-hand sides is row-major, a thread owns one
+// (row, rhs) pair, consecutive lanes own consecutive right-hand sides of a row.
+// Each lane polls exactly the operand elements it consumes, so lanes never have
+// to agree on anything.  W = lanes per row (power of two), KR = columns per lane.
+template <int W, int KR, int TPB>
+__global__ void __launch_bounds__(TPB) csr_syncfree_multi_kernel(const CsrSolveParams p) {
+    constexpr int R = TPB / W;
+    extern __shared__ double smem_multi[];  // R x (W*KR)
+    __shared__ int s_chunk;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    for (int k = tid; k < R * W * KR; k += TPB)
+        reinterpret_cast<unsigned long long *>(smem_multi)[k] = kPendingBits;
+    __syncthreads();
+    volatile double *sxv = smem_multi;
+    const int row0 = s_chunk * R;
+    const int local = tid / W;
+    const int lane = tid % W;
+    const int task = row0 + local;
+    if (task >= p.n) return;
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const int r = upper ? p.n - 1 - task : task;
+    int lo = 0, hi = 0, d = -1;
+    bool failed = false;
+    if (!csr_row_range(p, r, lo, hi, d)) {
+        if (lane == 0)
+            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                               : LCD_ERR_BAD_POINTERS, r);
+        failed = true;
+        lo = hi = 0;
+        d = -1;
+    }
+    // number of right-hand sides this lane owns: lane, lane+W, ...
+    const int nlive = lane < p.nrhs ? min(KR, (p.nrhs - lane + W - 1) / W) : 0;
+    if (nlive == 0) return;
+    double acc0 = __ldg(p.b + (long long)r * p.ld + lane);
+    double acc1 = (KR > 1 && nlive > 1) ? __ldg(p.b + (long long)r * p.ld + lane + W) : 0.0;
+    const double rinv = d >= 0 ? 1.0 / __ldg(p.Ax + d) : 1.0;
+    int j = lo, kk = 0;
+    bool have = j < hi;
+    int c = 0;
+    double a = 0.0;
+    if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        if (have) {
+            const int tc = upper ? p.n - 1 - c : c;
+            if ((unsigned)tc >= (unsigned)task) {
+                raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                failed = true;
+                have = false;
+            } else {
+                const int q = lane + kk * W;
+                const double xv = (tc >= row0) ? sxv[(tc - row0) * (W * KR) + q]
+                                               : ld_relaxed_f64(p.x + (long long)c * p.ld + q);
+                if (!is_pending(xv)) {
+                    if (KR == 1 || kk == 0) acc0 = fma(-a, xv, acc0);
+                    else acc1 = fma(-a, xv, acc1);
+                    if (++kk == nlive) {
+                        kk = 0;
+                        ++j;
+                        have = j < hi;
+                        if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
+                    }
+                } else if (dl.tick(p.status, r)) {
+                    failed = true;
+                    have = false;
+                }
+            }
+        } else {
+            const double nanv = __longlong_as_double(kCanonicalNaN);
+            double v0 = publishable(failed ? nanv : acc0 * rinv);
+            st_relaxed_f64(p.x + (long long)r * p.ld + lane, v0);
+            sxv[local * (W * KR) + lane] = v0;
+            if (KR > 1 && nlive > 1) {
+                double v1 = publishable(failed ? nanv : acc1 * rinv);
+                st_relaxed_f64(p.x + (long long)r * p.ld + lane + W, v1);
+                sxv[local * (W * KR) + lane + W] = v1;
+            }
+            break;
+        }
+    }
+}
+
+// ---- CSC, push protocol ---------------------------------------------------
+struct CscSolveParams {
+    int n;
+    long long nnz;
+    const int *__restrict__ Ap;
+    const int *__restrict__ Ai;
+    const double *__restrict__ Ax;
+    const double *__restrict__ b;
+    double *x;
+    int *dep;
+    int flags;
+    int32_t *status;
+    unsigned long long budget_ns;
+};
+
+template <int G, int TPB>
+__global__ void __launch_bounds__(TPB) csc_syncfree_kernel(const CscSolveParams p) {
+    constexpr int R = TPB / G;
+    __shared__ int s_chunk;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    __syncthreads();
+    const int local = tid / G;
+    const int lane = tid % G;
+    const int task = s_chunk * R + local;
+    if (task >= p.n) return;
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const bool exact = p.flags & LCD_SOLVE_EXACT;
+    const int i = upper ? p.n - 1 - task : task;
+    const unsigned gmask =
+        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+    const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
+    int state = 0;  // 0 waiting, 1 go, 2 give up
+    if (s < 0 || e <= s || (long long)e > p.nnz) {
+        if (lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
+        state = 2;
+    }
+    const int d = upper ? e - 1 : s;
+    const int lo = upper ? s : s + 1;
+    const int hi = upper ? e - 1 : e;
+    double bv = 0.0, dv = 1.0, rinv = 1.0;
+    if (lane == 0 && state == 0) {
+        bv = __ldg(p.b + i);
+        dv = __ldg(p.Ax + d);
+        if (!exact) rinv = 1.0 / dv;
+    }
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        if (lane == 0 && state == 0) {
+            if (ld_acquire_s32(p.dep + i) == 0) state = 1;
+            else if (dl.tick(p.status, i)) state = 2;
+        }
+        if (G > 1) state = __shfl_sync(gmask, state, 0, G);
+        if (state == 1) {
+            double xi = 0.0;
+            if (lane == 0) {
+                const double accv = ld_relaxed_f64(p.x + i);
+                xi = exact ? __dsub_rn(bv, accv) / dv : (bv - accv) * rinv;
+                st_relaxed_f64(p.x + i, xi);
+            }
+            if (G > 1) xi = __shfl_sync(gmask, xi, 0, G);
+            for (int j = lo + lane; j < hi; j += G) {
+                const int r = __ldg(p.Ai + j);
+                const bool ok = upper ? (r >= 0 && r < i) : (r > i && r < p.n);
+                if (!ok) {
+                    raise_error(p.status, LCD_ERR_INDEX_RANGE, i);
+                    continue;
+                }
+                red_relaxed_add_f64(p.x + r, __dmul_rn(__ldg(p.Ax + j), xi));
+                red_release_add_s32(p.dep + r, -1);
+            }
+            break;
+        }
+        if (state == 2) break;
+    }
+}
+
+__global__ void csc_edge_count_kernel(int n, const int *__restrict__ Ap,
+                                      const int *__restrict__ Ai, int upper, int *count) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int s = Ap[i], e = Ap[i + 1];
+    const int lo = upper ? s : s + 1, hi = upper ? e - 1 : e;
+    for (int j = lo; j < hi; ++j) {
+        const int r = Ai[j];
+        const bool ok = upper ? (r >= 0 && r < i) : (r > i && r < n);
+        if (ok) atomicAdd(count + r, 1);
+    }
+}
+
+__global__ void fill_u64_kernel(unsigned long long *dst, long long count, unsigned long long v) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride)
+        dst[k] = v;
+}
+
+__global__ void transpose_f64_kernel(long long rows, long long cols, const double *__restrict__ in,
+                                     long long ld_in, double *__restrict__ out, long long ld_out) {
+    // in is rows x cols with leading dimension ld_in (element (r,c) at in[r*ld_in + c]);
+    // out is cols x rows.  32x32 tiles through padded shared memory.
+    __shared__ double tile[32][33];
+    const long long c0 = (long long)blockIdx.x * 32, r0 = (long long)blockIdx.y * 32;
+    for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+        const long long r = r0 + k, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[k][threadIdx.x] = in[r * ld_in + c];
+    }
+    __syncthreads();
+    for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+        const long long c = c0 + k, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[c * ld_out + r] = tile[threadIdx.x][k];
+    }
+}
+
+static int pick_lanes(long long nnz, int n) {
+    const double avg = n > 0 ? (double)nnz / n : 0.0;
+    if (avg <= 24) return 1;
+    if (avg <= 48) return 2;
+    if (avg <= 96) return 4;
+    if (avg <= 192) return 8;
+    if (avg <= 384) return 16;
+    return 32;
+}
+
+static cudaError_t launch_csr_row(const CsrSolveParams &p, int tpb, cudaStream_t st) {
+    if (tpb == 1024)
+        csr_syncfree_row_kernel<1024, 1><<<(p.n + 1023) / 1024, 1024, 0, st>>>(p, g_row_tuning);
+    else if (tpb == 512)
+        csr_syncfree_row_kernel<512, 2><<<(p.n + 511) / 512, 512, 0, st>>>(p, g_row_tuning);
+    else
+        csr_syncfree_row_kernel<256, 4><<<(p.n + 255) / 256, 256, 0, st>>>(p, g_row_tuning);
+    return cudaGetLastError();
+}
+
+template <int G>
+static cudaError_t launch_csr(const CsrSolveParams &p, int tpb, cudaStream_t st) {
+    if (tpb == 1024) {
+        constexpr int R = 1024 / G;
+        csr_syncfree_kernel<G, 1024, 1><<<(p.n + R - 1) / R, 1024, 0, st>>>(p);
+    } else if (tpb == 512) {
+        constexpr int R = 512 / G;
+        csr_syncfree_kernel<G, 512, 3><<<(p.n + R - 1) / R, 512, 0, st>>>(p);
+    } else {
+        constexpr int R = 256 / G;
+        csr_syncfree_kernel<G, 256, 6><<<(p.n + R - 1) / R, 256, 0, st>>>(p);
+    }
+    return cudaGetLastError();
+}
+
+template <int G>
+static cudaError_t launch_csc(const CscSolveParams &p, cudaStream_t st) {
+    constexpr int TPB = 256, R = TPB / G;
+    csc_syncfree_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <int W, int KR>
+static cudaError_t launch_multi(const CsrSolveParams &p, cudaStream_t st) {
+    constexpr int TPB = 512, R = TPB / W;
+    const size_t smem = (size_t)R * W * KR * sizeof(double);
+    csr_syncfree_multi_kernel<W, KR, TPB><<<(p.n + R - 1) / R, TPB, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" int lcd_set_tuning(int key, int value) {
+    switch (key) {
+        case LCD_TUNE_SLEEP_LOCAL_NS: g_row_tuning.sleep_local_ns = value; break;
+        case LCD_TUNE_SLEEP_GLOBAL_NS: g_row_tuning.sleep_global_ns = value; break;
+        case LCD_TUNE_GAP_NS: g_row_tuning.gap_ns = value; break;
+        case LCD_TUNE_ROW_VARIANT: g_row_tuning.variant = value; break;
+        default: return LCD_ERR_INVALID_ARGUMENT;
+    }
+    return LCD_OK;
+}
+
+extern "C" int lcd_fill_u64(uint64_t *dst, int64_t count, uint64_t value, void *stream) {
+    if (count < 0 || (count > 0 && !dst)) return LCD_ERR_INVALID_ARGUMENT;
+    if (count == 0) return LCD_OK;
+    const int blocks = (int)((count + 1023) / 1024 < 148 * 16 ? (count + 1023) / 1024 : 148 * 16);
+    fill_u64_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<unsigned long long *>(dst), count, value);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_transpose_f64(int64_t rows, int64_t cols, const double *in, int64_t ld_in,
+                                 double *out, int64_t ld_out, void *stream) {
+    if (rows < 0 || cols < 0 || ld_in < cols || ld_out < rows) return LCD_ERR_INVALID_ARGUMENT;
+    if (rows == 0 || cols == 0) return LCD_OK;
+    const long long gx = (cols + 31) / 32, gy = (rows + 31) / 32;
+    if (gy > 65535) {
+        // split the row range so that gridDim.y stays legal
+        const int64_t step = 65535LL * 32;
+        for (int64_t r = 0; r < rows; r += step) {
+            const int64_t part = rows - r < step ? rows - r : step;
+            dim3 grid((unsigned)gx, (unsigned)((part + 31) / 32));
+            transpose_f64_kernel<<<grid, dim3(32, 8), 0, (cudaStream_t)stream>>>(
+                part, cols, in + r * ld_in, ld_in, out + r, ld_out);
+        }
+    } else {
+        dim3 grid((unsigned)gx, (unsigned)gy);
+        transpose_f64_kernel<<<grid, dim3(32, 8), 0, (cudaStream_t)stream>>>(rows, cols, in, ld_in,
+                                                                           out, ld_out);
+    }
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap,
+                                       const int32_t *Ai, const double *Ax,
+                                       const int32_t *diag_pos, const double *b, double *x,
+                                       int flags, int lanes_per_row, int threads_per_block,
+                                       int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                       int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_OF_FULL) && !diag_pos) return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_UNIT_DIAG) && !(flags & LCD_SOLVE_OF_FULL))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !b || !x || (nnz > 0 && (!Ai || !Ax)))) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && x == b) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int G = lanes_per_row > 0 ? lanes_per_row : pick_lanes(nnz, n);
+    if (flags & LCD_SOLVE_EXACT) G = 1;
+    int tpb = threads_per_block > 0 ? threads_per_block : 1024;
+    if (tpb != 256 && tpb != 512 && tpb != 1024) return LCD_ERR_INVALID_ARGUMENT;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
+        CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
+                         timeout_ns(timeout_ms)};
+        cudaError_t e;
+        switch (G) {
+            case 1:
+                e = g_row_tuning.variant == 0 ? launch_csr_row(p, tpb, st) : launch_csr<1>(p, tpb, st);
+                break;
+            case 2: e = launch_csr<2>(p, tpb, st); break;
+            case 4: e = launch_csr<4>(p, tpb, st); break;
+            case 8: e = launch_csr<8>(p, tpb, st); break;
+            case 16: e = launch_csr<16>(p, tpb, st); break;
+            case 32: e = launch_csr<32>(p, tpb, st); break;
+            default: return LCD_ERR_INVALID_ARGUMENT;
+        }
+        LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_sptrsv_csr_syncfree_multi(int32_t n, int64_t nnz, int32_t nrhs,
+                                             const int32_t *Ap, const int32_t *Ai,
+                                             const double *Ax, const int32_t *diag_pos,
+                                             const double *B, double *X, int64_t ld, int flags,
+                                             int32_t *status_dev, int32_t timeout_ms,
+                                             void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || nrhs < 1 || nrhs > 64 || ld < nrhs || !status_dev)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_OF_FULL) && !diag_pos) return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_UNIT_DIAG) && !(flags & LCD_SOLVE_OF_FULL))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !B || !X || X == B)) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        // X may be strided (ld > nrhs): fill the whole block, padding included.
+        LCD_CUDA_TRY(cudaMemsetAsync(X, 0xFF, (size_t)n * (size_t)ld * sizeof(double), st));
+        CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, B, X, flags, nrhs, ld, status_dev,
+                         timeout_ns(timeout_ms)};
+        cudaError_t e;
+        if (nrhs <= 1) e = launch_multi<1, 1>(p, st);
+        else if (nrhs <= 2) e = launch_multi<2, 1>(p, st);
+        else if (nrhs <= 4) e = launch_multi<4, 1>(p, st);
+        else if (nrhs <= 8) e = launch_multi<8, 1>(p, st);
+        else if (nrhs <= 16) e = launch_multi<16, 1>(p, st);
+        else if (nrhs <= 32) e = launch_multi<32, 1>(p, st);
+        else e = launch_multi<32, 2>(p, st);
+        LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_csc_edge_count(int32_t n, const int32_t *Ap, const int32_t *Ai, int flags,
+                                  int32_t *edge_count, void *stream) {
+    if (n < 0 || (n > 0 && (!Ap || !edge_count))) return LCD_ERR_INVALID_ARGUMENT;
+    if (n == 0) return LCD_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    LCD_CUDA_TRY(cudaMemsetAsync(edge_count, 0, (size_t)n * sizeof(int32_t), st));
+    csc_edge_count_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, Ap, Ai,
+                                                          (flags & LCD_SOLVE_UPPER) ? 1 : 0,
+                                                          edge_count);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_sptrsv_csc_syncfree(int32_t n, int64_t nnz, const int32_t *Ap,
+                                       const int32_t *Ai, const double *Ax, const double *b,
+                                       double *x, int32_t *dep_count, int flags,
+                                       int lanes_per_col, int32_t *status_dev,
+                                       int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !Ai || !Ax || !b || !x || !dep_count || x == b))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int G = lanes_per_col > 0 ? lanes_per_col : pick_lanes(nnz, n);
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(x, 0, (size_t)n * sizeof(double), st));
+        CscSolveParams p{n, nnz, Ap, Ai, Ax, b, x, dep_count, flags, status_dev,
+                         timeout_ns(timeout_ms)};
+        cudaError_t e;
+        switch (G) {
+            case 1: e = launch_csc<1>(p, st); break;
+            case 2: e = launch_csc<2>(p, st); break;
+            case 4: e = launch_csc<4>(p, st); break;
+            case 8: e = launch_csc<8>(p, st); break;
+            case 16: e = launch_csc<16>(p, st); break;
+            case 32: e = launch_csc<32>(p, st); break;
+            default: return LCD_ERR_INVALID_ARGUMENT;
+        }
+        LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}

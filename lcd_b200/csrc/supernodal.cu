@@ -1,0 +1,196 @@
+// Sync-free supernodal lower-triangular solve on column-major panels (sm_100a).
+//
+// Work is cut into tasks handed out by ticket in supernode order (a topological
+// order): task (s, 0) waits until every update into the columns of supernode s
+// has arrived (pending[s] == 0), solves the dense w x w diagonal block in 32-column
+// steps (a warp solves the 32 x 32 triangle with shuffles, the block then applies
+// the 32 solved values to the rows below), publishes x_s and raises solved[s];
+// tasks (s, q) stream one strip of the off-diagonal panel (coalesced down the
+// columns), subtract the strip's product from x with fp64 atomics and release
+// the target supernodes' counters, one decrement per distinct target per warp.
+// The solve is HBM-bound: every panel value is read exactly once.
+#include "common.cuh"
+
+namespace lcd {
+
+constexpr int kSnThreads = 256;
+constexpr int kSnMaxWidth = 1024;  // x_s lives in shared memory
+
+struct SupernodalParams {
+    int n_super;
+    int n_tasks;
+    const int *__restrict__ task_super;
+    const int *__restrict__ task_strip;
+    const int *__restrict__ sn;
+    const int *__restrict__ Lip;
+    const int *__restrict__ Li;
+    const long long *__restrict__ Lp;
+    const double *__restrict__ Lx;
+    const int *__restrict__ col_to_super;
+    int *pending;
+    int *solved;
+    double *x;
+    int n;
+    int32_t *status;
+    unsigned long long budget_ns;
+};
+
+__global__ void __launch_bounds__(kSnThreads) supernodal_kernel(const SupernodalParams p) {
+    __shared__ double xs[kSnMaxWidth];
+    __shared__ int s_task;
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) s_task = atomicAdd(&p.status[kStatusTicket], 1);
+    __syncthreads();
+    const int task = s_task;
+    if (task >= p.n_tasks) return;
+    const int s = __ldg(p.task_super + task);
+    const int strip = __ldg(p.task_strip + task);
+    const int c0 = __ldg(p.sn + s), w = __ldg(p.sn + s + 1) - c0;
+    const int row_begin = __ldg(p.Lip + s);
+    const int len = __ldg(p.Lip + s + 1) - row_begin;
+    const double *M = p.Lx + __ldg(p.Lp + c0);
+    if (w <= 0 || w > kSnMaxWidth || len < w) {
+        if (tid == 0) raise_error(p.status, w > kSnMaxWidth ? LCD_ERR_TOO_LARGE : LCD_ERR_BAD_POINTERS, s);
+        return;
+    }
+    // ---- wait for the inputs of this task --------------------------------
+    if (tid == 0) {
+        Deadline dl;
+        dl.start(p.budget_ns);
+        int ok = 1;
+        const int *flag = strip == 0 ? p.pending + s : p.solved + s;
+        const int want_zero = strip == 0;
+        for (;;) {
+            const int v = ld_acquire_s32(flag);
+            if (want_zero ? v == 0 : v != 0) break;
+            if (dl.tick(p.status, s)) { ok = 0; break; }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    for (int c = tid; c < w; c += kSnThreads) xs[c] = ld_relaxed_f64(p.x + c0 + c);
+    __syncthreads();
+    if (strip == 0) {
+        // ---- dense triangular solve, 32 columns at a time --------------------
+        for (int cb = 0; cb < w; cb += 32) {
+            const int bw = min(32, w - cb);
+            if (warp == 0) {
+                const int r = cb + lane;  // row of this lane inside the diagonal block
+                double m[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    m[c] = (lane < bw && c <= lane) ? __ldg(M + (long long)(cb + c) * len + r) : 1.0;
+                double v = lane < bw ? xs[r] : 0.0;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    if (lane == c) v = v / m[c];
+                    const double xc = __shfl_sync(0xffffffffu, v, c);
+                    if (lane > c && c < bw) v = fma(-m[c], xc, v);
+                }
+                if (lane < bw) xs[r] = v;
+            }
+            __syncthreads();
+            for (int r = cb + 32 + tid; r < w; r += kSnThreads) {
+                double v = xs[r];
+#pragma unroll 8
+                for (int c = 0; c < bw; ++c)
+                    v = fma(-__ldg(M + (long long)(cb + c) * len + r), xs[cb + c], v);
+                xs[r] = v;
+            }
+            __syncthreads();
+        }
+        for (int c = tid; c < w; c += kSnThreads) st_relaxed_f64(p.x + c0 + c, xs[c]);
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            st_release_s32(p.solved + s, 1);
+        }
+    }
+    // ---- one strip of the off-diagonal panel -------------------------------
+    const int rows = len - w;
+    const int j = strip * kSnThreads + tid;
+    const bool active = j < rows;
+    int target = -1;
+    if (active) {
+        const double *P = M + w + j;
+        double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+        int c = 0;
+        for (; c + 4 <= w; c += 4) {
+            acc0 = fma(__ldg(P + (long long)(c + 0) * len), xs[c + 0], acc0);
+            acc1 = fma(__ldg(P + (long long)(c + 1) * len), xs[c + 1], acc1);
+            acc2 = fma(__ldg(P + (long long)(c + 2) * len), xs[c + 2], acc2);
+            acc3 = fma(__ldg(P + (long long)(c + 3) * len), xs[c + 3], acc3);
+        }
+        for (; c < w; ++c) acc0 = fma(__ldg(P + (long long)c * len), xs[c], acc0);
+        const int row = __ldg(p.Li + row_begin + w + j);
+        if ((unsigned)row >= (unsigned)p.n || row < c0 + w) {
+            raise_error(p.status, LCD_ERR_INDEX_RANGE, s);
+        } else {
+            red_relaxed_add_f64(p.x + row, -((acc0 + acc1) + (acc2 + acc3)));
+            target = __ldg(p.col_to_super + row);
+        }
+    }
+    // one counter decrement per distinct target supernode per warp
+    const unsigned peers = __match_any_sync(0xffffffffu, target);
+    __syncwarp();
+    if (target >= 0 && (peers & ((1u << lane) - 1u)) == 0)
+        red_release_add_s32(p.pending + target, -__popc(peers));
+}
+
+__global__ void supernodal_pending_kernel(int n_super, const int *__restrict__ sn,
+                                          const int *__restrict__ Lip, const int *__restrict__ Li,
+                                          const int *__restrict__ col_to_super, int *pending) {
+    // one warp per supernode, lanes over its off-diagonal rows
+    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (s >= n_super) return;
+    const int w = sn[s + 1] - sn[s];
+    for (int j = Lip[s] + w + lane; j < Lip[s + 1]; j += 32) atomicAdd(pending + col_to_super[Li[j]], 1);
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const int32_t *Lip,
+                                      const int32_t *Li, const int32_t *col_to_super,
+                                      int32_t *pending, void *stream) {
+    if (n_super < 0 || (n_super > 0 && (!sn || !Lip || !Li || !col_to_super || !pending)))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n_super == 0) return LCD_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    LCD_CUDA_TRY(cudaMemsetAsync(pending, 0, (size_t)n_super * sizeof(int32_t), st));
+    const long long threads = (long long)n_super * 32;
+    supernodal_pending_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+        n_super, sn, Lip, Li, col_to_super, pending);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_supernodal_strip_rows(void) { return kSnThreads; }
+
+extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
+                                     const int32_t *task_super, const int32_t *task_strip,
+                                     const int32_t *sn, const int32_t *Lip, const int32_t *Li,
+                                     const int64_t *Lp, const double *Lx,
+                                     const int32_t *col_to_super, int32_t *pending,
+                                     int32_t *solved, double *x, int32_t *status_dev,
+                                     int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || n_super < 0 || n_tasks < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
+    if (n_super > 0 && (!task_super || !task_strip || !sn || !Lip || !Li || !Lp || !Lx ||
+                        !col_to_super || !pending || !solved || !x))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n_super > 0 && n_tasks > 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(solved, 0, (size_t)n_super * sizeof(int32_t), st));
+        SupernodalParams p{n_super, n_tasks, task_super, task_strip, sn, Lip, Li,
+                           reinterpret_cast<const long long *>(Lp), Lx, col_to_super, pending,
+                           solved, x, n, status_dev, timeout_ns(timeout_ms)};
+        supernodal_kernel<<<n_tasks, kSnThreads, 0, st>>>(p);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    return finish(status_dev, st, status_host);
+}

@@ -1,0 +1,257 @@
+"""Torch-tensor front end of the C ABI: one thin function per entry point.
+
+Tensors only provide device memory and the current stream; all work happens in
+``liblcd_b200.so``.  Index tensors are ``int32``, values ``float64``, everything
+contiguous and on the same CUDA device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as nat
+from ._native import NativeError, check, ptr
+
+OPS = {"csr_lower": nat.OP_CSR_LOWER, "csc_lower": nat.OP_CSC_LOWER,
+       "ilu0_csr": nat.OP_ILU0_CSR, "csr_upper": nat.OP_CSR_UPPER,
+       "csc_upper": nat.OP_CSC_UPPER}
+
+
+def _op_code(op):
+    return OPS[op] if isinstance(op, str) else int(op)
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _require(t, dtype, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor (lcd_b200 has no CPU path)")
+    if t.dtype != dtype or not t.is_contiguous():
+        raise TypeError(f"{name} must be a contiguous {dtype} tensor")
+    return t
+
+
+def new_status(device):
+    return torch.zeros(nat.STATUS_WORDS, dtype=torch.int32, device=device)
+
+
+def read_status(status):
+    node = ctypes.c_int32(-1)
+    code = nat.load().lcd_read_status(ptr(status), _stream(), ctypes.byref(node))
+    return code, node.value
+
+
+def to_device(array, dtype=None, device="cuda"):
+    """Host array -> device tensor through pinned memory."""
+    a = np.ascontiguousarray(array, dtype=dtype)
+    return torch.from_numpy(a).to(device, non_blocking=False)
+
+
+@dataclass
+class DeviceDag:
+    """Outputs of the on-device DAG build (all int32 device tensors)."""
+
+    n: int
+    op: int
+    dep_count: torch.Tensor
+    edge_count: torch.Tensor
+    dag_ptr: torch.Tensor
+    dag_index: torch.Tensor
+    level: torch.Tensor
+    wavefronts: torch.Tensor
+    wavefront_ptr: torch.Tensor
+    n_edges: int
+    n_levels: int
+    _wavefront_ptr_host: np.ndarray | None = None
+
+    @property
+    def wavefront_ptr_host(self):
+        if self._wavefront_ptr_host is None:
+            self._wavefront_ptr_host = self.wavefront_ptr.cpu().numpy()
+        return self._wavefront_ptr_host
+
+
+def dag_build(op, ptr_t, idx_t, n=None, timeout_ms=0):
+    """Dependence DAG, level sets and topological order of one operator."""
+    op = _op_code(op)
+    _require(ptr_t, torch.int32, "ptr")
+    _require(idx_t, torch.int32, "idx")
+    n = ptr_t.numel() - 1 if n is None else int(n)
+    nnz = idx_t.numel()
+    dev = ptr_t.device
+    lib = nat.load()
+    need = ctypes.c_int64(0)
+    check(lib.lcd_dag_workspace_bytes(op, n, nnz, ctypes.byref(need)), "lcd_dag_workspace_bytes")
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    dep = torch.empty(n, **i32)
+    edge = torch.empty(n, **i32)
+    dag_ptr = torch.empty(n + 1, **i32)
+    dag_index = torch.empty(max(nnz, 1), **i32)
+    level = torch.empty(n, **i32)
+    waves = torch.empty(n, **i32)
+    wptr = torch.empty(n + 1, **i32)
+    n_edges = ctypes.c_int64(0)
+    n_levels = ctypes.c_int32(0)
+    rc = lib.lcd_dag_build(op, n, ptr(ptr_t), ptr(idx_t), nnz, ptr(dep), ptr(edge), ptr(dag_ptr),
+                           ptr(dag_index), ctypes.byref(n_edges), ptr(level), ptr(waves),
+                           ptr(wptr), ctypes.byref(n_levels), ptr(ws), need.value,
+                           int(timeout_ms), _stream())
+    check(rc, "lcd_dag_build")
+    del ws
+    return DeviceDag(n, op, dep, edge, dag_ptr, dag_index[:n_edges.value], level, waves,
+                     wptr[:n_levels.value + 1], n_edges.value, n_levels.value)
+
+
+def diag_positions(ptr_t, idx_t, status=None):
+    _require(ptr_t, torch.int32, "ptr")
+    _require(idx_t, torch.int32, "idx")
+    n = ptr_t.numel() - 1
+    pos = torch.empty(n, dtype=torch.int32, device=ptr_t.device)
+    status = new_status(ptr_t.device) if status is None else status
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_diag_positions(n, ptr(ptr_t), ptr(idx_t), idx_t.numel(), ptr(pos),
+                                       ptr(status), _stream(), ctypes.byref(host))
+    check(rc, "lcd_diag_positions")
+    return pos
+
+
+def _solve_flags(upper, unit_diag, of_full, exact):
+    return ((nat.SOLVE_UPPER if upper else 0) | (nat.SOLVE_UNIT_DIAG if unit_diag else 0)
+            | (nat.SOLVE_OF_FULL if of_full else 0) | (nat.SOLVE_EXACT if exact else 0))
+
+
+def sptrsv_csr_syncfree(Ap, Ai, Ax, b, x=None, *, upper=False, unit_diag=False, diag_pos=None,
+                        exact=False, lanes=0, threads=0, status=None, timeout_ms=0, sync=True):
+    """Sync-free CSR triangular solve; returns x (a new tensor unless given)."""
+    _require(Ap, torch.int32, "Ap")
+    _require(Ai, torch.int32, "Ai")
+    _require(Ax, torch.float64, "Ax")
+    _require(b, torch.float64, "b")
+    n = Ap.numel() - 1
+    x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
+    status = new_status(b.device) if status is None else status
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, exact)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_csr_syncfree(
+        n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
+        int(lanes), int(threads), ptr(status), int(timeout_ms), _stream(),
+        ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_csr_syncfree")
+    return x
+
+
+def sptrsv_csr_syncfree_multi(Ap, Ai, Ax, B, X=None, *, upper=False, unit_diag=False,
+                              diag_pos=None, status=None, timeout_ms=0, sync=True):
+    """Multi-RHS solve on a row-major n x nrhs block (nrhs <= 64)."""
+    _require(B, torch.float64, "B")
+    n = Ap.numel() - 1
+    if B.dim() != 2 or B.shape[0] != n:
+        raise ValueError("B must be a row-major n x nrhs tensor")
+    nrhs = B.shape[1]
+    X = torch.empty_like(B) if X is None else X
+    status = new_status(B.device) if status is None else status
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_csr_syncfree_multi(
+        n, Ai.numel(), nrhs, ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(B), ptr(X), nrhs,
+        flags, ptr(status), int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_csr_syncfree_multi")
+    return X
+
+
+def transpose(src, rows, cols, out=None):
+    """out[c, r] = src[r, c] for a row-major rows x cols block."""
+    out = torch.empty(cols, rows, dtype=torch.float64, device=src.device) if out is None else out
+    check(nat.load().lcd_transpose_f64(rows, cols, ptr(src), cols, ptr(out), rows, _stream()),
+          "lcd_transpose_f64")
+    return out
+
+
+def csc_edge_count(Ap, Ai, upper=False):
+    n = Ap.numel() - 1
+    out = torch.empty(n, dtype=torch.int32, device=Ap.device)
+    check(nat.load().lcd_csc_edge_count(n, ptr(Ap), ptr(Ai), nat.SOLVE_UPPER if upper else 0,
+                                        ptr(out), _stream()), "lcd_csc_edge_count")
+    return out
+
+
+def sptrsv_csc_syncfree(Ap, Ai, Ax, b, dep_count, x=None, *, upper=False, exact=False, lanes=0,
+                        status=None, timeout_ms=0, sync=True):
+    """Sync-free CSC solve (push protocol).  ``dep_count`` is consumed."""
+    _require(dep_count, torch.int32, "dep_count")
+    n = Ap.numel() - 1
+    x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
+    status = new_status(b.device) if status is None else status
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_csc_syncfree(
+        n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(b), ptr(x), ptr(dep_count),
+        _solve_flags(upper, False, False, exact), int(lanes), ptr(status), int(timeout_ms),
+        _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_csc_syncfree")
+    return x
+
+
+def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr_host=None,
+                     x=None, *, mode="cooperative", diag_pos=None, unit_diag=False, exact=False,
+                     lanes=1, status=None, timeout_ms=0, sync=True):
+    """Level-synchronous solve over the level sets of ``dag_build``."""
+    op = _op_code(op)
+    n = Ap.numel() - 1
+    x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
+    status = new_status(b.device) if status is None else status
+    n_levels = wavefront_ptr.numel() - 1
+    mode_code = nat.WAVEFRONT_COOPERATIVE if mode == "cooperative" else nat.WAVEFRONT_PER_LEVEL
+    host_ptr = None
+    if mode_code == nat.WAVEFRONT_PER_LEVEL:
+        if wavefront_ptr_host is None:
+            wavefront_ptr_host = wavefront_ptr.cpu().numpy()
+        wavefront_ptr_host = np.ascontiguousarray(wavefront_ptr_host, dtype=np.int32)
+        host_ptr = wavefront_ptr_host.ctypes.data_as(ctypes.c_void_p)
+    flags = _solve_flags(False, unit_diag, diag_pos is not None, exact)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_wavefront(
+        op, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
+        ptr(wavefronts), ptr(wavefront_ptr), host_ptr, n_levels, mode_code, int(lanes),
+        ptr(status), int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_wavefront")
+    return x
+
+
+def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
+               wavefront_ptr_host=None, done=None, lanes=0, status=None, timeout_ms=0, sync=True):
+    """In-place ILU(0) of a sorted CSR matrix; returns Ax."""
+    _require(Ax, torch.float64, "Ax")
+    _require(diag_pos, torch.int32, "diag_pos")
+    n = Ap.numel() - 1
+    status = new_status(Ax.device) if status is None else status
+    host = ctypes.c_int(0)
+    if mode.replace("-", "_") == "sync_free":
+        done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 0,
+                                       ptr(done), None, None, 0, int(lanes), ptr(status),
+                                       int(timeout_ms), _stream(),
+                                       ctypes.byref(host) if sync else None)
+    else:
+        wph = np.ascontiguousarray(wavefront_ptr_host, dtype=np.int32)
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 1,
+                                       None, ptr(wavefronts), wph.ctypes.data_as(ctypes.c_void_p),
+                                       len(wph) - 1, int(lanes), ptr(status), int(timeout_ms),
+                                       _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_spilu0_csr")
+    return Ax
+
+
+def fill_u64(t, value):
+    check(nat.load().lcd_fill_u64(ptr(t), t.numel() * t.element_size() // 8, value, _stream()),
+          "lcd_fill_u64")
+    return t
+
+
+__all__ = [name for name in dir() if not name.startswith("_")] + ["NativeError"]

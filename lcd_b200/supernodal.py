@@ -1,0 +1,153 @@
+"""Supernodal lower-triangular solve on the reference's supernodal layout.
+
+Layout (``utils/symbolic_cholesky_csc.py:950-1021`` of the reference): supernode
+``s`` owns columns ``[sn[s], sn[s+1])``; ``Li[Lip[s]:Lip[s+1]]`` lists its rows,
+own columns first; its values form a column-major ``len x width`` panel at
+``Lx[Lp[sn[s]]:]`` with leading dimension ``len``.  ``Lp`` is widened to int64.
+
+The solve mirrors ``benchmark/sptrsv_supernodal.py:12-28`` (sequential) and
+``:55-94`` (the sync-free CUDA kernel): dense triangular solve of the diagonal
+block, panel product, scatter-subtract into ``x``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as nat
+from ._native import check, ptr
+from .ops import _stream, new_status
+
+MAX_WIDTH = 1024
+
+
+class SupernodalError(ValueError):
+    """The supernodal arrays are inconsistent."""
+
+
+@dataclass
+class SupernodalPlan:
+    """Device-resident matrix plus the task list and initial dependency counters."""
+
+    n: int
+    n_super: int
+    n_tasks: int
+    sn: torch.Tensor
+    Lip: torch.Tensor
+    Li: torch.Tensor
+    Lp: torch.Tensor
+    Lx: torch.Tensor
+    col_to_super: torch.Tensor
+    task_super: torch.Tensor
+    task_strip: torch.Tensor
+    initial_pending: torch.Tensor
+    pending: torch.Tensor
+    solved: torch.Tensor
+    status: torch.Tensor
+    panel_values: int
+    flops: float
+
+    @property
+    def algorithmic_bytes(self):
+        """8 bytes per panel value, 4 per row index, 16 per unknown."""
+        return 8 * self.panel_values + 4 * int(self.Li.numel()) + 16 * self.n
+
+
+def _host(a, dtype):
+    if isinstance(a, torch.Tensor):
+        a = a.cpu().numpy()
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda"):
+    """Validate the layout, upload it and build the task list.
+
+    Host work is O(n_super + n); the per-row counters are accumulated on the
+    device.  ``Lx`` may already be a CUDA tensor (it is the large array).
+    """
+    sn_h = _host(sn, np.int64)
+    Lip_h = _host(Lip, np.int64)
+    Lp_h = _host(Lp, np.int64)
+    n_super = len(sn_h) - 1
+    n = int(sn_h[-1]) if n is None else int(n)
+    width = np.diff(sn_h)
+    length = np.diff(Lip_h)
+    if n_super < 0 or len(Lip_h) != n_super + 1 or len(Lp_h) < n + 1:
+        raise SupernodalError("sn, Lip and Lp have inconsistent lengths")
+    if n_super and (width.min() <= 0 or (length < width).any()):
+        raise SupernodalError("every supernode needs width > 0 and at least width rows")
+    if n_super and width.max() > MAX_WIDTH:
+        raise SupernodalError(f"supernode wider than {MAX_WIDTH} columns")
+    if col_to_super is None:
+        col_to_super = np.repeat(np.arange(n_super, dtype=np.int32), width)
+    strip_rows = nat.load().lcd_supernodal_strip_rows()
+    strips = np.maximum(1, -(-(length - width) // strip_rows))
+    task_super = np.repeat(np.arange(n_super, dtype=np.int32), strips)
+    first = np.zeros(n_super + 1, dtype=np.int64)
+    np.cumsum(strips, out=first[1:])
+    task_strip = (np.arange(int(first[-1]), dtype=np.int64) - np.repeat(first[:-1], strips))
+    dev = torch.device(device)
+
+    def up(a, dtype):
+        if isinstance(a, torch.Tensor) and a.is_cuda:
+            return a.to(dtype).contiguous()
+        return torch.from_numpy(_host(a, dtype)).to(dev)
+
+    t_sn, t_Lip = up(sn_h, np.int32), up(Lip_h, np.int32)
+    t_Li = up(Li, np.int32)
+    t_Lp = up(Lp_h, np.int64)
+    t_Lx = Lx if isinstance(Lx, torch.Tensor) and Lx.is_cuda else up(Lx, np.float64)
+    t_cts = up(col_to_super, np.int32)
+    if t_Li.numel() != int(Lip_h[-1]):
+        raise SupernodalError("Li does not match Lip")
+    if t_Li.numel() and (int(t_Li.min()) < 0 or int(t_Li.max()) >= n):
+        raise SupernodalError("row index out of range")
+    pending = torch.empty(n_super, dtype=torch.int32, device=dev)
+    check(nat.load().lcd_supernodal_pending(n_super, ptr(t_sn), ptr(t_Lip), ptr(t_Li), ptr(t_cts),
+                                            ptr(pending), _stream()), "lcd_supernodal_pending")
+    panel_values = int((width * length).sum())
+    flops = float((width * width + 2 * width * (length - width)).sum())
+    return SupernodalPlan(
+        n=n, n_super=n_super, n_tasks=int(first[-1]), sn=t_sn, Lip=t_Lip, Li=t_Li, Lp=t_Lp,
+        Lx=t_Lx, col_to_super=t_cts, task_super=up(task_super, np.int32),
+        task_strip=up(task_strip, np.int32), initial_pending=pending,
+        pending=torch.empty_like(pending),
+        solved=torch.empty(n_super, dtype=torch.int32, device=dev), status=new_status(dev),
+        panel_values=panel_values, flops=flops)
+
+
+def solve(plan: SupernodalPlan, b, x=None, timeout_ms=0, sync=True):
+    """x = L^{-1} b.  ``b`` is a CUDA float64 tensor; x is returned (device)."""
+    if x is None:
+        x = torch.empty_like(b)
+    x.copy_(b)
+    plan.pending.copy_(plan.initial_pending)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_supernodal(
+        plan.n, plan.n_super, plan.n_tasks, ptr(plan.task_super), ptr(plan.task_strip),
+        ptr(plan.sn), ptr(plan.Lip), ptr(plan.Li), ptr(plan.Lp), ptr(plan.Lx),
+        ptr(plan.col_to_super), ptr(plan.pending), ptr(plan.solved), ptr(x), ptr(plan.status),
+        int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_supernodal")
+    return x
+
+
+def sptrsv_csc_supernodal(sn_begin, col_to_sup, Lip, Li, Lp, Lx, x, flag_thread=None,
+                          max_width=None):
+    """Drop-in for ``sptrsv_csc_supernodal_numba_cuda`` of the reference
+    (``benchmark/sptrsv_supernodal.py:89-94``): solves in place on ``x`` (which
+    holds the right-hand side).  ``flag_thread`` / ``max_width`` are accepted for
+    signature compatibility; the counters are recomputed on the device."""
+    plan = analyse(sn_begin, Lip, Li, Lp, Lx, col_to_sup, n=len(x))
+    if isinstance(x, torch.Tensor) and x.is_cuda:
+        b = x.clone()
+        solve(plan, b, x)
+        return x
+    xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float64)).to(plan.Lx.device)
+    out = solve(plan, xd).cpu().numpy()
+    x[...] = out
+    return x

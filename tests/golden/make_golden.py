@@ -1,0 +1,184 @@
+"""Regenerates tests/golden/*.npz by running the REFERENCE's own pipeline.
+
+Run where the reference checkout is available:
+
+    cd <scratch dir> && PYTHONDONTWRITEBYTECODE=1 \
+      PYTHONPATH=<reference>:<this repo> python <this repo>/tests/golden/make_golden.py
+
+(the reference writes ``smt_file.smt2`` into the current directory, hence the
+scratch directory).  The fixtures hold, for small seeded inputs, the arrays the
+reference's inspector / preprocessing / undecorated operators produce; the
+tests compare the CPU oracle and the CUDA path against them.
+"""
+import ast
+import contextlib
+import io
+import os
+import sys
+
+import numpy as np
+import scipy.sparse as sp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+REF = next(p for p in sys.path if os.path.isdir(os.path.join(p, "compiler", "demo")))
+
+from lcd_b200 import generators as gen  # noqa: E402
+
+_sink = io.StringIO()
+with contextlib.redirect_stdout(_sink):
+    import ref_ops  # noqa: E402
+    from compiler.demo.spilu0 import compile_ilu0_csr, ilu0_csr  # noqa: E402
+    ilu_syncfree = compile_ilu0_csr("sync_free", 128, 1)
+    ilu_wavefront = compile_ilu0_csr("wavefront", 128, 1)
+from compiler.dag_preprocessing import (  # noqa: E402
+    preprocess_sync_free, preprocess_wavefront, preprocess_warp_tasks, wavefronts_from_dag)
+from compiler.structural_lookups import materialize_structural_lookups  # noqa: E402
+import utils.dense_blas as dense_blas  # noqa: E402
+from utils.symbolic_cholesky_csc import convert_csc_to_supernodal  # noqa: E402
+
+
+def ragged(lists):
+    flat = np.asarray([v for l in lists for v in l], dtype=np.int32)
+    ptr = np.zeros(len(lists) + 1, dtype=np.int32)
+    ptr[1:] = np.cumsum([len(l) for l in lists])
+    return ptr, flat
+
+
+def dag_record(prefix, op, args, out):
+    """Inspector + every preprocessing format for one decorated operator."""
+    with contextlib.redirect_stdout(_sink):
+        succ, sched = op.build_dag(*args)
+        plan = op.schedule_plan(*args)
+    data = plan.execution_data
+    out[prefix + "succ_ptr"], out[prefix + "succ_idx"] = ragged(succ)
+    for name in ("dep_count", "initial_dep_count", "dag_ptr", "dag_index", "wavefronts",
+                 "wavefront_ptr", "task_nodes", "task_ptr", "band_ptr"):
+        value = getattr(data, name, None)
+        if value is not None:
+            out[prefix + name] = np.asarray(value)
+    for name, value in getattr(data, "auxiliary_values", {}).items():
+        out[prefix + "aux_" + name] = np.asarray(value)
+    out[prefix + "schedule"] = np.asarray(list(map(str, plan.schedule.lowering_key)))
+    return succ, sched
+
+
+def triangular_cases():
+    cases = {}
+    cases["lap2d_g8"] = gen.laplacian2d_tril(8, seed=0)
+    cases["band_n300"] = gen.random_band_lower(300, seed=1, mean_degree=6.0, band=16)
+    cases["band_n600"] = gen.random_band_lower(600, seed=2, mean_degree=15.0, band=64)
+    cases["lap3d_g5"] = gen.laplacian3d_tril(5, seed=3)
+    return cases
+
+
+def main():
+    out_dir = HERE
+    # ---- SpTRSV, lower, CSR and CSC -------------------------------------
+    for name, tri in triangular_cases().items():
+        out = {}
+        Ap, Ai, Ax = tri.csr_arrays()
+        Cp, Ci, Cx = tri.csc_arrays()
+        n, b = tri.n, tri.b
+        out.update(csr_Ap=Ap, csr_Ai=Ai, csr_Ax=Ax, csc_Ap=Cp, csc_Ai=Ci, csc_Ax=Cx, b=b)
+        succ, dep = dag_record("csr_warp_syncfree/", ref_ops.csr_warp_syncfree, (Ap, Ai, Ax, b, n), out)
+        dag_record("csr_plain_wavefront/", ref_ops.csr_plain_wavefront, (Ap, Ai, Ax, b, n), out)
+        dag_record("csr_plain_syncfree/", ref_ops.csr_plain_syncfree, (Ap, Ai, Ax, b, n), out)
+        dag_record("csc_warp_push/", ref_ops.csc_warp_push, (Cp, Ci, Cx, b, n), out)
+        dag_record("csc_plain_wavefront/", ref_ops.csc_plain_wavefront, (Cp, Ci, Cx, b, n), out)
+        waves = wavefronts_from_dag(succ, dep)
+        out["levels_ptr"], out["levels_idx"] = ragged(waves)
+        out["x_csr"] = ref_ops.csr_warp_syncfree.original_function(Ap, Ai, Ax, b, n)
+        out["x_csc"] = ref_ops.csc_warp_push.original_function(Cp, Ci, Cx, b, n)
+        np.savez_compressed(os.path.join(out_dir, f"sptrsv_{name}.npz"), **out)
+        print("wrote", name, "n", n, "levels", len(waves))
+
+    # ---- inspector on unsorted rows with repeated entries -----------------
+    rng = np.random.default_rng(7)
+    n = 60
+    rows = []
+    for i in range(n):
+        k = int(min(rng.integers(0, 9), i))
+        cols = list(rng.integers(0, max(i, 1), size=k)) if i else []
+        rows.append([int(c) for c in cols] + [i])          # duplicates, unsorted, diag last
+    Ap, Ai = ragged(rows)
+    Ax = rng.uniform(0.5, 1.5, len(Ai))
+    b = rng.uniform(-1, 1, n)
+    out = dict(csr_Ap=Ap, csr_Ai=Ai, csr_Ax=Ax, b=b)
+    dag_record("csr_warp_syncfree/", ref_ops.csr_warp_syncfree, (Ap, Ai, Ax, b, n), out)
+    dag_record("csr_plain_wavefront/", ref_ops.csr_plain_wavefront, (Ap, Ai, Ax, b, n), out)
+    cols = [[] for _ in range(n)]
+    for i, r in enumerate(rows):
+        for c in r[:-1]:
+            cols[c].append(i)
+    cols = [[c] + list(rng.permutation(v)) for c, v in enumerate(cols)]  # diag first, unsorted
+    Cp, Ci = ragged(cols)
+    Cx = rng.uniform(0.5, 1.5, len(Ci))
+    out.update(csc_Ap=Cp, csc_Ai=Ci, csc_Ax=Cx)
+    dag_record("csc_warp_push/", ref_ops.csc_warp_push, (Cp, Ci, Cx, b, n), out)
+    dag_record("csc_plain_wavefront/", ref_ops.csc_plain_wavefront, (Cp, Ci, Cx, b, n), out)
+    out["x_csr"] = ref_ops.csr_warp_syncfree.original_function(Ap, Ai, Ax, b, n)
+    out["x_csc"] = ref_ops.csc_warp_push.original_function(Cp, Ci, Cx, b, n)
+    np.savez_compressed(os.path.join(out_dir, "sptrsv_unsorted_dups.npz"), **out)
+
+    # ---- upper triangular through the reversed-index loop -----------------
+    tri = gen.upper_from_lower(gen.random_band_lower(48, seed=4, mean_degree=4.0, band=8))
+    Ap, Ai, Ax = tri.csr_arrays()
+    out = dict(csr_Ap=Ap, csr_Ai=Ai, csr_Ax=Ax, b=tri.b)
+    dag_record("csr_upper_reversed/", ref_ops.csr_upper_reversed, (Ap, Ai, Ax, tri.b, tri.n), out)
+    out["x_csr"] = ref_ops.csr_upper_reversed.original_function(Ap, Ai, Ax, tri.b, tri.n)
+    np.savez_compressed(os.path.join(out_dir, "sptrsv_upper_n48.npz"), **out)
+
+    # ---- ILU0 CSR ---------------------------------------------------------
+    ilu_inputs = {"lap3d_g4": gen.laplacian3d_ilu0(4, seed=5)[0]}
+    rnd = sp.random(90, 90, density=0.08, random_state=6, format="csr")
+    rnd = rnd + rnd.T + sp.identity(90) * 4.0
+    rnd = sp.csr_matrix(rnd)
+    rnd.sort_indices()
+    ilu_inputs["random_n90"] = rnd
+    nodiag = sp.csr_matrix(rnd.copy())
+    nodiag = nodiag.tolil()
+    nodiag[5, 5] = 0.0
+    nodiag = sp.csr_matrix(nodiag)
+    nodiag.eliminate_zeros()
+    nodiag.sort_indices()
+    ilu_inputs["missing_diag_n90"] = nodiag
+    for name, mat in ilu_inputs.items():
+        data = mat.data.astype(np.float64)
+        indices = mat.indices.astype(np.int32)
+        indptr = mat.indptr.astype(np.int32)
+        out = dict(data=data, indices=indices, indptr=indptr)
+        dag_record("ilu_syncfree/", ilu_syncfree, (data.copy(), indices, indptr), out)
+        dag_record("ilu_wavefront/", ilu_wavefront, (data.copy(), indices, indptr), out)
+        lookups = materialize_structural_lookups(
+            ilu_syncfree.structural_lookups, dict(A_indptr=indptr, A_indices=indices))
+        (out["diag_pos"],) = [np.asarray(v) for v in lookups.values()]
+        out["factored"] = ilu0_csr(data.copy(), indices, indptr)
+        np.savez_compressed(os.path.join(out_dir, f"ilu0_{name}.npz"), **out)
+        print("wrote ilu0", name)
+
+    # ---- supernodal solve ------------------------------------------------
+    source = open(os.path.join(REF, "benchmark", "sptrsv_supernodal.py")).read()
+    fn = next(node for node in ast.parse(source).body
+              if isinstance(node, ast.FunctionDef) and node.name == "sptrv_csc_supernodal")
+    ns = dict(lsolve_dense_col_order=dense_blas.lsolve_dense_col_order,
+              dense_matvec_col_order=dense_blas.dense_matvec_col_order)
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), "<supernodal>", "exec"), ns)
+    for name, kw in {"n200": dict(n=200, seed=8, widths=(2, 3, 4, 8), min_targets=1, max_targets=4),
+                     "n360": dict(n=360, seed=9, widths=(16, 32), min_targets=2, max_targets=4)}.items():
+        s = gen.supernodal_random(**kw)
+        x = s.b.copy()
+        ns["sptrv_csc_supernodal"](s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b, x)
+        out = dict(sn=s.sn, Lip=s.Lip, Li=s.Li, Lp=s.Lp, Lx=s.Lx, b=s.b, x=x,
+                   col_to_super=s.col_to_super)
+        # layout cross-check: the reference's own CSC -> supernodal converter
+        with contextlib.redirect_stdout(_sink):
+            Ls = convert_csc_to_supernodal(s.to_csc(), relaxation=0)
+        out["conv_supernodes"] = Ls["supernodes"]
+        out["conv_i"], out["conv_ip"], out["conv_p"], out["conv_x"] = Ls["i"], Ls["ip"], Ls["p"], Ls["x"]
+        np.savez_compressed(os.path.join(out_dir, f"supernodal_{name}.npz"), **out)
+        print("wrote supernodal", name, s.n_super)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,109 @@
+"""The CPU oracle against fixtures produced by the reference's own pipeline."""
+import numpy as np
+import pytest
+
+from conftest import golden, golden_names
+
+SPTRSV = golden_names("sptrsv_")
+ILU = golden_names("ilu0_")
+SUPER = golden_names("supernodal_")
+
+
+def _check_dag(d, g, prefix, edge_multiplicity=False):
+    np.testing.assert_array_equal(d.dag_ptr, g[prefix + "succ_ptr"])
+    np.testing.assert_array_equal(d.dag_index, g[prefix + "succ_idx"])
+    if prefix + "dag_ptr" in g:
+        np.testing.assert_array_equal(d.dag_ptr, g[prefix + "dag_ptr"])
+        np.testing.assert_array_equal(d.dag_index, g[prefix + "dag_index"])
+    if prefix + "dep_count" in g:
+        want = d.edge_count if edge_multiplicity else d.dep_count
+        np.testing.assert_array_equal(want, g[prefix + "dep_count"])
+        np.testing.assert_array_equal(want, g[prefix + "initial_dep_count"])
+    if prefix + "wavefronts" in g:
+        np.testing.assert_array_equal(d.wavefronts, g[prefix + "wavefronts"])
+        np.testing.assert_array_equal(d.wavefront_ptr, g[prefix + "wavefront_ptr"])
+    if prefix + "task_nodes" in g:
+        np.testing.assert_array_equal(d.wavefronts, g[prefix + "task_nodes"])
+        np.testing.assert_array_equal(d.wavefront_ptr, g[prefix + "band_ptr"])
+        np.testing.assert_array_equal(np.arange(len(d.dep_count) + 1), g[prefix + "task_ptr"])
+    assert not d.cyclic
+
+
+@pytest.mark.parametrize("name", SPTRSV)
+def test_dag_arrays_match_reference(oracle, name):
+    g = golden(name)
+    if "csr_upper_reversed/succ_ptr" in g:
+        d = oracle.dag_build("csr_upper", g["csr_Ap"], g["csr_Ai"])
+        _check_dag(d, g, "csr_upper_reversed/")
+        return
+    d = oracle.dag_build("csr_lower", g["csr_Ap"], g["csr_Ai"])
+    for variant in ("csr_warp_syncfree/", "csr_plain_wavefront/", "csr_plain_syncfree/"):
+        if variant + "succ_ptr" in g:
+            _check_dag(d, g, variant)
+    d = oracle.dag_build("csc_lower", g["csc_Ap"], g["csc_Ai"])
+    _check_dag(d, g, "csc_warp_push/", edge_multiplicity=True)
+    _check_dag(d, g, "csc_plain_wavefront/")
+    if "levels_ptr" in g:
+        np.testing.assert_array_equal(d.wavefronts, g["levels_idx"])
+        np.testing.assert_array_equal(d.wavefront_ptr, g["levels_ptr"])
+
+
+@pytest.mark.parametrize("name", SPTRSV)
+def test_sptrsv_matches_undecorated_reference(oracle, name):
+    g = golden(name)
+    if "csr_upper_reversed/succ_ptr" in g:
+        x = oracle.sptrsv_csr_upper(g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"])
+        np.testing.assert_array_equal(x, g["x_csr"])  # same arithmetic, same order: bit-exact
+        return
+    x = oracle.sptrsv_csr_lower(g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"])
+    np.testing.assert_array_equal(x, g["x_csr"])
+    x = oracle.sptrsv_csc_lower(g["csc_Ap"], g["csc_Ai"], g["csc_Ax"], g["b"])
+    np.testing.assert_array_equal(x, g["x_csc"])
+
+
+@pytest.mark.parametrize("name", ILU)
+def test_ilu0_matches_reference(oracle, name):
+    g = golden(name)
+    pos, rc = oracle.diag_positions(g["indptr"], g["indices"])
+    assert rc == 0
+    np.testing.assert_array_equal(pos, g["diag_pos"])
+    np.testing.assert_array_equal(pos, g["ilu_syncfree/aux__lcd_lookup_position_0"])
+    out = oracle.ilu0_csr(g["indptr"], g["indices"], g["data"])
+    np.testing.assert_array_equal(out, g["factored"])
+    fast = oracle.ilu0_csr(g["indptr"], g["indices"], g["data"], fast=True)
+    np.testing.assert_array_equal(fast, g["factored"])
+    d = oracle.dag_build("ilu0_csr", g["indptr"], g["indices"])
+    _check_dag(d, g, "ilu_syncfree/")
+    _check_dag(d, g, "ilu_wavefront/")
+
+
+@pytest.mark.parametrize("name", SUPER)
+def test_supernodal_matches_reference(oracle, name):
+    g = golden(name)
+    x = oracle.sptrsv_supernodal(g["sn"], g["Lip"], g["Li"], g["Lp"], g["Lx"], g["b"])
+    np.testing.assert_allclose(x, g["x"], rtol=1e-14, atol=1e-15)
+
+
+def test_reference_unit_test_vectors(oracle):
+    # compiler/transform_tests/test_dag_codegen.py:113-167 (CSR and CSC, one repeated entry)
+    d = oracle.dag_build("csr_lower", [0, 1, 3, 6, 9], [0, 0, 1, 0, 1, 2, 1, 2, 3])
+    np.testing.assert_array_equal(d.dep_count, [0, 1, 2, 2])
+    np.testing.assert_array_equal(d.dag_ptr, [0, 2, 4, 5, 5])
+    np.testing.assert_array_equal(d.dag_index, [1, 2, 2, 3, 3])
+    d = oracle.dag_build("csc_lower", [0, 4, 7, 9, 10], [0, 1, 2, 2, 1, 2, 3, 2, 3, 3])
+    np.testing.assert_array_equal(d.dep_count, [0, 1, 2, 2])
+    np.testing.assert_array_equal(d.dag_index, [1, 2, 2, 3, 3])
+    # :204-226 wavefronts of the CSC chain
+    d = oracle.dag_build("csc_lower", [0, 3, 6, 8, 9], [0, 1, 2, 1, 2, 3, 2, 3, 3])
+    np.testing.assert_array_equal(d.wavefronts, [0, 1, 2, 3])
+    np.testing.assert_array_equal(d.wavefront_ptr, [0, 1, 2, 3, 4])
+    # compiler/transform_tests/test_spilu0_codegen.py:159-167 dense 3x3
+    d = oracle.dag_build("ilu0_csr", [0, 3, 6, 9], [0, 1, 2, 0, 1, 2, 0, 1, 2])
+    np.testing.assert_array_equal(d.dep_count, [0, 1, 2])
+    np.testing.assert_array_equal(d.dag_index, [1, 2, 2])
+    # compiler/transform_tests/test_structural_lookups.py:64-92
+    pos, rc = oracle.diag_positions([0, 2, 3, 5], [0, 2, 0, 1, 2])
+    assert rc == 0
+    np.testing.assert_array_equal(pos, [0, -1, 4])
+    _, rc = oracle.diag_positions([0, 2], [1, 0])
+    assert rc == 2  # unsorted segment -> StructuralLookupError in the reference
