@@ -225,12 +225,24 @@ enum {
     LCD_TUNE_SLEEP_LOCAL_NS = 0,  /* pause after a failed poll inside the own chunk */
     LCD_TUNE_SLEEP_GLOBAL_NS = 1, /* pause after a failed poll of another chunk's row */
     LCD_TUNE_GAP_NS = 2,          /* extra pause per row the producer's warp still owes */
-    LCD_TUNE_ROW_VARIANT = 3      /* 0: thread-per-row kernel, 1: generic lane-group kernel */
+    LCD_TUNE_ROW_VARIANT = 3,     /* 0: thread-per-row kernel, 1: generic lane-group kernel */
+    LCD_TUNE_STAGE_PERCENT = 4    /* shared-memory staging of a chunk's matrix entries, in percent
+                                     of the average chunk size (0 = read entries from global) */
 };
 int lcd_set_tuning(int key, int value);
+/* Profiling aid (no reference counterpart): with a non-NULL device array of n 64-bit
+ * words, the one-lane-per-row solver records the SM cycle counter at which each node
+ * was published.  Pass NULL to switch it off again. */
+int lcd_debug_set_trace(long long *trace_dev);
 
 /* ---- small device utilities used by the host layer ---------------------------- */
 int lcd_fill_u64(uint64_t *dst, int64_t count, uint64_t value, void *stream);
+/* 128-bit order-sensitive checksum of an int32 device array, used as the plan-cache
+ * key in place of the host-side content hash of compiler/scheduler.py:678-711.
+ * out_dev: two 64-bit words of device scratch; out_host (optional): the result,
+ * read back after synchronising the stream. */
+int lcd_checksum_i32(const int32_t *data, int64_t count, uint64_t *out_dev, uint64_t *out_host,
+                     void *stream);
 int lcd_device_sm_count(int *sm_count);
 
 #ifdef __cplusplus

@@ -20,7 +20,7 @@ OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER = range(5)
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
 WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
-TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT = range(4)
+TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT = range(5)
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -67,6 +67,8 @@ _SIGNATURES = {
     "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
                                       _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_set_tuning": (c_int, [c_int, c_int]),
+    "lcd_debug_set_trace": (c_int, [_P]),
+    "lcd_checksum_i32": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_uint64 * 2), _P]),
     "lcd_fill_u64": (c_int, [_P, c_int64, c_uint64, _P]),
     "lcd_device_sm_count": (c_int, [ctypes.POINTER(c_int)]),
 }

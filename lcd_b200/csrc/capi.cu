@@ -39,9 +39,58 @@ int sm_count() {
     return cached;
 }
 
+// 128-bit order-sensitive checksum of an int32 array: every element is mixed with
+// its position (splitmix64 finaliser) and the mixes are combined by sum and xor.
+__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void checksum_i32_kernel(const int *__restrict__ data, long long count,
+                                    unsigned long long *out) {
+    unsigned long long sum = 0, fold = 0;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
+        const unsigned long long m =
+            mix64(((unsigned long long)k << 32) ^ (unsigned long long)(unsigned)data[k]);
+        sum += m;
+        fold ^= mix64(m + (unsigned long long)k);
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        fold ^= __shfl_xor_sync(0xffffffffu, fold, off);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicAdd(out, sum);
+        atomicXor(out + 1, fold);
+    }
+}
+
 }  // namespace lcd
 
 using namespace lcd;
+
+extern "C" int lcd_checksum_i32(const int32_t *data, int64_t count, uint64_t *out_dev,
+                                uint64_t *out_host, void *stream) {
+    if (count < 0 || !out_dev || (count > 0 && !data)) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    LCD_CUDA_TRY(cudaMemsetAsync(out_dev, 0, 2 * sizeof(uint64_t), st));
+    if (count > 0) {
+        long long blocks = (count + 1023) / 1024;
+        if (blocks > 148 * 8) blocks = 148 * 8;
+        checksum_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+            data, count, reinterpret_cast<unsigned long long *>(out_dev));
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    if (out_host) {
+        LCD_CUDA_TRY(cudaMemcpyAsync(out_host, out_dev, 2 * sizeof(uint64_t),
+                                     cudaMemcpyDeviceToHost, st));
+        LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return LCD_OK;
+}
 
 extern "C" const char *lcd_error_string(int code) {
     switch (code) {

@@ -133,6 +133,7 @@ struct CsrSolveParams {
     long long ld;
     int32_t *status;
     unsigned long long budget_ns;
+    long long *trace;  // optional: per-row SM cycle counter at publication (profiling aid)
 };
 
 // Off-diagonal range [lo, hi) and diagonal position d (-1: implicit unit) of a row.

@@ -107,8 +107,10 @@ struct RowTuning {
     int gap_ns;           // pause per row of distance between the awaited row and the
                           // progress of the warp that owns it (0 = off)
     int variant;          // 0: thread-per-row kernel for one lane per row, 1: generic kernel
+    int stage_percent;    // staging area for matrix entries, percent of the average chunk
 };
-static RowTuning g_row_tuning = {0, 200, 40, 0};
+static RowTuning g_row_tuning = {0, 200, 0, 0, 120};
+static long long *g_trace = nullptr;
 
 // Thread per row.  Leading operands that live before the chunk and are already
 // available are consumed first without waiting; everything else goes through a
@@ -119,9 +121,13 @@ static RowTuning g_row_tuning = {0, 200, 40, 0};
 // the threads on the critical chain need.
 template <int TPB, int MINB>
 __global__ void __launch_bounds__(TPB, MINB)
-csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
+csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int cap) {
     constexpr int kWarps = TPB / 32;
-    __shared__ double sx[TPB];
+    // dynamic shared memory: x mirror of the chunk | staged values | staged indices
+    extern __shared__ __align__(16) unsigned char row_smem[];
+    double *sx = reinterpret_cast<double *>(row_smem);
+    double *sval = sx + TPB;
+    int *sidx = reinterpret_cast<int *>(sval + cap);
     __shared__ int s_wdone[kWarps];
     __shared__ int s_chunk;
     const int tid = threadIdx.x;
@@ -133,8 +139,29 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
     volatile int *wdone = s_wdone;
     const int row0 = s_chunk * TPB;
     const int task = row0 + tid;
-    if (task >= p.n) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
+    // The rows of a chunk are contiguous in the matrix, so their entries form one
+    // segment of Ai / Ax: stage it with coalesced loads before anybody waits, so
+    // that no matrix fetch sits on a dependence chain.
+    const int task_end = min(row0 + TPB, p.n);
+    const int first_row = upper ? p.n - task_end : row0;
+    const int last_row = upper ? p.n - 1 - row0 : task_end - 1;
+    long long seg_begin = 0;
+    int count = 0;
+    if (task_end > row0) {
+        seg_begin = __ldg(p.Ap + first_row);
+        const long long seg_end = __ldg(p.Ap + last_row + 1);
+        if (seg_begin >= 0 && seg_end >= seg_begin && seg_end <= p.nnz)
+            count = (int)min((long long)cap, seg_end - seg_begin);
+        else
+            seg_begin = 0;
+    }
+    for (int k = tid; k < count; k += TPB) {
+        sidx[k] = __ldg(p.Ai + seg_begin + k);
+        sval[k] = __ldg(p.Ax + seg_begin + k);
+    }
+    __syncthreads();
+    if (task >= p.n) return;
     const bool exact = p.flags & LCD_SOLVE_EXACT;
     const int r = upper ? p.n - 1 - task : task;
     int lo = 0, hi = 0, d = -1;
@@ -146,9 +173,10 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
         lo = hi = 0;
         d = -1;
     }
+    const int sbase = (int)seg_begin;  // seg_begin <= nnz < 2^31
     double acc = __ldg(p.b + r);
     double dv = 1.0, rinv = 1.0;
-    if (d >= 0) dv = __ldg(p.Ax + d);
+    if (d >= 0) dv = ((unsigned)(d - sbase) < (unsigned)count) ? sval[d - sbase] : __ldg(p.Ax + d);
     if (!exact) rinv = 1.0 / dv;
     int j = lo;
     int cl = 0, c = 0;  // cl: operand's position relative to the chunk (>= 0: mirrored)
@@ -156,8 +184,14 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
     bool have = j < hi;
 #define LCD_FETCH_OPERAND()                                                  \
     do {                                                                     \
-        c = __ldg(p.Ai + j);                                                 \
-        a = __ldg(p.Ax + j);                                                 \
+        const unsigned pos_ = (unsigned)(j - sbase);                         \
+        if (pos_ < (unsigned)count) {                                        \
+            c = sidx[pos_];                                                  \
+            a = sval[pos_];                                                  \
+        } else {                                                             \
+            c = __ldg(p.Ai + j);                                             \
+            a = __ldg(p.Ax + j);                                             \
+        }                                                                    \
         const int tc_ = upper ? p.n - 1 - c : c;                             \
         if ((unsigned)tc_ >= (unsigned)task) {                               \
             raise_error(p.status, LCD_ERR_INDEX_RANGE, r);                   \
@@ -207,7 +241,8 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune) {
             val = publishable(val);
             sxv[tid] = val;
             st_relaxed_f64(p.x + r, val);
-            atomicAdd(&s_wdone[tid >> 5], 1);
+            if (tune.gap_ns) atomicAdd(&s_wdone[tid >> 5], 1);
+            if (p.trace) p.trace[task] = clock64();
             break;
         }
     }
@@ -423,14 +458,41 @@ static int pick_lanes(long long nnz, int n) {
     return 32;
 }
 
-static cudaError_t launch_csr_row(const CsrSolveParams &p, int tpb, cudaStream_t st) {
-    if (tpb == 1024)
-        csr_syncfree_row_kernel<1024, 1><<<(p.n + 1023) / 1024, 1024, 0, st>>>(p, g_row_tuning);
-    else if (tpb == 512)
-        csr_syncfree_row_kernel<512, 2><<<(p.n + 511) / 512, 512, 0, st>>>(p, g_row_tuning);
-    else
-        csr_syncfree_row_kernel<256, 4><<<(p.n + 255) / 256, 256, 0, st>>>(p, g_row_tuning);
+// Shared memory of the thread-per-row kernel: the x mirror plus room for the
+// chunk's matrix entries (12 bytes each).  `stage` scales the staging area
+// relative to the average chunk (0 disables staging).
+static size_t row_kernel_smem(int tpb, long long nnz, int n, int *cap_out) {
+    const size_t limit = 227 * 1024 - 256;
+    const double avg = n > 0 ? (double)nnz / n : 0.0;
+    long long cap = g_row_tuning.stage_percent > 0
+                        ? (long long)(avg * tpb * g_row_tuning.stage_percent / 100.0) + 256 : 0;
+    const long long max_cap = ((long long)limit - (long long)tpb * 8) / 12;
+    if (cap > max_cap) cap = max_cap;
+    cap &= ~1ll;  // keeps the index area 8-byte aligned
+    *cap_out = (int)cap;
+    return (size_t)tpb * 8 + (size_t)cap * 12;
+}
+
+template <int TPB, int MINB>
+static cudaError_t launch_csr_row_t(const CsrSolveParams &p, cudaStream_t st) {
+    int cap = 0;
+    const size_t smem = row_kernel_smem(TPB, p.nnz, p.n, &cap);
+    static size_t configured = 0;
+    if (smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(csr_syncfree_row_kernel<TPB, MINB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(227 * 1024 - 256));
+        if (e != cudaSuccess) return e;
+        configured = 227 * 1024;
+    }
+    csr_syncfree_row_kernel<TPB, MINB><<<(p.n + TPB - 1) / TPB, TPB, smem, st>>>(p, g_row_tuning, cap);
     return cudaGetLastError();
+}
+
+static cudaError_t launch_csr_row(const CsrSolveParams &p, int tpb, cudaStream_t st) {
+    if (tpb == 1024) return launch_csr_row_t<1024, 1>(p, st);
+    if (tpb == 512) return launch_csr_row_t<512, 2>(p, st);
+    return launch_csr_row_t<256, 4>(p, st);
 }
 
 template <int G>
@@ -473,8 +535,16 @@ extern "C" int lcd_set_tuning(int key, int value) {
         case LCD_TUNE_SLEEP_GLOBAL_NS: g_row_tuning.sleep_global_ns = value; break;
         case LCD_TUNE_GAP_NS: g_row_tuning.gap_ns = value; break;
         case LCD_TUNE_ROW_VARIANT: g_row_tuning.variant = value; break;
+        case LCD_TUNE_STAGE_PERCENT: g_row_tuning.stage_percent = value; break;
         default: return LCD_ERR_INVALID_ARGUMENT;
     }
+    return LCD_OK;
+}
+
+// Profiling aid: when set, the one-lane-per-row kernel stores the SM cycle counter
+// at which each row was published into trace[node] (n 64-bit words).
+extern "C" int lcd_debug_set_trace(long long *trace_dev) {
+    g_trace = trace_dev;
     return LCD_OK;
 }
 
@@ -533,7 +603,7 @@ extern "C" int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap
     if (n > 0) {
         LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
         CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
-                         timeout_ns(timeout_ms)};
+                         timeout_ns(timeout_ms), g_trace};
         cudaError_t e;
         switch (G) {
             case 1:
@@ -570,7 +640,7 @@ extern "C" int lcd_sptrsv_csr_syncfree_multi(int32_t n, int64_t nnz, int32_t nrh
         // X may be strided (ld > nrhs): fill the whole block, padding included.
         LCD_CUDA_TRY(cudaMemsetAsync(X, 0xFF, (size_t)n * (size_t)ld * sizeof(double), st));
         CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, B, X, flags, nrhs, ld, status_dev,
-                         timeout_ns(timeout_ms)};
+                         timeout_ns(timeout_ms), nullptr};
         cudaError_t e;
         if (nrhs <= 1) e = launch_multi<1, 1>(p, st);
         else if (nrhs <= 2) e = launch_multi<2, 1>(p, st);

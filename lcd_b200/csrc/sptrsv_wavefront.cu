@@ -199,7 +199,7 @@ extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_
         if (csc) LCD_CUDA_TRY(cudaMemsetAsync(x, 0, (size_t)n * sizeof(double), st));
         WavefrontParams w;
         w.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
-                             timeout_ns(timeout_ms)};
+                             timeout_ns(timeout_ms), nullptr};
         w.csc = csc ? 1 : 0;
         w.wavefronts = wavefronts;
         w.wavefront_ptr = wavefront_ptr_dev;

@@ -1,0 +1,341 @@
+"""Prepare host values and device arrays for the native launchers, launch, and
+restore the decorated function's return semantics.
+
+Same contract as the reference's ``compiler/cuda_runtime.py``
+(``compile_cuda_module`` ``:70-125``, ``prepare_cuda_arguments`` ``:128-181``,
+``evaluate_host_prelude`` ``:184-199``, ``execute_cuda_call`` ``:202-228``):
+
+* launcher arguments are positional, in ``lowering.launcher_arguments`` order;
+* scalars stay host values, anything exposing ``__cuda_array_interface__`` passes
+  through untouched, lists/tuples/ndarrays are copied to the device, everything
+  else raises :class:`CUDARuntimePreparationError` (``:391-401``);
+* ``wavefront_ptr`` and ``band_ptr`` stay on the host (``:16``);
+* after the launch the runtime synchronises, copies returned arguments and lifted
+  locals back (``copy_to_host`` when the value has it) and evaluates the removed
+  host epilogue (``:215-228``, ``:267-304``).
+
+Device memory and streams come from torch; the "module" bound by
+``compile_cuda_module`` is the pair of Python callables that forward to the C ABI.
+"""
+
+from __future__ import annotations
+
+import ast
+from copy import deepcopy
+from dataclasses import dataclass
+
+import numpy as np
+
+from .dag_preprocessing import (SyncFreeExecutionData, WarpTaskExecutionData,
+                                WavefrontExecutionData)
+
+HOST_LAUNCH_ARGUMENTS = frozenset({"wavefront_ptr", "band_ptr"})
+
+
+class CUDARuntimePreparationError(Exception):
+    """Lowered launcher arguments cannot be prepared."""
+
+
+class CUDAModuleCompilationError(Exception):
+    """A native kernel binding cannot be created."""
+
+
+class DeviceArray:
+    """A CUDA tensor with the two members the runtime contract relies on:
+    ``__cuda_array_interface__`` and ``copy_to_host()``."""
+
+    def __init__(self, tensor):
+        self.tensor = tensor
+
+    @property
+    def __cuda_array_interface__(self):
+        return self.tensor.__cuda_array_interface__
+
+    @property
+    def shape(self):
+        return tuple(self.tensor.shape)
+
+    def copy_to_host(self):
+        return self.tensor.cpu().numpy()
+
+    def __len__(self):
+        return self.tensor.shape[0]
+
+
+class TorchCUDA:
+    """The ``cuda`` object of a bound module: ``to_device`` and ``synchronize``
+    (the two calls ``cuda_runtime`` makes on Numba's ``cuda`` in the reference)."""
+
+    @staticmethod
+    def to_device(array):
+        import torch
+        host = torch.from_numpy(np.ascontiguousarray(array))
+        return DeviceArray(host.to("cuda", non_blocking=host.is_pinned()))
+
+    @staticmethod
+    def synchronize():
+        import torch
+        torch.cuda.synchronize()
+
+    @staticmethod
+    def device_array(shape, dtype):
+        import torch
+        torch_dtype = torch.from_numpy(np.zeros(0, dtype=dtype)).dtype
+        return DeviceArray(torch.empty(shape, dtype=torch_dtype, device="cuda"))
+
+
+def as_tensor(value, dtype=None):
+    """View any device array of the contract as a torch tensor (no copy)."""
+    import torch
+    if isinstance(value, DeviceArray):
+        tensor = value.tensor
+    elif isinstance(value, torch.Tensor):
+        tensor = value
+    elif hasattr(value, "__cuda_array_interface__"):
+        tensor = torch.as_tensor(value, device="cuda")
+    else:
+        raise CUDARuntimePreparationError(
+            f"expected a device array, received {type(value).__name__}")
+    if dtype is not None and tensor.dtype != dtype:
+        tensor = tensor.to(dtype)
+    return tensor.contiguous()
+
+
+@dataclass
+class CompiledCUDAModule:
+    """Callables and globals belonging to one bound operator schedule."""
+
+    kernel: object
+    launcher: object
+    namespace: dict
+
+
+@dataclass
+class CUDAPreparedArguments:
+    """Host/device values ordered for a launcher."""
+
+    launcher_argument_names: tuple
+    values: dict
+    host_values: dict
+    lifted_variables: tuple
+
+    @property
+    def launcher_arguments(self):
+        return tuple(self.values[name] for name in self.launcher_argument_names)
+
+    def copy_to_host(self, name):
+        if name not in self.values:
+            raise CUDARuntimePreparationError(f"Unknown prepared CUDA argument {name!r}.")
+        value = self.values[name]
+        method = getattr(value, "copy_to_host", None)
+        return method() if method is not None else value
+
+    def copy_lifted_variables_to_host(self):
+        return {name: self.copy_to_host(name) for name in self.lifted_variables}
+
+
+def compile_cuda_module(lowering, function_globals=None, cuda_module=None):
+    """Bind the native kernel and launcher of one lowering.
+
+    Nothing is compiled at run time: the kernels were built ahead of time for
+    sm_100a; a missing library raises (there is no other implementation)."""
+    from . import _native, launchers
+    namespace = dict(function_globals or {})
+    namespace["cuda"] = cuda_module if cuda_module is not None else TorchCUDA
+    try:
+        _native.load()
+        kernel, launcher = launchers.bind(lowering)
+    except Exception as error:
+        raise CUDAModuleCompilationError(
+            f"Failed to bind the native kernel for {lowering.operator!r}: {error}") from error
+    namespace[lowering.kernel_name] = kernel
+    namespace[lowering.launcher_name] = launcher
+    return CompiledCUDAModule(kernel=kernel, launcher=launcher, namespace=namespace)
+
+
+def prepare_cuda_arguments(lowering, argument_values, execution_data, function_globals=None,
+                           cuda_module=None):
+    """Create lifted locals and prepare all launcher arguments."""
+    if cuda_module is None:
+        cuda_module = TorchCUDA
+    host_values = dict(argument_values)
+    host_values.update(_evaluate_host_prelude(lowering, host_values, function_globals or {}))
+    host_values.update(_execution_values(lowering.execution_mode, execution_data))
+    missing = [name for name in lowering.launcher_arguments if name not in host_values]
+    if missing:
+        raise CUDARuntimePreparationError(
+            "Values are missing for generated launcher arguments: " + ", ".join(missing))
+    device_only = set(getattr(lowering, "device_only_variables", ()))
+    prepared = {}
+    for name in lowering.launcher_arguments:
+        value = host_values[name]
+        if name in HOST_LAUNCH_ARGUMENTS:
+            prepared[name] = value  # the host launcher reads the offsets
+        elif (name in device_only and isinstance(value, np.ndarray)
+              and hasattr(cuda_module, "device_array")):
+            # an output the kernel overwrites completely: allocate, do not upload
+            prepared[name] = cuda_module.device_array(value.shape, value.dtype)
+        else:
+            prepared[name] = _prepare_value(value, cuda_module)
+    return CUDAPreparedArguments(tuple(lowering.launcher_arguments), prepared, host_values,
+                                 tuple(lowering.lifted_variables))
+
+
+def evaluate_host_prelude(lowering, argument_values, function_globals=None):
+    """Evaluate the removed host statements (e.g. ``n = len(indptr) - 1``)."""
+    return _evaluate_host_prelude(lowering, argument_values, function_globals or {})
+
+
+def execute_cuda_call(compiled_module, lowering, prepared_arguments, function_globals=None):
+    """Launch prepared work and restore the original return semantics."""
+    compiled_module.launcher(*prepared_arguments.launcher_arguments)
+    cuda_module = compiled_module.namespace.get("cuda")
+    if cuda_module is None or not hasattr(cuda_module, "synchronize"):
+        raise CUDARuntimePreparationError(
+            "The compiled CUDA module does not provide cuda.synchronize().")
+    cuda_module.synchronize()
+    results = dict(prepared_arguments.host_values)
+    results.update({name: prepared_arguments.copy_to_host(name)
+                    for name in _returned_names(lowering.host_epilogue)
+                    if name in prepared_arguments.values})
+    results.update(prepared_arguments.copy_lifted_variables_to_host())
+    return _evaluate_host_epilogue(lowering, results, function_globals or {})
+
+
+def _evaluate_host_prelude(lowering, argument_values, function_globals):
+    if not lowering.host_prelude:
+        return {}
+    namespace = dict(function_globals)
+    namespace.update(argument_values)
+    module = ast.fix_missing_locations(
+        ast.Module(body=deepcopy(lowering.host_prelude), type_ignores=[]))
+    exec(compile(module, filename="<cuda-host-prelude>", mode="exec"), namespace, namespace)
+    missing = [name for name in lowering.lifted_variables if name not in namespace]
+    if missing:
+        raise CUDARuntimePreparationError(
+            "The removed host prelude did not define lifted variables: " + ", ".join(missing))
+    return {name: namespace[name] for name in _stored_names(lowering.host_prelude)
+            if name in namespace}
+
+
+def _evaluate_host_epilogue(lowering, result_values, function_globals):
+    if not lowering.host_epilogue:
+        return None
+    namespace = dict(function_globals)
+    namespace.update(result_values)
+    helper = ast.FunctionDef(
+        name="_lcd_host_epilogue",
+        args=ast.arguments(posonlyargs=[], args=[], kwonlyargs=[], kw_defaults=[], defaults=[]),
+        body=deepcopy(lowering.host_epilogue), decorator_list=[], returns=None,
+        type_comment=None)
+    if hasattr(helper, "type_params"):
+        helper.type_params = []
+    module = ast.fix_missing_locations(ast.Module(body=[helper], type_ignores=[]))
+    exec(compile(module, filename="<cuda-host-epilogue>", mode="exec"), namespace, namespace)
+    return namespace["_lcd_host_epilogue"]()
+
+
+def _returned_names(statements):
+    names = []
+    for statement in statements:
+        for node in ast.walk(statement):
+            if isinstance(node, ast.Return) and node.value is not None:
+                for value in ast.walk(node.value):
+                    if (isinstance(value, ast.Name) and isinstance(value.ctx, ast.Load)
+                            and value.id not in names):
+                        names.append(value.id)
+    return names
+
+
+def _stored_names(statements):
+    names = []
+    for statement in statements:
+        for node in ast.walk(statement):
+            if (isinstance(node, ast.Name) and isinstance(node.ctx, ast.Store)
+                    and node.id not in names):
+                names.append(node.id)
+    return names
+
+
+def _zeros_like_count(count_array, length=None, device_like=None):
+    """int32 zeros next to an existing executor array (device or host)."""
+    try:
+        import torch
+        if isinstance(count_array, torch.Tensor):
+            n = count_array.numel() if length is None else length
+            return torch.zeros(n, dtype=torch.int32, device=count_array.device)
+    except ImportError:  # pragma: no cover
+        pass
+    n = len(count_array) if length is None else length
+    return np.zeros(n, dtype=np.int32)
+
+
+def _copy_of(array):
+    return array.clone() if hasattr(array, "clone") else array.copy()
+
+
+def _execution_values(execution_mode, execution_data):
+    execution_mode = execution_mode.replace("-", "_")
+    if isinstance(execution_data, WarpTaskExecutionData):
+        initial = execution_data.initial_dep_count
+        if initial is None:
+            initial = _copy_of(execution_data.dep_count)
+        return _with_auxiliary_values({
+            "task_nodes": execution_data.task_nodes,
+            "task_ptr": execution_data.task_ptr,
+            "band_ptr": execution_data.band_ptr,
+            "task_counter": _zeros_like_count(execution_data.dep_count, 1),
+            "done": _zeros_like_count(execution_data.dep_count),
+            "dep_count": execution_data.dep_count,
+            "initial_dep_count": initial,
+            "dag_ptr": execution_data.dag_ptr,
+            "dag_index": execution_data.dag_index,
+        }, execution_data)
+    if execution_mode == "sync_free":
+        if not isinstance(execution_data, SyncFreeExecutionData):
+            raise CUDARuntimePreparationError(
+                "Sync-free lowering requires SyncFreeExecutionData.")
+        initial = execution_data.initial_dep_count
+        if initial is None:
+            initial = _copy_of(execution_data.dep_count)
+        return _with_auxiliary_values({
+            "dep_count": execution_data.dep_count,
+            "initial_dep_count": initial,
+            "dag_ptr": execution_data.dag_ptr,
+            "dag_index": execution_data.dag_index,
+        }, execution_data)
+    if execution_mode == "wavefront":
+        if not isinstance(execution_data, WavefrontExecutionData):
+            raise CUDARuntimePreparationError(
+                "Wavefront lowering requires WavefrontExecutionData.")
+        return _with_auxiliary_values({
+            "wavefronts": execution_data.wavefronts,
+            "wavefront_ptr": execution_data.wavefront_ptr,
+        }, execution_data)
+    return {}
+
+
+def _with_auxiliary_values(values, execution_data):
+    auxiliary = getattr(execution_data, "auxiliary_values", {})
+    collisions = set(values) & set(auxiliary)
+    if collisions:
+        raise CUDARuntimePreparationError(
+            "Auxiliary values conflict with executor arguments: " + ", ".join(sorted(collisions)))
+    values.update(auxiliary)
+    return values
+
+
+def _prepare_value(value, cuda_module):
+    if _is_cuda_array(value) or np.isscalar(value) or value is None:
+        return value
+    if isinstance(value, (list, tuple)):
+        value = np.asarray(value)
+    if isinstance(value, np.ndarray):
+        return cuda_module.to_device(value)
+    raise CUDARuntimePreparationError(
+        "CUDA launcher arguments must be scalars, NumPy arrays, sequences, or existing CUDA "
+        f"arrays; received {type(value).__name__}.")
+
+
+def _is_cuda_array(value):
+    return hasattr(value, "__cuda_array_interface__")

@@ -1,0 +1,298 @@
+"""``parallel(...)``: the reference's decorator in front of the native kernels.
+
+Call-compatible with ``compiler/decorator.py:138-528`` of the reference: the same
+keyword arguments (``loop | block_map | block_loop``, ``function_props``,
+``execution_mode``, ``threads_per_block``, ``thread_map | thread_loop``,
+``thread_unroll | thread_unroll_factor``, ``n_warp``, ``dependence_protocol``,
+``scheduler``, ``arch_constants``, ``sync_free_ready_count``,
+``validate_dag_endpoints``, ``band_width``; unknown ones are ignored), host NumPy
+arrays in, host NumPy arrays out, and the same attributes on the wrapper
+(``original_function``, ``build_dag``, ``build_execution_data``,
+``prepare_cuda_arguments``, ``schedule_plan``, ``schedule_call``,
+``schedule_space``, ``scheduler``, ``execution_mode``, ``structural_lookups``,
+``current_schedule`` and the per-variant ``cuda_*`` attributes).
+
+What differs is what happens behind it:
+
+* decoration recognises the loop nest (no SMT solving, milliseconds instead of
+  seconds) and raises ``CUDALoweringError`` for loop nests the native kernels do
+  not serve -- there is no interpreter and no CPU fallback;
+* the inspector (edge rule, in-degree counts, level sets, topological order) runs
+  on the GPU (``lcd_dag_build``) and its arrays stay there;
+* plans are cached under a fingerprint of the structure arrays computed on the
+  device from the copies that are uploaded anyway (the reference hashes them on
+  the host on every call, ``compiler/scheduler.py:678-711``).
+"""
+
+from __future__ import annotations
+
+import ast
+import functools
+import inspect
+import textwrap
+
+import numpy as np
+
+from .cuda_lowering import (COUNTER_DEPENDENCE, PUSH_DEPENDENCE, CUDALoweringError,
+                            direct_protocol_of, lower_to_native, recognise_operator)
+from .cuda_runtime import (DeviceArray, TorchCUDA, compile_cuda_module, evaluate_host_prelude,
+                           execute_cuda_call, prepare_cuda_arguments)
+from .dag_preprocessing import (attach_auxiliary_values, preprocess_sync_free,
+                                preprocess_warp_tasks, preprocess_wavefront)
+from .scheduler import (AUTO, SYNC_FREE, WAVEFRONT, AnalyticScheduler, SchedulePlan,
+                        ScheduleSpace, extract_workload_features, pointer_array_names)
+from .structural_lookups import (create_structural_lookup_plan, materialize_structural_lookups,
+                                 structural_argument_names)
+
+SCHEDULE_CACHE_SIZE = 8
+VARIANT_ATTRIBUTES = ("cuda_lowering", "compiled_cuda_module", "cuda_kernel", "cuda_launcher",
+                      "cuda_module_ast", "cuda_kernel_ast", "cuda_source", "cuda_kernel_source",
+                      "cuda_launcher_ast", "cuda_launcher_source")
+_DAG_OPERATORS = {("sptrsv_csr", False): "csr_lower", ("sptrsv_csr", True): "csr_upper",
+                  ("sptrsv_csc", False): "csc_lower", ("sptrsv_csc", True): "csc_upper",
+                  ("ilu0_csr", False): "ilu0_csr"}
+
+
+def _variant_attributes(lowering, module):
+    kernel_source = ast.unparse(lowering.kernel_ast) if lowering.kernel_ast is not None else None
+    return {"cuda_lowering": lowering, "compiled_cuda_module": module,
+            "cuda_kernel": module.kernel, "cuda_launcher": module.launcher,
+            "cuda_module_ast": lowering.module_ast, "cuda_kernel_ast": lowering.kernel_ast,
+            "cuda_source": lowering.source, "cuda_kernel_source": kernel_source,
+            "cuda_launcher_ast": lowering.launcher_ast, "cuda_launcher_source": lowering.source}
+
+
+def _function_source(function):
+    source = textwrap.dedent(inspect.getsource(function))
+    return "\n".join(line for line in source.splitlines() if not line.startswith("@"))
+
+
+def parallel(**kwargs):
+    """Decorator factory; see the module docstring for the accepted keywords."""
+
+    def decorator(function):
+        loop = kwargs.get("loop", kwargs.get("block_map", kwargs.get("block_loop")))
+        if loop is None:
+            raise ValueError("parallel requires a block-mapped iterator via `loop`, "
+                             "`block_map`, or `block_loop`.")
+        function_props = kwargs.get("function_props", {})
+        tree = ast.parse(_function_source(function))
+        structural_lookups = create_structural_lookup_plan(tree, function_props)
+        signature = inspect.signature(function)
+        argument_names = list(signature.parameters)
+        execution_mode = kwargs.get("execution_mode", AUTO)
+        thread_loop = kwargs.get("thread_loop", kwargs.get("thread_map"))
+        thread_unroll = kwargs.get("thread_unroll", kwargs.get("thread_unroll_factor"))
+        band_width = kwargs.get("band_width", 1)
+        scheduler = kwargs.get("scheduler") or AnalyticScheduler(kwargs.get("arch_constants"))
+        operator, upper, roles, inner_loop, _, _ = recognise_operator(tree, loop)
+        if thread_loop is not None and thread_loop != inner_loop:
+            raise CUDALoweringError(
+                f"thread_map={thread_loop!r} is not the inner loop ({inner_loop!r}) of the "
+                "recognised operator.")
+        dag_operator = _DAG_OPERATORS[(operator, upper)]
+        direct = direct_protocol_of(operator, thread_loop)
+        space_options = dict(execution_mode=execution_mode,
+                             threads_per_block=kwargs.get("threads_per_block"),
+                             thread_unroll=thread_unroll, thread_mapped=thread_loop is not None,
+                             n_warp=kwargs.get("n_warp"))
+        schedule_space = ScheduleSpace.from_options(
+            **space_options, direct_protocol=direct,
+            dependence_protocol=kwargs.get("dependence_protocol"))
+        fixed_schedule = schedule_space.fixed_schedule() if schedule_space.is_fixed else None
+        lowered, compiled = {}, {}
+
+        def lower_variant(key):
+            if key not in lowered:
+                mode, threads, unroll, n_warp, protocol = key
+                lowered[key] = lower_to_native(
+                    tree, loop_iterator=loop, execution_mode=mode,
+                    sync_free_ready_count=kwargs.get("sync_free_ready_count", 0),
+                    wavefront_threads_per_block=threads, thread_loop_iterator=thread_loop,
+                    thread_unroll_factor=unroll, n_warp=n_warp, dependence_protocol=protocol,
+                    direct_dependence=None if protocol == COUNTER_DEPENDENCE else direct,
+                    function_props=function_props, structural_lookups=structural_lookups)
+            return lowered[key]
+
+        def compile_variant(key):
+            lowering = lower_variant(key)
+            if key not in compiled:
+                compiled[key] = compile_cuda_module(lowering,
+                                                    function_globals=function.__globals__)
+            return lowering, compiled[key]
+
+        host_lowering = lower_variant(schedule_space.configurations()[0])
+        dag_argument_names = argument_names + [
+            name for name in host_lowering.lifted_loop_parameters if name not in argument_names]
+        structure_names = [roles["ptr"], roles["idx"]]
+        fingerprint_names = list(dict.fromkeys(
+            structure_names + pointer_array_names(function_props)
+            + structural_argument_names(structural_lookups)))
+        schedule_plans = {}
+
+        def bind_arguments(args, call_kwargs):
+            bound = signature.bind(*args, **call_kwargs)
+            bound.apply_defaults()
+            return dict(bound.arguments)
+
+        def dag_values_for(argument_values):
+            values = dict(argument_values)
+            values.update(evaluate_host_prelude(host_lowering, values, function.__globals__))
+            return values
+
+        def device_structure(values):
+            """int32 device copies of the structure arrays (uploaded once per call)."""
+            import torch
+            out = {}
+            for name in structure_names:
+                value = values[name]
+                if isinstance(value, DeviceArray):
+                    value = value.tensor
+                if isinstance(value, torch.Tensor):
+                    out[name] = value.to(device="cuda", dtype=torch.int32).contiguous()
+                else:
+                    host = torch.from_numpy(np.ascontiguousarray(value, dtype=np.int32))
+                    out[name] = host.to("cuda", non_blocking=host.is_pinned())
+            return out
+
+        def node_count(values, structure):
+            n = values.get(roles.get("n"))
+            return int(n) if n is not None else structure[roles["ptr"]].numel() - 1
+
+        def device_dag(values, structure):
+            from . import ops
+            return ops.dag_build(dag_operator, structure[roles["ptr"]], structure[roles["idx"]],
+                                 n=node_count(values, structure))
+
+        def build_dag(*args, **call_kwargs):
+            """(successor lists, dep_count) -- or wavefront lists when the fixed mode is
+            wavefront -- as Python lists, like the reference's generated inspector."""
+            values = dag_values_for(bind_arguments(args, call_kwargs))
+            dag = device_dag(values, device_structure(values))
+            ptr = dag.dag_ptr.cpu().numpy()
+            index = dag.dag_index.cpu().numpy()
+            successors = [index[ptr[v]:ptr[v + 1]].tolist() for v in range(dag.n)]
+            if fixed_schedule is not None and fixed_schedule.execution_mode == WAVEFRONT:
+                nodes = dag.wavefronts.cpu().numpy()
+                wptr = dag.wavefront_ptr_host
+                return successors, [nodes[wptr[k]:wptr[k + 1]].tolist()
+                                    for k in range(len(wptr) - 1)]
+            return successors, dag.dep_count.cpu().numpy().tolist()
+
+        def execution_data_for(schedule, dag):
+            lowering = lower_variant(schedule.lowering_key)
+            if lowering.warp_mapped:
+                pushed = lowering.dependence_protocol == PUSH_DEPENDENCE
+                return preprocess_warp_tasks(dag, None, band_width,
+                                             edge_count=dag.edge_count if pushed else None)
+            if schedule.execution_mode == SYNC_FREE:
+                return preprocess_sync_free(dag)
+            return preprocess_wavefront(dag)
+
+        def create_schedule_plan(values, structure):
+            lookup_arguments = dict(values)
+            lookup_arguments.update(structure)
+            lookups = materialize_structural_lookups(structural_lookups, lookup_arguments)
+            dag = device_dag(values, structure)
+            features = None
+            schedule = fixed_schedule
+            if schedule is None:
+                n = dag.n
+                nnz = int(structure[roles["idx"]].numel())
+                trips = (max(nnz - n, 0), n) if thread_loop is not None else None
+                features = extract_workload_features(
+                    dag, None, values, function_props=function_props,
+                    flops_per_iteration=2, thread_trip_counts=trips)
+                schedule = scheduler.schedule(features, schedule_space)
+            data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
+            return SchedulePlan(schedule=schedule, execution_data=data, features=features)
+
+        def plan_for(values, structure):
+            from . import ops
+            fingerprint = tuple(
+                (name,) + ops.fingerprint(structure[name]) for name in structure_names
+            ) + (node_count(values, structure),)
+            plan = schedule_plans.get(fingerprint)
+            if plan is None:
+                plan = create_schedule_plan(values, structure)
+                if len(schedule_plans) >= SCHEDULE_CACHE_SIZE:
+                    schedule_plans.pop(next(iter(schedule_plans)))
+                schedule_plans[fingerprint] = plan
+            return plan
+
+        def schedule_plan(*args, **call_kwargs):
+            values = dag_values_for(bind_arguments(args, call_kwargs))
+            return plan_for(values, device_structure(values))
+
+        def schedule_call(*args, **call_kwargs):
+            return schedule_plan(*args, **call_kwargs).schedule
+
+        def build_execution_data(*args, **call_kwargs):
+            return schedule_plan(*args, **call_kwargs).execution_data
+
+        def publish_variant(schedule, lowering, module):
+            if wrapper.current_schedule == schedule:
+                return
+            wrapper.current_schedule = schedule
+            wrapper.__dict__.update(_variant_attributes(lowering, module))
+
+        def resolve_call(args, call_kwargs):
+            argument_values = bind_arguments(args, call_kwargs)
+            values = dag_values_for(argument_values)
+            structure = device_structure(values)
+            plan = plan_for(values, structure)
+            lowering, module = compile_variant(plan.schedule.lowering_key)
+            publish_variant(plan.schedule, lowering, module)
+            # hand the already uploaded structure arrays to the launcher
+            launch_values = dict(argument_values)
+            for name, tensor in structure.items():
+                if name in launch_values:
+                    launch_values[name] = DeviceArray(tensor)
+            prepared = prepare_cuda_arguments(
+                lowering=lowering, argument_values=launch_values,
+                execution_data=_fresh_counters(plan.execution_data),
+                function_globals=function.__globals__, cuda_module=module.namespace["cuda"])
+            return lowering, module, prepared
+
+        def prepare_cuda_call(*args, **call_kwargs):
+            return resolve_call(args, call_kwargs)[2]
+
+        @functools.wraps(function)
+        def wrapper(*args, **call_kwargs):
+            lowering, module, prepared = resolve_call(args, call_kwargs)
+            return execute_cuda_call(module, lowering, prepared, function.__globals__)
+
+        wrapper.original_function = function
+        wrapper.build_dag = build_dag
+        wrapper.build_execution_data = build_execution_data
+        wrapper.prepare_cuda_arguments = prepare_cuda_call
+        wrapper.schedule_plan = schedule_plan
+        wrapper.schedule_call = schedule_call
+        wrapper.schedule_space = schedule_space
+        wrapper.scheduler = scheduler
+        wrapper.dag_plan = {"operator": operator, "upper": upper, "edge_rule": dag_operator,
+                            "roles": dict(roles), "arguments": dag_argument_names}
+        wrapper.dag_source = (f"# edge rule {dag_operator!r} evaluated on the device by "
+                              "lcd_dag_build (liblcd_b200.so)")
+        wrapper.execution_mode = execution_mode
+        wrapper.dependence_analysis = None
+        wrapper.structural_lookups = structural_lookups
+        wrapper.reduction_statements = ()
+        wrapper.current_schedule = None
+        wrapper.fingerprint_names = fingerprint_names
+        wrapper.__dict__.update(dict.fromkeys(VARIANT_ATTRIBUTES))
+        if fixed_schedule is not None:
+            publish_variant(fixed_schedule, *compile_variant(fixed_schedule.lowering_key))
+        return wrapper
+
+    return decorator
+
+
+def _fresh_counters(execution_data):
+    """The kernels consume ``dep_count``; every call gets its own copy of the
+    pristine counters (the reference re-uploads them per call)."""
+    from dataclasses import replace
+    initial = getattr(execution_data, "initial_dep_count", None)
+    if initial is None or not hasattr(initial, "clone"):
+        return execution_data
+    return replace(execution_data, dep_count=initial.clone())

@@ -1,0 +1,139 @@
+"""Native launchers behind the reference's launcher contract.
+
+The reference generates a Python launcher per lowering
+(``compiler/cuda_lowering.py:673-735`` single sync-free launch, ``:855-1016``
+per-level wavefront launches with a device synchronisation after each,
+``:1022-1068`` per-band, ``:1070-1119`` persistent warps).  Here a launcher is a
+closure that receives the same positional arguments (original parameters, lifted
+locals, lookup tables, executor arrays) and forwards the device pointers to one
+C-ABI entry point; level loops and barriers live inside the library.
+
+Executor arrays the native kernels do not need (successor lists, task tables and
+ticket counters of the row-form solver, which polls operands instead of counting)
+are accepted and ignored, so call sites written for the reference keep working.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import ops
+from .cuda_lowering import CUDALoweringError, PUSH_DEPENDENCE
+from .cuda_runtime import as_tensor
+
+# Launch policy of the wavefront entry point: the cooperative single-launch walk
+# unless the level count is small enough for per-level launches to be cheaper.
+PER_LEVEL_MAX_LEVELS = 8
+
+
+def _lanes_from_schedule(lowering, average_work):
+    """Lane-group width for one row.  ``n_warp``/``threads_per_block`` describe the
+    reference's mapping (a warp or a block per node); natively the group is sized
+    to the row length, capped by what the schedule asked for."""
+    if lowering.thread_loop_iterator is None:
+        return 1
+    cap = 32 * max(1, lowering.n_warp or 1)
+    lanes = 1
+    while lanes < 32 and lanes * 24 < average_work and lanes * 2 <= cap:
+        lanes *= 2
+    return lanes
+
+
+def bind(lowering):
+    """(kernel, launcher) callables for a lowering of a recognised operator."""
+    names = list(lowering.launcher_arguments)
+    roles = lowering.roles
+    import torch
+
+    def split(args):
+        if len(args) != len(names):
+            raise TypeError(f"{lowering.launcher_name} expects {len(names)} arguments "
+                            f"({', '.join(names)}), received {len(args)}")
+        return dict(zip(names, args))
+
+    def matrix(values):
+        Ap = as_tensor(values[roles["ptr"]], torch.int32)
+        Ai = as_tensor(values[roles["idx"]], torch.int32)
+        Ax = as_tensor(values[roles["val"]], torch.float64)
+        return Ap, Ai, Ax
+
+    def average_row(Ap, Ai):
+        return Ai.numel() / max(1, Ap.numel() - 1)
+
+    def wavefront_arrays(values):
+        if "wavefronts" in values:
+            nodes, ptr_host = values["wavefronts"], values["wavefront_ptr"]
+        else:
+            nodes, ptr_host = values["task_nodes"], values["band_ptr"]
+            task_ptr = values["task_ptr"]
+            if len(task_ptr) - 1 != len(nodes):
+                raise CUDALoweringError("band_width > 1 task chains are not served natively")
+        nodes = as_tensor(nodes, torch.int32)
+        ptr_host = np.ascontiguousarray(
+            ptr_host.copy_to_host() if hasattr(ptr_host, "copy_to_host") else
+            (ptr_host.cpu().numpy() if hasattr(ptr_host, "cpu") else ptr_host), dtype=np.int32)
+        ptr_dev = torch.from_numpy(ptr_host).to(nodes.device)
+        return nodes, ptr_dev, ptr_host
+
+    def sptrsv_csr(*args):
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        b = as_tensor(v[roles["rhs"]], torch.float64)
+        x = as_tensor(v[roles["out"]], torch.float64)
+        lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
+        if lowering.execution_mode == "sync_free":
+            ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper, lanes=lanes)
+        else:
+            nodes, ptr_dev, ptr_host = wavefront_arrays(v)
+            mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
+            ops.sptrsv_wavefront("csr_upper" if lowering.upper else "csr_lower", Ap, Ai, Ax, b,
+                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes)
+
+    def sptrsv_csc(*args):
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        b = as_tensor(v[roles["rhs"]], torch.float64)
+        x = as_tensor(v[roles["out"]], torch.float64)
+        lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
+        if lowering.execution_mode == "sync_free":
+            if lowering.dependence_protocol == PUSH_DEPENDENCE:
+                # push protocol: the counters already hold edge multiplicities
+                dep = as_tensor(v["dep_count"], torch.int32)
+            else:
+                # counter protocol counts distinct predecessors; the push kernel
+                # decrements once per stored entry, so recount on the device
+                dep = ops.csc_edge_count(Ap, Ai, upper=lowering.upper)
+            ops.sptrsv_csc_syncfree(Ap, Ai, Ax, b, dep, x, upper=lowering.upper, lanes=lanes)
+        else:
+            nodes, ptr_dev, ptr_host = wavefront_arrays(v)
+            mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
+            ops.sptrsv_wavefront("csc_upper" if lowering.upper else "csc_lower", Ap, Ai, Ax, b,
+                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes)
+
+    def ilu0_csr(*args):
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        lookup = [name for name in names if name.startswith("_lcd_lookup_position_")]
+        pos = as_tensor(v[lookup[0]], torch.int32) if lookup else ops.diag_positions(Ap, Ai)
+        lanes = 0 if lowering.thread_loop_iterator is not None else 1
+        if lowering.execution_mode == "sync_free":
+            ops.spilu0_csr(Ap, Ai, Ax, pos, mode="sync_free", lanes=lanes)
+        else:
+            nodes, _, ptr_host = wavefront_arrays(v)
+            ops.spilu0_csr(Ap, Ai, Ax, pos, mode="wavefront", wavefronts=nodes,
+                           wavefront_ptr_host=ptr_host, lanes=lanes)
+
+    launcher = {"sptrsv_csr": sptrsv_csr, "sptrsv_csc": sptrsv_csc, "ilu0_csr": ilu0_csr}.get(
+        lowering.operator)
+    if launcher is None:
+        raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
+    launcher.__name__ = lowering.launcher_name
+
+    def kernel(*args, **kwargs):
+        raise CUDALoweringError(
+            f"{lowering.kernel_name} is a native sm_100a kernel inside liblcd_b200.so "
+            f"({lowering.entry_point}); launch it through {lowering.launcher_name}.")
+
+    kernel.__name__ = lowering.kernel_name
+    kernel.entry_point = lowering.entry_point
+    return kernel, launcher

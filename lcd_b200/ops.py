@@ -248,6 +248,21 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
     return Ax
 
 
+_checksum_scratch = {}
+
+
+def fingerprint(t):
+    """(length, checksum_lo, checksum_hi) of an int32 device tensor."""
+    _require(t, torch.int32, "fingerprint input")
+    scratch = _checksum_scratch.get(t.device)
+    if scratch is None:
+        scratch = _checksum_scratch[t.device] = torch.zeros(2, dtype=torch.int64, device=t.device)
+    out = (ctypes.c_uint64 * 2)()
+    check(nat.load().lcd_checksum_i32(ptr(t), t.numel(), ptr(scratch), ctypes.byref(out),
+                                      _stream()), "lcd_checksum_i32")
+    return t.numel(), int(out[0]), int(out[1])
+
+
 def fill_u64(t, value):
     check(nat.load().lcd_fill_u64(ptr(t), t.numel() * t.element_size() // 8, value, _stream()),
           "lcd_fill_u64")

@@ -1,0 +1,116 @@
+"""The decorator path end to end on the GPU: host NumPy in, host NumPy out, checked
+against the reference fixtures, SciPy and the CPU oracle (modelled on the reference's
+compiler/e2e_tests/test_sptrsv_e2e.py and test_spilu0_e2e.py)."""
+import numpy as np
+import pytest
+import scipy.sparse as sp
+from scipy.sparse.linalg import spsolve_triangular
+
+from conftest import golden, golden_names
+
+pytestmark = pytest.mark.gpu
+
+
+def _lists(ptr, idx):
+    return [idx[ptr[k]:ptr[k + 1]].tolist() for k in range(len(ptr) - 1)]
+
+
+@pytest.mark.parametrize("name", ["sptrsv_lap2d_g8", "sptrsv_band_n300", "sptrsv_unsorted_dups"])
+def test_inspector_outputs_equal_the_reference(cuda, name):
+    import ops_decorated as od
+    g = golden(name)
+    csr = (g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"], len(g["b"]))
+    csc = (g["csc_Ap"], g["csc_Ai"], g["csc_Ax"], g["b"], len(g["b"]))
+    succ, dep = od.csr_warp_syncfree.build_dag(*csr)
+    assert succ == _lists(g["csr_warp_syncfree/succ_ptr"], g["csr_warp_syncfree/succ_idx"])
+    assert dep == np.bincount(g["csr_warp_syncfree/succ_idx"], minlength=len(dep)).tolist()
+    succ, waves = od.simple_sptrsv_csr.build_dag(*csr)
+    wp = g["csr_plain_wavefront/wavefront_ptr"]
+    assert waves == _lists(wp, g["csr_plain_wavefront/wavefronts"])
+    cases = [(od.csr_warp_syncfree, csr, "csr_warp_syncfree/"), (od.csr_plain_syncfree, csr, "csr_plain_syncfree/"),
+             (od.simple_sptrsv_csr, csr, "csr_plain_wavefront/"), (od.csc_warp_push, csc, "csc_warp_push/"),
+             (od.simple_sptrsv_csc, csc, "csc_plain_wavefront/")]
+    for op, args, prefix in cases:
+        plan = op.schedule_plan(*args)
+        assert list(map(str, plan.schedule.lowering_key)) == g[prefix + "schedule"].tolist()
+        data = plan.execution_data
+        for field in ("dep_count", "initial_dep_count", "dag_ptr", "dag_index", "wavefronts", "wavefront_ptr",
+                      "task_nodes", "task_ptr", "band_ptr"):
+            if prefix + field in g:
+                value = getattr(data, field)
+                value = value.cpu().numpy() if hasattr(value, "cpu") else np.asarray(value)
+                np.testing.assert_array_equal(value, g[prefix + field], err_msg=prefix + field)
+                assert value.dtype == np.int32
+        assert op.schedule_plan(*args) is plan            # cached by structure fingerprint
+        prepared = op.prepare_cuda_arguments(*args)
+        assert prepared.launcher_argument_names == tuple(op.cuda_lowering.launcher_arguments)
+        assert isinstance(prepared.values["n"], (int, np.integer))
+
+
+@pytest.mark.parametrize("name", golden_names("sptrsv_"))
+def test_decorated_sptrsv_matches_scipy_and_reference(cuda, name):
+    import ops_decorated as od
+    g = golden(name)
+    n = len(g["b"])
+    if "csr_upper_reversed/succ_ptr" in g:
+        x = od.csr_upper_reversed(g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"], n)
+        np.testing.assert_allclose(x, g["x_csr"], rtol=1e-10, atol=1e-12)
+        return
+    L = sp.csr_matrix((g["csr_Ax"], g["csr_Ai"], g["csr_Ap"]), shape=(n, n))
+    L.sum_duplicates()
+    want = spsolve_triangular(L, g["b"], lower=True)
+    for op in (od.simple_sptrsv_csr, od.csr_warp_syncfree, od.csr_plain_syncfree, od.csr_auto):
+        b_before = g["b"].copy()
+        x = op(g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"], n)
+        assert isinstance(x, np.ndarray) and x.shape == (n,)
+        np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)     # the reference's E2E tolerance
+        np.testing.assert_allclose(x, g["x_csr"], rtol=1e-10, atol=1e-12)
+        np.testing.assert_array_equal(g["b"], b_before)                   # inputs are never mutated
+    for op in (od.simple_sptrsv_csc, od.csc_warp_push):
+        x = op(g["csc_Ap"], g["csc_Ai"], g["csc_Ax"], g["b"], n)
+        np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    assert od.csr_auto.current_schedule is not None and od.csr_auto.cuda_source is not None
+
+
+def test_decorated_first_configuration(cuda, oracle):
+    """L = tril of the 2-D 5-point Laplacian on a 256 x 256 grid through the decorated CSC demo."""
+    import ops_decorated as od
+    from lcd_b200 import generators as gen
+    tri = gen.laplacian2d_tril(256, seed=0)
+    Cp, Ci, Cx = tri.csc_arrays()
+    x = od.csc_warp_push(Cp, Ci, Cx, tri.b, tri.n)
+    want = spsolve_triangular(tri.csr, tri.b, lower=True)
+    np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    Ap, Ai, Ax = tri.csr_arrays()
+    assert oracle.relative_residual_csr(Ap, Ai, Ax, x, tri.b) <= 1e-12
+    host = od.csc_warp_push.original_function(Cp, Ci, Cx, tri.b, tri.n)
+    np.testing.assert_allclose(x, host, rtol=1e-10, atol=1e-12)
+    plan = od.csc_warp_push.schedule_plan(Cp, Ci, Cx, tri.b, tri.n)
+    assert len(plan.execution_data.band_ptr) - 1 == 511           # levels of the 256 x 256 grid
+
+
+@pytest.mark.parametrize("mode", ["wavefront", "sync_free"])
+@pytest.mark.parametrize("name", golden_names("ilu0_"))
+def test_decorated_ilu0_is_bit_identical(cuda, name, mode):
+    import ops_decorated as od
+    g = golden(name)
+    op = od.compile_ilu0_csr(mode, 128, 1)
+    data = g["data"].copy()
+    out = op(data, g["indices"], g["indptr"])
+    np.testing.assert_array_equal(out, g["factored"])
+    np.testing.assert_array_equal(data, g["data"])                 # the caller's array is not modified
+    np.testing.assert_array_equal(out, od.ilu0_csr(g["data"].copy(), g["indices"], g["indptr"]))
+    assert op.current_schedule.execution_mode == mode
+    data_obj = op.build_execution_data(g["data"].copy(), g["indices"], g["indptr"])
+    table = data_obj.auxiliary_values["_lcd_lookup_position_0"]
+    np.testing.assert_array_equal(table.cpu().numpy(), g["diag_pos"])
+
+
+def test_structural_lookup_errors_surface_as_in_the_reference(cuda):
+    import ops_decorated as od
+    from lcd_b200.structural_lookups import StructuralLookupError
+    op = od.compile_ilu0_csr("sync_free", 128, 1)
+    indptr = np.array([0, 2, 4], np.int32)
+    indices = np.array([1, 0, 0, 1], np.int32)        # first row unsorted
+    with pytest.raises(StructuralLookupError):
+        op(np.ones(4), indices, indptr)

@@ -1,0 +1,300 @@
+"""Host-side logic and the C-ABI surface; no GPU needed."""
+import ast
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, golden, golden_names
+
+
+# ---- C ABI ---------------------------------------------------------------
+def test_library_exports_every_declared_symbol():
+    from lcd_b200 import _native, build
+    header = open(os.path.join(ROOT, "include", "lcd_b200.h")).read()
+    declared = set(re.findall(r"\b(lcd_[a-z0-9_]+)\s*\(", header))
+    assert declared, "no declarations found"
+    lib = ctypes.CDLL(build.build())
+    missing = [name for name in sorted(declared) if not hasattr(lib, name)]
+    assert not missing, missing
+    assert set(_native.EXPORTED_SYMBOLS) <= declared
+    loaded = _native.load()
+    assert loaded.lcd_version() >= 100
+    assert loaded.lcd_error_string(4).decode().startswith("a bounded device wait")
+    # argument validation happens before any CUDA call
+    assert loaded.lcd_sptrsv_csr_syncfree(-1, 0, None, None, None, None, None, None, 0, 0, 0,
+                                          None, 0, None, None) == _native.ERR_INVALID_ARGUMENT
+    need = ctypes.c_int64(0)
+    assert loaded.lcd_dag_workspace_bytes(0, 1000, 5000, ctypes.byref(need)) == 0
+    assert need.value > 5000 * 16
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    from lcd_b200 import _native
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "absent.so"))
+    with pytest.raises(_native.NativeLibraryMissing):
+        _native.load()
+
+
+def test_product_code_never_touches_the_oracle():
+    for folder, _, files in os.walk(os.path.join(ROOT, "lcd_b200")):
+        for name in files:
+            if name.endswith((".py", ".cu", ".cuh")):
+                text = open(os.path.join(folder, name)).read()
+                assert "oracle" not in text.replace("# oracle", ""), name
+
+
+# ---- DAG preprocessing on the reference's list format -------------------------
+def _lists(ptr, idx):
+    return [idx[ptr[k]:ptr[k + 1]].tolist() for k in range(len(ptr) - 1)]
+
+
+@pytest.mark.parametrize("name", golden_names("sptrsv_"))
+def test_list_preprocessing_matches_reference_fixture(name):
+    from lcd_b200 import dag_preprocessing as dp
+    g = golden(name)
+    prefixes = [p for p in ("csr_warp_syncfree/", "csc_warp_push/", "csr_upper_reversed/") if p + "succ_ptr" in g]
+    for prefix in prefixes:
+        succ = _lists(g[prefix + "succ_ptr"], g[prefix + "succ_idx"])
+        dag_ptr, dag_index = dp.compact_successors(succ)
+        np.testing.assert_array_equal(dag_ptr, g[prefix + "succ_ptr"])
+        np.testing.assert_array_equal(dag_index, g[prefix + "succ_idx"])
+        dep = np.bincount(dag_index, minlength=len(succ)).astype(np.int32)
+        waves = dp.wavefronts_from_dag(succ, dep)
+        data = dp.preprocess_wavefront(succ, waves)
+        if prefix == "csr_upper_reversed/":
+            np.testing.assert_array_equal(data.wavefronts, g[prefix + "wavefronts"])
+            np.testing.assert_array_equal(data.wavefront_ptr, g[prefix + "wavefront_ptr"])
+            continue
+        edge = g[prefix + "dep_count"] if prefix == "csc_warp_push/" else None
+        tasks = dp.preprocess_warp_tasks(succ, waves, 1, edge_count=edge)
+        for field in ("task_nodes", "task_ptr", "band_ptr", "dep_count", "dag_ptr", "dag_index"):
+            np.testing.assert_array_equal(getattr(tasks, field), g[prefix + field])
+        assert tasks.dep_count.dtype == np.int32 and tasks.task_ptr.dtype == np.int32
+        sync = dp.preprocess_dag_output(succ, dep, "sync-free")
+        np.testing.assert_array_equal(sync.dag_index, g[prefix + "succ_idx"])
+        assert sync.launcher_arguments[0] is sync.dep_count
+
+
+def test_preprocessing_errors_follow_the_reference():
+    from lcd_b200 import dag_preprocessing as dp
+    # compiler/transform_tests/test_dag_codegen.py:237-246
+    with pytest.raises(dp.DAGPreprocessingError, match="may contain a cycle"):
+        dp.preprocess_dag_output([[1], [0]], [], execution_mode="wavefront")
+    with pytest.raises(dp.DAGPreprocessingError, match="out of bounds"):
+        dp.compact_successors([[5], []])
+    with pytest.raises(dp.DAGPreprocessingError, match="more than one wavefront"):
+        dp.preprocess_wavefront([[1], []], [[0, 1], [1]])
+    with pytest.raises(dp.DAGPreprocessingError, match="Unknown execution mode"):
+        dp.preprocess_dag_output([[]], [0], "plain")
+    with pytest.raises(dp.DAGPreprocessingError, match="positive integer"):
+        dp.preprocess_warp_tasks([[]], [[0]], band_width=0)
+    with pytest.raises(dp.DAGPreprocessingError, match="negative"):
+        dp.preprocess_sync_free([[]], [-1])
+    data = dp.preprocess_sync_free([[1, 1, 2], [2], []], [0, 1, 2])
+    np.testing.assert_array_equal(data.dag_ptr, [0, 2, 3, 3])
+    with_aux = dp.attach_auxiliary_values(data, {"t": np.zeros(1)})
+    assert "t" in with_aux.auxiliary_values
+    with pytest.raises(dp.DAGPreprocessingError, match="Duplicate"):
+        dp.attach_auxiliary_values(with_aux, {"t": np.zeros(1)})
+
+
+def test_band_chains_group_connected_nodes():
+    from lcd_b200 import dag_preprocessing as dp
+    succ = [[2], [3], [4], [], []]           # 0->2->4 and 1->3
+    waves = dp.wavefronts_from_dag(succ, [0, 0, 1, 1, 1])
+    assert waves == [[0, 1], [2, 3], [4]]
+    tasks = dp.preprocess_warp_tasks(succ, waves, band_width=2)
+    np.testing.assert_array_equal(tasks.task_nodes, [0, 2, 1, 3, 4])
+    np.testing.assert_array_equal(tasks.task_ptr, [0, 2, 4, 5])
+    np.testing.assert_array_equal(tasks.band_ptr, [0, 2, 3])
+
+
+# ---- scheduler -----------------------------------------------------------------
+def test_schedule_space_matches_reference_rules():
+    from lcd_b200 import scheduler as sc
+    fixed = sc.ScheduleSpace.from_options("wavefront", 128)
+    assert fixed.is_fixed and fixed.fixed_schedule().lowering_key == ("wavefront", 128, 1, 1, "counter")
+    space = sc.ScheduleSpace.from_options(None, None, None, thread_mapped=True, direct_protocol="pull")
+    assert len(space.configurations()) == 48            # 16 wavefront + 16 x (counter, pull)
+    push = sc.ScheduleSpace.from_options("sync_free", 128, 1, thread_mapped=True, direct_protocol="push")
+    assert push.fixed_schedule().dependence_protocol == "push"
+    assert sc.normalize_execution_mode("sync-free") == "sync_free" and sc.normalize_execution_mode("auto") is None
+    with pytest.raises(sc.SchedulerError):
+        sc.ScheduleSpace.from_options(n_warp=0)
+    with pytest.raises(sc.SchedulerError):
+        sc.ScheduleSpace.from_options(threads_per_block=100, thread_mapped=True, n_warp=1)
+    with pytest.raises(sc.SchedulerError):
+        sc.ScheduleSpace.from_options(threads_per_block=128, n_warp=2)
+    with pytest.raises(sc.SchedulerError):
+        sc.ScheduleSpace.from_options(dependence_protocol="push")
+    with pytest.raises(sc.SchedulerError):
+        space.fixed_schedule()
+
+
+def test_scheduler_decides_from_level_structure():
+    from lcd_b200 import scheduler as sc
+    space = sc.ScheduleSpace.from_options(None, 128, 1, thread_mapped=True, n_warp=1)
+    sched = sc.AnalyticScheduler(sc.FALLBACK_ARCH_CONSTANTS)
+    # long chain of narrow levels: every level costs a hand-off, sync-free wins
+    narrow = sc.WorkloadFeatures(rows=4_194_304, edges=61_000_000, levels=755_000, nonzeros=65_000_000,
+                                 flops=1.3e8, memory_bytes=870_000_000, thread_work_items=61_000_000,
+                                 thread_loop_invocations=4_194_304, max_level_width=17)
+    assert sched.schedule(narrow, space).execution_mode == "sync_free"
+    wide = sc.WorkloadFeatures(rows=2_097_152, edges=6_000_000, levels=382, nonzeros=8_300_000,
+                               flops=1.6e7, memory_bytes=140_000_000, thread_work_items=6_000_000,
+                               thread_loop_invocations=2_097_152, max_level_width=12000)
+    assert sched.schedule(wide, space).execution_mode == "sync_free"
+    cost = sched.estimate(wide, "wavefront", 128, 1, 1, True)
+    assert cost.total_s > 0 and cost.sync_s == pytest.approx(382 * sc.FALLBACK_ARCH_CONSTANTS.barrier_s)
+    f = sc.extract_workload_features([[1, 2], [2], []], [[0], [1], [2]], {"Ap": np.array([0, 1, 3, 6])},
+                                     function_props={"Ap": ["monotonically_increasing"]},
+                                     flops_per_iteration=2, thread_trip_counts=(0, 1, 2))
+    assert (f.rows, f.edges, f.levels, f.nonzeros, f.thread_work_items, f.thread_loop_invocations) == (3, 3, 3, 6, 3, 3)
+    a = sc.inspection_fingerprint({"Ap": np.arange(4), "n": 3}, ["Ap"])
+    b = sc.inspection_fingerprint({"Ap": np.arange(4), "n": 3}, ["Ap"])
+    c = sc.inspection_fingerprint({"Ap": np.arange(4)[::-1].copy(), "n": 3}, ["Ap"])
+    assert a == b and a != c
+
+
+# ---- recognition / lowering ---------------------------------------------------
+def test_decoration_recognises_the_demo_operators():
+    import ops_decorated as od
+    low = od.simple_sptrsv_csr.cuda_lowering
+    assert low.operator == "sptrsv_csr" and not low.upper and low.execution_mode == "wavefront"
+    # launcher contract: parameters, lifted locals, executor arrays (reference test_cuda_lowering.py:91-94)
+    assert low.launcher_arguments == ["Ap", "Ai", "Ax", "b", "n", "x", "wavefronts", "wavefront_ptr"]
+    assert low.kernel_arguments[-3:] == ["wavefronts", "wave_start", "wave_end"]
+    assert low.lifted_variables == ["x"] and low.lifted_loop_parameters == []
+    assert od.csc_warp_push.cuda_lowering.launcher_arguments == [
+        "Ap", "Ai", "Ax", "b", "n", "x", "dep_count", "task_nodes", "task_ptr", "task_counter"]
+    assert od.csc_warp_push.cuda_lowering.dependence_protocol == "push"
+    assert od.csr_warp_syncfree.cuda_lowering.launcher_arguments[-6:] == [
+        "dep_count", "dag_ptr", "dag_index", "task_nodes", "task_ptr", "task_counter"]
+    assert od.csr_plain_syncfree.cuda_lowering.launcher_arguments[-3:] == ["dep_count", "dag_ptr", "dag_index"]
+    assert od.csr_upper_reversed.cuda_lowering.upper
+    assert od.csr_auto.cuda_lowering is None and od.csr_auto.current_schedule is None
+    ilu = od.compile_ilu0_csr("sync_free", 128, 1)
+    assert ilu.cuda_lowering.launcher_arguments[:5] == ["A_data", "A_indices", "A_indptr", "n", "_lcd_lookup_position_0"]
+    assert ilu.cuda_lowering.lifted_loop_parameters == ["n"]      # reference test_spilu0_codegen.py:104
+    assert [l.name for l in ilu.structural_lookups] == ["_lcd_lookup_position_0"]
+    assert od.simple_sptrsv_csr.original_function(np.array([0, 1]), np.array([0]), np.array([2.0]), np.array([1.0]), 1)[0] == 0.5
+    for attr in ("build_dag", "build_execution_data", "prepare_cuda_arguments", "schedule_plan", "schedule_call",
+                 "schedule_space", "scheduler", "dag_plan", "dag_source", "execution_mode", "structural_lookups",
+                 "reduction_statements", "cuda_kernel", "cuda_launcher", "cuda_source"):
+        assert hasattr(od.simple_sptrsv_csr, attr), attr
+
+
+def test_unserved_loops_are_rejected_not_interpreted():
+    import ops_decorated as od
+    from lcd_b200.cuda_lowering import CUDALoweringError, lower_to_native
+    from lcd_b200.decorator import parallel
+    with pytest.raises(CUDALoweringError):
+        parallel(loop="i", function_props={})(od.not_served)
+    with pytest.raises(ValueError, match="block-mapped iterator"):
+        parallel(function_props={})(od.not_served)
+    src = "def f(Ap, Ai, Ax, b, n):\n    x = np.zeros(n)\n    for i in range(n):\n        x[i] = b[i]\n        for j in range(Ap[i], Ap[i + 1] - 1):\n            x[i] -= Ax[j] * x[Ai[j]]\n        x[i] /= Ax[Ap[i + 1] - 1]\n    return x\n"
+    with pytest.raises(CUDALoweringError, match="thread unroll"):
+        lower_to_native(src, "i", execution_mode="wavefront", thread_unroll_factor=2)
+    with pytest.raises(CUDALoweringError, match="n_warp"):
+        lower_to_native(src, "i", execution_mode="wavefront", n_warp=0)
+    with pytest.raises(CUDALoweringError, match="No loop"):
+        lower_to_native(src, "q", execution_mode="wavefront")
+    renamed = src.replace("Ap", "rowptr").replace("Ai", "cols").replace("x", "sol")
+    assert lower_to_native(renamed, "i", execution_mode="sync_free").roles["ptr"] == "rowptr"
+
+
+def test_structural_lookup_plan():
+    import ops_decorated as od
+    from lcd_b200 import structural_lookups as sl
+    tree = ast.parse(open(od.__file__).read())
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "ilu0_csr")
+    plan = sl.create_structural_lookup_plan(fn, od.PROPS_ILU)
+    assert plan == (sl.StructuralLookup("_lcd_lookup_position_0", "A_indptr", "A_indices", True),)
+    assert sl.structural_argument_names(plan) == ["A_indptr", "A_indices"]
+    assert sl.create_structural_lookup_plan(fn, {"A_indptr": ["monotonically_increasing"]}) == ()
+
+
+# ---- runtime contract with a fake CUDA module (reference test_cuda_lowering.py:51-80) ----
+class _FakeDeviceArray:
+    def __init__(self, host):
+        self.host = np.array(host, copy=True)
+        self.__cuda_array_interface__ = {"shape": self.host.shape}
+
+    def copy_to_host(self):
+        return self.host.copy()
+
+
+class _FakeCUDA:
+    def __init__(self):
+        self.uploads, self.syncs = [], 0
+
+    def to_device(self, array):
+        self.uploads.append(array)
+        return _FakeDeviceArray(array)
+
+    def synchronize(self):
+        self.syncs += 1
+
+
+def test_runtime_prepare_and_execute_with_fake_backend():
+    import ops_decorated as od
+    from lcd_b200 import cuda_runtime as rt
+    from lcd_b200.dag_preprocessing import WavefrontExecutionData
+    low = od.simple_sptrsv_csr.cuda_lowering
+    fake = _FakeCUDA()
+    Ap, Ai = np.array([0, 1, 3], np.int32), np.array([0, 0, 1], np.int32)
+    Ax, b = np.array([2.0, 1.0, 4.0]), np.array([2.0, 5.0])
+    data = WavefrontExecutionData(np.array([0, 1], np.int32), np.array([0, 1, 2], np.int32))
+    existing = _FakeDeviceArray(Ax)
+    prepared = rt.prepare_cuda_arguments(low, dict(Ap=Ap, Ai=Ai, Ax=existing, b=b, n=2), data,
+                                         function_globals={"np": np}, cuda_module=fake)
+    assert prepared.launcher_argument_names == tuple(low.launcher_arguments)
+    assert prepared.values["Ax"] is existing                    # device arrays pass through
+    assert prepared.values["n"] == 2                             # scalars stay on the host
+    assert isinstance(prepared.values["wavefront_ptr"], np.ndarray)   # host launch argument
+    assert isinstance(prepared.values["x"], _FakeDeviceArray) and prepared.lifted_variables == ("x",)
+    with pytest.raises(rt.CUDARuntimePreparationError):
+        rt.prepare_cuda_arguments(low, dict(Ap=Ap, Ai=Ai, Ax=object(), b=b, n=2), data, {"np": np}, fake)
+    with pytest.raises(rt.CUDARuntimePreparationError, match="Unknown prepared"):
+        prepared.copy_to_host("nope")
+    calls = []
+
+    def launcher(*args):
+        calls.append(args)
+        args[5].host[:] = [1.0, 1.0]                               # "kernel" writes x
+
+    module = rt.CompiledCUDAModule(kernel=None, launcher=launcher, namespace={"cuda": fake})
+    out = rt.execute_cuda_call(module, low, prepared, {"np": np})
+    np.testing.assert_array_equal(out, [1.0, 1.0])
+    assert len(calls) == 1 and fake.syncs == 1
+    with pytest.raises(rt.CUDARuntimePreparationError, match="synchronize"):
+        rt.execute_cuda_call(rt.CompiledCUDAModule(None, launcher, {}), low, prepared, {"np": np})
+    assert rt.evaluate_host_prelude(low, dict(n=3), {"np": np})["x"].shape == (3,)
+    with pytest.raises(rt.CUDARuntimePreparationError, match="Wavefront lowering requires"):
+        rt.prepare_cuda_arguments(low, dict(Ap=Ap, Ai=Ai, Ax=Ax, b=b, n=2), object(), {"np": np}, fake)
+
+
+# ---- generators ---------------------------------------------------------------
+def test_generators_have_the_documented_shapes():
+    from lcd_b200 import generators as gen
+    t = gen.laplacian2d_tril(256)
+    assert (t.n, t.nnz) == (65_536, 196_096)                        # first benchmark configuration
+    Ap, Ai, Ax = t.csr_arrays()
+    assert (Ai[Ap[1:] - 1] == np.arange(t.n)).all() and (Ax[Ap[1:] - 1] == 4.0).all()
+    Cp, Ci, Cx = t.csc_arrays()
+    assert (Ci[Cp[:-1]] == np.arange(t.n)).all()
+    m, b = gen.laplacian3d_ilu0(8)
+    assert m.shape == (512, 512) and m.nnz == 7 * 512 - 6 * 64 and m.has_sorted_indices
+    r = gen.random_band_lower(50_000, seed=1)
+    assert 15.0 < r.nnz / r.n < 16.2
+    Ap, Ai, Ax = r.csr_arrays()
+    rows = np.repeat(np.arange(r.n), np.diff(Ap))
+    assert (Ai <= rows).all() and (np.abs(Ax[Ai < rows]) <= 1 / 16).all()
+    s = gen.supernodal_random(3000, seed=2, widths=(16, 32), min_targets=2, max_targets=5)
+    assert s.sn[-1] == 3000 and (np.diff(s.Lip) >= np.diff(s.sn)).all() and s.Lp.dtype == np.int64
+    L = s.to_csc()
+    assert (L.indices >= np.repeat(np.arange(3000), np.diff(L.indptr))).all()
