@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Benchmark of the dependence-DAG hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+One step is one pass of the hot path over one batch of synthetic input.  The
+default workload is the sync-free / wavefront SpTRSV configuration: a random
+lower-triangular CSR matrix with n = 4,194,304 rows (about 15.6 entries per
+row, half of them inside a band of 64), fp64, one right-hand side; the metric is
+SpTRSV GFLOP/s with the reference's formula (n + 2 nnz) / t
+(benchmark/sptrsv_benchmark.py:626 of the reference).  With N > 1 every rank holds
+the matrix and solves its own right-hand side (multi-RHS sharding by column,
+no data-path collective, weak scaling).
+
+Prints ONE JSON line (rank 0).  ``--impl reference`` times the CPU restatement of
+the reference's sequential loop on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "sptrsv_gflops_fp64"
+UNIT = "GFLOP/s"
+WORKLOADS = {
+    # name: (kind, size)
+    "sptrsv_random_n4194304": ("band", 4_194_304),
+    "sptrsv_random_n1048576": ("band", 1_048_576),
+    "sptrsv_lap2d_g256": ("lap2d", 256),
+    "sptrsv_lap3d_g128": ("lap3d", 128),
+}
+DEFAULT_WORKLOAD = "sptrsv_random_n4194304"
+
+
+def log(*args):
+    print(*args, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ inputs ----
+def load_workload(name, rank=0, world=1, barrier=None):
+    """Seeded synthetic matrix of the workload; generated once per box (rank 0) and
+    shared through a cache file so that several ranks / both arms reuse it."""
+    from lcd_b200 import generators as gen
+    kind, size = WORKLOADS[name]
+    cache = os.path.join(os.environ.get("LCD_B200_CACHE", "/tmp"), f"lcd_b200_{name}_seed0.npz")
+    if rank == 0 and not os.path.exists(cache):
+        t0 = time.time()
+        if kind == "band":
+            tri = gen.random_band_lower(size, seed=0)
+        elif kind == "lap2d":
+            tri = gen.laplacian2d_tril(size, seed=0)
+        else:
+            tri = gen.laplacian3d_tril(size, seed=0)
+        Ap, Ai, Ax = tri.csr_arrays()
+        tmp = cache + f".tmp{os.getpid()}.npz"
+        np.savez(tmp, Ap=Ap, Ai=Ai, Ax=Ax, b=tri.b)
+        os.replace(tmp, cache)
+        log(f"[bench] generated {name} in {time.time() - t0:.1f}s")
+    if barrier is not None:
+        barrier()
+    data = np.load(cache)
+    Ap, Ai, Ax, b = data["Ap"], data["Ai"], data["Ax"], data["b"]
+    if rank:
+        b = np.random.default_rng([0, rank]).uniform(-1.0, 1.0, len(b))  # own RHS column
+    return Ap, Ai, Ax, b
+
+
+def algorithmic_bytes(n, nnz):
+    """nnz (8 + 4) + (n + 1) 4 + n 8 (b) + n 8 (x): every matrix entry, pointer and
+    vector element moved once; gathers of x, flags and DAG arrays are not counted."""
+    return nnz * 12 + (n + 1) * 4 + n * 16
+
+
+def flops(n, nnz):
+    return n + 2 * nnz
+
+
+# ------------------------------------------------------------------ clocks ----
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.rows = []
+        self.proc = None
+        self.gpu_index = gpu_index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for row in self.rows:
+            try:
+                sm.append(float(row[1]))
+                smax.append(float(row[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, cell in zip(names, row[5:9]):
+                if cell.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------- reference arm ----
+def run_reference(args):
+    """The reference's CPU path for this operator is a sequential loop nest
+    (compiler/demo/sptrsv.py:26-34); its compiled restatement (oracle/lcd_oracle.c)
+    is timed on one host core.  A step is one full solve of the workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as cpu
+    cpu.build()
+    Ap, Ai, Ax, b = load_workload(args.workload)
+    n, nnz = len(Ap) - 1, len(Ai)
+    for _ in range(max(1, min(args.warmup, 2))):
+        cpu.sptrsv_csr_lower(Ap, Ai, Ax, b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        x = cpu.sptrsv_csr_lower(Ap, Ai, Ax, b)
+    elapsed = time.perf_counter() - t0
+    per_step = elapsed / args.steps
+    value = flops(n, nnz) / per_step / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": args.workload, "n": n, "nnz": nnz, "format": "csr_lower"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
+                         "sample": f"{args.steps} full solves of the workload",
+                         "host_cores_available": os.cpu_count()},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "effective_gbs": algorithmic_bytes(n, nnz) / per_step / 1e9,
+        "residual": cpu.relative_residual_csr(Ap, Ai, Ax, x, b),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm ----
+def measured_peak_gbs():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as handle:
+            return float(json.load(handle)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def run_native(args):
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from lcd_b200 import _native as nat, ops
+    nat.load()
+    Ap, Ai, Ax, b = load_workload(args.workload, rank, world, barrier)
+    n, nnz = len(Ap) - 1, len(Ai)
+    up = lambda a: torch.from_numpy(a).to(dev)
+    dAp, dAi, dAx, db = up(Ap), up(Ai), up(Ax), up(b)
+    x = torch.empty(n, dtype=torch.float64, device=dev)
+    status = ops.new_status(dev)
+    lanes, threads = args.lanes, args.threads
+
+    def step():
+        ops.sptrsv_csr_syncfree(dAp, dAi, dAx, db, x, lanes=lanes, threads=threads,
+                                status=status, sync=False)
+
+    # correctness before timing: status word and relative residual (fp64 tolerance 1e-12)
+    step()
+    code, node = ops.read_status(status)
+    if code != 0:
+        raise RuntimeError(f"solver reported {nat.error_string(code)} at row {node}")
+    from oracle import oracle as cpu   # checker only (residual), never the measured path
+    residual = cpu.relative_residual_csr(Ap, Ai, Ax, x.cpu().numpy(), b)
+    if not residual <= 1e-12:
+        raise RuntimeError(f"relative residual {residual:.3e} exceeds 1e-12")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    torch.cuda.synchronize()
+    events[0].record()
+    for k in range(args.steps):
+        step()
+        events[k + 1].record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    total_ms = events[0].elapsed_time(events[-1])
+    per_launch_ms = [events[k].elapsed_time(events[k + 1]) for k in range(args.steps)]
+    if ops.read_status(status)[0] != 0:
+        raise RuntimeError("solver reported an error inside the timed region")
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * flops(n, nnz) / (ms_per_step * 1e-3) / 1e9
+
+    # end to end through the public API: the decorated operator called with host
+    # (pinned) arrays; upload, solve and download are all inside the timed region
+    e2e = None
+    if rank == 0 or world > 1:
+        e2e = measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier)
+
+    extras = {}
+    if rank == 0 and not args.skip_extras:
+        extras = measure_extras(args, dAp, dAi, dAx, db, x, status, Ap, Ai, Ax, b)
+    cpu_baseline = None
+    if rank == 0 and world == 1:
+        cpu_baseline = measure_cpu_baseline(cpu, Ap, Ai, Ax, b, n, nnz)
+    if rank == 0:
+        peak, peak_kind = measured_peak_gbs()
+        kernel_ms = float(np.mean(per_launch_ms))
+        achieved = algorithmic_bytes(n, nnz) / (kernel_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "n": n, "nnz": nnz, "format": "csr_lower",
+                       "mode": "sync_free", "lanes_per_row": lanes or "auto",
+                       "threads_per_block": threads or 1024, "rhs_per_gpu": 1,
+                       "l2_policy": "inputs (%.2f GB) exceed the 126 MB L2" % (
+                           algorithmic_bytes(n, nnz) / 1e9)},
+            "e2e": e2e, "gpu_launches": args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "csr_syncfree_row_kernel", "kernel_ms": kernel_ms},
+            "cpu_baseline": cpu_baseline, "clocks": clocks,
+            "effective_gbs": world * achieved, "residual": residual,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier):
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from lcd_b200.decorator import parallel
+    op = parallel(block_map="i", thread_map="j", execution_mode="sync_free", threads_per_block=128,
+                  thread_unroll=1,
+                  function_props={"Ap": ["monotonically_increasing"], "Ai": []})(_sptrsv_csr)
+    pinned = [torch.from_numpy(a).pin_memory().numpy() for a in (Ap, Ai, Ax, b)]
+    op(*pinned, n)          # first call builds and caches the plan (DAG on the device)
+    steps = max(2, min(args.steps, 5))
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out = op(*pinned, n)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([elapsed], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    per_call = elapsed / steps
+    h2d = sum(a.nbytes for a in pinned)
+    return {"value": world * flops(n, nnz) / per_call / 1e9, "unit": UNIT,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(out.nbytes),
+            "ms_per_call": per_call * 1e3, "calls": steps,
+            "api": "lcd_b200.decorator.parallel(...)(sptrsv_csr)(Ap, Ai, Ax, b, n)"}
+
+
+def _sptrsv_csr(Ap, Ai, Ax, b, n):
+    x = np.zeros(n)
+    for i in range(n):
+        x[i] = b[i]
+        for j in range(Ap[i], Ap[i + 1] - 1):
+            x[i] -= Ax[j] * x[Ai[j]]
+        x[i] /= Ax[Ap[i + 1] - 1]
+    return x
+
+
+def measure_extras(args, dAp, dAi, dAx, db, x, status, Ap, Ai, Ax, b):
+    """DAG build time and the wavefront mode on the same matrix (one run each)."""
+    import torch
+    from lcd_b200 import ops
+    out = {}
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dag = ops.dag_build("csr_lower", dAp, dAi)
+    torch.cuda.synchronize()
+    out["dag_build_ms"] = (time.perf_counter() - t0) * 1e3
+    out["levels"] = dag.n_levels
+    out["dag_edges"] = dag.n_edges
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ops.sptrsv_wavefront("csr_lower", dAp, dAi, dAx, db, dag.wavefronts, dag.wavefront_ptr, None,
+                         x, mode="cooperative", lanes=16, status=status, sync=False)
+    e1.record()
+    torch.cuda.synchronize()
+    out["wavefront_ms"] = e0.elapsed_time(e1)
+    out["wavefront_status"] = ops.read_status(status)[0]
+    return out
+
+
+def measure_cpu_baseline(cpu, Ap, Ai, Ax, b, n, nnz):
+    """The CPU restatement of the reference's loop on one host core: repeated full
+    solves for about ten seconds (at least three)."""
+    cpu.sptrsv_csr_lower(Ap, Ai, Ax, b)
+    count, t0 = 0, time.perf_counter()
+    while count < 3 or (time.perf_counter() - t0 < 10.0 and count < 200):
+        cpu.sptrsv_csr_lower(Ap, Ai, Ax, b)
+        count += 1
+    per = (time.perf_counter() - t0) / count
+    return {"value": flops(n, nnz) / per / 1e9, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{count} full solves of the workload ({per * 1e3:.1f} ms each)",
+            "host_cores_available": os.cpu_count()}
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="native", choices=("native", "reference"))
+    parser.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    parser.add_argument("--lanes", type=int, default=0)
+    parser.add_argument("--threads", type=int, default=0)
+    parser.add_argument("--skip-extras", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "native" else args.warmup
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

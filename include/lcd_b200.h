@@ -54,8 +54,11 @@ enum {
     LCD_SOLVE_UNIT_DIAG = 2,  /* implicit unit diagonal, no division (needs OF_FULL) */
     LCD_SOLVE_OF_FULL = 4,    /* the triangle is the part of a full sorted CSR row before
                                  (lower) / after (upper) diag_pos[row]; used on ILU0 factors */
-    LCD_SOLVE_EXACT = 8       /* one lane per row, unfused multiply/subtract in storage order
+    LCD_SOLVE_EXACT = 8,      /* one lane per row, unfused multiply/subtract in storage order
                                  and a true division: bit-identical to the sequential loop */
+    LCD_SOLVE_CHAIN = 16      /* sync-free CSR only: one warp walks each chunk of rows in blocks
+                                 of 32 with no waiting inside a chunk; for matrices whose levels
+                                 hold only a few rows (ignored together with LCD_SOLVE_EXACT) */
 };
 
 /* Device-side status block every solver uses: 8 int32 words in device memory,

@@ -128,8 +128,10 @@ def _solve_flags(upper, unit_diag, of_full, exact):
 
 
 def sptrsv_csr_syncfree(Ap, Ai, Ax, b, x=None, *, upper=False, unit_diag=False, diag_pos=None,
-                        exact=False, lanes=0, threads=0, status=None, timeout_ms=0, sync=True):
-    """Sync-free CSR triangular solve; returns x (a new tensor unless given)."""
+                        exact=False, chain=False, lanes=0, threads=0, status=None, timeout_ms=0,
+                        sync=True):
+    """Sync-free CSR triangular solve; returns x (a new tensor unless given).
+    ``chain=True`` selects the kernel for matrices with narrow levels."""
     _require(Ap, torch.int32, "Ap")
     _require(Ai, torch.int32, "Ai")
     _require(Ax, torch.float64, "Ax")
@@ -138,6 +140,8 @@ def sptrsv_csr_syncfree(Ap, Ai, Ax, b, x=None, *, upper=False, unit_diag=False, 
     x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
     status = new_status(b.device) if status is None else status
     flags = _solve_flags(upper, unit_diag, diag_pos is not None, exact)
+    if chain:
+        flags |= nat.SOLVE_CHAIN
     host = ctypes.c_int(0)
     rc = nat.load().lcd_sptrsv_csr_syncfree(
         n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
