@@ -191,6 +191,28 @@ int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
                    int32_t n_levels, int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
                    void *stream, int *status_host);
 
+/*
+ * ILU(0) for callers that cannot allocate.  No counterpart in the reference: it exists
+ * for users of this library that call it where device memory cannot be requested (inside
+ * a fixed memory pool, in a callback that runs while the allocator is held elsewhere, or
+ * in a loop where a device-wide synchronising cudaMalloc is not acceptable).
+ * Same factorisation and same result as lcd_spilu0_csr in sync-free mode, but the
+ * completion flags and the status block live in a fixed array inside the library
+ * (4 MiB per GPU, held until the process exits) instead of caller scratch; the call
+ * performs no cudaMalloc / cudaFree and calls no allocating routine.
+ *   - n is limited to LCD_ILU0_STATIC_MAX_ROWS (1,048,576); larger n returns
+ *     LCD_ERR_TOO_LARGE.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call outside any stream capture.
+ *   - All calls on one device share the array: calls that overlap on the GPU (two
+ *     streams, two host threads) race.  Issue them one after the other.
+ *   - status_host is required; the call synchronises `stream` and reports there.
+ */
+#define LCD_ILU0_STATIC_MAX_ROWS (1 << 20)
+int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                          double *Ax, const int32_t *diag_pos, int lanes_per_row,
+                          int32_t timeout_ms, void *stream, int *status_host);
+
 /* ---- supernodal SpTRSV ------------------------------------------------------- */
 /*
  * Lower-triangular solve on the supernodal layout of

@@ -62,6 +62,8 @@ _SIGNATURES = {
                                      ctypes.POINTER(c_int)]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_spilu0_csr_static": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, c_int32, _P,
+                                      ctypes.POINTER(c_int)]),
     "lcd_supernodal_pending": (c_int, [c_int32, _P, _P, _P, _P, _P, _P]),
     "lcd_supernodal_strip_rows": (c_int, []),
     "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,

@@ -194,3 +194,81 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
     }
     return finish(status_dev, st, status_host);
 }
+
+// ---- variant that allocates nothing -------------------------------------------
+// Some callers cannot obtain device memory at the moment they need a factorisation:
+// code running inside a memory pool that must not grow, a solver callback invoked
+// while another library holds the allocator, or a latency-critical loop in which a
+// cudaMalloc (which may synchronise the whole device) is not acceptable.  For them
+// the per-row completion flags and the status block of the sync-free ILU(0) live in
+// the fixed array below instead of caller-provided scratch.  Every GPU that loads the
+// library carries the array (4 MiB + 256 B) until the process exits.
+
+constexpr int kStaticStatusWords = 64;  // status block, padded to keep the flags aligned
+static __device__ __align__(256) int32_t g_ilu0_static_scratch[kStaticStatusWords +
+                                                              LCD_ILU0_STATIC_MAX_ROWS];
+
+// In host code the array's name is only a handle: the device address has to be asked
+// for, once per device, with that device current.
+static int32_t *ilu0_static_scratch_for_current_device(int *rc) {
+    constexpr int kMaxDevices = 64;
+    static int32_t *address[kMaxDevices] = {nullptr};
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        if (e != cudaSuccess) set_cuda_error(e, "cudaGetDevice");
+        *rc = e != cudaSuccess ? LCD_ERR_CUDA : LCD_ERR_TOO_LARGE;
+        return nullptr;
+    }
+    if (!address[dev]) {
+        void *ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_ilu0_static_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_cuda_error(e, "cudaGetSymbolAddress(g_ilu0_static_scratch)");
+            *rc = LCD_ERR_CUDA;
+            return nullptr;
+        }
+        address[dev] = static_cast<int32_t *>(ptr);
+    }
+    *rc = LCD_OK;
+    return address[dev];
+}
+
+extern "C" int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                     double *Ax, const int32_t *diag_pos, int lanes_per_row,
+                                     int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || !status_host) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > LCD_ILU0_STATIC_MAX_ROWS) return LCD_ERR_TOO_LARGE;  // the fixed scratch holds 2^20 rows
+    if (n > 0 && (!Ap || !Ai || !Ax || !diag_pos)) return LCD_ERR_INVALID_ARGUMENT;
+    int rc = LCD_OK;
+    int32_t *scratch = ilu0_static_scratch_for_current_device(&rc);
+    if (!scratch) return rc;
+    int32_t *status_dev = scratch;
+    int32_t *done = scratch + kStaticStatusWords;
+    cudaStream_t st = (cudaStream_t)stream;
+    int G = lanes_per_row;
+    if (G <= 0) {
+        const double avg = n > 0 ? (double)nnz / n : 0.0;
+        G = avg <= 12 ? 4 : (avg <= 40 ? 8 : (avg <= 96 ? 16 : 32));
+    }
+    // the array keeps the previous call's contents: clear what has to start at zero
+    rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
+        Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, nullptr, status_dev,
+                     timeout_ns(timeout_ms)};
+        cudaError_t e;
+        switch (G) {
+            case 1: e = launch_ilu0<1>(p, 0, nullptr, 0, st); break;
+            case 2: e = launch_ilu0<2>(p, 0, nullptr, 0, st); break;
+            case 4: e = launch_ilu0<4>(p, 0, nullptr, 0, st); break;
+            case 8: e = launch_ilu0<8>(p, 0, nullptr, 0, st); break;
+            case 16: e = launch_ilu0<16>(p, 0, nullptr, 0, st); break;
+            case 32: e = launch_ilu0<32>(p, 0, nullptr, 0, st); break;
+            default: return LCD_ERR_INVALID_ARGUMENT;
+        }
+        LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}
