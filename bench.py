@@ -39,6 +39,16 @@ WORKLOADS = {
     "sptrsv_random_n1048576": ("band", 1_048_576),
     "sptrsv_lap2d_g256": ("lap2d", 256),
     "sptrsv_lap3d_g128": ("lap3d", 128),
+    "sptrsv_lap3d_g256": ("lap3d", 256),
+}
+# side workloads (other configurations of the path); they print their own JSON line
+SIDE_WORKLOADS = {
+    "ilu0_lap3d_g128": ("ilu0", 128),
+    "ilu0_lap3d_g64": ("ilu0", 64),
+    "supernodal_n1048576": ("supernodal", 1_048_576),
+    "supernodal_n131072": ("supernodal", 131_072),
+    "multirhs_lap3d_g192": ("multirhs", 192),
+    "multirhs_lap3d_g96": ("multirhs", 96),
 }
 DEFAULT_WORKLOAD = "sptrsv_random_n4194304"
 
@@ -247,14 +257,14 @@ def run_native(args):
     # end to end through the public API: the decorated operator called with host
     # (pinned) arrays; upload, solve and download are all inside the timed region
     e2e = None
-    if rank == 0 or world > 1:
+    if not args.kernel_only:
         e2e = measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier)
 
     extras = {}
-    if rank == 0 and not args.skip_extras:
+    if rank == 0 and not args.skip_extras and not args.kernel_only:
         extras = measure_extras(args, dAp, dAi, dAx, db, x, status, Ap, Ai, Ax, b)
     cpu_baseline = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.kernel_only:
         cpu_baseline = measure_cpu_baseline(cpu, Ap, Ai, Ax, b, n, nnz)
     if rank == 0:
         peak, peak_kind = measured_peak_gbs()
@@ -360,19 +370,193 @@ def measure_cpu_baseline(cpu, Ap, Ai, Ax, b, n, nnz):
             "host_cores_available": os.cpu_count()}
 
 
+# ------------------------------------------------------------ side workloads ----
+def _time_steps(step, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    events[0].record()
+    for k in range(steps):
+        step()
+        events[k + 1].record()
+    torch.cuda.synchronize()
+    return [events[k].elapsed_time(events[k + 1]) for k in range(steps)]
+
+
+def _host_time(fn, min_seconds=2.0, min_count=2):
+    fn()
+    count, t0 = 0, time.perf_counter()
+    while count < min_count or time.perf_counter() - t0 < min_seconds:
+        fn()
+        count += 1
+    return (time.perf_counter() - t0) / count, count
+
+
+def run_side_workload(args):
+    """ILU0, supernodal and multi-RHS configurations: one JSON line each with the
+    kernel time, the effective bandwidth against the measured copy peak, the parity
+    check and the CPU restatement timed on one host core."""
+    import torch
+    import torch.distributed as dist
+    from lcd_b200 import generators as gen, ops
+    from oracle import oracle as cpu
+    kind, size = SIDE_WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    peak, peak_kind = measured_peak_gbs()
+    line = {"workload": args.workload, "n_gpus": world, "steps": args.steps, "dtype": "f64",
+            "data": "synthetic", "peak_gbs": peak, "peak_kind": peak_kind}
+    if kind == "ilu0":
+        mat, b = gen.laplacian3d_ilu0(size, seed=0)
+        Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+        n, nnz = len(Ap) - 1, len(Ai)
+        dAp, dAi, dA0, db = up(Ap), up(Ai), up(Ax), up(b)
+        work = dA0.clone()
+        pos = ops.diag_positions(dAp, dAi)
+        dag = ops.dag_build("ilu0_csr", dAp, dAi)
+        done = torch.empty(n, dtype=torch.int32, device=dev)
+        status = ops.new_status(dev)
+        y, x = torch.empty_like(db), torch.empty_like(db)
+        results = {}
+        for mode in ("sync_free", "wavefront"):
+            def step():
+                work.copy_(dA0)
+                ops.spilu0_csr(dAp, dAi, work, pos, mode=mode, wavefronts=dag.wavefronts,
+                               wavefront_ptr_host=dag.wavefront_ptr_host, done=done,
+                               status=status, sync=False)
+            ms = _time_steps(step, args.steps, args.warmup)
+            copy_ms = float(np.median(_time_steps(lambda: work.copy_(dA0), args.steps, 1)))
+            results[mode] = float(np.median(ms)) - copy_ms
+        want = cpu.ilu0_csr(Ap, Ai, Ax, fast=True)
+        line["bit_identical_to_sequential"] = bool(np.array_equal(work.cpu().numpy(), want))
+        fwd = _time_steps(lambda: ops.sptrsv_csr_syncfree(dAp, dAi, work, db, y, diag_pos=pos,
+                                                          unit_diag=True, status=status, sync=False),
+                          args.steps, args.warmup)
+        bwd = _time_steps(lambda: ops.sptrsv_csr_syncfree(dAp, dAi, work, y, x, diag_pos=pos,
+                                                          upper=True, status=status, sync=False),
+                          args.steps, args.warmup)
+        hp = pos.cpu().numpy()
+        x_ref = cpu.sptrsv_upper_of_full(Ap, Ai, want, hp,
+                                         cpu.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, b))
+        err = float(np.max(np.abs(x.cpu().numpy() - x_ref)) / np.max(np.abs(x_ref)))
+        cpu_s, count = _host_time(lambda: cpu.ilu0_csr(Ap, Ai, Ax, fast=True))
+        bytes_ilu = 20 * nnz + 4 * (n + 1) + 4 * n
+        best = min(results.values())
+        line.update({"metric": "spilu0_ms_per_factorization", "unit": "ms", "higher_is_better": False,
+                     "value": best, "sync_free_ms": results["sync_free"],
+                     "wavefront_ms": results["wavefront"], "n": n, "nnz": nnz,
+                     "levels": dag.n_levels, "gflops_2nnz": 2 * nnz / (best * 1e-3) / 1e9,
+                     "forward_solve_ms": float(np.median(fwd)),
+                     "backward_solve_ms": float(np.median(bwd)), "solve_max_rel_error": err,
+                     "roofline": {"bound": "hbm", "achieved": bytes_ilu / (best * 1e-3) / 1e9,
+                                  "peak": peak, "unit": "GB/s",
+                                  "frac": bytes_ilu / (best * 1e-3) / 1e9 / peak},
+                     "cpu_baseline": {"value": cpu_s * 1e3, "unit": "ms", "cores": 1, "kind": "port",
+                                      "sample": f"{count} full factorisations"}})
+    elif kind == "supernodal":
+        from lcd_b200 import supernodal
+        t0 = time.time()
+        s = gen.supernodal_random(size, seed=0)
+        log(f"[bench] generated {args.workload} in {time.time() - t0:.1f}s "
+            f"({s.Lx.nbytes / 1e9:.2f} GB of panels, {s.n_super} supernodes)")
+        plan = supernodal.analyse(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.col_to_super, device=dev)
+        db = up(s.b)
+        x = torch.empty_like(db)
+        ms = _time_steps(lambda: supernodal.solve(plan, db, x, sync=False), args.steps, args.warmup)
+        best = float(np.median(ms))
+        code = ops.read_status(plan.status)[0]
+        xs = x.cpu().numpy()
+        check_n = min(size, 131_072)
+        if size <= 131_072:
+            want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
+            err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
+        else:
+            err = None
+        cpu_s, count = _host_time(lambda: cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b),
+                                  min_seconds=5.0, min_count=1)
+        if err is None:
+            want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
+            err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
+        nbytes = plan.algorithmic_bytes
+        line.update({"metric": "supernodal_sptrsv_gflops", "unit": "GFLOP/s", "higher_is_better": True,
+                     "value": plan.flops / (best * 1e-3) / 1e9, "ms_per_step": best,
+                     "n": size, "n_super": plan.n_super, "tasks": plan.n_tasks,
+                     "panel_gb": plan.panel_values * 8 / 1e9, "status": code,
+                     "max_rel_error_vs_sequential": err,
+                     "roofline": {"bound": "hbm", "achieved": nbytes / (best * 1e-3) / 1e9,
+                                  "peak": peak, "unit": "GB/s",
+                                  "frac": nbytes / (best * 1e-3) / 1e9 / peak},
+                     "cpu_baseline": {"value": plan.flops / cpu_s / 1e9, "unit": "GFLOP/s", "cores": 1,
+                                      "kind": "port", "sample": f"{count} full solves, {cpu_s * 1e3:.0f} ms each"}})
+    else:  # multi-RHS, sharded by column over the ranks
+        from lcd_b200.multigpu import ShardedMultiRHS
+        nrhs = 64
+        tri = gen.laplacian3d_tril(size, seed=0)
+        Ap, Ai, Ax = tri.csr_arrays()
+        n, nnz = tri.n, tri.nnz
+        solver = ShardedMultiRHS(Ap, Ai, Ax, device=dev)
+        start, stop = solver.shard(nrhs)
+        k = stop - start
+        rng = np.random.default_rng([0, 7])
+        B = torch.from_numpy(rng.uniform(-1.0, 1.0, (k, n))).to(dev)       # this rank's columns
+        out = [None]
+        def step():
+            out[0] = solver.solve(B)
+        ms = _time_steps(step, args.steps, args.warmup)
+        total_ms = float(np.sum(ms))
+        if world > 1:
+            t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total_ms = float(t.item())
+        per = total_ms / args.steps
+        X = out[0].cpu().numpy()
+        col = 0
+        want = cpu.sptrsv_csr_lower(Ap, Ai, Ax, B[col].cpu().numpy())
+        err = float(np.max(np.abs(X[col] - want)) / np.max(np.abs(want)))
+        nbytes = world * (12 * nnz + 4 * (n + 1)) + 16 * n * nrhs
+        cpu_s, count = _host_time(lambda: cpu.sptrsv_csr_lower(Ap, Ai, Ax, want), min_seconds=2.0)
+        line.update({"metric": "multirhs_sptrsv_gflops", "unit": "GFLOP/s", "higher_is_better": True,
+                     "scaling": "strong", "value": nrhs * flops(n, nnz) / (per * 1e-3) / 1e9,
+                     "ms_per_step": per, "n": n, "nnz": nnz, "nrhs": nrhs, "rhs_per_gpu": k,
+                     "max_rel_error_col0": err,
+                     "roofline": {"bound": "hbm", "achieved": nbytes / (per * 1e-3) / 1e9,
+                                  "peak": peak * world, "unit": "GB/s",
+                                  "frac": nbytes / (per * 1e-3) / 1e9 / (peak * world)},
+                     "cpu_baseline": {"value": flops(n, nnz) / cpu_s / 1e9, "unit": "GFLOP/s", "cores": 1,
+                                      "kind": "port", "sample": f"{count} single-RHS solves"}})
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="native", choices=("native", "reference"))
-    parser.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    parser.add_argument("--workload", default=DEFAULT_WORKLOAD,
+                        choices=sorted(WORKLOADS) + sorted(SIDE_WORKLOADS))
     parser.add_argument("--lanes", type=int, default=0)
     parser.add_argument("--threads", type=int, default=0)
-    parser.add_argument("--skip-extras", action="store_true")
+    parser.add_argument("--skip-extras", action="store_true",
+                        help="skip the DAG-build and wavefront side measurements")
+    parser.add_argument("--kernel-only", action="store_true",
+                        help="time the kernel only (profiling runs): no e2e, CPU baseline, extras")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "native" else args.warmup
-    if args.impl == "reference":
+    if args.workload in SIDE_WORKLOADS:
+        run_side_workload(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_native(args)

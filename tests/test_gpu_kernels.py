@@ -285,6 +285,20 @@ def test_csr_syncfree_multi_rhs(cuda, oracle, nrhs):
         assert csr_residual(Ap, Ai, Ax, X[:, q], B[:, q]) <= RESIDUAL_TOL
 
 
+def test_sharded_multi_rhs_single_rank(cuda, oracle):
+    """The multi-GPU front end with one rank: 70 columns go through two launches."""
+    from lcd_b200 import generators as gen
+    from lcd_b200.multigpu import ShardedMultiRHS
+    tri = gen.laplacian3d_tril(14, seed=2, nrhs=70)
+    Ap, Ai, Ax = tri.csr_arrays()
+    solver = ShardedMultiRHS(Ap, Ai, Ax)
+    X = host(solver.solve(np.asarray(tri.b), gather=True))
+    assert X.shape == (70, tri.n)
+    for q in (0, 33, 63, 64, 69):
+        want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, np.ascontiguousarray(tri.b[:, q]))
+        np.testing.assert_allclose(X[q], want, rtol=1e-10, atol=1e-12)
+
+
 def test_transpose_roundtrip(cuda):
     import torch
     from lcd_b200 import ops
