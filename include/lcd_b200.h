@@ -177,6 +177,16 @@ int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_t *Ap, cons
                          int lanes_per_row, int32_t *status_dev, int32_t timeout_ms, void *stream,
                          int *status_host);
 
+/* Multi-RHS level-synchronous CSR solve on row-major n x nrhs blocks (nrhs <= 64): a warp
+ * per row, lanes over right-hand sides, one cooperative launch.  The choice between this
+ * and lcd_sptrsv_csr_syncfree_multi follows the level width (wide levels: this one). */
+int lcd_sptrsv_wavefront_multi(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap,
+                               const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
+                               const double *B, double *X, int64_t ld, int flags,
+                               const int32_t *wavefronts, const int32_t *wavefront_ptr_dev,
+                               int32_t n_levels, int32_t *status_dev, int32_t timeout_ms,
+                               void *stream, int *status_host);
+
 /* ---- SpILU0 (CSR, in place) -------------------------------------------------- */
 /*
  * In-place ILU(0) of a CSR matrix with sorted rows; arithmetic identical to the
@@ -242,6 +252,38 @@ int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
                           const int64_t *Lp, const double *Lx, const int32_t *col_to_super,
                           int32_t *pending, int32_t *solved, double *x, int32_t *status_dev,
                           int32_t timeout_ms, void *stream, int *status_host);
+
+/* ---- block-row partition of one solve across the GPUs of a node ---------------- */
+/*
+ * No counterpart in the reference (it is single-GPU).  One process per GPU; rank q owns
+ * the nodes [bounds[q], bounds[q+1]) and holds a full-length x array in its own memory.
+ * A rank that produces a value some other rank needs stores it straight into that rank's
+ * x array through a peer mapping (NVLink); consumers only ever poll their own memory.
+ *   lcd_peer_alloc / lcd_peer_open / lcd_peer_close / lcd_peer_free
+ *       allocate an x array that other processes of the node can map (CUDA IPC handle,
+ *       64 bytes) -- the only entry points of the library that allocate device memory.
+ *   lcd_partition_need_mask
+ *       need_mask[c] (one byte per row, array padded to a multiple of 4 bytes) gets bit q
+ *       when a row owned by rank q uses column c produced by another rank.
+ *   lcd_sptrsv_csr_syncfree_part
+ *       solves the nodes [task_begin, task_end) of a CSR triangular system.  x must have
+ *       been filled with the reserved pattern (lcd_fill_u64(x, n, ~0)) on EVERY rank, and
+ *       all ranks must have synchronised, before any rank makes this call.  peer_x is a
+ *       host array of n_ranks device pointers (rank q's x as mapped in this process).
+ */
+int lcd_peer_alloc(int64_t bytes, void **ptr, unsigned char *handle64);
+int lcd_peer_open(const unsigned char *handle64, void **ptr);
+int lcd_peer_close(void *ptr);
+int lcd_peer_free(void *ptr);
+int lcd_partition_need_mask(int32_t n, const int32_t *Ap, const int32_t *Ai, int flags,
+                            const int32_t *bounds_dev, int32_t parts, unsigned char *need_mask,
+                            void *stream);
+int lcd_sptrsv_csr_syncfree_part(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                 const double *Ax, const double *b, double *x, int flags,
+                                 int32_t task_begin, int32_t task_end,
+                                 const unsigned char *need_mask, double *const *peer_x,
+                                 int32_t n_ranks, int threads_per_block, int32_t *status_dev,
+                                 int32_t timeout_ms, void *stream, int *status_host);
 
 /* Scheduling knobs of the one-lane-per-row sync-free kernel (process-wide).  They
  * change waiting behaviour only, never results.  The reference's counterpart is the

@@ -60,6 +60,9 @@ _SIGNATURES = {
     "lcd_sptrsv_wavefront": (c_int, [c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P,
                                      _P, _P, c_int32, c_int, c_int, _P, c_int32, _P,
                                      ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_wavefront_multi": (c_int, [c_int32, c_int64, c_int32, _P, _P, _P, _P, _P, _P, c_int64,
+                                           c_int, _P, _P, c_int32, _P, c_int32, _P,
+                                           ctypes.POINTER(c_int)]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_spilu0_csr_static": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, c_int32, _P,
@@ -68,6 +71,14 @@ _SIGNATURES = {
     "lcd_supernodal_strip_rows": (c_int, []),
     "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
                                       _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_peer_alloc": (c_int, [c_int64, ctypes.POINTER(c_void_p), ctypes.c_char_p]),
+    "lcd_peer_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
+    "lcd_peer_close": (c_int, [_P]),
+    "lcd_peer_free": (c_int, [_P]),
+    "lcd_partition_need_mask": (c_int, [c_int32, _P, _P, c_int, _P, c_int32, _P, _P]),
+    "lcd_sptrsv_csr_syncfree_part": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, c_int, c_int32,
+                                             c_int32, _P, ctypes.POINTER(c_void_p), c_int32, c_int,
+                                             _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_set_tuning": (c_int, [c_int, c_int]),
     "lcd_debug_set_trace": (c_int, [_P]),
     "lcd_checksum_i32": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_uint64 * 2), _P]),

@@ -128,3 +128,42 @@ extern "C" int lcd_device_sm_count(int *count) {
     *count = sm_count();
     return LCD_OK;
 }
+
+// ---- peer-visible buffers for the multi-GPU partitioned solve --------------------
+// One process per GPU: a rank allocates its x array here, exports an IPC handle, and
+// the other ranks of the node map it.  These are the only entry points that allocate.
+extern "C" int lcd_peer_alloc(int64_t bytes, void **ptr, unsigned char *handle64) {
+    if (bytes <= 0 || !ptr || !handle64) return LCD_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    LCD_CUDA_TRY(cudaMalloc(ptr, (size_t)bytes));
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, *ptr);
+    if (e != cudaSuccess) {
+        set_cuda_error(e, "cudaIpcGetMemHandle");
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return LCD_ERR_CUDA;
+    }
+    memcpy(handle64, &h, 64);
+    return LCD_OK;
+}
+
+extern "C" int lcd_peer_open(const unsigned char *handle64, void **ptr) {
+    if (!handle64 || !ptr) return LCD_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, 64);
+    LCD_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return LCD_OK;
+}
+
+extern "C" int lcd_peer_close(void *ptr) {
+    if (!ptr) return LCD_OK;
+    LCD_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return LCD_OK;
+}
+
+extern "C" int lcd_peer_free(void *ptr) {
+    if (!ptr) return LCD_OK;
+    LCD_CUDA_TRY(cudaFree(ptr));
+    return LCD_OK;
+}

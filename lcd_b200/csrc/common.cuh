@@ -58,6 +58,9 @@ __device__ __forceinline__ double ld_relaxed_f64(const double *p) {
 __device__ __forceinline__ void st_relaxed_f64(double *p, double v) {
     asm volatile("st.relaxed.gpu.global.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_sys_f64(double *p, double v) {
+    asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
+}
 __device__ __forceinline__ int ld_relaxed_s32(const int *p) {
     int v;
     asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -134,6 +137,13 @@ struct CsrSolveParams {
     int32_t *status;
     unsigned long long budget_ns;
     long long *trace;  // optional: per-row SM cycle counter at publication (profiling aid)
+    // block-row partition across GPUs: this launch owns the nodes [task_begin, task_end);
+    // a published value is also stored into the x arrays of the ranks whose bit is set in
+    // need_mask[row] (peer-mapped pointers, indexed by rank)
+    int task_begin;
+    int task_end;
+    const unsigned char *__restrict__ need_mask;
+    double *peers[8];
 };
 
 // Off-diagonal range [lo, hi) and diagonal position d (-1: implicit unit) of a row.

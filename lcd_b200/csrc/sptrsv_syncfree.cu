@@ -137,13 +137,13 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
     __syncthreads();
     volatile double *sxv = sx;
     volatile int *wdone = s_wdone;
-    const int row0 = s_chunk * TPB;
+    const int row0 = p.task_begin + s_chunk * TPB;
     const int task = row0 + tid;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     // The rows of a chunk are contiguous in the matrix, so their entries form one
     // segment of Ai / Ax: stage it with coalesced loads before anybody waits, so
     // that no matrix fetch sits on a dependence chain.
-    const int task_end = min(row0 + TPB, p.n);
+    const int task_end = min(row0 + TPB, p.task_end);
     const int first_row = upper ? p.n - task_end : row0;
     const int last_row = upper ? p.n - 1 - row0 : task_end - 1;
     long long seg_begin = 0;
@@ -161,7 +161,7 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
         sval[k] = __ldg(p.Ax + seg_begin + k);
     }
     __syncthreads();
-    if (task >= p.n) return;
+    if (task >= p.task_end) return;
     const bool exact = p.flags & LCD_SOLVE_EXACT;
     const int r = upper ? p.n - 1 - task : task;
     int lo = 0, hi = 0, d = -1;
@@ -241,6 +241,14 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
             val = publishable(val);
             sxv[tid] = val;
             st_relaxed_f64(p.x + r, val);
+            if (p.need_mask) {  // rows of other GPUs wait for this value in their own memory
+                unsigned m = p.need_mask[r];
+                while (m) {
+                    const int q = __ffs(m) - 1;
+                    m &= m - 1;
+                    st_relaxed_sys_f64(p.peers[q] + r, val);
+                }
+            }
             if (tune.gap_ns) atomicAdd(&s_wdone[tid >> 5], 1);
             if (p.trace) p.trace[task] = clock64();
             break;
@@ -452,18 +460,20 @@ csr_syncfree_chain_kernel(const CsrSolveParams p, const RowTuning tune, const in
 #undef LCD_ENTRY
 }
 
-// Multi-RHS: the block of right-hand sides is row-major, a thread owns one
-// (row, rhs) pair, consecutive lanes own consecutive right-hand sides of a row.
-// Each lane polls exactly the operand elements it consumes, so lanes never have
-// to agree on anything.  W = lanes per row (power of two), KR = columns per lane.
+// Multi-RHS: the block of right-hand sides is row-major, W consecutive lanes own a
+// row, lane l owns the right-hand sides l, l + W, ... (KR of them at most).  A lane
+// polls exactly the operand elements it consumes (written by the same lane position of
+// the producer row), so lanes never have to agree on anything.  Few lanes per row keep
+// many rows in flight, which is what grid-like matrices need.
 template <int W, int KR, int TPB>
 __global__ void __launch_bounds__(TPB) csr_syncfree_multi_kernel(const CsrSolveParams p) {
     constexpr int R = TPB / W;
-    extern __shared__ double smem_multi[];  // R x (W*KR)
+    constexpr int NC = W * KR;  // columns of the shared-memory mirror
+    extern __shared__ double smem_multi[];  // R x NC
     __shared__ int s_chunk;
     const int tid = threadIdx.x;
     if (tid == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
-    for (int k = tid; k < R * W * KR; k += TPB)
+    for (int k = tid; k < R * NC; k += TPB)
         reinterpret_cast<unsigned long long *>(smem_multi)[k] = kPendingBits;
     __syncthreads();
     volatile double *sxv = smem_multi;
@@ -484,13 +494,15 @@ __global__ void __launch_bounds__(TPB) csr_syncfree_multi_kernel(const CsrSolveP
         lo = hi = 0;
         d = -1;
     }
-    // number of right-hand sides this lane owns: lane, lane+W, ...
+    // number of right-hand sides this lane owns: lane, lane + W, ...
     const int nlive = lane < p.nrhs ? min(KR, (p.nrhs - lane + W - 1) / W) : 0;
     if (nlive == 0) return;
-    double acc0 = __ldg(p.b + (long long)r * p.ld + lane);
-    double acc1 = (KR > 1 && nlive > 1) ? __ldg(p.b + (long long)r * p.ld + lane + W) : 0.0;
+    double acc[KR];
+#pragma unroll
+    for (int k = 0; k < KR; ++k)
+        acc[k] = k < nlive ? __ldg(p.b + (long long)r * p.ld + lane + k * W) : 0.0;
     const double rinv = d >= 0 ? 1.0 / __ldg(p.Ax + d) : 1.0;
-    int j = lo, kk = 0;
+    int j = lo;
     bool have = j < hi;
     int c = 0;
     double a = 0.0;
@@ -505,18 +517,27 @@ __global__ void __launch_bounds__(TPB) csr_syncfree_multi_kernel(const CsrSolveP
                 failed = true;
                 have = false;
             } else {
-                const int q = lane + kk * W;
-                const double xv = (tc >= row0) ? sxv[(tc - row0) * (W * KR) + q]
-                                               : ld_relaxed_f64(p.x + (long long)c * p.ld + q);
-                if (!is_pending(xv)) {
-                    if (KR == 1 || kk == 0) acc0 = fma(-a, xv, acc0);
-                    else acc1 = fma(-a, xv, acc1);
-                    if (++kk == nlive) {
-                        kk = 0;
-                        ++j;
-                        have = j < hi;
-                        if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
-                    }
+                // all operands of this lane for entry j; they are published together
+                double xv[KR];
+                bool ready = true;
+                if (tc >= row0) {
+                    const int base = (tc - row0) * NC + lane;
+#pragma unroll
+                    for (int k = 0; k < KR; ++k)
+                        if (k < nlive) { xv[k] = sxv[base + k * W]; ready = ready && !is_pending(xv[k]); }
+                } else {
+                    const double *src = p.x + (long long)c * p.ld + lane;
+#pragma unroll
+                    for (int k = 0; k < KR; ++k)
+                        if (k < nlive) { xv[k] = ld_relaxed_f64(src + k * W); ready = ready && !is_pending(xv[k]); }
+                }
+                if (ready) {
+#pragma unroll
+                    for (int k = 0; k < KR; ++k)
+                        if (k < nlive) acc[k] = fma(-a, xv[k], acc[k]);
+                    ++j;
+                    have = j < hi;
+                    if (have) { c = __ldg(p.Ai + j); a = __ldg(p.Ax + j); }
                 } else if (dl.tick(p.status, r)) {
                     failed = true;
                     have = false;
@@ -524,13 +545,13 @@ __global__ void __launch_bounds__(TPB) csr_syncfree_multi_kernel(const CsrSolveP
             }
         } else {
             const double nanv = __longlong_as_double(kCanonicalNaN);
-            double v0 = publishable(failed ? nanv : acc0 * rinv);
-            st_relaxed_f64(p.x + (long long)r * p.ld + lane, v0);
-            sxv[local * (W * KR) + lane] = v0;
-            if (KR > 1 && nlive > 1) {
-                double v1 = publishable(failed ? nanv : acc1 * rinv);
-                st_relaxed_f64(p.x + (long long)r * p.ld + lane + W, v1);
-                sxv[local * (W * KR) + lane + W] = v1;
+#pragma unroll
+            for (int k = 0; k < KR; ++k) {
+                if (k < nlive) {
+                    const double v = publishable(failed ? nanv : acc[k] * rinv);
+                    sxv[local * NC + lane + k * W] = v;
+                    st_relaxed_f64(p.x + (long long)r * p.ld + lane + k * W, v);
+                }
             }
             break;
         }
@@ -688,7 +709,8 @@ static cudaError_t launch_csr_row_t(const CsrSolveParams &p, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured = 227 * 1024;
     }
-    csr_syncfree_row_kernel<TPB, MINB><<<(p.n + TPB - 1) / TPB, TPB, smem, st>>>(p, g_row_tuning, cap);
+    csr_syncfree_row_kernel<TPB, MINB><<<(p.task_end - p.task_begin + TPB - 1) / TPB, TPB, smem, st>>>(
+        p, g_row_tuning, cap);
     return cudaGetLastError();
 }
 
@@ -752,6 +774,16 @@ template <int W, int KR>
 static cudaError_t launch_multi(const CsrSolveParams &p, cudaStream_t st) {
     constexpr int TPB = 512, R = TPB / W;
     const size_t smem = (size_t)R * W * KR * sizeof(double);
+    if (smem > 48 * 1024) {
+        static bool configured = false;
+        if (!configured) {
+            cudaError_t e = cudaFuncSetAttribute(csr_syncfree_multi_kernel<W, KR, TPB>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+            configured = true;
+        }
+    }
     csr_syncfree_multi_kernel<W, KR, TPB><<<(p.n + R - 1) / R, TPB, smem, st>>>(p);
     return cudaGetLastError();
 }
@@ -834,7 +866,7 @@ extern "C" int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap
     if (n > 0) {
         LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
         CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
-                         timeout_ns(timeout_ms), g_trace};
+                         timeout_ns(timeout_ms), g_trace, 0, n, nullptr, {nullptr}};
         cudaError_t e;
         switch (G) {
             case 1:
@@ -875,15 +907,16 @@ extern "C" int lcd_sptrsv_csr_syncfree_multi(int32_t n, int64_t nnz, int32_t nrh
         // X may be strided (ld > nrhs): fill the whole block, padding included.
         LCD_CUDA_TRY(cudaMemsetAsync(X, 0xFF, (size_t)n * (size_t)ld * sizeof(double), st));
         CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, B, X, flags, nrhs, ld, status_dev,
-                         timeout_ns(timeout_ms), nullptr};
+                         timeout_ns(timeout_ms), nullptr, 0, n, nullptr, {nullptr}};
         cudaError_t e;
+        // few lanes per row keep many rows in flight; a lane owns up to 8 right-hand sides
         if (nrhs <= 1) e = launch_multi<1, 1>(p, st);
         else if (nrhs <= 2) e = launch_multi<2, 1>(p, st);
         else if (nrhs <= 4) e = launch_multi<4, 1>(p, st);
-        else if (nrhs <= 8) e = launch_multi<8, 1>(p, st);
-        else if (nrhs <= 16) e = launch_multi<16, 1>(p, st);
-        else if (nrhs <= 32) e = launch_multi<32, 1>(p, st);
-        else e = launch_multi<32, 2>(p, st);
+        else if (nrhs <= 8) e = launch_multi<4, 2>(p, st);
+        else if (nrhs <= 16) e = launch_multi<4, 4>(p, st);
+        else if (nrhs <= 32) e = launch_multi<8, 4>(p, st);
+        else e = launch_multi<8, 8>(p, st);
         LCD_CUDA_TRY(e);
     }
     return finish(status_dev, st, status_host);
@@ -929,6 +962,74 @@ extern "C" int lcd_sptrsv_csc_syncfree(int32_t n, int64_t nnz, const int32_t *Ap
             default: return LCD_ERR_INVALID_ARGUMENT;
         }
         LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}
+
+// ---- block-row partition across GPUs --------------------------------------------
+// need[c] gets bit q set when a row owned by rank q (q != owner of c) stores an
+// off-diagonal entry in column c.  bounds[0..parts] are node (task) boundaries.
+__global__ void partition_need_kernel(int n, const int *__restrict__ Ap, const int *__restrict__ Ai,
+                                      int upper, int of_full_unused, const int *__restrict__ bounds,
+                                      int parts, unsigned *need_words) {
+    const int task = blockIdx.x * blockDim.x + threadIdx.x;
+    if (task >= n) return;
+    const int r = upper ? n - 1 - task : task;
+    int owner = 0;
+    while (owner + 1 < parts && task >= bounds[owner + 1]) ++owner;
+    const int s = Ap[r], e = Ap[r + 1];
+    const int lo = upper ? s + 1 : s, hi = upper ? e : e - 1;
+    for (int j = lo; j < hi; ++j) {
+        const int c = Ai[j];
+        if ((unsigned)c >= (unsigned)n) continue;
+        const int tc = upper ? n - 1 - c : c;
+        if (tc < bounds[owner])  // produced on another GPU
+            atomicOr(need_words + (c >> 2), (1u << owner) << ((c & 3) * 8));
+    }
+}
+
+extern "C" int lcd_partition_need_mask(int32_t n, const int32_t *Ap, const int32_t *Ai, int flags,
+                                       const int32_t *bounds_dev, int32_t parts,
+                                       unsigned char *need_mask, void *stream) {
+    if (n < 0 || parts < 1 || parts > 8 || (n > 0 && (!Ap || !Ai || !bounds_dev || !need_mask)))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n == 0) return LCD_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    // the mask array must be padded to a multiple of 4 bytes (it is updated word-wise)
+    LCD_CUDA_TRY(cudaMemsetAsync(need_mask, 0, ((size_t)n + 3) / 4 * 4, st));
+    partition_need_kernel<<<(n + 255) / 256, 256, 0, st>>>(
+        n, Ap, Ai, (flags & LCD_SOLVE_UPPER) ? 1 : 0, 0, bounds_dev, parts,
+        reinterpret_cast<unsigned *>(need_mask));
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_sptrsv_csr_syncfree_part(int32_t n, int64_t nnz, const int32_t *Ap,
+                                            const int32_t *Ai, const double *Ax, const double *b,
+                                            double *x, int flags, int32_t task_begin,
+                                            int32_t task_end, const unsigned char *need_mask,
+                                            double *const *peer_x, int32_t n_ranks,
+                                            int threads_per_block, int32_t *status_dev,
+                                            int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev || task_begin < 0 || task_end < task_begin || task_end > n ||
+        n_ranks < 1 || n_ranks > 8)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (flags & (LCD_SOLVE_OF_FULL | LCD_SOLVE_UNIT_DIAG | LCD_SOLVE_CHAIN))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !Ai || !Ax || !b || !x || x == b)) return LCD_ERR_INVALID_ARGUMENT;
+    if (need_mask && !peer_x) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int tpb = threads_per_block > 0 ? threads_per_block : 1024;
+    if (tpb != 256 && tpb != 512 && tpb != 1024) return LCD_ERR_INVALID_ARGUMENT;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (task_end > task_begin) {
+        // x is NOT filled here: every rank fills its x with the reserved pattern and all
+        // ranks synchronise on the host before the first rank is allowed to publish
+        CsrSolveParams p{n, nnz, Ap, Ai, Ax, nullptr, b, x, flags, 1, 1, status_dev,
+                         timeout_ns(timeout_ms), nullptr, task_begin, task_end, need_mask, {nullptr}};
+        for (int q = 0; q < n_ranks && peer_x; ++q) p.peers[q] = peer_x[q];
+        LCD_CUDA_TRY(launch_csr_row(p, tpb, st));
     }
     return finish(status_dev, st, status_host);
 }

@@ -167,6 +167,108 @@ __global__ void __launch_bounds__(kCoopThreads) wavefront_coop_kernel(const Wave
     }
 }
 
+// ---- multi-RHS, level-synchronous ---------------------------------------------
+// Row-major blocks of right-hand sides: a warp owns a row, lane l owns the columns
+// l, l + 32, ...  Every gather of x is a coalesced row segment and there is nothing to
+// wait for inside a level, so wide levels stream at memory speed.
+template <int KR>
+__device__ __forceinline__ void solve_node_multi(const WavefrontParams &w, int node) {
+    const CsrSolveParams &p = w.m;
+    const int lane = threadIdx.x & 31;
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const int r = upper ? p.n - 1 - node : node;
+    int lo = 0, hi = 0, d = -1;
+    if (!csr_row_range(p, r, lo, hi, d)) {
+        if (lane == 0)
+            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                               : LCD_ERR_BAD_POINTERS, r);
+        return;
+    }
+    double acc[KR];
+#pragma unroll
+    for (int k = 0; k < KR; ++k) {
+        const int q = lane + 32 * k;
+        acc[k] = q < p.nrhs ? __ldg(p.b + (long long)r * p.ld + q) : 0.0;
+    }
+    for (int j = lo; j < hi; ++j) {
+        const int c = __ldg(p.Ai + j);
+        if ((unsigned)c >= (unsigned)p.n) {
+            if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+            continue;
+        }
+        const double a = __ldg(p.Ax + j);
+        const double *src = p.x + (long long)c * p.ld;
+#pragma unroll
+        for (int k = 0; k < KR; ++k) {
+            const int q = lane + 32 * k;
+            if (q < p.nrhs) acc[k] = fma(-a, __ldcg(src + q), acc[k]);
+        }
+    }
+    const double rinv = d >= 0 ? 1.0 / __ldg(p.Ax + d) : 1.0;
+#pragma unroll
+    for (int k = 0; k < KR; ++k) {
+        const int q = lane + 32 * k;
+        if (q < p.nrhs) __stcg(p.x + (long long)r * p.ld + q, acc[k] * rinv);
+    }
+}
+
+template <int KR>
+__global__ void __launch_bounds__(kCoopThreads) wavefront_multi_coop_kernel(const WavefrontParams w) {
+    __shared__ int s_ok;
+    constexpr int rows_per_block = kCoopThreads / 32;
+    const int warp = threadIdx.x >> 5;
+    unsigned long long target = 0;
+    int l = 0;
+    while (l < w.n_levels) {
+        const int ws = __ldg(w.wavefront_ptr + l), we = __ldg(w.wavefront_ptr + l + 1);
+        if (we - ws <= rows_per_block) {
+            int end = l + 1;
+            while (end < w.n_levels &&
+                   __ldg(w.wavefront_ptr + end + 1) - __ldg(w.wavefront_ptr + end) <= rows_per_block)
+                ++end;
+            if (blockIdx.x == 0) {
+                for (int k = l; k < end; ++k) {
+                    const int t = __ldg(w.wavefront_ptr + k) + warp;
+                    if (t < __ldg(w.wavefront_ptr + k + 1)) {
+                        const int node = __ldg(w.wavefronts + t);
+                        if ((unsigned)node < (unsigned)w.m.n) solve_node_multi<KR>(w, node);
+                    }
+                    __syncthreads();
+                }
+            }
+            l = end;
+        } else {
+            const int total_rows = gridDim.x * rows_per_block;
+            for (int t = ws + blockIdx.x * rows_per_block + warp; t < we; t += total_rows) {
+                const int node = __ldg(w.wavefronts + t);
+                if ((unsigned)node < (unsigned)w.m.n) solve_node_multi<KR>(w, node);
+            }
+            ++l;
+        }
+        if (l < w.n_levels && gridDim.x > 1) {
+            if (!grid_barrier(w, target, &s_ok)) return;
+        } else {
+            __syncthreads();
+        }
+    }
+}
+
+template <int KR>
+static int launch_multi_coop(WavefrontParams &w, cudaStream_t st) {
+    int per_sm = 0;
+    LCD_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, wavefront_multi_coop_kernel<KR>,
+                                                              kCoopThreads, 0));
+    if (per_sm < 1) return LCD_ERR_CUDA;
+    long long grid = (long long)per_sm * sm_count();
+    const long long useful = ((long long)w.m.n + 15) / 16;
+    if (grid > useful) grid = useful;
+    if (grid < 1) grid = 1;
+    void *args[] = {(void *)&w};
+    LCD_CUDA_TRY(cudaLaunchCooperativeKernel((void *)wavefront_multi_coop_kernel<KR>,
+                                             dim3((unsigned)grid), dim3(kCoopThreads), args, 0, st));
+    return LCD_OK;
+}
+
 }  // namespace lcd
 
 using namespace lcd;
@@ -199,7 +301,7 @@ extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_
         if (csc) LCD_CUDA_TRY(cudaMemsetAsync(x, 0, (size_t)n * sizeof(double), st));
         WavefrontParams w;
         w.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
-                             timeout_ns(timeout_ms), nullptr};
+                             timeout_ns(timeout_ms), nullptr, 0, n, nullptr, {nullptr}};
         w.csc = csc ? 1 : 0;
         w.wavefronts = wavefronts;
         w.wavefront_ptr = wavefront_ptr_dev;
@@ -229,6 +331,37 @@ extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_
         } else {
             return LCD_ERR_INVALID_ARGUMENT;
         }
+    }
+    return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_sptrsv_wavefront_multi(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap,
+                                          const int32_t *Ai, const double *Ax,
+                                          const int32_t *diag_pos, const double *B, double *X,
+                                          int64_t ld, int flags, const int32_t *wavefronts,
+                                          const int32_t *wavefront_ptr_dev, int32_t n_levels,
+                                          int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                          int *status_host) {
+    if (n < 0 || nnz < 0 || nrhs < 1 || nrhs > 64 || ld < nrhs || n_levels < 0 || !status_dev)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_OF_FULL) && !diag_pos) return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_UNIT_DIAG) && !(flags & LCD_SOLVE_OF_FULL)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !B || !X || X == B || !wavefronts || !wavefront_ptr_dev))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0 && n_levels > 0) {
+        WavefrontParams w;
+        w.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, B, X, flags, nrhs, ld, status_dev,
+                             timeout_ns(timeout_ms), nullptr, 0, n, nullptr, {nullptr}};
+        w.csc = 0;
+        w.wavefronts = wavefronts;
+        w.wavefront_ptr = wavefront_ptr_dev;
+        w.n_levels = n_levels;
+        w.lanes = 32;
+        rc = nrhs <= 32 ? launch_multi_coop<1>(w, st) : launch_multi_coop<2>(w, st);
+        if (rc) return rc;
     }
     return finish(status_dev, st, status_host);
 }

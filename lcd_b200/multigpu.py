@@ -31,19 +31,45 @@ def column_shard(nrhs, world, rank):
     return start, start + base + (1 if rank < extra else 0)
 
 
+# Levels at least this wide (on average) are solved level by level: every gather is a
+# coalesced row of the right-hand-side block and nothing waits inside a level.  Narrower
+# level structures are dependence chains and go to the sync-free kernel.
+WAVEFRONT_MIN_AVERAGE_WIDTH = 256
+_level_sets = {}
+
+
+def _levels_for(matrix, upper):
+    """Level sets of a device matrix, built once per matrix object."""
+    from . import ops
+    Ap, Ai, _ = matrix
+    key = (Ap.data_ptr(), Ai.data_ptr(), Ap.numel(), Ai.numel(), bool(upper))
+    dag = _level_sets.get(key)
+    if dag is None:
+        if len(_level_sets) >= 8:
+            _level_sets.pop(next(iter(_level_sets)))
+        dag = _level_sets[key] = ops.dag_build("csr_upper" if upper else "csr_lower", Ap, Ai)
+    return dag
+
+
 def _native_local_solve(matrix, block, upper=False):
     """Solve for a column-major shard (k columns of length n, device tensor of shape
-    (k, n)) with the multi-RHS kernel; returns the same layout."""
+    (k, n)) with a multi-RHS kernel chosen from the level width; same layout out."""
     import torch
     from . import ops
     Ap, Ai, Ax = matrix
     k, n = block.shape
     out = torch.empty_like(block)
+    dag = _levels_for(matrix, upper)
+    wide = dag.n_levels > 0 and n / dag.n_levels >= WAVEFRONT_MIN_AVERAGE_WIDTH
     for first in range(0, k, MAX_RHS_PER_LAUNCH):
         last = min(first + MAX_RHS_PER_LAUNCH, k)
         cols = last - first
-        rows_major = ops.transpose(block[first:last].contiguous(), cols, n)      # n x cols
-        solved = ops.sptrsv_csr_syncfree_multi(Ap, Ai, Ax, rows_major.view(n, cols), upper=upper)
+        rows_major = ops.transpose(block[first:last].contiguous(), cols, n).view(n, cols)
+        if wide:
+            solved = ops.sptrsv_wavefront_multi(Ap, Ai, Ax, rows_major, dag.wavefronts,
+                                                dag.wavefront_ptr, upper=upper)
+        else:
+            solved = ops.sptrsv_csr_syncfree_multi(Ap, Ai, Ax, rows_major, upper=upper)
         ops.transpose(solved, n, cols, out=out[first:last])
     return out
 
@@ -106,3 +132,137 @@ class ShardedMultiRHS:
         parts = [torch.empty_like(padded) for _ in range(self.world)]
         self.dist.all_gather(parts, padded, group=self.group)
         return torch.cat([part[:e - s] for part, (s, e) in zip(parts, sizes)], dim=0)
+
+
+def row_partition(n, world):
+    """Node boundaries of a balanced contiguous block-row partition (world + 1 ints)."""
+    return np.asarray([(n * q) // world for q in range(world + 1)], dtype=np.int32)
+
+
+class _PeerBuffer:
+    """A device array other processes of the node can map (CUDA IPC)."""
+
+    def __init__(self, nbytes):
+        import ctypes
+        from . import _native as nat
+        self.nbytes = int(nbytes)
+        self._lib = nat.load()
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        nat.check(self._lib.lcd_peer_alloc(self.nbytes, ctypes.byref(ptr), handle), "lcd_peer_alloc")
+        self.ptr = ptr.value
+        self.handle = handle.raw
+        self.mapped = []
+
+    def open_peer(self, handle):
+        import ctypes
+        from . import _native as nat
+        ptr = ctypes.c_void_p()
+        nat.check(self._lib.lcd_peer_open(handle, ctypes.byref(ptr)), "lcd_peer_open")
+        self.mapped.append(ptr.value)
+        return ptr.value
+
+    @property
+    def __cuda_array_interface__(self):
+        return {"shape": (self.nbytes // 8,), "typestr": "<f8", "data": (self.ptr, False),
+                "version": 3, "strides": None}
+
+    def release(self):
+        import ctypes
+        for ptr in self.mapped:
+            self._lib.lcd_peer_close(ctypes.c_void_p(ptr))
+        self.mapped = []
+        if self.ptr:
+            self._lib.lcd_peer_free(ctypes.c_void_p(self.ptr))
+            self.ptr = None
+
+
+class PartitionedSolve:
+    """One triangular solve (CSR, lower or upper) split into contiguous block rows,
+    one per GPU.  Cross-partition operands travel as plain 8-byte peer stores into the
+    consumer's own x array; there is no collective on the data path (the optional
+    final gather uses NCCL)."""
+
+    def __init__(self, Ap, Ai, Ax, upper=False, group=None, threads=0):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _native as nat
+        from .ops import _stream, new_status
+        if not dist.is_initialized():
+            raise RuntimeError("PartitionedSolve needs an initialised process group")
+        self.dist, self.group = dist, group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (one node)")
+        self.upper, self.threads = upper, threads
+        dev = torch.device("cuda", torch.cuda.current_device())
+        up = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dtype=dt)).to(dev)
+        self.Ap, self.Ai, self.Ax = up(Ap, np.int32), up(Ai, np.int32), up(Ax, np.float64)
+        self.n = len(Ap) - 1
+        self.bounds = row_partition(self.n, self.world)
+        self.status = new_status(dev)
+        self.device = dev
+        lib = nat.load()
+        self._lib = lib
+        # which ranks need each value
+        self.need = torch.zeros((self.n + 3) // 4 * 4, dtype=torch.uint8, device=dev)
+        bounds_dev = up(self.bounds, np.int32)
+        nat.check(lib.lcd_partition_need_mask(self.n, nat.ptr(self.Ap), nat.ptr(self.Ai),
+                                              nat.SOLVE_UPPER if upper else 0, nat.ptr(bounds_dev),
+                                              self.world, nat.ptr(self.need), _stream()),
+                  "lcd_partition_need_mask")
+        # peer-visible x arrays
+        self.buffer = _PeerBuffer(max(self.n, 1) * 8)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.buffer.handle, group=group)
+        self.peer_ptrs = (ctypes.c_void_p * self.world)()
+        for q, handle in enumerate(handles):
+            self.peer_ptrs[q] = self.buffer.ptr if q == self.rank else self.buffer.open_peer(handle)
+        self.x = torch.as_tensor(self.buffer, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    def solve(self, b, gather=True, timeout_ms=0):
+        """``b``: full right-hand side (host array or device tensor, same on every
+        rank).  Returns x: the full vector on every rank (``gather=True``) or this
+        rank's block."""
+        import ctypes
+        import torch
+        from . import _native as nat, ops
+        from .ops import _stream
+        b_dev = b if isinstance(b, torch.Tensor) else torch.from_numpy(
+            np.ascontiguousarray(b, dtype=np.float64)).to(self.device)
+        ops.fill_u64(self.x, 0xFFFFFFFFFFFFFFFF)
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)       # nobody publishes into an unfilled array
+        host = ctypes.c_int(0)
+        t0, t1 = int(self.bounds[self.rank]), int(self.bounds[self.rank + 1])
+        rc = self._lib.lcd_sptrsv_csr_syncfree_part(
+            self.n, self.Ai.numel(), nat.ptr(self.Ap), nat.ptr(self.Ai), nat.ptr(self.Ax),
+            nat.ptr(b_dev), nat.ptr(self.x), nat.SOLVE_UPPER if self.upper else 0, t0, t1,
+            nat.ptr(self.need) if self.world > 1 else None, self.peer_ptrs, self.world,
+            int(self.threads), nat.ptr(self.status), int(timeout_ms), _stream(),
+            ctypes.byref(host))
+        nat.check(rc, "lcd_sptrsv_csr_syncfree_part")
+        lo, hi = (self.n - t1, self.n - t0) if self.upper else (t0, t1)
+        mine = self.x[lo:hi].clone()
+        self.dist.barrier(group=self.group)       # peers may still be reading / writing x
+        if not gather or self.world == 1:
+            return mine
+        widest = int(np.max(np.diff(self.bounds)))
+        padded = torch.zeros(widest, dtype=torch.float64, device=self.device)
+        padded[:mine.numel()] = mine
+        parts = [torch.empty_like(padded) for _ in range(self.world)]
+        self.dist.all_gather(parts, padded, group=self.group)
+        blocks = [parts[q][:int(self.bounds[q + 1] - self.bounds[q])] for q in range(self.world)]
+        if self.upper:
+            blocks = blocks[::-1]
+        return torch.cat(blocks)
+
+    def close(self):
+        import torch
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        self.x = None
+        self.buffer.release()

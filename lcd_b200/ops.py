@@ -170,6 +170,28 @@ def sptrsv_csr_syncfree_multi(Ap, Ai, Ax, B, X=None, *, upper=False, unit_diag=F
     return X
 
 
+def sptrsv_wavefront_multi(Ap, Ai, Ax, B, wavefronts, wavefront_ptr, X=None, *, upper=False,
+                           unit_diag=False, diag_pos=None, status=None, timeout_ms=0, sync=True):
+    """Level-synchronous multi-RHS solve on a row-major n x nrhs block (nrhs <= 64).
+    ``wavefronts`` / ``wavefront_ptr`` come from ``dag_build`` of the matching operator
+    (``csr_lower`` or ``csr_upper``)."""
+    _require(B, torch.float64, "B")
+    n = Ap.numel() - 1
+    if B.dim() != 2 or B.shape[0] != n:
+        raise ValueError("B must be a row-major n x nrhs tensor")
+    nrhs = B.shape[1]
+    X = torch.empty_like(B) if X is None else X
+    status = new_status(B.device) if status is None else status
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_wavefront_multi(
+        n, Ai.numel(), nrhs, ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(B), ptr(X), nrhs, flags,
+        ptr(wavefronts), ptr(wavefront_ptr), wavefront_ptr.numel() - 1, ptr(status),
+        int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_wavefront_multi")
+    return X
+
+
 def transpose(src, rows, cols, out=None):
     """out[c, r] = src[r, c] for a row-major rows x cols block."""
     out = torch.empty(cols, rows, dtype=torch.float64, device=src.device) if out is None else out

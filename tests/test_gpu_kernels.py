@@ -285,6 +285,27 @@ def test_csr_syncfree_multi_rhs(cuda, oracle, nrhs):
         assert csr_residual(Ap, Ai, Ax, X[:, q], B[:, q]) <= RESIDUAL_TOL
 
 
+@pytest.mark.parametrize("nrhs", [1, 5, 32, 33, 64])
+def test_wavefront_multi_rhs(cuda, oracle, nrhs):
+    from lcd_b200 import generators as gen, ops
+    for tri, upper in ((gen.laplacian3d_tril(18, seed=1, nrhs=nrhs), False),
+                       (gen.random_band_lower(4000, seed=2, mean_degree=9.0, band=40), True)):
+        if upper:
+            tri = gen.upper_from_lower(tri)
+            B = np.random.default_rng(nrhs).uniform(-1, 1, (tri.n, nrhs))
+        else:
+            B = np.ascontiguousarray(tri.b)
+        Ap, Ai, Ax = tri.csr_arrays()
+        dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+        dag = ops.dag_build("csr_upper" if upper else "csr_lower", dAp, dAi)
+        X = host(ops.sptrsv_wavefront_multi(dAp, dAi, dev(Ax, np.float64, cuda), dev(B, np.float64, cuda),
+                                            dag.wavefronts, dag.wavefront_ptr, upper=upper))
+        solve = oracle.sptrsv_csr_upper if upper else oracle.sptrsv_csr_lower
+        for q in range(0, nrhs, max(1, nrhs // 4)):
+            np.testing.assert_allclose(X[:, q], solve(Ap, Ai, Ax, np.ascontiguousarray(B[:, q])),
+                                       rtol=1e-10, atol=1e-12)
+
+
 def test_sharded_multi_rhs_single_rank(cuda, oracle):
     """The multi-GPU front end with one rank: 70 columns go through two launches."""
     from lcd_b200 import generators as gen
