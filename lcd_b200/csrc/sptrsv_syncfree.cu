@@ -119,11 +119,11 @@ static long long *g_trace = nullptr;
 // per-warp completion count tells a waiting thread how far the producer's warp is
 // from the row it needs; distant waiters pause instead of burning issue slots that
 // the threads on the critical chain need.
-template <int TPB, int MINB>
+template <int TPB, int MINB, bool EXACT>
 __global__ void __launch_bounds__(TPB, MINB)
 csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int cap) {
     constexpr int kWarps = TPB / 32;
-    // dynamic shared memory: x mirror of the chunk | staged values | staged indices
+    // dynamic shared memory: x mirror of the chunk | staged values | staged operands
     extern __shared__ __align__(16) unsigned char row_smem[];
     double *sx = reinterpret_cast<double *>(row_smem);
     double *sval = sx + TPB;
@@ -142,7 +142,9 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     // The rows of a chunk are contiguous in the matrix, so their entries form one
     // segment of Ai / Ax: stage it with coalesced loads before anybody waits, so
-    // that no matrix fetch sits on a dependence chain.
+    // that no matrix fetch sits on a dependence chain.  Staged operands are stored
+    // as node ids relative to the chunk (>= 0: a row of this chunk, mirrored in
+    // shared memory; < 0: a row of an earlier chunk, polled in global memory).
     const int task_end = min(row0 + TPB, p.task_end);
     const int first_row = upper ? p.n - task_end : row0;
     const int last_row = upper ? p.n - 1 - row0 : task_end - 1;
@@ -157,77 +159,84 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
             seg_begin = 0;
     }
     for (int k = tid; k < count; k += TPB) {
-        sidx[k] = __ldg(p.Ai + seg_begin + k);
+        const int c = __ldg(p.Ai + seg_begin + k);
+        // out-of-range columns become "far in the future": caught by the per-row check
+        const bool in_range = (unsigned)c < (unsigned)p.n;
+        sidx[k] = in_range ? (upper ? p.n - 1 - c : c) - row0 : TPB;
         sval[k] = __ldg(p.Ax + seg_begin + k);
     }
     __syncthreads();
     if (task >= p.task_end) return;
-    const bool exact = p.flags & LCD_SOLVE_EXACT;
     const int r = upper ? p.n - 1 - task : task;
     int lo = 0, hi = 0, d = -1;
-    bool failed = false;
     if (!csr_row_range(p, r, lo, hi, d)) {
         raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
                                                            : LCD_ERR_BAD_POINTERS, r);
-        failed = true;
-        lo = hi = 0;
-        d = -1;
+        const double nanv = __longlong_as_double(kCanonicalNaN);
+        sxv[tid] = nanv;
+        st_relaxed_f64(p.x + r, nanv);
+        return;
     }
     const int sbase = (int)seg_begin;  // seg_begin <= nnz < 2^31
     double acc = __ldg(p.b + r);
     double dv = 1.0, rinv = 1.0;
     if (d >= 0) dv = ((unsigned)(d - sbase) < (unsigned)count) ? sval[d - sbase] : __ldg(p.Ax + d);
-    if (!exact) rinv = 1.0 / dv;
-    int j = lo;
-    int cl = 0, c = 0;  // cl: operand's position relative to the chunk (>= 0: mirrored)
-    double a = 0.0;
-    bool have = j < hi;
-#define LCD_FETCH_OPERAND()                                                  \
-    do {                                                                     \
-        const unsigned pos_ = (unsigned)(j - sbase);                         \
-        if (pos_ < (unsigned)count) {                                        \
-            c = sidx[pos_];                                                  \
-            a = sval[pos_];                                                  \
-        } else {                                                             \
-            c = __ldg(p.Ai + j);                                             \
-            a = __ldg(p.Ax + j);                                             \
-        }                                                                    \
-        const int tc_ = upper ? p.n - 1 - c : c;                             \
-        if ((unsigned)tc_ >= (unsigned)task) {                               \
-            raise_error(p.status, LCD_ERR_INDEX_RANGE, r);                   \
-            failed = true;                                                   \
-            have = false;                                                    \
-        }                                                                    \
-        cl = tc_ - row0;                                                     \
+    if (!EXACT) rinv = 1.0 / dv;  // off the critical path: computed before any wait
+    // operand j: cl = node id relative to the chunk, a = matrix value
+#define LCD_FETCH(j_, cl_, a_)                                                   \
+    do {                                                                         \
+        const unsigned pos_ = (unsigned)((j_) - sbase);                          \
+        if (pos_ < (unsigned)count) {                                            \
+            cl_ = sidx[pos_];                                                    \
+            a_ = sval[pos_];                                                     \
+        } else {                                                                 \
+            const int c_ = __ldg(p.Ai + (j_));                                   \
+            a_ = __ldg(p.Ax + (j_));                                             \
+            cl_ = ((unsigned)c_ < (unsigned)p.n) ? (upper ? p.n - 1 - c_ : c_) - row0 : TPB; \
+        }                                                                        \
     } while (0)
-    if (have) LCD_FETCH_OPERAND();
-    // fast-forward over operands outside the chunk that are already there
-    while (have && cl < 0) {
-        const double xv = ld_relaxed_f64(p.x + c);
-        if (is_pending(xv)) break;
-        acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
-        ++j;
-        have = j < hi;
-        if (have) LCD_FETCH_OPERAND();
+#define LCD_GLOBAL_X(cl_) (p.x + (upper ? p.n - 1 - ((cl_) + row0) : (cl_) + row0))
+#define LCD_ACCUMULATE(a_, xv_) \
+    acc = EXACT ? __dsub_rn(acc, __dmul_rn((a_), (xv_))) : fma(-(a_), (xv_), acc)
+    int j = lo;
+    int cl = 0, cl_next = 0;
+    double a = 0.0, a_next = 0.0;
+    bool failed = false;
+    if (j < hi) {
+        LCD_FETCH(j, cl, a);
+        // fast-forward over operands of earlier chunks that are already there
+        while (cl < 0) {
+            const double xv = ld_relaxed_f64(LCD_GLOBAL_X(cl));
+            if (is_pending(xv)) break;
+            LCD_ACCUMULATE(a, xv);
+            if (++j == hi) break;
+            LCD_FETCH(j, cl, a);
+        }
     }
+    if (j + 1 < hi) LCD_FETCH(j + 1, cl_next, a_next);
     Deadline dl;
     dl.start(p.budget_ns);
+    // One loop, publication inside it: a lane that is done never has to reconverge
+    // with lanes of its warp that still wait (they may be waiting for this very row).
     for (;;) {
-        if (have) {
-            const double xv = cl >= 0 ? sxv[cl] : ld_relaxed_f64(p.x + c);
-            if (!is_pending(xv)) {
-                acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
-                ++j;
-                have = j < hi;
-                if (have) LCD_FETCH_OPERAND();
+        if (j < hi && !failed) {
+            if (cl >= tid) {  // not strictly before this row (or out of range)
+                raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                failed = true;
             } else {
-                if (dl.tick(p.status, r)) {
+                const double xv = cl >= 0 ? sxv[cl] : ld_relaxed_f64(LCD_GLOBAL_X(cl));
+                if (!is_pending(xv)) {
+                    LCD_ACCUMULATE(a, xv);
+                    ++j;
+                    cl = cl_next;
+                    a = a_next;
+                    if (j + 1 < hi) LCD_FETCH(j + 1, cl_next, a_next);
+                } else if (dl.tick(p.status, r)) {
                     failed = true;
-                    have = false;
                 } else if (cl >= 0) {
                     int pause = tune.sleep_local_ns;
                     if (tune.gap_ns) {
-                        const int gap = (cl & 31) - wdone[cl >> 5];  // rows the owner warp still owes
+                        const int gap = (cl & 31) - wdone[cl >> 5];  // rows the owner warp owes
                         if (gap > 1) pause += (gap - 1) * tune.gap_ns;
                     }
                     if (pause > 0) __nanosleep(pause);
@@ -235,8 +244,9 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
                     __nanosleep(tune.sleep_global_ns);
                 }
             }
-        } else {
-            double val = (d < 0) ? acc : (exact ? acc / dv : acc * rinv);
+        }
+        if (j >= hi || failed) {
+            double val = (d < 0) ? acc : (EXACT ? acc / dv : acc * rinv);
             if (failed) val = __longlong_as_double(kCanonicalNaN);
             val = publishable(val);
             sxv[tid] = val;
@@ -254,7 +264,9 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
             break;
         }
     }
-#undef LCD_FETCH_OPERAND
+#undef LCD_FETCH
+#undef LCD_GLOBAL_X
+#undef LCD_ACCUMULATE
 }
 
 // ---- chain kernel: for matrices whose levels are narrow ------------------------
@@ -697,20 +709,20 @@ static size_t row_kernel_smem(int tpb, long long nnz, int n, int *cap_out) {
     return (size_t)tpb * 8 + (size_t)cap * 12;
 }
 
-template <int TPB, int MINB>
+template <int TPB, int MINB, bool EXACT>
 static cudaError_t launch_csr_row_t(const CsrSolveParams &p, cudaStream_t st) {
     int cap = 0;
     const size_t smem = row_kernel_smem(TPB, p.nnz, p.n, &cap);
-    static size_t configured = 0;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(csr_syncfree_row_kernel<TPB, MINB>,
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(csr_syncfree_row_kernel<TPB, MINB, EXACT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)(227 * 1024 - 256));
         if (e != cudaSuccess) return e;
-        configured = 227 * 1024;
+        configured = true;
     }
-    csr_syncfree_row_kernel<TPB, MINB><<<(p.task_end - p.task_begin + TPB - 1) / TPB, TPB, smem, st>>>(
-        p, g_row_tuning, cap);
+    csr_syncfree_row_kernel<TPB, MINB, EXACT>
+        <<<(p.task_end - p.task_begin + TPB - 1) / TPB, TPB, smem, st>>>(p, g_row_tuning, cap);
     return cudaGetLastError();
 }
 
@@ -743,9 +755,12 @@ static cudaError_t launch_csr_chain(const CsrSolveParams &p, int tpb, cudaStream
 }
 
 static cudaError_t launch_csr_row(const CsrSolveParams &p, int tpb, cudaStream_t st) {
-    if (tpb == 1024) return launch_csr_row_t<1024, 1>(p, st);
-    if (tpb == 512) return launch_csr_row_t<512, 2>(p, st);
-    return launch_csr_row_t<256, 4>(p, st);
+    const bool exact = p.flags & LCD_SOLVE_EXACT;
+    if (tpb == 1024)
+        return exact ? launch_csr_row_t<1024, 1, true>(p, st) : launch_csr_row_t<1024, 1, false>(p, st);
+    if (tpb == 512)
+        return exact ? launch_csr_row_t<512, 2, true>(p, st) : launch_csr_row_t<512, 2, false>(p, st);
+    return exact ? launch_csr_row_t<256, 4, true>(p, st) : launch_csr_row_t<256, 4, false>(p, st);
 }
 
 template <int G>

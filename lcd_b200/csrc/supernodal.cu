@@ -35,8 +35,13 @@ struct SupernodalParams {
     unsigned long long budget_ns;
 };
 
-__global__ void __launch_bounds__(kSnThreads) supernodal_kernel(const SupernodalParams p) {
+__device__ __forceinline__ void prefetch_l2(const void *ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+__global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const SupernodalParams p) {
     __shared__ double xs[kSnMaxWidth];
+    __shared__ double tri[32][33];  // current 32 x 32 diagonal sub-block, row-major, padded
     __shared__ int s_task;
     __shared__ int s_ok;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -53,6 +58,27 @@ __global__ void __launch_bounds__(kSnThreads) supernodal_kernel(const Supernodal
     if (w <= 0 || w > kSnMaxWidth || len < w) {
         if (tid == 0) raise_error(p.status, w > kSnMaxWidth ? LCD_ERR_TOO_LARGE : LCD_ERR_BAD_POINTERS, s);
         return;
+    }
+    // ---- while the inputs are not there yet: pull this task's panel strip (and, for the
+    // task that solves the diagonal block, that block) towards L2, so that the dependence
+    // wait overlaps the HBM stream instead of preceding it
+    {
+        const int rows = len - w;
+        const int j0 = strip * kSnThreads;
+        const int nrow = min(kSnThreads, rows - j0);
+        if (nrow > 0) {
+            // one prefetch per 32-byte sector: 4 consecutive rows share a sector per column
+            const double *P = M + w + j0;
+            for (int idx = tid; idx < ((nrow + 3) >> 2) * w; idx += kSnThreads) {
+                const int c = idx / ((nrow + 3) >> 2), q = idx % ((nrow + 3) >> 2);
+                prefetch_l2(P + (long long)c * len + 4 * q);
+            }
+        }
+        if (strip == 0)
+            for (int idx = tid; idx < ((w + 3) >> 2) * w; idx += kSnThreads) {
+                const int c = idx / ((w + 3) >> 2), q = idx % ((w + 3) >> 2);
+                prefetch_l2(M + (long long)c * len + 4 * q);
+            }
     }
     // ---- wait for the inputs of this task --------------------------------
     if (tid == 0) {
@@ -76,18 +102,19 @@ __global__ void __launch_bounds__(kSnThreads) supernodal_kernel(const Supernodal
         // ---- dense triangular solve, 32 columns at a time --------------------
         for (int cb = 0; cb < w; cb += 32) {
             const int bw = min(32, w - cb);
+            // stage the 32 x 32 triangle (coalesced down the columns), then warp 0 solves it
+            for (int idx = tid; idx < 32 * bw; idx += kSnThreads) {
+                const int c = idx >> 5, rr = idx & 31;
+                if (rr < bw && rr >= c) tri[rr][c] = __ldg(M + (long long)(cb + c) * len + cb + rr);
+            }
+            __syncthreads();
             if (warp == 0) {
                 const int r = cb + lane;  // row of this lane inside the diagonal block
-                double m[32];
-#pragma unroll
-                for (int c = 0; c < 32; ++c)
-                    m[c] = (lane < bw && c <= lane) ? __ldg(M + (long long)(cb + c) * len + r) : 1.0;
                 double v = lane < bw ? xs[r] : 0.0;
-#pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    if (lane == c) v = v / m[c];
+                for (int c = 0; c < bw; ++c) {
+                    if (lane == c) v = v / tri[c][c];
                     const double xc = __shfl_sync(0xffffffffu, v, c);
-                    if (lane > c && c < bw) v = fma(-m[c], xc, v);
+                    if (lane > c && lane < bw) v = fma(-tri[lane][c], xc, v);
                 }
                 if (lane < bw) xs[r] = v;
             }

@@ -202,7 +202,10 @@ def parallel(**kwargs):
                 trips = (max(nnz - n, 0), n) if thread_loop is not None else None
                 features = extract_workload_features(
                     dag, None, values, function_props=function_props,
-                    flops_per_iteration=2, thread_trip_counts=trips)
+                    flops_per_iteration=2, thread_trip_counts=trips,
+                    # measured on B200: the ILU0 sync-free kernel pays about 8x the SpTRSV
+                    # hand-off (acquire/release flags plus the row update before the release)
+                    sync_free_penalty=8.0 if operator == "ilu0_csr" else 1.0)
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
             return SchedulePlan(schedule=schedule, execution_data=data, features=features)

@@ -54,9 +54,13 @@ class ArchConstants:
     atomic_cost_s: float
     memory_bandwidth_bytes_per_s: float
     lane_flops_per_s: float
-    barrier_s: float = 2.5e-6
-    handoff_s: float = 0.9e-6
-    local_handoff_s: float = 0.1e-6
+    barrier_s: float = 3.0e-6           # grid-wide barrier after a level that spans the grid
+    block_level_s: float = 2.4e-6       # one level walked by a single block (__syncthreads)
+    block_level_row_s: float = 1.3e-8   # ... plus this much per row of that level
+    wavefront_row_s: float = 0.5e-9     # streaming cost per row in wide levels
+    handoff_s: float = 0.6e-6           # sync-free: one dependence hop on the critical chain
+    syncfree_row_s: float = 1.1e-9      # sync-free: per-row cost when many rows are in flight
+    block_level_width: int = 512        # levels up to this width stay inside one block
 
 
 FALLBACK_ARCH_CONSTANTS = ArchConstants(
@@ -78,6 +82,7 @@ class WorkloadFeatures:
     thread_work_items: int = 0
     thread_loop_invocations: int = 0
     max_level_width: int = 0
+    sync_free_penalty: float = 1.0   # operators whose sync-free kernel does more work per hop
 
     @property
     def average_in_degree(self):
@@ -247,18 +252,21 @@ class AnalyticScheduler:
             thread_mapped and features.thread_loop_invocations) else features.average_in_degree
         active = min(lanes, max(trip, 1.0))
         compute_s = features.flops / (active * arch.lane_flops_per_s * 148 * 64)
+        width = features.average_level_width
         if execution_mode == WAVEFRONT:
-            # narrow levels are walked by one block with block-level barriers
-            narrow = features.average_level_width <= 512
-            per_level = arch.local_handoff_s * 12 if narrow else arch.barrier_s
-            return CostEstimate(arch.launch_latency_s, features.levels * per_level, memory_s,
-                                compute_s)
+            if width <= arch.block_level_width:
+                per_level = arch.block_level_s + arch.block_level_row_s * width
+                sync_s = features.levels * per_level
+            else:
+                sync_s = features.levels * arch.barrier_s + features.rows * arch.wavefront_row_s
+            return CostEstimate(arch.launch_latency_s, sync_s, memory_s, compute_s)
         if execution_mode == SYNC_FREE:
-            # a hand-off is a poll of the operand itself; chains between nearby rows
-            # stay inside one block's shared memory
-            sync_s = features.levels * arch.handoff_s
+            # a hand-off is a poll of the operand itself; the chain pays one per level,
+            # wide levels add a throughput term
+            sync_s = (features.levels * arch.handoff_s + features.rows * arch.syncfree_row_s)
+            sync_s *= features.sync_free_penalty
             if dependence_protocol == PULL_DEPENDENCE:
-                sync_s *= 0.9
+                sync_s *= 0.99
             return CostEstimate(arch.launch_latency_s, sync_s, memory_s, compute_s)
         raise SchedulerError(f"Unknown execution mode {execution_mode!r}.")
 
@@ -311,7 +319,8 @@ def _array_nbytes(value):
 
 
 def extract_workload_features(dag, wavefront_list, argument_values, function_props=None,
-                              flops_per_iteration=1, thread_trip_counts=None):
+                              flops_per_iteration=1, thread_trip_counts=None,
+                              sync_free_penalty=1.0):
     """Features of one concrete input.  ``dag`` is either the reference's list of
     successor lists or a device DAG (then everything is read from its sizes)."""
     if hasattr(dag, "n_edges"):
@@ -348,7 +357,8 @@ def extract_workload_features(dag, wavefront_list, argument_values, function_pro
                             flops=float(flops_per_iteration * work),
                             memory_bytes=int(sum(seen.values())),
                             thread_work_items=items, thread_loop_invocations=invocations,
-                            max_level_width=int(widths.max()) if len(widths) else 0)
+                            max_level_width=int(widths.max()) if len(widths) else 0,
+                            sync_free_penalty=float(sync_free_penalty))
 
 
 def _digest(value):

@@ -147,9 +147,17 @@ def test_scheduler_decides_from_level_structure():
     wide = sc.WorkloadFeatures(rows=2_097_152, edges=6_000_000, levels=382, nonzeros=8_300_000,
                                flops=1.6e7, memory_bytes=140_000_000, thread_work_items=6_000_000,
                                thread_loop_invocations=2_097_152, max_level_width=12000)
-    assert sched.schedule(wide, space).execution_mode == "sync_free"
+    # wide levels (3-D grid): a near tie, decided for the level-synchronous kernel
+    assert sched.schedule(wide, space).execution_mode == "wavefront"
+    arch = sc.FALLBACK_ARCH_CONSTANTS
     cost = sched.estimate(wide, "wavefront", 128, 1, 1, True)
-    assert cost.total_s > 0 and cost.sync_s == pytest.approx(382 * sc.FALLBACK_ARCH_CONSTANTS.barrier_s)
+    assert cost.sync_s == pytest.approx(382 * arch.barrier_s + wide.rows * arch.wavefront_row_s)
+    import dataclasses
+    ilu = dataclasses.replace(wide, sync_free_penalty=8.0)
+    assert sched.schedule(ilu, space).execution_mode == "wavefront"
+    # measured: 754,679 levels -> 480 ms sync-free, 1.83 s level-synchronous
+    assert sched.estimate(narrow, "sync_free", 128, 1, 1, True).sync_s == pytest.approx(0.4575, rel=0.02)
+    assert sched.estimate(narrow, "wavefront", 128, 1, 1, True).sync_s == pytest.approx(1.87, rel=0.05)
     f = sc.extract_workload_features([[1, 2], [2], []], [[0], [1], [2]], {"Ap": np.array([0, 1, 3, 6])},
                                      function_props={"Ap": ["monotonically_increasing"]},
                                      flops_per_iteration=2, thread_trip_counts=(0, 1, 2))
