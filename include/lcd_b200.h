@@ -54,11 +54,8 @@ enum {
     LCD_SOLVE_UNIT_DIAG = 2,  /* implicit unit diagonal, no division (needs OF_FULL) */
     LCD_SOLVE_OF_FULL = 4,    /* the triangle is the part of a full sorted CSR row before
                                  (lower) / after (upper) diag_pos[row]; used on ILU0 factors */
-    LCD_SOLVE_EXACT = 8,      /* one lane per row, unfused multiply/subtract in storage order
+    LCD_SOLVE_EXACT = 8       /* one lane per row, unfused multiply/subtract in storage order
                                  and a true division: bit-identical to the sequential loop */
-    LCD_SOLVE_CHAIN = 16      /* sync-free CSR only: one warp walks each chunk of rows in blocks
-                                 of 32 with no waiting inside a chunk; for matrices whose levels
-                                 hold only a few rows (ignored together with LCD_SOLVE_EXACT) */
 };
 
 /* Device-side status block every solver uses: 8 int32 words in device memory,
@@ -130,6 +127,28 @@ int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int
                             const int32_t *diag_pos, const double *b, double *x, int flags,
                             int lanes_per_row, int threads_per_block, int32_t *status_dev,
                             int32_t timeout_ms, void *stream, int *status_host);
+
+/*
+ * Block-inverse chain solver for CSR systems whose levels hold only a few rows (long
+ * dependence chains).  No counterpart in the reference, which substitutes level by level;
+ * it serves the same loop nest (compiler/demo/sptrsv.py:26-34) and returns the same x up
+ * to rounding.  The 32 x 32 diagonal blocks of consecutive rows are inverted once per
+ * matrix (lcd_chain_prepare: numeric, repeat it whenever Ax changes; fully parallel), then
+ * lcd_sptrsv_csr_chain performs a block forward substitution in which each block costs one
+ * dense mat-vec by warp shuffles instead of 5-6 dependent levels.
+ *   workspace: lcd_chain_workspace_bytes(n) bytes (8 KiB per 32 rows), 8-byte aligned.
+ *   flags: LCD_SOLVE_UPPER / OF_FULL / UNIT_DIAG as for lcd_sptrsv_csr_syncfree.
+ * Explicit inverses are safe for diagonally dominant blocks; for other matrices prefer
+ * lcd_sptrsv_csr_syncfree.
+ */
+int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes);
+int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                      const double *Ax, const int32_t *diag_pos, int flags, void *workspace,
+                      int64_t workspace_bytes, void *stream);
+int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                         const double *Ax, const int32_t *diag_pos, const double *b, double *x,
+                         int flags, const void *workspace, int64_t workspace_bytes,
+                         int32_t *status_dev, int32_t timeout_ms, void *stream, int *status_host);
 
 /*
  * Multi-RHS variant: B and X are row-major n x nrhs blocks (leading dimension

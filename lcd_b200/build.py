@@ -15,8 +15,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB_PATH = os.path.join(HERE, "liblcd_b200.so")
-SOURCES = ("capi.cu", "dag_build.cu", "sptrsv_syncfree.cu", "sptrsv_wavefront.cu",
-           "spilu0.cu", "supernodal.cu")
+SOURCES = ("capi.cu", "dag_build.cu", "sptrsv_syncfree.cu", "sptrsv_chain.cu",
+           "sptrsv_wavefront.cu", "spilu0.cu", "supernodal.cu")
 NVCC_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
               "-Xcompiler", "-fPIC", "-I" + INCLUDE, "-I" + CSRC)
 

@@ -26,6 +26,10 @@ int finish(int32_t *status_dev, cudaStream_t stream, int *status_host) {
     return rc;
 }
 
+static long long *g_trace = nullptr;
+long long *debug_trace() { return g_trace; }
+void set_debug_trace(long long *p) { g_trace = p; }
+
 int sm_count() {
     static int cached = 0;
     if (!cached) {
@@ -89,6 +93,13 @@ extern "C" int lcd_checksum_i32(const int32_t *data, int64_t count, uint64_t *ou
                                      cudaMemcpyDeviceToHost, st));
         LCD_CUDA_TRY(cudaStreamSynchronize(st));
     }
+    return LCD_OK;
+}
+
+// Profiling aid: when set, the one-lane-per-row and chain solvers store the SM cycle
+// counter at which each row was published into trace[node] (n 64-bit words).
+extern "C" int lcd_debug_set_trace(long long *trace_dev) {
+    set_debug_trace(trace_dev);
     return LCD_OK;
 }
 

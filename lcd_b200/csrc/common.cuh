@@ -39,6 +39,8 @@ inline unsigned long long timeout_ns(int32_t timeout_ms) {
     return (unsigned long long)(timeout_ms > 0 ? timeout_ms : kDefaultTimeoutMs) * 1000000ull;
 }
 int sm_count();
+void set_debug_trace(long long *p);
+long long *debug_trace();  // profiling aid set by lcd_debug_set_trace (NULL = off)
 
 #ifdef __CUDACC__
 
@@ -84,6 +86,17 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Flags are polled with relaxed loads (an acquire load on every failed poll costs an
+// ordering operation each time); the acquire ordering is established once, by this
+// fence, after the poll that observed the released value.
+__device__ __forceinline__ void acquire_fence() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 __device__ __forceinline__ bool is_pending(double v) {

@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(TPB) ilu0_syncfree_kernel(const Ilu0Params p) 
         if (k >= 0) {
             int ready = 0;  // 0 not yet, 1 go, 2 give up
             if (lane == 0) {
-                if (ld_acquire_s32(p.done + k) != 0) ready = 1;
+                if (ld_relaxed_s32(p.done + k) != 0) { acquire_fence(); ready = 1; }
                 else if (dl.tick(p.status, i)) ready = 2;
             }
             if (G > 1) ready = __shfl_sync(gmask, ready, 0, G);

@@ -110,7 +110,6 @@ struct RowTuning {
     int stage_percent;    // staging area for matrix entries, percent of the average chunk
 };
 static RowTuning g_row_tuning = {0, 200, 0, 0, 120};
-static long long *g_trace = nullptr;
 
 // Thread per row.  Leading operands that live before the chunk and are already
 // available are consumed first without waiting; everything else goes through a
@@ -269,209 +268,6 @@ csr_syncfree_row_kernel(const CsrSolveParams p, const RowTuning tune, const int 
 #undef LCD_ACCUMULATE
 }
 
-// ---- chain kernel: for matrices whose levels are narrow ------------------------
-// When every level holds only a handful of rows the solve is one long dependence
-// chain and any scheme that hands values from thread to thread by polling pays a
-// poll per level.  Here a chunk of TPB consecutive rows is solved by ONE warp that
-// walks the chunk in blocks of 32 rows, so inside a chunk nothing is ever waited
-// for:
-//   phase A (all threads, one row each): stage the chunk's matrix entries in shared
-//     memory, subtract every contribution that comes from rows before the chunk
-//     (polling x in global memory; those rows belong to earlier tickets), leave the
-//     partial sums in shared memory;
-//   phase B (warp 0): for each block of 32 rows, lanes subtract the contributions
-//     of earlier blocks of the chunk (values are in the shared-memory mirror
-//     already), then the 32 x 32 triangle inside the block is resolved level by
-//     level: a ballot tells which rows have all in-block operands final.
-// The only hand-off through global memory is between consecutive chunks.
-constexpr int kChainSlots = 4;  // in-block operands a lane keeps in registers
-
-template <int TPB>
-__global__ void __launch_bounds__(TPB, 1)
-csr_syncfree_chain_kernel(const CsrSolveParams p, const RowTuning tune, const int cap) {
-    extern __shared__ __align__(16) unsigned char chain_smem[];
-    double *sx = reinterpret_cast<double *>(chain_smem);  // x of the chunk
-    double *sacc = sx + TPB;                               // b - (contributions from before the chunk)
-    double *sdiv = sacc + TPB;                             // 1/diag (fast) or diag (exact)
-    double *sval = sdiv + TPB;                             // staged values
-    int *sidx = reinterpret_cast<int *>(sval + cap);       // staged indices
-    int *s_in = sidx + cap;                                // first entry that may lie in the chunk
-    int *s_hi = s_in + TPB;                                // end of the off-diagonal range
-    __shared__ int s_chunk;
-    __shared__ int s_failed;
-    const int tid = threadIdx.x;
-    if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; }
-    __syncthreads();
-    const int row0 = s_chunk * TPB;
-    const int task = row0 + tid;
-    const bool upper = p.flags & LCD_SOLVE_UPPER;
-    const bool exact = p.flags & LCD_SOLVE_EXACT;
-    const int task_end = min(row0 + TPB, p.n);
-    const int rows_here = task_end - row0;
-    const int first_row = upper ? p.n - task_end : row0;
-    const int last_row = upper ? p.n - 1 - row0 : task_end - 1;
-    long long seg_begin = 0;
-    int count = 0;
-    if (rows_here > 0) {
-        seg_begin = __ldg(p.Ap + first_row);
-        const long long seg_end = __ldg(p.Ap + last_row + 1);
-        if (seg_begin >= 0 && seg_end >= seg_begin && seg_end <= p.nnz)
-            count = (int)min((long long)cap, seg_end - seg_begin);
-        else
-            seg_begin = 0;
-    }
-    for (int k = tid; k < count; k += TPB) {
-        sidx[k] = __ldg(p.Ai + seg_begin + k);
-        sval[k] = __ldg(p.Ax + seg_begin + k);
-    }
-    __syncthreads();
-    const int sbase = (int)seg_begin;
-#define LCD_ENTRY(j_, c_, a_)                                               \
-    do {                                                                    \
-        const unsigned pos_ = (unsigned)((j_) - sbase);                     \
-        if (pos_ < (unsigned)count) { c_ = sidx[pos_]; a_ = sval[pos_]; }   \
-        else { c_ = __ldg(p.Ai + (j_)); a_ = __ldg(p.Ax + (j_)); }          \
-    } while (0)
-
-    // ---- phase A ---------------------------------------------------------------
-    if (task < p.n) {
-        const int r = upper ? p.n - 1 - task : task;
-        int lo = 0, hi = 0, d = -1;
-        bool failed = false;
-        if (!csr_row_range(p, r, lo, hi, d)) {
-            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
-                                                               : LCD_ERR_BAD_POINTERS, r);
-            failed = true;
-            lo = hi = 0;
-            d = -1;
-        }
-        double acc = __ldg(p.b + r);
-        double dv = 1.0;
-        if (d >= 0) dv = ((unsigned)(d - sbase) < (unsigned)count) ? sval[d - sbase] : __ldg(p.Ax + d);
-        int first_in = hi;
-        Deadline dl;
-        dl.start(p.budget_ns);
-        for (int j = lo; j < hi && !failed; ++j) {
-            int c;
-            double a;
-            LCD_ENTRY(j, c, a);
-            const int tc = upper ? p.n - 1 - c : c;
-            if ((unsigned)tc >= (unsigned)task) {
-                raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
-                failed = true;
-                break;
-            }
-            if (tc >= row0) {  // an operand of this chunk: phase B
-                if (first_in == hi) first_in = j;
-                continue;
-            }
-            double xv;
-            // rows before the chunk belong to earlier tickets: a plain bounded spin is safe
-            while (is_pending(xv = ld_relaxed_f64(p.x + c))) {
-                if (dl.tick(p.status, r)) { failed = true; break; }
-                if (tune.sleep_global_ns > 0) __nanosleep(tune.sleep_global_ns);
-            }
-            if (failed) break;
-            acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
-        }
-        sacc[tid] = acc;
-        sdiv[tid] = (d < 0) ? 1.0 : (exact ? dv : 1.0 / dv);
-        s_in[tid] = first_in;
-        s_hi[tid] = hi;
-        if (failed) s_failed = 1;
-    }
-    __syncthreads();
-    if (tid >= 32) return;
-
-    // ---- phase B: warp 0 walks the chunk -------------------------------------------
-    const int lane = tid;
-    const bool chunk_failed = s_failed != 0;
-    const double nanv = __longlong_as_double(kCanonicalNaN);
-    volatile double *sxv = sx;
-    for (int base = 0; base < rows_here; base += 32) {
-        const int local = base + lane;
-        const bool active = local < rows_here;
-        const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-        double acc = 0.0, div = 1.0;
-        int j = 0, hi = 0;
-        if (active) { acc = sacc[local]; div = sdiv[local]; j = s_in[local]; hi = s_hi[local]; }
-        if (chunk_failed) {  // drain: publish something so that later chunks do not wait
-            if (active) sxv[local] = nanv;
-            continue;
-        }
-        if (p.trace && active) p.trace[(long long)p.n + row0 + local] = clock64();
-        // operands from earlier blocks of the chunk are final: no waiting.  In-block
-        // operands are remembered (a few in registers, the rest re-read later).
-        unsigned depmask = 0;
-        int jb = hi;  // first in-block entry
-        int c0 = 0, c1 = 0, c2 = 0, c3 = 0, nslot = 0;
-        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-        for (; j < hi; ++j) {
-            int c;
-            double a;
-            LCD_ENTRY(j, c, a);
-            const int cl = (upper ? p.n - 1 - c : c) - row0;
-            if (cl < 0) continue;  // already taken in phase A (unsorted rows only)
-            if (cl >= base) {
-                if (jb == hi) jb = j;
-                depmask |= 1u << (cl - base);
-                if (nslot == 0) { c0 = cl; a0 = a; }
-                else if (nslot == 1) { c1 = cl; a1 = a; }
-                else if (nslot == 2) { c2 = cl; a2 = a; }
-                else if (nslot == 3) { c3 = cl; a3 = a; }
-                ++nslot;
-            } else {
-                const double xv = sxv[cl];
-                acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
-            }
-        }
-        if (p.trace && active) p.trace[2ll * p.n + row0 + local] = clock64();
-        // in-block triangle, level by level
-        unsigned final_mask = __ballot_sync(0xffffffffu, !active);
-        bool final = !active;
-        for (int round = 0; round < 33; ++round) {
-            const bool ready = !final && (depmask & ~final_mask) == 0;
-            if (ready) {
-                if (nslot <= kChainSlots && !exact) {
-                    if (nslot > 0) acc = fma(-a0, sxv[c0], acc);
-                    if (nslot > 1) acc = fma(-a1, sxv[c1], acc);
-                    if (nslot > 2) acc = fma(-a2, sxv[c2], acc);
-                    if (nslot > 3) acc = fma(-a3, sxv[c3], acc);
-                } else {
-                    for (int jj = jb; jj < hi; ++jj) {
-                        int c;
-                        double a;
-                        LCD_ENTRY(jj, c, a);
-                        const int cl = (upper ? p.n - 1 - c : c) - row0;
-                        if (cl < base) continue;
-                        const double xv = sxv[cl];
-                        acc = exact ? __dsub_rn(acc, __dmul_rn(a, xv)) : fma(-a, xv, acc);
-                    }
-                }
-                const double val = publishable(exact ? ((p.flags & LCD_SOLVE_UNIT_DIAG) ? acc : acc / div)
-                                                     : acc * div);
-                sxv[local] = val;  // global publication is deferred: a warp barrier after a
-                final = true;      // global store would wait for the store to be performed
-                if (p.trace) p.trace[row0 + local] = clock64();
-            }
-            __syncwarp();
-            const unsigned now = __ballot_sync(0xffffffffu, final);
-            if (now == 0xffffffffu) break;
-            if (now == final_mask) {  // no progress: cannot happen for validated rows
-                raise_error(p.status, LCD_ERR_CYCLE, r);
-                if (!final && active) sxv[local] = nanv;
-                break;
-            }
-            final_mask = now;
-        }
-        __syncwarp();
-    }
-    // publish the chunk: coalesced, and nothing waits on these stores inside the kernel
-    for (int k = lane; k < rows_here; k += 32)
-        st_relaxed_f64(p.x + (upper ? p.n - 1 - (row0 + k) : row0 + k), sxv[k]);
-#undef LCD_ENTRY
-}
-
 // Multi-RHS: the block of right-hand sides is row-major, W consecutive lanes own a
 // row, lane l owns the right-hand sides l, l + W, ... (KR of them at most).  A lane
 // polls exactly the operand elements it consumes (written by the same lane position of
@@ -620,7 +416,7 @@ __global__ void __launch_bounds__(TPB) csc_syncfree_kernel(const CscSolveParams 
     dl.start(p.budget_ns);
     for (;;) {
         if (lane == 0 && state == 0) {
-            if (ld_acquire_s32(p.dep + i) == 0) state = 1;
+            if (ld_relaxed_s32(p.dep + i) == 0) { acquire_fence(); state = 1; }
             else if (dl.tick(p.status, i)) state = 2;
         }
         if (G > 1) state = __shfl_sync(gmask, state, 0, G);
@@ -726,34 +522,6 @@ static cudaError_t launch_csr_row_t(const CsrSolveParams &p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-template <int TPB>
-static cudaError_t launch_csr_chain_t(const CsrSolveParams &p, cudaStream_t st) {
-    const size_t limit = 227 * 1024 - 256;
-    const size_t fixed = (size_t)TPB * (3 * 8 + 2 * 4);
-    const double avg = p.n > 0 ? (double)p.nnz / p.n : 0.0;
-    long long cap = (long long)(avg * TPB * 1.25) + 256;
-    const long long max_cap = ((long long)limit - (long long)fixed) / 12;
-    if (cap > max_cap) cap = max_cap;
-    cap &= ~1ll;
-    const size_t smem = fixed + (size_t)cap * 12;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(csr_syncfree_chain_kernel<TPB>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)limit);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
-    csr_syncfree_chain_kernel<TPB><<<(p.n + TPB - 1) / TPB, TPB, smem, st>>>(p, g_row_tuning, (int)cap);
-    return cudaGetLastError();
-}
-
-static cudaError_t launch_csr_chain(const CsrSolveParams &p, int tpb, cudaStream_t st) {
-    if (tpb == 512) return launch_csr_chain_t<512>(p, st);
-    if (tpb == 256) return launch_csr_chain_t<256>(p, st);
-    return launch_csr_chain_t<1024>(p, st);
-}
-
 static cudaError_t launch_csr_row(const CsrSolveParams &p, int tpb, cudaStream_t st) {
     const bool exact = p.flags & LCD_SOLVE_EXACT;
     if (tpb == 1024)
@@ -819,13 +587,6 @@ extern "C" int lcd_set_tuning(int key, int value) {
     return LCD_OK;
 }
 
-// Profiling aid: when set, the one-lane-per-row kernel stores the SM cycle counter
-// at which each row was published into trace[node] (n 64-bit words).
-extern "C" int lcd_debug_set_trace(long long *trace_dev) {
-    g_trace = trace_dev;
-    return LCD_OK;
-}
-
 extern "C" int lcd_fill_u64(uint64_t *dst, int64_t count, uint64_t value, void *stream) {
     if (count < 0 || (count > 0 && !dst)) return LCD_ERR_INVALID_ARGUMENT;
     if (count == 0) return LCD_OK;
@@ -873,7 +634,7 @@ extern "C" int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap
     if (n > 0 && x == b) return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;
     int G = lanes_per_row > 0 ? lanes_per_row : pick_lanes(nnz, n);
-    if (flags & (LCD_SOLVE_EXACT | LCD_SOLVE_CHAIN)) G = 1;
+    if (flags & LCD_SOLVE_EXACT) G = 1;
     int tpb = threads_per_block > 0 ? threads_per_block : 1024;
     if (tpb != 256 && tpb != 512 && tpb != 1024) return LCD_ERR_INVALID_ARGUMENT;
     int rc = reset_status(status_dev, st);
@@ -881,15 +642,11 @@ extern "C" int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap
     if (n > 0) {
         LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
         CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, 1, 1, status_dev,
-                         timeout_ns(timeout_ms), g_trace, 0, n, nullptr, {nullptr}};
+                         timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
         cudaError_t e;
         switch (G) {
             case 1:
-                if ((flags & LCD_SOLVE_CHAIN) && !(flags & LCD_SOLVE_EXACT))
-                    e = launch_csr_chain(p, tpb, st);
-                else
-                    e = g_row_tuning.variant == 0 ? launch_csr_row(p, tpb, st)
-                                                  : launch_csr<1>(p, tpb, st);
+                e = g_row_tuning.variant == 0 ? launch_csr_row(p, tpb, st) : launch_csr<1>(p, tpb, st);
                 break;
             case 2: e = launch_csr<2>(p, tpb, st); break;
             case 4: e = launch_csr<4>(p, tpb, st); break;
@@ -1029,8 +786,7 @@ extern "C" int lcd_sptrsv_csr_syncfree_part(int32_t n, int64_t nnz, const int32_
     if (n < 0 || nnz < 0 || !status_dev || task_begin < 0 || task_end < task_begin || task_end > n ||
         n_ranks < 1 || n_ranks > 8)
         return LCD_ERR_INVALID_ARGUMENT;
-    if (flags & (LCD_SOLVE_OF_FULL | LCD_SOLVE_UNIT_DIAG | LCD_SOLVE_CHAIN))
-        return LCD_ERR_INVALID_ARGUMENT;
+    if (flags & (LCD_SOLVE_OF_FULL | LCD_SOLVE_UNIT_DIAG)) return LCD_ERR_INVALID_ARGUMENT;
     if (n > 0 && (!Ap || !Ai || !Ax || !b || !x || x == b)) return LCD_ERR_INVALID_ARGUMENT;
     if (need_mask && !peer_x) return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;

@@ -113,9 +113,10 @@ __device__ __forceinline__ bool grid_barrier(const WavefrontParams &w, unsigned 
         atomicAdd(counter, 1ull);
         Deadline dl;
         dl.start(w.m.budget_ns);
-        while (ld_acquire_u64(counter) < target) {
+        while (ld_relaxed_u64(counter) < target) {
             if (dl.tick(w.m.status, -1)) { ok = 0; break; }
         }
+        acquire_fence();
         if (aborted(w.m.status)) ok = 0;
         *s_ok = ok;
     }

@@ -88,8 +88,8 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         const int *flag = strip == 0 ? p.pending + s : p.solved + s;
         const int want_zero = strip == 0;
         for (;;) {
-            const int v = ld_acquire_s32(flag);
-            if (want_zero ? v == 0 : v != 0) break;
+            const int v = ld_relaxed_s32(flag);
+            if (want_zero ? v == 0 : v != 0) { acquire_fence(); break; }
             if (dl.tick(p.status, s)) { ok = 0; break; }
         }
         s_ok = ok;

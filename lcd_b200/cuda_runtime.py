@@ -159,7 +159,10 @@ def prepare_cuda_arguments(lowering, argument_values, execution_data, function_g
     if cuda_module is None:
         cuda_module = TorchCUDA
     host_values = dict(argument_values)
-    host_values.update(_evaluate_host_prelude(lowering, host_values, function_globals or {}))
+    prelude_names = _stored_names(lowering.host_prelude)
+    if not all(name in host_values for name in prelude_names):
+        # (callers that already evaluated the prelude pass its values along)
+        host_values.update(_evaluate_host_prelude(lowering, host_values, function_globals or {}))
     host_values.update(_execution_values(lowering.execution_mode, execution_data))
     missing = [name for name in lowering.launcher_arguments if name not in host_values]
     if missing:
@@ -195,10 +198,12 @@ def execute_cuda_call(compiled_module, lowering, prepared_arguments, function_gl
             "The compiled CUDA module does not provide cuda.synchronize().")
     cuda_module.synchronize()
     results = dict(prepared_arguments.host_values)
-    results.update({name: prepared_arguments.copy_to_host(name)
-                    for name in _returned_names(lowering.host_epilogue)
-                    if name in prepared_arguments.values})
-    results.update(prepared_arguments.copy_lifted_variables_to_host())
+    # returned arguments and lifted locals come back to the host; a name that is both
+    # (the usual ``x``) is copied once
+    names = [name for name in _returned_names(lowering.host_epilogue)
+             if name in prepared_arguments.values]
+    names += [name for name in prepared_arguments.lifted_variables if name not in names]
+    results.update({name: prepared_arguments.copy_to_host(name) for name in names})
     return _evaluate_host_epilogue(lowering, results, function_globals or {})
 
 

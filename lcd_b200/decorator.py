@@ -247,7 +247,7 @@ def parallel(**kwargs):
             lowering, module = compile_variant(plan.schedule.lowering_key)
             publish_variant(plan.schedule, lowering, module)
             # hand the already uploaded structure arrays to the launcher
-            launch_values = dict(argument_values)
+            launch_values = dict(values)          # arguments plus the evaluated host prelude
             for name, tensor in structure.items():
                 if name in launch_values:
                     launch_values[name] = DeviceArray(tensor)

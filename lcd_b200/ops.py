@@ -127,11 +127,43 @@ def _solve_flags(upper, unit_diag, of_full, exact):
             | (nat.SOLVE_OF_FULL if of_full else 0) | (nat.SOLVE_EXACT if exact else 0))
 
 
+def chain_workspace(n, device):
+    """Scratch for the block-inverse chain solver (8 KiB per 32 rows)."""
+    need = ctypes.c_int64(0)
+    check(nat.load().lcd_chain_workspace_bytes(int(n), ctypes.byref(need)), "lcd_chain_workspace_bytes")
+    return torch.empty((need.value + 7) // 8, dtype=torch.float64, device=device)
+
+
+def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_pos=None):
+    """Invert the 32 x 32 diagonal blocks into ``workspace`` (repeat when Ax changes)."""
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    check(nat.load().lcd_chain_prepare(Ap.numel() - 1, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax),
+                                       ptr(diag_pos), flags, ptr(workspace),
+                                       workspace.numel() * 8, _stream()), "lcd_chain_prepare")
+    return workspace
+
+
+def sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, unit_diag=False,
+                     diag_pos=None, status=None, timeout_ms=0, sync=True):
+    """Block-inverse chain solve (for matrices whose levels hold only a few rows).
+    ``workspace`` must have been filled by ``chain_prepare`` for the same matrix."""
+    _require(b, torch.float64, "b")
+    n = Ap.numel() - 1
+    x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
+    status = new_status(b.device) if status is None else status
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_csr_chain(
+        n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
+        ptr(workspace), workspace.numel() * 8, ptr(status), int(timeout_ms), _stream(),
+        ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_csr_chain")
+    return x
+
+
 def sptrsv_csr_syncfree(Ap, Ai, Ax, b, x=None, *, upper=False, unit_diag=False, diag_pos=None,
-                        exact=False, chain=False, lanes=0, threads=0, status=None, timeout_ms=0,
-                        sync=True):
-    """Sync-free CSR triangular solve; returns x (a new tensor unless given).
-    ``chain=True`` selects the kernel for matrices with narrow levels."""
+                        exact=False, lanes=0, threads=0, status=None, timeout_ms=0, sync=True):
+    """Sync-free CSR triangular solve; returns x (a new tensor unless given)."""
     _require(Ap, torch.int32, "Ap")
     _require(Ai, torch.int32, "Ai")
     _require(Ax, torch.float64, "Ax")
@@ -140,8 +172,6 @@ def sptrsv_csr_syncfree(Ap, Ai, Ax, b, x=None, *, upper=False, unit_diag=False, 
     x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
     status = new_status(b.device) if status is None else status
     flags = _solve_flags(upper, unit_diag, diag_pos is not None, exact)
-    if chain:
-        flags |= nat.SOLVE_CHAIN
     host = ctypes.c_int(0)
     rc = nat.load().lcd_sptrsv_csr_syncfree(
         n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,

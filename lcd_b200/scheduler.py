@@ -7,15 +7,18 @@ Keeps the public interface of the reference's ``compiler/scheduler.py``
 working, but replaces the cost model.  The reference estimates
 ``launch_latency * levels`` against ``atomic_cost * rows`` and has no term for
 the critical path; here the decision is taken from the level structure the DAG
-build measured:
+build measured, with constants measured on B200:
 
-* time of a level-synchronous run  ~ levels * t_barrier + bytes / bandwidth,
-* time of a sync-free run          ~ levels * t_handoff + bytes / bandwidth,
+* sync-free:        levels * t_handoff (0.6 us) + rows * 1.1 ns
+* level-synchronous, levels that fit one block (<= 512 rows):
+                    levels * (2.4 us + 13 ns * width)   (block-level barriers)
+* level-synchronous, wide levels:
+                    levels * t_grid_barrier (3 us) + rows * 0.5 ns
 
-with ``t_handoff < t_barrier`` on this hardware, so wavefront execution is only
-chosen when it was asked for or when the average level is so wide that the
-barrier cost vanishes against the streaming time and the wavefront kernel's
-better load balance wins.  Lane-group width follows the measured trip counts.
+so a long chain of narrow levels goes to the sync-free kernel (754,679 levels:
+0.46 s against 1.8 s), while grids with thousands of rows per level are a near
+tie that the level-synchronous kernel wins, clearly so for ILU0 whose sync-free
+hand-off is about 8x dearer.
 """
 
 from __future__ import annotations

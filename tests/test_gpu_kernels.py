@@ -169,53 +169,55 @@ def test_csr_syncfree_lane_groups(cuda, oracle, lanes, threads):
     np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b), rtol=1e-10, atol=1e-12)
 
 
-@pytest.mark.parametrize("threads", [256, 512, 1024])
-def test_csr_syncfree_chain_kernel(cuda, oracle, threads):
-    """The narrow-level kernel (one warp walks each chunk) on banded, grid, unsorted,
-    upper-triangular and ragged-size inputs."""
+def _chain_solve(ops, cuda, Ap, Ai, Ax, b, **kw):
+    dAp, dAi, dAx = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda)
+    ws = ops.chain_prepare(dAp, dAi, dAx, ops.chain_workspace(len(Ap) - 1, cuda), **kw)
+    return host(ops.sptrsv_csr_chain(dAp, dAi, dAx, dev(b, np.float64, cuda), ws, **kw))
+
+
+def test_csr_chain_solver(cuda, oracle):
+    """The block-inverse chain solver on banded, grid, unsorted, upper-triangular, dense
+    and ragged-size inputs."""
     from lcd_b200 import generators as gen, ops
-    cases = [gen.random_band_lower(30_011, seed=threads, mean_degree=15.0, band=64),
-             gen.random_band_lower(5_000, seed=1, mean_degree=40.0, band=200),   # rows longer than the register slots
+    cases = [gen.random_band_lower(30_011, seed=7, mean_degree=15.0, band=64),
+             gen.random_band_lower(5_000, seed=1, mean_degree=40.0, band=200),
+             gen.random_band_lower(2_500, seed=2, mean_degree=120.0, band=900),   # compact list overflows
              gen.laplacian2d_tril(96, seed=2), gen.laplacian3d_tril(17, seed=3)]
     for tri in cases:
         Ap, Ai, Ax = tri.csr_arrays()
-        x = host(ops.sptrsv_csr_syncfree(dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda),
-                                         dev(tri.b, np.float64, cuda), chain=True, threads=threads))
+        x = _chain_solve(ops, cuda, Ap, Ai, Ax, tri.b)
         assert csr_residual(Ap, Ai, Ax, x, tri.b) <= RESIDUAL_TOL
         np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b), rtol=1e-10, atol=1e-12)
         up = gen.upper_from_lower(tri)
         Up, Ui, Ux = up.csr_arrays()
-        x = host(ops.sptrsv_csr_syncfree(dev(Up, np.int32, cuda), dev(Ui, np.int32, cuda), dev(Ux, np.float64, cuda),
-                                         dev(up.b, np.float64, cuda), chain=True, upper=True, threads=threads))
+        x = _chain_solve(ops, cuda, Up, Ui, Ux, up.b, upper=True)
         np.testing.assert_allclose(x, oracle.sptrsv_csr_upper(Up, Ui, Ux, up.b), rtol=1e-10, atol=1e-12)
     for name in ("sptrsv_unsorted_dups", "sptrsv_band_n600", "sptrsv_lap2d_g8"):
         g = golden(name)
-        x = ops.sptrsv_csr_syncfree(dev(g["csr_Ap"], np.int32, cuda), dev(g["csr_Ai"], np.int32, cuda),
-                                    dev(g["csr_Ax"], np.float64, cuda), dev(g["b"], np.float64, cuda),
-                                    chain=True, threads=threads)
-        np.testing.assert_allclose(host(x), g["x_csr"], rtol=1e-10, atol=1e-12)
-    one = ops.sptrsv_csr_syncfree(dev([0, 1], np.int32, cuda), dev([0], np.int32, cuda),
-                                  dev([4.0], np.float64, cuda), dev([2.0], np.float64, cuda), chain=True, threads=threads)
-    assert host(one)[0] == 0.5
+        x = _chain_solve(ops, cuda, g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"])
+        np.testing.assert_allclose(x, g["x_csr"], rtol=1e-10, atol=1e-12)
+    assert _chain_solve(ops, cuda, [0, 1], [0], [4.0], [2.0])[0] == 0.5
     # a dense lower triangle: every row of a block depends on all earlier rows of the block
     n = 150
     L = sp.csr_matrix(np.tril(np.random.default_rng(0).uniform(0.01, 0.02, (n, n))) + 2 * np.eye(n))
     b = np.ones(n)
-    x = host(ops.sptrsv_csr_syncfree(dev(L.indptr, np.int32, cuda), dev(L.indices, np.int32, cuda),
-                                     dev(L.data, np.float64, cuda), dev(b, np.float64, cuda), chain=True, threads=threads))
+    x = _chain_solve(ops, cuda, L.indptr, L.indices, L.data, b)
     np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(L.indptr, L.indices, L.data, b), rtol=1e-10, atol=1e-12)
 
 
-def test_csr_syncfree_chain_kernel_on_ilu_factors_and_errors(cuda, oracle):
+def test_csr_chain_solver_on_ilu_factors_and_errors(cuda, oracle):
     from lcd_b200 import generators as gen, ops
-    from lcd_b200._native import ERR_INDEX_RANGE, NativeError
+    from lcd_b200._native import ERR_INDEX_RANGE, ERR_WORKSPACE, NativeError
     mat, b = gen.laplacian3d_ilu0(12, seed=0)
     Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
     dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
     pos = ops.diag_positions(dAp, dAi)
     fac = ops.spilu0_csr(dAp, dAi, dev(Ax, np.float64, cuda), pos)
-    y = ops.sptrsv_csr_syncfree(dAp, dAi, fac, dev(b, np.float64, cuda), diag_pos=pos, unit_diag=True, chain=True)
-    x = ops.sptrsv_csr_syncfree(dAp, dAi, fac, y, diag_pos=pos, upper=True, chain=True)
+    ws = ops.chain_workspace(len(Ap) - 1, cuda)
+    ops.chain_prepare(dAp, dAi, fac, ws, diag_pos=pos, unit_diag=True)
+    y = ops.sptrsv_csr_chain(dAp, dAi, fac, dev(b, np.float64, cuda), ws, diag_pos=pos, unit_diag=True)
+    ops.chain_prepare(dAp, dAi, fac, ws, diag_pos=pos, upper=True)
+    x = ops.sptrsv_csr_chain(dAp, dAi, fac, y, ws, diag_pos=pos, upper=True)
     want = oracle.ilu0_csr(Ap, Ai, Ax, fast=True)
     hp = host(pos)
     x_ref = oracle.sptrsv_upper_of_full(Ap, Ai, want, hp, oracle.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, b))
@@ -225,10 +227,16 @@ def test_csr_syncfree_chain_kernel_on_ilu_factors_and_errors(cuda, oracle):
     bad = Ai.copy()
     row = next(r for r in range(10, 100) if Ap[r + 1] - Ap[r] >= 2)
     bad[Ap[row]] = row + 10
+    dAp, dbad, dAx = dev(Ap, np.int32, cuda), dev(bad, np.int32, cuda), dev(Ax, np.float64, cuda)
+    ws = ops.chain_prepare(dAp, dbad, dAx, ops.chain_workspace(tri.n, cuda))
     with pytest.raises(NativeError) as err:
-        ops.sptrsv_csr_syncfree(dev(Ap, np.int32, cuda), dev(bad, np.int32, cuda), dev(Ax, np.float64, cuda),
-                                dev(tri.b, np.float64, cuda), chain=True, timeout_ms=300)
+        ops.sptrsv_csr_chain(dAp, dbad, dAx, dev(tri.b, np.float64, cuda), ws, timeout_ms=300)
     assert err.value.code == ERR_INDEX_RANGE
+    import torch
+    with pytest.raises(NativeError) as err:
+        ops.sptrsv_csr_chain(dAp, dev(Ai, np.int32, cuda), dAx, dev(tri.b, np.float64, cuda),
+                             torch.empty(16, dtype=torch.float64, device=cuda))
+    assert err.value.code == ERR_WORKSPACE
 
 
 def test_csr_syncfree_upper_and_golden(cuda, oracle):
