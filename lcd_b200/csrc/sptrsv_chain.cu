@@ -1,221 +1,366 @@
-// Block-inverse chain solver: CSR triangular solves whose levels hold only a few rows.
+// Block-recurrence chain solver: CSR triangular solves whose levels hold only a few rows.
 //
 // Such a matrix is one long dependence chain: level-by-level substitution pays one
 // hand-off (a poll, a barrier, or a dozen dependent instructions of a lone warp) per
 // level, and there are hundreds of thousands of levels.  The chain is shortened
-// algebraically instead: rows are grouped into blocks of 32 consecutive rows, the
-// 32 x 32 lower-triangular diagonal block D_b of every group is inverted once per
-// matrix (lcd_chain_prepare, fully parallel, one warp per block), and the solve
-// becomes a block forward substitution
-//        x_b = D_b^{-1} ( b_b - sum_{c < b} L_bc x_c )
-// in which the 5-6 levels inside a block collapse into one dense 32 x 32 mat-vec done
-// with warp shuffles (no dependent chain: 32 independent shuffle/FMA pairs).
+// algebraically instead.  Rows are grouped into blocks of 32 consecutive rows; with
+// D_b the 32 x 32 diagonal block and L_bc the coupling of block b to block c, the solve
+//        D_b x_b = r_b - L_b,b-1 x_b-1 - L_b,b-2 x_b-2 - sum_{c <= b-3} L_bc x_c
+// is rewritten, once per matrix (lcd_chain_prepare, one warp per block, fully parallel),
+// as
+//        x_b = y_b - W1_b x_b-1 - W2_b x_b-2,     W1_b = D_b^-1 L_b,b-1,  W2_b = D_b^-1 L_b,b-2
+//        y_b = D_b^-1 ( r_b - sum_{c <= b-3} L_bc x_c )
+// so that the part of the chain that cannot be overlapped, x_b-1 -> x_b, is one dense
+// 32 x 32 mat-vec (no dependent chain inside it), and everything that reaches at least
+// three blocks back is taken off that path.
 //
-//   phase A (all threads of a block, several rows each): subtract the contributions of
-//     rows before the chunk (polling x in global memory, rows of earlier tickets), copy
-//     the operands that come from earlier 32-row blocks of the chunk into a compact
-//     shared-memory list, leave partial sums in shared memory;
-//   phase B (warp 0): walks the chunk block by block; lanes subtract their compact
-//     operands (values of earlier blocks are final in shared memory, nothing to wait for),
-//     then apply the inverse block from registers (loaded one block ahead) and publish.
+// The solve kernel works on chunks of 1024 rows handed out by ticket (a chunk only waits
+// for chunks with smaller tickets, which are running or done, so the waits terminate):
+//   phase A (256 threads, four rows each): operands from before the chunk are fetched by
+//     polling x in global memory (a solution vector pre-filled with a reserved NaN is its
+//     own ready flag); operands that lie in the chunk, three or more blocks back, go into
+//     a shared-memory list (one column-major strip per block, so a warp reads it without
+//     bank conflicts and with one trip count);
+//   helpers (6 warps, blocks b mod 6): finish y_b - subtract the listed operands, polling
+//     the chunk's x in shared memory, then apply D_b^-1 held in registers;
+//   main (1 warp): x_b = y_b - W1_b x_b-1 - W2_b x_b-2 with the W tiles streamed into a
+//     shared-memory ring by bulk asynchronous copies (one lane of the last warp keeps the
+//     ring full)
+//     and the two previous blocks read from shared memory as broadcasts;
+//   every wait is bounded; a failed wait raises an error and poisons the rest of the chunk
+//     with NaN so that later chunks do not wait for it.
 //
-// The result differs from plain substitution only by rounding (the inverse is applied
-// instead of substituting inside the block); the relative residual stays at the 1e-16
-// level for diagonally dominant blocks.  Callers that need the sequential order use the
-// LCD_SOLVE_EXACT path of lcd_sptrsv_csr_syncfree instead.
+// The result differs from plain substitution only by rounding; the relative residual
+// stays at the 1e-16 level for diagonally dominant blocks.  Callers that need the
+// sequential order use the LCD_SOLVE_EXACT path of lcd_sptrsv_csr_syncfree instead.
 #include "common.cuh"
 
 namespace lcd {
 
-constexpr int kChainThreads = 256;
-constexpr int kChainRows = 1024;                       // rows per chunk
-constexpr int kChainRowsPerThread = kChainRows / kChainThreads;
+constexpr int kChainThreads = 256;                    // main warp, six helper warps, loader warp
+constexpr int kChainWorkers = 256;
+constexpr int kChainRows = 1024;                      // rows per chunk
+constexpr int kChainRowsPerThread = kChainRows / kChainWorkers;
 constexpr int kChainBlocks = kChainRows / 32;
+constexpr int kChainHelpers = 6;
+constexpr int kChainStages = 8;                       // ring of (W1, W2) tile pairs
+constexpr int kTileDoubles = 1024;
+constexpr int kBlockDoubles = 3 * kTileDoubles;       // per 32-row block: D^-1, W1, W2
+constexpr int kChainHalo = 64;                        // the two blocks before the chunk
+constexpr int kChainGate = 3;                         // chunks ahead at which pending operands are polled
+constexpr int kStatusDone = 6;                        // status word: chunks finished
+constexpr unsigned kFullMask = 0xffffffffu;
 
-// ---- numeric preparation: invert the 32 x 32 diagonal blocks ----------------------
-constexpr int kInvWarps = 2;
-
-__global__ void __launch_bounds__(kInvWarps * 32)
-chain_block_inverse_kernel(const CsrSolveParams p, double *__restrict__ minv, int n_blocks) {
-    __shared__ double D[kInvWarps][32][33];
-    __shared__ double M[kInvWarps][32][33];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int blk = blockIdx.x * kInvWarps + warp;
-    if (blk >= n_blocks) return;
+// ---- numeric preparation ------------------------------------------------------------
+// One warp per 32-row block walks the block's rows in order.  Row r of D^-1, W1 and W2
+// all satisfy the same recurrence  row_r = (rhs_r - sum_{k<r} D[r][k] row_k) / D[r][r]
+// with right-hand sides e_r, L_b,b-1[r][:] and L_b,b-2[r][:]; lane c carries column c of
+// the three rows.  Only the stored entries are visited: a row's entries are loaded 32 at
+// a time, the ones that matter are found with a ballot and handed round with shuffles.
+__global__ void __launch_bounds__(32)
+chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_blocks) {
+    __shared__ double M[32][33];
+    __shared__ double W1[32][33];
+    __shared__ double W2[32][33];
+    const int lane = threadIdx.x;
+    const int gb = blockIdx.x;
+    if (gb >= n_blocks) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
-    const int base = blk * 32;
-    const int task = base + lane;
-    for (int k = 0; k < 32; ++k) { D[warp][lane][k] = 0.0; M[warp][lane][k] = 0.0; }
-    double diag = 1.0;  // rows past the end form an identity block
-    if (task < p.n) {
-        const int r = upper ? p.n - 1 - task : task;
-        int lo = 0, hi = 0, d = -1;
-        if (csr_row_range(p, r, lo, hi, d)) {
-            if (d >= 0) diag = __ldg(p.Ax + d);
-            for (int j = lo; j < hi; ++j) {
-                const int c = __ldg(p.Ai + j);
-                if ((unsigned)c >= (unsigned)p.n) continue;
-                const int tc = upper ? p.n - 1 - c : c;
-                if (tc >= base && tc < task) D[warp][lane][tc - base] += __ldg(p.Ax + j);
+    const int base = gb * 32;
+    int lo = 0, hi = 0;
+    double diag = 1.0;  // rows past the end, and rows with bad pointers, act as identity rows
+    {
+        const int task = base + lane;
+        if (task < p.n) {
+            const int r = upper ? p.n - 1 - task : task;
+            int d = -1;
+            if (csr_row_range(p, r, lo, hi, d)) {
+                if (d >= 0) diag = __ldg(p.Ax + d);
+            } else {
+                lo = hi = 0;
             }
         }
     }
-    D[warp][lane][lane] = diag;
-    __syncwarp();
-    // lane c solves D m = e_c by forward substitution: column c of the inverse
-    const int c = lane;
-    for (int r = c; r < 32; ++r) {
-        double s = (r == c) ? 1.0 : 0.0;
-        for (int k = c; k < r; ++k) s = fma(-D[warp][r][k], M[warp][k][c], s);
-        M[warp][r][c] = s / D[warp][r][r];
+    // the first 32 entries of the next row are requested while the current row is processed
+    int nlo = __shfl_sync(kFullMask, lo, 0), nhi = __shfl_sync(kFullMask, hi, 0);
+    int pc = -1;
+    double pa = 0.0;
+    if (nlo + lane < nhi) { pc = __ldg(p.Ai + nlo + lane); pa = __ldg(p.Ax + nlo + lane); }
+    for (int r = 0; r < 32; ++r) {
+        const int rlo = nlo, rhi = nhi;
+        int cc = pc;
+        double ca = pa;
+        if (r + 1 < 32) {
+            nlo = __shfl_sync(kFullMask, lo, r + 1);
+            nhi = __shfl_sync(kFullMask, hi, r + 1);
+            pc = -1;
+            pa = 0.0;
+            if (nlo + lane < nhi) { pc = __ldg(p.Ai + nlo + lane); pa = __ldg(p.Ax + nlo + lane); }
+        }
+        const double d = __shfl_sync(kFullMask, diag, r);
+        double accM = lane == r ? 1.0 : 0.0, acc1 = 0.0, acc2 = 0.0;
+        for (int j0 = rlo; j0 < rhi; j0 += 32) {
+            if (j0 != rlo) {
+                cc = -1;
+                ca = 0.0;
+                if (j0 + lane < rhi) { cc = __ldg(p.Ai + j0 + lane); ca = __ldg(p.Ax + j0 + lane); }
+            }
+            // kind 1: two blocks back, 2: the block before, 3: this block (before row r)
+            int kind = 0, col = 0;
+            if ((unsigned)cc < (unsigned)p.n) {
+                const int tc = upper ? p.n - 1 - cc : cc;
+                const int off = tc - (base - 64);
+                if (off >= 0 && tc < base + r) { kind = 1 + (off >> 5); col = off & 31; }
+            }
+            unsigned todo = __ballot_sync(kFullMask, kind != 0);
+            while (todo) {
+                const int src = __ffs(todo) - 1;
+                todo &= todo - 1;
+                const int kd = __shfl_sync(kFullMask, kind, src);
+                const int c = __shfl_sync(kFullMask, col, src);
+                const double av = __shfl_sync(kFullMask, ca, src);
+                if (kd == 3) {
+                    accM = fma(-av, M[c][lane], accM);
+                    acc1 = fma(-av, W1[c][lane], acc1);
+                    acc2 = fma(-av, W2[c][lane], acc2);
+                } else if (lane == c) {
+                    if (kd == 2) acc1 += av; else acc2 += av;
+                }
+            }
+        }
+        M[r][lane] = accM / d;
+        W1[r][lane] = acc1 / d;
+        W2[r][lane] = acc2 / d;
+        __syncwarp();
     }
-    __syncwarp();
-    // element (r, k) at k * 32 + r: the solver's lane r reads column after column coalesced
-    double *out = minv + (long long)blk * 1024;
-    for (int k = 0; k < 32; ++k) out[k * 32 + lane] = M[warp][lane][k];
+    // D^-1: element (r, k) at k * 32 + r (a helper lane r loads its row coalesced);
+    // W tiles: elements (r, 2q) and (r, 2q + 1) side by side at (q * 32 + r) * 2, so that the
+    // main warp's lane r reads its row with 16-byte loads that do not conflict
+    double *out = ws + (long long)gb * kBlockDoubles;
+    for (int k = 0; k < 32; ++k) out[k * 32 + lane] = M[lane][k];
+    double2 *o1 = reinterpret_cast<double2 *>(out + kTileDoubles);
+    double2 *o2 = reinterpret_cast<double2 *>(out + 2 * kTileDoubles);
+    for (int q = 0; q < 16; ++q) {
+        o1[q * 32 + lane] = make_double2(W1[lane][2 * q], W1[lane][2 * q + 1]);
+        o2[q * 32 + lane] = make_double2(W2[lane][2 * q], W2[lane][2 * q + 1]);
+    }
 }
 
-// ---- the solve -------------------------------------------------------------------
-struct ChainParams {
-    CsrSolveParams m;
-    const double *__restrict__ minv;
-    int cap;  // capacity of the compact operand list (entries)
-};
-
-__device__ __forceinline__ int before_fill(const int *eptr, int local) { return eptr[local]; }
-
+// ---- asynchronous-copy plumbing --------------------------------------------------------
+__device__ __forceinline__ unsigned smem_addr(const void *ptr) {
+    return (unsigned)__cvta_generic_to_shared(ptr);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned parity) {
+    unsigned done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// global -> shared bulk copy (source, destination and size are multiples of 16 bytes);
+// completion is signalled on the mbarrier as transferred bytes
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes,
+                                          unsigned long long *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
 __device__ __forceinline__ void chain_prefetch_l2(const void *ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
+__device__ __forceinline__ void workers_barrier() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kChainWorkers) : "memory");
+}
+
+// A wait of a whole warp: every lane polls its own condition, but the loop is left by all
+// lanes together (a vote decides).  Lanes that left a polling loop one by one would run the
+// code after it as separately scheduled groups, and every warp-wide shuffle there would
+// cost a re-synchronisation of the groups (measured: 15,000 cycles for one 32-step mat-vec).
+template <class Ready>
+__device__ __forceinline__ bool warp_wait(Ready ready, Deadline &dl, volatile int *failed_flag,
+                                          int32_t *status, int node) {
+    unsigned polls = 0;
+    for (;;) {
+        if (__all_sync(kFullMask, ready())) return true;
+        if ((++polls & 15u) == 0 &&
+            __any_sync(kFullMask, *failed_flag != 0 || dl.tick(status, node)))
+            return false;
+    }
+}
+
+// ---- the solve ---------------------------------------------------------------------------
+struct ChainParams {
+    CsrSolveParams m;
+    const double *__restrict__ ws;
+    int cap;  // capacity of the in-chunk operand list (entries)
+};
 
 __global__ void __launch_bounds__(kChainThreads, 1)
 csr_chain_kernel(const ChainParams q) {
     const CsrSolveParams &p = q.m;
-    extern __shared__ __align__(16) unsigned char chain_smem[];
-    double *sx = reinterpret_cast<double *>(chain_smem);      // x of the chunk
-    double *sacc = sx + kChainRows + 2;                        // partial sums after phase A (sx has a zero slot)
-    double *eval = sacc + kChainRows;                          // compact operands: values
-    int *ecol = reinterpret_cast<int *>(eval + q.cap);         // ... and chunk-local columns
-    int *eptr = ecol + q.cap;                                  // kChainRows + 1 offsets
+    extern __shared__ __align__(128) unsigned char chain_smem[];
+    double *ring = reinterpret_cast<double *>(chain_smem);      // kChainStages x (W1, W2)
+    double *sxh = ring + kChainStages * 2 * kTileDoubles;        // halo, chunk, zero slot
+    double *sx = sxh + kChainHalo;                               // x of the chunk (chunk-local index)
+    double *sacc = sx + kChainRows + 2;                          // partial sums after phase A
+    double *sy = sacc + kChainRows;                              // y_b, produced by the helpers
+    double *eval = sy + kChainRows;                              // in-chunk operands: values
+    int *ecol = reinterpret_cast<int *>(eval + q.cap);           // ... and chunk-local columns
+    __shared__ unsigned long long s_full[kChainStages];
+    __shared__ unsigned long long s_empty[kChainStages];
     __shared__ int s_chunk;
     __shared__ int s_failed;
-    __shared__ int s_warp_sums[kChainThreads / 32 + 1];
+    __shared__ int s_width[kChainBlocks];
+    __shared__ int s_bptr[kChainBlocks + 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    volatile int *failed_flag = &s_failed;
     if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; }
+    if (tid == kChainThreads - 32) {
+        for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 1); }
+        mbar_init_fence();
+    }
     __syncthreads();
-    const int row0 = s_chunk * kChainRows;
+    const int chunk = s_chunk;
+    const int row0 = chunk * kChainRows;
     const int rows_here = min(kChainRows, p.n - row0);
     if (rows_here <= 0) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
-    // pull this chunk's inverse blocks towards L2 while phase A waits on earlier chunks
-    {
-        const char *src = reinterpret_cast<const char *>(q.minv + (long long)(row0 / 32) * 1024);
-        const long long bytes = (long long)((rows_here + 31) / 32) * 1024 * 8;
-        for (long long off = (long long)tid * 128; off < bytes; off += (long long)kChainThreads * 128)
-            chain_prefetch_l2(src + off);
-    }
+    const int nblk = (rows_here + 31) / 32;
+    const double *wsc = q.ws + (long long)(row0 / 32) * kBlockDoubles;
+    constexpr unsigned kTileBytes = 2 * kTileDoubles * sizeof(double);
+    Deadline dl;
+    dl.start(p.budget_ns);
 
-    // ---- phase A: thread t owns rows t, t + 256, t + 512, t + 768 of the chunk ---------
-    // A1 (pattern only, nothing to wait for): count the operands that come from earlier
-    // 32-row blocks of the chunk, lay the compact list out (every row padded to a multiple
-    // of four entries that point at a zero slot) and fill it.
+    // the first tiles of the ring are requested right away (nothing to wait for)
+    int issued = 0;
+    if (tid == kChainThreads - 32)
+        for (; issued < min(kChainStages, nblk); ++issued) {
+            mbar_expect_tx(&s_full[issued], kTileBytes);
+            bulk_load(ring + issued * 2 * kTileDoubles,
+                      wsc + (long long)issued * kBlockDoubles + kTileDoubles, kTileBytes,
+                      &s_full[issued]);
+        }
+
+    // ---- phase A: thread t owns rows t, t + 256, t + 512, t + 768 of the chunk ------------
+    // (the 32 lanes of a warp hold exactly the 32 rows of block warp + 8 k for each k)
+    // A1 (pattern only, nothing to wait for): operands in the chunk that lie three or more
+    // blocks back are counted, the per-block strips are laid out and filled.
     int lo_[kChainRowsPerThread], hi_[kChainRowsPerThread], cnt_[kChainRowsPerThread];
     bool failed = false;
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int local = tid + k * kChainThreads;
+        const int local = tid + k * kChainWorkers;
         lo_[k] = hi_[k] = cnt_[k] = 0;
-        if (local >= rows_here) continue;
-        const int task = row0 + local;
-        const int r = upper ? p.n - 1 - task : task;
-        const int base = local & ~31;  // first row of this row's 32-block, chunk-local
-        int lo = 0, hi = 0, d = -1;
-        if (!csr_row_range(p, r, lo, hi, d)) {
-            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
-                                                               : LCD_ERR_BAD_POINTERS, r);
-            failed = true;
-            continue;
-        }
-        lo_[k] = lo;
-        hi_[k] = hi;
-        int externals = 0;
-        for (int j = lo; j < hi; ++j) {
-            const int c = __ldg(p.Ai + j);
-            const int tc = ((unsigned)c < (unsigned)p.n) ? (upper ? p.n - 1 - c : c) : task;
-            if (tc >= task) {  // not strictly before this row (or out of range)
-                raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+        sx[local] = __longlong_as_double((long long)kPendingBits);
+        sy[local] = __longlong_as_double((long long)kPendingBits);
+        if (local < rows_here) {
+            const int task = row0 + local;
+            const int r = upper ? p.n - 1 - task : task;
+            const int near0 = (local & ~31) - 64;  // chunk-local start of the two blocks before
+            int lo = 0, hi = 0, d = -1;
+            if (!csr_row_range(p, r, lo, hi, d)) {
+                raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                                   : LCD_ERR_BAD_POINTERS, r);
                 failed = true;
-                break;
+            } else {
+                lo_[k] = lo;
+                hi_[k] = hi;
+                int listed = 0;
+                for (int j = lo; j < hi; ++j) {
+                    const int c = __ldg(p.Ai + j);
+                    const int tc = ((unsigned)c < (unsigned)p.n) ? (upper ? p.n - 1 - c : c) : task;
+                    if (tc >= task) {  // not strictly before this row (or out of range)
+                        raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                        failed = true;
+                        hi_[k] = lo;   // the row is not touched again
+                        break;
+                    }
+                    const int cl = tc - row0;
+                    if (cl >= 0 && cl < near0) ++listed;
+                }
+                cnt_[k] = failed ? 0 : listed;
             }
-            const int cl = tc - row0;
-            if (cl >= 0 && cl < base) ++externals;
         }
-        cnt_[k] = (externals + 3) & ~3;
+        const int width = (__reduce_max_sync(kFullMask, cnt_[k]) + 1) & ~1;
+        if (lane == 0) s_width[warp + 8 * k] = width;
     }
-    // exclusive scan of the padded counts in row order (rows are interleaved over threads,
-    // so the four row groups are scanned one after another)
-    int running = 0;
-#pragma unroll
-    for (int k = 0; k < kChainRowsPerThread; ++k) {
-        int incl = cnt_[k];
+    if (tid == 0) sx[kChainRows] = 0.0;  // padding entries of the strips point here
+    workers_barrier();
+    if (warp == 0) {
+        int incl = s_width[lane] * 32;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, incl, off);
+            const int t = __shfl_up_sync(kFullMask, incl, off);
             if (lane >= off) incl += t;
         }
-        __syncthreads();
-        if (lane == 31) s_warp_sums[warp] = incl;
-        __syncthreads();
-        int before = running;
-        for (int w = 0; w < warp; ++w) before += s_warp_sums[w];
-        int total = 0;
-        for (int w = 0; w < kChainThreads / 32; ++w) total += s_warp_sums[w];
-        eptr[tid + k * kChainThreads] = before + incl - cnt_[k];
-        running += total;
+        s_bptr[lane + 1] = incl;
+        if (lane == 0) s_bptr[0] = 0;
     }
-    if (tid == 0) { eptr[kChainRows] = running; sx[kChainRows] = 0.0; }  // zero slot for padding
-    const bool overflow = running > q.cap;  // block-uniform
+    workers_barrier();
+    const bool overflow = s_bptr[kChainBlocks] > q.cap;  // block-uniform
     if (!overflow) {
 #pragma unroll
         for (int k = 0; k < kChainRowsPerThread; ++k) {
-            const int local = tid + k * kChainThreads;
-            if (local >= rows_here || cnt_[k] == 0) continue;
-            const int task = row0 + local, base = local & ~31;
-            int pos = before_fill(eptr, local);
-            const int pos_end = pos + cnt_[k];
-            for (int j = lo_[k]; j < hi_[k]; ++j) {
-                const int c = __ldg(p.Ai + j);
-                if ((unsigned)c >= (unsigned)p.n) continue;
-                const int cl = (upper ? p.n - 1 - c : c) - row0;
-                if (cl >= 0 && cl < base && cl + row0 < task) {
-                    ecol[pos] = cl;
-                    eval[pos] = __ldg(p.Ax + j);
-                    ++pos;
+            const int local = tid + k * kChainWorkers;
+            const int blk = warp + 8 * k;
+            const int width = s_width[blk];
+            if (width == 0) continue;
+            const int near0 = (local & ~31) - 64;
+            int pos = s_bptr[blk] + lane;
+            const int pos_end = pos + width * 32;
+            if (local < rows_here && cnt_[k] > 0)
+                for (int j = lo_[k]; j < hi_[k]; ++j) {
+                    const int c = __ldg(p.Ai + j);
+                    const int cl = (upper ? p.n - 1 - c : c) - row0;
+                    if (cl >= 0 && cl < near0) {
+                        ecol[pos] = cl;
+                        eval[pos] = __ldg(p.Ax + j);
+                        pos += 32;
+                    }
                 }
-            }
-            for (; pos < pos_end; ++pos) { ecol[pos] = kChainRows; eval[pos] = 0.0; }
+            for (; pos < pos_end; pos += 32) { ecol[pos] = kChainRows; eval[pos] = 0.0; }
         }
     }
-    // A2: contributions of rows before the chunk (they belong to earlier tickets, so a
-    // bounded spin is safe).  First every operand that is already there is consumed without
-    // waiting; operands still pending are remembered in a bit mask and revisited afterwards,
-    // so that when the previous chunk finishes only those few remain to be fetched.
-    Deadline dl;
-    dl.start(p.budget_ns);
+    // A2: contributions of rows before the chunk that are not covered by the W tiles (they
+    // belong to earlier tickets, so a bounded spin is safe).  First every operand that is
+    // already there is consumed without waiting; operands still pending are remembered in a
+    // bit mask and revisited afterwards, so that when the previous chunks finish only those
+    // few remain to be fetched.
     double acc_[kChainRowsPerThread];
     unsigned long long pend_[kChainRowsPerThread];
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int local = tid + k * kChainThreads;
+        const int local = tid + k * kChainWorkers;
         acc_[k] = 0.0;
         pend_[k] = 0ull;
         if (local >= rows_here || failed) continue;
         const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+        // tasks before far_end are fetched here, the rest is covered by the strips and tiles
+        const int far_end = min(row0, row0 + (local & ~31) - 64);
         double acc = __ldg(p.b + r);
         for (int j = lo_[k]; j < hi_[k] && !failed; ++j) {
             const int c = __ldg(p.Ai + j);
             const int tc = upper ? p.n - 1 - c : c;
-            if (tc >= row0) continue;  // this chunk: compact list or inverse block
+            if (tc >= far_end) continue;
             double xv = ld_relaxed_f64(p.x + c);
             if (is_pending(xv)) {
                 if (j - lo_[k] < 64) { pend_[k] |= 1ull << (j - lo_[k]); continue; }
@@ -227,112 +372,285 @@ csr_chain_kernel(const ChainParams q) {
         }
         acc_[k] = acc;
     }
-#pragma unroll
-    for (int k = kChainRowsPerThread - 1; k >= 0; --k) {
-        const int local = tid + k * kChainThreads;
-        if (local >= rows_here) continue;
-        const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-        double acc = acc_[k];
-        unsigned long long mask = pend_[k];
-        while (mask && !failed) {
-            const int j = lo_[k] + __ffsll((long long)mask) - 1;
-            mask &= mask - 1;
-            const int c = __ldg(p.Ai + j);
-            double xv;
-            while (is_pending(xv = ld_relaxed_f64(p.x + c)))
-                if (dl.tick(p.status, r)) { failed = true; break; }
-            if (!failed) acc = fma(-__ldg(p.Ax + j), xv, acc);
+    // Hundreds of resident chunks spinning on operands that are many chunks away would only
+    // congest L2 for the few chunks whose turn it is: the chunk sleeps until its turn is near,
+    // then sweeps over what is still pending, four loads in flight per thread.
+    if (tid == 0) {
+        while (ld_relaxed_s32(&p.status[kStatusDone]) < chunk - kChainGate) {
+            __nanosleep(1000);
+            if (dl.tick(p.status, row0)) break;
         }
-        sacc[local] = acc;
     }
-    if (failed) s_failed = 1;
-    __syncthreads();
-    if (tid >= 32) return;
-
-    // ---- phase B: warp 0 walks the chunk, one 32-row block per step ----------------------
-    if (p.trace && lane == 0) p.trace[(long long)p.n + row0] = clock64();
-    volatile double *sxv = sx;
-    const bool chunk_failed = s_failed != 0;
-    const double nanv = __longlong_as_double(kCanonicalNaN);
-    const int n_blocks_here = (rows_here + 31) / 32;
-    const double *mbase = q.minv + (long long)(row0 / 32) * 1024 + lane;
-    double m[32];
+    workers_barrier();
+    {
+        // the chunk's tiles are pulled towards L2 now, shortly before its turn (all resident
+        // chunks doing so at launch would only evict one another's tiles)
+        const char *src = reinterpret_cast<const char *>(wsc);
+        const long long bytes = (long long)nblk * kBlockDoubles * 8;
+        for (long long off = (long long)tid * 128; off < bytes; off += (long long)kChainThreads * 128)
+            chain_prefetch_l2(src + off);
+    }
+    while (!failed) {
+        bool any = false;
 #pragma unroll
-    for (int k = 0; k < 32; ++k) m[k] = __ldg(mbase + k * 32);
-    for (int blk = 0; blk < n_blocks_here; ++blk) {
-        const int base = blk * 32;
-        const int local = base + lane;
-        const bool active = local < rows_here;
-        const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-        // the next block's inverse is requested now and consumed one step later
-        double mnext[32];
-        const bool more = blk + 1 < n_blocks_here;
+        for (int k = kChainRowsPerThread - 1; k >= 0; --k) {
+            unsigned long long mask = pend_[k];
+            if (!mask) continue;
+            double acc = acc_[k];
+            unsigned long long left = mask;
+            while (left) {
+                int jq[4];
+                double xq[4];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) mnext[k] = more ? __ldg(mbase + (long long)(blk + 1) * 1024 + k * 32) : 0.0;
-        double acc = active ? sacc[local] : 0.0;
-        if (chunk_failed) {
-            if (active) { sxv[local] = nanv; st_relaxed_f64(p.x + r, nanv); }
-            __syncwarp();
-            continue;
-        }
-        if (active) {
-            if (!overflow) {
-                // every row's list is a multiple of four entries (padding reads a zero slot)
-                int e = eptr[local];
-                const int e_end = eptr[local + 1];
-                double acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
-                for (; e < e_end; e += 4) {
-                    const int c0 = ecol[e], c1 = ecol[e + 1], c2 = ecol[e + 2], c3 = ecol[e + 3];
-                    const double a0 = eval[e], a1 = eval[e + 1], a2 = eval[e + 2], a3 = eval[e + 3];
-                    acc = fma(-a0, sxv[c0], acc);
-                    acc1 = fma(-a1, sxv[c1], acc1);
-                    acc2 = fma(-a2, sxv[c2], acc2);
-                    acc3 = fma(-a3, sxv[c3], acc3);
+                for (int u = 0; u < 4; ++u) {
+                    jq[u] = -1;
+                    if (left) { jq[u] = lo_[k] + __ffsll((long long)left) - 1; left &= left - 1; }
                 }
-                acc += (acc1 + acc2) + acc3;
-            } else {
-                // the compact list did not fit: read the operands from the matrix again
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    xq[u] = jq[u] >= 0 ? ld_relaxed_f64(p.x + __ldg(p.Ai + jq[u])) : 0.0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (jq[u] >= 0 && !is_pending(xq[u])) {
+                        acc = fma(-__ldg(p.Ax + jq[u]), xq[u], acc);
+                        mask &= ~(1ull << (jq[u] - lo_[k]));
+                    }
+            }
+            acc_[k] = acc;
+            pend_[k] = mask;
+            any |= mask != 0;
+        }
+        if (!any) break;
+        if (dl.tick(p.status, row0 + tid)) { failed = true; break; }
+        __nanosleep(100);
+    }
+#pragma unroll
+    for (int k = 0; k < kChainRowsPerThread; ++k) {
+        const int local = tid + k * kChainWorkers;
+        if (local < rows_here) sacc[local] = acc_[k];
+    }
+    if (failed) *failed_flag = 1;
+    workers_barrier();
+    volatile double *sxv = sx;
+    volatile double *syv = sy;
+
+    if (warp == kChainThreads / 32 - 1) {
+        // ---- loader warp (one lane): keeps the ring of W tiles full -------------------------
+        if (lane != 0) return;
+        bool ok = true;
+        for (int b = kChainStages; b < nblk && ok; ++b) {
+            const int s = b % kChainStages;
+            const unsigned parity = ((b / kChainStages) - 1) & 1;
+            while (!mbar_try_wait(&s_empty[s], parity))
+                if (*failed_flag || dl.tick(p.status, row0)) { ok = false; break; }
+            if (!ok) break;
+            mbar_expect_tx(&s_full[s], kTileBytes);
+            bulk_load(ring + s * 2 * kTileDoubles, wsc + (long long)b * kBlockDoubles + kTileDoubles,
+                      kTileBytes, &s_full[s]);
+            issued = b + 1;
+        }
+        // no copy may still be in flight when the block's shared memory is released
+        const unsigned long long drain_end = global_timer() + p.budget_ns;
+        for (int b = max(0, issued - kChainStages); b < issued; ++b) {
+            unsigned spins = 0;
+            while (!mbar_try_wait(&s_full[b % kChainStages], (b / kChainStages) & 1))
+                if ((++spins & 255u) == 0 && global_timer() > drain_end) break;
+        }
+        return;
+    }
+
+    if (warp == 0) {
+        // ---- main warp ---------------------------------------------------------------------
+        if (p.trace && lane == 0) p.trace[2ll * p.n + chunk] = clock64();
+        const double nanv = __longlong_as_double(kCanonicalNaN);
+        bool dead = *failed_flag != 0;
+        // the two blocks before the chunk
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int t = row0 - kChainHalo + h * 32 + lane;
+            double v = 0.0;
+            if (row0 > 0 && !dead) {   // (a chunk after the first has both blocks before it)
+                const int r = upper ? p.n - 1 - t : t;
+                dead = !warp_wait([&] { return !is_pending(v = ld_relaxed_f64(p.x + r)); }, dl,
+                                  failed_flag, p.status, r);
+            }
+            sxh[h * 32 + lane] = v;
+        }
+        __syncwarp();
+        // The W2 half of a tile multiplies the block two back, which is known one step
+        // early: step b computes x_b = y_b + z_b - W1_b x_b-1 and, from the same broadcast
+        // of x_b-1, z_b+1 = -W2_b+1 x_b-1 for the next step.
+        const double2 *ring2 = reinterpret_cast<const double2 *>(ring);
+        double z = 0.0;
+        if (!dead)
+            dead = !warp_wait([&] { return mbar_try_wait(&s_full[0], 0); }, dl, failed_flag,
+                              p.status, row0);
+        if (!dead) {
+            const double2 *w2 = ring2 + kTileDoubles / 2 + lane;
+            const double2 *xb = reinterpret_cast<const double2 *>(sxh);
+            double c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
+#pragma unroll
+            for (int qd = 0; qd < 16; qd += 2) {
+                const double2 u0 = w2[qd * 32], v0 = xb[qd];
+                const double2 u1 = w2[(qd + 1) * 32], v1 = xb[qd + 1];
+                c0 = fma(-u0.x, v0.x, c0);
+                c1 = fma(-u0.y, v0.y, c1);
+                c2 = fma(-u1.x, v1.x, c2);
+                c3 = fma(-u1.y, v1.y, c3);
+            }
+            z = (c0 + c1) + (c2 + c3);
+        }
+        double ynext = syv[lane];
+        int b = 0;
+        for (; b < nblk; ++b) {
+            const int base = b * 32, local = base + lane;
+            const bool active = local < rows_here;
+            const bool more = b + 1 < nblk;
+            const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+            const int s = b % kChainStages, sn = (b + 1) % kChainStages;
+            const long long t0_ = clock64();
+            if (!dead && more)
+                dead = !warp_wait([&] { return mbar_try_wait(&s_full[sn], ((b + 1) / kChainStages) & 1); },
+                                  dl, failed_flag, p.status, row0 + base);
+            const long long t1_ = clock64();
+            double y = ynext;
+            if (!dead && __any_sync(kFullMask, is_pending(y)))
+                dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
+                                  p.status, row0 + base);
+            if (dead) break;
+            const long long t2_ = clock64();
+            if (more) ynext = syv[local + 32];
+            const double2 *xa = reinterpret_cast<const double2 *>(sx + base - 32);
+            double2 v[16];
+#pragma unroll
+            for (int qd = 0; qd < 16; ++qd) v[qd] = xa[qd];
+            const double2 *w1 = ring2 + s * kTileDoubles + lane;
+            const double2 *w2 = ring2 + sn * kTileDoubles + kTileDoubles / 2 + lane;
+            double a0 = y, a1 = z, a2 = 0.0, a3 = 0.0, c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
+#pragma unroll
+            for (int qd = 0; qd < 16; qd += 2) {
+                const double2 u0 = w1[qd * 32], u1 = w1[(qd + 1) * 32];
+                a0 = fma(-u0.x, v[qd].x, a0);
+                a1 = fma(-u0.y, v[qd].y, a1);
+                a2 = fma(-u1.x, v[qd + 1].x, a2);
+                a3 = fma(-u1.y, v[qd + 1].y, a3);
+            }
+            if (more) {
+#pragma unroll
+                for (int qd = 0; qd < 16; qd += 2) {
+                    const double2 u0 = w2[qd * 32], u1 = w2[(qd + 1) * 32];
+                    c0 = fma(-u0.x, v[qd].x, c0);
+                    c1 = fma(-u0.y, v[qd].y, c1);
+                    c2 = fma(-u1.x, v[qd + 1].x, c2);
+                    c3 = fma(-u1.y, v[qd + 1].y, c3);
+                }
+            }
+            const double val = publishable((a0 + a1) + (a2 + a3));
+            z = (c0 + c1) + (c2 + c3);
+            sxv[local] = active ? val : 0.0;
+            if (active) {
+                st_relaxed_f64(p.x + r, val);
+                if (p.trace) p.trace[row0 + local] = lane == 0 ? t0_ : lane == 1 ? t1_ : lane == 2 ? t2_ : clock64();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[s]);
+        }
+        if (dead) {
+            // poison what is left of the chunk: later chunks must not wait for it
+            if (lane == 0) *failed_flag = 1;
+            for (int local = b * 32 + lane; local < rows_here; local += 32) {
+                const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+                sxv[local] = nanv;
+                st_relaxed_f64(p.x + r, nanv);
+            }
+        }
+        if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
+        return;
+    }
+
+    // ---- helper warps: y_b for blocks b = warp - 1, warp - 1 + 6, ... ----------------------
+    {
+        int b = warp - 1;
+        if (b >= nblk) return;
+        const double *mbase = wsc + lane;
+        double m[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) m[k] = __ldg(mbase + (long long)b * kBlockDoubles + k * 32);
+        for (; b < nblk; b += kChainHelpers) {
+            const int base = b * 32, local = base + lane;
+            const bool active = local < rows_here;
+            const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+            // this warp's next inverse block is requested now and consumed one step later
+            double mnext[32];
+            const bool more = b + kChainHelpers < nblk;
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+                mnext[k] = more ? __ldg(mbase + (long long)(b + kChainHelpers) * kBlockDoubles + k * 32) : 0.0;
+            const long long h0_ = clock64();
+            double t0 = active ? sacc[local] : 0.0, t1 = 0.0;
+            bool bad = *failed_flag != 0;
+            if (!overflow) {
+                const int width = s_width[b];
+                int pos = s_bptr[b] + lane;
+                for (int j = 0; j < width && !bad; j += 2, pos += 64) {
+                    const int c0 = ecol[pos], c1 = ecol[pos + 32];
+                    const double e0 = eval[pos], e1 = eval[pos + 32];
+                    double x0 = 0.0, x1 = 0.0;
+                    bad = !warp_wait([&] {
+                        x0 = sxv[c0];
+                        x1 = sxv[c1];
+                        return !is_pending(x0) && !is_pending(x1);
+                    }, dl, failed_flag, p.status, row0 + base);
+                    t0 = fma(-e0, x0, t0);
+                    t1 = fma(-e1, x1, t1);
+                }
+            } else if (active) {
+                // the strips did not fit: read the operands from the matrix again
                 int lo = 0, hi = 0, d = -1;
                 csr_row_range(p, r, lo, hi, d);
-                for (int j = lo; j < hi; ++j) {
+                for (int j = lo; j < hi && !bad; ++j) {
                     const int c = __ldg(p.Ai + j);
                     if ((unsigned)c >= (unsigned)p.n) continue;
                     const int cl = (upper ? p.n - 1 - c : c) - row0;
-                    if (cl >= 0 && cl < base) acc = fma(-__ldg(p.Ax + j), sxv[cl], acc);
+                    if (cl < 0 || cl >= base - 64) continue;
+                    double xv = 0.0;
+                    while (is_pending(xv = sxv[cl]))
+                        if (*failed_flag || dl.tick(p.status, r)) { bad = true; break; }
+                    t0 = fma(-__ldg(p.Ax + j), xv, t0);
                 }
             }
-        }
-        // x_block = inverse block * acc_block: 32 independent shuffle / FMA pairs
-        double x0 = 0.0, x1 = 0.0, x2 = 0.0, x3 = 0.0;
+            __syncwarp();
+            if (__any_sync(kFullMask, bad)) {
+                if (lane == 0) *failed_flag = 1;
+                return;
+            }
+            const double t = t0 + t1;
+            const long long h1_ = clock64();
+            // y_block = inverse block * t_block: 32 independent shuffle / FMA pairs
+            double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
 #pragma unroll
-        for (int k = 0; k < 32; k += 4) {
-            x0 = fma(m[k + 0], __shfl_sync(0xffffffffu, acc, k + 0), x0);
-            x1 = fma(m[k + 1], __shfl_sync(0xffffffffu, acc, k + 1), x1);
-            x2 = fma(m[k + 2], __shfl_sync(0xffffffffu, acc, k + 2), x2);
-            x3 = fma(m[k + 3], __shfl_sync(0xffffffffu, acc, k + 3), x3);
-        }
-        if (active) {
-            const double val = publishable((x0 + x1) + (x2 + x3));
-            sxv[local] = val;
-            st_relaxed_f64(p.x + r, val);
-            if (p.trace) p.trace[row0 + local] = clock64();
-        }
-        __syncwarp();
+            for (int k = 0; k < 32; k += 4) {
+                y0 = fma(m[k + 0], __shfl_sync(kFullMask, t, k + 0), y0);
+                y1 = fma(m[k + 1], __shfl_sync(kFullMask, t, k + 1), y1);
+                y2 = fma(m[k + 2], __shfl_sync(kFullMask, t, k + 2), y2);
+                y3 = fma(m[k + 3], __shfl_sync(kFullMask, t, k + 3), y3);
+            }
+            syv[local] = publishable((y0 + y1) + (y2 + y3));
+            const long long h2_ = clock64();
 #pragma unroll
-        for (int k = 0; k < 32; ++k) m[k] = mnext[k];
+            for (int k = 0; k < 32; ++k) m[k] = mnext[k];
+            if (p.trace && active) p.trace[(long long)p.n + row0 + local] = lane == 0 ? h0_ : lane == 1 ? h1_ : lane == 2 ? h2_ : clock64();
+        }
     }
 }
 
-static size_t chain_smem_bytes(long long nnz, int n, int *cap_out) {
-    const size_t limit = 227 * 1024 - 512;
-    const size_t fixed = ((size_t)kChainRows * 2 + 2) * 8 + ((size_t)kChainRows + 2) * 4;
-    const double avg = n > 0 ? (double)nnz / n : 0.0;
-    long long cap = (long long)(avg * kChainRows * 0.75) + 4 * kChainRows;  // incl. padding
-    const long long max_cap = ((long long)limit - (long long)fixed) / 12;
-    if (cap > max_cap) cap = max_cap;
-    cap &= ~1ll;
+static size_t chain_smem_bytes(int *cap_out) {
+    const size_t limit = 227 * 1024 - 1024;  // static shared memory takes a few hundred bytes
+    const size_t fixed = (size_t)kChainStages * 2 * kTileDoubles * 8 +
+                         ((size_t)kChainHalo + kChainRows + 2 + 2 * kChainRows) * 8;
+    const size_t cap = ((limit - fixed) / 12) & ~(size_t)1;
     *cap_out = (int)cap;
-    return fixed + (size_t)cap * 12;
+    return fixed + cap * 12;
 }
 
 }  // namespace lcd
@@ -341,7 +659,7 @@ using namespace lcd;
 
 extern "C" int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes) {
     if (n < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
-    *bytes = ((int64_t)n + 31) / 32 * 1024 * 8 + 256;
+    *bytes = ((int64_t)n + 31) / 32 * kBlockDoubles * 8 + 256;
     return LCD_OK;
 }
 
@@ -355,7 +673,8 @@ static int chain_check(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t 
     int64_t need = 0;
     lcd_chain_workspace_bytes(n, &need);
     if (workspace_bytes < need) return LCD_ERR_WORKSPACE;
-    if (reinterpret_cast<uintptr_t>(workspace) & 7) return LCD_ERR_INVALID_ARGUMENT;
+    // the tiles are fetched with bulk copies, which need 16-byte aligned addresses
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return LCD_ERR_INVALID_ARGUMENT;
     return LCD_OK;
 }
 
@@ -367,8 +686,8 @@ extern "C" int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, cons
     const int n_blocks = (n + 31) / 32;
     CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, nullptr, nullptr, flags, 1, 1, nullptr,
                      0, nullptr, 0, n, nullptr, {nullptr}};
-    chain_block_inverse_kernel<<<(n_blocks + kInvWarps - 1) / kInvWarps, kInvWarps * 32, 0,
-                                 (cudaStream_t)stream>>>(p, static_cast<double *>(workspace), n_blocks);
+    chain_prepare_kernel<<<n_blocks, 32, 0, (cudaStream_t)stream>>>(p, static_cast<double *>(workspace),
+                                                                    n_blocks);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }
@@ -390,15 +709,11 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
         ChainParams q;
         q.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags & ~LCD_SOLVE_EXACT, 1, 1,
                              status_dev, timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
-        q.minv = static_cast<const double *>(workspace);
-        const size_t smem = chain_smem_bytes(nnz, n, &q.cap);
-        static bool configured = false;
-        if (!configured) {
-            LCD_CUDA_TRY(cudaFuncSetAttribute(csr_chain_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)(227 * 1024 - 512)));
-            configured = true;
-        }
+        q.ws = static_cast<const double *>(workspace);
+        const size_t smem = chain_smem_bytes(&q.cap);
+        // the attribute belongs to the current device's copy of the function
+        LCD_CUDA_TRY(cudaFuncSetAttribute(csr_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
         csr_chain_kernel<<<(n + kChainRows - 1) / kChainRows, kChainThreads, smem, st>>>(q);
         LCD_CUDA_TRY(cudaGetLastError());
     }

@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import ast
 from copy import deepcopy
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 
@@ -118,6 +118,7 @@ class CUDAPreparedArguments:
     values: dict
     host_values: dict
     lifted_variables: tuple
+    hints: dict = field(default_factory=dict)   # what the inspector learnt (rows, levels, ...)
 
     @property
     def launcher_arguments(self):
@@ -191,7 +192,11 @@ def evaluate_host_prelude(lowering, argument_values, function_globals=None):
 
 def execute_cuda_call(compiled_module, lowering, prepared_arguments, function_globals=None):
     """Launch prepared work and restore the original return semantics."""
-    compiled_module.launcher(*prepared_arguments.launcher_arguments)
+    launcher = compiled_module.launcher
+    if prepared_arguments.hints and getattr(launcher, "accepts_hints", False):
+        launcher(*prepared_arguments.launcher_arguments, _hints=prepared_arguments.hints)
+    else:
+        launcher(*prepared_arguments.launcher_arguments)
     cuda_module = compiled_module.namespace.get("cuda")
     if cuda_module is None or not hasattr(cuda_module, "synchronize"):
         raise CUDARuntimePreparationError(

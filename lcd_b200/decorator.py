@@ -129,6 +129,7 @@ def parallel(**kwargs):
             structure_names + pointer_array_names(function_props)
             + structural_argument_names(structural_lookups)))
         schedule_plans = {}
+        launch_caches = {}      # per plan: what a launcher keeps between calls (workspaces)
 
         def bind_arguments(args, call_kwargs):
             bound = signature.bind(*args, **call_kwargs)
@@ -205,10 +206,12 @@ def parallel(**kwargs):
                     flops_per_iteration=2, thread_trip_counts=trips,
                     # measured on B200: the ILU0 sync-free kernel pays about 8x the SpTRSV
                     # hand-off (acquire/release flags plus the row update before the release)
-                    sync_free_penalty=8.0 if operator == "ilu0_csr" else 1.0)
+                    sync_free_penalty=8.0 if operator == "ilu0_csr" else 1.0,
+                    chain_capable=operator == "sptrsv_csr")
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
-            return SchedulePlan(schedule=schedule, execution_data=data, features=features)
+            return SchedulePlan(schedule=schedule, execution_data=data, features=features,
+                                rows=dag.n, levels=dag.n_levels)
 
         def plan_for(values, structure):
             from . import ops
@@ -219,7 +222,7 @@ def parallel(**kwargs):
             if plan is None:
                 plan = create_schedule_plan(values, structure)
                 if len(schedule_plans) >= SCHEDULE_CACHE_SIZE:
-                    schedule_plans.pop(next(iter(schedule_plans)))
+                    launch_caches.pop(id(schedule_plans.pop(next(iter(schedule_plans)))), None)
                 schedule_plans[fingerprint] = plan
             return plan
 
@@ -255,6 +258,9 @@ def parallel(**kwargs):
                 lowering=lowering, argument_values=launch_values,
                 execution_data=_fresh_counters(plan.execution_data),
                 function_globals=function.__globals__, cuda_module=module.namespace["cuda"])
+            prepared.hints = {"rows": plan.rows, "levels": plan.levels,
+                              "arch": getattr(scheduler, "_arch_constants", None),
+                              "cache": launch_caches.setdefault(id(plan), {})}
             return lowering, module, prepared
 
         def prepare_cuda_call(*args, **call_kwargs):

@@ -8,6 +8,10 @@ closure that receives the same positional arguments (original parameters, lifted
 locals, lookup tables, executor arrays) and forwards the device pointers to one
 C-ABI entry point; level loops and barriers live inside the library.
 
+A sync-free CSR triangular solve whose levels are narrow (the inspector's row and level
+counts arrive as hints from the decorator) goes to the block-recurrence chain solver
+instead of the polling kernel.
+
 Executor arrays the native kernels do not need (successor lists, task tables and
 ticket counters of the row-form solver, which polls operands instead of counting)
 are accepted and ignored, so call sites written for the reference keep working.
@@ -20,6 +24,7 @@ import numpy as np
 from . import ops
 from .cuda_lowering import CUDALoweringError, PUSH_DEPENDENCE
 from .cuda_runtime import as_tensor
+from .scheduler import chain_solver_preferred
 
 # Launch policy of the wavefront entry point: the cooperative single-launch walk
 # unless the level count is small enough for per-level launches to be cheaper.
@@ -75,14 +80,33 @@ def bind(lowering):
         ptr_dev = torch.from_numpy(ptr_host).to(nodes.device)
         return nodes, ptr_dev, ptr_host
 
-    def sptrsv_csr(*args):
+    def chain_solve(Ap, Ai, Ax, b, x, cache):
+        # the block tiles depend on the values: they are rebuilt unless the value array is
+        # the one (same storage, same contents) they were built from
+        n = Ap.numel() - 1
+        workspace = cache.get("chain_workspace")
+        if workspace is None or workspace.device != Ax.device:
+            workspace = cache["chain_workspace"] = ops.chain_workspace(n, Ax.device)
+            cache.pop("chain_values", None)
+        stamp = (Ax.data_ptr(),) + ops.fingerprint(Ax.view(torch.int32))
+        if cache.get("chain_values") != stamp:
+            ops.chain_prepare(Ap, Ai, Ax, workspace, upper=lowering.upper)
+            cache["chain_values"] = stamp
+        ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
+
+    def sptrsv_csr(*args, _hints=None):
         v = split(args)
         Ap, Ai, Ax = matrix(v)
         b = as_tensor(v[roles["rhs"]], torch.float64)
         x = as_tensor(v[roles["out"]], torch.float64)
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
         if lowering.execution_mode == "sync_free":
-            ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper, lanes=lanes)
+            hints = _hints or {}
+            if chain_solver_preferred(hints.get("rows", 0), hints.get("levels", 0),
+                                      hints.get("arch")):
+                chain_solve(Ap, Ai, Ax, b, x, hints.setdefault("cache", {}))
+            else:
+                ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper, lanes=lanes)
         else:
             nodes, ptr_dev, ptr_host = wavefront_arrays(v)
             mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
@@ -128,6 +152,7 @@ def bind(lowering):
     if launcher is None:
         raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
     launcher.__name__ = lowering.launcher_name
+    launcher.accepts_hints = lowering.operator == "sptrsv_csr"
 
     def kernel(*args, **kwargs):
         raise CUDALoweringError(

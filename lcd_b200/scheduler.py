@@ -9,7 +9,8 @@ working, but replaces the cost model.  The reference estimates
 the critical path; here the decision is taken from the level structure the DAG
 build measured, with constants measured on B200:
 
-* sync-free:        levels * t_handoff (0.6 us) + rows * 1.1 ns
+* sync-free:        levels * t_handoff (0.6 us) + rows * 1.1 ns, or, for CSR triangular
+                    solves with narrow levels, rows * 7 ns (block-recurrence chain solver)
 * level-synchronous, levels that fit one block (<= 512 rows):
                     levels * (2.4 us + 13 ns * width)   (block-level barriers)
 * level-synchronous, wide levels:
@@ -63,6 +64,8 @@ class ArchConstants:
     wavefront_row_s: float = 0.5e-9     # streaming cost per row in wide levels
     handoff_s: float = 0.6e-6           # sync-free: one dependence hop on the critical chain
     syncfree_row_s: float = 1.1e-9      # sync-free: per-row cost when many rows are in flight
+    chain_row_s: float = 7.0e-9         # block-recurrence chain solver: per row, whatever the levels
+    chain_min_rows: int = 32768         # ... below this the preparation does not pay
     block_level_width: int = 512        # levels up to this width stay inside one block
 
 
@@ -86,6 +89,7 @@ class WorkloadFeatures:
     thread_loop_invocations: int = 0
     max_level_width: int = 0
     sync_free_penalty: float = 1.0   # operators whose sync-free kernel does more work per hop
+    chain_capable: bool = False      # the operator has a block-recurrence solver (CSR SpTRSV)
 
     @property
     def average_in_degree(self):
@@ -134,6 +138,8 @@ class SchedulePlan:
     schedule: Schedule
     execution_data: object
     features: WorkloadFeatures | None = None
+    rows: int = 0
+    levels: int = 0
 
 
 def normalize_execution_mode(execution_mode):
@@ -268,6 +274,9 @@ class AnalyticScheduler:
             # wide levels add a throughput term
             sync_s = (features.levels * arch.handoff_s + features.rows * arch.syncfree_row_s)
             sync_s *= features.sync_free_penalty
+            if features.chain_capable and chain_solver_preferred(features.rows, features.levels,
+                                                                 arch):
+                sync_s = features.rows * arch.chain_row_s
             if dependence_protocol == PULL_DEPENDENCE:
                 sync_s *= 0.99
             return CostEstimate(arch.launch_latency_s, sync_s, memory_s, compute_s)
@@ -281,6 +290,17 @@ class AnalyticScheduler:
 
     def schedule(self, features, space):
         return min(self.candidates(features, space), key=_schedule_rank)
+
+
+def chain_solver_preferred(rows, levels, arch=None):
+    """True when the block-recurrence chain solver is expected to beat the polling
+    sync-free kernel: its time grows with the rows only, the polling kernel's with the
+    levels.  The sync-free launcher of CSR triangular solves takes the same decision."""
+    arch = arch or FALLBACK_ARCH_CONSTANTS
+    if rows < arch.chain_min_rows or levels <= 0:
+        return False
+    polling_s = levels * arch.handoff_s + rows * arch.syncfree_row_s
+    return rows * arch.chain_row_s < polling_s
 
 
 def _schedule_rank(schedule):
@@ -323,7 +343,7 @@ def _array_nbytes(value):
 
 def extract_workload_features(dag, wavefront_list, argument_values, function_props=None,
                               flops_per_iteration=1, thread_trip_counts=None,
-                              sync_free_penalty=1.0):
+                              sync_free_penalty=1.0, chain_capable=False):
     """Features of one concrete input.  ``dag`` is either the reference's list of
     successor lists or a device DAG (then everything is read from its sizes)."""
     if hasattr(dag, "n_edges"):
@@ -361,7 +381,8 @@ def extract_workload_features(dag, wavefront_list, argument_values, function_pro
                             memory_bytes=int(sum(seen.values())),
                             thread_work_items=items, thread_loop_invocations=invocations,
                             max_level_width=int(widths.max()) if len(widths) else 0,
-                            sync_free_penalty=float(sync_free_penalty))
+                            sync_free_penalty=float(sync_free_penalty),
+                            chain_capable=bool(chain_capable))
 
 
 def _digest(value):

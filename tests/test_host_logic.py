@@ -158,6 +158,17 @@ def test_scheduler_decides_from_level_structure():
     # measured: 754,679 levels -> 480 ms sync-free, 1.83 s level-synchronous
     assert sched.estimate(narrow, "sync_free", 128, 1, 1, True).sync_s == pytest.approx(0.4575, rel=0.02)
     assert sched.estimate(narrow, "wavefront", 128, 1, 1, True).sync_s == pytest.approx(1.87, rel=0.05)
+    # a CSR triangular solve also has the block-recurrence chain solver, whose time follows the
+    # rows: it takes over the sync-free estimate for narrow levels, never for wide ones or
+    # small systems
+    chain = dataclasses.replace(narrow, chain_capable=True)
+    assert sched.estimate(chain, "sync_free", 128, 1, 1, True).sync_s == pytest.approx(
+        narrow.rows * arch.chain_row_s)
+    assert sched.schedule(chain, space).execution_mode == "sync_free"
+    assert sc.chain_solver_preferred(4_194_304, 755_000) and sc.chain_solver_preferred(65_536, 20_000, arch)
+    assert not sc.chain_solver_preferred(2_097_152, 382) and not sc.chain_solver_preferred(4_096, 4_096)
+    wide_chain = dataclasses.replace(wide, chain_capable=True)
+    assert sched.estimate(wide_chain, "sync_free", 128, 1, 1, True) == sched.estimate(wide, "sync_free", 128, 1, 1, True)
     f = sc.extract_workload_features([[1, 2], [2], []], [[0], [1], [2]], {"Ap": np.array([0, 1, 3, 6])},
                                      function_props={"Ap": ["monotonically_increasing"]},
                                      flops_per_iteration=2, thread_trip_counts=(0, 1, 2))
@@ -279,6 +290,17 @@ def test_runtime_prepare_and_execute_with_fake_backend():
     out = rt.execute_cuda_call(module, low, prepared, {"np": np})
     np.testing.assert_array_equal(out, [1.0, 1.0])
     assert len(calls) == 1 and fake.syncs == 1
+    # what the inspector learnt travels as a keyword to launchers that ask for it
+    seen = {}
+
+    def hinted(*args, _hints=None):
+        seen.update(_hints)
+
+    hinted.accepts_hints = True
+    prepared.hints = {"rows": 2, "levels": 2}
+    rt.execute_cuda_call(rt.CompiledCUDAModule(None, hinted, {"cuda": fake}), low, prepared, {"np": np})
+    assert seen == {"rows": 2, "levels": 2}
+    prepared.hints = {}
     with pytest.raises(rt.CUDARuntimePreparationError, match="synchronize"):
         rt.execute_cuda_call(rt.CompiledCUDAModule(None, launcher, {}), low, prepared, {"np": np})
     assert rt.evaluate_host_prelude(low, dict(n=3), {"np": np})["x"].shape == (3,)
