@@ -21,12 +21,13 @@
 //     own ready flag); operands that lie in the chunk, three or more blocks back, go into
 //     a shared-memory list (one column-major strip per block, so a warp reads it without
 //     bank conflicts and with one trip count);
-//   helpers (6 warps, blocks b mod 6): finish y_b - subtract the listed operands, polling
+//   helpers (5 warps, blocks b mod 5): finish y_b - subtract the listed operands, polling
 //     the chunk's x in shared memory, then apply D_b^-1 held in registers;
-//   main (1 warp): x_b = y_b - W1_b x_b-1 - W2_b x_b-2 with the W tiles streamed into a
-//     shared-memory ring by bulk asynchronous copies (one lane of the last warp keeps the
-//     ring full)
-//     and the two previous blocks read from shared memory as broadcasts;
+//   main warp and partner warp: the partner computes z_b = -W2_b x_b-2 one step ahead, the
+//     main warp x_b = y_b + z_b - W1_b x_b-1; they hand over through named barriers; the W
+//     tiles are streamed into a shared-memory ring by bulk asynchronous copies (one lane
+//     of the last warp keeps the ring full) and the previous blocks are read from shared
+//     memory as broadcasts;
 //   every wait is bounded; a failed wait raises an error and poisons the rest of the chunk
 //     with NaN so that later chunks do not wait for it.
 //
@@ -42,7 +43,7 @@ constexpr int kChainWorkers = 256;
 constexpr int kChainRows = 1024;                      // rows per chunk
 constexpr int kChainRowsPerThread = kChainRows / kChainWorkers;
 constexpr int kChainBlocks = kChainRows / 32;
-constexpr int kChainHelpers = 6;
+constexpr int kChainHelpers = 5;
 constexpr int kChainStages = 8;                       // ring of (W1, W2) tile pairs
 constexpr int kTileDoubles = 1024;
 constexpr int kBlockDoubles = 3 * kTileDoubles;       // per 32-row block: D^-1, W1, W2
@@ -174,6 +175,25 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned 
         : "memory");
     return done != 0;
 }
+__device__ __forceinline__ bool mbar_test_wait(unsigned long long *bar, unsigned parity) {
+    unsigned done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ int ld_acquire_shared(const int *ptr) {
+    int v;
+    asm volatile("ld.acquire.cta.shared.s32 %0, [%1];" : "=r"(v) : "r"(smem_addr(ptr)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_shared(int *ptr, int v) {
+    asm volatile("st.release.cta.shared.s32 [%0], %1;" ::"r"(smem_addr(ptr)), "r"(v) : "memory");
+}
 // global -> shared bulk copy (source, destination and size are multiples of 16 bytes);
 // completion is signalled on the mbarrier as transferred bytes
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes,
@@ -186,6 +206,24 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned b
 }
 __device__ __forceinline__ void chain_prefetch_l2(const void *ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+// Named barriers between the main warp and its partner (64 threads: one warp arrives, the
+// other waits).  They have no timeout, so both warps perform them unconditionally.
+constexpr int kBarX0 = 2, kBarX1 = 3, kBarZ0 = 4, kBarZ1 = 5;
+__device__ __forceinline__ void pair_arrive(int id) {
+    asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ void pair_sync(int id) {
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+// one arrival per warp, predicated instead of branched so that the warp stays converged
+__device__ __forceinline__ void mbar_arrive_lane0(unsigned long long *bar, int lane) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.eq.s32 p, %1, 0;\n\t"
+        "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(smem_addr(bar)),
+        "r"(lane)
+        : "memory");
 }
 __device__ __forceinline__ void workers_barrier() {
     asm volatile("bar.sync 1, %0;" ::"n"(kChainWorkers) : "memory");
@@ -229,13 +267,15 @@ csr_chain_kernel(const ChainParams q) {
     __shared__ unsigned long long s_empty[kChainStages];
     __shared__ int s_chunk;
     __shared__ int s_failed;
+    __shared__ int s_tiles;                                    // tiles of the ring that have landed
     __shared__ int s_width[kChainBlocks];
     __shared__ int s_bptr[kChainBlocks + 1];
+    __shared__ double s_z[2][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     volatile int *failed_flag = &s_failed;
-    if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; }
+    if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; s_tiles = 0; }
     if (tid == kChainThreads - 32) {
-        for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 1); }
+        for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 2); }
         mbar_init_fence();
     }
     __syncthreads();
@@ -435,36 +475,55 @@ csr_chain_kernel(const ChainParams q) {
     volatile double *syv = sy;
 
     if (warp == kChainThreads / 32 - 1) {
-        // ---- loader warp (one lane): keeps the ring of W tiles full -------------------------
+        // ---- loader warp (one lane): keeps the ring of W tiles full and announces, in order,
+        // the tiles that have landed (the consumers then read one counter instead of waiting
+        // on a barrier per tile, which costs them about 150 cycles per block)
         if (lane != 0) return;
-        bool ok = true;
-        for (int b = kChainStages; b < nblk && ok; ++b) {
-            const int s = b % kChainStages;
-            const unsigned parity = ((b / kChainStages) - 1) & 1;
-            while (!mbar_try_wait(&s_empty[s], parity))
-                if (*failed_flag || dl.tick(p.status, row0)) { ok = false; break; }
-            if (!ok) break;
-            mbar_expect_tx(&s_full[s], kTileBytes);
-            bulk_load(ring + s * 2 * kTileDoubles, wsc + (long long)b * kBlockDoubles + kTileDoubles,
-                      kTileBytes, &s_full[s]);
-            issued = b + 1;
-        }
-        // no copy may still be in flight when the block's shared memory is released
-        const unsigned long long drain_end = global_timer() + p.budget_ns;
-        for (int b = max(0, issued - kChainStages); b < issued; ++b) {
-            unsigned spins = 0;
-            while (!mbar_try_wait(&s_full[b % kChainStages], (b / kChainStages) & 1))
-                if ((++spins & 255u) == 0 && global_timer() > drain_end) break;
+        int retired = 0;
+        unsigned idle = 0;
+        bool stop = false;
+        const unsigned long long give_up = global_timer() + p.budget_ns;
+        while (retired < issued || (issued < nblk && !stop)) {
+            bool progressed = false;
+            if (!stop && issued < nblk) {
+                const int s = issued % kChainStages;
+                if (issued < kChainStages ||
+                    mbar_test_wait(&s_empty[s], ((issued / kChainStages) - 1) & 1)) {
+                    mbar_expect_tx(&s_full[s], kTileBytes);
+                    bulk_load(ring + s * 2 * kTileDoubles,
+                              wsc + (long long)issued * kBlockDoubles + kTileDoubles, kTileBytes, &s_full[s]);
+                    ++issued;
+                    progressed = true;
+                }
+            }
+            if (retired < issued &&
+                mbar_test_wait(&s_full[retired % kChainStages], (retired / kChainStages) & 1)) {
+                ++retired;
+                st_release_shared(&s_tiles, retired);
+                progressed = true;
+            }
+            if (progressed) {
+                idle = 0;
+            } else if ((++idle & 255u) == 0) {
+                // after an error nothing more is requested, but no copy may still be in flight
+                // when the block's shared memory is released: what was requested is awaited
+                if (*failed_flag || aborted(p.status)) stop = true;
+                if (global_timer() > give_up) break;
+            }
         }
         return;
     }
 
+    const double2 *ring2 = reinterpret_cast<const double2 *>(ring);
     if (warp == 0) {
-        // ---- main warp ---------------------------------------------------------------------
+        // ---- main warp: x_b = y_b + z_b - W1_b x_b-1 --------------------------------------
+        // The loop always runs to the end and always performs its barrier operations (the
+        // partner warp blocks on them); after a failed wait it only publishes NaN.
         if (p.trace && lane == 0) p.trace[2ll * p.n + chunk] = clock64();
         const double nanv = __longlong_as_double(kCanonicalNaN);
         bool dead = *failed_flag != 0;
-        // the two blocks before the chunk
+        // the two blocks before the chunk (the partner can start on z_0 as soon as the
+        // first of them is there)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int t = row0 - kChainHalo + h * 32 + lane;
@@ -475,102 +534,88 @@ csr_chain_kernel(const ChainParams q) {
                                   failed_flag, p.status, r);
             }
             sxh[h * 32 + lane] = v;
+            __syncwarp();
+            if (h == 0 || nblk > 1) pair_arrive(h ? kBarX1 : kBarX0);   // "x_-2 / x_-1 is there"
         }
-        __syncwarp();
-        // The W2 half of a tile multiplies the block two back, which is known one step
-        // early: step b computes x_b = y_b + z_b - W1_b x_b-1 and, from the same broadcast
-        // of x_b-1, z_b+1 = -W2_b+1 x_b-1 for the next step.
-        const double2 *ring2 = reinterpret_cast<const double2 *>(ring);
-        double z = 0.0;
-        if (!dead)
-            dead = !warp_wait([&] { return mbar_try_wait(&s_full[0], 0); }, dl, failed_flag,
-                              p.status, row0);
-        if (!dead) {
-            const double2 *w2 = ring2 + kTileDoubles / 2 + lane;
-            const double2 *xb = reinterpret_cast<const double2 *>(sxh);
+        double ynext = syv[lane];
+        int tiles = 0;   // tiles known to have landed
+        for (int b = 0; b < nblk; ++b) {
+            const int base = b * 32, local = base + lane;
+            const bool active = local < rows_here;
+            const bool more = b + 1 < nblk;
+            const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+            const int s = b % kChainStages;
+            if (!dead && tiles <= b)
+                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
+                                  failed_flag, p.status, row0 + base);
+            double y = ynext;
+            if (!dead && __any_sync(kFullMask, is_pending(y)))
+                dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
+                                  p.status, row0 + base);
+            if (more) ynext = syv[local + 32];
+            dead = dead || *failed_flag != 0;
+            const double2 *xa = reinterpret_cast<const double2 *>(sx + base - 32);
+            const double2 *w1 = ring2 + s * kTileDoubles + lane;
+            double a0 = y, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+            for (int qd = 0; qd < 16; qd += 2) {
+                const double2 u0 = w1[qd * 32], u1 = w1[(qd + 1) * 32];
+                const double2 v0 = xa[qd], v1 = xa[qd + 1];
+                a0 = fma(-u0.x, v0.x, a0);
+                a1 = fma(-u0.y, v0.y, a1);
+                a2 = fma(-u1.x, v1.x, a2);
+                a3 = fma(-u1.y, v1.y, a3);
+            }
+            pair_sync(b & 1 ? kBarZ1 : kBarZ0);            // z_b = -W2_b x_b-2 from the partner
+            const double z = s_z[b & 1][lane];
+            const double val = dead ? nanv : publishable(((a0 + a1) + (a2 + a3)) + z);
+            sxv[local] = active ? val : 0.0;
+            if (active) {
+                st_relaxed_f64(p.x + r, val);
+                if (p.trace) p.trace[row0 + local] = clock64();
+            }
+            __syncwarp();
+            if (b + 2 < nblk) pair_arrive(b & 1 ? kBarX1 : kBarX0);   // "x_b is there"
+            mbar_arrive_lane0(&s_empty[s], lane);
+        }
+        if (dead && lane == 0) *failed_flag = 1;
+        if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
+        return;
+    }
+    if (warp == 1) {
+        // ---- partner warp: z_k = -W2_k x_k-2, one step ahead of the main warp ------------
+        bool dead = false;
+        int tiles = 0;
+        for (int k = 0; k < nblk; ++k) {
+            const int s = k % kChainStages;
+            if (!dead && tiles <= k)
+                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > k; }, dl,
+                                  failed_flag, p.status, row0 + k * 32);
+            pair_sync(k & 1 ? kBarX1 : kBarX0);            // x_k-2 is in shared memory
+            const double2 *xb = reinterpret_cast<const double2 *>(sx + k * 32 - 64);
+            const double2 *w2 = ring2 + s * kTileDoubles + kTileDoubles / 2 + lane;
             double c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
 #pragma unroll
             for (int qd = 0; qd < 16; qd += 2) {
-                const double2 u0 = w2[qd * 32], v0 = xb[qd];
-                const double2 u1 = w2[(qd + 1) * 32], v1 = xb[qd + 1];
+                const double2 u0 = w2[qd * 32], u1 = w2[(qd + 1) * 32];
+                const double2 v0 = xb[qd], v1 = xb[qd + 1];
                 c0 = fma(-u0.x, v0.x, c0);
                 c1 = fma(-u0.y, v0.y, c1);
                 c2 = fma(-u1.x, v1.x, c2);
                 c3 = fma(-u1.y, v1.y, c3);
             }
-            z = (c0 + c1) + (c2 + c3);
-        }
-        double ynext = syv[lane];
-        int b = 0;
-        for (; b < nblk; ++b) {
-            const int base = b * 32, local = base + lane;
-            const bool active = local < rows_here;
-            const bool more = b + 1 < nblk;
-            const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-            const int s = b % kChainStages, sn = (b + 1) % kChainStages;
-            const long long t0_ = clock64();
-            if (!dead && more)
-                dead = !warp_wait([&] { return mbar_try_wait(&s_full[sn], ((b + 1) / kChainStages) & 1); },
-                                  dl, failed_flag, p.status, row0 + base);
-            const long long t1_ = clock64();
-            double y = ynext;
-            if (!dead && __any_sync(kFullMask, is_pending(y)))
-                dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
-                                  p.status, row0 + base);
-            if (dead) break;
-            const long long t2_ = clock64();
-            if (more) ynext = syv[local + 32];
-            const double2 *xa = reinterpret_cast<const double2 *>(sx + base - 32);
-            double2 v[16];
-#pragma unroll
-            for (int qd = 0; qd < 16; ++qd) v[qd] = xa[qd];
-            const double2 *w1 = ring2 + s * kTileDoubles + lane;
-            const double2 *w2 = ring2 + sn * kTileDoubles + kTileDoubles / 2 + lane;
-            double a0 = y, a1 = z, a2 = 0.0, a3 = 0.0, c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
-#pragma unroll
-            for (int qd = 0; qd < 16; qd += 2) {
-                const double2 u0 = w1[qd * 32], u1 = w1[(qd + 1) * 32];
-                a0 = fma(-u0.x, v[qd].x, a0);
-                a1 = fma(-u0.y, v[qd].y, a1);
-                a2 = fma(-u1.x, v[qd + 1].x, a2);
-                a3 = fma(-u1.y, v[qd + 1].y, a3);
-            }
-            if (more) {
-#pragma unroll
-                for (int qd = 0; qd < 16; qd += 2) {
-                    const double2 u0 = w2[qd * 32], u1 = w2[(qd + 1) * 32];
-                    c0 = fma(-u0.x, v[qd].x, c0);
-                    c1 = fma(-u0.y, v[qd].y, c1);
-                    c2 = fma(-u1.x, v[qd + 1].x, c2);
-                    c3 = fma(-u1.y, v[qd + 1].y, c3);
-                }
-            }
-            const double val = publishable((a0 + a1) + (a2 + a3));
-            z = (c0 + c1) + (c2 + c3);
-            sxv[local] = active ? val : 0.0;
-            if (active) {
-                st_relaxed_f64(p.x + r, val);
-                if (p.trace) p.trace[row0 + local] = lane == 0 ? t0_ : lane == 1 ? t1_ : lane == 2 ? t2_ : clock64();
-            }
+            s_z[k & 1][lane] = (c0 + c1) + (c2 + c3);
+            if (dead && lane == 0) *failed_flag = 1;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[s]);
+            pair_arrive(k & 1 ? kBarZ1 : kBarZ0);
+            mbar_arrive_lane0(&s_empty[s], lane);
         }
-        if (dead) {
-            // poison what is left of the chunk: later chunks must not wait for it
-            if (lane == 0) *failed_flag = 1;
-            for (int local = b * 32 + lane; local < rows_here; local += 32) {
-                const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-                sxv[local] = nanv;
-                st_relaxed_f64(p.x + r, nanv);
-            }
-        }
-        if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
         return;
     }
 
-    // ---- helper warps: y_b for blocks b = warp - 1, warp - 1 + 6, ... ----------------------
+    // ---- helper warps 2..6: y_b for blocks b = warp - 2, warp - 2 + 5, ... -------------------
     {
-        int b = warp - 1;
+        int b = warp - 2;
         if (b >= nblk) return;
         const double *mbase = wsc + lane;
         double m[32];
@@ -586,7 +631,6 @@ csr_chain_kernel(const ChainParams q) {
 #pragma unroll
             for (int k = 0; k < 32; ++k)
                 mnext[k] = more ? __ldg(mbase + (long long)(b + kChainHelpers) * kBlockDoubles + k * 32) : 0.0;
-            const long long h0_ = clock64();
             double t0 = active ? sacc[local] : 0.0, t1 = 0.0;
             bool bad = *failed_flag != 0;
             if (!overflow) {
@@ -625,7 +669,6 @@ csr_chain_kernel(const ChainParams q) {
                 return;
             }
             const double t = t0 + t1;
-            const long long h1_ = clock64();
             // y_block = inverse block * t_block: 32 independent shuffle / FMA pairs
             double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
 #pragma unroll
@@ -636,10 +679,8 @@ csr_chain_kernel(const ChainParams q) {
                 y3 = fma(m[k + 3], __shfl_sync(kFullMask, t, k + 3), y3);
             }
             syv[local] = publishable((y0 + y1) + (y2 + y3));
-            const long long h2_ = clock64();
 #pragma unroll
             for (int k = 0; k < 32; ++k) m[k] = mnext[k];
-            if (p.trace && active) p.trace[(long long)p.n + row0 + local] = lane == 0 ? h0_ : lane == 1 ? h1_ : lane == 2 ? h2_ : clock64();
         }
     }
 }
