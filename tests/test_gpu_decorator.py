@@ -93,6 +93,39 @@ def test_decorated_first_configuration(cuda, oracle):
     assert len(plan.execution_data.band_ptr) - 1 == 511           # levels of the 256 x 256 grid
 
 
+def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch):
+    """A long dependence chain (5-6 rows per level) through the decorator: the inspector's level
+    count sends the sync-free launcher to the block-recurrence chain solver; the block tiles are
+    rebuilt when the values change and only then."""
+    import ops_decorated as od
+    from lcd_b200 import generators as gen, ops
+    tri = gen.random_band_lower(65_536, seed=3)
+    Ap, Ai, Ax = tri.csr_arrays()
+    calls = {"prepare": 0, "solve": 0}
+    real_prepare, real_solve = ops.chain_prepare, ops.sptrsv_csr_chain
+    monkeypatch.setattr(ops, "chain_prepare", lambda *a, **k: (calls.__setitem__("prepare", calls["prepare"] + 1), real_prepare(*a, **k))[1])
+    monkeypatch.setattr(ops, "sptrsv_csr_chain", lambda *a, **k: (calls.__setitem__("solve", calls["solve"] + 1), real_solve(*a, **k))[1])
+    plan = od.csr_warp_syncfree.schedule_plan(Ap, Ai, Ax, tri.b, tri.n)
+    assert plan.rows == tri.n and plan.rows / plan.levels < 64
+    want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+    x = od.csr_warp_syncfree(Ap, Ai, Ax, tri.b, tri.n)
+    np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)         # the reference's E2E tolerance
+    assert oracle.relative_residual_csr(Ap, Ai, Ax, x, tri.b) <= 1e-12
+    assert calls == {"prepare": 1, "solve": 1}
+    x2 = od.csr_warp_syncfree(Ap, Ai, Ax, tri.b, tri.n)                 # same values: tiles are kept
+    np.testing.assert_array_equal(x2, x)
+    assert calls == {"prepare": 1, "solve": 2}
+    Ax2 = Ax.copy()
+    Ax2[Ap[1:] - 1] *= 2.0                                               # new diagonal: tiles rebuilt
+    x3 = od.csr_warp_syncfree(Ap, Ai, Ax2, tri.b, tri.n)
+    np.testing.assert_allclose(x3, oracle.sptrsv_csr_lower(Ap, Ai, Ax2, tri.b), rtol=1e-10, atol=1e-12)
+    assert calls == {"prepare": 2, "solve": 3}
+    # small systems and wide levels stay on the polling kernel
+    grid = gen.laplacian2d_tril(64, seed=0)
+    od.csr_warp_syncfree(*grid.csr_arrays(), grid.b, grid.n)
+    assert calls["solve"] == 3
+
+
 @pytest.mark.parametrize("mode", ["wavefront", "sync_free"])
 @pytest.mark.parametrize("name", golden_names("ilu0_"))
 def test_decorated_ilu0_is_bit_identical(cuda, name, mode):
