@@ -45,7 +45,10 @@ enum {
     LCD_OP_CSC_LOWER = 1, /* cols, diagonal first  (compiler/demo/sptrsv.py:37-43)  */
     LCD_OP_ILU0_CSR = 2,  /* full rows, sorted     (compiler/demo/spilu0.py:21-47)  */
     LCD_OP_CSR_UPPER = 3, /* rows, diagonal first, visited last to first            */
-    LCD_OP_CSC_UPPER = 4  /* cols, diagonal last,  visited last to first            */
+    LCD_OP_CSC_UPPER = 4, /* cols, diagonal last,  visited last to first            */
+    LCD_OP_CSR_LOWER_ROWS = 5 /* rows, every stored entry left of the diagonal is an operand,
+                                 the diagonal is stored anywhere or kept apart
+                                 (compiler/demo/gauss_seidel.py:18-41); DAG build only */
 };
 
 /* Flags of the CSR solvers. */
@@ -97,6 +100,32 @@ int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_t *idx, int
                   int32_t *wavefronts, int32_t *wavefront_ptr, int32_t *n_levels_host,
                   void *workspace, int64_t workspace_bytes, int32_t timeout_ms,
                   void *stream);
+
+/*
+ * Rows of a Gauss-Seidel sweep over a lower-triangular matrix -> the diagonal-last rows the
+ * CSR solvers read.  Replaces what the reference's generated kernels do per row
+ * (compiler/demo/gauss_seidel.py:18-26: strictly lower rows, diagonal in a separate
+ * array; :29-41: the diagonal is the last stored entry equal to the row index, 1.0
+ * when absent).  One sweep is then one lower-triangular solve on the converted arrays.
+ *   lcd_gs_layout  (structure only, once per matrix)
+ *     mode 0: diagonal kept apart; mode 1: diagonal searched in the row.
+ *     Ap_out: n+1 ints, Ai_out: nnz+n ints (capacity), perm: nnz ints - the slot of
+ *     every stored entry in the converted arrays, -1 for an entry that is dropped (a
+ *     diagonal entry superseded by a later one).  *nnz_out_host receives Ap_out[n].
+ *     workspace: lcd_gs_layout_workspace_bytes(n) bytes.  Errors (status block):
+ *     LCD_ERR_INDEX_RANGE for an entry right of the diagonal (only lower-triangular
+ *     inputs are served) or, in mode 0, on it; LCD_ERR_BAD_POINTERS.
+ *   lcd_gs_values  (every call: the values may have changed)
+ *     Ax_out[perm[j]] = Ax[j]; diagonal slots (last of each row) = D[i] in mode 0,
+ *     else the row's diagonal entry or 1.0.
+ */
+int lcd_gs_layout_workspace_bytes(int32_t n, int64_t *bytes);
+int lcd_gs_layout(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, int mode,
+                  int32_t *Ap_out, int32_t *Ai_out, int32_t *perm, int64_t *nnz_out_host,
+                  void *workspace, int64_t workspace_bytes, int32_t *status_dev, void *stream,
+                  int *status_host);
+int lcd_gs_values(int32_t n, int64_t nnz, const int32_t *Ap_out, const int32_t *perm,
+                  const double *Ax, const double *D, double *Ax_out, void *stream);
 
 /*
  * Diagonal-position table: pos[s] = first p in [ptr[s], ptr[s+1]) with idx[p] == s,

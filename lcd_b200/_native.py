@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(_HERE, "liblcd_b200.so")
 # LCD_* codes of include/lcd_b200.h
 OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
     ERR_BAD_POINTERS, ERR_INDEX_RANGE, ERR_CYCLE, ERR_MISSING_DIAGONAL, ERR_TOO_LARGE = range(11)
-OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER = range(5)
+OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER, OP_CSR_LOWER_ROWS = range(6)
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
 WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
@@ -50,6 +50,10 @@ _SIGNATURES = {
     "lcd_diag_positions": (c_int, [c_int32, _P, _P, c_int64, _P, _P, _P, ctypes.POINTER(c_int)]),
     "lcd_sptrsv_csr_syncfree": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, c_int,
                                         c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_gs_layout_workspace_bytes": (c_int, [c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_gs_layout": (c_int, [c_int32, c_int64, _P, _P, c_int, _P, _P, _P, ctypes.POINTER(c_int64),
+                              _P, c_int64, _P, _P, ctypes.POINTER(c_int)]),
+    "lcd_gs_values": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P]),
     "lcd_chain_workspace_bytes": (c_int, [c_int32, ctypes.POINTER(c_int64)]),
     "lcd_chain_prepare": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, c_int64, _P]),
     "lcd_sptrsv_csr_chain": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P, c_int64,

@@ -239,7 +239,8 @@ __device__ __forceinline__ int visit_edges(const EdgeRule &q, int v, F f) {
         const int c = q.idx[j];
         if (c < 0 || c >= q.n) { rc = LCD_ERR_INDEX_RANGE; continue; }
         switch (q.op) {
-            case LCD_OP_CSR_LOWER: if (i > c) f(c, i); break;
+            case LCD_OP_CSR_LOWER:
+            case LCD_OP_CSR_LOWER_ROWS: if (i > c) f(c, i); break;
             case LCD_OP_CSC_LOWER: if (c > i) f(i, c); break;
             case LCD_OP_ILU0_CSR:
                 if (c >= i) return rc;
@@ -441,6 +442,62 @@ static DagScratch plan_scratch(Bump &b, int n, long long cap) {
     return s;
 }
 
+// ---- Gauss-Seidel rows -> diagonal-last rows ------------------------------------------
+// One thread per row.  count: operands (entries left of the diagonal) + 1 diagonal slot.
+__global__ void gs_count_kernel(int n, long long nnz, const int *__restrict__ Ap,
+                                const int *__restrict__ Ai, int mode, int *__restrict__ len,
+                                int32_t *status) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int s = Ap[i], e = Ap[i + 1];
+    if (s < 0 || e < s || (long long)e > nnz) {
+        raise_error(status, LCD_ERR_BAD_POINTERS, i);
+        len[i] = 1;
+        return;
+    }
+    int operands = 0;
+    for (int j = s; j < e; ++j) {
+        const int c = Ai[j];
+        if (c < 0 || c > i || (c == i && mode == 0)) raise_error(status, LCD_ERR_INDEX_RANGE, i);
+        else if (c < i) ++operands;
+    }
+    len[i] = operands + 1;
+}
+
+__global__ void gs_fill_kernel(int n, const int *__restrict__ Ap, const int *__restrict__ Ai,
+                               const int *__restrict__ Ap_out, int *__restrict__ Ai_out,
+                               int *__restrict__ perm, const int32_t *status) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n || status[kStatusCode] != 0) return;
+    int pos = Ap_out[i];
+    const int slot = Ap_out[i + 1] - 1;
+    int last = -1;
+    for (int j = Ap[i]; j < Ap[i + 1]; ++j) {
+        const int c = Ai[j];
+        if (c < i) {
+            Ai_out[pos] = c;
+            perm[j] = pos++;
+        } else {
+            perm[j] = -1;
+            last = j;   // the reference's loop keeps the last entry equal to the row index
+        }
+    }
+    Ai_out[slot] = i;
+    if (last >= 0) perm[last] = slot;
+}
+
+__global__ void gs_diag_kernel(int n, const int *__restrict__ Ap_out, const double *__restrict__ D,
+                               double *__restrict__ Ax_out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) Ax_out[Ap_out[i + 1] - 1] = D ? D[i] : 1.0;
+}
+
+__global__ void gs_scatter_kernel(long long nnz, const int *__restrict__ perm,
+                                  const double *__restrict__ Ax, double *__restrict__ Ax_out) {
+    const long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < nnz && perm[j] >= 0) Ax_out[perm[j]] = Ax[j];
+}
+
 static inline int grid_for(long long m, int threads) {
     long long g = (m + threads - 1) / threads;
     const long long cap = 148ll * 32;
@@ -452,7 +509,7 @@ static inline int grid_for(long long m, int threads) {
 using namespace lcd;
 
 extern "C" int lcd_dag_workspace_bytes(int op, int32_t n, int64_t nnz, int64_t *bytes) {
-    if (op < 0 || op > LCD_OP_CSC_UPPER || n < 0 || nnz < 0 || !bytes)
+    if (op < 0 || op > LCD_OP_CSR_LOWER_ROWS || n < 0 || nnz < 0 || !bytes)
         return LCD_ERR_INVALID_ARGUMENT;
     Bump b{nullptr, 0};
     b.take<int32_t>(LCD_STATUS_WORDS);
@@ -467,7 +524,7 @@ extern "C" int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_
                              int32_t *level, int32_t *wavefronts, int32_t *wavefront_ptr,
                              int32_t *n_levels_host, void *workspace, int64_t workspace_bytes,
                              int32_t timeout_ms, void *stream) {
-    if (op < 0 || op > LCD_OP_CSC_UPPER || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
+    if (op < 0 || op > LCD_OP_CSR_LOWER_ROWS || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
         return LCD_ERR_INVALID_ARGUMENT;
     *n_edges_host = 0;
     *n_levels_host = 0;
@@ -580,4 +637,66 @@ extern "C" int lcd_diag_positions(int32_t n, const int32_t *ptr, const int32_t *
         LCD_CUDA_TRY(cudaGetLastError());
     }
     return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_gs_layout_workspace_bytes(int32_t n, int64_t *bytes) {
+    if (n < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
+    Bump b{nullptr, 0};
+    b.take<long long>(8);
+    b.take<int>(n);
+    b.take<int>(scan_blocks(n) + 2);
+    *bytes = (int64_t)b.used + 256;
+    return LCD_OK;
+}
+
+extern "C" int lcd_gs_layout(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, int mode,
+                             int32_t *Ap_out, int32_t *Ai_out, int32_t *perm,
+                             int64_t *nnz_out_host, void *workspace, int64_t workspace_bytes,
+                             int32_t *status_dev, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || (mode != 0 && mode != 1) || !status_dev || !nnz_out_host)
+        return LCD_ERR_INVALID_ARGUMENT;
+    *nnz_out_host = 0;
+    if (n > 0 && (!Ap || (nnz > 0 && (!Ai || !perm)) || !Ap_out || !Ai_out || !workspace))
+        return LCD_ERR_INVALID_ARGUMENT;
+    int64_t need = 0;
+    lcd_gs_layout_workspace_bytes(n, &need);
+    if (n > 0 && workspace_bytes < need) return LCD_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        Bump b{static_cast<char *>(workspace), 0};
+        long long *total = b.take<long long>(8);
+        int *len = b.take<int>(n);
+        int *sums = b.take<int>(scan_blocks(n) + 2);
+        gs_count_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, nnz, Ap, Ai, mode, len, status_dev);
+        LCD_CUDA_TRY(cudaGetLastError());
+        LCD_CUDA_TRY(exclusive_scan(len, n, Ap_out, sums, total, st));
+        long long total_host = 0;
+        LCD_CUDA_TRY(cudaMemcpyAsync(&total_host, total, sizeof total_host, cudaMemcpyDeviceToHost, st));
+        LCD_CUDA_TRY(cudaStreamSynchronize(st));
+        const int32_t last = (int32_t)total_host;
+        LCD_CUDA_TRY(cudaMemcpyAsync(Ap_out + n, &last, sizeof last, cudaMemcpyHostToDevice, st));
+        gs_fill_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, Ap, Ai, Ap_out, Ai_out, perm, status_dev);
+        LCD_CUDA_TRY(cudaGetLastError());
+        LCD_CUDA_TRY(cudaStreamSynchronize(st));   // `last` is read by the copy above
+        *nnz_out_host = total_host;
+    }
+    return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_gs_values(int32_t n, int64_t nnz, const int32_t *Ap_out, const int32_t *perm,
+                             const double *Ax, const double *D, double *Ax_out, void *stream) {
+    if (n < 0 || nnz < 0) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap_out || !Ax_out || (nnz > 0 && (!perm || !Ax)))) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (n > 0) {
+        gs_diag_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, Ap_out, D, Ax_out);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    if (nnz > 0) {
+        gs_scatter_kernel<<<(unsigned)((nnz + 255) / 256), 256, 0, st>>>(nnz, perm, Ax, Ax_out);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    return LCD_OK;
 }

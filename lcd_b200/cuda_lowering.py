@@ -13,7 +13,9 @@ then structural-lookup tables, then the executor arrays of the chosen mode
 Recognition is alpha-equivalence: identifiers are renamed in order of first
 appearance and the block loop's AST is compared with the canonical forms below
 (the operators of ``compiler/demo/sptrsv.py:26-43`` and
-``compiler/demo/spilu0.py:21-47`` plus their backward-substitution forms).
+``compiler/demo/spilu0.py:21-47`` plus their backward-substitution forms, and the
+Gauss-Seidel sweeps of ``compiler/demo/gauss_seidel.py:18-41``, whose block loop sits
+inside a host sweep loop that the launcher runs).
 """
 
 from __future__ import annotations
@@ -115,10 +117,30 @@ for i in range(n):
                         A_data[j_ptr] = A_data[j_ptr] - l_ik * u_kj
                         break
 """),
+    "gauss_seidel_simple_csr": (dict(Ap="ptr", Ai="idx", Ax="val", D="diagonal", b="rhs", x="out", n="n"), """
+for i in range(n):
+    x[i] = b[i]
+    for j in range(Ap[i], Ap[i + 1]):
+        x[i] -= Ax[j] * x[Ai[j]]
+    x[i] /= D[i]
+"""),
+    "gauss_seidel_full_csr": (dict(Ap="ptr", Ai="idx", Ax="val", b="rhs", x="out", n="n"), """
+for i in range(n):
+    sigma = 0.0
+    diag = 1.0
+    for j in range(Ap[i], Ap[i + 1]):
+        if Ai[j] == i:
+            diag = Ax[j]
+        else:
+            sigma += Ax[j] * x[Ai[j]]
+    x[i] = (b[i] - sigma) / diag
+"""),
 }
 # name of the inner loop a thread map may refer to, per operator
 _THREAD_LOOPS = {"sptrsv_csr_lower": "j", "sptrsv_csc_lower": "j", "sptrsv_csr_upper": "j",
-                 "sptrsv_csc_upper": "j", "ilu0_csr": "j_ptr"}
+                 "sptrsv_csc_upper": "j", "ilu0_csr": "j_ptr", "gauss_seidel_simple_csr": "j",
+                 "gauss_seidel_full_csr": "j"}
+GAUSS_SEIDEL_OPERATORS = ("gauss_seidel_simple_csr", "gauss_seidel_full_csr")
 # native entry point serving (operator, execution mode)
 _ENTRY_POINTS = {
     ("sptrsv_csr", "sync_free"): "lcd_sptrsv_csr_syncfree",
@@ -127,6 +149,11 @@ _ENTRY_POINTS = {
     ("sptrsv_csc", "wavefront"): "lcd_sptrsv_wavefront",
     ("ilu0_csr", "sync_free"): "lcd_spilu0_csr",
     ("ilu0_csr", "wavefront"): "lcd_spilu0_csr",
+    # a sweep is a lower-triangular solve on the diagonal-last rows lcd_gs_layout/lcd_gs_values make
+    ("gauss_seidel_simple_csr", "sync_free"): "lcd_sptrsv_csr_syncfree",
+    ("gauss_seidel_simple_csr", "wavefront"): "lcd_sptrsv_wavefront",
+    ("gauss_seidel_full_csr", "sync_free"): "lcd_sptrsv_csr_syncfree",
+    ("gauss_seidel_full_csr", "wavefront"): "lcd_sptrsv_wavefront",
 }
 _BUILTIN_NAMES = frozenset(dir(builtins))
 
@@ -177,19 +204,32 @@ _LIBRARY = _canonical_library()
 class _TargetLoop:
     loop: ast.For
     top_level_index: int
+    host_loops: tuple = ()     # (iterator name, range expression) of enclosing host loops
 
 
 def _find_block_loop(function, iterator):
+    """The block loop: a top-level ``for``, or the only statement of a nest of top-level
+    ``for ... in range(...)`` host loops (``compiler/cuda_lowering.py:1129-1140`` wraps the
+    launch in those loops; here the launcher runs them)."""
     for index, statement in enumerate(function.body):
-        if (isinstance(statement, ast.For) and isinstance(statement.target, ast.Name)
-                and statement.target.id == iterator):
-            return _TargetLoop(statement, index)
+        host_loops = []
+        node = statement
+        while isinstance(node, ast.For) and isinstance(node.target, ast.Name) and not node.orelse:
+            if node.target.id == iterator:
+                return _TargetLoop(node, index, tuple(host_loops))
+            call = node.iter
+            if not (isinstance(call, ast.Call) and isinstance(call.func, ast.Name)
+                    and call.func.id == "range" and not call.keywords and len(node.body) == 1):
+                break
+            host_loops.append((node.target.id, deepcopy(call)))
+            node = node.body[0]
     for node in ast.walk(function):
         if (isinstance(node, ast.For) and isinstance(node.target, ast.Name)
                 and node.target.id == iterator):
             raise CUDALoweringError(
                 f"The block loop over {iterator!r} must be a top-level statement of the "
-                "function (host loops around it are not served by the native kernels).")
+                "function or the only statement inside top-level `for ... in range(...)` "
+                "host loops.")
     raise CUDALoweringError(f"No loop over the block iterator {iterator!r} was found.")
 
 
@@ -232,6 +272,7 @@ class CUDALoweringResult:
     thread_loop_iterator: str | None = None
     thread_unroll_factor: int = 1
     host_loop_iterators: tuple = ()
+    host_loop_ranges: tuple = ()       # ast.Call `range(...)` of each host loop, outermost first
     n_warp: int | None = None
     warp_mapped: bool = False
     dependence_protocol: str = COUNTER_DEPENDENCE
@@ -271,14 +312,14 @@ def recognise_operator(code, loop_iterator):
     if match is None:
         raise CUDALoweringError(
             "The loop nest over %r is not one of the operators served by the native kernels "
-            "(SpTRSV CSR/CSC lower/upper, SpILU0 CSR); lcd_b200 does not interpret or "
+            "(SpTRSV CSR/CSC lower/upper, SpILU0 CSR, Gauss-Seidel CSR sweeps); lcd_b200 does not interpret or "
             "fall back to the CPU." % loop_iterator)
     operator, by_canonical, thread_canonical = match
     roles = {}
     thread_loop = None
     for original, canonical in names.items():
         role = by_canonical.get(canonical)
-        if role in ("ptr", "idx", "val", "rhs", "out", "n"):
+        if role in ("ptr", "idx", "val", "rhs", "out", "n", "diagonal"):
             roles[role] = original
         if canonical == thread_canonical:
             thread_loop = original
@@ -367,6 +408,8 @@ def lower_to_native(code, loop_iterator, reductions=None, kernel_name=None,
         entry_point=_ENTRY_POINTS[(family, mode)],
         threads_per_block=wavefront_threads_per_block,
         thread_loop_iterator=thread_loop_iterator, thread_unroll_factor=thread_unroll_factor,
+        host_loop_iterators=tuple(name for name, _ in target.host_loops),
+        host_loop_ranges=tuple(call for _, call in target.host_loops),
         n_warp=n_warp, warp_mapped=warp_mapped, dependence_protocol=protocol,
         device_only_variables=tuple(v for v in lifted if v == out_name),
         module_ast=ast.Module(body=[deepcopy(function)], type_ignores=[]),

@@ -48,9 +48,12 @@ SCHEDULE_CACHE_SIZE = 8
 VARIANT_ATTRIBUTES = ("cuda_lowering", "compiled_cuda_module", "cuda_kernel", "cuda_launcher",
                       "cuda_module_ast", "cuda_kernel_ast", "cuda_source", "cuda_kernel_source",
                       "cuda_launcher_ast", "cuda_launcher_source")
+CHAIN_CAPABLE_OPERATORS = ("sptrsv_csr", "gauss_seidel_simple_csr", "gauss_seidel_full_csr")
 _DAG_OPERATORS = {("sptrsv_csr", False): "csr_lower", ("sptrsv_csr", True): "csr_upper",
                   ("sptrsv_csc", False): "csc_lower", ("sptrsv_csc", True): "csc_upper",
-                  ("ilu0_csr", False): "ilu0_csr"}
+                  ("ilu0_csr", False): "ilu0_csr",
+                  ("gauss_seidel_simple_csr", False): "csr_lower_rows",
+                  ("gauss_seidel_full_csr", False): "csr_lower_rows"}
 
 
 def _variant_attributes(lowering, module):
@@ -207,7 +210,7 @@ def parallel(**kwargs):
                     # measured on B200: the ILU0 sync-free kernel pays about 8x the SpTRSV
                     # hand-off (acquire/release flags plus the row update before the release)
                     sync_free_penalty=8.0 if operator == "ilu0_csr" else 1.0,
-                    chain_capable=operator == "sptrsv_csr")
+                    chain_capable=operator in CHAIN_CAPABLE_OPERATORS)
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
             return SchedulePlan(schedule=schedule, execution_data=data, features=features,

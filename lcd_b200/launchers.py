@@ -8,6 +8,10 @@ closure that receives the same positional arguments (original parameters, lifted
 locals, lookup tables, executor arrays) and forwards the device pointers to one
 C-ABI entry point; level loops and barriers live inside the library.
 
+Gauss-Seidel sweeps (``compiler/demo/gauss_seidel.py``) keep their host sweep loop inside the
+launcher, as the reference's generated launcher does; a sweep is a triangular solve on the
+diagonal-last form of the rows.
+
 A sync-free CSR triangular solve whose levels are narrow (the inspector's row and level
 counts arrive as hints from the decorator) goes to the block-recurrence chain solver
 instead of the polling kernel.
@@ -18,6 +22,8 @@ are accepted and ignored, so call sites written for the reference keep working.
 """
 
 from __future__ import annotations
+
+import ast
 
 import numpy as np
 
@@ -81,27 +87,23 @@ def bind(lowering):
         return nodes, ptr_dev, ptr_host
 
     def chain_solve(Ap, Ai, Ax, b, x, cache):
-        # the block tiles depend on the values: they are rebuilt unless the value array is
-        # the one (same storage, same contents) they were built from
+        # the block tiles depend on the values (the structure is fixed per plan): they are
+        # rebuilt unless the value array has the contents they were built from (position-keyed
+        # 128-bit device checksum, as for the structure fingerprint of the plan cache)
         n = Ap.numel() - 1
         workspace = cache.get("chain_workspace")
         if workspace is None or workspace.device != Ax.device:
             workspace = cache["chain_workspace"] = ops.chain_workspace(n, Ax.device)
             cache.pop("chain_values", None)
-        stamp = (Ax.data_ptr(),) + ops.fingerprint(Ax.view(torch.int32))
+        stamp = ops.fingerprint(Ax.view(torch.int32))
         if cache.get("chain_values") != stamp:
             ops.chain_prepare(Ap, Ai, Ax, workspace, upper=lowering.upper)
             cache["chain_values"] = stamp
         ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
 
-    def sptrsv_csr(*args, _hints=None):
-        v = split(args)
-        Ap, Ai, Ax = matrix(v)
-        b = as_tensor(v[roles["rhs"]], torch.float64)
-        x = as_tensor(v[roles["out"]], torch.float64)
+    def csr_solve(Ap, Ai, Ax, b, x, v, hints):
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
         if lowering.execution_mode == "sync_free":
-            hints = _hints or {}
             if chain_solver_preferred(hints.get("rows", 0), hints.get("levels", 0),
                                       hints.get("arch")):
                 chain_solve(Ap, Ai, Ax, b, x, hints.setdefault("cache", {}))
@@ -112,6 +114,42 @@ def bind(lowering):
             mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
             ops.sptrsv_wavefront("csr_upper" if lowering.upper else "csr_lower", Ap, Ai, Ax, b,
                                  nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes)
+
+    def sptrsv_csr(*args, _hints=None):
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        b = as_tensor(v[roles["rhs"]], torch.float64)
+        x = as_tensor(v[roles["out"]], torch.float64)
+        csr_solve(Ap, Ai, Ax, b, x, v, _hints or {})
+
+    def host_trip_count(v):
+        """Product of the trip counts of the host loops around the block loop."""
+        count = 1
+        scalars = {k: val for k, val in v.items() if isinstance(val, (int, np.integer))}
+        for call in lowering.host_loop_ranges:
+            code = compile(ast.Expression(body=ast.fix_missing_locations(call)), "<host-loop>", "eval")
+            count *= len(eval(code, {"__builtins__": {"range": range}}, scalars))
+        return count
+
+    def gauss_seidel(*args, _hints=None):
+        # Sweeps over a lower-triangular matrix: every sweep recomputes x from b in row order,
+        # i.e. it is the triangular solve on the diagonal-last form of the rows.  The structure
+        # part of the conversion is kept with the plan, the values are converted every call.
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        b = as_tensor(v[roles["rhs"]], torch.float64)
+        x = as_tensor(v[roles["out"]], torch.float64)
+        hints = _hints or {}
+        cache = hints.setdefault("cache", {})
+        separate = "diagonal" in roles
+        layout = cache.get("gs_layout")
+        if layout is None or layout.perm.device != Ap.device:
+            layout = cache["gs_layout"] = ops.gs_layout(Ap, Ai, separate_diagonal=separate)
+        diagonal = as_tensor(v[roles["diagonal"]], torch.float64) if separate else None
+        values = ops.gs_values(layout, Ax, diagonal, out=cache.get("gs_values"))
+        cache["gs_values"] = values
+        for _ in range(host_trip_count(v)):
+            csr_solve(layout.Ap, layout.Ai, values, b, x, v, hints)
 
     def sptrsv_csc(*args):
         v = split(args)
@@ -147,12 +185,13 @@ def bind(lowering):
             ops.spilu0_csr(Ap, Ai, Ax, pos, mode="wavefront", wavefronts=nodes,
                            wavefront_ptr_host=ptr_host, lanes=lanes)
 
-    launcher = {"sptrsv_csr": sptrsv_csr, "sptrsv_csc": sptrsv_csc, "ilu0_csr": ilu0_csr}.get(
+    launcher = {"sptrsv_csr": sptrsv_csr, "sptrsv_csc": sptrsv_csc, "ilu0_csr": ilu0_csr,
+                "gauss_seidel_simple_csr": gauss_seidel, "gauss_seidel_full_csr": gauss_seidel}.get(
         lowering.operator)
     if launcher is None:
         raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
     launcher.__name__ = lowering.launcher_name
-    launcher.accepts_hints = lowering.operator == "sptrsv_csr"
+    launcher.accepts_hints = launcher in (sptrsv_csr, gauss_seidel)
 
     def kernel(*args, **kwargs):
         raise CUDALoweringError(

@@ -18,7 +18,7 @@ from ._native import NativeError, check, ptr
 
 OPS = {"csr_lower": nat.OP_CSR_LOWER, "csc_lower": nat.OP_CSC_LOWER,
        "ilu0_csr": nat.OP_ILU0_CSR, "csr_upper": nat.OP_CSR_UPPER,
-       "csc_upper": nat.OP_CSC_UPPER}
+       "csc_upper": nat.OP_CSC_UPPER, "csr_lower_rows": nat.OP_CSR_LOWER_ROWS}
 
 
 def _op_code(op):
@@ -125,6 +125,57 @@ def diag_positions(ptr_t, idx_t, status=None):
 def _solve_flags(upper, unit_diag, of_full, exact):
     return ((nat.SOLVE_UPPER if upper else 0) | (nat.SOLVE_UNIT_DIAG if unit_diag else 0)
             | (nat.SOLVE_OF_FULL if of_full else 0) | (nat.SOLVE_EXACT if exact else 0))
+
+
+@dataclass
+class GaussSeidelLayout:
+    """Diagonal-last rows of a Gauss-Seidel sweep over a lower-triangular matrix."""
+
+    Ap: torch.Tensor
+    Ai: torch.Tensor
+    perm: torch.Tensor
+    nnz: int
+    separate_diagonal: bool
+
+
+def gs_layout(Ap, Ai, *, separate_diagonal):
+    """Structure part of the conversion (once per matrix): rows whose diagonal is kept in a
+    separate array (``separate_diagonal``) or stored somewhere in the row become rows with
+    the diagonal last, which is what the CSR solvers read."""
+    _require(Ap, torch.int32, "Ap")
+    _require(Ai, torch.int32, "Ai")
+    n, nnz, dev = Ap.numel() - 1, Ai.numel(), Ap.device
+    lib = nat.load()
+    need = ctypes.c_int64(0)
+    check(lib.lcd_gs_layout_workspace_bytes(n, ctypes.byref(need)), "lcd_gs_layout_workspace_bytes")
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    Ap_out = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    Ai_out = torch.empty(max(nnz + n, 1), dtype=torch.int32, device=dev)
+    perm = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    status = new_status(dev)
+    total, host = ctypes.c_int64(0), ctypes.c_int(0)
+    rc = lib.lcd_gs_layout(n, nnz, ptr(Ap), ptr(Ai), 0 if separate_diagonal else 1, ptr(Ap_out),
+                           ptr(Ai_out), ptr(perm), ctypes.byref(total), ptr(ws), ws.numel(),
+                           ptr(status), _stream(), ctypes.byref(host))
+    check(rc, "lcd_gs_layout")
+    if n == 0:
+        Ap_out.zero_()
+    return GaussSeidelLayout(Ap_out, Ai_out[:max(total.value, 0)].contiguous() if total.value else Ai_out[:0],
+                             perm, int(total.value), bool(separate_diagonal))
+
+
+def gs_values(layout, Ax, diagonal=None, out=None):
+    """Value part of the conversion (every call): scatter the stored values to their slots and
+    fill the diagonal slots from ``diagonal`` (separate array), the row's own entry, or 1.0."""
+    _require(Ax, torch.float64, "Ax")
+    if layout.separate_diagonal:
+        _require(diagonal, torch.float64, "diagonal")
+    n = layout.Ap.numel() - 1
+    out = torch.empty(max(layout.nnz, 1), dtype=torch.float64, device=Ax.device) if out is None else out
+    check(nat.load().lcd_gs_values(n, Ax.numel(), ptr(layout.Ap), ptr(layout.perm), ptr(Ax),
+                                   ptr(diagonal) if layout.separate_diagonal else None, ptr(out),
+                                   _stream()), "lcd_gs_values")
+    return out[:layout.nnz]
 
 
 def chain_workspace(n, device):

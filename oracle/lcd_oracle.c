@@ -29,7 +29,7 @@
 #include <string.h>
 
 enum { ORC_CSR_LOWER = 0, ORC_CSC_LOWER = 1, ORC_ILU0_CSR = 2,
-       ORC_CSR_UPPER = 3, ORC_CSC_UPPER = 4 };
+       ORC_CSR_UPPER = 3, ORC_CSC_UPPER = 4, ORC_CSR_LOWER_ROWS = 5 };
 
 /* ---- edge enumeration ------------------------------------------------- */
 /* Calls emit(src,dst) for every edge instance of the operator's rule, in the
@@ -50,6 +50,12 @@ static void enumerate_edges(int kind, int32_t n, const int32_t *ptr,
         if (kind == ORC_CSR_LOWER) {
             int32_t i = v;
             for (int32_t j = ptr[i]; j < ptr[i + 1] - 1; ++j)
+                if (i > idx[j]) emit(e, idx[j], i);
+        } else if (kind == ORC_CSR_LOWER_ROWS) {
+            /* Gauss-Seidel rows (compiler/demo/gauss_seidel.py:18-41): the whole row is
+             * visited, an entry left of the diagonal is a flow dependence */
+            int32_t i = v;
+            for (int32_t j = ptr[i]; j < ptr[i + 1]; ++j)
                 if (i > idx[j]) emit(e, idx[j], i);
         } else if (kind == ORC_CSC_LOWER) {
             int32_t i = v;
@@ -196,6 +202,37 @@ void orc_sptrsv_csr_lower(int32_t n, const int32_t *Ap, const int32_t *Ai,
         for (int32_t j = Ap[i]; j < Ap[i + 1] - 1; ++j) s -= Ax[j] * x[Ai[j]];
         x[i] = s / Ax[Ap[i + 1] - 1];
     }
+}
+
+/* Gauss-Seidel sweeps, strictly lower rows and a separate diagonal
+ * (compiler/demo/gauss_seidel.py:18-26, same loop in
+ * compiler/e2e_tests/test_gauss_seidel_e2e.py:19-28); x is updated in place. */
+void orc_gauss_seidel_simple_csr(int32_t n, const int32_t *Ap, const int32_t *Ai,
+                                 const double *Ax, const double *D, const double *b,
+                                 double *x, int32_t max_iter) {
+    for (int32_t sweep = 0; sweep < max_iter; ++sweep)
+        for (int32_t i = 0; i < n; ++i) {
+            x[i] = b[i];
+            for (int32_t j = Ap[i]; j < Ap[i + 1]; ++j) x[i] -= Ax[j] * x[Ai[j]];
+            x[i] /= D[i];
+        }
+}
+
+/* Gauss-Seidel sweeps, the diagonal is the last stored entry equal to the row index,
+ * 1.0 when absent (compiler/demo/gauss_seidel.py:29-41,
+ * compiler/e2e_tests/test_gauss_seidel_e2e.py:31-43). */
+void orc_gauss_seidel_full_csr(int32_t n, const int32_t *Ap, const int32_t *Ai,
+                               const double *Ax, const double *b, double *x,
+                               int32_t max_iter) {
+    for (int32_t sweep = 0; sweep < max_iter; ++sweep)
+        for (int32_t i = 0; i < n; ++i) {
+            double sigma = 0.0, diag = 1.0;
+            for (int32_t j = Ap[i]; j < Ap[i + 1]; ++j) {
+                if (Ai[j] == i) diag = Ax[j];
+                else sigma += Ax[j] * x[Ai[j]];
+            }
+            x[i] = (b[i] - sigma) / diag;
+        }
 }
 
 /* Upper CSR, diagonal first, rows visited from the last to the first. */

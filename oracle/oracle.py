@@ -18,9 +18,9 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liblcd_oracle.so")
 
-CSR_LOWER, CSC_LOWER, ILU0_CSR, CSR_UPPER, CSC_UPPER = range(5)
+CSR_LOWER, CSC_LOWER, ILU0_CSR, CSR_UPPER, CSC_UPPER, CSR_LOWER_ROWS = range(6)
 KINDS = {"csr_lower": CSR_LOWER, "csc_lower": CSC_LOWER, "ilu0_csr": ILU0_CSR,
-         "csr_upper": CSR_UPPER, "csc_upper": CSC_UPPER}
+         "csr_upper": CSR_UPPER, "csc_upper": CSC_UPPER, "csr_lower_rows": CSR_LOWER_ROWS}
 
 
 def build(force=False):
@@ -110,6 +110,24 @@ def _solve(name, Ap, Ai, Ax, b, extra=()):
 
 def sptrsv_csr_lower(Ap, Ai, Ax, b):
     return _solve("orc_sptrsv_csr_lower", Ap, Ai, Ax, b)
+
+
+def gauss_seidel_simple_csr(Ap, Ai, Ax, D, b, x0, max_iter):
+    """Sweeps over strictly lower rows with a separate diagonal; returns the new x."""
+    Ap, Ai, Ax, D, b = _i32(Ap), _i32(Ai), _f64(Ax), _f64(D), _f64(b)
+    x = np.array(x0, dtype=np.float64)
+    lib().orc_gauss_seidel_simple_csr(len(Ap) - 1, _p(Ap), _p(Ai), _p(Ax), _p(D), _p(b), _p(x),
+                                      ctypes.c_int32(int(max_iter)))
+    return x
+
+
+def gauss_seidel_full_csr(Ap, Ai, Ax, b, x0, max_iter):
+    """Sweeps over lower rows that store their diagonal; returns the new x."""
+    Ap, Ai, Ax, b = _i32(Ap), _i32(Ai), _f64(Ax), _f64(b)
+    x = np.array(x0, dtype=np.float64)
+    lib().orc_gauss_seidel_full_csr(len(Ap) - 1, _p(Ap), _p(Ai), _p(Ax), _p(b), _p(x),
+                                    ctypes.c_int32(int(max_iter)))
+    return x
 
 
 def sptrsv_csr_upper(Ap, Ai, Ax, b):

@@ -29,6 +29,8 @@ _sink = io.StringIO()
 with contextlib.redirect_stdout(_sink):
     import ref_ops  # noqa: E402
     from compiler.demo.spilu0 import compile_ilu0_csr, ilu0_csr  # noqa: E402
+    from compiler.demo.gauss_seidel import (  # noqa: E402
+        full_gauss_seidel_csr, simple_gauss_seidel_csr)
     ilu_syncfree = compile_ilu0_csr("sync_free", 128, 1)
     ilu_wavefront = compile_ilu0_csr("wavefront", 128, 1)
 from compiler.dag_preprocessing import (  # noqa: E402
@@ -128,6 +130,30 @@ def main():
     dag_record("csr_upper_reversed/", ref_ops.csr_upper_reversed, (Ap, Ai, Ax, tri.b, tri.n), out)
     out["x_csr"] = ref_ops.csr_upper_reversed.original_function(Ap, Ai, Ax, tri.b, tri.n)
     np.savez_compressed(os.path.join(out_dir, "sptrsv_upper_n48.npz"), **out)
+
+    # ---- Gauss-Seidel sweeps (the reference's demo operators, inputs as its E2E test builds them)
+    for name, tri in (("lap2d_g8", gen.laplacian2d_tril(8, seed=0)),
+                      ("band_n300", gen.random_band_lower(300, seed=1, mean_degree=6.0, band=16))):
+        full = tri.csr.tocsr()
+        full.sort_indices()
+        strict = sp.tril(full, k=-1, format="csr")
+        strict.sort_indices()
+        n = tri.n
+        D = full.diagonal().copy()
+        b = np.asarray(full @ np.linspace(1.0, 2.0, n)).ravel()
+        x0 = np.zeros(n)
+        sAp, sAi, sAx = strict.indptr.astype(np.int32), strict.indices.astype(np.int32), strict.data.copy()
+        fAp, fAi, fAx = full.indptr.astype(np.int32), full.indices.astype(np.int32), full.data.copy()
+        out = dict(simple_Ap=sAp, simple_Ai=sAi, simple_Ax=sAx, D=D, full_Ap=fAp, full_Ai=fAi,
+                   full_Ax=fAx, b=b, x0=x0, max_iter=np.int32(2))
+        dag_record("simple/", simple_gauss_seidel_csr, (sAp, sAi, sAx, D, b, x0.copy(), n, 2), out)
+        dag_record("full/", full_gauss_seidel_csr, (fAp, fAi, fAx, b, x0.copy(), n, 2), out)
+        out["simple/launcher_arguments"] = np.asarray(simple_gauss_seidel_csr.cuda_lowering.launcher_arguments)
+        out["full/launcher_arguments"] = np.asarray(full_gauss_seidel_csr.cuda_lowering.launcher_arguments)
+        out["x_simple"] = simple_gauss_seidel_csr.original_function(sAp, sAi, sAx, D, b, x0.copy(), n, 2)
+        out["x_full"] = full_gauss_seidel_csr.original_function(fAp, fAi, fAx, b, x0.copy(), n, 2)
+        np.savez_compressed(os.path.join(out_dir, f"gauss_seidel_{name}.npz"), **out)
+        print("wrote gauss_seidel", name)
 
     # ---- ILU0 CSR ---------------------------------------------------------
     ilu_inputs = {"lap3d_g4": gen.laplacian3d_ilu0(4, seed=5)[0]}

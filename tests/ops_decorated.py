@@ -84,6 +84,48 @@ def csr_upper_reversed(Ap, Ai, Ax, b, n):
     return x
 
 
+# the reference's Gauss-Seidel demo operators (compiler/demo/gauss_seidel.py:18-41)
+@parallel(block_map="i", function_props=PROPS_CSR, execution_mode="wavefront", threads_per_block=128)
+def simple_gauss_seidel_csr(Ap, Ai, Ax, D, b, x, n, max_iter):
+    for sweep in range(max_iter):
+        for i in range(n):
+            x[i] = b[i]
+            for j in range(Ap[i], Ap[i + 1]):
+                x[i] -= Ax[j] * x[Ai[j]]
+            x[i] /= D[i]
+    return x
+
+
+@parallel(block_map="i", function_props=PROPS_CSR, execution_mode="wavefront", threads_per_block=128)
+def full_gauss_seidel_csr(Ap, Ai, Ax, b, x, n, max_iter):
+    for sweep in range(max_iter):
+        for i in range(n):
+            sigma = 0.0
+            diag = 1.0
+            for j in range(Ap[i], Ap[i + 1]):
+                if Ai[j] == i:
+                    diag = Ax[j]
+                else:
+                    sigma += Ax[j] * x[Ai[j]]
+            x[i] = (b[i] - sigma) / diag
+    return x
+
+
+@parallel(block_map="i", function_props=PROPS_CSR, execution_mode="sync_free", threads_per_block=128)
+def full_gauss_seidel_csr_syncfree(Ap, Ai, Ax, b, x, n, max_iter):
+    for sweep in range(max_iter):
+        for i in range(n):
+            sigma = 0.0
+            diag = 1.0
+            for j in range(Ap[i], Ap[i + 1]):
+                if Ai[j] == i:
+                    diag = Ax[j]
+                else:
+                    sigma += Ax[j] * x[Ai[j]]
+            x[i] = (b[i] - sigma) / diag
+    return x
+
+
 def ilu0_csr(A_data, A_indices, A_indptr):
     n = len(A_indptr) - 1
     for i in range(n):

@@ -93,6 +93,75 @@ def test_decorated_first_configuration(cuda, oracle):
     assert len(plan.execution_data.band_ptr) - 1 == 511           # levels of the 256 x 256 grid
 
 
+@pytest.mark.parametrize("name", golden_names("gauss_seidel_"))
+def test_decorated_gauss_seidel_matches_the_reference(cuda, oracle, name):
+    """The reference's Gauss-Seidel demo operators (compiler/demo/gauss_seidel.py:18-41), inputs
+    built as compiler/e2e_tests/test_gauss_seidel_e2e.py:57-84 does; inspector arrays against
+    the reference's, results against its undecorated loops (rtol 1e-10 / atol 1e-12)."""
+    import ops_decorated as od
+    g = golden(name)
+    n, sweeps = len(g["b"]), int(g["max_iter"])
+    simple = (g["simple_Ap"], g["simple_Ai"], g["simple_Ax"], g["D"], g["b"], g["x0"].copy(), n, sweeps)
+    full = (g["full_Ap"], g["full_Ai"], g["full_Ax"], g["b"], g["x0"].copy(), n, sweeps)
+    for op, args, prefix in ((od.simple_gauss_seidel_csr, simple, "simple/"), (od.full_gauss_seidel_csr, full, "full/")):
+        succ, waves = op.build_dag(*args)
+        assert succ == _lists(g[prefix + "succ_ptr"], g[prefix + "succ_idx"])
+        assert waves == _lists(g[prefix + "wavefront_ptr"], g[prefix + "wavefronts"])
+        plan = op.schedule_plan(*args)
+        assert list(map(str, plan.schedule.lowering_key)) == g[prefix + "schedule"].tolist()
+        np.testing.assert_array_equal(plan.execution_data.wavefronts.cpu().numpy(), g[prefix + "wavefronts"])
+    x0 = simple[5].copy()
+    x = od.simple_gauss_seidel_csr(*simple)
+    np.testing.assert_allclose(x, g["x_simple"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_array_equal(simple[5], x0)                       # arguments are never mutated
+    x = od.full_gauss_seidel_csr(*full)
+    np.testing.assert_allclose(x, g["x_full"], rtol=1e-10, atol=1e-12)
+    x = od.full_gauss_seidel_csr_syncfree(*full)
+    np.testing.assert_allclose(x, g["x_full"], rtol=1e-10, atol=1e-12)
+    # zero sweeps return the start vector, one sweep already is the triangular solve
+    start = np.linspace(-1.0, 1.0, n)
+    np.testing.assert_array_equal(od.full_gauss_seidel_csr(*full[:4], start, n, 0), start)
+    np.testing.assert_allclose(od.full_gauss_seidel_csr(*full[:4], start, n, 1), g["x_full"], rtol=1e-10, atol=1e-12)
+    # new values on the same structure (plan and layout are reused, values converted again)
+    D2 = g["D"] * 2.0
+    want = oracle.gauss_seidel_simple_csr(g["simple_Ap"], g["simple_Ai"], g["simple_Ax"], D2, g["b"], g["x0"], sweeps)
+    got = od.simple_gauss_seidel_csr(g["simple_Ap"], g["simple_Ai"], g["simple_Ax"], D2, g["b"], g["x0"].copy(), n, sweeps)
+    np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
+
+
+def test_gauss_seidel_layout_edge_cases(cuda, oracle):
+    """Unsorted rows, repeated and missing diagonal entries, and entries right of the diagonal."""
+    from lcd_b200 import ops
+    from lcd_b200._native import ERR_INDEX_RANGE, NativeError
+    import torch
+    rows = [[0], [1, 0], [0], [3, 1, 3, 0], [2, 4, 2], [], [5, 6, 0, 3]]      # row 2 and 5: no diagonal
+    Ap = np.cumsum([0] + [len(r) for r in rows]).astype(np.int32)
+    Ai = np.asarray([c for r in rows for c in r], dtype=np.int32)
+    rng = np.random.default_rng(0)
+    Ax = rng.uniform(1.0, 2.0, len(Ai))
+    b = rng.uniform(-1, 1, len(rows))
+    dev = lambda a, t: torch.from_numpy(np.ascontiguousarray(a, dtype=t)).to(cuda)
+    layout = ops.gs_layout(dev(Ap, np.int32), dev(Ai, np.int32), separate_diagonal=False)
+    values = ops.gs_values(layout, dev(Ax, np.float64))
+    x = ops.sptrsv_csr_syncfree(layout.Ap, layout.Ai, values, dev(b, np.float64), exact=True).cpu().numpy()
+    want = oracle.gauss_seidel_full_csr(Ap, Ai, Ax, b, np.zeros(len(rows)), 1)
+    np.testing.assert_allclose(x, want, rtol=1e-13, atol=1e-15)
+    hAp, hAi = layout.Ap.cpu().numpy(), layout.Ai.cpu().numpy()
+    assert hAp.tolist() == [0, 1, 3, 5, 8, 11, 12, 16] and layout.nnz == 16
+    assert all(hAi[hAp[i + 1] - 1] == i for i in range(len(rows)))            # diagonal last
+    assert layout.perm.cpu().numpy()[:len(Ai)].tolist()[4:8] == [-1, 5, 7, 6]   # the later diagonal entry wins
+    bad = Ai.copy()
+    bad[1] = 4                                                                 # right of the diagonal
+    with pytest.raises(NativeError) as err:
+        ops.gs_layout(dev(Ap, np.int32), dev(bad, np.int32), separate_diagonal=False)
+    assert err.value.code == ERR_INDEX_RANGE
+    with pytest.raises(NativeError) as err:                                    # a diagonal entry in "separate" form
+        ops.gs_layout(dev(Ap, np.int32), dev(Ai, np.int32), separate_diagonal=True)
+    assert err.value.code == ERR_INDEX_RANGE
+    empty = ops.gs_layout(dev([0], np.int32), dev([], np.int32), separate_diagonal=True)
+    assert empty.nnz == 0
+
+
 def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch):
     """A long dependence chain (5-6 rows per level) through the decorator: the inspector's level
     count sends the sync-free launcher to the block-recurrence chain solver; the block tiles are

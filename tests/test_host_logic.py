@@ -201,6 +201,16 @@ def test_decoration_recognises_the_demo_operators():
     assert ilu.cuda_lowering.lifted_loop_parameters == ["n"]      # reference test_spilu0_codegen.py:104
     assert [l.name for l in ilu.structural_lookups] == ["_lcd_lookup_position_0"]
     assert od.simple_sptrsv_csr.original_function(np.array([0, 1]), np.array([0]), np.array([2.0]), np.array([1.0]), 1)[0] == 0.5
+    # Gauss-Seidel: the block loop sits inside a host sweep loop that the launcher runs; argument
+    # order as the reference generates it (golden fixture written by the reference itself)
+    g = golden("gauss_seidel_lap2d_g8")
+    gs = od.simple_gauss_seidel_csr.cuda_lowering
+    assert gs.operator == "gauss_seidel_simple_csr" and gs.host_loop_iterators == ("sweep",)
+    assert gs.launcher_arguments == g["simple/launcher_arguments"].tolist() and gs.lifted_variables == []
+    assert gs.roles["diagonal"] == "D" and gs.entry_point == "lcd_sptrsv_wavefront"
+    full = od.full_gauss_seidel_csr.cuda_lowering
+    assert full.operator == "gauss_seidel_full_csr" and "diagonal" not in full.roles
+    assert full.launcher_arguments == g["full/launcher_arguments"].tolist()
     for attr in ("build_dag", "build_execution_data", "prepare_cuda_arguments", "schedule_plan", "schedule_call",
                  "schedule_space", "scheduler", "dag_plan", "dag_source", "execution_mode", "structural_lookups",
                  "reduction_statements", "cuda_kernel", "cuda_launcher", "cuda_source"):

@@ -61,6 +61,27 @@ def test_sptrsv_matches_undecorated_reference(oracle, name):
     np.testing.assert_array_equal(x, g["x_csc"])
 
 
+@pytest.mark.parametrize("name", golden_names("gauss_seidel_"))
+def test_gauss_seidel_matches_reference(oracle, name):
+    """Inspector arrays and sweep results of the reference's Gauss-Seidel demo operators."""
+    g = golden(name)
+    for variant in ("simple", "full"):
+        d = oracle.dag_build("csr_lower_rows", g[variant + "_Ap"], g[variant + "_Ai"])
+        _check_dag(d, g, variant + "/")
+    sweeps = int(g["max_iter"])
+    x = oracle.gauss_seidel_simple_csr(g["simple_Ap"], g["simple_Ai"], g["simple_Ax"], g["D"], g["b"],
+                                       g["x0"], sweeps)
+    np.testing.assert_array_equal(x, g["x_simple"])     # same arithmetic, same order: bit-exact
+    x = oracle.gauss_seidel_full_csr(g["full_Ap"], g["full_Ai"], g["full_Ax"], g["b"], g["x0"], sweeps)
+    np.testing.assert_array_equal(x, g["x_full"])
+    # no sweep leaves the start vector alone; sweeps of a triangular system repeat themselves
+    start = np.linspace(-1.0, 1.0, len(g["b"]))
+    np.testing.assert_array_equal(
+        oracle.gauss_seidel_full_csr(g["full_Ap"], g["full_Ai"], g["full_Ax"], g["b"], start, 0), start)
+    np.testing.assert_array_equal(
+        oracle.gauss_seidel_full_csr(g["full_Ap"], g["full_Ai"], g["full_Ax"], g["b"], start, 1), g["x_full"])
+
+
 @pytest.mark.parametrize("name", ILU)
 def test_ilu0_matches_reference(oracle, name):
     g = golden(name)
