@@ -155,6 +155,42 @@ def main():
         np.savez_compressed(os.path.join(out_dir, f"gauss_seidel_{name}.npz"), **out)
         print("wrote gauss_seidel", name)
 
+    # ---- Matrix Market ingestion + regularisation (compiler/demo/matrix.py:26-81) ------
+    # Synthetic files (no matrix collection is shipped): the file text and what the
+    # reference's loader makes of it.
+    from compiler.demo.matrix import load_matrix_market as reference_loader
+    from lcd_b200.matrix_market import write_matrix_market
+    import tempfile
+    rng = np.random.default_rng(11)
+    base = sp.random(40, 40, density=0.12, random_state=12, format="coo")
+    base.data = rng.uniform(-3.0, 3.0, base.nnz)
+    sym = sp.random(30, 30, density=0.15, random_state=13, format="csr")
+    sym = sym + sym.T + sp.diags(rng.uniform(0.0, 1.0, 30))
+    files = {"general": dict(matrix=base, comment="synthetic, with an explicit zero"),
+             "symmetric": dict(matrix=sym, symmetric=True),
+             "pattern": dict(matrix=sp.csr_matrix(np.tril(rng.uniform(0, 1, (12, 12)) < 0.4)), pattern=True)}
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, options in files.items():
+            path = os.path.join(tmp, name + ".mtx")
+            write_matrix_market(path, **options)
+            text = open(path).read()
+            if name == "general":       # repeated position and an explicit zero entry
+                lines = text.splitlines()
+                head, entries = lines[:3], lines[3:]
+                entries += [entries[0], "5 7 0.0"]
+                head[2] = f"40 40 {len(entries)}"
+                text = "\n".join(head + entries) + "\n"
+                open(path, "w").write(text)
+            out[name + "/text"] = np.frombuffer(text.encode(), dtype=np.uint8)
+            for size in (0, 16):
+                got = reference_loader(path, size)
+                out[f"{name}/n{size}/indptr"] = got.indptr
+                out[f"{name}/n{size}/indices"] = got.indices
+                out[f"{name}/n{size}/data"] = got.data
+    np.savez_compressed(os.path.join(out_dir, "matrix_market_cases.npz"), **out)
+    print("wrote matrix_market_cases")
+
     # ---- ILU0 CSR ---------------------------------------------------------
     ilu_inputs = {"lap3d_g4": gen.laplacian3d_ilu0(4, seed=5)[0]}
     rnd = sp.random(90, 90, density=0.08, random_state=6, format="csr")

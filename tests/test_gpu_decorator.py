@@ -162,6 +162,36 @@ def test_gauss_seidel_layout_edge_cases(cuda, oracle):
     assert empty.nnz == 0
 
 
+def test_demos_on_a_matrix_market_file(cuda, tmp_path, capsys):
+    """The three demos end to end on a file (the reference's E2E tests load theirs the same way,
+    compiler/e2e_tests/gpu_test_utils.py:24-33): CSR and CSC solves against SciPy, ILU0 and the
+    Gauss-Seidel sweeps against the sequential loops, and the command line."""
+    import scipy.sparse as sp
+    from lcd_b200 import demos
+    from lcd_b200.matrix_market import write_matrix_market
+    rng = np.random.default_rng(5)
+    pattern = sp.random(300, 300, density=0.03, random_state=6, format="csr")
+    pattern = pattern + pattern.T + sp.identity(300)
+    pattern.data = rng.uniform(-5.0, 5.0, pattern.nnz)
+    path = tmp_path / "synthetic.mtx"
+    write_matrix_market(path, pattern)
+    solves = demos.run_sptrsv(path, 0, "both")
+    np.testing.assert_allclose(solves["csr"], np.linspace(1.0, 2.0, 300), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(solves["csc"], solves["csr"], rtol=1e-10, atol=1e-12)
+    assert demos.run_sptrsv(path, 128, "csr")["csr"].shape == (128,)          # leading principal sample
+    for mode in ("wavefront", "sync_free"):
+        demos.run_spilu0(path, 0, mode)
+    sweeps = demos.run_gauss_seidel(path, 0, "both", 2)
+    np.testing.assert_allclose(sweeps["simple"], np.linspace(1.0, 2.0, 300), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(sweeps["full"], sweeps["simple"], rtol=1e-10, atol=1e-12)
+    demos.main(["gauss-seidel", str(path), "--max-n", "64", "--variant", "full", "--iterations", "3"])
+    printed = capsys.readouterr().out
+    errors = [float(line.rsplit("=", 1)[1]) for line in printed.splitlines() if "max_abs_error" in line]
+    assert len(errors) == 8 and max(errors) <= 1e-12
+    with pytest.raises(SystemExit):
+        demos.main(["sptrsv", str(path), "--max-n", "-1"])
+
+
 def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch):
     """A long dependence chain (5-6 rows per level) through the decorator: the inspector's level
     count sends the sync-free launcher to the block-recurrence chain solver; the block tiles are

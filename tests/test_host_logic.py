@@ -318,6 +318,53 @@ def test_runtime_prepare_and_execute_with_fake_backend():
         rt.prepare_cuda_arguments(low, dict(Ap=Ap, Ai=Ai, Ax=Ax, b=b, n=2), object(), {"np": np}, fake)
 
 
+# ---- Matrix Market ingestion ------------------------------------------------------
+def test_matrix_market_loader_matches_the_reference(tmp_path):
+    """Files written by the fixture generator, expected arrays by the reference's
+    ``load_matrix_market`` (compiler/demo/matrix.py:26-81); plus its error behaviour."""
+    import scipy.sparse as sp
+    from lcd_b200.matrix_market import load_matrix_market, read_matrix_market, write_matrix_market
+    g = golden("matrix_market_cases")
+    for name in ("general", "symmetric", "pattern"):
+        path = tmp_path / (name + ".mtx")
+        path.write_bytes(g[name + "/text"].tobytes())
+        for size in (0, 16):
+            got = load_matrix_market(path, size)
+            assert sp.issparse(got) and got.format == "csr" and got.dtype == np.float64
+            np.testing.assert_array_equal(got.indptr, g[f"{name}/n{size}/indptr"])
+            np.testing.assert_array_equal(got.indices, g[f"{name}/n{size}/indices"])
+            np.testing.assert_allclose(got.data, g[f"{name}/n{size}/data"], rtol=1e-15, atol=0)
+            dense = got.toarray()
+            off = np.abs(dense).sum(axis=1) - np.abs(np.diag(dense))
+            np.testing.assert_allclose(np.diag(dense), off + 1.0)           # strictly dominant
+            assert np.abs(dense - np.diag(np.diag(dense))).max() <= 1.0     # scaled
+    rows, cols, values, shape = read_matrix_market(tmp_path / "symmetric.mtx")
+    assert shape == (30, 30) and len(rows) == len(cols) == len(values)
+    with pytest.raises(ValueError, match="nonnegative"):
+        load_matrix_market(tmp_path / "general.mtx", -1)
+    with pytest.raises(FileNotFoundError):
+        load_matrix_market(tmp_path / "missing.mtx")
+    with pytest.raises(FileNotFoundError):
+        load_matrix_market()
+    (tmp_path / "dense.mtx").write_text("%%MatrixMarket matrix array real general\n2 2\n1\n2\n3\n4\n")
+    with pytest.raises(ValueError, match="sparse"):
+        load_matrix_market(tmp_path / "dense.mtx")
+    (tmp_path / "rect.mtx").write_text("%%MatrixMarket matrix coordinate real general\n2 3 1\n1 1 1.0\n")
+    with pytest.raises(ValueError, match="square"):
+        load_matrix_market(tmp_path / "rect.mtx")
+    (tmp_path / "cplx.mtx").write_text("%%MatrixMarket matrix coordinate complex general\n1 1 1\n1 1 1.0 0.0\n")
+    with pytest.raises(ValueError, match="Complex"):
+        load_matrix_market(tmp_path / "cplx.mtx")
+    (tmp_path / "zero.mtx").write_text("%%MatrixMarket matrix coordinate real general\n3 3 1\n1 2 0.0\n")
+    with pytest.raises(ValueError, match="empty"):
+        load_matrix_market(tmp_path / "zero.mtx")
+    write_matrix_market(tmp_path / "skew.mtx", sp.csr_matrix(np.array([[0, 0], [2.0, 0]])))
+    text = (tmp_path / "skew.mtx").read_text().replace("general", "skew-symmetric")
+    (tmp_path / "skew.mtx").write_text(text)
+    rows, cols, values, _ = read_matrix_market(tmp_path / "skew.mtx")
+    assert sorted(zip(rows.tolist(), cols.tolist(), values.tolist())) == [(0, 1, -2.0), (1, 0, 2.0)]
+
+
 # ---- generators ---------------------------------------------------------------
 def test_generators_have_the_documented_shapes():
     from lcd_b200 import generators as gen
