@@ -20,20 +20,25 @@
 //     polling x in global memory (a solution vector pre-filled with a reserved NaN is its
 //     own ready flag); operands that lie in the chunk, three or more blocks back, go into
 //     a shared-memory list (one column-major strip per block, so a warp reads it without
-//     bank conflicts and with one trip count);
-//   helpers (5 warps, blocks b mod 5): finish y_b - subtract the listed operands, polling
-//     the chunk's x in shared memory, then apply D_b^-1 held in registers;
+//     bank conflicts and with one trip count); blocks whose rows are complete when the
+//     chunk's turn comes near and that have no listed operand get their y_b right there;
+//   helpers (5 warps, blocks b mod 5): y_b of the remaining blocks - subtract the listed
+//     operands, polling the chunk's x in shared memory, then apply D_b^-1 held in registers;
 //   main warp and partner warp: the partner computes z_b = -W2_b x_b-2 one step ahead, the
 //     main warp x_b = y_b + z_b - W1_b x_b-1; they hand over through named barriers; the W
 //     tiles are streamed into a shared-memory ring by bulk asynchronous copies (one lane
 //     of the last warp keeps the ring full) and the previous blocks are read from shared
-//     memory as broadcasts;
+//     memory as broadcasts.  (Splitting the main warp's 32 columns over four warps was
+//     measured slower: the per-block bookkeeping, not the multiply-adds, is what a lone
+//     warp spends its issue slots on.);
 //   every wait is bounded; a failed wait raises an error and poisons the rest of the chunk
 //     with NaN so that later chunks do not wait for it.
 //
 // The result differs from plain substitution only by rounding; the relative residual
-// stays at the 1e-16 level for diagonally dominant blocks.  Callers that need the
-// sequential order use the LCD_SOLVE_EXACT path of lcd_sptrsv_csr_syncfree instead.
+// stays at the 1e-16 level for diagonally dominant blocks.  Operands from earlier chunks
+// are subtracted in the order they arrive, so two runs can differ in the last bits.
+// Callers that need the sequential order, bit for bit, use the LCD_SOLVE_EXACT path of
+// lcd_sptrsv_csr_syncfree instead.
 #include "common.cuh"
 
 namespace lcd {
@@ -261,7 +266,7 @@ csr_chain_kernel(const ChainParams q) {
     double *sx = sxh + kChainHalo;                               // x of the chunk (chunk-local index)
     double *sacc = sx + kChainRows + 2;                          // partial sums after phase A
     double *sy = sacc + kChainRows;                              // y_b, produced by the helpers
-    double *eval = sy + kChainRows;                              // in-chunk operands: values
+    double *eval = sy + kChainRows + 32;                         // in-chunk operands: values
     int *ecol = reinterpret_cast<int *>(eval + q.cap);           // ... and chunk-local columns
     __shared__ unsigned long long s_full[kChainStages];
     __shared__ unsigned long long s_empty[kChainStages];
@@ -271,11 +276,12 @@ csr_chain_kernel(const ChainParams q) {
     __shared__ int s_width[kChainBlocks];
     __shared__ int s_bptr[kChainBlocks + 1];
     __shared__ double s_z[2][32];
+    __shared__ int s_early[kChainBlocks];                      // y_b was computed in phase A
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     volatile int *failed_flag = &s_failed;
     if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; s_tiles = 0; }
     if (tid == kChainThreads - 32) {
-        for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 2); }
+        for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 1); }
         mbar_init_fence();
     }
     __syncthreads();
@@ -430,7 +436,7 @@ csr_chain_kernel(const ChainParams q) {
         for (long long off = (long long)tid * 128; off < bytes; off += (long long)kChainThreads * 128)
             chain_prefetch_l2(src + off);
     }
-    while (!failed) {
+    auto sweep = [&]() {   // one pass over what is still pending; true when something is left
         bool any = false;
 #pragma unroll
         for (int k = kChainRowsPerThread - 1; k >= 0; --k) {
@@ -460,9 +466,45 @@ csr_chain_kernel(const ChainParams q) {
             pend_[k] = mask;
             any |= mask != 0;
         }
-        if (!any) break;
+        return any;
+    };
+    bool left_over = !failed && sweep();
+    // Blocks whose rows are complete now, several chunks before the chunk's turn, and that
+    // have no operand inside the chunk get their y_b right here, from the warp that holds
+    // their rows: the helper warps then have (almost) nothing to do while the main warp
+    // runs, and a busy helper costs the main warp about a third of its speed (they share
+    // the shuffle/load pipe).
+#pragma unroll
+    for (int k = 0; k < kChainRowsPerThread; ++k) {
+        const int blk = warp + 8 * k;
+        const int local = tid + k * kChainWorkers;
+        const bool ready = !failed && pend_[k] == 0;
+        bool early = false;
+        if (blk < nblk && !overflow && s_width[blk] == 0 && __all_sync(kFullMask, ready)) {
+            // (operands through shared memory, not shuffles: the lanes may still run as
+            // separate groups after the sweep's per-lane loops)
+            sacc[local] = local < rows_here ? acc_[k] : 0.0;
+            __syncwarp();
+            const double *mrow = wsc + (long long)blk * kBlockDoubles + lane;
+            const double2 *tb = reinterpret_cast<const double2 *>(sacc + (local & ~31));
+            double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
+#pragma unroll
+            for (int c = 0; c < 32; c += 4) {
+                const double2 ta = tb[c / 2], tc = tb[c / 2 + 1];
+                y0 = fma(__ldg(mrow + (c + 0) * 32), ta.x, y0);
+                y1 = fma(__ldg(mrow + (c + 1) * 32), ta.y, y1);
+                y2 = fma(__ldg(mrow + (c + 2) * 32), tc.x, y2);
+                y3 = fma(__ldg(mrow + (c + 3) * 32), tc.y, y3);
+            }
+            sy[local] = publishable((y0 + y1) + (y2 + y3));
+            early = true;
+        }
+        if (lane == 0 && blk < kChainBlocks) s_early[blk] = early;
+    }
+    while (left_over && !failed) {
         if (dl.tick(p.status, row0 + tid)) { failed = true; break; }
         __nanosleep(100);
+        left_over = sweep();
     }
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
@@ -535,26 +577,28 @@ csr_chain_kernel(const ChainParams q) {
             }
             sxh[h * 32 + lane] = v;
             __syncwarp();
-            if (h == 0 || nblk > 1) pair_arrive(h ? kBarX1 : kBarX0);   // "x_-2 / x_-1 is there"
+            pair_arrive(h ? kBarX1 : kBarX0);               // "x_-2 / x_-1 is there"
         }
+        // Every instruction of this loop is on the critical path of the whole solve (a lone
+        // warp issues one about every four cycles), so it carries nothing it can do without:
+        // the partner releases the ring stages and reports its own failures through a NaN z,
+        // the barrier operations are unconditional (the partner runs two extra steps for them).
         double ynext = syv[lane];
         int tiles = 0;   // tiles known to have landed
-        for (int b = 0; b < nblk; ++b) {
-            const int base = b * 32, local = base + lane;
-            const bool active = local < rows_here;
-            const bool more = b + 1 < nblk;
-            const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+        const int step = upper ? -32 : 32;
+        double *xout = p.x + (upper ? p.n - 1 - (row0 + lane) : row0 + lane);
+        const double2 *xa = reinterpret_cast<const double2 *>(sxh + 32);
+        for (int b = 0; b < nblk; ++b, xout += step, xa += 16) {
+            const int local = b * 32 + lane;
             const int s = b % kChainStages;
             if (!dead && tiles <= b)
                 dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
-                                  failed_flag, p.status, row0 + base);
+                                  failed_flag, p.status, row0 + local);
             double y = ynext;
             if (!dead && __any_sync(kFullMask, is_pending(y)))
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
-                                  p.status, row0 + base);
-            if (more) ynext = syv[local + 32];
-            dead = dead || *failed_flag != 0;
-            const double2 *xa = reinterpret_cast<const double2 *>(sx + base - 32);
+                                  p.status, row0 + local);
+            ynext = syv[local + 32];   // (one block of slack behind sy keeps this in bounds)
             const double2 *w1 = ring2 + s * kTileDoubles + lane;
             double a0 = y, a1 = 0.0, a2 = 0.0, a3 = 0.0;
 #pragma unroll
@@ -569,14 +613,14 @@ csr_chain_kernel(const ChainParams q) {
             pair_sync(b & 1 ? kBarZ1 : kBarZ0);            // z_b = -W2_b x_b-2 from the partner
             const double z = s_z[b & 1][lane];
             const double val = dead ? nanv : publishable(((a0 + a1) + (a2 + a3)) + z);
+            const bool active = local < rows_here;
             sxv[local] = active ? val : 0.0;
             if (active) {
-                st_relaxed_f64(p.x + r, val);
+                st_relaxed_f64(xout, val);
                 if (p.trace) p.trace[row0 + local] = clock64();
             }
             __syncwarp();
-            if (b + 2 < nblk) pair_arrive(b & 1 ? kBarX1 : kBarX0);   // "x_b is there"
-            mbar_arrive_lane0(&s_empty[s], lane);
+            pair_arrive(b & 1 ? kBarX1 : kBarX0);          // "x_b is there"
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
@@ -584,14 +628,20 @@ csr_chain_kernel(const ChainParams q) {
     }
     if (warp == 1) {
         // ---- partner warp: z_k = -W2_k x_k-2, one step ahead of the main warp ------------
+        // It also releases the ring stages: once x_k-2 is published the main warp is done
+        // with tile k-2 (and this warp was done with it two steps ago).  Two extra steps at
+        // the end only take the main warp's last two barrier arrivals.
         bool dead = false;
         int tiles = 0;
-        for (int k = 0; k < nblk; ++k) {
+        const double nanv = __longlong_as_double(kCanonicalNaN);
+        for (int k = 0; k < nblk + 2; ++k) {
             const int s = k % kChainStages;
-            if (!dead && tiles <= k)
+            if (k < nblk && !dead && tiles <= k)
                 dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > k; }, dl,
                                   failed_flag, p.status, row0 + k * 32);
             pair_sync(k & 1 ? kBarX1 : kBarX0);            // x_k-2 is in shared memory
+            if (k >= 2) mbar_arrive_lane0(&s_empty[(k - 2) % kChainStages], lane);
+            if (k >= nblk) continue;
             const double2 *xb = reinterpret_cast<const double2 *>(sx + k * 32 - 64);
             const double2 *w2 = ring2 + s * kTileDoubles + kTileDoubles / 2 + lane;
             double c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
@@ -604,11 +654,10 @@ csr_chain_kernel(const ChainParams q) {
                 c2 = fma(-u1.x, v1.x, c2);
                 c3 = fma(-u1.y, v1.y, c3);
             }
-            s_z[k & 1][lane] = (c0 + c1) + (c2 + c3);
+            s_z[k & 1][lane] = dead ? nanv : (c0 + c1) + (c2 + c3);   // a failure travels as NaN
             if (dead && lane == 0) *failed_flag = 1;
             __syncwarp();
             pair_arrive(k & 1 ? kBarZ1 : kBarZ0);
-            mbar_arrive_lane0(&s_empty[s], lane);
         }
         return;
     }
@@ -620,17 +669,23 @@ csr_chain_kernel(const ChainParams q) {
         const double *mbase = wsc + lane;
         double m[32];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) m[k] = __ldg(mbase + (long long)b * kBlockDoubles + k * 32);
+        for (int k = 0; k < 32; ++k)
+            m[k] = s_early[b] ? 0.0 : __ldg(mbase + (long long)b * kBlockDoubles + k * 32);
         for (; b < nblk; b += kChainHelpers) {
             const int base = b * 32, local = base + lane;
             const bool active = local < rows_here;
             const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
             // this warp's next inverse block is requested now and consumed one step later
             double mnext[32];
-            const bool more = b + kChainHelpers < nblk;
+            const bool more = b + kChainHelpers < nblk && !s_early[b + kChainHelpers];
 #pragma unroll
             for (int k = 0; k < 32; ++k)
                 mnext[k] = more ? __ldg(mbase + (long long)(b + kChainHelpers) * kBlockDoubles + k * 32) : 0.0;
+            if (s_early[b]) {
+#pragma unroll
+                for (int k = 0; k < 32; ++k) m[k] = mnext[k];
+                continue;
+            }
             double t0 = active ? sacc[local] : 0.0, t1 = 0.0;
             bool bad = *failed_flag != 0;
             if (!overflow) {
@@ -686,9 +741,9 @@ csr_chain_kernel(const ChainParams q) {
 }
 
 static size_t chain_smem_bytes(int *cap_out) {
-    const size_t limit = 227 * 1024 - 1024;  // static shared memory takes a few hundred bytes
+    const size_t limit = 227 * 1024 - 2048;  // static shared memory takes about 1.2 KB
     const size_t fixed = (size_t)kChainStages * 2 * kTileDoubles * 8 +
-                         ((size_t)kChainHalo + kChainRows + 2 + 2 * kChainRows) * 8;
+                         ((size_t)kChainHalo + kChainRows + 2 + 2 * kChainRows + 32) * 8;
     const size_t cap = ((limit - fixed) / 12) & ~(size_t)1;
     *cap_out = (int)cap;
     return fixed + cap * 12;
