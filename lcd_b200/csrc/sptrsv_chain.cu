@@ -58,21 +58,25 @@ constexpr int kStatusDone = 6;                        // status word: chunks fin
 constexpr unsigned kFullMask = 0xffffffffu;
 
 // ---- numeric preparation ------------------------------------------------------------
-// One warp per 32-row block walks the block's rows in order.  Row r of D^-1, W1 and W2
-// all satisfy the same recurrence  row_r = (rhs_r - sum_{k<r} D[r][k] row_k) / D[r][r]
-// with right-hand sides e_r, L_b,b-1[r][:] and L_b,b-2[r][:]; lane c carries column c of
-// the three rows.  Only the stored entries are visited: a row's entries are loaded 32 at
-// a time, the ones that matter are found with a ballot and handed round with shuffles.
-__global__ void __launch_bounds__(32)
+// Three warps per 32-row block, one per tile, each walking the block's rows in order.  Row r
+// of D^-1, W1 and W2 all satisfy the same recurrence
+//        row_r = (rhs_r - sum_{k<r} D[r][k] row_k) / D[r][r]
+// with right-hand sides e_r, L_b,b-1[r][:] and L_b,b-2[r][:]; lane c carries column c of the
+// warp's row.  Only the stored entries are visited: a row's entries are loaded 32 at a time,
+// the ones that matter to the warp are found with a ballot and handed round with shuffles.
+// (The recurrences do not read one another, so the warps never synchronise; three warps on
+// the latency-bound walk instead of one is what the split buys.)
+__global__ void __launch_bounds__(96)
 chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_blocks) {
-    __shared__ double M[32][33];
-    __shared__ double W1[32][33];
-    __shared__ double W2[32][33];
-    const int lane = threadIdx.x;
+    __shared__ double tiles[3][32][33];
+    const int lane = threadIdx.x & 31;
+    const int which = threadIdx.x >> 5;          // 0: D^-1, 1: W1 (block before), 2: W2 (two before)
+    double (*T)[33] = tiles[which];
     const int gb = blockIdx.x;
     if (gb >= n_blocks) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     const int base = gb * 32;
+    const int mine = which == 0 ? 3 : 3 - which;  // entry kind that feeds this tile's right-hand side
     int lo = 0, hi = 0;
     double diag = 1.0;  // rows past the end, and rows with bad pointers, act as identity rows
     {
@@ -104,7 +108,7 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_bloc
             if (nlo + lane < nhi) { pc = __ldg(p.Ai + nlo + lane); pa = __ldg(p.Ax + nlo + lane); }
         }
         const double d = __shfl_sync(kFullMask, diag, r);
-        double accM = lane == r ? 1.0 : 0.0, acc1 = 0.0, acc2 = 0.0;
+        double acc = (which == 0 && lane == r) ? 1.0 : 0.0;
         for (int j0 = rlo; j0 < rhi; j0 += 32) {
             if (j0 != rlo) {
                 cc = -1;
@@ -118,37 +122,29 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_bloc
                 const int off = tc - (base - 64);
                 if (off >= 0 && tc < base + r) { kind = 1 + (off >> 5); col = off & 31; }
             }
-            unsigned todo = __ballot_sync(kFullMask, kind != 0);
+            unsigned todo = __ballot_sync(kFullMask, kind == 3 || kind == mine);
             while (todo) {
                 const int src = __ffs(todo) - 1;
                 todo &= todo - 1;
                 const int kd = __shfl_sync(kFullMask, kind, src);
                 const int c = __shfl_sync(kFullMask, col, src);
                 const double av = __shfl_sync(kFullMask, ca, src);
-                if (kd == 3) {
-                    accM = fma(-av, M[c][lane], accM);
-                    acc1 = fma(-av, W1[c][lane], acc1);
-                    acc2 = fma(-av, W2[c][lane], acc2);
-                } else if (lane == c) {
-                    if (kd == 2) acc1 += av; else acc2 += av;
-                }
+                if (kd == 3) acc = fma(-av, T[c][lane], acc);
+                else if (lane == c) acc += av;
             }
         }
-        M[r][lane] = accM / d;
-        W1[r][lane] = acc1 / d;
-        W2[r][lane] = acc2 / d;
+        T[r][lane] = acc / d;
         __syncwarp();
     }
     // D^-1: element (r, k) at k * 32 + r (a helper lane r loads its row coalesced);
     // W tiles: elements (r, 2q) and (r, 2q + 1) side by side at (q * 32 + r) * 2, so that the
     // main warp's lane r reads its row with 16-byte loads that do not conflict
-    double *out = ws + (long long)gb * kBlockDoubles;
-    for (int k = 0; k < 32; ++k) out[k * 32 + lane] = M[lane][k];
-    double2 *o1 = reinterpret_cast<double2 *>(out + kTileDoubles);
-    double2 *o2 = reinterpret_cast<double2 *>(out + 2 * kTileDoubles);
-    for (int q = 0; q < 16; ++q) {
-        o1[q * 32 + lane] = make_double2(W1[lane][2 * q], W1[lane][2 * q + 1]);
-        o2[q * 32 + lane] = make_double2(W2[lane][2 * q], W2[lane][2 * q + 1]);
+    double *out = ws + (long long)gb * kBlockDoubles + which * kTileDoubles;
+    if (which == 0) {
+        for (int k = 0; k < 32; ++k) out[k * 32 + lane] = T[lane][k];
+    } else {
+        double2 *o = reinterpret_cast<double2 *>(out);
+        for (int q = 0; q < 16; ++q) o[q * 32 + lane] = make_double2(T[lane][2 * q], T[lane][2 * q + 1]);
     }
 }
 
@@ -782,7 +778,7 @@ extern "C" int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, cons
     const int n_blocks = (n + 31) / 32;
     CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, nullptr, nullptr, flags, 1, 1, nullptr,
                      0, nullptr, 0, n, nullptr, {nullptr}};
-    chain_prepare_kernel<<<n_blocks, 32, 0, (cudaStream_t)stream>>>(p, static_cast<double *>(workspace),
+    chain_prepare_kernel<<<n_blocks, 96, 0, (cudaStream_t)stream>>>(p, static_cast<double *>(workspace),
                                                                     n_blocks);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
