@@ -92,6 +92,12 @@ def algorithmic_bytes(n, nnz):
     return nnz * 12 + (n + 1) * 4 + n * 16
 
 
+# DRAM traffic per row of the dominant kernel (dram__bytes_read.sum + dram__bytes_write.sum of one
+# ncu capture at 1,048,576 rows divided by the rows; both kernels' traffic grows in proportion to
+# the rows, so a launch on n rows is charged n times this; see profiles/)
+TRAFFIC_BYTES_PER_ROW = {"csr_chain_kernel": 1.311e9 / 1048576, "csr_syncfree_row_kernel": 227.3e6 / 1048576}
+
+
 def flops(n, nnz):
     return n + 2 * nnz
 
@@ -315,7 +321,11 @@ def run_native(args):
                            algorithmic_bytes(n, nnz) / 1e9)},
             "e2e": e2e, "gpu_launches": args.steps * launches_per_step,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / peak,
+                         "traffic": (TRAFFIC_BYTES_PER_ROW[kernel_name] * n
+                                     if args.workload.startswith("sptrsv_random") else None),
+                         "traffic_source": "ncu capture at n=1048576 scaled by rows",
+                         "peak_kind": peak_kind,
                          "kernel": kernel_name,
                          "kernel_ms": extras.get("solve_ms", kernel_ms)},
             "cpu_baseline": cpu_baseline, "clocks": clocks,

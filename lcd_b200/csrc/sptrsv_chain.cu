@@ -41,6 +41,8 @@
 // lcd_sptrsv_csr_syncfree instead.
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace lcd {
 
 constexpr int kChainThreads = 256;                    // main warp, six helper warps, loader warp
@@ -253,6 +255,7 @@ struct ChainParams {
     int cap;  // capacity of the in-chunk operand list (entries)
 };
 
+template <bool TRACE>
 __global__ void __launch_bounds__(kChainThreads, 1)
 csr_chain_kernel(const ChainParams q) {
     const CsrSolveParams &p = q.m;
@@ -557,7 +560,7 @@ csr_chain_kernel(const ChainParams q) {
         // ---- main warp: x_b = y_b + z_b - W1_b x_b-1 --------------------------------------
         // The loop always runs to the end and always performs its barrier operations (the
         // partner warp blocks on them); after a failed wait it only publishes NaN.
-        if (p.trace && lane == 0) p.trace[2ll * p.n + chunk] = clock64();
+        if (TRACE && lane == 0) p.trace[2ll * p.n + chunk] = clock64();
         const double nanv = __longlong_as_double(kCanonicalNaN);
         bool dead = *failed_flag != 0;
         // the two blocks before the chunk (the partner can start on z_0 as soon as the
@@ -584,16 +587,22 @@ csr_chain_kernel(const ChainParams q) {
         const int step = upper ? -32 : 32;
         double *xout = p.x + (upper ? p.n - 1 - (row0 + lane) : row0 + lane);
         const double2 *xa = reinterpret_cast<const double2 *>(sxh + 32);
-        for (int b = 0; b < nblk; ++b, xout += step, xa += 16) {
-            const int local = b * 32 + lane;
+        int local = lane;
+        // one step; PARITY is the block's parity, so that the barrier ids are immediates
+        auto step_block = [&](const int b, auto parity) {
+            constexpr int kParity = decltype(parity)::value;
             const int s = b % kChainStages;
-            if (!dead && tiles <= b)
+            if (!dead && tiles <= b) {
                 dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
                                   failed_flag, p.status, row0 + local);
+                if (dead) ynext = nanv;            // a failure travels as NaN from here on
+            }
             double y = ynext;
-            if (!dead && __any_sync(kFullMask, is_pending(y)))
+            if (!dead && __any_sync(kFullMask, is_pending(y))) {
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
                                   p.status, row0 + local);
+                if (dead) y = nanv;
+            }
             ynext = syv[local + 32];   // (one block of slack behind sy keeps this in bounds)
             const double2 *w1 = ring2 + s * kTileDoubles + lane;
             double a0 = y, a1 = 0.0, a2 = 0.0, a3 = 0.0;
@@ -606,17 +615,25 @@ csr_chain_kernel(const ChainParams q) {
                 a2 = fma(-u1.x, v1.x, a2);
                 a3 = fma(-u1.y, v1.y, a3);
             }
-            pair_sync(b & 1 ? kBarZ1 : kBarZ0);            // z_b = -W2_b x_b-2 from the partner
-            const double z = s_z[b & 1][lane];
-            const double val = dead ? nanv : publishable(((a0 + a1) + (a2 + a3)) + z);
-            const bool active = local < rows_here;
-            sxv[local] = active ? val : 0.0;
-            if (active) {
+            pair_sync(kParity ? kBarZ1 : kBarZ0);          // z_b = -W2_b x_b-2 from the partner
+            const double z = s_z[kParity][lane];
+            // (a sum is never the reserved all-ones pattern: arithmetic returns the canonical NaN)
+            const double val = ((a0 + a1) + (a2 + a3)) + z;
+            sxv[local] = val;       // (rows past the end: their W rows and y are zero, so is val)
+            if (local < rows_here) {
                 st_relaxed_f64(xout, val);
-                if (p.trace) p.trace[row0 + local] = clock64();
+                if (TRACE) p.trace[row0 + local] = clock64();
             }
             __syncwarp();
-            pair_arrive(b & 1 ? kBarX1 : kBarX0);          // "x_b is there"
+            pair_arrive(kParity ? kBarX1 : kBarX0);        // "x_b is there"
+            xout += step;
+            xa += 16;
+            local += 32;
+        };
+        if (dead) ynext = nanv;
+        for (int b = 0; b < nblk; b += 2) {
+            step_block(b, std::integral_constant<int, 0>());
+            if (b + 1 < nblk) step_block(b + 1, std::integral_constant<int, 1>());
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
@@ -804,9 +821,9 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
         q.ws = static_cast<const double *>(workspace);
         const size_t smem = chain_smem_bytes(&q.cap);
         // the attribute belongs to the current device's copy of the function
-        LCD_CUDA_TRY(cudaFuncSetAttribute(csr_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-        csr_chain_kernel<<<(n + kChainRows - 1) / kChainRows, kChainThreads, smem, st>>>(q);
+        auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
+        LCD_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        kernel<<<(n + kChainRows - 1) / kChainRows, kChainThreads, smem, st>>>(q);
         LCD_CUDA_TRY(cudaGetLastError());
     }
     return finish(status_dev, st, status_host);
