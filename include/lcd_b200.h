@@ -171,6 +171,9 @@ int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int
  * lcd_sptrsv_csr_syncfree.
  */
 int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes);
+/* Diagnostic: blocks per thread-block cluster of the last lcd_sptrsv_csr_chain launch of this
+ * process (8 where the device hosts such clusters, else 1; 0 before the first launch). */
+int lcd_chain_cluster_size(void);
 int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
                       const double *Ax, const int32_t *diag_pos, int flags, void *workspace,
                       int64_t workspace_bytes, void *stream);

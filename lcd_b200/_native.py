@@ -55,6 +55,7 @@ _SIGNATURES = {
                               _P, c_int64, _P, _P, ctypes.POINTER(c_int)]),
     "lcd_gs_values": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P]),
     "lcd_chain_workspace_bytes": (c_int, [c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_chain_cluster_size": (c_int, []),
     "lcd_chain_prepare": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, c_int64, _P]),
     "lcd_sptrsv_csr_chain": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P, c_int64,
                                      _P, c_int32, _P, ctypes.POINTER(c_int)]),

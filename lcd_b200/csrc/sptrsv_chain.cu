@@ -56,6 +56,7 @@ constexpr int kTileDoubles = 1024;
 constexpr int kBlockDoubles = 3 * kTileDoubles;       // per 32-row block: D^-1, W1, W2
 constexpr int kChainHalo = 64;                        // the two blocks before the chunk
 constexpr int kChainGate = 3;                         // chunks ahead at which pending operands are polled
+constexpr int kChainCluster = 8;                      // blocks per cluster (portable maximum)
 constexpr int kStatusDone = 6;                        // status word: chunks finished
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -248,6 +249,38 @@ __device__ __forceinline__ bool warp_wait(Ready ready, Deadline &dl, volatile in
     }
 }
 
+// ---- thread-block cluster plumbing ------------------------------------------------------
+// Consecutive chunks run on the blocks of one cluster, so that the hand-over between them (the
+// two blocks of x before a chunk) is a store into the next block's shared memory instead of a
+// round trip through L2.
+__device__ __forceinline__ unsigned cluster_ctarank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned cluster_nctarank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// address of the same shared-memory location in another block of the cluster
+__device__ __forceinline__ unsigned cluster_map(const void *ptr, unsigned rank) {
+    unsigned out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(ptr)), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void st_cluster_f64(unsigned addr, double v) {
+    asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
+}
+__device__ __forceinline__ int ld_cluster_s32(unsigned addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 // ---- the solve ---------------------------------------------------------------------------
 struct ChainParams {
     CsrSolveParams m;
@@ -265,7 +298,9 @@ csr_chain_kernel(const ChainParams q) {
     double *sx = sxh + kChainHalo;                               // x of the chunk (chunk-local index)
     double *sacc = sx + kChainRows + 2;                          // partial sums after phase A
     double *sy = sacc + kChainRows;                              // y_b, produced by the helpers
-    double *eval = sy + kChainRows + 32;                         // in-chunk operands: values
+    unsigned long long *spend = reinterpret_cast<unsigned long long *>(sy + kChainRows + 32);  // operands from
+                                                                 // before the chunk still pending per row
+    double *eval = reinterpret_cast<double *>(spend + kChainRows);  // in-chunk operands: values
     int *ecol = reinterpret_cast<int *>(eval + q.cap);           // ... and chunk-local columns
     __shared__ unsigned long long s_full[kChainStages];
     __shared__ unsigned long long s_empty[kChainStages];
@@ -278,13 +313,25 @@ csr_chain_kernel(const ChainParams q) {
     __shared__ int s_early[kChainBlocks];                      // y_b was computed in phase A
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     volatile int *failed_flag = &s_failed;
-    if (tid == 0) { s_chunk = atomicAdd(&p.status[kStatusTicket], 1); s_failed = 0; s_tiles = 0; }
+    // One ticket per cluster: its blocks take consecutive chunks.  (A cluster is resident as a
+    // whole, and a chunk still only waits for chunks with smaller numbers.)
+    const unsigned crank = cluster_ctarank(), csize = cluster_nctarank();
+    if (tid == 0) {
+        if (crank == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1) * (int)csize;
+        s_failed = 0;
+        s_tiles = 0;
+    }
+    if (tid < kChainHalo) reinterpret_cast<unsigned long long *>(sxh)[tid] = kPendingBits;
     if (tid == kChainThreads - 32) {
         for (int s = 0; s < kChainStages; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], 1); }
         mbar_init_fence();
     }
     __syncthreads();
-    const int chunk = s_chunk;
+    if (csize > 1) cluster_barrier();   // ticket and halo sentinels are in place everywhere
+    const int chunk = (csize > 1 ? ld_cluster_s32(cluster_map(&s_chunk, 0)) : s_chunk) + (int)crank;
+    // (the body is a lambda so that every thread, whatever its role, comes back to the closing
+    // cluster barrier: no block may leave while a neighbour can still store into it)
+    auto body = [&]() {
     const int row0 = chunk * kChainRows;
     const int rows_here = min(kChainRows, p.n - row0);
     if (rows_here <= 0) return;
@@ -500,15 +547,15 @@ csr_chain_kernel(const ChainParams q) {
         }
         if (lane == 0 && blk < kChainBlocks) s_early[blk] = early;
     }
-    while (left_over && !failed) {
-        if (dl.tick(p.status, row0 + tid)) { failed = true; break; }
-        __nanosleep(100);
-        left_over = sweep();
-    }
+    // What is still pending now (operands in the chunks just before this one) is left to the
+    // helper warp of the row's block: waiting for it here would hold back the main warp, whose
+    // first blocks rarely depend on it.
+    (void)left_over;
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
         const int local = tid + k * kChainWorkers;
         if (local < rows_here) sacc[local] = acc_[k];
+        spend[local] = local < rows_here ? pend_[k] : 0ull;
     }
     if (failed) *failed_flag = 1;
     workers_barrier();
@@ -560,7 +607,7 @@ csr_chain_kernel(const ChainParams q) {
         // ---- main warp: x_b = y_b + z_b - W1_b x_b-1 --------------------------------------
         // The loop always runs to the end and always performs its barrier operations (the
         // partner warp blocks on them); after a failed wait it only publishes NaN.
-        if (TRACE && lane == 0) p.trace[2ll * p.n + chunk] = clock64();
+        if (TRACE && lane == 0) { p.trace[2ll * p.n + chunk] = clock64(); p.trace[2ll * p.n + 65536 + 4 * chunk] = (long long)global_timer(); }
         const double nanv = __longlong_as_double(kCanonicalNaN);
         bool dead = *failed_flag != 0;
         // the two blocks before the chunk (the partner can start on z_0 as soon as the
@@ -571,8 +618,13 @@ csr_chain_kernel(const ChainParams q) {
             double v = 0.0;
             if (row0 > 0 && !dead) {   // (a chunk after the first has both blocks before it)
                 const int r = upper ? p.n - 1 - t : t;
-                dead = !warp_wait([&] { return !is_pending(v = ld_relaxed_f64(p.x + r)); }, dl,
-                                  failed_flag, p.status, r);
+                if (crank > 0) {       // the previous chunk's block stores them into this halo
+                    volatile double *mine = sxh + h * 32 + lane;
+                    dead = !warp_wait([&] { return !is_pending(v = *mine); }, dl, failed_flag, p.status, r);
+                } else {
+                    dead = !warp_wait([&] { return !is_pending(v = ld_relaxed_f64(p.x + r)); }, dl,
+                                      failed_flag, p.status, r);
+                }
             }
             sxh[h * 32 + lane] = v;
             __syncwarp();
@@ -582,6 +634,7 @@ csr_chain_kernel(const ChainParams q) {
         // warp issues one about every four cycles), so it carries nothing it can do without:
         // the partner releases the ring stages and reports its own failures through a NaN z,
         // the barrier operations are unconditional (the partner runs two extra steps for them).
+        if (TRACE && lane == 0) p.trace[2ll * p.n + 65536 + 4 * chunk + 1] = (long long)global_timer();
         double ynext = syv[lane];
         int tiles = 0;   // tiles known to have landed
         const int step = upper ? -32 : 32;
@@ -589,8 +642,11 @@ csr_chain_kernel(const ChainParams q) {
         const double2 *xa = reinterpret_cast<const double2 *>(sxh + 32);
         int local = lane;
         // one step; PARITY is the block's parity, so that the barrier ids are immediates
-        auto step_block = [&](const int b, auto parity) {
+        const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then nblk is 32)
+        const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + lane * 8 : 0u;
+        auto step_block = [&](const int b, auto parity, auto pushing) {
             constexpr int kParity = decltype(parity)::value;
+            constexpr bool kPush = decltype(pushing)::value;
             const int s = b % kChainStages;
             if (!dead && tiles <= b) {
                 dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
@@ -620,9 +676,10 @@ csr_chain_kernel(const ChainParams q) {
             // (a sum is never the reserved all-ones pattern: arithmetic returns the canonical NaN)
             const double val = ((a0 + a1) + (a2 + a3)) + z;
             sxv[local] = val;       // (rows past the end: their W rows and y are zero, so is val)
+            if (kPush) st_cluster_f64(next_halo + kParity * 256, val);   // the next chunk's halo
             if (local < rows_here) {
                 st_relaxed_f64(xout, val);
-                if (TRACE) p.trace[row0 + local] = clock64();
+                if (TRACE) { p.trace[row0 + local] = clock64(); if (lane == 0 && (b == 0 || b == nblk - 1)) p.trace[2ll * p.n + 65536 + 4 * chunk + (b == 0 ? 2 : 3)] = (long long)global_timer(); }
             }
             __syncwarp();
             pair_arrive(kParity ? kBarX1 : kBarX0);        // "x_b is there"
@@ -631,9 +688,14 @@ csr_chain_kernel(const ChainParams q) {
             local += 32;
         };
         if (dead) ynext = nanv;
-        for (int b = 0; b < nblk; b += 2) {
-            step_block(b, std::integral_constant<int, 0>());
-            if (b + 1 < nblk) step_block(b + 1, std::integral_constant<int, 1>());
+        const int plain = push ? nblk - 2 : nblk;   // the last two blocks also feed the neighbour
+        for (int b = 0; b < plain; b += 2) {
+            step_block(b, std::integral_constant<int, 0>(), std::false_type());
+            if (b + 1 < plain) step_block(b + 1, std::integral_constant<int, 1>(), std::false_type());
+        }
+        if (push) {
+            step_block(nblk - 2, std::integral_constant<int, 0>(), std::true_type());
+            step_block(nblk - 1, std::integral_constant<int, 1>(), std::true_type());
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
@@ -701,6 +763,25 @@ csr_chain_kernel(const ChainParams q) {
             }
             double t0 = active ? sacc[local] : 0.0, t1 = 0.0;
             bool bad = *failed_flag != 0;
+            unsigned long long mask = spend[local];
+            if (!bad && __any_sync(kFullMask, mask != 0)) {
+                // operands from before the chunk that had not been produced when phase A looked
+                int lo = 0, hi = 0, d = -1;
+                if (mask) csr_row_range(p, r, lo, hi, d);
+                bad = !warp_wait([&] {
+                    unsigned long long left = mask;
+                    for (int u = 0; u < 4 && left; ++u) {
+                        const int bit = __ffsll((long long)left) - 1;
+                        left &= left - 1;
+                        const double xv = ld_relaxed_f64(p.x + __ldg(p.Ai + lo + bit));
+                        if (!is_pending(xv)) {
+                            t0 = fma(-__ldg(p.Ax + lo + bit), xv, t0);
+                            mask &= ~(1ull << bit);
+                        }
+                    }
+                    return mask == 0;
+                }, dl, failed_flag, p.status, r);
+            }
             if (!overflow) {
                 const int width = s_width[b];
                 int pos = s_bptr[b] + lane;
@@ -751,12 +832,15 @@ csr_chain_kernel(const ChainParams q) {
             for (int k = 0; k < 32; ++k) m[k] = mnext[k];
         }
     }
+    };
+    body();
+    if (csize > 1) cluster_barrier();
 }
 
 static size_t chain_smem_bytes(int *cap_out) {
     const size_t limit = 227 * 1024 - 2048;  // static shared memory takes about 1.2 KB
     const size_t fixed = (size_t)kChainStages * 2 * kTileDoubles * 8 +
-                         ((size_t)kChainHalo + kChainRows + 2 + 2 * kChainRows + 32) * 8;
+                         ((size_t)kChainHalo + kChainRows + 2 + 3 * kChainRows + 32) * 8;
     const size_t cap = ((limit - fixed) / 12) & ~(size_t)1;
     *cap_out = (int)cap;
     return fixed + cap * 12;
@@ -765,6 +849,10 @@ static size_t chain_smem_bytes(int *cap_out) {
 }  // namespace lcd
 
 using namespace lcd;
+
+static int g_last_cluster = 0;
+
+extern "C" int lcd_chain_cluster_size(void) { return g_last_cluster; }
 
 extern "C" int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes) {
     if (n < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
@@ -823,7 +911,40 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
         // the attribute belongs to the current device's copy of the function
         auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
         LCD_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        kernel<<<(n + kChainRows - 1) / kChainRows, kChainThreads, smem, st>>>(q);
+        const int chunks = (n + kChainRows - 1) / kChainRows;
+        // clusters of up to eight blocks (consecutive chunks hand over through shared memory);
+        // where the device cannot host such a cluster the same kernel runs as plain blocks
+        int cluster = 1;
+        if (chunks > 1) {
+            cudaLaunchConfig_t probe = {};
+            probe.gridDim = dim3(kChainCluster);
+            probe.blockDim = dim3(kChainThreads);
+            probe.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = kChainCluster;
+            attr.val.clusterDim.y = attr.val.clusterDim.z = 1;
+            probe.attrs = &attr;
+            probe.numAttrs = 1;
+            int fit = 0;
+            if (cudaOccupancyMaxActiveClusters(&fit, kernel, &probe) == cudaSuccess && fit > 0)
+                cluster = kChainCluster;
+            else
+                cudaGetLastError();
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((chunks + cluster - 1) / cluster * cluster);
+        cfg.blockDim = dim3(kChainThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = cluster;
+        attr.val.clusterDim.y = attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        g_last_cluster = cluster;
+        LCD_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, q));
         LCD_CUDA_TRY(cudaGetLastError());
     }
     return finish(status_dev, st, status_host);
