@@ -644,19 +644,24 @@ csr_chain_kernel(const ChainParams q) {
         // one step; PARITY is the block's parity, so that the barrier ids are immediates
         const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then nblk is 32)
         const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + lane * 8 : 0u;
+        long long tile_wait_ = 0, y_wait_ = 0, z_wait_ = 0; int tile_waits_ = 0, y_waits_ = 0;
         auto step_block = [&](const int b, auto parity, auto pushing) {
             constexpr int kParity = decltype(parity)::value;
             constexpr bool kPush = decltype(pushing)::value;
             const int s = b % kChainStages;
             if (!dead && tiles <= b) {
+                long long c0_ = TRACE ? clock64() : 0;
                 dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
                                   failed_flag, p.status, row0 + local);
+                if (TRACE) { tile_wait_ += clock64() - c0_; ++tile_waits_; }
                 if (dead) ynext = nanv;            // a failure travels as NaN from here on
             }
             double y = ynext;
             if (!dead && __any_sync(kFullMask, is_pending(y))) {
+                long long c0_ = TRACE ? clock64() : 0;
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
                                   p.status, row0 + local);
+                if (TRACE) { y_wait_ += clock64() - c0_; ++y_waits_; }
                 if (dead) y = nanv;
             }
             ynext = syv[local + 32];   // (one block of slack behind sy keeps this in bounds)
@@ -671,7 +676,9 @@ csr_chain_kernel(const ChainParams q) {
                 a2 = fma(-u1.x, v1.x, a2);
                 a3 = fma(-u1.y, v1.y, a3);
             }
+            long long z0_ = TRACE ? clock64() : 0;
             pair_sync(kParity ? kBarZ1 : kBarZ0);          // z_b = -W2_b x_b-2 from the partner
+            if (TRACE) z_wait_ += clock64() - z0_;
             const double z = s_z[kParity][lane];
             // (a sum is never the reserved all-ones pattern: arithmetic returns the canonical NaN)
             const double val = ((a0 + a1) + (a2 + a3)) + z;
@@ -696,6 +703,10 @@ csr_chain_kernel(const ChainParams q) {
         if (push) {
             step_block(nblk - 2, std::integral_constant<int, 0>(), std::true_type());
             step_block(nblk - 1, std::integral_constant<int, 1>(), std::true_type());
+        }
+        if (TRACE && lane == 0) {
+            long long *o = p.trace + 2ll * p.n + 65536 + 4 * 8192 + 8 * chunk;
+            o[0] = tile_wait_; o[1] = tile_waits_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_;
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);

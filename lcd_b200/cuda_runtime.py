@@ -56,7 +56,14 @@ class DeviceArray:
         return tuple(self.tensor.shape)
 
     def copy_to_host(self):
-        return self.tensor.cpu().numpy()
+        # through page-locked memory: a copy into a fresh pageable array runs at a few GB/s
+        # (33 MB took 15 ms), the pinned pool of torch hands back recycled blocks
+        import torch
+        if self.tensor.numel() * self.tensor.element_size() < (1 << 20):
+            return self.tensor.cpu().numpy()
+        host = torch.empty(self.tensor.shape, dtype=self.tensor.dtype, pin_memory=True)
+        host.copy_(self.tensor)
+        return host.numpy()
 
     def __len__(self):
         return self.tensor.shape[0]
