@@ -14,16 +14,22 @@
 // 32 x 32 mat-vec (no dependent chain inside it), and everything that reaches at least
 // three blocks back is taken off that path.
 //
-// The solve kernel works on chunks of 1024 rows handed out by ticket (a chunk only waits
-// for chunks with smaller tickets, which are running or done, so the waits terminate):
+// The solve kernel works on chunks of 1024 rows.  It runs as thread-block clusters of eight
+// where the device hosts them: a cluster takes one ticket and its blocks take eight
+// consecutive chunks (a chunk only waits for chunks with smaller numbers, which are running
+// or done, so the waits terminate), and the hand-over between consecutive chunks of a
+// cluster goes through distributed shared memory instead of L2.
 //   phase A (256 threads, four rows each): operands from before the chunk are fetched by
 //     polling x in global memory (a solution vector pre-filled with a reserved NaN is its
-//     own ready flag); operands that lie in the chunk, three or more blocks back, go into
-//     a shared-memory list (one column-major strip per block, so a warp reads it without
-//     bank conflicts and with one trip count); blocks whose rows are complete when the
-//     chunk's turn comes near and that have no listed operand get their y_b right there;
-//   helpers (5 warps, blocks b mod 5): y_b of the remaining blocks - subtract the listed
-//     operands, polling the chunk's x in shared memory, then apply D_b^-1 held in registers;
+//     own ready flag) - once at launch, once more when the chunk's turn is near; what is
+//     missing even then is left to the helper of the row's block; operands that lie in the
+//     chunk, three or more blocks back, go into a shared-memory list (one column-major
+//     strip per block, so a warp reads it without bank conflicts and with one trip count);
+//     blocks whose rows are complete by then and that have no listed operand get their y_b
+//     right there;
+//   helpers (5 warps, blocks b mod 5): y_b of the remaining blocks - fetch the late operands,
+//     subtract the listed ones, polling the chunk's x in shared memory, then apply D_b^-1
+//     held in registers;
 //   main warp and partner warp: the partner computes z_b = -W2_b x_b-2 one step ahead, the
 //     main warp x_b = y_b + z_b - W1_b x_b-1; they hand over through named barriers; the W
 //     tiles are streamed into a shared-memory ring by bulk asynchronous copies (one lane
