@@ -228,6 +228,22 @@ int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_t *Ap, cons
                          int lanes_per_row, int32_t *status_dev, int32_t timeout_ms, void *stream,
                          int *status_host);
 
+/*
+ * The same solve over band chains, the reference's warp tasks with band_width > 1
+ * (compiler/dag_preprocessing.py:207-298, per-band launcher compiler/cuda_lowering.py:1022-1068):
+ * task t is the chain of nodes task_nodes[task_ptr[t] .. task_ptr[t+1]) (connected inside a
+ * band of consecutive levels, in level order) and is solved by one lane group, node after
+ * node; band k holds the tasks band_ptr[k] .. band_ptr[k+1]) and bands are separated like
+ * levels above.  task_ptr has n_tasks+1 entries, band_ptr n_bands+1 (device and host copy).
+ */
+int lcd_sptrsv_wavefront_tasks(int op, int32_t n, int64_t nnz, const int32_t *Ap,
+                               const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
+                               const double *b, double *x, int flags, const int32_t *task_nodes,
+                               const int32_t *task_ptr_dev, const int32_t *band_ptr_dev,
+                               const int32_t *band_ptr_host, int32_t n_bands, int mode,
+                               int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
+                               void *stream, int *status_host);
+
 /* Multi-RHS level-synchronous CSR solve on row-major n x nrhs blocks (nrhs <= 64): a warp
  * per row, lanes over right-hand sides, one cooperative launch.  The choice between this
  * and lcd_sptrsv_csr_syncfree_multi follows the level width (wide levels: this one). */

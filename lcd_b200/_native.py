@@ -69,6 +69,9 @@ _SIGNATURES = {
     "lcd_sptrsv_wavefront": (c_int, [c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P,
                                      _P, _P, c_int32, c_int, c_int, _P, c_int32, _P,
                                      ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_wavefront_tasks": (c_int, [c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int,
+                                           _P, _P, _P, _P, c_int32, c_int, c_int, _P, c_int32, _P,
+                                           ctypes.POINTER(c_int)]),
     "lcd_sptrsv_wavefront_multi": (c_int, [c_int32, c_int64, c_int32, _P, _P, _P, _P, _P, _P, c_int64,
                                            c_int, _P, _P, c_int32, _P, c_int32, _P,
                                            ctypes.POINTER(c_int)]),

@@ -20,7 +20,36 @@ struct WavefrontParams {
     const int *__restrict__ wavefront_ptr;
     int n_levels;
     int lanes;          // lanes per node, power of two <= 32
+    // Band chains (band_width > 1 of the reference's warp tasks): when set, the items of a
+    // level are tasks, task t being the nodes wavefronts[task_ptr[t] .. task_ptr[t + 1]) that
+    // one lane group solves one after another; levels are then bands of such tasks.
+    const int *__restrict__ task_ptr;
 };
+
+__device__ __forceinline__ void solve_node(const WavefrontParams &w, int node, bool active,
+                                           int lane, int lanes);
+
+// One item of a level: a node, or a chain of nodes solved in order by the same lane group.
+// Must be called by all 32 lanes of the warp.
+__device__ __forceinline__ void solve_item(const WavefrontParams &w, int t, bool active, int lane,
+                                           int lanes) {
+    if (!w.task_ptr) {
+        const int node = active ? __ldg(w.wavefronts + t) : 0;
+        solve_node(w, node, active && (unsigned)node < (unsigned)w.m.n, lane, lanes);
+        return;
+    }
+    const int first = active ? __ldg(w.task_ptr + t) : 0;
+    const int count = active ? __ldg(w.task_ptr + t + 1) - first : 0;
+    const int longest = __reduce_max_sync(0xffffffffu, count);
+    for (int k = 0; k < longest; ++k) {
+        const bool on = k < count;
+        const int node = on ? __ldg(w.wavefronts + first + k) : 0;
+        solve_node(w, node, on && (unsigned)node < (unsigned)w.m.n, lane, lanes);
+        // the next node of the chain reads what this one wrote (stores and atomics to L2)
+        __threadfence();
+        __syncwarp();
+    }
+}
 
 // One node handled by `lanes` consecutive lanes of a warp.  Must be called by
 // all 32 lanes of the warp (inactive groups pass active = false).
@@ -92,9 +121,7 @@ __global__ void __launch_bounds__(256)
 wavefront_level_kernel(const WavefrontParams w, int wave_start, int wave_end) {
     const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
     const int t = wave_start + gtid / w.lanes;
-    const bool active = t < wave_end;
-    const int node = active ? __ldg(w.wavefronts + t) : 0;
-    solve_node(w, node, active && (unsigned)node < (unsigned)w.m.n, gtid % w.lanes, w.lanes);
+    solve_item(w, t, t < wave_end, gtid % w.lanes, w.lanes);
 }
 
 constexpr int kCoopThreads = 512;
@@ -143,9 +170,7 @@ __global__ void __launch_bounds__(kCoopThreads) wavefront_coop_kernel(const Wave
                 for (int k = l; k < end; ++k) {
                     const int s = __ldg(w.wavefront_ptr + k), e = __ldg(w.wavefront_ptr + k + 1);
                     const int t = s + local;
-                    const bool active = t < e;
-                    const int node = active ? __ldg(w.wavefronts + t) : 0;
-                    solve_node(w, node, active && (unsigned)node < (unsigned)w.m.n, lane, lanes);
+                    solve_item(w, t, t < e, lane, lanes);
                     __syncthreads();
                 }
             }
@@ -154,9 +179,7 @@ __global__ void __launch_bounds__(kCoopThreads) wavefront_coop_kernel(const Wave
             const int total_rows = gridDim.x * rows_per_block;
             for (int base = ws + blockIdx.x * rows_per_block; base < we; base += total_rows) {
                 const int t = base + local;
-                const bool active = t < we;
-                const int node = active ? __ldg(w.wavefronts + t) : 0;
-                solve_node(w, node, active && (unsigned)node < (unsigned)w.m.n, lane, lanes);
+                solve_item(w, t, t < we, lane, lanes);
             }
             ++l;
         }
@@ -274,13 +297,12 @@ static int launch_multi_coop(WavefrontParams &w, cudaStream_t st) {
 
 using namespace lcd;
 
-extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_t *Ap,
-                                    const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
-                                    const double *b, double *x, int flags,
-                                    const int32_t *wavefronts, const int32_t *wavefront_ptr_dev,
-                                    const int32_t *wavefront_ptr_host, int32_t n_levels, int mode,
-                                    int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
-                                    void *stream, int *status_host) {
+static int wavefront_solve(int op, int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                           const double *Ax, const int32_t *diag_pos, const double *b, double *x,
+                           int flags, const int32_t *wavefronts, const int32_t *task_ptr_dev,
+                           const int32_t *wavefront_ptr_dev, const int32_t *wavefront_ptr_host,
+                           int32_t n_levels, int mode, int lanes_per_row, int32_t *status_dev,
+                           int32_t timeout_ms, void *stream, int *status_host) {
     if (n < 0 || nnz < 0 || n_levels < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
     const bool csc = (op == LCD_OP_CSC_LOWER || op == LCD_OP_CSC_UPPER);
     const bool csr = (op == LCD_OP_CSR_LOWER || op == LCD_OP_CSR_UPPER);
@@ -308,6 +330,7 @@ extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_
         w.wavefront_ptr = wavefront_ptr_dev;
         w.n_levels = n_levels;
         w.lanes = lanes;
+        w.task_ptr = task_ptr_dev;
         if (mode == LCD_WAVEFRONT_PER_LEVEL) {
             for (int l = 0; l < n_levels; ++l) {
                 const int ws = wavefront_ptr_host[l], we = wavefront_ptr_host[l + 1];
@@ -336,6 +359,32 @@ extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_
     return finish(status_dev, st, status_host);
 }
 
+extern "C" int lcd_sptrsv_wavefront(int op, int32_t n, int64_t nnz, const int32_t *Ap,
+                                    const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
+                                    const double *b, double *x, int flags,
+                                    const int32_t *wavefronts, const int32_t *wavefront_ptr_dev,
+                                    const int32_t *wavefront_ptr_host, int32_t n_levels, int mode,
+                                    int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
+                                    void *stream, int *status_host) {
+    return wavefront_solve(op, n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, wavefronts, nullptr,
+                           wavefront_ptr_dev, wavefront_ptr_host, n_levels, mode, lanes_per_row,
+                           status_dev, timeout_ms, stream, status_host);
+}
+
+extern "C" int lcd_sptrsv_wavefront_tasks(int op, int32_t n, int64_t nnz, const int32_t *Ap,
+                                          const int32_t *Ai, const double *Ax,
+                                          const int32_t *diag_pos, const double *b, double *x,
+                                          int flags, const int32_t *task_nodes,
+                                          const int32_t *task_ptr_dev, const int32_t *band_ptr_dev,
+                                          const int32_t *band_ptr_host, int32_t n_bands, int mode,
+                                          int lanes_per_row, int32_t *status_dev,
+                                          int32_t timeout_ms, void *stream, int *status_host) {
+    if (n > 0 && !task_ptr_dev) return LCD_ERR_INVALID_ARGUMENT;
+    return wavefront_solve(op, n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, task_nodes, task_ptr_dev,
+                           band_ptr_dev, band_ptr_host, n_bands, mode, lanes_per_row, status_dev,
+                           timeout_ms, stream, status_host);
+}
+
 extern "C" int lcd_sptrsv_wavefront_multi(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap,
                                           const int32_t *Ai, const double *Ax,
                                           const int32_t *diag_pos, const double *B, double *X,
@@ -361,6 +410,7 @@ extern "C" int lcd_sptrsv_wavefront_multi(int32_t n, int64_t nnz, int32_t nrhs, 
         w.wavefront_ptr = wavefront_ptr_dev;
         w.n_levels = n_levels;
         w.lanes = 32;
+        w.task_ptr = nullptr;
         rc = nrhs <= 32 ? launch_multi_coop<1>(w, st) : launch_multi_coop<2>(w, st);
         if (rc) return rc;
     }

@@ -71,19 +71,25 @@ def bind(lowering):
     def average_row(Ap, Ai):
         return Ai.numel() / max(1, Ap.numel() - 1)
 
-    def wavefront_arrays(values):
+    def wavefront_arrays(values, serves_tasks=False):
+        tasks = None
         if "wavefronts" in values:
             nodes, ptr_host = values["wavefronts"], values["wavefront_ptr"]
         else:
             nodes, ptr_host = values["task_nodes"], values["band_ptr"]
             task_ptr = values["task_ptr"]
-            if len(task_ptr) - 1 != len(nodes):
-                raise CUDALoweringError("band_width > 1 task chains are not served natively")
+            if len(task_ptr) - 1 != len(nodes):    # band chains (band_width > 1)
+                if not serves_tasks:
+                    raise CUDALoweringError("band_width > 1 task chains are not served natively "
+                                            "for this operator")
+                tasks = as_tensor(task_ptr, torch.int32)
         nodes = as_tensor(nodes, torch.int32)
         ptr_host = np.ascontiguousarray(
             ptr_host.copy_to_host() if hasattr(ptr_host, "copy_to_host") else
             (ptr_host.cpu().numpy() if hasattr(ptr_host, "cpu") else ptr_host), dtype=np.int32)
         ptr_dev = torch.from_numpy(ptr_host).to(nodes.device)
+        if serves_tasks:
+            return nodes, ptr_dev, ptr_host, tasks
         return nodes, ptr_dev, ptr_host
 
     def chain_solve(Ap, Ai, Ax, b, x, cache):
@@ -110,10 +116,10 @@ def bind(lowering):
             else:
                 ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper, lanes=lanes)
         else:
-            nodes, ptr_dev, ptr_host = wavefront_arrays(v)
+            nodes, ptr_dev, ptr_host, tasks = wavefront_arrays(v, serves_tasks=True)
             mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
             ops.sptrsv_wavefront("csr_upper" if lowering.upper else "csr_lower", Ap, Ai, Ax, b,
-                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes)
+                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes, task_ptr=tasks)
 
     def sptrsv_csr(*args, _hints=None):
         v = split(args)
@@ -167,10 +173,10 @@ def bind(lowering):
                 dep = ops.csc_edge_count(Ap, Ai, upper=lowering.upper)
             ops.sptrsv_csc_syncfree(Ap, Ai, Ax, b, dep, x, upper=lowering.upper, lanes=lanes)
         else:
-            nodes, ptr_dev, ptr_host = wavefront_arrays(v)
+            nodes, ptr_dev, ptr_host, tasks = wavefront_arrays(v, serves_tasks=True)
             mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
             ops.sptrsv_wavefront("csc_upper" if lowering.upper else "csc_lower", Ap, Ai, Ax, b,
-                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes)
+                                 nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes, task_ptr=tasks)
 
     def ilu0_csr(*args):
         v = split(args)

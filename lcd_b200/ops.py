@@ -307,8 +307,11 @@ def sptrsv_csc_syncfree(Ap, Ai, Ax, b, dep_count, x=None, *, upper=False, exact=
 
 def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr_host=None,
                      x=None, *, mode="cooperative", diag_pos=None, unit_diag=False, exact=False,
-                     lanes=1, status=None, timeout_ms=0, sync=True):
-    """Level-synchronous solve over the level sets of ``dag_build``."""
+                     lanes=1, status=None, timeout_ms=0, sync=True, task_ptr=None):
+    """Level-synchronous solve over the level sets of ``dag_build``.  With ``task_ptr`` the
+    items of a level are chains of nodes (band chains of ``preprocess_warp_tasks`` with
+    ``band_width > 1``): ``wavefronts`` then holds the task nodes, ``wavefront_ptr`` the
+    band pointer."""
     op = _op_code(op)
     n = Ap.numel() - 1
     x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
@@ -323,10 +326,18 @@ def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr
         host_ptr = wavefront_ptr_host.ctypes.data_as(ctypes.c_void_p)
     flags = _solve_flags(False, unit_diag, diag_pos is not None, exact)
     host = ctypes.c_int(0)
-    rc = nat.load().lcd_sptrsv_wavefront(
-        op, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
-        ptr(wavefronts), ptr(wavefront_ptr), host_ptr, n_levels, mode_code, int(lanes),
-        ptr(status), int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    if task_ptr is None:
+        rc = nat.load().lcd_sptrsv_wavefront(
+            op, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
+            ptr(wavefronts), ptr(wavefront_ptr), host_ptr, n_levels, mode_code, int(lanes),
+            ptr(status), int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    else:
+        _require(task_ptr, torch.int32, "task_ptr")
+        rc = nat.load().lcd_sptrsv_wavefront_tasks(
+            op, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
+            ptr(wavefronts), ptr(task_ptr), ptr(wavefront_ptr), host_ptr, n_levels, mode_code,
+            int(lanes), ptr(status), int(timeout_ms), _stream(),
+            ctypes.byref(host) if sync else None)
     check(rc, "lcd_sptrsv_wavefront")
     return x
 

@@ -84,6 +84,28 @@ def csr_upper_reversed(Ap, Ai, Ax, b, n):
     return x
 
 
+# band chains: tasks are chains of nodes connected inside two consecutive levels
+@parallel(block_map="i", thread_map="j", function_props=PROPS_CSR, execution_mode="wavefront", threads_per_block=128, thread_unroll=1, band_width=2)
+def csr_warp_wavefront_band2(Ap, Ai, Ax, b, n):
+    x = np.zeros(n)
+    for i in range(n):
+        x[i] = b[i]
+        for j in range(Ap[i], Ap[i + 1] - 1):
+            x[i] -= Ax[j] * x[Ai[j]]
+        x[i] /= Ax[Ap[i + 1] - 1]
+    return x
+
+
+@parallel(block_map="i", thread_map="j", function_props=PROPS_CSC, execution_mode="wavefront", threads_per_block=128, thread_unroll=1, band_width=3)
+def csc_warp_wavefront_band3(Ap, Ai, Ax, b, n):
+    x = np.zeros(n)
+    for i in range(n):
+        x[i] = (b[i] - x[i]) / Ax[Ap[i]]
+        for j in range(Ap[i] + 1, Ap[i + 1]):
+            x[Ai[j]] += Ax[j] * x[i]
+    return x
+
+
 # the reference's Gauss-Seidel demo operators (compiler/demo/gauss_seidel.py:18-41)
 @parallel(block_map="i", function_props=PROPS_CSR, execution_mode="wavefront", threads_per_block=128)
 def simple_gauss_seidel_csr(Ap, Ai, Ax, D, b, x, n, max_iter):

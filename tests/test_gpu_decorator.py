@@ -93,6 +93,30 @@ def test_decorated_first_configuration(cuda, oracle):
     assert len(plan.execution_data.band_ptr) - 1 == 511           # levels of the 256 x 256 grid
 
 
+@pytest.mark.parametrize("name", ["sptrsv_lap2d_g8", "sptrsv_band_n600", "sptrsv_lap3d_g5", "sptrsv_unsorted_dups"])
+def test_decorated_band_chains(cuda, name):
+    """band_width > 1 (compiler/dag_preprocessing.py:207-298): tasks are chains of nodes connected
+    inside a band of consecutive levels; a lane group solves a chain node after node, bands are
+    separated like levels.  Same results as every other schedule."""
+    import ops_decorated as od
+    from lcd_b200.dag_preprocessing import preprocess_warp_tasks
+    g = golden(name)
+    n = len(g["b"])
+    csr = (g["csr_Ap"], g["csr_Ai"], g["csr_Ax"], g["b"], n)
+    csc = (g["csc_Ap"], g["csc_Ai"], g["csc_Ax"], g["b"], n)
+    data = od.csr_warp_wavefront_band2.schedule_plan(*csr).execution_data
+    succ, waves = od.simple_sptrsv_csr.build_dag(*csr)
+    want = preprocess_warp_tasks(succ, waves, band_width=2)               # list form (host logic tests pin it)
+    np.testing.assert_array_equal(np.asarray(data.task_nodes), want.task_nodes)
+    np.testing.assert_array_equal(np.asarray(data.task_ptr), want.task_ptr)
+    np.testing.assert_array_equal(np.asarray(data.band_ptr), want.band_ptr)
+    assert len(data.task_ptr) - 1 < n or len(waves) == n                  # chains do form
+    x = od.csr_warp_wavefront_band2(*csr)
+    np.testing.assert_allclose(x, g["x_csr"], rtol=1e-10, atol=1e-12)
+    x = od.csc_warp_wavefront_band3(*csc)
+    np.testing.assert_allclose(x, g["x_csc"], rtol=1e-10, atol=1e-12)
+
+
 @pytest.mark.parametrize("name", golden_names("gauss_seidel_"))
 def test_decorated_gauss_seidel_matches_the_reference(cuda, oracle, name):
     """The reference's Gauss-Seidel demo operators (compiler/demo/gauss_seidel.py:18-41), inputs
