@@ -111,8 +111,11 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
             if (warp == 0) {
                 const int r = cb + lane;  // row of this lane inside the diagonal block
                 double v = lane < bw ? xs[r] : 0.0;
+                // the 32 reciprocals are taken at once, off the 32-step dependent chain (a
+                // division per step would cost about 100 cycles each)
+                const double rinv = lane < bw ? 1.0 / tri[lane][lane] : 0.0;
                 for (int c = 0; c < bw; ++c) {
-                    if (lane == c) v = v / tri[c][c];
+                    if (lane == c) v = v * rinv;
                     const double xc = __shfl_sync(0xffffffffu, v, c);
                     if (lane > c && lane < bw) v = fma(-tri[lane][c], xc, v);
                 }
@@ -120,11 +123,20 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
             }
             __syncthreads();
             for (int r = cb + 32 + tid; r < w; r += kSnThreads) {
-                double v = xs[r];
-#pragma unroll 8
-                for (int c = 0; c < bw; ++c)
-                    v = fma(-__ldg(M + (long long)(cb + c) * len + r), xs[cb + c], v);
-                xs[r] = v;
+                double v0 = xs[r], v1 = 0.0;
+                int c = 0;
+                for (; c + 16 <= bw; c += 16) {
+                    double m[16];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) m[u] = __ldg(M + (long long)(cb + c + u) * len + r);
+#pragma unroll
+                    for (int u = 0; u < 16; u += 2) {
+                        v0 = fma(-m[u], xs[cb + c + u], v0);
+                        v1 = fma(-m[u + 1], xs[cb + c + u + 1], v1);
+                    }
+                }
+                for (; c < bw; ++c) v0 = fma(-__ldg(M + (long long)(cb + c) * len + r), xs[cb + c], v0);
+                xs[r] = v0 + v1;
             }
             __syncthreads();
         }
@@ -144,6 +156,20 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         const double *P = M + w + j;
         double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
         int c = 0;
+        // sixteen loads in flight per thread: the strip's latency is w / 16 round trips to
+        // L2 or HBM instead of w / 4, and a strip sits on the critical path of its level
+        for (; c + 16 <= w; c += 16) {
+            double v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = __ldg(P + (long long)(c + u) * len);
+#pragma unroll
+            for (int u = 0; u < 16; u += 4) {
+                acc0 = fma(v[u + 0], xs[c + u + 0], acc0);
+                acc1 = fma(v[u + 1], xs[c + u + 1], acc1);
+                acc2 = fma(v[u + 2], xs[c + u + 2], acc2);
+                acc3 = fma(v[u + 3], xs[c + u + 3], acc3);
+            }
+        }
         for (; c + 4 <= w; c += 4) {
             acc0 = fma(__ldg(P + (long long)(c + 0) * len), xs[c + 0], acc0);
             acc1 = fma(__ldg(P + (long long)(c + 1) * len), xs[c + 1], acc1);

@@ -63,6 +63,34 @@ def _host(a, dtype):
     return np.ascontiguousarray(a, dtype=dtype)
 
 
+def _level_order(sn_h, Lip_h, Li_h, cts_h, n_super):
+    """Supernodes sorted by (level, index), level(t) = 1 + max level of the supernodes whose
+    panels have a row in t's columns (``utils/symbolic_cholesky_csc.py:1024-1050`` builds the
+    same dependence graph)."""
+    if n_super == 0:
+        return np.zeros(0, dtype=np.int64)
+    width = np.diff(sn_h)
+    length = np.diff(Lip_h)
+    # off-diagonal rows of every panel -> (source supernode, target supernode), distinct pairs
+    positions = np.arange(int(Lip_h[-1]), dtype=np.int64)
+    owner = np.repeat(np.arange(n_super, dtype=np.int64), length)
+    off = positions - Lip_h[owner] >= width[owner]
+    src = owner[off]
+    dst = cts_h[Li_h[off]].astype(np.int64)
+    keep = dst > src
+    pair = np.unique(src[keep] * n_super + dst[keep])
+    src, dst = pair // n_super, pair % n_super
+    by_target = np.argsort(dst, kind="stable")
+    src, dst = src[by_target], dst[by_target]
+    start = np.searchsorted(dst, np.arange(n_super + 1))
+    level = np.zeros(n_super, dtype=np.int64)
+    for t in range(n_super):          # sources have smaller indices: one pass in index order
+        a, b = start[t], start[t + 1]
+        if b > a:
+            level[t] = level[src[a:b]].max() + 1
+    return np.lexsort((np.arange(n_super), level))
+
+
 def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda"):
     """Validate the layout, upload it and build the task list.
 
@@ -86,10 +114,14 @@ def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda"):
         col_to_super = np.repeat(np.arange(n_super, dtype=np.int32), width)
     strip_rows = nat.load().lcd_supernodal_strip_rows()
     strips = np.maximum(1, -(-(length - width) // strip_rows))
-    task_super = np.repeat(np.arange(n_super, dtype=np.int32), strips)
+    # Tasks are handed out by ticket; a task whose inputs are not there yet keeps its block
+    # waiting.  In index order a supernode often follows one it depends on closely; in level
+    # order (a topological order too) the tasks around it in the queue are independent of it.
+    order = _level_order(sn_h, Lip_h, _host(Li, np.int32), _host(col_to_super, np.int32), n_super)
+    task_super = np.repeat(order.astype(np.int32), strips[order])
     first = np.zeros(n_super + 1, dtype=np.int64)
-    np.cumsum(strips, out=first[1:])
-    task_strip = (np.arange(int(first[-1]), dtype=np.int64) - np.repeat(first[:-1], strips))
+    np.cumsum(strips[order], out=first[1:])
+    task_strip = (np.arange(int(first[-1]), dtype=np.int64) - np.repeat(first[:-1], strips[order]))
     dev = torch.device(device)
 
     def up(a, dtype):
