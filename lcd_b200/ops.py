@@ -186,7 +186,8 @@ def chain_workspace(n, device):
 
 
 def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_pos=None):
-    """Invert the 32 x 32 diagonal blocks into ``workspace`` (repeat when Ax changes)."""
+    """Build the block tiles (inverse diagonal blocks and their products with the two
+    couplings before) into ``workspace``; repeat when Ax changes."""
     flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
     check(nat.load().lcd_chain_prepare(Ap.numel() - 1, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax),
                                        ptr(diag_pos), flags, ptr(workspace),
@@ -196,7 +197,7 @@ def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_p
 
 def sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, unit_diag=False,
                      diag_pos=None, status=None, timeout_ms=0, sync=True):
-    """Block-inverse chain solve (for matrices whose levels hold only a few rows).
+    """Block-recurrence chain solve (for matrices whose levels hold only a few rows).
     ``workspace`` must have been filled by ``chain_prepare`` for the same matrix."""
     _require(b, torch.float64, "b")
     n = Ap.numel() - 1
