@@ -282,6 +282,8 @@ def run_native(args):
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     value = world * flops(n, nnz) / (ms_per_step * 1e-3) / 1e9
+    spread = {"p20": float(np.percentile(per_launch_ms, 20)), "p50": float(np.percentile(per_launch_ms, 50)),
+              "p80": float(np.percentile(per_launch_ms, 80))}   # this rank's steps, CUDA events
 
     # end to end through the public API: the decorated operator called with host
     # (pinned) arrays; upload, solve and download are all inside the timed region
@@ -309,6 +311,7 @@ def run_native(args):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "ms_per_step_spread": spread,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic",
             "config": {"workload": args.workload, "n": n, "nnz": nnz, "format": "csr_lower",
