@@ -317,8 +317,16 @@ int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
                           const int32_t *task_super, const int32_t *task_strip,
                           const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                           const int64_t *Lp, const double *Lx, const int32_t *col_to_super,
-                          int32_t *pending, int32_t *solved, double *x, int32_t *status_dev,
-                          int32_t timeout_ms, void *stream, int *status_host);
+                          int32_t *pending, int32_t *solved, double *x, const double *tinv,
+                          int32_t *status_dev, int32_t timeout_ms, void *stream, int *status_host);
+/*
+ * Optional numeric preparation (repeat when Lx changes): tinv (32 * n doubles) receives the
+ * inverses of the 32 x 32 lower triangles on the diagonal of every supernode's diagonal
+ * block.  With tinv the solve replaces the 32 dependent steps of each triangle by 32
+ * independent multiply-adds; with tinv == NULL it substitutes step by step.
+ */
+int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
+                           const int64_t *Lp, const double *Lx, double *tinv, void *stream);
 
 /* ---- block-row partition of one solve across the GPUs of a node ---------------- */
 /*

@@ -33,6 +33,7 @@ struct SupernodalParams {
     int n;
     int32_t *status;
     unsigned long long budget_ns;
+    const double *__restrict__ tinv;   // inverses of the 32 x 32 diagonal triangles, or NULL
 };
 
 __device__ __forceinline__ void prefetch_l2(const void *ptr) {
@@ -103,6 +104,24 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         for (int cb = 0; cb < w; cb += 32) {
             const int bw = min(32, w - cb);
             // stage the 32 x 32 triangle (coalesced down the columns), then warp 0 solves it
+            if (p.tinv) {
+                // the triangle's inverse (lcd_supernodal_prepare): the 32-step chain of the
+                // substitution becomes 32 independent shuffle / multiply-add pairs
+                const double *inv = p.tinv + (long long)(c0 + cb) * 32;
+                for (int idx = tid; idx < 32 * bw; idx += kSnThreads) tri[idx & 31][idx >> 5] = __ldg(inv + idx);
+                __syncthreads();
+                if (warp == 0) {
+                    const double v = lane < bw ? xs[cb + lane] : 0.0;
+                    double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
+                    for (int c = 0; c < bw; c += 4) {    // (columns past bw read stale entries times zero)
+                        y0 = fma(tri[lane][c + 0], __shfl_sync(0xffffffffu, v, c + 0), y0);
+                        y1 = fma(c + 1 < bw ? tri[lane][c + 1] : 0.0, __shfl_sync(0xffffffffu, v, c + 1), y1);
+                        y2 = fma(c + 2 < bw ? tri[lane][c + 2] : 0.0, __shfl_sync(0xffffffffu, v, c + 2), y2);
+                        y3 = fma(c + 3 < bw ? tri[lane][c + 3] : 0.0, __shfl_sync(0xffffffffu, v, c + 3), y3);
+                    }
+                    if (lane < bw) xs[cb + lane] = (y0 + y1) + (y2 + y3);
+                }
+            } else {
             for (int idx = tid; idx < 32 * bw; idx += kSnThreads) {
                 const int c = idx >> 5, rr = idx & 31;
                 if (rr < bw && rr >= c) tri[rr][c] = __ldg(M + (long long)(cb + c) * len + cb + rr);
@@ -120,6 +139,7 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
                     if (lane > c && lane < bw) v = fma(-tri[lane][c], xc, v);
                 }
                 if (lane < bw) xs[r] = v;
+            }
             }
             __syncthreads();
             for (int r = cb + 32 + tid; r < w; r += kSnThreads) {
@@ -192,6 +212,43 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         red_release_add_s32(p.pending + target, -__popc(peers));
 }
 
+// Inverses of the 32 x 32 lower triangles on the diagonal of every supernode's diagonal block,
+// one warp per supernode, lane c computing column c by forward substitution.  Element (rr, c)
+// of the triangle that starts at column g goes to tinv[(g + c) * 32 + rr]; entries above the
+// diagonal and rows past a short last triangle are stored as zeros.
+constexpr int kInvWarpsPerBlock = 2;
+__global__ void __launch_bounds__(kInvWarpsPerBlock * 32)
+supernodal_inverse_kernel(int n_super, const int *__restrict__ sn, const int *__restrict__ Lip,
+                          const long long *__restrict__ Lp, const double *__restrict__ Lx,
+                          double *__restrict__ tinv) {
+    __shared__ double T[kInvWarpsPerBlock][32][33];
+    __shared__ double I[kInvWarpsPerBlock][32][33];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s = blockIdx.x * kInvWarpsPerBlock + wid;
+    if (s >= n_super) return;
+    const int c0 = sn[s], w = sn[s + 1] - c0;
+    const int len = Lip[s + 1] - Lip[s];
+    const double *M = Lx + Lp[c0];
+    for (int cb = 0; cb < w; cb += 32) {
+        const int bw = min(32, w - cb);
+        for (int c = 0; c < bw; ++c)
+            T[wid][lane][c] = (lane < bw && lane >= c) ? M[(long long)(cb + c) * len + cb + lane] : 0.0;
+        __syncwarp();
+        if (lane < bw) {
+            const int c = lane;
+            for (int r = c; r < bw; ++r) {
+                double acc = (r == c) ? 1.0 : 0.0;
+                for (int k = c; k < r; ++k) acc = fma(-T[wid][r][k], I[wid][k][c], acc);
+                I[wid][r][c] = acc / T[wid][r][r];
+            }
+        }
+        __syncwarp();
+        double *out = tinv + (long long)(c0 + cb) * 32;
+        for (int c = 0; c < bw; ++c) out[c * 32 + lane] = (lane < bw && lane >= c) ? I[wid][lane][c] : 0.0;
+        __syncwarp();
+    }
+}
+
 __global__ void supernodal_pending_kernel(int n_super, const int *__restrict__ sn,
                                           const int *__restrict__ Lip, const int *__restrict__ Li,
                                           const int *__restrict__ col_to_super, int *pending) {
@@ -221,6 +278,19 @@ extern "C" int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const 
     return LCD_OK;
 }
 
+extern "C" int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
+                                      const int64_t *Lp, const double *Lx, double *tinv,
+                                      void *stream) {
+    if (n_super < 0 || (n_super > 0 && (!sn || !Lip || !Lp || !Lx || !tinv)))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n_super == 0) return LCD_OK;
+    supernodal_inverse_kernel<<<(n_super + kInvWarpsPerBlock - 1) / kInvWarpsPerBlock,
+                                kInvWarpsPerBlock * 32, 0, (cudaStream_t)stream>>>(
+        n_super, sn, Lip, reinterpret_cast<const long long *>(Lp), Lx, tinv);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
 extern "C" int lcd_supernodal_strip_rows(void) { return kSnThreads; }
 
 extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
@@ -228,8 +298,9 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
                                      const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                                      const int64_t *Lp, const double *Lx,
                                      const int32_t *col_to_super, int32_t *pending,
-                                     int32_t *solved, double *x, int32_t *status_dev,
-                                     int32_t timeout_ms, void *stream, int *status_host) {
+                                     int32_t *solved, double *x, const double *tinv,
+                                     int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                     int *status_host) {
     if (n < 0 || n_super < 0 || n_tasks < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
     if (n_super > 0 && (!task_super || !task_strip || !sn || !Lip || !Li || !Lp || !Lx ||
                         !col_to_super || !pending || !solved || !x))
@@ -241,7 +312,7 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
         LCD_CUDA_TRY(cudaMemsetAsync(solved, 0, (size_t)n_super * sizeof(int32_t), st));
         SupernodalParams p{n_super, n_tasks, task_super, task_strip, sn, Lip, Li,
                            reinterpret_cast<const long long *>(Lp), Lx, col_to_super, pending,
-                           solved, x, n, status_dev, timeout_ns(timeout_ms)};
+                           solved, x, n, status_dev, timeout_ns(timeout_ms), tinv};
         supernodal_kernel<<<n_tasks, kSnThreads, 0, st>>>(p);
         LCD_CUDA_TRY(cudaGetLastError());
     }
