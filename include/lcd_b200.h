@@ -317,16 +317,19 @@ int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
                           const int32_t *task_super, const int32_t *task_strip,
                           const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                           const int64_t *Lp, const double *Lx, const int32_t *col_to_super,
-                          int32_t *pending, int32_t *solved, double *x, const double *tinv,
-                          int32_t *status_dev, int32_t timeout_ms, void *stream, int *status_host);
+                          int32_t *pending, int32_t *solved, double *x, const int64_t *inv_ptr,
+                          const double *inv, int32_t *status_dev, int32_t timeout_ms, void *stream,
+                          int *status_host);
 /*
- * Optional numeric preparation (repeat when Lx changes): tinv (32 * n doubles) receives the
- * inverses of the 32 x 32 lower triangles on the diagonal of every supernode's diagonal
- * block.  With tinv the solve replaces the 32 dependent steps of each triangle by 32
- * independent multiply-adds; with tinv == NULL it substitutes step by step.
+ * Optional numeric preparation (repeat when Lx changes): the inverse of every supernode's
+ * w x w diagonal block, column-major with leading dimension w, is written to
+ * inv[inv_ptr[s] ..); inv_ptr[s] = sum of w_t^2 over t < s (n_super + 1 entries, device).
+ * With them the solve multiplies by the inverse - independent loads and multiply-adds -
+ * instead of substituting through w dependent steps; with inv_ptr == NULL it substitutes.
  */
 int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
-                           const int64_t *Lp, const double *Lx, double *tinv, void *stream);
+                           const int64_t *Lp, const double *Lx, const int64_t *inv_ptr,
+                           double *inv, void *stream);
 
 /* ---- block-row partition of one solve across the GPUs of a node ---------------- */
 /*

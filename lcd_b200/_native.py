@@ -82,8 +82,8 @@ _SIGNATURES = {
     "lcd_supernodal_pending": (c_int, [c_int32, _P, _P, _P, _P, _P, _P]),
     "lcd_supernodal_strip_rows": (c_int, []),
     "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
-                                      _P, _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
-    "lcd_supernodal_prepare": (c_int, [c_int32, _P, _P, _P, _P, _P, _P]),
+                                      _P, _P, _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_supernodal_prepare": (c_int, [c_int32, _P, _P, _P, _P, _P, _P, _P]),
     "lcd_peer_alloc": (c_int, [c_int64, ctypes.POINTER(c_void_p), ctypes.c_char_p]),
     "lcd_peer_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
     "lcd_peer_close": (c_int, [_P]),

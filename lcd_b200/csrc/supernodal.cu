@@ -33,7 +33,8 @@ struct SupernodalParams {
     int n;
     int32_t *status;
     unsigned long long budget_ns;
-    const double *__restrict__ tinv;   // inverses of the 32 x 32 diagonal triangles, or NULL
+    const double *__restrict__ inv;        // inverses of the diagonal blocks (column-major w x w), or NULL
+    const long long *__restrict__ inv_ptr; // where each supernode's inverse starts
 };
 
 __device__ __forceinline__ void prefetch_l2(const void *ptr) {
@@ -42,7 +43,9 @@ __device__ __forceinline__ void prefetch_l2(const void *ptr) {
 
 __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const SupernodalParams p) {
     __shared__ double xs[kSnMaxWidth];
+    __shared__ double ys[kSnMaxWidth];   // product with the inverse diagonal block
     __shared__ double tri[32][33];  // current 32 x 32 diagonal sub-block, row-major, padded
+    double *part = &tri[0][0];      // ... or the partial sums of the threads that share a row
     __shared__ int s_task;
     __shared__ int s_ok;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -75,11 +78,15 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
                 prefetch_l2(P + (long long)c * len + 4 * q);
             }
         }
-        if (strip == 0)
+        if (strip == 0 && p.inv) {
+            const double *inv = p.inv + __ldg(p.inv_ptr + s);
+            for (int idx = tid * 4; idx < w * w; idx += kSnThreads * 4) prefetch_l2(inv + idx);
+        } else if (strip == 0) {
             for (int idx = tid; idx < ((w + 3) >> 2) * w; idx += kSnThreads) {
                 const int c = idx / ((w + 3) >> 2), q = idx % ((w + 3) >> 2);
                 prefetch_l2(M + (long long)c * len + 4 * q);
             }
+        }
     }
     // ---- wait for the inputs of this task --------------------------------
     if (tid == 0) {
@@ -99,29 +106,49 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
     if (!s_ok) return;
     for (int c = tid; c < w; c += kSnThreads) xs[c] = ld_relaxed_f64(p.x + c0 + c);
     __syncthreads();
-    if (strip == 0) {
+    if (strip == 0 && p.inv) {
+        // ---- x_s = T^-1 v with the inverse of the diagonal block (lcd_supernodal_prepare): one
+        // pass of independent loads and multiply-adds instead of a chain of w dependent steps.
+        // A row is shared by 256 / w' threads (w' = w rounded up to a power of two) that take
+        // every (256 / w')-th column; wide blocks give every thread several rows.
+        const double *inv = p.inv + __ldg(p.inv_ptr + s);
+        int wp = 16;
+        while (wp < w && wp < kSnThreads) wp <<= 1;
+        const int tpr = kSnThreads / wp;              // threads per row (1 when w >= 256)
+        const int sub = tid / wp;
+        for (int r = tid % wp; r < w; r += wp) {       // (one trip unless w > 256)
+            double y0 = 0.0, y1 = 0.0;
+            int c = sub;
+            for (; c + 7 * tpr <= r; c += 8 * tpr) {   // eight loads in flight
+                double m[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) m[u] = __ldg(inv + (long long)(c + u * tpr) * w + r);
+#pragma unroll
+                for (int u = 0; u < 8; u += 2) {
+                    y0 = fma(m[u], xs[c + u * tpr], y0);
+                    y1 = fma(m[u + 1], xs[c + (u + 1) * tpr], y1);
+                }
+            }
+            for (; c <= r; c += tpr) y0 = fma(__ldg(inv + (long long)c * w + r), xs[c], y0);
+            if (tpr == 1) ys[r] = y0 + y1;
+            else part[sub * wp + r] = y0 + y1;
+        }
+        __syncthreads();
+        if (tpr > 1) {
+            if (tid < w) {
+                double y = 0.0;
+                for (int q = 0; q < tpr; ++q) y += part[q * wp + tid];
+                ys[tid] = y;
+            }
+            __syncthreads();
+        }
+        for (int c = tid; c < w; c += kSnThreads) xs[c] = ys[c];
+        __syncthreads();
+    } else if (strip == 0) {
         // ---- dense triangular solve, 32 columns at a time --------------------
         for (int cb = 0; cb < w; cb += 32) {
             const int bw = min(32, w - cb);
             // stage the 32 x 32 triangle (coalesced down the columns), then warp 0 solves it
-            if (p.tinv) {
-                // the triangle's inverse (lcd_supernodal_prepare): the 32-step chain of the
-                // substitution becomes 32 independent shuffle / multiply-add pairs
-                const double *inv = p.tinv + (long long)(c0 + cb) * 32;
-                for (int idx = tid; idx < 32 * bw; idx += kSnThreads) tri[idx & 31][idx >> 5] = __ldg(inv + idx);
-                __syncthreads();
-                if (warp == 0) {
-                    const double v = lane < bw ? xs[cb + lane] : 0.0;
-                    double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
-                    for (int c = 0; c < bw; c += 4) {    // (columns past bw read stale entries times zero)
-                        y0 = fma(tri[lane][c + 0], __shfl_sync(0xffffffffu, v, c + 0), y0);
-                        y1 = fma(c + 1 < bw ? tri[lane][c + 1] : 0.0, __shfl_sync(0xffffffffu, v, c + 1), y1);
-                        y2 = fma(c + 2 < bw ? tri[lane][c + 2] : 0.0, __shfl_sync(0xffffffffu, v, c + 2), y2);
-                        y3 = fma(c + 3 < bw ? tri[lane][c + 3] : 0.0, __shfl_sync(0xffffffffu, v, c + 3), y3);
-                    }
-                    if (lane < bw) xs[cb + lane] = (y0 + y1) + (y2 + y3);
-                }
-            } else {
             for (int idx = tid; idx < 32 * bw; idx += kSnThreads) {
                 const int c = idx >> 5, rr = idx & 31;
                 if (rr < bw && rr >= c) tri[rr][c] = __ldg(M + (long long)(cb + c) * len + cb + rr);
@@ -139,7 +166,6 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
                     if (lane > c && lane < bw) v = fma(-tri[lane][c], xc, v);
                 }
                 if (lane < bw) xs[r] = v;
-            }
             }
             __syncthreads();
             for (int r = cb + 32 + tid; r < w; r += kSnThreads) {
@@ -160,6 +186,8 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
             }
             __syncthreads();
         }
+    }
+    if (strip == 0) {
         for (int c = tid; c < w; c += kSnThreads) st_relaxed_f64(p.x + c0 + c, xs[c]);
         __syncthreads();
         if (tid == 0) {
@@ -212,40 +240,27 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         red_release_add_s32(p.pending + target, -__popc(peers));
 }
 
-// Inverses of the 32 x 32 lower triangles on the diagonal of every supernode's diagonal block,
-// one warp per supernode, lane c computing column c by forward substitution.  Element (rr, c)
-// of the triangle that starts at column g goes to tinv[(g + c) * 32 + rr]; entries above the
-// diagonal and rows past a short last triangle are stored as zeros.
-constexpr int kInvWarpsPerBlock = 2;
-__global__ void __launch_bounds__(kInvWarpsPerBlock * 32)
+// Inverse of every supernode's w x w lower-triangular diagonal block, column-major with
+// leading dimension w at inv[inv_ptr[s]]: thread c computes column c by forward substitution
+// (entries above the diagonal are stored as zeros).
+__global__ void __launch_bounds__(128)
 supernodal_inverse_kernel(int n_super, const int *__restrict__ sn, const int *__restrict__ Lip,
                           const long long *__restrict__ Lp, const double *__restrict__ Lx,
-                          double *__restrict__ tinv) {
-    __shared__ double T[kInvWarpsPerBlock][32][33];
-    __shared__ double I[kInvWarpsPerBlock][32][33];
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int s = blockIdx.x * kInvWarpsPerBlock + wid;
+                          const long long *__restrict__ inv_ptr, double *inv) {
+    const int s = blockIdx.x;
     if (s >= n_super) return;
     const int c0 = sn[s], w = sn[s + 1] - c0;
     const int len = Lip[s + 1] - Lip[s];
     const double *M = Lx + Lp[c0];
-    for (int cb = 0; cb < w; cb += 32) {
-        const int bw = min(32, w - cb);
-        for (int c = 0; c < bw; ++c)
-            T[wid][lane][c] = (lane < bw && lane >= c) ? M[(long long)(cb + c) * len + cb + lane] : 0.0;
-        __syncwarp();
-        if (lane < bw) {
-            const int c = lane;
-            for (int r = c; r < bw; ++r) {
-                double acc = (r == c) ? 1.0 : 0.0;
-                for (int k = c; k < r; ++k) acc = fma(-T[wid][r][k], I[wid][k][c], acc);
-                I[wid][r][c] = acc / T[wid][r][r];
-            }
+    double *out = inv + inv_ptr[s];
+    for (int c = threadIdx.x; c < w; c += blockDim.x) {
+        double *col = out + (long long)c * w;
+        for (int r = 0; r < c; ++r) col[r] = 0.0;
+        for (int r = c; r < w; ++r) {
+            double acc = (r == c) ? 1.0 : 0.0;
+            for (int k = c; k < r; ++k) acc = fma(-M[(long long)k * len + r], col[k], acc);
+            col[r] = acc / M[(long long)r * len + r];
         }
-        __syncwarp();
-        double *out = tinv + (long long)(c0 + cb) * 32;
-        for (int c = 0; c < bw; ++c) out[c * 32 + lane] = (lane < bw && lane >= c) ? I[wid][lane][c] : 0.0;
-        __syncwarp();
     }
 }
 
@@ -279,14 +294,14 @@ extern "C" int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const 
 }
 
 extern "C" int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
-                                      const int64_t *Lp, const double *Lx, double *tinv,
-                                      void *stream) {
-    if (n_super < 0 || (n_super > 0 && (!sn || !Lip || !Lp || !Lx || !tinv)))
+                                      const int64_t *Lp, const double *Lx, const int64_t *inv_ptr,
+                                      double *inv, void *stream) {
+    if (n_super < 0 || (n_super > 0 && (!sn || !Lip || !Lp || !Lx || !inv_ptr || !inv)))
         return LCD_ERR_INVALID_ARGUMENT;
     if (n_super == 0) return LCD_OK;
-    supernodal_inverse_kernel<<<(n_super + kInvWarpsPerBlock - 1) / kInvWarpsPerBlock,
-                                kInvWarpsPerBlock * 32, 0, (cudaStream_t)stream>>>(
-        n_super, sn, Lip, reinterpret_cast<const long long *>(Lp), Lx, tinv);
+    supernodal_inverse_kernel<<<n_super, 128, 0, (cudaStream_t)stream>>>(
+        n_super, sn, Lip, reinterpret_cast<const long long *>(Lp), Lx,
+        reinterpret_cast<const long long *>(inv_ptr), inv);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }
@@ -298,9 +313,9 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
                                      const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                                      const int64_t *Lp, const double *Lx,
                                      const int32_t *col_to_super, int32_t *pending,
-                                     int32_t *solved, double *x, const double *tinv,
-                                     int32_t *status_dev, int32_t timeout_ms, void *stream,
-                                     int *status_host) {
+                                     int32_t *solved, double *x, const int64_t *inv_ptr,
+                                     const double *inv, int32_t *status_dev, int32_t timeout_ms,
+                                     void *stream, int *status_host) {
     if (n < 0 || n_super < 0 || n_tasks < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
     if (n_super > 0 && (!task_super || !task_strip || !sn || !Lip || !Li || !Lp || !Lx ||
                         !col_to_super || !pending || !solved || !x))
@@ -312,7 +327,8 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
         LCD_CUDA_TRY(cudaMemsetAsync(solved, 0, (size_t)n_super * sizeof(int32_t), st));
         SupernodalParams p{n_super, n_tasks, task_super, task_strip, sn, Lip, Li,
                            reinterpret_cast<const long long *>(Lp), Lx, col_to_super, pending,
-                           solved, x, n, status_dev, timeout_ns(timeout_ms), tinv};
+                           solved, x, n, status_dev, timeout_ns(timeout_ms), inv_ptr ? inv : nullptr,
+                           reinterpret_cast<const long long *>(inv_ptr)};
         supernodal_kernel<<<n_tasks, kSnThreads, 0, st>>>(p);
         LCD_CUDA_TRY(cudaGetLastError());
     }

@@ -50,7 +50,8 @@ class SupernodalPlan:
     status: torch.Tensor
     panel_values: int
     flops: float
-    triangle_inverses: torch.Tensor | None = None
+    block_inverses: torch.Tensor | None = None      # inverse diagonal blocks, column-major
+    inverse_ptr: torch.Tensor | None = None         # int64 start of each supernode's inverse
 
     @property
     def algorithmic_bytes(self):
@@ -94,8 +95,9 @@ def _level_order(sn_h, Lip_h, Li_h, cts_h, n_super):
 
 def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda", invert_triangles=True):
     """Validate the layout, upload it and build the task list.  With ``invert_triangles`` the
-    32 x 32 triangles on the diagonal of every diagonal block are inverted once (numeric:
-    analyse again when the values change), which shortens the dependent chain of each solve.
+    triangular diagonal block of every supernode is inverted once (numeric: analyse again
+    when the values change; 8 * sum(width^2) bytes), which turns the dependent chain of each
+    diagonal solve into one pass of independent multiply-adds.
 
     Host work is O(n_super + n); the per-row counters are accumulated on the
     device.  ``Lx`` may already be a CUDA tensor (it is the large array).
@@ -146,18 +148,22 @@ def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda", inver
                                             ptr(pending), _stream()), "lcd_supernodal_pending")
     panel_values = int((width * length).sum())
     flops = float((width * width + 2 * width * (length - width)).sum())
-    tinv = None
+    inv = inv_ptr = None
     if invert_triangles and n_super:
-        tinv = torch.empty(32 * n, dtype=torch.float64, device=dev)
+        starts = np.zeros(n_super + 1, dtype=np.int64)
+        np.cumsum(width * width, out=starts[1:])
+        inv_ptr = up(starts, np.int64)
+        inv = torch.empty(int(starts[-1]), dtype=torch.float64, device=dev)
         check(nat.load().lcd_supernodal_prepare(n_super, ptr(t_sn), ptr(t_Lip), ptr(t_Lp), ptr(t_Lx),
-                                                ptr(tinv), _stream()), "lcd_supernodal_prepare")
+                                                ptr(inv_ptr), ptr(inv), _stream()),
+              "lcd_supernodal_prepare")
     return SupernodalPlan(
         n=n, n_super=n_super, n_tasks=int(first[-1]), sn=t_sn, Lip=t_Lip, Li=t_Li, Lp=t_Lp,
         Lx=t_Lx, col_to_super=t_cts, task_super=up(task_super, np.int32),
         task_strip=up(task_strip, np.int32), initial_pending=pending,
         pending=torch.empty_like(pending),
         solved=torch.empty(n_super, dtype=torch.int32, device=dev), status=new_status(dev),
-        panel_values=panel_values, flops=flops, triangle_inverses=tinv)
+        panel_values=panel_values, flops=flops, block_inverses=inv, inverse_ptr=inv_ptr)
 
 
 def solve(plan: SupernodalPlan, b, x=None, timeout_ms=0, sync=True):
@@ -171,7 +177,7 @@ def solve(plan: SupernodalPlan, b, x=None, timeout_ms=0, sync=True):
         plan.n, plan.n_super, plan.n_tasks, ptr(plan.task_super), ptr(plan.task_strip),
         ptr(plan.sn), ptr(plan.Lip), ptr(plan.Li), ptr(plan.Lp), ptr(plan.Lx),
         ptr(plan.col_to_super), ptr(plan.pending), ptr(plan.solved), ptr(x),
-        ptr(plan.triangle_inverses), ptr(plan.status),
+        ptr(plan.inverse_ptr), ptr(plan.block_inverses), ptr(plan.status),
         int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
     check(rc, "lcd_sptrsv_supernodal")
     return x

@@ -462,14 +462,14 @@ def test_supernodal_medium(cuda, oracle):
     s = gen.supernodal_random(n=20_000, seed=3, widths=(16, 32, 64, 128), min_targets=4, max_targets=12)
     want = oracle.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
     L = s.to_csc().tocsr()
-    for invert in (True, False):      # with the inverted 32 x 32 triangles, and step by step
+    for invert in (True, False):      # with the inverted diagonal blocks, and step by step
         plan = supernodal.analyse(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.col_to_super, invert_triangles=invert)
-        assert (plan.triangle_inverses is not None) == invert
+        assert (plan.block_inverses is not None) == invert
         x = host(supernodal.solve(plan, dev(s.b, np.float64, cuda)))
         np.testing.assert_allclose(x, want, rtol=1e-9, atol=1e-12)
         assert np.linalg.norm(L @ x - s.b) / np.linalg.norm(s.b) <= RESIDUAL_TOL
-    # widths that are not multiples of 32 (short last triangle)
-    s = gen.supernodal_random(n=3_000, seed=5, widths=(5, 17, 40, 70), min_targets=2, max_targets=6)
+    # widths that are no powers of two, and some wider than a thread block
+    s = gen.supernodal_random(n=6_000, seed=5, widths=(5, 17, 40, 70, 300), min_targets=2, max_targets=6)
     plan = supernodal.analyse(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.col_to_super)
     x = host(supernodal.solve(plan, dev(s.b, np.float64, cuda)))
     np.testing.assert_allclose(x, oracle.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b), rtol=1e-9, atol=1e-12)
