@@ -119,17 +119,17 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         for (int r = tid % wp; r < w; r += wp) {       // (one trip unless w > 256)
             double y0 = 0.0, y1 = 0.0;
             int c = sub;
-            for (; c + 7 * tpr <= r; c += 8 * tpr) {   // eight loads in flight
-                double m[8];
+            for (; c <= r; c += 16 * tpr) {            // sixteen loads in flight, the tail masked
+                double m[16];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) m[u] = __ldg(inv + (long long)(c + u * tpr) * w + r);
+                for (int u = 0; u < 16; ++u)
+                    m[u] = c + u * tpr <= r ? __ldg(inv + (long long)(c + u * tpr) * w + r) : 0.0;
 #pragma unroll
-                for (int u = 0; u < 8; u += 2) {
-                    y0 = fma(m[u], xs[c + u * tpr], y0);
-                    y1 = fma(m[u + 1], xs[c + (u + 1) * tpr], y1);
+                for (int u = 0; u < 16; u += 2) {
+                    y0 = fma(m[u], xs[min(c + u * tpr, w - 1)], y0);
+                    y1 = fma(m[u + 1], xs[min(c + (u + 1) * tpr, w - 1)], y1);
                 }
             }
-            for (; c <= r; c += tpr) y0 = fma(__ldg(inv + (long long)c * w + r), xs[c], y0);
             if (tpr == 1) ys[r] = y0 + y1;
             else part[sub * wp + r] = y0 + y1;
         }
