@@ -309,7 +309,7 @@ int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const int32_t *Li
  * like every other strip, multiplies lcd_supernodal_strip_rows() rows of the
  * off-diagonal panel starting at row task_strip[t] * strip_rows.  Every supernode
  * needs its strip-0 task even when it has no off-diagonal rows.
- *   solved[n_super]   scratch flags (zeroed by the call)
+ *   solved[n]         scratch (doubles): x as published for the waiting strips
  *   supernode widths are limited to 1024 columns (LCD_ERR_TOO_LARGE)
  */
 int lcd_supernodal_strip_rows(void);
@@ -317,7 +317,7 @@ int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
                           const int32_t *task_super, const int32_t *task_strip,
                           const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                           const int64_t *Lp, const double *Lx, const int32_t *col_to_super,
-                          int32_t *pending, int32_t *solved, double *x, const int64_t *inv_ptr,
+                          int32_t *pending, double *solved, double *x, const int64_t *inv_ptr,
                           const double *inv, int32_t *status_dev, int32_t timeout_ms, void *stream,
                           int *status_host);
 /*

@@ -1,14 +1,17 @@
 // Sync-free supernodal lower-triangular solve on column-major panels (sm_100a).
 //
-// Work is cut into tasks handed out by ticket in supernode order (a topological
-// order): task (s, 0) waits until every update into the columns of supernode s
-// has arrived (pending[s] == 0), solves the dense w x w diagonal block in 32-column
-// steps (a warp solves the 32 x 32 triangle with shuffles, the block then applies
-// the 32 solved values to the rows below), publishes x_s and raises solved[s];
-// tasks (s, q) stream one strip of the off-diagonal panel (coalesced down the
-// columns), subtract the strip's product from x with fp64 atomics and release
-// the target supernodes' counters, one decrement per distinct target per warp.
-// The solve is HBM-bound: every panel value is read exactly once.
+// Work is cut into tasks handed out by ticket in dependence-level order (a topological
+// order): task (s, 0) waits until every update into the columns of supernode s has arrived
+// (pending[s] == 0), solves the dense w x w diagonal block - by one product with its inverse
+// when lcd_supernodal_prepare was run (independent loads and multiply-adds), else in
+// 32-column steps (a warp solves the 32 x 32 triangle with shuffles, the block then applies
+// the 32 solved values to the rows below) - and publishes x_s into a second vector whose
+// reserved-NaN pre-fill makes each value its own ready flag; tasks (s, q) wait for those
+// values, stream one strip of the off-diagonal panel (coalesced down the columns, sixteen
+// loads in flight per thread, the strip pulled towards L2 while the task waits), subtract
+// the strip's product from x with fp64 atomics and release the target supernodes' counters,
+// one decrement per distinct target per warp.  Every panel value is read exactly once; what
+// keeps the solve below the HBM roofline is the critical path through the supernode DAG.
 #include "common.cuh"
 
 namespace lcd {
@@ -28,7 +31,7 @@ struct SupernodalParams {
     const double *__restrict__ Lx;
     const int *__restrict__ col_to_super;
     int *pending;
-    int *solved;
+    double *solved;   // x_s as published for the strips (pre-filled with the reserved NaN)
     double *x;
     int n;
     int32_t *status;
@@ -89,22 +92,38 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         }
     }
     // ---- wait for the inputs of this task --------------------------------
-    if (tid == 0) {
+    // Strip 0 waits for the last update into its columns (a counter, then the values); the
+    // other strips wait for x_s itself: the solved values are published into a second vector
+    // that was pre-filled with a reserved NaN, so a value is its own ready flag and a strip
+    // needs one round trip to L2 instead of two (flag, then values) and no fence.
+    if (strip == 0) {
+        if (tid == 0) {
+            Deadline dl;
+            dl.start(p.budget_ns);
+            int ok = 1;
+            for (;;) {
+                if (ld_relaxed_s32(p.pending + s) == 0) { acquire_fence(); break; }
+                if (dl.tick(p.status, s)) { ok = 0; break; }
+            }
+            s_ok = ok;
+        }
+        __syncthreads();
+        if (!s_ok) return;
+        for (int c = tid; c < w; c += kSnThreads) xs[c] = ld_relaxed_f64(p.x + c0 + c);
+    } else {
+        if (tid == 0) s_ok = 1;
+        __syncthreads();
         Deadline dl;
         dl.start(p.budget_ns);
-        int ok = 1;
-        const int *flag = strip == 0 ? p.pending + s : p.solved + s;
-        const int want_zero = strip == 0;
-        for (;;) {
-            const int v = ld_relaxed_s32(flag);
-            if (want_zero ? v == 0 : v != 0) { acquire_fence(); break; }
-            if (dl.tick(p.status, s)) { ok = 0; break; }
+        for (int c = tid; c < w; c += kSnThreads) {
+            double v;
+            while (is_pending(v = ld_relaxed_f64(p.solved + c0 + c)))
+                if (dl.tick(p.status, s)) { s_ok = 0; break; }
+            xs[c] = v;
         }
-        s_ok = ok;
+        __syncthreads();
+        if (!s_ok) return;
     }
-    __syncthreads();
-    if (!s_ok) return;
-    for (int c = tid; c < w; c += kSnThreads) xs[c] = ld_relaxed_f64(p.x + c0 + c);
     __syncthreads();
     if (strip == 0 && p.inv) {
         // ---- x_s = T^-1 v with the inverse of the diagonal block (lcd_supernodal_prepare): one
@@ -188,11 +207,9 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
         }
     }
     if (strip == 0) {
-        for (int c = tid; c < w; c += kSnThreads) st_relaxed_f64(p.x + c0 + c, xs[c]);
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            st_release_s32(p.solved + s, 1);
+        for (int c = tid; c < w; c += kSnThreads) {
+            st_relaxed_f64(p.solved + c0 + c, publishable(xs[c]));   // what the strips wait for
+            st_relaxed_f64(p.x + c0 + c, xs[c]);
         }
     }
     // ---- one strip of the off-diagonal panel -------------------------------
@@ -313,7 +330,7 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
                                      const int32_t *sn, const int32_t *Lip, const int32_t *Li,
                                      const int64_t *Lp, const double *Lx,
                                      const int32_t *col_to_super, int32_t *pending,
-                                     int32_t *solved, double *x, const int64_t *inv_ptr,
+                                     double *solved, double *x, const int64_t *inv_ptr,
                                      const double *inv, int32_t *status_dev, int32_t timeout_ms,
                                      void *stream, int *status_host) {
     if (n < 0 || n_super < 0 || n_tasks < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
@@ -324,7 +341,7 @@ extern "C" int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks
     int rc = reset_status(status_dev, st);
     if (rc) return rc;
     if (n_super > 0 && n_tasks > 0) {
-        LCD_CUDA_TRY(cudaMemsetAsync(solved, 0, (size_t)n_super * sizeof(int32_t), st));
+        LCD_CUDA_TRY(cudaMemsetAsync(solved, 0xFF, (size_t)n * sizeof(double), st));
         SupernodalParams p{n_super, n_tasks, task_super, task_strip, sn, Lip, Li,
                            reinterpret_cast<const long long *>(Lp), Lx, col_to_super, pending,
                            solved, x, n, status_dev, timeout_ns(timeout_ms), inv_ptr ? inv : nullptr,

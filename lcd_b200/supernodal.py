@@ -162,7 +162,7 @@ def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda", inver
         Lx=t_Lx, col_to_super=t_cts, task_super=up(task_super, np.int32),
         task_strip=up(task_strip, np.int32), initial_pending=pending,
         pending=torch.empty_like(pending),
-        solved=torch.empty(n_super, dtype=torch.int32, device=dev), status=new_status(dev),
+        solved=torch.empty(max(n, 1), dtype=torch.float64, device=dev), status=new_status(dev),
         panel_values=panel_values, flops=flops, block_inverses=inv, inverse_ptr=inv_ptr)
 
 
