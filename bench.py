@@ -194,6 +194,26 @@ def measured_peak_gbs():
         return 6650.0, "fallback"
 
 
+def bind_to_gpu_cpus(gpu_index):
+    """Run this process on the CPUs next to its GPU (NVML's affinity mask), so that pinned host
+    buffers are first touched on the memory node the PCIe link hangs off: host<->device copies
+    of the end-to-end measurement otherwise lose up to half their bandwidth on two-socket
+    hosts.  A process setting only; nothing of the GPU is changed."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception as error:   # no NVML, no permission: measure where we are
+        log("cpu affinity not set:", error)
+        return None
+
+
 def run_native(args):
     import torch
     import torch.distributed as dist
@@ -202,6 +222,7 @@ def run_native(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    cpu_affinity = bind_to_gpu_cpus(local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
@@ -331,7 +352,7 @@ def run_native(args):
                          "peak_kind": peak_kind,
                          "kernel": kernel_name,
                          "kernel_ms": extras.get("solve_ms", kernel_ms)},
-            "cpu_baseline": cpu_baseline, "clocks": clocks,
+            "cpu_baseline": cpu_baseline, "clocks": clocks, "cpus_near_gpu": cpu_affinity,
             "effective_gbs": world * achieved, "residual": residual,
         }
         line.update(extras)
@@ -354,8 +375,10 @@ def measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier):
     torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
+    marks = [t0]
     for _ in range(steps):
         out = op(*pinned, n)
+        marks.append(time.perf_counter())
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
     if world > 1:
@@ -364,9 +387,18 @@ def measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier):
         elapsed = float(t.item())
     per_call = elapsed / steps
     h2d = sum(a.nbytes for a in pinned)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    copies = [torch.from_numpy(a).to(dev, non_blocking=True) for a in pinned]
+    e1.record()
+    torch.cuda.synchronize()
+    h2d_ms = e0.elapsed_time(e1)
+    del copies
     return {"value": world * flops(n, nnz) / per_call / 1e9, "unit": UNIT,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(out.nbytes),
             "ms_per_call": per_call * 1e3, "calls": steps,
+            "h2d_copy_alone_ms": h2d_ms, "h2d_gb_per_s": h2d / h2d_ms / 1e6,
+            "ms_each_call": [round((b - a) * 1e3, 2) for a, b in zip(marks, marks[1:])],
             "api": "lcd_b200.decorator.parallel(...)(sptrsv_csr)(Ap, Ai, Ax, b, n)"}
 
 
