@@ -371,13 +371,16 @@ enum {
     LCD_TUNE_SLEEP_GLOBAL_NS = 1, /* pause after a failed poll of another chunk's row */
     LCD_TUNE_GAP_NS = 2,          /* extra pause per row the producer's warp still owes */
     LCD_TUNE_ROW_VARIANT = 3,     /* 0: thread-per-row kernel, 1: generic lane-group kernel */
-    LCD_TUNE_STAGE_PERCENT = 4    /* shared-memory staging of a chunk's matrix entries, in percent
+    LCD_TUNE_STAGE_PERCENT = 4,   /* shared-memory staging of a chunk's matrix entries, in percent
                                      of the average chunk size (0 = read entries from global) */
+    LCD_TUNE_CHAIN_CLUSTER = 5    /* blocks per cluster of the chain solver: 0 = as many as the device
+                                     hosts (up to 8), 1 = plain blocks, 2 / 4 / 8 = at most that */
 };
 int lcd_set_tuning(int key, int value);
-/* Profiling aid (no reference counterpart): with a non-NULL device array of n 64-bit
- * words, the one-lane-per-row solver records the SM cycle counter at which each node
- * was published.  Pass NULL to switch it off again. */
+/* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,
+ * the one-lane-per-row solver (n words) and the chain solver (3 n + 128 K words: row stamps,
+ * per-chunk start times and wait counters) record SM cycle counters and timer values.  Pass
+ * NULL to switch it off again. */
 int lcd_debug_set_trace(long long *trace_dev);
 
 /* ---- small device utilities used by the host layer ---------------------------- */

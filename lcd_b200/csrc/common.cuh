@@ -40,6 +40,7 @@ inline unsigned long long timeout_ns(int32_t timeout_ms) {
 }
 int sm_count();
 void set_debug_trace(long long *p);
+int set_chain_cluster_limit(int blocks);  // LCD_TUNE_CHAIN_CLUSTER
 long long *debug_trace();  // profiling aid set by lcd_debug_set_trace (NULL = off)
 
 #ifdef __CUDACC__

@@ -868,6 +868,16 @@ static size_t chain_smem_bytes(int *cap_out) {
 using namespace lcd;
 
 static int g_last_cluster = 0;
+static int g_cluster_limit = 0;   // 0: as many as the device hosts
+
+namespace lcd {
+int set_chain_cluster_limit(int blocks) {
+    if (blocks != 0 && blocks != 1 && blocks != 2 && blocks != 4 && blocks != 8)
+        return LCD_ERR_INVALID_ARGUMENT;
+    g_cluster_limit = blocks;
+    return LCD_OK;
+}
+}  // namespace lcd
 
 extern "C" int lcd_chain_cluster_size(void) { return g_last_cluster; }
 
@@ -932,20 +942,21 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
         // clusters of up to eight blocks (consecutive chunks hand over through shared memory);
         // where the device cannot host such a cluster the same kernel runs as plain blocks
         int cluster = 1;
-        if (chunks > 1) {
+        const int wanted = g_cluster_limit ? g_cluster_limit : kChainCluster;
+        for (int size = wanted; size > 1 && chunks > 1 && cluster == 1; size >>= 1) {
             cudaLaunchConfig_t probe = {};
-            probe.gridDim = dim3(kChainCluster);
+            probe.gridDim = dim3(size);
             probe.blockDim = dim3(kChainThreads);
             probe.dynamicSmemBytes = smem;
             cudaLaunchAttribute attr;
             attr.id = cudaLaunchAttributeClusterDimension;
-            attr.val.clusterDim.x = kChainCluster;
+            attr.val.clusterDim.x = size;
             attr.val.clusterDim.y = attr.val.clusterDim.z = 1;
             probe.attrs = &attr;
             probe.numAttrs = 1;
             int fit = 0;
             if (cudaOccupancyMaxActiveClusters(&fit, kernel, &probe) == cudaSuccess && fit > 0)
-                cluster = kChainCluster;
+                cluster = size;
             else
                 cudaGetLastError();
         }

@@ -582,6 +582,7 @@ extern "C" int lcd_set_tuning(int key, int value) {
         case LCD_TUNE_GAP_NS: g_row_tuning.gap_ns = value; break;
         case LCD_TUNE_ROW_VARIANT: g_row_tuning.variant = value; break;
         case LCD_TUNE_STAGE_PERCENT: g_row_tuning.stage_percent = value; break;
+        case LCD_TUNE_CHAIN_CLUSTER: return set_chain_cluster_limit(value);
         default: return LCD_ERR_INVALID_ARGUMENT;
     }
     return LCD_OK;

@@ -205,6 +205,28 @@ def test_csr_chain_solver(cuda, oracle):
     np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(L.indptr, L.indices, L.data, b), rtol=1e-10, atol=1e-12)
 
 
+def test_csr_chain_solver_cluster_sizes(cuda, oracle):
+    """Consecutive chunks hand over through distributed shared memory inside a cluster and through
+    L2 across clusters (or everywhere, for plain blocks): every cluster size gives the solution."""
+    from lcd_b200 import _native as nat, generators as gen, ops
+    lib = nat.load()
+    tri = gen.random_band_lower(40_000, seed=11, mean_degree=15.0, band=64)     # 40 chunks, the last partial
+    Ap, Ai, Ax = tri.csr_arrays()
+    want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+    used = []
+    try:
+        for limit in (1, 2, 4, 8, 0):
+            assert lib.lcd_set_tuning(nat.TUNE_CHAIN_CLUSTER, limit) == 0
+            x = _chain_solve(ops, cuda, Ap, Ai, Ax, tri.b)
+            np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+            used.append(lib.lcd_chain_cluster_size())
+            assert used[-1] >= 1 and (limit == 0 or used[-1] <= limit)
+        assert lib.lcd_set_tuning(nat.TUNE_CHAIN_CLUSTER, 3) != 0
+    finally:
+        lib.lcd_set_tuning(nat.TUNE_CHAIN_CLUSTER, 0)
+    assert used[0] == 1
+
+
 def test_csr_chain_solver_on_ilu_factors_and_errors(cuda, oracle):
     from lcd_b200 import generators as gen, ops
     from lcd_b200._native import ERR_INDEX_RANGE, ERR_WORKSPACE, NativeError
