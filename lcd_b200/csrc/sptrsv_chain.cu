@@ -613,7 +613,14 @@ csr_chain_kernel(const ChainParams q) {
         // ---- main warp: x_b = y_b + z_b - W1_b x_b-1 --------------------------------------
         // The loop always runs to the end and always performs its barrier operations (the
         // partner warp blocks on them); after a failed wait it only publishes NaN.
-        if (TRACE && lane == 0) { p.trace[2ll * p.n + chunk] = clock64(); p.trace[2ll * p.n + 65536 + 4 * chunk] = (long long)global_timer(); }
+        // Trace layout (64-bit words, C = number of chunks): [0, n) cycle counter at each row's
+        // publication; [2n, 2n + C) cycle counter at the main warp's start; 2n + C + 4 chunk + k:
+        // timer (ns) at main start, halo complete, first and last publication; 2n + 5C +
+        // 8 chunk + k: cycles waited for tiles, number of such waits, cycles waited for y, number
+        // of such waits, cycles at the partner barrier.
+        const long long n_chunks = (p.n + kChainRows - 1) / kChainRows;
+        long long *chunk_times = TRACE ? p.trace + 2ll * p.n + n_chunks + 4ll * chunk : nullptr;
+        if (TRACE && lane == 0) { p.trace[2ll * p.n + chunk] = clock64(); chunk_times[0] = (long long)global_timer(); }
         const double nanv = __longlong_as_double(kCanonicalNaN);
         bool dead = *failed_flag != 0;
         // the two blocks before the chunk (the partner can start on z_0 as soon as the
@@ -640,7 +647,7 @@ csr_chain_kernel(const ChainParams q) {
         // warp issues one about every four cycles), so it carries nothing it can do without:
         // the partner releases the ring stages and reports its own failures through a NaN z,
         // the barrier operations are unconditional (the partner runs two extra steps for them).
-        if (TRACE && lane == 0) p.trace[2ll * p.n + 65536 + 4 * chunk + 1] = (long long)global_timer();
+        if (TRACE && lane == 0) chunk_times[1] = (long long)global_timer();
         double ynext = syv[lane];
         int tiles = 0;   // tiles known to have landed
         const int step = upper ? -32 : 32;
@@ -692,7 +699,7 @@ csr_chain_kernel(const ChainParams q) {
             if (kPush) st_cluster_f64(next_halo + kParity * 256, val);   // the next chunk's halo
             if (local < rows_here) {
                 st_relaxed_f64(xout, val);
-                if (TRACE) { p.trace[row0 + local] = clock64(); if (lane == 0 && (b == 0 || b == nblk - 1)) p.trace[2ll * p.n + 65536 + 4 * chunk + (b == 0 ? 2 : 3)] = (long long)global_timer(); }
+                if (TRACE) { p.trace[row0 + local] = clock64(); if (lane == 0 && (b == 0 || b == nblk - 1)) chunk_times[b == 0 ? 2 : 3] = (long long)global_timer(); }
             }
             __syncwarp();
             pair_arrive(kParity ? kBarX1 : kBarX0);        // "x_b is there"
@@ -711,7 +718,7 @@ csr_chain_kernel(const ChainParams q) {
             step_block(nblk - 1, std::integral_constant<int, 1>(), std::true_type());
         }
         if (TRACE && lane == 0) {
-            long long *o = p.trace + 2ll * p.n + 65536 + 4 * 8192 + 8 * chunk;
+            long long *o = p.trace + 2ll * p.n + 5 * n_chunks + 8ll * chunk;
             o[0] = tile_wait_; o[1] = tile_waits_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_;
         }
         if (dead && lane == 0) *failed_flag = 1;
