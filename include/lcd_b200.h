@@ -161,11 +161,12 @@ int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int
  * Block-recurrence chain solver for CSR systems whose levels hold only a few rows (long
  * dependence chains).  No counterpart in the reference, which substitutes level by level;
  * it serves the same loop nest (compiler/demo/sptrsv.py:26-34) and returns the same x up
- * to rounding.  Rows are taken in blocks of 32; lcd_chain_prepare (numeric: repeat it
+ * to rounding.  Rows are taken in blocks of 64; lcd_chain_prepare (numeric: repeat it
  * whenever Ax changes; fully parallel) stores per block the inverse of the diagonal
- * block and its products with the couplings to the two blocks before; lcd_sptrsv_csr_chain
- * then advances one dense 32 x 32 mat-vec per block instead of 5-6 dependent levels.
- *   workspace: lcd_chain_workspace_bytes(n) bytes (24 KiB per 32 rows), 16-byte aligned.
+ * block and its product with the coupling to the block before; lcd_sptrsv_csr_chain
+ * then advances one dense 64 x 64 mat-vec (four warps) per block instead of about a dozen
+ * dependent levels.
+ *   workspace: lcd_chain_workspace_bytes(n) bytes (56 KiB per 64 rows), 16-byte aligned.
  *   flags: LCD_SOLVE_UPPER / OF_FULL / UNIT_DIAG as for lcd_sptrsv_csr_syncfree.
  * Explicit inverses are safe for diagonally dominant blocks; for other matrices prefer
  * lcd_sptrsv_csr_syncfree.

@@ -47,45 +47,61 @@
 // lcd_sptrsv_csr_syncfree instead.
 #include "common.cuh"
 
+#include <cstdlib>
 #include <type_traits>
 
 namespace lcd {
 
-constexpr int kChainThreads = 256;                    // main warp, six helper warps, loader warp
+constexpr int kChainThreads = 256;                    // four main warps, three helpers, loader warp
 constexpr int kChainWorkers = 256;
 constexpr int kChainRows = 1024;                      // rows per chunk
 constexpr int kChainRowsPerThread = kChainRows / kChainWorkers;
-constexpr int kChainBlocks = kChainRows / 32;
-constexpr int kChainHelpers = 5;
-constexpr int kChainStages = 8;                       // ring of (W1, W2) tile pairs
+constexpr int kChainBlocks = kChainRows / 32;         // 32-row halves (operand strips are per half)
+constexpr int kChainPairs = kChainRows / 64;          // 64-row blocks
+constexpr int kChainMain = 4;                         // main warps
+constexpr int kChainHelpers = 3;
+constexpr int kChainStages = 4;                       // ring of T tiles (32 KB per stage)
 constexpr int kTileDoubles = 1024;
-constexpr int kBlockDoubles = 3 * kTileDoubles;       // per 32-row block: D^-1, W1, W2
-constexpr int kChainHalo = 64;                        // the two blocks before the chunk
+constexpr int kPairDoubles = 7 * kTileDoubles;        // per 64-row block: M11, M21, M22, T00, T01, T10, T11
+constexpr int kPairT = 3 * kTileDoubles;              // offset of the four T tiles
+constexpr int kStageDoubles = 4 * kTileDoubles;
+constexpr int kChainHalo = 64;                        // the block before the chunk
 constexpr int kChainGate = 3;                         // chunks ahead at which pending operands are polled
 constexpr int kChainCluster = 8;                      // blocks per cluster (portable maximum)
 constexpr int kStatusDone = 6;                        // status word: chunks finished
 constexpr unsigned kFullMask = 0xffffffffu;
 
 // ---- numeric preparation ------------------------------------------------------------
-// Three warps per 32-row block, one per tile, each walking the block's rows in order.  Row r
-// of D^-1, W1 and W2 all satisfy the same recurrence
+// One thread block per 64-row block, seven warps.  Each warp walks the rows of one 32-row
+// half in order and builds one 32 x 32 tile: row r of every tile satisfies the same recurrence
 //        row_r = (rhs_r - sum_{k<r} D[r][k] row_k) / D[r][r]
-// with right-hand sides e_r, L_b,b-1[r][:] and L_b,b-2[r][:]; lane c carries column c of the
-// warp's row.  Only the stored entries are visited: a row's entries are loaded 32 at a time,
-// the ones that matter to the warp are found with a ballot and handed round with shuffles.
-// (The recurrences do not read one another, so the warps never synchronise; three warps on
-// the latency-bound walk instead of one is what the split buys.)
-__global__ void __launch_bounds__(96)
-chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_blocks) {
-    __shared__ double tiles[3][32][33];
-    const int lane = threadIdx.x & 31;
-    const int which = threadIdx.x >> 5;          // 0: D^-1, 1: W1 (block before), 2: W2 (two before)
-    double (*T)[33] = tiles[which];
-    const int gb = blockIdx.x;
-    if (gb >= n_blocks) return;
+// (D the half's own diagonal block) with right-hand sides e_r (the inverse of D) or row r of
+// the coupling to the half one, two or three halves back; lane c carries column c.  Only the
+// stored entries are visited: a row's entries are loaded 32 at a time, the ones that matter
+// to the warp are found with a ballot and handed round with shuffles.  The walks do not read
+// one another.  Top half (b): M11 = D_b^-1, W1 = M11 L_b,b-1, W2 = M11 L_b,b-2.  Bottom half
+// (b+1): M22 = D_b+1^-1, V1 = M22 L_b+1,b, V2 = M22 L_b+1,b-1, V3 = M22 L_b+1,b-2.
+// Eliminating x_b from the bottom half's equation then takes three dense products:
+//        M21 = -V1 M11,   T11 = V2 - V1 W1,   T10 = V3 - V1 W2       (T00 = W2, T01 = W1).
+// Tiles sit in shared memory with column c of row r at r * 32 + (c ^ r): rows and columns are
+// both read without bank conflicts, and seven tiles fit four blocks to an SM.
+constexpr int kPrepThreads = 224;
+constexpr int kPrepSmemBytes = 7 * kTileDoubles * 8;
+__device__ __forceinline__ int swz(int row, int col) { return row * 32 + (col ^ row); }
+
+__global__ void __launch_bounds__(kPrepThreads)
+chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_pairs) {
+    extern __shared__ __align__(16) double prep_tiles[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int odd = warp >= 3;                   // bottom half
+    const int which = odd ? warp - 3 : warp;     // 0: inverse, k: coupling to the half k back
+    double *T = prep_tiles + warp * kTileDoubles;
+    const int gp = blockIdx.x;
+    if (gp >= n_pairs) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
-    const int base = gb * 32;
-    const int mine = which == 0 ? 3 : 3 - which;  // entry kind that feeds this tile's right-hand side
+    const int base = (gp * 2 + odd) * 32;
+    // entry kinds: 1, 2, 3 = three, two, one half back, 4 = this half (before row r)
+    const int mine = 4 - which;
     int lo = 0, hi = 0;
     double diag = 1.0;  // rows past the end, and rows with bad pointers, act as identity rows
     {
@@ -124,36 +140,67 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_bloc
                 ca = 0.0;
                 if (j0 + lane < rhi) { cc = __ldg(p.Ai + j0 + lane); ca = __ldg(p.Ax + j0 + lane); }
             }
-            // kind 1: two blocks back, 2: the block before, 3: this block (before row r)
             int kind = 0, col = 0;
             if ((unsigned)cc < (unsigned)p.n) {
                 const int tc = upper ? p.n - 1 - cc : cc;
-                const int off = tc - (base - 64);
+                const int off = tc - (base - 96);
                 if (off >= 0 && tc < base + r) { kind = 1 + (off >> 5); col = off & 31; }
             }
-            unsigned todo = __ballot_sync(kFullMask, kind == 3 || kind == mine);
+            unsigned todo = __ballot_sync(kFullMask, kind == 4 || kind == mine);
             while (todo) {
                 const int src = __ffs(todo) - 1;
                 todo &= todo - 1;
                 const int kd = __shfl_sync(kFullMask, kind, src);
                 const int c = __shfl_sync(kFullMask, col, src);
                 const double av = __shfl_sync(kFullMask, ca, src);
-                if (kd == 3) acc = fma(-av, T[c][lane], acc);
+                if (kd == 4) acc = fma(-av, T[swz(c, lane)], acc);
                 else if (lane == c) acc += av;
             }
         }
-        T[r][lane] = acc / d;
+        T[swz(r, lane)] = acc / d;
         __syncwarp();
     }
-    // D^-1: element (r, k) at k * 32 + r (a helper lane r loads its row coalesced);
-    // W tiles: elements (r, 2q) and (r, 2q + 1) side by side at (q * 32 + r) * 2, so that the
-    // main warp's lane r reads its row with 16-byte loads that do not conflict
-    double *out = ws + (long long)gb * kBlockDoubles + which * kTileDoubles;
-    if (which == 0) {
-        for (int k = 0; k < 32; ++k) out[k * 32 + lane] = T[lane][k];
+    __syncthreads();
+    // Output layouts.  Inverse tiles (M11, M21, M22): element (r, k) at k * 32 + r, so that lane
+    // r of a warp applying them loads its row coalesced.  T tiles: elements (r, 2q), (r, 2q + 1)
+    // side by side at (q * 32 + r) * 2, so that lane r of a main warp reads its row from shared
+    // memory with 16-byte loads that do not conflict.
+    const double *tM11 = prep_tiles, *tW1 = tM11 + kTileDoubles, *tW2 = tW1 + kTileDoubles;
+    const double *tM22 = tW2 + kTileDoubles, *tV1 = tM22 + kTileDoubles, *tV2 = tV1 + kTileDoubles;
+    const double *tV3 = tV2 + kTileDoubles;
+    double *out = ws + (long long)gp * kPairDoubles;
+    if (warp == 6) {
+        double2 *o00 = reinterpret_cast<double2 *>(out + kPairT);
+        double2 *o01 = o00 + kTileDoubles / 2;
+        for (int k = 0; k < 32; ++k) {
+            out[k * 32 + lane] = tM11[swz(lane, k)];
+            out[2 * kTileDoubles + k * 32 + lane] = tM22[swz(lane, k)];
+        }
+        for (int q = 0; q < 16; ++q) {
+            o00[q * 32 + lane] = make_double2(tW2[swz(lane, 2 * q)], tW2[swz(lane, 2 * q + 1)]);
+            o01[q * 32 + lane] = make_double2(tW1[swz(lane, 2 * q)], tW1[swz(lane, 2 * q + 1)]);
+        }
     } else {
-        double2 *o = reinterpret_cast<double2 *>(out);
-        for (int q = 0; q < 16; ++q) o[q * 32 + lane] = make_double2(T[lane][2 * q], T[lane][2 * q + 1]);
+        // products: warp pair 0 -> M21, 1 -> T11, 2 -> T10; each warp 16 columns, lane = row
+        const int prod = warp >> 1, c0 = (warp & 1) * 16;
+        const double *X = prod == 0 ? tM11 : prod == 1 ? tW1 : tW2;
+        const double *S = prod == 1 ? tV2 : tV3;
+        double acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = prod == 0 ? 0.0 : S[swz(lane, c0 + j)];
+        for (int k = 0; k < 32; ++k) {
+            const double v = tV1[swz(lane, k)];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = fma(-v, X[swz(k, c0 + j)], acc[j]);
+        }
+        if (prod == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[kTileDoubles + (c0 + j) * 32 + lane] = acc[j];
+        } else {
+            double2 *o = reinterpret_cast<double2 *>(out + kPairT + (prod == 1 ? 3 : 2) * kTileDoubles);
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) o[((c0 + j) / 2) * 32 + lane] = make_double2(acc[j], acc[j + 1]);
+        }
     }
 }
 
@@ -217,14 +264,21 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned b
 __device__ __forceinline__ void chain_prefetch_l2(const void *ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
-// Named barriers between the main warp and its partner (64 threads: one warp arrives, the
-// other waits).  They have no timeout, so both warps perform them unconditionally.
-constexpr int kBarX0 = 2, kBarX1 = 3, kBarZ0 = 4, kBarZ1 = 5;
+__device__ __forceinline__ void chain_prefetch_l1(const void *ptr) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr));
+}
+// Named barriers of the main warps.  A row half's two warps meet at kBarZ0 + half (64 threads:
+// the warp with the partial sum arrives, the finishing warp waits); all four meet at kBarStep
+// once per block.  Named barriers have no timeout, so every warp performs them unconditionally.
+constexpr int kBarZ0 = 2, kBarStep = 4;
 __device__ __forceinline__ void pair_arrive(int id) {
     asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory");
 }
 __device__ __forceinline__ void pair_sync(int id) {
     asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ void step_sync() {
+    asm volatile("bar.sync %0, %1;" ::"n"(kBarStep), "n"(kChainMain * 32) : "memory");
 }
 // one arrival per warp, predicated instead of branched so that the warp stays converged
 __device__ __forceinline__ void mbar_arrive_lane0(unsigned long long *bar, int lane) {
@@ -292,19 +346,57 @@ struct ChainParams {
     CsrSolveParams m;
     const double *__restrict__ ws;
     int cap;  // capacity of the in-chunk operand list (entries)
+    int gate; // chunks ahead of its turn at which a chunk wakes up
 };
+
+// y += M d for one 64-row block (M11, M21, M22 at m11, element (r, k) at k * 32 + r, m11
+// already offset by the lane): shuffle / FMA pairs on independent accumulators
+__device__ __noinline__ void apply_inverse(const double *m11, double d0, double d1, double &ytop,
+                                           double &ybot) {
+    const double *m21 = m11 + kTileDoubles, *m22 = m21 + kTileDoubles;
+    double y0 = 0.0, y1 = 0.0, z0 = 0.0, z1 = 0.0, z2 = 0.0, z3 = 0.0;
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+        const double ta = __shfl_sync(kFullMask, d0, k), tb = __shfl_sync(kFullMask, d0, k + 1);
+        const double tc = __shfl_sync(kFullMask, d1, k), td = __shfl_sync(kFullMask, d1, k + 1);
+        y0 = fma(__ldg(m11 + k * 32), ta, y0);
+        y1 = fma(__ldg(m11 + (k + 1) * 32), tb, y1);
+        z0 = fma(__ldg(m21 + k * 32), ta, z0);
+        z1 = fma(__ldg(m21 + (k + 1) * 32), tb, z1);
+        z2 = fma(__ldg(m22 + k * 32), tc, z2);
+        z3 = fma(__ldg(m22 + (k + 1) * 32), td, z3);
+    }
+    ytop += y0 + y1;
+    ybot += (z0 + z1) + (z2 + z3);
+}
+
+// one 32 x 32 tile times one half of the previous block: lane r's row (16-byte loads that
+// do not conflict) against broadcast loads of x
+__device__ __forceinline__ double tile_matvec(const double2 *w, const double2 *xa, double a0) {
+    double a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+    for (int qd = 0; qd < 16; qd += 2) {
+        const double2 u0 = w[qd * 32], u1 = w[(qd + 1) * 32];
+        const double2 v0 = xa[qd], v1 = xa[qd + 1];
+        a0 = fma(-u0.x, v0.x, a0);
+        a1 = fma(-u0.y, v0.y, a1);
+        a2 = fma(-u1.x, v1.x, a2);
+        a3 = fma(-u1.y, v1.y, a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
 
 template <bool TRACE>
 __global__ void __launch_bounds__(kChainThreads, 1)
 csr_chain_kernel(const ChainParams q) {
     const CsrSolveParams &p = q.m;
     extern __shared__ __align__(128) unsigned char chain_smem[];
-    double *ring = reinterpret_cast<double *>(chain_smem);      // kChainStages x (W1, W2)
-    double *sxh = ring + kChainStages * 2 * kTileDoubles;        // halo, chunk, zero slot
+    double *ring = reinterpret_cast<double *>(chain_smem);      // kChainStages x (T00, T01, T10, T11)
+    double *sxh = ring + kChainStages * kStageDoubles;           // halo, chunk, zero slot
     double *sx = sxh + kChainHalo;                               // x of the chunk (chunk-local index)
     double *sacc = sx + kChainRows + 2;                          // partial sums after phase A
-    double *sy = sacc + kChainRows;                              // y_b, produced by the helpers
-    unsigned long long *spend = reinterpret_cast<unsigned long long *>(sy + kChainRows + 32);  // operands from
+    double *sy = sacc + kChainRows;                              // y_B, from phase A or the helpers
+    unsigned long long *spend = reinterpret_cast<unsigned long long *>(sy + kChainRows + 64);  // operands from
                                                                  // before the chunk still pending per row
     double *eval = reinterpret_cast<double *>(spend + kChainRows);  // in-chunk operands: values
     int *ecol = reinterpret_cast<int *>(eval + q.cap);           // ... and chunk-local columns
@@ -312,11 +404,11 @@ csr_chain_kernel(const ChainParams q) {
     __shared__ unsigned long long s_empty[kChainStages];
     __shared__ int s_chunk;
     __shared__ int s_failed;
-    __shared__ int s_tiles;                                    // tiles of the ring that have landed
+    __shared__ int s_tiles;                                    // ring stages that have landed
     __shared__ int s_width[kChainBlocks];
     __shared__ int s_bptr[kChainBlocks + 1];
     __shared__ double s_z[2][32];
-    __shared__ int s_early[kChainBlocks];                      // y_b was computed in phase A
+    __shared__ int s_early[kChainPairs];                       // y_B was computed in phase A
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     volatile int *failed_flag = &s_failed;
     // One ticket per cluster: its blocks take consecutive chunks.  (A cluster is resident as a
@@ -342,38 +434,38 @@ csr_chain_kernel(const ChainParams q) {
     const int rows_here = min(kChainRows, p.n - row0);
     if (rows_here <= 0) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
-    const int nblk = (rows_here + 31) / 32;
-    const double *wsc = q.ws + (long long)(row0 / 32) * kBlockDoubles;
-    constexpr unsigned kTileBytes = 2 * kTileDoubles * sizeof(double);
+    const int npair = (rows_here + 63) / 64;
+    const double *wsc = q.ws + (long long)(row0 / 64) * kPairDoubles;
+    constexpr unsigned kStageBytes = kStageDoubles * sizeof(double);
     Deadline dl;
     dl.start(p.budget_ns);
 
-    // the first tiles of the ring are requested right away (nothing to wait for)
+    // the first stages of the ring are requested right away (nothing to wait for)
     int issued = 0;
     if (tid == kChainThreads - 32)
-        for (; issued < min(kChainStages, nblk); ++issued) {
-            mbar_expect_tx(&s_full[issued], kTileBytes);
-            bulk_load(ring + issued * 2 * kTileDoubles,
-                      wsc + (long long)issued * kBlockDoubles + kTileDoubles, kTileBytes,
-                      &s_full[issued]);
+        for (; issued < min(kChainStages, npair); ++issued) {
+            mbar_expect_tx(&s_full[issued], kStageBytes);
+            bulk_load(ring + issued * kStageDoubles, wsc + (long long)issued * kPairDoubles + kPairT,
+                      kStageBytes, &s_full[issued]);
         }
 
-    // ---- phase A: thread t owns rows t, t + 256, t + 512, t + 768 of the chunk ------------
-    // (the 32 lanes of a warp hold exactly the 32 rows of block warp + 8 k for each k)
-    // A1 (pattern only, nothing to wait for): operands in the chunk that lie three or more
-    // blocks back are counted, the per-block strips are laid out and filled.
+    // ---- phase A: a warp owns the 64-row blocks warp and warp + 8, a thread one row of each
+    // of their four halves (row k of the thread: half k & 1 of block warp + 8 (k >> 1)) ------
+    // A1 (pattern only, nothing to wait for): operands in the chunk that lie before the
+    // previous 64-row block are counted, the per-half strips are laid out and filled.
+    auto half_of = [&](int k) { return 2 * (warp + 8 * (k >> 1)) + (k & 1); };
     int lo_[kChainRowsPerThread], hi_[kChainRowsPerThread], cnt_[kChainRowsPerThread];
     bool failed = false;
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int local = tid + k * kChainWorkers;
+        const int local = half_of(k) * 32 + lane;
         lo_[k] = hi_[k] = cnt_[k] = 0;
         sx[local] = __longlong_as_double((long long)kPendingBits);
         sy[local] = __longlong_as_double((long long)kPendingBits);
         if (local < rows_here) {
             const int task = row0 + local;
             const int r = upper ? p.n - 1 - task : task;
-            const int near0 = (local & ~31) - 64;  // chunk-local start of the two blocks before
+            const int near0 = (local & ~63) - 64;  // chunk-local start of the block before
             int lo = 0, hi = 0, d = -1;
             if (!csr_row_range(p, r, lo, hi, d)) {
                 raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
@@ -399,7 +491,7 @@ csr_chain_kernel(const ChainParams q) {
             }
         }
         const int width = (__reduce_max_sync(kFullMask, cnt_[k]) + 1) & ~1;
-        if (lane == 0) s_width[warp + 8 * k] = width;
+        if (lane == 0) s_width[half_of(k)] = width;
     }
     if (tid == 0) sx[kChainRows] = 0.0;  // padding entries of the strips point here
     workers_barrier();
@@ -418,11 +510,11 @@ csr_chain_kernel(const ChainParams q) {
     if (!overflow) {
 #pragma unroll
         for (int k = 0; k < kChainRowsPerThread; ++k) {
-            const int local = tid + k * kChainWorkers;
-            const int blk = warp + 8 * k;
+            const int blk = half_of(k);
+            const int local = blk * 32 + lane;
             const int width = s_width[blk];
             if (width == 0) continue;
-            const int near0 = (local & ~31) - 64;
+            const int near0 = (local & ~63) - 64;
             int pos = s_bptr[blk] + lane;
             const int pos_end = pos + width * 32;
             if (local < rows_here && cnt_[k] > 0)
@@ -438,7 +530,7 @@ csr_chain_kernel(const ChainParams q) {
             for (; pos < pos_end; pos += 32) { ecol[pos] = kChainRows; eval[pos] = 0.0; }
         }
     }
-    // A2: contributions of rows before the chunk that are not covered by the W tiles (they
+    // A2: contributions of rows before the chunk that are not covered by the T tiles (they
     // belong to earlier tickets, so a bounded spin is safe).  First every operand that is
     // already there is consumed without waiting; operands still pending are remembered in a
     // bit mask and revisited afterwards, so that when the previous chunks finish only those
@@ -447,13 +539,13 @@ csr_chain_kernel(const ChainParams q) {
     unsigned long long pend_[kChainRowsPerThread];
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int local = tid + k * kChainWorkers;
+        const int local = half_of(k) * 32 + lane;
         acc_[k] = 0.0;
         pend_[k] = 0ull;
         if (local >= rows_here || failed) continue;
         const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
         // tasks before far_end are fetched here, the rest is covered by the strips and tiles
-        const int far_end = min(row0, row0 + (local & ~31) - 64);
+        const int far_end = min(row0, row0 + (local & ~63) - 64);
         double acc = __ldg(p.b + r);
         for (int j = lo_[k]; j < hi_[k] && !failed; ++j) {
             const int c = __ldg(p.Ai + j);
@@ -474,7 +566,7 @@ csr_chain_kernel(const ChainParams q) {
     // congest L2 for the few chunks whose turn it is: the chunk sleeps until its turn is near,
     // then sweeps over what is still pending, four loads in flight per thread.
     if (tid == 0) {
-        while (ld_relaxed_s32(&p.status[kStatusDone]) < chunk - kChainGate) {
+        while (ld_relaxed_s32(&p.status[kStatusDone]) < chunk - q.gate) {
             __nanosleep(1000);
             if (dl.tick(p.status, row0)) break;
         }
@@ -484,7 +576,7 @@ csr_chain_kernel(const ChainParams q) {
         // the chunk's tiles are pulled towards L2 now, shortly before its turn (all resident
         // chunks doing so at launch would only evict one another's tiles)
         const char *src = reinterpret_cast<const char *>(wsc);
-        const long long bytes = (long long)nblk * kBlockDoubles * 8;
+        const long long bytes = (long long)npair * kPairDoubles * 8;
         for (long long off = (long long)tid * 128; off < bytes; off += (long long)kChainThreads * 128)
             chain_prefetch_l2(src + off);
     }
@@ -521,46 +613,63 @@ csr_chain_kernel(const ChainParams q) {
         return any;
     };
     bool left_over = !failed && sweep();
-    // Blocks whose rows are complete now, several chunks before the chunk's turn, and that
-    // have no operand inside the chunk get their y_b right here, from the warp that holds
-    // their rows: the helper warps then have (almost) nothing to do while the main warp
-    // runs, and a busy helper costs the main warp about a third of its speed (they share
-    // the shuffle/load pipe).
+    // Every block gets y_B = M t_B right here, several chunks before the chunk's turn, from
+    // the warp that holds its rows: y_top = M11 t_top, y_bottom = M21 t_top + M22 t_bottom.
+    // Where operands are still missing (from the chunks just before, or from inside the
+    // chunk), the product is formed without them and parked (state 2): the product is linear,
+    // so the helper adds one column of M per late operand when it arrives.  The helper warps
+    // then have (almost) nothing to do while the main warps run.
+    int state_[2];
 #pragma unroll
-    for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int blk = warp + 8 * k;
-        const int local = tid + k * kChainWorkers;
-        const bool ready = !failed && pend_[k] == 0;
-        bool early = false;
-        if (blk < nblk && !overflow && s_width[blk] == 0 && __all_sync(kFullMask, ready)) {
+    for (int kk = 0; kk < 2; ++kk) {
+        const int pr = warp + 8 * kk;
+        const int base = pr * 64;
+        int state = 0;
+        if (pr < npair && !overflow && __all_sync(kFullMask, !failed)) {
             // (operands through shared memory, not shuffles: the lanes may still run as
             // separate groups after the sweep's per-lane loops)
-            sacc[local] = local < rows_here ? acc_[k] : 0.0;
+            sacc[base + lane] = base + lane < rows_here ? acc_[2 * kk] : 0.0;
+            sacc[base + 32 + lane] = base + 32 + lane < rows_here ? acc_[2 * kk + 1] : 0.0;
             __syncwarp();
-            const double *mrow = wsc + (long long)blk * kBlockDoubles + lane;
-            const double2 *tb = reinterpret_cast<const double2 *>(sacc + (local & ~31));
-            double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
+            const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+            const double *m21 = m11 + kTileDoubles, *m22 = m21 + kTileDoubles;
+            const double2 *tt = reinterpret_cast<const double2 *>(sacc + base);
+            const double2 *tb = tt + 16;
+            double y0 = 0.0, y1 = 0.0, z0 = 0.0, z1 = 0.0, z2 = 0.0, z3 = 0.0;
 #pragma unroll
-            for (int c = 0; c < 32; c += 4) {
-                const double2 ta = tb[c / 2], tc = tb[c / 2 + 1];
-                y0 = fma(__ldg(mrow + (c + 0) * 32), ta.x, y0);
-                y1 = fma(__ldg(mrow + (c + 1) * 32), ta.y, y1);
-                y2 = fma(__ldg(mrow + (c + 2) * 32), tc.x, y2);
-                y3 = fma(__ldg(mrow + (c + 3) * 32), tc.y, y3);
+            for (int c = 0; c < 32; c += 2) {
+                const double2 ta = tt[c / 2], tc = tb[c / 2];
+                y0 = fma(__ldg(m11 + (c + 0) * 32), ta.x, y0);
+                y1 = fma(__ldg(m11 + (c + 1) * 32), ta.y, y1);
+                z0 = fma(__ldg(m21 + (c + 0) * 32), ta.x, z0);
+                z1 = fma(__ldg(m21 + (c + 1) * 32), ta.y, z1);
+                z2 = fma(__ldg(m22 + (c + 0) * 32), tc.x, z2);
+                z3 = fma(__ldg(m22 + (c + 1) * 32), tc.y, z3);
             }
-            sy[local] = publishable((y0 + y1) + (y2 + y3));
-            early = true;
+            const double ytop = y0 + y1, ybot = (z0 + z1) + (z2 + z3);
+            // (the vote also makes sure that every lane has read its operands)
+            const bool late = __any_sync(kFullMask, (pend_[2 * kk] | pend_[2 * kk + 1]) != 0);
+            if (late || (s_width[2 * pr] | s_width[2 * pr + 1]) != 0) {
+                sacc[base + lane] = ytop;
+                sacc[base + 32 + lane] = ybot;
+                state = 2;
+            } else {
+                sy[base + lane] = publishable(ytop);
+                sy[base + 32 + lane] = publishable(ybot);
+                state = 1;
+            }
         }
-        if (lane == 0 && blk < kChainBlocks) s_early[blk] = early;
+        state_[kk] = state;
+        if (lane == 0 && pr < kChainPairs) s_early[pr] = state;
     }
     // What is still pending now (operands in the chunks just before this one) is left to the
-    // helper warp of the row's block: waiting for it here would hold back the main warp, whose
+    // helper warp of the row's block: waiting for it here would hold back the main warps, whose
     // first blocks rarely depend on it.
     (void)left_over;
 #pragma unroll
     for (int k = 0; k < kChainRowsPerThread; ++k) {
-        const int local = tid + k * kChainWorkers;
-        if (local < rows_here) sacc[local] = acc_[k];
+        const int local = half_of(k) * 32 + lane;
+        if (local < rows_here && state_[k >> 1] == 0) sacc[local] = acc_[k];
         spend[local] = local < rows_here ? pend_[k] : 0ull;
     }
     if (failed) *failed_flag = 1;
@@ -569,23 +678,23 @@ csr_chain_kernel(const ChainParams q) {
     volatile double *syv = sy;
 
     if (warp == kChainThreads / 32 - 1) {
-        // ---- loader warp (one lane): keeps the ring of W tiles full and announces, in order,
-        // the tiles that have landed (the consumers then read one counter instead of waiting
-        // on a barrier per tile, which costs them about 150 cycles per block)
+        // ---- loader warp (one lane): keeps the ring of T tiles full and announces, in order,
+        // the stages that have landed (the consumers then read one counter instead of waiting
+        // on a barrier per stage, which costs them about 150 cycles per block)
         if (lane != 0) return;
         int retired = 0;
         unsigned idle = 0;
         bool stop = false;
         const unsigned long long give_up = global_timer() + p.budget_ns;
-        while (retired < issued || (issued < nblk && !stop)) {
+        while (retired < issued || (issued < npair && !stop)) {
             bool progressed = false;
-            if (!stop && issued < nblk) {
+            if (!stop && issued < npair) {
                 const int s = issued % kChainStages;
                 if (issued < kChainStages ||
                     mbar_test_wait(&s_empty[s], ((issued / kChainStages) - 1) & 1)) {
-                    mbar_expect_tx(&s_full[s], kTileBytes);
-                    bulk_load(ring + s * 2 * kTileDoubles,
-                              wsc + (long long)issued * kBlockDoubles + kTileDoubles, kTileBytes, &s_full[s]);
+                    mbar_expect_tx(&s_full[s], kStageBytes);
+                    bulk_load(ring + s * kStageDoubles, wsc + (long long)issued * kPairDoubles + kPairT,
+                              kStageBytes, &s_full[s]);
                     ++issued;
                     progressed = true;
                 }
@@ -608,63 +717,80 @@ csr_chain_kernel(const ChainParams q) {
         return;
     }
 
-    const double2 *ring2 = reinterpret_cast<const double2 *>(ring);
-    if (warp == 0) {
-        // ---- main warp: x_b = y_b + z_b - W1_b x_b-1 --------------------------------------
-        // The loop always runs to the end and always performs its barrier operations (the
-        // partner warp blocks on them); after a failed wait it only publishes NaN.
+    if (warp < kChainMain) {
+        // ---- main warps: x_B = y_B - T_B x_B-1, four warps to a 64 x 64 block -------------
+        // Warp (half, side): rows half * 32 + lane of the block against columns side * 32 ..
+        // of the previous block.  The side-0 warp hands its partial sums to the side-1 warp of
+        // the same rows, which adds y, publishes x_B (shared memory, the next chunk's halo,
+        // global memory) and then all four meet before the next block.  The loops always run
+        // to the end and always perform their barrier operations; after a failed wait they
+        // only publish NaN.
         // Trace layout (64-bit words, C = number of chunks): [0, n) cycle counter at each row's
-        // publication; [2n, 2n + C) cycle counter at the main warp's start; 2n + C + 4 chunk + k:
+        // publication; [2n, 2n + C) cycle counter at the main warps' start; 2n + C + 4 chunk + k:
         // timer (ns) at main start, halo complete, first and last publication; 2n + 5C +
         // 8 chunk + k: cycles waited for tiles, number of such waits, cycles waited for y, number
-        // of such waits, cycles at the partner barrier.
+        // of such waits, cycles at the partial-sum barrier.
+        const int half = warp & 1, side = warp >> 1;
+        const double nanv = __longlong_as_double(kCanonicalNaN);
+        const double2 *w = reinterpret_cast<const double2 *>(ring) + (half * 2 + side) * (kTileDoubles / 2) + lane;
+        const double2 *xa = reinterpret_cast<const double2 *>(sxh + side * 32);
+        bool dead = *failed_flag != 0;
+        int tiles = 0;   // stages known to have landed
+        if (side == 0) {
+            step_sync();                                   // the halo is there
+            for (int B = 0; B < npair; ++B) {
+                const int s = B % kChainStages;
+                if (!dead && tiles <= B)
+                    dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > B; }, dl,
+                                      failed_flag, p.status, row0 + B * 64);
+                const double part = tile_matvec(w + s * (kStageDoubles / 2), xa, 0.0);
+                s_z[half][lane] = dead ? nanv : part;      // a failure travels as NaN
+                __syncwarp();
+                pair_arrive(kBarZ0 + half);
+                xa += 32;
+                step_sync();                               // x_B is there, the stage is free
+                if (half == 0) mbar_arrive_lane0(&s_empty[s], lane);
+            }
+            if (dead && lane == 0) *failed_flag = 1;
+            return;
+        }
+        const bool tracer = TRACE && half == 0 && lane == 0;
         const long long n_chunks = (p.n + kChainRows - 1) / kChainRows;
         long long *chunk_times = TRACE ? p.trace + 2ll * p.n + n_chunks + 4ll * chunk : nullptr;
-        if (TRACE && lane == 0) { p.trace[2ll * p.n + chunk] = clock64(); chunk_times[0] = (long long)global_timer(); }
-        const double nanv = __longlong_as_double(kCanonicalNaN);
-        bool dead = *failed_flag != 0;
-        // the two blocks before the chunk (the partner can start on z_0 as soon as the
-        // first of them is there)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int t = row0 - kChainHalo + h * 32 + lane;
+        if (tracer) { p.trace[2ll * p.n + chunk] = clock64(); chunk_times[0] = (long long)global_timer(); }
+        {
+            // this warp's half of the block before the chunk
+            const int t = row0 - kChainHalo + half * 32 + lane;
             double v = 0.0;
-            if (row0 > 0 && !dead) {   // (a chunk after the first has both blocks before it)
+            if (row0 > 0 && !dead) {   // (a chunk after the first has a whole block before it)
                 const int r = upper ? p.n - 1 - t : t;
-                if (crank > 0) {       // the previous chunk's block stores them into this halo
-                    volatile double *mine = sxh + h * 32 + lane;
+                if (crank > 0) {       // the previous chunk's block stores it into this halo
+                    volatile double *mine = sxh + half * 32 + lane;
                     dead = !warp_wait([&] { return !is_pending(v = *mine); }, dl, failed_flag, p.status, r);
                 } else {
                     dead = !warp_wait([&] { return !is_pending(v = ld_relaxed_f64(p.x + r)); }, dl,
                                       failed_flag, p.status, r);
                 }
             }
-            sxh[h * 32 + lane] = v;
-            __syncwarp();
-            pair_arrive(h ? kBarX1 : kBarX0);               // "x_-2 / x_-1 is there"
+            sxh[half * 32 + lane] = v;
         }
+        step_sync();
+        if (tracer) chunk_times[1] = (long long)global_timer();
         // Every instruction of this loop is on the critical path of the whole solve (a lone
-        // warp issues one about every four cycles), so it carries nothing it can do without:
-        // the partner releases the ring stages and reports its own failures through a NaN z,
-        // the barrier operations are unconditional (the partner runs two extra steps for them).
-        if (TRACE && lane == 0) chunk_times[1] = (long long)global_timer();
-        double ynext = syv[lane];
-        int tiles = 0;   // tiles known to have landed
-        const int step = upper ? -32 : 32;
-        double *xout = p.x + (upper ? p.n - 1 - (row0 + lane) : row0 + lane);
-        const double2 *xa = reinterpret_cast<const double2 *>(sxh + 32);
-        int local = lane;
-        // one step; PARITY is the block's parity, so that the barrier ids are immediates
-        const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then nblk is 32)
-        const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + lane * 8 : 0u;
-        long long tile_wait_ = 0, y_wait_ = 0, z_wait_ = 0; int tile_waits_ = 0, y_waits_ = 0;
-        auto step_block = [&](const int b, auto parity, auto pushing) {
-            constexpr int kParity = decltype(parity)::value;
+        // warp issues one about every four cycles), so it carries nothing it can do without.
+        int local = half * 32 + lane;
+        double ynext = dead ? nanv : syv[local];
+        const int step = upper ? -64 : 64;
+        double *xout = p.x + (upper ? p.n - 1 - (row0 + local) : row0 + local);
+        const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then npair is 16)
+        const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + (half * 32 + lane) * 8 : 0u;
+        long long tile_wait_ = 0, y_wait_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int tile_waits_ = 0, y_waits_ = 0;
+        auto step_block = [&](const int B, auto pushing) {
             constexpr bool kPush = decltype(pushing)::value;
-            const int s = b % kChainStages;
-            if (!dead && tiles <= b) {
+            const int s = B % kChainStages;
+            if (!dead && tiles <= B) {
                 long long c0_ = TRACE ? clock64() : 0;
-                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > b; }, dl,
+                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > B; }, dl,
                                   failed_flag, p.status, row0 + local);
                 if (TRACE) { tile_wait_ += clock64() - c0_; ++tile_waits_; }
                 if (dead) ynext = nanv;            // a failure travels as NaN from here on
@@ -674,119 +800,193 @@ csr_chain_kernel(const ChainParams q) {
                 long long c0_ = TRACE ? clock64() : 0;
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
                                   p.status, row0 + local);
-                if (TRACE) { y_wait_ += clock64() - c0_; ++y_waits_; }
+                if (TRACE) { y_wait_ += clock64() - c0_; y_waits_ |= 1 << B; }
                 if (dead) y = nanv;
             }
-            ynext = syv[local + 32];   // (one block of slack behind sy keeps this in bounds)
-            const double2 *w1 = ring2 + s * kTileDoubles + lane;
-            double a0 = y, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-#pragma unroll
-            for (int qd = 0; qd < 16; qd += 2) {
-                const double2 u0 = w1[qd * 32], u1 = w1[(qd + 1) * 32];
-                const double2 v0 = xa[qd], v1 = xa[qd + 1];
-                a0 = fma(-u0.x, v0.x, a0);
-                a1 = fma(-u0.y, v0.y, a1);
-                a2 = fma(-u1.x, v1.x, a2);
-                a3 = fma(-u1.y, v1.y, a3);
-            }
+            ynext = dead ? nanv : syv[local + 64];   // (one block of slack behind sy keeps this in bounds)
+            long long m0_ = 0, m1_ = 0;
+            if (TRACE) asm volatile("mov.u64 %0, %%clock64;" : "=l"(m0_) : "d"(y) : "memory");
+            const double sum = tile_matvec(w + s * (kStageDoubles / 2), xa, y);
+            if (TRACE) { asm volatile("mov.u64 %0, %%clock64;" : "=l"(m1_) : "d"(sum) : "memory"); mv_ += m1_ - m0_; }
             long long z0_ = TRACE ? clock64() : 0;
-            pair_sync(kParity ? kBarZ1 : kBarZ0);          // z_b = -W2_b x_b-2 from the partner
+            pair_sync(kBarZ0 + half);                      // the other 32 columns' partial sums
             if (TRACE) z_wait_ += clock64() - z0_;
-            const double z = s_z[kParity][lane];
             // (a sum is never the reserved all-ones pattern: arithmetic returns the canonical NaN)
-            const double val = ((a0 + a1) + (a2 + a3)) + z;
-            sxv[local] = val;       // (rows past the end: their W rows and y are zero, so is val)
-            if (kPush) st_cluster_f64(next_halo + kParity * 256, val);   // the next chunk's halo
+            const double val = sum + s_z[half][lane];
+            sxv[local] = val;       // (rows past the end: their T rows and y are zero, so is val)
+            if (kPush) st_cluster_f64(next_halo, val);     // the next chunk's halo
             if (local < rows_here) {
                 st_relaxed_f64(xout, val);
-                if (TRACE) { p.trace[row0 + local] = clock64(); if (lane == 0 && (b == 0 || b == nblk - 1)) chunk_times[b == 0 ? 2 : 3] = (long long)global_timer(); }
+                if (TRACE) { p.trace[row0 + local] = clock64(); if (tracer && (B == 0 || B == npair - 1)) chunk_times[B == 0 ? 2 : 3] = (long long)global_timer(); }
             }
-            __syncwarp();
-            pair_arrive(kParity ? kBarX1 : kBarX0);        // "x_b is there"
+            long long s0_ = TRACE ? clock64() : 0;
+            if (TRACE) pub_ += s0_ - z0_;
+            step_sync();                                   // "x_B is there"
+            if (TRACE) ss_ += clock64() - s0_;
             xout += step;
-            xa += 16;
-            local += 32;
+            xa += 32;
+            local += 64;
         };
-        if (dead) ynext = nanv;
-        const int plain = push ? nblk - 2 : nblk;   // the last two blocks also feed the neighbour
-        for (int b = 0; b < plain; b += 2) {
-            step_block(b, std::integral_constant<int, 0>(), std::false_type());
-            if (b + 1 < plain) step_block(b + 1, std::integral_constant<int, 1>(), std::false_type());
-        }
-        if (push) {
-            step_block(nblk - 2, std::integral_constant<int, 0>(), std::true_type());
-            step_block(nblk - 1, std::integral_constant<int, 1>(), std::true_type());
-        }
-        if (TRACE && lane == 0) {
+        const int plain = push ? npair - 1 : npair;   // the last block also feeds the neighbour
+        for (int B = 0; B < plain; ++B) step_block(B, std::false_type());
+        if (push) step_block(npair - 1, std::true_type());
+        if (tracer) {
             long long *o = p.trace + 2ll * p.n + 5 * n_chunks + 8ll * chunk;
-            o[0] = tile_wait_; o[1] = tile_waits_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_;
+            o[0] = tile_wait_; o[1] = tile_waits_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_; o[5] = mv_; o[6] = ss_; o[7] = pub_;
         }
         if (dead && lane == 0) *failed_flag = 1;
-        if (lane == 0) atomicAdd(&p.status[kStatusDone], 1);
-        return;
-    }
-    if (warp == 1) {
-        // ---- partner warp: z_k = -W2_k x_k-2, one step ahead of the main warp ------------
-        // It also releases the ring stages: once x_k-2 is published the main warp is done
-        // with tile k-2 (and this warp was done with it two steps ago).  Two extra steps at
-        // the end only take the main warp's last two barrier arrivals.
-        bool dead = false;
-        int tiles = 0;
-        const double nanv = __longlong_as_double(kCanonicalNaN);
-        for (int k = 0; k < nblk + 2; ++k) {
-            const int s = k % kChainStages;
-            if (k < nblk && !dead && tiles <= k)
-                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > k; }, dl,
-                                  failed_flag, p.status, row0 + k * 32);
-            pair_sync(k & 1 ? kBarX1 : kBarX0);            // x_k-2 is in shared memory
-            if (k >= 2) mbar_arrive_lane0(&s_empty[(k - 2) % kChainStages], lane);
-            if (k >= nblk) continue;
-            const double2 *xb = reinterpret_cast<const double2 *>(sx + k * 32 - 64);
-            const double2 *w2 = ring2 + s * kTileDoubles + kTileDoubles / 2 + lane;
-            double c0 = 0.0, c1 = 0.0, c2 = 0.0, c3 = 0.0;
-#pragma unroll
-            for (int qd = 0; qd < 16; qd += 2) {
-                const double2 u0 = w2[qd * 32], u1 = w2[(qd + 1) * 32];
-                const double2 v0 = xb[qd], v1 = xb[qd + 1];
-                c0 = fma(-u0.x, v0.x, c0);
-                c1 = fma(-u0.y, v0.y, c1);
-                c2 = fma(-u1.x, v1.x, c2);
-                c3 = fma(-u1.y, v1.y, c3);
-            }
-            s_z[k & 1][lane] = dead ? nanv : (c0 + c1) + (c2 + c3);   // a failure travels as NaN
-            if (dead && lane == 0) *failed_flag = 1;
-            __syncwarp();
-            pair_arrive(k & 1 ? kBarZ1 : kBarZ0);
-        }
+        if (half == 0 && lane == 0) atomicAdd(&p.status[kStatusDone], 1);
         return;
     }
 
-    // ---- helper warps 2..6: y_b for blocks b = warp - 2, warp - 2 + 5, ... -------------------
+    // ---- helper warps: y_B for the blocks B = warp - 4, warp - 4 + 3, ... that phase A left --
+    // Parked products (state 2): y_B was formed in phase A without a few operands.  A late
+    // operand delta_i of row i adds delta_i times column i of M.
+    auto finish_parked = [&](const int pr, const double d0, const double d1) {
+        const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+        double ytop = sacc[pr * 64 + lane], ybot = sacc[pr * 64 + 32 + lane];
+        unsigned top = __ballot_sync(kFullMask, d0 != 0.0), bot = __ballot_sync(kFullMask, d1 != 0.0);
+        if (__popc(top) + __popc(bot) > 12) {
+            apply_inverse(m11, d0, d1, ytop, ybot);   // many rows: the whole product
+        } else {
+            while (top) {
+                const int c = __ffs(top) - 1;
+                top &= top - 1;
+                const double dv = __shfl_sync(kFullMask, d0, c);
+                ytop = fma(__ldg(m11 + c * 32), dv, ytop);
+                ybot = fma(__ldg(m11 + kTileDoubles + c * 32), dv, ybot);
+            }
+            while (bot) {
+                const int c = __ffs(bot) - 1;
+                bot &= bot - 1;
+                ybot = fma(__ldg(m11 + 2 * kTileDoubles + c * 32), __shfl_sync(kFullMask, d1, c), ybot);
+            }
+        }
+        syv[pr * 64 + lane] = publishable(ytop);
+        syv[pr * 64 + 32 + lane] = publishable(ybot);
+        if (TRACE && lane == 0) p.trace[2ll * p.n + 13ll * ((p.n + kChainRows - 1) / kChainRows) + 16ll * chunk + pr] = clock64();
+    };
+    // the columns of M that row `lane` of half h will need, towards L1
+    auto prefetch_columns = [&](const int pr, const int h) {
+        const double *col = wsc + (long long)pr * kPairDoubles + (h ? 2 * kTileDoubles : 0) + lane * 32;
+        chain_prefetch_l1(col);
+        chain_prefetch_l1(col + 16);
+        if (!h) { chain_prefetch_l1(col + kTileDoubles); chain_prefetch_l1(col + kTileDoubles + 16); }
+    };
     {
-        int b = warp - 2;
-        if (b >= nblk) return;
-        const double *mbase = wsc + lane;
-        double m[32];
+        // Operands from the chunks just before: all of this warp's parked blocks are polled in
+        // turn, one load per row and pass, all loads of a pass in flight together, so that an
+        // operand is picked up about one round trip after the chunk before publishes it.
+        // Blocks without operands inside the chunk are finished as soon as they are complete;
+        // the others follow in order, each once its operands inside the chunk are there.
+        constexpr int kMine = (kChainPairs + kChainHelpers - 1) / kChainHelpers;
+        const int first = warp - kChainMain;
+        unsigned long long mask[kMine][2];
+        double delta[kMine][2];
+        int lo[kMine][2];
+        unsigned remaining = 0, listed = 0;
 #pragma unroll
-        for (int k = 0; k < 32; ++k)
-            m[k] = s_early[b] ? 0.0 : __ldg(mbase + (long long)b * kBlockDoubles + k * 32);
-        for (; b < nblk; b += kChainHelpers) {
-            const int base = b * 32, local = base + lane;
+        for (int i = 0; i < kMine; ++i) {
+            const int pr = first + i * kChainHelpers;
+            const bool parked = pr < npair && s_early[pr] == 2;
+            if (parked) remaining |= 1u << i;
+            if (parked && (s_width[2 * pr] | s_width[2 * pr + 1]) != 0) listed |= 1u << i;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mask[i][h] = 0ull;
+                delta[i][h] = 0.0;
+                lo[i][h] = 0;
+                if (!parked) continue;
+                const int local = pr * 64 + h * 32 + lane;
+                mask[i][h] = spend[local];
+                if (mask[i][h]) {
+                    const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
+                    int hi = 0, d = -1;
+                    csr_row_range(p, r, lo[i][h], hi, d);
+                    prefetch_columns(pr, h);
+                }
+            }
+        }
+        unsigned polls = 0;
+        while (remaining) {
+            int at[kMine][2];
+            double xv[kMine][2];
+#pragma unroll
+            for (int i = 0; i < kMine; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    at[i][h] = mask[i][h] ? lo[i][h] + __ffsll((long long)mask[i][h]) - 1 : -1;
+#pragma unroll
+            for (int i = 0; i < kMine; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    xv[i][h] = at[i][h] >= 0 ? ld_relaxed_f64(p.x + __ldg(p.Ai + at[i][h]))
+                                             : __longlong_as_double((long long)kPendingBits);
+#pragma unroll
+            for (int i = 0; i < kMine; ++i) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    if (!is_pending(xv[i][h])) {
+                        delta[i][h] = fma(-__ldg(p.Ax + at[i][h]), xv[i][h], delta[i][h]);
+                        mask[i][h] &= mask[i][h] - 1;
+                    }
+                if (!(remaining >> i & 1u)) continue;
+                if (!__all_sync(kFullMask, (mask[i][0] | mask[i][1]) == 0)) continue;
+                if (!(listed >> i & 1u)) finish_parked(first + i * kChainHelpers, delta[i][0], delta[i][1]);
+                remaining &= ~(1u << i);
+            }
+            if (remaining && (++polls & 15u) == 0 &&
+                __any_sync(kFullMask, *failed_flag != 0 || dl.tick(p.status, row0))) {
+                if (lane == 0) *failed_flag = 1;
+                return;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kMine; ++i) {
+            if (!(listed >> i & 1u)) continue;
+            const int pr = first + i * kChainHelpers;
+            bool bad = false;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int blk = 2 * pr + h;
+                const int width = s_width[blk];
+                int pos = s_bptr[blk] + lane;
+                if (width && ecol[pos] != kChainRows) prefetch_columns(pr, h);
+                double t0 = delta[i][h], t1 = 0.0;
+                for (int j = 0; j < width && !bad; j += 2, pos += 64) {
+                    const int c0 = ecol[pos], c1 = ecol[pos + 32];
+                    const double e0 = eval[pos], e1 = eval[pos + 32];
+                    double x0 = 0.0, x1 = 0.0;
+                    bad = !warp_wait([&] {
+                        x0 = sxv[c0];
+                        x1 = sxv[c1];
+                        return !is_pending(x0) && !is_pending(x1);
+                    }, dl, failed_flag, p.status, row0 + pr * 64);
+                    t0 = fma(-e0, x0, t0);
+                    t1 = fma(-e1, x1, t1);
+                }
+                delta[i][h] = t0 + t1;
+            }
+            if (bad) {
+                if (lane == 0) *failed_flag = 1;
+                return;
+            }
+            finish_parked(pr, delta[i][0], delta[i][1]);
+        }
+    }
+    // Then the blocks without a parked product (their operand list did not fit), in order.
+    for (int pr = warp - kChainMain; pr < npair; pr += kChainHelpers) {
+        if (s_early[pr]) continue;
+        bool bad = __any_sync(kFullMask, *failed_flag != 0);   // (kept warp-uniform throughout)
+        const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+        double t[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int blk = 2 * pr + h;
+            const int local = blk * 32 + lane;
             const bool active = local < rows_here;
             const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
-            // this warp's next inverse block is requested now and consumed one step later
-            double mnext[32];
-            const bool more = b + kChainHelpers < nblk && !s_early[b + kChainHelpers];
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-                mnext[k] = more ? __ldg(mbase + (long long)(b + kChainHelpers) * kBlockDoubles + k * 32) : 0.0;
-            if (s_early[b]) {
-#pragma unroll
-                for (int k = 0; k < 32; ++k) m[k] = mnext[k];
-                continue;
-            }
             double t0 = active ? sacc[local] : 0.0, t1 = 0.0;
-            bool bad = *failed_flag != 0;
             unsigned long long mask = spend[local];
             if (!bad && __any_sync(kFullMask, mask != 0)) {
                 // operands from before the chunk that had not been produced when phase A looked
@@ -807,8 +1007,8 @@ csr_chain_kernel(const ChainParams q) {
                 }, dl, failed_flag, p.status, r);
             }
             if (!overflow) {
-                const int width = s_width[b];
-                int pos = s_bptr[b] + lane;
+                const int width = s_width[blk];
+                int pos = s_bptr[blk] + lane;
                 for (int j = 0; j < width && !bad; j += 2, pos += 64) {
                     const int c0 = ecol[pos], c1 = ecol[pos + 32];
                     const double e0 = eval[pos], e1 = eval[pos + 32];
@@ -817,7 +1017,7 @@ csr_chain_kernel(const ChainParams q) {
                         x0 = sxv[c0];
                         x1 = sxv[c1];
                         return !is_pending(x0) && !is_pending(x1);
-                    }, dl, failed_flag, p.status, row0 + base);
+                    }, dl, failed_flag, p.status, row0 + pr * 64);
                     t0 = fma(-e0, x0, t0);
                     t1 = fma(-e1, x1, t1);
                 }
@@ -829,32 +1029,24 @@ csr_chain_kernel(const ChainParams q) {
                     const int c = __ldg(p.Ai + j);
                     if ((unsigned)c >= (unsigned)p.n) continue;
                     const int cl = (upper ? p.n - 1 - c : c) - row0;
-                    if (cl < 0 || cl >= base - 64) continue;
+                    if (cl < 0 || cl >= pr * 64 - 64) continue;
                     double xv = 0.0;
                     while (is_pending(xv = sxv[cl]))
                         if (*failed_flag || dl.tick(p.status, r)) { bad = true; break; }
                     t0 = fma(-__ldg(p.Ax + j), xv, t0);
                 }
             }
-            __syncwarp();
-            if (__any_sync(kFullMask, bad)) {
-                if (lane == 0) *failed_flag = 1;
-                return;
-            }
-            const double t = t0 + t1;
-            // y_block = inverse block * t_block: 32 independent shuffle / FMA pairs
-            double y0 = 0.0, y1 = 0.0, y2 = 0.0, y3 = 0.0;
-#pragma unroll
-            for (int k = 0; k < 32; k += 4) {
-                y0 = fma(m[k + 0], __shfl_sync(kFullMask, t, k + 0), y0);
-                y1 = fma(m[k + 1], __shfl_sync(kFullMask, t, k + 1), y1);
-                y2 = fma(m[k + 2], __shfl_sync(kFullMask, t, k + 2), y2);
-                y3 = fma(m[k + 3], __shfl_sync(kFullMask, t, k + 3), y3);
-            }
-            syv[local] = publishable((y0 + y1) + (y2 + y3));
-#pragma unroll
-            for (int k = 0; k < 32; ++k) m[k] = mnext[k];
+            bad = __any_sync(kFullMask, bad);
+            t[h] = t0 + t1;
         }
+        if (bad) {
+            if (lane == 0) *failed_flag = 1;
+            return;
+        }
+        double ytop = 0.0, ybot = 0.0;
+        apply_inverse(m11, t[0], t[1], ytop, ybot);
+        syv[pr * 64 + lane] = publishable(ytop);
+        syv[pr * 64 + 32 + lane] = publishable(ybot);
     }
     };
     body();
@@ -863,8 +1055,8 @@ csr_chain_kernel(const ChainParams q) {
 
 static size_t chain_smem_bytes(int *cap_out) {
     const size_t limit = 227 * 1024 - 2048;  // static shared memory takes about 1.2 KB
-    const size_t fixed = (size_t)kChainStages * 2 * kTileDoubles * 8 +
-                         ((size_t)kChainHalo + kChainRows + 2 + 3 * kChainRows + 32) * 8;
+    const size_t fixed = (size_t)kChainStages * kStageDoubles * 8 +
+                         ((size_t)kChainHalo + kChainRows + 2 + 3 * kChainRows + 64) * 8;
     const size_t cap = ((limit - fixed) / 12) & ~(size_t)1;
     *cap_out = (int)cap;
     return fixed + cap * 12;
@@ -890,7 +1082,7 @@ extern "C" int lcd_chain_cluster_size(void) { return g_last_cluster; }
 
 extern "C" int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes) {
     if (n < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
-    *bytes = ((int64_t)n + 31) / 32 * kBlockDoubles * 8 + 256;
+    *bytes = ((int64_t)n + 63) / 64 * kPairDoubles * 8 + 256;
     return LCD_OK;
 }
 
@@ -914,11 +1106,14 @@ extern "C" int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, cons
                                  void *workspace, int64_t workspace_bytes, void *stream) {
     int rc = chain_check(n, nnz, Ap, Ai, Ax, diag_pos, flags, workspace, workspace_bytes);
     if (rc || n == 0) return rc;
-    const int n_blocks = (n + 31) / 32;
+    const int n_pairs = (n + 63) / 64;
     CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, nullptr, nullptr, flags, 1, 1, nullptr,
                      0, nullptr, 0, n, nullptr, {nullptr}};
-    chain_prepare_kernel<<<n_blocks, 96, 0, (cudaStream_t)stream>>>(p, static_cast<double *>(workspace),
-                                                                    n_blocks);
+    // the attribute belongs to the current device's copy of the function
+    LCD_CUDA_TRY(cudaFuncSetAttribute(chain_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kPrepSmemBytes));
+    chain_prepare_kernel<<<n_pairs, kPrepThreads, kPrepSmemBytes, (cudaStream_t)stream>>>(
+        p, static_cast<double *>(workspace), n_pairs);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }
@@ -942,6 +1137,7 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
                              status_dev, timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
         q.ws = static_cast<const double *>(workspace);
         const size_t smem = chain_smem_bytes(&q.cap);
+        q.gate = getenv("LCD_CHAIN_GATE") ? atoi(getenv("LCD_CHAIN_GATE")) : kChainGate;
         // the attribute belongs to the current device's copy of the function
         auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
         LCD_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

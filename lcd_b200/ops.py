@@ -179,7 +179,7 @@ def gs_values(layout, Ax, diagonal=None, out=None):
 
 
 def chain_workspace(n, device):
-    """Scratch for the block-recurrence chain solver (24 KiB per 32 rows)."""
+    """Scratch for the block-recurrence chain solver (56 KiB per 64 rows)."""
     need = ctypes.c_int64(0)
     check(nat.load().lcd_chain_workspace_bytes(int(n), ctypes.byref(need)), "lcd_chain_workspace_bytes")
     return torch.empty((need.value + 7) // 8, dtype=torch.float64, device=device)
