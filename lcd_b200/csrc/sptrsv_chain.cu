@@ -47,26 +47,26 @@
 // lcd_sptrsv_csr_syncfree instead.
 #include "common.cuh"
 
-#include <cstdlib>
 #include <type_traits>
 
 namespace lcd {
 
 constexpr int kChainThreads = 256;                    // four main warps, three helpers, loader warp
 constexpr int kChainWorkers = 256;
-constexpr int kChainRows = 1024;                      // rows per chunk
+constexpr int kChainRows = 512;                       // rows per chunk
 constexpr int kChainRowsPerThread = kChainRows / kChainWorkers;
 constexpr int kChainBlocks = kChainRows / 32;         // 32-row halves (operand strips are per half)
 constexpr int kChainPairs = kChainRows / 64;          // 64-row blocks
+constexpr int kPairsPerWarp = kChainPairs / 8;        // phase A: blocks per warp
 constexpr int kChainMain = 4;                         // main warps
 constexpr int kChainHelpers = 3;
-constexpr int kChainStages = 4;                       // ring of T tiles (32 KB per stage)
+constexpr int kChainStages = 6;                       // ring of T tiles (32 KB per stage)
 constexpr int kTileDoubles = 1024;
 constexpr int kPairDoubles = 7 * kTileDoubles;        // per 64-row block: M11, M21, M22, T00, T01, T10, T11
 constexpr int kPairT = 3 * kTileDoubles;              // offset of the four T tiles
 constexpr int kStageDoubles = 4 * kTileDoubles;
 constexpr int kChainHalo = 64;                        // the block before the chunk
-constexpr int kChainGate = 3;                         // chunks ahead at which pending operands are polled
+constexpr int kChainGate = 4;                         // chunks ahead at which pending operands are polled
 constexpr int kChainCluster = 8;                      // blocks per cluster (portable maximum)
 constexpr int kStatusDone = 6;                        // status word: chunks finished
 constexpr unsigned kFullMask = 0xffffffffu;
@@ -84,7 +84,7 @@ constexpr unsigned kFullMask = 0xffffffffu;
 // Eliminating x_b from the bottom half's equation then takes three dense products:
 //        M21 = -V1 M11,   T11 = V2 - V1 W1,   T10 = V3 - V1 W2       (T00 = W2, T01 = W1).
 // Tiles sit in shared memory with column c of row r at r * 32 + (c ^ r): rows and columns are
-// both read without bank conflicts, and seven tiles fit four blocks to an SM.
+// both read without bank conflicts.
 constexpr int kPrepThreads = 224;
 constexpr int kPrepSmemBytes = 7 * kTileDoubles * 8;
 __device__ __forceinline__ int swz(int row, int col) { return row * 32 + (col ^ row); }
@@ -104,6 +104,8 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_pair
     const int mine = 4 - which;
     int lo = 0, hi = 0;
     double diag = 1.0;  // rows past the end, and rows with bad pointers, act as identity rows
+    // (the walk multiplies by the reciprocal: one division per row of the half, not one per
+    // row and tile)
     {
         const int task = base + lane;
         if (task < p.n) {
@@ -116,6 +118,7 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_pair
             }
         }
     }
+    diag = 1.0 / diag;
     // the first 32 entries of the next row are requested while the current row is processed
     int nlo = __shfl_sync(kFullMask, lo, 0), nhi = __shfl_sync(kFullMask, hi, 0);
     int pc = -1;
@@ -140,24 +143,24 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_pair
                 ca = 0.0;
                 if (j0 + lane < rhi) { cc = __ldg(p.Ai + j0 + lane); ca = __ldg(p.Ax + j0 + lane); }
             }
-            int kind = 0, col = 0;
+            int where = 0;   // (kind << 5) + column within the half the entry points to
             if ((unsigned)cc < (unsigned)p.n) {
                 const int tc = upper ? p.n - 1 - cc : cc;
                 const int off = tc - (base - 96);
-                if (off >= 0 && tc < base + r) { kind = 1 + (off >> 5); col = off & 31; }
+                if (off >= 0 && tc < base + r) where = off + 32;
             }
-            unsigned todo = __ballot_sync(kFullMask, kind == 4 || kind == mine);
+            unsigned todo = __ballot_sync(kFullMask, (where >> 5) == 4 || (where >> 5) == mine);
             while (todo) {
                 const int src = __ffs(todo) - 1;
                 todo &= todo - 1;
-                const int kd = __shfl_sync(kFullMask, kind, src);
-                const int c = __shfl_sync(kFullMask, col, src);
+                const int w = __shfl_sync(kFullMask, where, src);
                 const double av = __shfl_sync(kFullMask, ca, src);
-                if (kd == 4) acc = fma(-av, T[swz(c, lane)], acc);
+                const int c = w & 31;
+                if (w >= 128) acc = fma(-av, T[swz(c, lane)], acc);
                 else if (lane == c) acc += av;
             }
         }
-        T[swz(r, lane)] = acc / d;
+        T[swz(r, lane)] = acc * d;
         __syncwarp();
     }
     __syncthreads();
@@ -449,8 +452,8 @@ csr_chain_kernel(const ChainParams q) {
                       kStageBytes, &s_full[issued]);
         }
 
-    // ---- phase A: a warp owns the 64-row blocks warp and warp + 8, a thread one row of each
-    // of their four halves (row k of the thread: half k & 1 of block warp + 8 (k >> 1)) ------
+    // ---- phase A: warp w owns the 64-row blocks w, w + 8, ..., a thread one row of each of
+    // their halves (row k of the thread: half k & 1 of block w + 8 (k >> 1)) ----------------
     // A1 (pattern only, nothing to wait for): operands in the chunk that lie before the
     // previous 64-row block are counted, the per-half strips are laid out and filled.
     auto half_of = [&](int k) { return 2 * (warp + 8 * (k >> 1)) + (k & 1); };
@@ -496,13 +499,13 @@ csr_chain_kernel(const ChainParams q) {
     if (tid == 0) sx[kChainRows] = 0.0;  // padding entries of the strips point here
     workers_barrier();
     if (warp == 0) {
-        int incl = s_width[lane] * 32;
+        int incl = lane < kChainBlocks ? s_width[lane] * 32 : 0;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
             const int t = __shfl_up_sync(kFullMask, incl, off);
             if (lane >= off) incl += t;
         }
-        s_bptr[lane + 1] = incl;
+        if (lane < kChainBlocks) s_bptr[lane + 1] = incl;
         if (lane == 0) s_bptr[0] = 0;
     }
     workers_barrier();
@@ -619,9 +622,9 @@ csr_chain_kernel(const ChainParams q) {
     // chunk), the product is formed without them and parked (state 2): the product is linear,
     // so the helper adds one column of M per late operand when it arrives.  The helper warps
     // then have (almost) nothing to do while the main warps run.
-    int state_[2];
+    int state_[kPairsPerWarp];
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
+    for (int kk = 0; kk < kPairsPerWarp; ++kk) {
         const int pr = warp + 8 * kk;
         const int base = pr * 64;
         int state = 0;
@@ -735,19 +738,26 @@ csr_chain_kernel(const ChainParams q) {
         const double2 *w = reinterpret_cast<const double2 *>(ring) + (half * 2 + side) * (kTileDoubles / 2) + lane;
         const double2 *xa = reinterpret_cast<const double2 *>(sxh + side * 32);
         bool dead = *failed_flag != 0;
-        int tiles = 0;   // stages known to have landed
         if (side == 0) {
+            int tiles = 0;   // stages known to have landed
+            // These warps also make sure, while they wait for the other two to publish, that the
+            // next block's tiles have landed: the barrier hands that knowledge on, and the
+            // finishing warps (whose every instruction is on the critical path) never look.
+            auto await_stage = [&](const int B) {
+                if (!dead && tiles <= B && B < npair)
+                    dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > B; }, dl,
+                                      failed_flag, p.status, row0 + B * 64);
+            };
+            await_stage(0);
             step_sync();                                   // the halo is there
             for (int B = 0; B < npair; ++B) {
                 const int s = B % kChainStages;
-                if (!dead && tiles <= B)
-                    dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > B; }, dl,
-                                      failed_flag, p.status, row0 + B * 64);
                 const double part = tile_matvec(w + s * (kStageDoubles / 2), xa, 0.0);
                 s_z[half][lane] = dead ? nanv : part;      // a failure travels as NaN
                 __syncwarp();
                 pair_arrive(kBarZ0 + half);
                 xa += 32;
+                await_stage(B + 1);
                 step_sync();                               // x_B is there, the stage is free
                 if (half == 0) mbar_arrive_lane0(&s_empty[s], lane);
             }
@@ -780,6 +790,7 @@ csr_chain_kernel(const ChainParams q) {
         // warp issues one about every four cycles), so it carries nothing it can do without.
         int local = half * 32 + lane;
         double ynext = dead ? nanv : syv[local];
+        bool ylate = __any_sync(kFullMask, is_pending(ynext));
         const int step = upper ? -64 : 64;
         double *xout = p.x + (upper ? p.n - 1 - (row0 + local) : row0 + local);
         const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then npair is 16)
@@ -788,22 +799,15 @@ csr_chain_kernel(const ChainParams q) {
         auto step_block = [&](const int B, auto pushing) {
             constexpr bool kPush = decltype(pushing)::value;
             const int s = B % kChainStages;
-            if (!dead && tiles <= B) {
-                long long c0_ = TRACE ? clock64() : 0;
-                dead = !warp_wait([&] { return (tiles = ld_acquire_shared(&s_tiles)) > B; }, dl,
-                                  failed_flag, p.status, row0 + local);
-                if (TRACE) { tile_wait_ += clock64() - c0_; ++tile_waits_; }
-                if (dead) ynext = nanv;            // a failure travels as NaN from here on
-            }
             double y = ynext;
-            if (!dead && __any_sync(kFullMask, is_pending(y))) {
+            if (!dead && ylate) {
                 long long c0_ = TRACE ? clock64() : 0;
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
                                   p.status, row0 + local);
                 if (TRACE) { y_wait_ += clock64() - c0_; y_waits_ |= 1 << B; }
                 if (dead) y = nanv;
             }
-            ynext = dead ? nanv : syv[local + 64];   // (one block of slack behind sy keeps this in bounds)
+            ynext = syv[local + 64];   // (one block of slack behind sy keeps this in bounds)
             long long m0_ = 0, m1_ = 0;
             if (TRACE) asm volatile("mov.u64 %0, %%clock64;" : "=l"(m0_) : "d"(y) : "memory");
             const double sum = tile_matvec(w + s * (kStageDoubles / 2), xa, y);
@@ -815,6 +819,7 @@ csr_chain_kernel(const ChainParams q) {
             const double val = sum + s_z[half][lane];
             sxv[local] = val;       // (rows past the end: their T rows and y are zero, so is val)
             if (kPush) st_cluster_f64(next_halo, val);     // the next chunk's halo
+            ylate = __any_sync(kFullMask, is_pending(ynext));   // (decided here, where the warp waits anyway)
             if (local < rows_here) {
                 st_relaxed_f64(xout, val);
                 if (TRACE) { p.trace[row0 + local] = clock64(); if (tracer && (B == 0 || B == npair - 1)) chunk_times[B == 0 ? 2 : 3] = (long long)global_timer(); }
@@ -907,28 +912,38 @@ csr_chain_kernel(const ChainParams q) {
                 }
             }
         }
+        // (column and coefficient of the operand a row is waiting for stay in registers: a
+        // pass then costs one round trip to L2, not two)
+        int col[kMine][2];
+        double coef[kMine][2];
+        auto next_operand = [&](const int i, const int h) {
+            col[i][h] = -1;
+            coef[i][h] = 0.0;
+            if (mask[i][h]) {
+                const int at = lo[i][h] + __ffsll((long long)mask[i][h]) - 1;
+                col[i][h] = __ldg(p.Ai + at);
+                coef[i][h] = __ldg(p.Ax + at);
+            }
+        };
+#pragma unroll
+        for (int i = 0; i < kMine; ++i) { next_operand(i, 0); next_operand(i, 1); }
         unsigned polls = 0;
         while (remaining) {
-            int at[kMine][2];
             double xv[kMine][2];
 #pragma unroll
             for (int i = 0; i < kMine; ++i)
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
-                    at[i][h] = mask[i][h] ? lo[i][h] + __ffsll((long long)mask[i][h]) - 1 : -1;
-#pragma unroll
-            for (int i = 0; i < kMine; ++i)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    xv[i][h] = at[i][h] >= 0 ? ld_relaxed_f64(p.x + __ldg(p.Ai + at[i][h]))
-                                             : __longlong_as_double((long long)kPendingBits);
+                    xv[i][h] = col[i][h] >= 0 ? ld_relaxed_f64(p.x + col[i][h])
+                                              : __longlong_as_double((long long)kPendingBits);
 #pragma unroll
             for (int i = 0; i < kMine; ++i) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
                     if (!is_pending(xv[i][h])) {
-                        delta[i][h] = fma(-__ldg(p.Ax + at[i][h]), xv[i][h], delta[i][h]);
+                        delta[i][h] = fma(-coef[i][h], xv[i][h], delta[i][h]);
                         mask[i][h] &= mask[i][h] - 1;
+                        next_operand(i, h);
                     }
                 if (!(remaining >> i & 1u)) continue;
                 if (!__all_sync(kFullMask, (mask[i][0] | mask[i][1]) == 0)) continue;
@@ -1137,7 +1152,7 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
                              status_dev, timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
         q.ws = static_cast<const double *>(workspace);
         const size_t smem = chain_smem_bytes(&q.cap);
-        q.gate = getenv("LCD_CHAIN_GATE") ? atoi(getenv("LCD_CHAIN_GATE")) : kChainGate;
+        q.gate = kChainGate;
         // the attribute belongs to the current device's copy of the function
         auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
         LCD_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
