@@ -66,7 +66,8 @@ constexpr int kPairDoubles = 7 * kTileDoubles;        // per 64-row block: M11, 
 constexpr int kPairT = 3 * kTileDoubles;              // offset of the four T tiles
 constexpr int kStageDoubles = 4 * kTileDoubles;
 constexpr int kChainHalo = 64;                        // the block before the chunk
-constexpr int kChainGate = 4;                         // chunks ahead at which pending operands are polled
+constexpr int kChainGateFar = 16;                     // chunks ahead at which a chunk gathers its operands
+constexpr int kChainGate = 2;                         // chunks ahead at which pending operands are polled again
 constexpr int kChainCluster = 8;                      // blocks per cluster (portable maximum)
 constexpr int kStatusDone = 6;                        // status word: chunks finished
 constexpr unsigned kFullMask = 0xffffffffu;
@@ -349,7 +350,8 @@ struct ChainParams {
     CsrSolveParams m;
     const double *__restrict__ ws;
     int cap;  // capacity of the in-chunk operand list (entries)
-    int gate; // chunks ahead of its turn at which a chunk wakes up
+    int gate_far;  // chunks ahead of its turn at which a chunk gathers its operands
+    int gate;      // ... and at which it polls the ones that were missing once more
 };
 
 // y += M d for one 64-row block (M11, M21, M22 at m11, element (r, k) at k * 32 + r, m11
@@ -371,6 +373,52 @@ __device__ __noinline__ void apply_inverse(const double *m11, double d0, double 
     }
     ytop += y0 + y1;
     ybot += (z0 + z1) + (z2 + z3);
+}
+
+// y += M d where only a few rows of d are nonzero: one column of M per such row, the loads of
+// four columns in flight together (many rows: the whole product)
+__device__ __forceinline__ void add_columns(const double *m11, const double d0, const double d1,
+                                            double &ytop, double &ybot) {
+    unsigned top = __ballot_sync(kFullMask, d0 != 0.0), bot = __ballot_sync(kFullMask, d1 != 0.0);
+    if (__popc(top) + __popc(bot) > 12) {
+        apply_inverse(m11, d0, d1, ytop, ybot);
+        return;
+    }
+    while (top) {
+        int c[4];
+        double dv[4], a[4], b[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            c[u] = -1;
+            if (top) { c[u] = __ffs(top) - 1; top &= top - 1; }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            dv[u] = __shfl_sync(kFullMask, d0, c[u] & 31);
+            a[u] = c[u] >= 0 ? __ldg(m11 + c[u] * 32) : 0.0;
+            b[u] = c[u] >= 0 ? __ldg(m11 + kTileDoubles + c[u] * 32) : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (c[u] >= 0) { ytop = fma(a[u], dv[u], ytop); ybot = fma(b[u], dv[u], ybot); }
+    }
+    while (bot) {
+        int c[4];
+        double dv[4], b[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            c[u] = -1;
+            if (bot) { c[u] = __ffs(bot) - 1; bot &= bot - 1; }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            dv[u] = __shfl_sync(kFullMask, d1, c[u] & 31);
+            b[u] = c[u] >= 0 ? __ldg(m11 + 2 * kTileDoubles + c[u] * 32) : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (c[u] >= 0) ybot = fma(b[u], dv[u], ybot);
+    }
 }
 
 // one 32 x 32 tile times one half of the previous block: lane r's row (16-byte loads that
@@ -533,11 +581,22 @@ csr_chain_kernel(const ChainParams q) {
             for (; pos < pos_end; pos += 32) { ecol[pos] = kChainRows; eval[pos] = 0.0; }
         }
     }
+    // Hundreds of resident chunks spinning on operands that are many chunks away would only
+    // congest L2 for the few chunks whose turn it is, and would find most of them missing: the
+    // chunk sleeps until its turn is kChainGateFar chunks away.
+    auto sleep_until = [&](const int ahead) {
+        if (tid == 0) {
+            while (ld_relaxed_s32(&p.status[kStatusDone]) < chunk - ahead) {
+                __nanosleep(200);
+                if (dl.tick(p.status, row0)) break;
+            }
+        }
+        workers_barrier();
+    };
+    sleep_until(q.gate_far);
     // A2: contributions of rows before the chunk that are not covered by the T tiles (they
-    // belong to earlier tickets, so a bounded spin is safe).  First every operand that is
-    // already there is consumed without waiting; operands still pending are remembered in a
-    // bit mask and revisited afterwards, so that when the previous chunks finish only those
-    // few remain to be fetched.
+    // belong to earlier tickets, so a bounded spin is safe).  Every operand that is already
+    // there is consumed without waiting; operands still pending are remembered in a bit mask.
     double acc_[kChainRowsPerThread];
     unsigned long long pend_[kChainRowsPerThread];
 #pragma unroll
@@ -550,46 +609,94 @@ csr_chain_kernel(const ChainParams q) {
         // tasks before far_end are fetched here, the rest is covered by the strips and tiles
         const int far_end = min(row0, row0 + (local & ~63) - 64);
         double acc = __ldg(p.b + r);
-        for (int j = lo_[k]; j < hi_[k] && !failed; ++j) {
-            const int c = __ldg(p.Ai + j);
-            const int tc = upper ? p.n - 1 - c : c;
-            if (tc >= far_end) continue;
-            double xv = ld_relaxed_f64(p.x + c);
-            if (is_pending(xv)) {
-                if (j - lo_[k] < 64) { pend_[k] |= 1ull << (j - lo_[k]); continue; }
-                while (is_pending(xv = ld_relaxed_f64(p.x + c)))   // very long rows: wait here
-                    if (dl.tick(p.status, r)) { failed = true; break; }
-                if (failed) break;
+        // (four entries at a time: their loads are in flight together)
+        for (int j = lo_[k]; j < hi_[k] && !failed; j += 4) {
+            int c[4];
+            double a[4], xv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool in = j + u < hi_[k];
+                c[u] = in ? __ldg(p.Ai + j + u) : -1;
+                a[u] = in ? __ldg(p.Ax + j + u) : 0.0;
             }
-            acc = fma(-__ldg(p.Ax + j), xv, acc);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (c[u] >= 0 && (upper ? p.n - 1 - c[u] : c[u]) >= far_end) c[u] = -1;
+                xv[u] = c[u] >= 0 ? ld_relaxed_f64(p.x + c[u]) : 0.0;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (c[u] < 0 || failed) continue;
+                if (is_pending(xv[u])) {
+                    const int bit = j + u - lo_[k];
+                    if (bit < 64) { pend_[k] |= 1ull << bit; continue; }
+                    while (is_pending(xv[u] = ld_relaxed_f64(p.x + c[u])))   // very long rows: wait here
+                        if (dl.tick(p.status, r)) { failed = true; break; }
+                    if (failed) continue;
+                }
+                acc = fma(-a[u], xv[u], acc);
+            }
         }
         acc_[k] = acc;
     }
-    // Hundreds of resident chunks spinning on operands that are many chunks away would only
-    // congest L2 for the few chunks whose turn it is: the chunk sleeps until its turn is near,
-    // then sweeps over what is still pending, four loads in flight per thread.
-    if (tid == 0) {
-        while (ld_relaxed_s32(&p.status[kStatusDone]) < chunk - q.gate) {
-            __nanosleep(1000);
-            if (dl.tick(p.status, row0)) break;
-        }
-    }
-    workers_barrier();
     {
-        // the chunk's tiles are pulled towards L2 now, shortly before its turn (all resident
-        // chunks doing so at launch would only evict one another's tiles)
+        // the chunk's tiles are pulled towards L2 now, before its turn (all resident chunks
+        // doing so at launch would only evict one another's tiles)
         const char *src = reinterpret_cast<const char *>(wsc);
         const long long bytes = (long long)npair * kPairDoubles * 8;
         for (long long off = (long long)tid * 128; off < bytes; off += (long long)kChainThreads * 128)
             chain_prefetch_l2(src + off);
     }
+    // Every block gets y_B = M t_B right here, from the warp that holds its rows:
+    // y_top = M11 t_top, y_bottom = M21 t_top + M22 t_bottom, formed without the operands that
+    // are still missing.  The product is linear: a late operand delta_i of row i adds delta_i
+    // times column i of M, which costs one load per lane instead of 96.
+    double ytop_[kPairsPerWarp], ybot_[kPairsPerWarp];
+    bool formed_[kPairsPerWarp];
+#pragma unroll
+    for (int kk = 0; kk < kPairsPerWarp; ++kk) {
+        const int pr = warp + 8 * kk;
+        const int base = pr * 64;
+        ytop_[kk] = ybot_[kk] = 0.0;
+        formed_[kk] = pr < npair && !overflow && __all_sync(kFullMask, !failed);
+        if (!formed_[kk]) continue;
+        // (operands through shared memory, not shuffles: the lanes may run as separate groups
+        // after the per-lane loops above)
+        sacc[base + lane] = base + lane < rows_here ? acc_[2 * kk] : 0.0;
+        sacc[base + 32 + lane] = base + 32 + lane < rows_here ? acc_[2 * kk + 1] : 0.0;
+        __syncwarp();
+        const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+        const double *m21 = m11 + kTileDoubles, *m22 = m21 + kTileDoubles;
+        const double2 *tt = reinterpret_cast<const double2 *>(sacc + base);
+        const double2 *tb = tt + 16;
+        double y0 = 0.0, y1 = 0.0, z0 = 0.0, z1 = 0.0, z2 = 0.0, z3 = 0.0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+            const double2 ta = tt[c / 2], tc = tb[c / 2];
+            y0 = fma(__ldg(m11 + (c + 0) * 32), ta.x, y0);
+            y1 = fma(__ldg(m11 + (c + 1) * 32), ta.y, y1);
+            z0 = fma(__ldg(m21 + (c + 0) * 32), ta.x, z0);
+            z1 = fma(__ldg(m21 + (c + 1) * 32), ta.y, z1);
+            z2 = fma(__ldg(m22 + (c + 0) * 32), tc.x, z2);
+            z3 = fma(__ldg(m22 + (c + 1) * 32), tc.y, z3);
+        }
+        ytop_[kk] = y0 + y1;
+        ybot_[kk] = (z0 + z1) + (z2 + z3);
+    }
+    // Shortly before the chunk's turn: one sweep over what was pending (four loads in flight
+    // per thread), the columns of M for what has arrived since, and y_B is published - or
+    // parked (state 2) for the helper warps where operands are missing even now or lie inside
+    // the chunk.  The helper warps then have (almost) nothing to do while the main warps run.
+    sleep_until(q.gate);
+    double dlt_[kChainRowsPerThread];
     auto sweep = [&]() {   // one pass over what is still pending; true when something is left
         bool any = false;
 #pragma unroll
         for (int k = kChainRowsPerThread - 1; k >= 0; --k) {
+            dlt_[k] = 0.0;
             unsigned long long mask = pend_[k];
             if (!mask) continue;
-            double acc = acc_[k];
+            double acc = 0.0;
             unsigned long long left = mask;
             while (left) {
                 int jq[4];
@@ -599,66 +706,49 @@ csr_chain_kernel(const ChainParams q) {
                     jq[u] = -1;
                     if (left) { jq[u] = lo_[k] + __ffsll((long long)left) - 1; left &= left - 1; }
                 }
+                int cq[4];
+                double aq[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    cq[u] = jq[u] >= 0 ? __ldg(p.Ai + jq[u]) : 0;
+                    aq[u] = jq[u] >= 0 ? __ldg(p.Ax + jq[u]) : 0.0;
+                }
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    xq[u] = jq[u] >= 0 ? ld_relaxed_f64(p.x + __ldg(p.Ai + jq[u])) : 0.0;
+                    xq[u] = jq[u] >= 0 ? ld_relaxed_f64(p.x + cq[u]) : 0.0;
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     if (jq[u] >= 0 && !is_pending(xq[u])) {
-                        acc = fma(-__ldg(p.Ax + jq[u]), xq[u], acc);
+                        acc = fma(-aq[u], xq[u], acc);
                         mask &= ~(1ull << (jq[u] - lo_[k]));
                     }
             }
-            acc_[k] = acc;
+            dlt_[k] = acc;
+            acc_[k] += acc;   // (blocks without a parked product start from the plain sums)
             pend_[k] = mask;
             any |= mask != 0;
         }
         return any;
     };
     bool left_over = !failed && sweep();
-    // Every block gets y_B = M t_B right here, several chunks before the chunk's turn, from
-    // the warp that holds its rows: y_top = M11 t_top, y_bottom = M21 t_top + M22 t_bottom.
-    // Where operands are still missing (from the chunks just before, or from inside the
-    // chunk), the product is formed without them and parked (state 2): the product is linear,
-    // so the helper adds one column of M per late operand when it arrives.  The helper warps
-    // then have (almost) nothing to do while the main warps run.
+    if (failed) { for (int k = 0; k < kChainRowsPerThread; ++k) dlt_[k] = 0.0; }
     int state_[kPairsPerWarp];
 #pragma unroll
     for (int kk = 0; kk < kPairsPerWarp; ++kk) {
         const int pr = warp + 8 * kk;
         const int base = pr * 64;
         int state = 0;
-        if (pr < npair && !overflow && __all_sync(kFullMask, !failed)) {
-            // (operands through shared memory, not shuffles: the lanes may still run as
-            // separate groups after the sweep's per-lane loops)
-            sacc[base + lane] = base + lane < rows_here ? acc_[2 * kk] : 0.0;
-            sacc[base + 32 + lane] = base + 32 + lane < rows_here ? acc_[2 * kk + 1] : 0.0;
-            __syncwarp();
-            const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
-            const double *m21 = m11 + kTileDoubles, *m22 = m21 + kTileDoubles;
-            const double2 *tt = reinterpret_cast<const double2 *>(sacc + base);
-            const double2 *tb = tt + 16;
-            double y0 = 0.0, y1 = 0.0, z0 = 0.0, z1 = 0.0, z2 = 0.0, z3 = 0.0;
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-                const double2 ta = tt[c / 2], tc = tb[c / 2];
-                y0 = fma(__ldg(m11 + (c + 0) * 32), ta.x, y0);
-                y1 = fma(__ldg(m11 + (c + 1) * 32), ta.y, y1);
-                z0 = fma(__ldg(m21 + (c + 0) * 32), ta.x, z0);
-                z1 = fma(__ldg(m21 + (c + 1) * 32), ta.y, z1);
-                z2 = fma(__ldg(m22 + (c + 0) * 32), tc.x, z2);
-                z3 = fma(__ldg(m22 + (c + 1) * 32), tc.y, z3);
-            }
-            const double ytop = y0 + y1, ybot = (z0 + z1) + (z2 + z3);
-            // (the vote also makes sure that every lane has read its operands)
+        if (formed_[kk] && __all_sync(kFullMask, !failed)) {
+            add_columns(wsc + (long long)pr * kPairDoubles + lane, dlt_[2 * kk], dlt_[2 * kk + 1],
+                        ytop_[kk], ybot_[kk]);
             const bool late = __any_sync(kFullMask, (pend_[2 * kk] | pend_[2 * kk + 1]) != 0);
             if (late || (s_width[2 * pr] | s_width[2 * pr + 1]) != 0) {
-                sacc[base + lane] = ytop;
-                sacc[base + 32 + lane] = ybot;
+                sacc[base + lane] = ytop_[kk];
+                sacc[base + 32 + lane] = ybot_[kk];
                 state = 2;
             } else {
-                sy[base + lane] = publishable(ytop);
-                sy[base + 32 + lane] = publishable(ybot);
+                sy[base + lane] = publishable(ytop_[kk]);
+                sy[base + 32 + lane] = publishable(ybot_[kk]);
                 state = 1;
             }
         }
@@ -850,23 +940,7 @@ csr_chain_kernel(const ChainParams q) {
     auto finish_parked = [&](const int pr, const double d0, const double d1) {
         const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
         double ytop = sacc[pr * 64 + lane], ybot = sacc[pr * 64 + 32 + lane];
-        unsigned top = __ballot_sync(kFullMask, d0 != 0.0), bot = __ballot_sync(kFullMask, d1 != 0.0);
-        if (__popc(top) + __popc(bot) > 12) {
-            apply_inverse(m11, d0, d1, ytop, ybot);   // many rows: the whole product
-        } else {
-            while (top) {
-                const int c = __ffs(top) - 1;
-                top &= top - 1;
-                const double dv = __shfl_sync(kFullMask, d0, c);
-                ytop = fma(__ldg(m11 + c * 32), dv, ytop);
-                ybot = fma(__ldg(m11 + kTileDoubles + c * 32), dv, ybot);
-            }
-            while (bot) {
-                const int c = __ffs(bot) - 1;
-                bot &= bot - 1;
-                ybot = fma(__ldg(m11 + 2 * kTileDoubles + c * 32), __shfl_sync(kFullMask, d1, c), ybot);
-            }
-        }
+        add_columns(m11, d0, d1, ytop, ybot);
         syv[pr * 64 + lane] = publishable(ytop);
         syv[pr * 64 + 32 + lane] = publishable(ybot);
         if (TRACE && lane == 0) p.trace[2ll * p.n + 13ll * ((p.n + kChainRows - 1) / kChainRows) + 16ll * chunk + pr] = clock64();
@@ -1152,6 +1226,7 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
                              status_dev, timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
         q.ws = static_cast<const double *>(workspace);
         const size_t smem = chain_smem_bytes(&q.cap);
+        q.gate_far = kChainGateFar;
         q.gate = kChainGate;
         // the attribute belongs to the current device's copy of the function
         auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
