@@ -385,3 +385,25 @@ def test_generators_have_the_documented_shapes():
     assert s.sn[-1] == 3000 and (np.diff(s.Lip) >= np.diff(s.sn)).all() and s.Lp.dtype == np.int64
     L = s.to_csc()
     assert (L.indices >= np.repeat(np.arange(3000), np.diff(L.indptr))).all()
+
+
+def test_pinned_result_blocks_are_reused_only_when_released(monkeypatch):
+    """Result buffers of copy_to_host come from a small pool; a block goes out again only when
+    neither the returned array nor any view of it is alive."""
+    import torch
+    import lcd_b200.cuda_runtime as rt
+    plain_empty = torch.empty
+    monkeypatch.setattr(torch, "empty", lambda *a, **k: plain_empty(
+        *a, **{name: v for name, v in k.items() if name != "pin_memory"}))
+    monkeypatch.setattr(rt, "_PINNED_BLOCKS", {})
+    first = rt._pinned_block((16,), torch.float64).numpy()
+    second = rt._pinned_block((16,), torch.float64).numpy()
+    address = lambda array: array.__array_interface__["data"][0]
+    assert address(first) != address(second)
+    view = first[4:]
+    del first
+    third = rt._pinned_block((16,), torch.float64).numpy()      # the view keeps the first block busy
+    assert address(third) not in (address(view) - 32, address(second))
+    released = address(view) - 32
+    del view
+    assert address(rt._pinned_block((16,), torch.float64).numpy()) == released
