@@ -182,6 +182,26 @@ int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, const int32_
                          const double *Ax, const int32_t *diag_pos, const double *b, double *x,
                          int flags, const void *workspace, int64_t workspace_bytes,
                          int32_t *status_dev, int32_t timeout_ms, void *stream, int *status_host);
+/*
+ * The same two steps on a range [row_begin, row_end) of rows in solve order (for an upper
+ * solve, position k is row n - 1 - k).  lcd_chain_prepare_rows: row_begin a multiple of 64,
+ * row_end too unless it is n; reads only the matrix entries of those rows.
+ * lcd_sptrsv_csr_chain_rows: row_begin a multiple of 512, row_end too unless it is n; the
+ * ranges of one solve are issued in order on one stream with the same x and status_dev,
+ * the first starting at 0 (it resets the status block and marks all of x as not produced),
+ * the last ending at n (it reads the status back when status_host is given; the others
+ * return without waiting).  A range needs the tiles, the matrix entries and the
+ * right-hand side of its own rows only: a solve can run while later rows are still being
+ * uploaded and prepared on other streams.
+ */
+int lcd_chain_prepare_rows(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                           const double *Ax, const int32_t *diag_pos, int flags, void *workspace,
+                           int64_t workspace_bytes, int32_t row_begin, int32_t row_end, void *stream);
+int lcd_sptrsv_csr_chain_rows(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                              const double *Ax, const int32_t *diag_pos, const double *b, double *x,
+                              int flags, const void *workspace, int64_t workspace_bytes,
+                              int32_t row_begin, int32_t row_end, int32_t *status_dev,
+                              int32_t timeout_ms, void *stream, int *status_host);
 
 /*
  * Multi-RHS variant: B and X are row-major n x nrhs blocks (leading dimension

@@ -91,14 +91,14 @@ constexpr int kPrepSmemBytes = 7 * kTileDoubles * 8;
 __device__ __forceinline__ int swz(int row, int col) { return row * 32 + (col ^ row); }
 
 __global__ void __launch_bounds__(kPrepThreads)
-chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int n_pairs) {
+chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int pair_begin, int pair_end) {
     extern __shared__ __align__(16) double prep_tiles[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int odd = warp >= 3;                   // bottom half
     const int which = odd ? warp - 3 : warp;     // 0: inverse, k: coupling to the half k back
     double *T = prep_tiles + warp * kTileDoubles;
-    const int gp = blockIdx.x;
-    if (gp >= n_pairs) return;
+    const int gp = pair_begin + blockIdx.x;
+    if (gp >= pair_end) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     const int base = (gp * 2 + odd) * 32;
     // entry kinds: 1, 2, 3 = three, two, one half back, 4 = this half (before row r)
@@ -350,6 +350,8 @@ struct ChainParams {
     CsrSolveParams m;
     const double *__restrict__ ws;
     int cap;  // capacity of the in-chunk operand list (entries)
+    int chunk_begin;  // this launch solves the chunks [chunk_begin, ...) up to row_end (solve order)
+    int row_end;
     int gate_far;  // chunks ahead of its turn at which a chunk gathers its operands
     int gate;      // ... and at which it polls the ones that were missing once more
 };
@@ -466,7 +468,7 @@ csr_chain_kernel(const ChainParams q) {
     // whole, and a chunk still only waits for chunks with smaller numbers.)
     const unsigned crank = cluster_ctarank(), csize = cluster_nctarank();
     if (tid == 0) {
-        if (crank == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1) * (int)csize;
+        if (crank == 0) s_chunk = q.chunk_begin + atomicAdd(&p.status[kStatusTicket], 1) * (int)csize;
         s_failed = 0;
         s_tiles = 0;
     }
@@ -482,7 +484,7 @@ csr_chain_kernel(const ChainParams q) {
     // cluster barrier: no block may leave while a neighbour can still store into it)
     auto body = [&]() {
     const int row0 = chunk * kChainRows;
-    const int rows_here = min(kChainRows, p.n - row0);
+    const int rows_here = min(kChainRows, q.row_end - row0);
     if (rows_here <= 0) return;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     const int npair = (rows_here + 63) / 64;
@@ -883,7 +885,7 @@ csr_chain_kernel(const ChainParams q) {
         bool ylate = __any_sync(kFullMask, is_pending(ynext));
         const int step = upper ? -64 : 64;
         double *xout = p.x + (upper ? p.n - 1 - (row0 + local) : row0 + local);
-        const bool push = crank + 1 < csize && row0 + kChainRows < p.n;   // (then npair is 16)
+        const bool push = crank + 1 < csize && row0 + kChainRows < q.row_end;   // (then the chunk is full)
         const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + (half * 32 + lane) * 8 : 0u;
         long long tile_wait_ = 0, y_wait_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int tile_waits_ = 0, y_waits_ = 0;
         auto step_block = [&](const int B, auto pushing) {
@@ -1190,48 +1192,74 @@ static int chain_check(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t 
     return LCD_OK;
 }
 
-extern "C" int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
-                                 const double *Ax, const int32_t *diag_pos, int flags,
-                                 void *workspace, int64_t workspace_bytes, void *stream) {
+static bool chain_range_ok(int32_t n, int32_t row_begin, int32_t row_end, int granule) {
+    return row_begin >= 0 && row_begin <= row_end && row_end <= n && row_begin % granule == 0 &&
+           (row_end % granule == 0 || row_end == n);
+}
+
+extern "C" int lcd_chain_prepare_rows(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                      const double *Ax, const int32_t *diag_pos, int flags,
+                                      void *workspace, int64_t workspace_bytes, int32_t row_begin,
+                                      int32_t row_end, void *stream) {
     int rc = chain_check(n, nnz, Ap, Ai, Ax, diag_pos, flags, workspace, workspace_bytes);
-    if (rc || n == 0) return rc;
-    const int n_pairs = (n + 63) / 64;
+    if (rc) return rc;
+    if (!chain_range_ok(n, row_begin, row_end, 64)) return LCD_ERR_INVALID_ARGUMENT;
+    if (row_begin == row_end) return LCD_OK;
+    const int pair_begin = row_begin / 64, pair_end = (row_end + 63) / 64;
     CsrSolveParams p{n, nnz, Ap, Ai, Ax, diag_pos, nullptr, nullptr, flags, 1, 1, nullptr,
                      0, nullptr, 0, n, nullptr, {nullptr}};
     // the attribute belongs to the current device's copy of the function
     LCD_CUDA_TRY(cudaFuncSetAttribute(chain_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kPrepSmemBytes));
-    chain_prepare_kernel<<<n_pairs, kPrepThreads, kPrepSmemBytes, (cudaStream_t)stream>>>(
-        p, static_cast<double *>(workspace), n_pairs);
+    chain_prepare_kernel<<<pair_end - pair_begin, kPrepThreads, kPrepSmemBytes, (cudaStream_t)stream>>>(
+        p, static_cast<double *>(workspace), pair_begin, pair_end);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }
 
-extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
-                                    const double *Ax, const int32_t *diag_pos, const double *b,
-                                    double *x, int flags, const void *workspace,
-                                    int64_t workspace_bytes, int32_t *status_dev,
-                                    int32_t timeout_ms, void *stream, int *status_host) {
+extern "C" int lcd_chain_prepare(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                 const double *Ax, const int32_t *diag_pos, int flags,
+                                 void *workspace, int64_t workspace_bytes, void *stream) {
+    return lcd_chain_prepare_rows(n, nnz, Ap, Ai, Ax, diag_pos, flags, workspace, workspace_bytes, 0, n,
+                                  stream);
+}
+
+extern "C" int lcd_sptrsv_csr_chain_rows(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                         const double *Ax, const int32_t *diag_pos, const double *b,
+                                         double *x, int flags, const void *workspace,
+                                         int64_t workspace_bytes, int32_t row_begin, int32_t row_end,
+                                         int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                         int *status_host) {
     if (!status_dev) return LCD_ERR_INVALID_ARGUMENT;
     int rc = chain_check(n, nnz, Ap, Ai, Ax, diag_pos, flags, workspace, workspace_bytes);
     if (rc) return rc;
     if (n > 0 && (!b || !x || x == b)) return LCD_ERR_INVALID_ARGUMENT;
+    if (!chain_range_ok(n, row_begin, row_end, kChainRows)) return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;
-    rc = reset_status(status_dev, st);
-    if (rc) return rc;
-    if (n > 0) {
-        LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
+    if (row_begin == 0) {
+        // the first range of a solve: error state, ticket and chunk counters start from zero and
+        // the whole of x becomes "not produced yet"
+        rc = reset_status(status_dev, st);
+        if (rc) return rc;
+        if (n > 0) LCD_CUDA_TRY(cudaMemsetAsync(x, 0xFF, (size_t)n * sizeof(double), st));
+    } else {
+        // a later range: the tickets restart, the count of finished chunks and a raised error stay
+        LCD_CUDA_TRY(cudaMemsetAsync(status_dev + kStatusTicket, 0, sizeof(int32_t), st));
+    }
+    if (row_end > row_begin) {
         ChainParams q;
         q.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags & ~LCD_SOLVE_EXACT, 1, 1,
                              status_dev, timeout_ns(timeout_ms), debug_trace(), 0, n, nullptr, {nullptr}};
         q.ws = static_cast<const double *>(workspace);
-        const size_t smem = chain_smem_bytes(&q.cap);
+        q.chunk_begin = row_begin / kChainRows;
+        q.row_end = row_end;
         q.gate_far = kChainGateFar;
         q.gate = kChainGate;
+        const size_t smem = chain_smem_bytes(&q.cap);
         // the attribute belongs to the current device's copy of the function
         auto kernel = q.m.trace ? csr_chain_kernel<true> : csr_chain_kernel<false>;
         LCD_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        const int chunks = (n + kChainRows - 1) / kChainRows;
+        const int chunks = (row_end - row_begin + kChainRows - 1) / kChainRows;
         // clusters of up to eight blocks (consecutive chunks hand over through shared memory);
         // where the device cannot host such a cluster the same kernel runs as plain blocks
         int cluster = 1;
@@ -1268,5 +1296,15 @@ extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, c
         LCD_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, q));
         LCD_CUDA_TRY(cudaGetLastError());
     }
+    if (row_end < n) return LCD_OK;       // more ranges follow: nothing is awaited
     return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_sptrsv_csr_chain(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                    const double *Ax, const int32_t *diag_pos, const double *b,
+                                    double *x, int flags, const void *workspace,
+                                    int64_t workspace_bytes, int32_t *status_dev,
+                                    int32_t timeout_ms, void *stream, int *status_host) {
+    return lcd_sptrsv_csr_chain_rows(n, nnz, Ap, Ai, Ax, diag_pos, b, x, flags, workspace,
+                                     workspace_bytes, 0, n, status_dev, timeout_ms, stream, status_host);
 }

@@ -185,31 +185,47 @@ def chain_workspace(n, device):
     return torch.empty((need.value + 7) // 8, dtype=torch.float64, device=device)
 
 
-def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_pos=None):
-    """Build the block tiles (inverse diagonal blocks and their products with the two
-    couplings before) into ``workspace``; repeat when Ax changes."""
+CHAIN_PREPARE_ROWS = 64      # granularity of the row ranges of chain_prepare
+CHAIN_SOLVE_ROWS = 512       # ... and of sptrsv_csr_chain
+
+
+def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_pos=None, rows=None):
+    """Build the block tiles (inverse of each 64-row diagonal block and its product with the
+    coupling to the block before) into ``workspace``; repeat when Ax changes.  ``rows`` =
+    (begin, end) restricts the call to those rows in solve order (begin a multiple of 64, end
+    too unless it is n): only their entries of Ax are read."""
     flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
-    check(nat.load().lcd_chain_prepare(Ap.numel() - 1, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax),
-                                       ptr(diag_pos), flags, ptr(workspace),
-                                       workspace.numel() * 8, _stream()), "lcd_chain_prepare")
+    n = Ap.numel() - 1
+    begin, end = (0, n) if rows is None else rows
+    check(nat.load().lcd_chain_prepare_rows(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax),
+                                            ptr(diag_pos), flags, ptr(workspace),
+                                            workspace.numel() * 8, int(begin), int(end), _stream()),
+          "lcd_chain_prepare_rows")
     return workspace
 
 
 def sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, unit_diag=False,
-                     diag_pos=None, status=None, timeout_ms=0, sync=True):
+                     diag_pos=None, status=None, timeout_ms=0, sync=True, rows=None):
     """Block-recurrence chain solve (for matrices whose levels hold only a few rows).
-    ``workspace`` must have been filled by ``chain_prepare`` for the same matrix."""
+    ``workspace`` must have been filled by ``chain_prepare`` for the same matrix.
+
+    ``rows`` = (begin, end) solves only those rows in solve order (begin a multiple of 512,
+    end too unless it is n); the ranges of one solve are issued in order on one stream, with
+    the same ``x`` and ``status``, starting at 0 and ending at n.  A range needs the tiles and
+    the matrix entries of its own rows only, so a solve can start while later rows are still
+    being uploaded or prepared.  The status is read back (``sync``) by the range that ends at n."""
     _require(b, torch.float64, "b")
     n = Ap.numel() - 1
     x = torch.empty(n, dtype=torch.float64, device=b.device) if x is None else x
     status = new_status(b.device) if status is None else status
     flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    begin, end = (0, n) if rows is None else rows
     host = ctypes.c_int(0)
-    rc = nat.load().lcd_sptrsv_csr_chain(
+    rc = nat.load().lcd_sptrsv_csr_chain_rows(
         n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(b), ptr(x), flags,
-        ptr(workspace), workspace.numel() * 8, ptr(status), int(timeout_ms), _stream(),
-        ctypes.byref(host) if sync else None)
-    check(rc, "lcd_sptrsv_csr_chain")
+        ptr(workspace), workspace.numel() * 8, int(begin), int(end), ptr(status), int(timeout_ms),
+        _stream(), ctypes.byref(host) if sync else None)
+    check(rc, "lcd_sptrsv_csr_chain_rows")
     return x
 
 

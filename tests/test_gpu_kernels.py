@@ -227,6 +227,43 @@ def test_csr_chain_solver_cluster_sizes(cuda, oracle):
     assert used[0] == 1
 
 
+def test_csr_chain_solver_in_row_ranges(cuda, oracle):
+    """A solve issued as consecutive row ranges (tiles prepared range by range, from values
+    that are only valid for the rows prepared so far) equals the solve in one piece."""
+    import torch
+    from lcd_b200 import generators as gen, ops
+    from lcd_b200._native import ERR_INVALID_ARGUMENT, NativeError
+    for upper in (False, True):
+        tri = gen.random_band_lower(40_000, seed=13, mean_degree=15.0, band=64)
+        if upper:
+            tri = gen.upper_from_lower(tri)
+        Ap, Ai, Ax = tri.csr_arrays()
+        want = (oracle.sptrsv_csr_upper if upper else oracle.sptrsv_csr_lower)(Ap, Ai, Ax, tri.b)
+        dAp, dAi, dAx = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda)
+        db = dev(tri.b, np.float64, cuda)
+        n = tri.n
+        ws = ops.chain_workspace(n, cuda)
+        x = torch.zeros(n, dtype=torch.float64, device=cuda)
+        status = ops.new_status(cuda)
+        # values arrive range by range: entries of rows not yet "uploaded" are NaN
+        staged = torch.full_like(dAx, float("nan"))
+        cuts = [0, 8192, 8192 + 512, 30720, n]
+        for begin, end in zip(cuts, cuts[1:]):
+            rows = range(begin, end) if not upper else range(n - end, n - begin)
+            lo, hi = int(Ap[rows[0]]), int(Ap[rows[-1] + 1])
+            staged[lo:hi] = dAx[lo:hi]
+            ops.chain_prepare(dAp, dAi, staged, ws, upper=upper, rows=(begin, end))
+            ops.sptrsv_csr_chain(dAp, dAi, staged, db, ws, x, upper=upper, status=status,
+                                 rows=(begin, end), sync=end == n)
+        np.testing.assert_allclose(host(x), want, rtol=1e-10, atol=1e-12)
+    with pytest.raises(NativeError) as err:
+        ops.sptrsv_csr_chain(dAp, dAi, dAx, db, ws, x, upper=True, rows=(100, n))
+    assert err.value.code == ERR_INVALID_ARGUMENT
+    with pytest.raises(NativeError) as err:
+        ops.chain_prepare(dAp, dAi, dAx, ws, rows=(64, 100))
+    assert err.value.code == ERR_INVALID_ARGUMENT
+
+
 def test_csr_chain_solver_on_ilu_factors_and_errors(cuda, oracle):
     from lcd_b200 import generators as gen, ops
     from lcd_b200._native import ERR_INDEX_RANGE, ERR_WORKSPACE, NativeError
