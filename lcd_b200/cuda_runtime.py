@@ -67,12 +67,46 @@ def _pinned_block(shape, dtype):
         return torch.empty(shape, dtype=dtype, pin_memory=True)
 
 
+# Page-locked host arrays of at least twice this size are uploaded in pieces of this size on a
+# copy stream of their own, with an event after each piece: a launcher that consumes its input
+# front to back (the chain solver) starts on the first rows while the rest is still in flight.
+STREAMED_UPLOAD_BYTES = 64 << 20
+_COPY_STREAMS = {}
+
+
+def _copy_stream():
+    import torch
+    device = torch.cuda.current_device()
+    if device not in _COPY_STREAMS:
+        _COPY_STREAMS[device] = torch.cuda.Stream(device=device)
+    return _COPY_STREAMS[device]
+
+
 class DeviceArray:
     """A CUDA tensor with the two members the runtime contract relies on:
-    ``__cuda_array_interface__`` and ``copy_to_host()``."""
+    ``__cuda_array_interface__`` and ``copy_to_host()``.
 
-    def __init__(self, tensor):
-        self.tensor = tensor
+    ``arrival`` is None, or the list of (elements uploaded so far, event) of an upload that is
+    still in flight.  Reading ``tensor`` makes the current stream wait for the whole upload; a
+    launcher that wants to follow the pieces takes the list with ``take_arrival()`` and waits
+    for the events itself."""
+
+    def __init__(self, tensor, arrival=None):
+        self._tensor = tensor
+        self.arrival = arrival
+
+    @property
+    def tensor(self):
+        if self.arrival:
+            import torch
+            torch.cuda.current_stream().wait_event(self.arrival[-1][1])
+            self.arrival = None
+        return self._tensor
+
+    def take_arrival(self):
+        """(tensor, pieces) with the waiting left to the caller; pieces is None once awaited."""
+        pieces, self.arrival = self.arrival, None
+        return self._tensor, pieces
 
     @property
     def __cuda_array_interface__(self):
@@ -80,7 +114,7 @@ class DeviceArray:
 
     @property
     def shape(self):
-        return tuple(self.tensor.shape)
+        return tuple(self._tensor.shape)
 
     def copy_to_host(self):
         # through page-locked memory: a copy into a fresh pageable array runs at a few GB/s
@@ -92,7 +126,7 @@ class DeviceArray:
         return host.numpy()
 
     def __len__(self):
-        return self.tensor.shape[0]
+        return self._tensor.shape[0]
 
 
 class TorchCUDA:
@@ -103,7 +137,24 @@ class TorchCUDA:
     def to_device(array):
         import torch
         host = torch.from_numpy(np.ascontiguousarray(array))
-        return DeviceArray(host.to("cuda", non_blocking=host.is_pinned()))
+        pinned = host.is_pinned()
+        if not (pinned and host.dim() == 1 and
+                host.numel() * host.element_size() >= 2 * STREAMED_UPLOAD_BYTES):
+            return DeviceArray(host.to("cuda", non_blocking=pinned))
+        device = torch.empty(host.shape, dtype=host.dtype, device="cuda")
+        copies = _copy_stream()
+        copies.wait_stream(torch.cuda.current_stream())   # the block may just have been in use there
+        device.record_stream(copies)
+        step = STREAMED_UPLOAD_BYTES // host.element_size()
+        arrival = []
+        with torch.cuda.stream(copies):
+            for start in range(0, host.numel(), step):
+                end = min(host.numel(), start + step)
+                device[start:end].copy_(host[start:end], non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(copies)
+                arrival.append((end, event))
+        return DeviceArray(device, arrival)
 
     @staticmethod
     def synchronize():
@@ -204,7 +255,12 @@ def prepare_cuda_arguments(lowering, argument_values, execution_data, function_g
             "Values are missing for generated launcher arguments: " + ", ".join(missing))
     device_only = set(getattr(lowering, "device_only_variables", ()))
     prepared = {}
-    for name in lowering.launcher_arguments:
+    # small arrays first: an upload that is streamed in pieces must not sit in front of them on
+    # the copy engine (the launcher that follows the pieces needs the other arguments complete)
+    def upload_order(name):
+        value = host_values[name]
+        return value.nbytes if isinstance(value, np.ndarray) else 0
+    for name in sorted(lowering.launcher_arguments, key=upload_order):
         value = host_values[name]
         if name in HOST_LAUNCH_ARGUMENTS:
             prepared[name] = value  # the host launcher reads the offsets
@@ -275,7 +331,12 @@ def _evaluate_host_epilogue(lowering, result_values, function_globals):
         helper.type_params = []
     module = ast.fix_missing_locations(ast.Module(body=[helper], type_ignores=[]))
     exec(compile(module, filename="<cuda-host-epilogue>", mode="exec"), namespace, namespace)
-    return namespace["_lcd_host_epilogue"]()
+    try:
+        return namespace["_lcd_host_epilogue"]()
+    finally:
+        # the helper's globals are this namespace, which holds the helper: without this the
+        # result arrays (and their page-locked buffers) would live until the next collection
+        namespace.clear()
 
 
 def _returned_names(statements):

@@ -107,6 +107,34 @@ def bind(lowering):
             cache["chain_values"] = stamp
         ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
 
+    def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache):
+        # The value array is still being uploaded, piece by piece (pieces: elements uploaded
+        # so far and the event that says so).  The chain solver consumes the matrix front to
+        # back, so tiles are prepared and rows solved as far as the values have arrived: the
+        # solve overlaps the upload instead of following it.  (No look at the tile cache: its
+        # key needs the whole array, and the preparation hides under the upload anyway.)
+        n = Ap.numel() - 1
+        workspace = cache.get("chain_workspace")
+        if workspace is None or workspace.device != Ax.device:
+            workspace = cache["chain_workspace"] = ops.chain_workspace(n, Ax.device)
+        cache.pop("chain_values", None)
+        ends = torch.tensor([end for end, _ in pieces], dtype=Ap.dtype, device=Ap.device)
+        # rows [0, r) are complete once Ap[r] entries are there
+        complete = (torch.searchsorted(Ap, ends, right=True) - 1).clamp(0, n)
+        complete = (complete // ops.CHAIN_SOLVE_ROWS * ops.CHAIN_SOLVE_ROWS).tolist()
+        complete[-1] = n
+        status = ops.new_status(Ax.device)
+        stream = torch.cuda.current_stream()
+        begin = 0
+        for (_, event), end in zip(pieces, complete):
+            stream.wait_event(event)
+            if end <= begin and end != n:
+                continue
+            ops.chain_prepare(Ap, Ai, Ax, workspace, rows=(begin, end))
+            ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, status=status, rows=(begin, end),
+                                 sync=end == n)
+            begin = end
+
     def csr_solve(Ap, Ai, Ax, b, x, v, hints):
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
         if lowering.execution_mode == "sync_free":
@@ -123,10 +151,20 @@ def bind(lowering):
 
     def sptrsv_csr(*args, _hints=None):
         v = split(args)
+        hints = _hints or {}
+        values = v[roles["val"]]
+        if (lowering.execution_mode == "sync_free" and not lowering.upper and
+                getattr(values, "arrival", None) and values._tensor.dtype == torch.float64 and
+                chain_solver_preferred(hints.get("rows", 0), hints.get("levels", 0), hints.get("arch"))):
+            Ax, pieces = values.take_arrival()
+            chain_solve_streamed(as_tensor(v[roles["ptr"]], torch.int32), as_tensor(v[roles["idx"]], torch.int32),
+                                 Ax, pieces, as_tensor(v[roles["rhs"]], torch.float64),
+                                 as_tensor(v[roles["out"]], torch.float64), hints.setdefault("cache", {}))
+            return
         Ap, Ai, Ax = matrix(v)
         b = as_tensor(v[roles["rhs"]], torch.float64)
         x = as_tensor(v[roles["out"]], torch.float64)
-        csr_solve(Ap, Ai, Ax, b, x, v, _hints or {})
+        csr_solve(Ap, Ai, Ax, b, x, v, hints)
 
     def host_trip_count(v):
         """Product of the trip counts of the host loops around the block loop."""

@@ -251,6 +251,39 @@ def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch
     assert calls["solve"] == 3
 
 
+def test_decorated_chain_solve_follows_a_streamed_upload(cuda, oracle, monkeypatch):
+    """Page-locked value arrays above the streaming threshold are uploaded in pieces; the chain
+    solver's launcher prepares and solves the rows of each piece as it arrives.  Other launchers
+    (and smaller arrays) see the whole array as before."""
+    import torch
+    import ops_decorated as od
+    import lcd_b200.cuda_runtime as rt
+    from lcd_b200 import generators as gen, ops
+    monkeypatch.setattr(rt, "STREAMED_UPLOAD_BYTES", 1 << 20)
+    tri = gen.random_band_lower(65_536, seed=5)
+    Ap, Ai, Ax = tri.csr_arrays()
+    pinned = torch.from_numpy(Ax).pin_memory().numpy()         # 8 MB: eight pieces
+    ranges = []
+    real_solve = ops.sptrsv_csr_chain
+    monkeypatch.setattr(ops, "sptrsv_csr_chain",
+                        lambda *a, **k: (ranges.append(k.get("rows")), real_solve(*a, **k))[1])
+    want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+    x = od.csr_warp_syncfree(Ap, Ai, pinned, tri.b, tri.n)
+    np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    assert len(ranges) >= 4 and ranges[0][0] == 0 and ranges[-1][1] == tri.n
+    assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    ranges.clear()
+    x = od.csr_warp_syncfree(Ap, Ai, Ax, tri.b, tri.n)          # pageable values: one piece
+    np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    assert ranges == [None]
+    # a launcher that does not follow the pieces waits for the whole array
+    grid = gen.laplacian2d_tril(300, seed=1)
+    gp, gi, gx = grid.csr_arrays()
+    monkeypatch.setattr(rt, "STREAMED_UPLOAD_BYTES", 1 << 18)
+    x = od.csr_warp_syncfree(gp, gi, torch.from_numpy(gx).pin_memory().numpy(), grid.b, grid.n)
+    np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(gp, gi, gx, grid.b), rtol=1e-10, atol=1e-12)
+
+
 @pytest.mark.parametrize("mode", ["wavefront", "sync_free"])
 @pytest.mark.parametrize("name", golden_names("ilu0_"))
 def test_decorated_ilu0_is_bit_identical(cuda, name, mode):
