@@ -442,4 +442,21 @@ def _prepare_value(value, cuda_module):
 
 
 def _is_cuda_array(value):
-    return hasattr(value, "__cuda_array_interface__")
+    # (a DeviceArray first: asking it for the interface would wait for an upload in flight)
+    return isinstance(value, DeviceArray) or hasattr(value, "__cuda_array_interface__")
+
+
+def start_large_uploads(values, skip=()):
+    """Begin the upload of the page-locked arrays among ``values`` (a dict, changed in place) if
+    one of them is large enough to be streamed in pieces, so that the transfer overlaps the host
+    work that follows.  Smaller arrays go first: the launcher that follows the pieces needs
+    them complete.  Everything else stays as it is."""
+    import torch
+    pinned = [(value.nbytes, name) for name, value in values.items()
+              if name not in skip and isinstance(value, np.ndarray) and value.ndim == 1
+              and value.flags.c_contiguous and value.nbytes >= (1 << 20)
+              and torch.from_numpy(value).is_pinned()]
+    if not pinned or max(pinned)[0] < 2 * STREAMED_UPLOAD_BYTES:
+        return
+    for _, name in sorted(pinned):
+        values[name] = TorchCUDA.to_device(values[name])

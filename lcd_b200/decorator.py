@@ -36,6 +36,7 @@ import numpy as np
 from .cuda_lowering import (COUNTER_DEPENDENCE, PUSH_DEPENDENCE, CUDALoweringError,
                             direct_protocol_of, lower_to_native, recognise_operator)
 from .cuda_runtime import (DeviceArray, TorchCUDA, compile_cuda_module, evaluate_host_prelude,
+                           start_large_uploads,
                            execute_cuda_call, prepare_cuda_arguments)
 from .dag_preprocessing import (attach_auxiliary_values, preprocess_sync_free,
                                 preprocess_warp_tasks, preprocess_wavefront)
@@ -249,11 +250,14 @@ def parallel(**kwargs):
             argument_values = bind_arguments(args, call_kwargs)
             values = dag_values_for(argument_values)
             structure = device_structure(values)
+            # large page-locked arguments start their way to the device now, behind the
+            # structure arrays: the plan lookup below waits for those on the host
+            launch_values = dict(values)          # arguments plus the evaluated host prelude
+            start_large_uploads(launch_values, skip=structure)
             plan = plan_for(values, structure)
             lowering, module = compile_variant(plan.schedule.lowering_key)
             publish_variant(plan.schedule, lowering, module)
             # hand the already uploaded structure arrays to the launcher
-            launch_values = dict(values)          # arguments plus the evaluated host prelude
             for name, tensor in structure.items():
                 if name in launch_values:
                     launch_values[name] = DeviceArray(tensor)
