@@ -399,9 +399,9 @@ enum {
 };
 int lcd_set_tuning(int key, int value);
 /* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,
- * the one-lane-per-row solver (n words) and the chain solver (2 n + 13 C words, C the number
- * of 1024-row chunks: row stamps, per-chunk start times and wait counters) record SM cycle
- * counters and timer values.  Pass NULL to switch it off again. */
+ * the one-lane-per-row solver (n words) and the chain solver (2 n + 29 C words, C the number
+ * of 512-row chunks: row stamps, per-chunk start times, wait counters and the helpers'
+ * publication stamps) record SM cycle counters and timer values.  Pass NULL to switch it off again. */
 int lcd_debug_set_trace(long long *trace_dev);
 
 /* ---- small device utilities used by the host layer ---------------------------- */

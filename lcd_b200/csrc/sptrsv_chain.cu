@@ -3,40 +3,41 @@
 // Such a matrix is one long dependence chain: level-by-level substitution pays one
 // hand-off (a poll, a barrier, or a dozen dependent instructions of a lone warp) per
 // level, and there are hundreds of thousands of levels.  The chain is shortened
-// algebraically instead.  Rows are grouped into blocks of 32 consecutive rows; with
-// D_b the 32 x 32 diagonal block and L_bc the coupling of block b to block c, the solve
-//        D_b x_b = r_b - L_b,b-1 x_b-1 - L_b,b-2 x_b-2 - sum_{c <= b-3} L_bc x_c
-// is rewritten, once per matrix (lcd_chain_prepare, one warp per block, fully parallel),
-// as
-//        x_b = y_b - W1_b x_b-1 - W2_b x_b-2,     W1_b = D_b^-1 L_b,b-1,  W2_b = D_b^-1 L_b,b-2
-//        y_b = D_b^-1 ( r_b - sum_{c <= b-3} L_bc x_c )
-// so that the part of the chain that cannot be overlapped, x_b-1 -> x_b, is one dense
-// 32 x 32 mat-vec (no dependent chain inside it), and everything that reaches at least
-// three blocks back is taken off that path.
+// algebraically instead.  Rows are grouped into blocks of 64 consecutive rows; with
+// D_B the 64 x 64 diagonal block and L_BC the coupling of block B to block C, the solve
+//        D_B x_B = r_B - L_B,B-1 x_B-1 - sum_{C <= B-2} L_BC x_C
+// is rewritten, once per value set (lcd_chain_prepare, fully parallel), as
+//        x_B = y_B - T_B x_B-1,     T_B = D_B^-1 L_B,B-1,     y_B = M_B ( r_B - sum_{C <= B-2} L_BC x_C ),
+//        M_B = D_B^-1
+// so that the part of the chain that cannot be overlapped, x_B-1 -> x_B, is one dense
+// 64 x 64 mat-vec shared by four warps (no dependent chain inside it), and everything that
+// reaches at least two blocks back is taken off that path.  T_B and M_B are kept as 32 x 32
+// tiles (T00 T01 / T10 T11 and M11, M21, M22; M12 is zero).
 //
-// The solve kernel works on chunks of 1024 rows.  It runs as thread-block clusters of eight
+// The solve kernel works on chunks of 512 rows.  It runs as thread-block clusters of eight
 // where the device hosts them: a cluster takes one ticket and its blocks take eight
 // consecutive chunks (a chunk only waits for chunks with smaller numbers, which are running
 // or done, so the waits terminate), and the hand-over between consecutive chunks of a
 // cluster goes through distributed shared memory instead of L2.
-//   phase A (256 threads, four rows each): operands from before the chunk are fetched by
-//     polling x in global memory (a solution vector pre-filled with a reserved NaN is its
-//     own ready flag) - once at launch, once more when the chunk's turn is near; what is
-//     missing even then is left to the helper of the row's block; operands that lie in the
-//     chunk, three or more blocks back, go into a shared-memory list (one column-major
-//     strip per block, so a warp reads it without bank conflicts and with one trip count);
-//     blocks whose rows are complete by then and that have no listed operand get their y_b
-//     right there;
-//   helpers (5 warps, blocks b mod 5): y_b of the remaining blocks - fetch the late operands,
-//     subtract the listed ones, polling the chunk's x in shared memory, then apply D_b^-1
-//     held in registers;
-//   main warp and partner warp: the partner computes z_b = -W2_b x_b-2 one step ahead, the
-//     main warp x_b = y_b + z_b - W1_b x_b-1; they hand over through named barriers; the W
-//     tiles are streamed into a shared-memory ring by bulk asynchronous copies (one lane
-//     of the last warp keeps the ring full) and the previous blocks are read from shared
-//     memory as broadcasts.  (Splitting the main warp's 32 columns over four warps was
-//     measured slower: the per-block bookkeeping, not the multiply-adds, is what a lone
-//     warp spends its issue slots on.);
+//   tiles: one SM streams only about 32 bytes per clock from L2, less than the four main warps
+//     consume, so six of a chunk's eight T tiles (32 KB each) are requested at launch, long
+//     before the chunk's turn, into a shared-memory ring by bulk asynchronous copies; the last
+//     two follow into freed stages (one lane of the last warp keeps the ring full);
+//   phase A (256 threads, two rows each, a warp per 64-row block): at launch the operands that
+//     lie in the chunk, two or more blocks back, go into a shared-memory list (one column-major
+//     strip per 32 rows, so a warp reads it without bank conflicts and with one trip count);
+//     16 chunks before the turn the operands from before the chunk are fetched by polling x in
+//     global memory without waiting (a solution vector pre-filled with a reserved NaN is its
+//     own ready flag) and y_B = M_B t_B is formed from what is there; 2 chunks before the turn
+//     the missing ones are polled once more and each that has arrived adds its value times one
+//     column of M_B; complete blocks are published, the others parked;
+//   helpers (3 warps, blocks B mod 3): parked blocks - the late operands (all of a warp's
+//     blocks polled in turn), the listed ones (polling the chunk's x in shared memory), one
+//     column of M_B for each;
+//   main warps (4): warp (half, side) multiplies tile T[half][side] with half `side` of x_B-1
+//     (read from shared memory as broadcasts); the side-0 warps hand their partial sums over
+//     through a named barrier, the side-1 warps add y_B and publish x_B; all four meet at a
+//     128-thread barrier per block;
 //   every wait is bounded; a failed wait raises an error and poisons the rest of the chunk
 //     with NaN so that later chunks do not wait for it.
 //
@@ -823,8 +824,10 @@ csr_chain_kernel(const ChainParams q) {
         // Trace layout (64-bit words, C = number of chunks): [0, n) cycle counter at each row's
         // publication; [2n, 2n + C) cycle counter at the main warps' start; 2n + C + 4 chunk + k:
         // timer (ns) at main start, halo complete, first and last publication; 2n + 5C +
-        // 8 chunk + k: cycles waited for tiles, number of such waits, cycles waited for y, number
-        // of such waits, cycles at the partial-sum barrier.
+        // 8 chunk + k: two unused words, cycles waited for y, bit mask of the blocks that waited,
+        // cycles at the partial-sum barrier, in the mat-vec, at the step barrier, from the
+        // partial-sum barrier to the publication; 2n + 13C + 16 chunk + B: cycle counter when a
+        // helper published y_B.
         const int half = warp & 1, side = warp >> 1;
         const double nanv = __longlong_as_double(kCanonicalNaN);
         const double2 *w = reinterpret_cast<const double2 *>(ring) + (half * 2 + side) * (kTileDoubles / 2) + lane;
@@ -887,7 +890,7 @@ csr_chain_kernel(const ChainParams q) {
         double *xout = p.x + (upper ? p.n - 1 - (row0 + local) : row0 + local);
         const bool push = crank + 1 < csize && row0 + kChainRows < q.row_end;   // (then the chunk is full)
         const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + (half * 32 + lane) * 8 : 0u;
-        long long tile_wait_ = 0, y_wait_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int tile_waits_ = 0, y_waits_ = 0;
+        long long y_wait_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int y_waits_ = 0;
         auto step_block = [&](const int B, auto pushing) {
             constexpr bool kPush = decltype(pushing)::value;
             const int s = B % kChainStages;
@@ -929,7 +932,7 @@ csr_chain_kernel(const ChainParams q) {
         if (push) step_block(npair - 1, std::true_type());
         if (tracer) {
             long long *o = p.trace + 2ll * p.n + 5 * n_chunks + 8ll * chunk;
-            o[0] = tile_wait_; o[1] = tile_waits_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_; o[5] = mv_; o[6] = ss_; o[7] = pub_;
+            o[0] = 0; o[1] = 0; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_; o[5] = mv_; o[6] = ss_; o[7] = pub_;
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (half == 0 && lane == 0) atomicAdd(&p.status[kStatusDone], 1);
