@@ -824,7 +824,7 @@ csr_chain_kernel(const ChainParams q) {
         // Trace layout (64-bit words, C = number of chunks): [0, n) cycle counter at each row's
         // publication; [2n, 2n + C) cycle counter at the main warps' start; 2n + C + 4 chunk + k:
         // timer (ns) at main start, halo complete, first and last publication; 2n + 5C +
-        // 8 chunk + k: two unused words, cycles waited for y, bit mask of the blocks that waited,
+        // 8 chunk + k: cycles waited for y of blocks with and without operands inside the chunk, their sum, bit mask of the blocks that waited,
         // cycles at the partial-sum barrier, in the mat-vec, at the step barrier, from the
         // partial-sum barrier to the publication; 2n + 13C + 16 chunk + B: cycle counter when a
         // helper published y_B.
@@ -890,7 +890,7 @@ csr_chain_kernel(const ChainParams q) {
         double *xout = p.x + (upper ? p.n - 1 - (row0 + local) : row0 + local);
         const bool push = crank + 1 < csize && row0 + kChainRows < q.row_end;   // (then the chunk is full)
         const unsigned next_halo = push ? cluster_map(sxh, crank + 1) + (half * 32 + lane) * 8 : 0u;
-        long long y_wait_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int y_waits_ = 0;
+        long long y_wait_ = 0, y_listed_ = 0, y_far_ = 0, z_wait_ = 0, mv_ = 0, ss_ = 0, pub_ = 0; int y_waits_ = 0;
         auto step_block = [&](const int B, auto pushing) {
             constexpr bool kPush = decltype(pushing)::value;
             const int s = B % kChainStages;
@@ -899,7 +899,7 @@ csr_chain_kernel(const ChainParams q) {
                 long long c0_ = TRACE ? clock64() : 0;
                 dead = !warp_wait([&] { return !is_pending(y = syv[local]); }, dl, failed_flag,
                                   p.status, row0 + local);
-                if (TRACE) { y_wait_ += clock64() - c0_; y_waits_ |= 1 << B; }
+                if (TRACE) { const long long w_ = clock64() - c0_; y_wait_ += w_; y_waits_ |= 1 << B; if ((s_width[2 * B] | s_width[2 * B + 1]) != 0) y_listed_ += w_; else y_far_ += w_; }
                 if (dead) y = nanv;
             }
             ynext = syv[local + 64];   // (one block of slack behind sy keeps this in bounds)
@@ -932,7 +932,7 @@ csr_chain_kernel(const ChainParams q) {
         if (push) step_block(npair - 1, std::true_type());
         if (tracer) {
             long long *o = p.trace + 2ll * p.n + 5 * n_chunks + 8ll * chunk;
-            o[0] = 0; o[1] = 0; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_; o[5] = mv_; o[6] = ss_; o[7] = pub_;
+            o[0] = y_listed_; o[1] = y_far_; o[2] = y_wait_; o[3] = y_waits_; o[4] = z_wait_; o[5] = mv_; o[6] = ss_; o[7] = pub_;
         }
         if (dead && lane == 0) *failed_flag = 1;
         if (half == 0 && lane == 0) atomicAdd(&p.status[kStatusDone], 1);
@@ -983,12 +983,37 @@ csr_chain_kernel(const ChainParams q) {
                 if (!parked) continue;
                 const int local = pr * 64 + h * 32 + lane;
                 mask[i][h] = spend[local];
+                // (rows with an operand inside the chunk have their list's first entry filled)
+                const bool in_chunk = s_width[2 * pr + h] != 0 && ecol[s_bptr[2 * pr + h] + lane] != kChainRows;
                 if (mask[i][h]) {
                     const int r = upper ? p.n - 1 - (row0 + local) : row0 + local;
                     int hi = 0, d = -1;
                     csr_row_range(p, r, lo[i][h], hi, d);
-                    prefetch_columns(pr, h);
                 }
+                if (mask[i][h] || in_chunk) prefetch_columns(pr, h);
+            }
+        }
+        // Blocks that only wait for operands from the chunks before: where at most two rows per
+        // half do, their columns of M are loaded now, so that the last operand's arrival is
+        // followed by shuffles and multiply-adds only.
+        int wt[kMine][2], wb[kMine][2];
+        double wa[kMine][2], wc[kMine][2], wd[kMine][2];
+        unsigned quick = 0;
+#pragma unroll
+        for (int i = 0; i < kMine; ++i) {
+            const int pr = first + i * kChainHelpers;
+            unsigned top = __ballot_sync(kFullMask, mask[i][0] != 0), bot = __ballot_sync(kFullMask, mask[i][1] != 0);
+            const bool few = (remaining >> i & 1u) && !(listed >> i & 1u) && __popc(top) <= 2 && __popc(bot) <= 2;
+            if (few) quick |= 1u << i;
+            const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                wt[i][u] = wb[i][u] = -1;
+                wa[i][u] = wc[i][u] = wd[i][u] = 0.0;
+                if (few && top) { wt[i][u] = __ffs(top) - 1; top &= top - 1; }
+                if (few && bot) { wb[i][u] = __ffs(bot) - 1; bot &= bot - 1; }
+                if (wt[i][u] >= 0) { wa[i][u] = __ldg(m11 + wt[i][u] * 32); wc[i][u] = __ldg(m11 + kTileDoubles + wt[i][u] * 32); }
+                if (wb[i][u] >= 0) wd[i][u] = __ldg(m11 + 2 * kTileDoubles + wb[i][u] * 32);
             }
         }
         // (column and coefficient of the operand a row is waiting for stay in registers: a
@@ -1026,7 +1051,25 @@ csr_chain_kernel(const ChainParams q) {
                     }
                 if (!(remaining >> i & 1u)) continue;
                 if (!__all_sync(kFullMask, (mask[i][0] | mask[i][1]) == 0)) continue;
-                if (!(listed >> i & 1u)) finish_parked(first + i * kChainHelpers, delta[i][0], delta[i][1]);
+                if (quick >> i & 1u) {
+                    const int pr = first + i * kChainHelpers;
+                    double ytop = sacc[pr * 64 + lane], ybot = sacc[pr * 64 + 32 + lane];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        if (wt[i][u] >= 0) {             // (warp-uniform)
+                            const double dt = __shfl_sync(kFullMask, delta[i][0], wt[i][u]);
+                            ytop = fma(wa[i][u], dt, ytop);
+                            ybot = fma(wc[i][u], dt, ybot);
+                        }
+                        if (wb[i][u] >= 0)
+                            ybot = fma(wd[i][u], __shfl_sync(kFullMask, delta[i][1], wb[i][u]), ybot);
+                    }
+                    syv[pr * 64 + lane] = publishable(ytop);
+                    syv[pr * 64 + 32 + lane] = publishable(ybot);
+                    if (TRACE && lane == 0) p.trace[2ll * p.n + 13ll * ((p.n + kChainRows - 1) / kChainRows) + 16ll * chunk + pr] = clock64();
+                } else if (!(listed >> i & 1u)) {
+                    finish_parked(first + i * kChainHelpers, delta[i][0], delta[i][1]);
+                }
                 remaining &= ~(1u << i);
             }
             if (remaining && (++polls & 15u) == 0 &&
@@ -1040,12 +1083,33 @@ csr_chain_kernel(const ChainParams q) {
             if (!(listed >> i & 1u)) continue;
             const int pr = first + i * kChainHelpers;
             bool bad = false;
+            // Which rows can end up with a correction is known before the operands are: rows
+            // with an entry in the list, and rows that already have one from the chunks before.
+            // Their columns of M are loaded now, while the warp waits, so that what follows the
+            // arrival of the last operand is shuffles and multiply-adds only (the block two
+            // blocks ahead of an operand has one step of the main warps to get its y out).
+            const double *m11 = wsc + (long long)pr * kPairDoubles + lane;
+            unsigned top = __ballot_sync(kFullMask, delta[i][0] != 0.0 ||
+                (s_width[2 * pr] != 0 && ecol[s_bptr[2 * pr] + lane] != kChainRows));
+            unsigned bot = __ballot_sync(kFullMask, delta[i][1] != 0.0 ||
+                (s_width[2 * pr + 1] != 0 && ecol[s_bptr[2 * pr + 1] + lane] != kChainRows));
+            const bool few = __popc(top) <= 4 && __popc(bot) <= 4;
+            int ct[4], cb[4];
+            double at[4], bt[4], bb[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ct[u] = cb[u] = -1;
+                at[u] = bt[u] = bb[u] = 0.0;
+                if (few && top) { ct[u] = __ffs(top) - 1; top &= top - 1; }
+                if (few && bot) { cb[u] = __ffs(bot) - 1; bot &= bot - 1; }
+                if (ct[u] >= 0) { at[u] = __ldg(m11 + ct[u] * 32); bt[u] = __ldg(m11 + kTileDoubles + ct[u] * 32); }
+                if (cb[u] >= 0) bb[u] = __ldg(m11 + 2 * kTileDoubles + cb[u] * 32);
+            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int blk = 2 * pr + h;
                 const int width = s_width[blk];
                 int pos = s_bptr[blk] + lane;
-                if (width && ecol[pos] != kChainRows) prefetch_columns(pr, h);
                 double t0 = delta[i][h], t1 = 0.0;
                 for (int j = 0; j < width && !bad; j += 2, pos += 64) {
                     const int c0 = ecol[pos], c1 = ecol[pos + 32];
@@ -1065,7 +1129,23 @@ csr_chain_kernel(const ChainParams q) {
                 if (lane == 0) *failed_flag = 1;
                 return;
             }
-            finish_parked(pr, delta[i][0], delta[i][1]);
+            if (!few) {
+                finish_parked(pr, delta[i][0], delta[i][1]);
+                continue;
+            }
+            double ytop = sacc[pr * 64 + lane], ybot = sacc[pr * 64 + 32 + lane];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (ct[u] >= 0) {                // (warp-uniform)
+                    const double dt = __shfl_sync(kFullMask, delta[i][0], ct[u]);
+                    ytop = fma(at[u], dt, ytop);
+                    ybot = fma(bt[u], dt, ybot);
+                }
+                if (cb[u] >= 0) ybot = fma(bb[u], __shfl_sync(kFullMask, delta[i][1], cb[u]), ybot);
+            }
+            syv[pr * 64 + lane] = publishable(ytop);
+            syv[pr * 64 + 32 + lane] = publishable(ybot);
+            if (TRACE && lane == 0) p.trace[2ll * p.n + 13ll * ((p.n + kChainRows - 1) / kChainRows) + 16ll * chunk + pr] = clock64();
         }
     }
     // Then the blocks without a parked product (their operand list did not fit), in order.
