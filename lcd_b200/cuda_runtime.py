@@ -67,8 +67,8 @@ def _pinned_block(shape, dtype):
         return torch.empty(shape, dtype=dtype, pin_memory=True)
 
 
-# Page-locked host arrays of at least twice this size are uploaded in pieces of this size on a
-# copy stream of their own, with an event after each piece: a launcher that consumes its input
+# Page-locked host arrays of at least twice this size are uploaded in pieces (a quarter of this
+# size first, then doubling) on a copy stream of their own, with an event after each piece: a launcher that consumes its input
 # front to back (the chain solver) starts on the first rows while the rest is still in flight.
 STREAMED_UPLOAD_BYTES = 64 << 20
 _COPY_STREAMS = {}
@@ -148,10 +148,12 @@ class TorchCUDA:
         step = STREAMED_UPLOAD_BYTES // host.element_size()
         arrival = []
         with torch.cuda.stream(copies):
-            start = 0
+            start, piece = 0, step // 4
             while start < host.numel():
-                # (a short first piece: whoever follows the pieces starts a millisecond earlier)
-                end = min(host.numel(), start + (step if start else step // 4))
+                # (a short first piece: whoever follows the pieces starts early; then doubling:
+                # the link is faster than any consumer here, and fewer pieces mean fewer launches)
+                end = min(host.numel(), start + piece)
+                piece *= 2
                 device[start:end].copy_(host[start:end], non_blocking=True)
                 event = torch.cuda.Event()
                 event.record(copies)
