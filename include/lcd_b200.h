@@ -310,6 +310,17 @@ int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
 int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
                           double *Ax, const int32_t *diag_pos, int lanes_per_row,
                           int32_t timeout_ms, void *stream, int *status_host);
+/*
+ * ILU0 on CSC storage (compiler/demo/spilu0.py:50-82, the right-looking column loop) is served by
+ * the row kernels: the column form updates the same entries in the same order, so the values are
+ * gathered into row order through a position map (position[k] = place in the column-ordered
+ * array of the k-th entry in row order; the host side builds it with the row pointers, column
+ * indices and diagonal positions of the row-ordered view), factored with lcd_spilu0_csr and
+ * scattered back.  lcd_permute_f64: scatter = 0: out[k] = in[position[k]]; scatter = 1:
+ * out[position[k]] = in[k]; in and out must not alias; positions are not range-checked.
+ */
+int lcd_permute_f64(int64_t count, const int32_t *position, const double *in, double *out, int scatter,
+                    void *stream);
 
 /* ---- supernodal SpTRSV ------------------------------------------------------- */
 /*

@@ -60,6 +60,7 @@ _SIGNATURES = {
     "lcd_chain_prepare": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, c_int64, _P]),
     "lcd_sptrsv_csr_chain": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P, c_int64,
                                      _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_permute_f64": (c_int, [c_int64, _P, _P, _P, c_int, _P]),
     "lcd_chain_prepare_rows": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, c_int64, c_int32,
                                        c_int32, _P]),
     "lcd_sptrsv_csr_chain_rows": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P, c_int64,

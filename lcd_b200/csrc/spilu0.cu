@@ -272,3 +272,33 @@ extern "C" int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, 
     }
     return finish(status_dev, st, status_host);
 }
+
+// ---- CSC storage -----------------------------------------------------------------------
+// ILU0 of a matrix stored by columns (compiler/demo/spilu0.py:50-82) applies the same updates to
+// the same entries in the same order as the row form does (every entry (i, j) is updated once
+// per pivot k < min(i, j), pivots ascending; l_ik is divided once its updates are in).  So the
+// column form is served by the row kernels on the row-ordered view of the values: gather them
+// through the position map (row order -> column order), factor, scatter back.
+namespace lcd {
+__global__ void __launch_bounds__(256)
+permute_f64_kernel(long long count, const int32_t *__restrict__ position, const double *__restrict__ in,
+                   double *__restrict__ out, int scatter) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
+        const int32_t q = __ldg(position + k);
+        if (scatter) out[q] = in[k];
+        else out[k] = __ldg(in + q);
+    }
+}
+}  // namespace lcd
+
+extern "C" int lcd_permute_f64(int64_t count, const int32_t *position, const double *in, double *out,
+                               int scatter, void *stream) {
+    if (count < 0 || (count > 0 && (!position || !in || !out || in == out))) return LCD_ERR_INVALID_ARGUMENT;
+    if (count == 0) return LCD_OK;
+    const long long want = (count + 255) / 256;
+    const int blocks = (int)(want < (long long)sm_count() * 16 ? want : (long long)sm_count() * 16);
+    permute_f64_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(count, position, in, out, scatter);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}

@@ -383,6 +383,57 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
     return Ax
 
 
+class CscRowView:
+    """Row-ordered view of a CSC pattern: CSR pointers, column indices, diagonal positions and
+    ``position`` (place in the column-ordered arrays of the k-th entry in row order)."""
+
+    def __init__(self, ptr_, idx, diag_pos, position):
+        self.Ap, self.Ai, self.diag_pos, self.position = ptr_, idx, diag_pos, position
+
+
+def csc_row_view(Ap, Ai):
+    """Build the row-ordered view of a CSC pattern on the device (structure only: once per
+    pattern).  Entries of a row come out by ascending column; entries of one position keep
+    their storage order."""
+    _require(Ap, torch.int32, "Ap")
+    _require(Ai, torch.int32, "Ai")
+    n = Ap.numel() - 1
+    counts = (Ap[1:] - Ap[:-1]).to(torch.int64)
+    cols = torch.repeat_interleave(torch.arange(n, device=Ap.device, dtype=torch.int64), counts)
+    rows = Ai.to(torch.int64)
+    if rows.numel() and (int(rows.min()) < 0 or int(rows.max()) >= n):
+        raise nat.NativeError(nat.ERR_INDEX_RANGE, "csc_row_view: row index outside the matrix")
+    order = torch.sort(rows * n + cols, stable=True).indices
+    ptr_ = torch.zeros(n + 1, dtype=torch.int64, device=Ap.device)
+    ptr_[1:] = torch.cumsum(torch.bincount(rows, minlength=n), 0)
+    ptr_, idx = ptr_.to(torch.int32), cols[order].to(torch.int32).contiguous()
+    return CscRowView(ptr_, idx, diag_positions(ptr_, idx), order.to(torch.int32).contiguous())
+
+
+def permute(position, values, out=None, *, scatter=False):
+    """out[k] = values[position[k]] (gather) or out[position[k]] = values[k] (scatter)."""
+    _require(values, torch.float64, "values")
+    out = torch.empty_like(values) if out is None else out
+    check(nat.load().lcd_permute_f64(position.numel(), ptr(position), ptr(values), ptr(out),
+                                     1 if scatter else 0, _stream()), "lcd_permute_f64")
+    return out
+
+
+def spilu0_csc(Ap, Ai, Ax, view=None, *, mode="sync_free", wavefronts=None, wavefront_ptr_host=None,
+               lanes=0, status=None, timeout_ms=0):
+    """In-place ILU(0) of a matrix stored by columns (the loop of compiler/demo/spilu0.py:50-82);
+    returns Ax.  The column loop applies the same updates to the same entries in the same order
+    as the row loop, so the values are gathered into row order (``view`` = ``csc_row_view(Ap,
+    Ai)``, reusable while the pattern stays), factored by the row kernel and scattered back.
+    ``wavefronts`` are level sets of the row view's DAG."""
+    _require(Ax, torch.float64, "Ax")
+    view = csc_row_view(Ap, Ai) if view is None else view
+    by_rows = permute(view.position, Ax)
+    spilu0_csr(view.Ap, view.Ai, by_rows, view.diag_pos, mode=mode, wavefronts=wavefronts,
+               wavefront_ptr_host=wavefront_ptr_host, lanes=lanes, status=status, timeout_ms=timeout_ms)
+    return permute(view.position, by_rows, Ax, scatter=True)
+
+
 _checksum_scratch = {}
 
 

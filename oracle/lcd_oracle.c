@@ -338,6 +338,55 @@ void orc_ilu0_csr_fast(int32_t n, const int32_t *Ap, const int32_t *Ai,
     }
 }
 
+/* In-place ILU0 on CSC storage, the right-looking loop nest of compiler/demo/spilu0.py:50-82:
+ * column k is divided by its diagonal, then every later column j that has a nonzero in row k
+ * gets l_ik * u_kj taken off its entry in row i.  The original finds those columns by scanning
+ * all j > k; here row k's entries come from a row index built once (`rowptr`, `rowpos`: for each
+ * row the positions of its entries, by ascending column), which visits the same (i, j) pairs -
+ * each entry receives at most one update per pivot, so their order within a pivot is
+ * immaterial.  Duplicate entries are not supported (the original would use the first match).
+ * work: n + 1 + nnz int32 words. */
+void orc_ilu0_csc(int32_t n, const int32_t *Ap, const int32_t *Ai, double *Ax, int32_t *work) {
+    int32_t *rowptr = work, *rowpos = work + n + 1;
+    int32_t nnz = Ap[n];
+    for (int32_t i = 0; i <= n; ++i) rowptr[i] = 0;
+    for (int32_t p = 0; p < nnz; ++p) rowptr[Ai[p] + 1]++;
+    for (int32_t i = 0; i < n; ++i) rowptr[i + 1] += rowptr[i];
+    for (int32_t j = 0; j < n; ++j)               /* columns ascending: rows come out sorted */
+        for (int32_t p = Ap[j]; p < Ap[j + 1]; ++p) rowpos[rowptr[Ai[p]]++] = p;
+    for (int32_t i = n; i > 0; --i) rowptr[i] = rowptr[i - 1];
+    rowptr[0] = 0;
+    /* column of a stored position, needed to walk row k */
+    for (int32_t k = 0; k < n; ++k) {
+        double diag = 0.0;
+        for (int32_t d = Ap[k]; d < Ap[k + 1]; ++d)
+            if (Ai[d] == k) { diag = Ax[d]; break; }
+        for (int32_t ip = Ap[k]; ip < Ap[k + 1]; ++ip) {
+            int32_t i = Ai[ip];
+            if (i <= k) continue;
+            if (diag != 0.0) {
+                Ax[ip] = Ax[ip] / diag;
+                double lik = Ax[ip];
+                for (int32_t q = rowptr[k]; q < rowptr[k + 1]; ++q) {
+                    int32_t kj = rowpos[q];
+                    /* the column j of position kj: the one whose range holds it */
+                    int32_t lo = 0, hi = n;
+                    while (hi - lo > 1) {
+                        int32_t mid = lo + (hi - lo) / 2;
+                        if (Ap[mid] <= kj) lo = mid; else hi = mid;
+                    }
+                    int32_t j = lo;
+                    if (j <= k) continue;
+                    double ukj = Ax[kj];
+                    if (ukj != 0.0)
+                        for (int32_t t = Ap[j]; t < Ap[j + 1]; ++t)
+                            if (Ai[t] == i) { Ax[t] = Ax[t] - lik * ukj; break; }
+                }
+            }
+        }
+    }
+}
+
 /* Supernodal lower solve, in place on x (x holds b on entry).  Panels are
  * column-major len x width with leading dimension len; Lp is 64-bit. */
 void orc_sptrsv_supernodal(int32_t n_super, const int32_t *sn,

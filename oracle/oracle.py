@@ -165,6 +165,16 @@ def ilu0_csr(Ap, Ai, Ax, fast=False):
     return out
 
 
+def ilu0_csc(Ap, Ai, Ax):
+    """ILU0 on CSC storage (compiler/demo/spilu0.py:50-82); returns the factored copy of Ax."""
+    Ap, Ai = _i32(Ap), _i32(Ai)
+    out = _f64(Ax).copy()
+    n = len(Ap) - 1
+    work = np.zeros(n + 1 + len(Ai), dtype=np.int32)
+    lib().orc_ilu0_csc(n, _p(Ap), _p(Ai), _p(out), _p(work))
+    return out
+
+
 def sptrsv_supernodal(sn, Lip, Li, Lp, Lx, b):
     sn, Lip, Li = _i32(sn), _i32(Lip), _i32(Li)
     Lp = np.ascontiguousarray(Lp, dtype=np.int64)

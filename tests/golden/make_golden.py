@@ -28,7 +28,7 @@ from lcd_b200 import generators as gen  # noqa: E402
 _sink = io.StringIO()
 with contextlib.redirect_stdout(_sink):
     import ref_ops  # noqa: E402
-    from compiler.demo.spilu0 import compile_ilu0_csr, ilu0_csr  # noqa: E402
+    from compiler.demo.spilu0 import compile_ilu0_csr, ilu0_csc, ilu0_csr  # noqa: E402
     from compiler.demo.gauss_seidel import (  # noqa: E402
         full_gauss_seidel_csr, simple_gauss_seidel_csr)
     ilu_syncfree = compile_ilu0_csr("sync_free", 128, 1)
@@ -74,8 +74,45 @@ def triangular_cases():
     return cases
 
 
+def ilu0_inputs():
+    inputs = {"lap3d_g4": gen.laplacian3d_ilu0(4, seed=5)[0]}
+    rnd = sp.random(90, 90, density=0.08, random_state=6, format="csr")
+    rnd = rnd + rnd.T + sp.identity(90) * 4.0
+    rnd = sp.csr_matrix(rnd)
+    rnd.sort_indices()
+    inputs["random_n90"] = rnd
+    nodiag = sp.csr_matrix(rnd.copy())
+    nodiag = nodiag.tolil()
+    nodiag[5, 5] = 0.0
+    nodiag = sp.csr_matrix(nodiag)
+    nodiag.eliminate_zeros()
+    nodiag.sort_indices()
+    inputs["missing_diag_n90"] = nodiag
+    return inputs
+
+
+def write_ilu0_csc(out_dir):
+    """ILU0 on CSC storage: the undecorated loop of compiler/demo/spilu0.py:50-82 on the ILU0
+    inputs, plus an unsymmetric matrix (columns differ from rows)."""
+    inputs = dict(ilu0_inputs())
+    uns = sp.random(70, 70, density=0.1, random_state=8, format="csr") + sp.identity(70) * 3.0
+    inputs["unsymmetric_n70"] = sp.csr_matrix(uns)
+    for name, mat in inputs.items():
+        csc = sp.csc_matrix(mat)
+        csc.sort_indices()
+        data = csc.data.astype(np.float64)
+        indices = csc.indices.astype(np.int32)
+        indptr = csc.indptr.astype(np.int32)
+        out = dict(data=data, indices=indices, indptr=indptr,
+                   factored=ilu0_csc(data.copy(), indices, indptr))
+        np.savez_compressed(os.path.join(out_dir, f"csc_ilu0_{name}.npz"), **out)
+        print("wrote ilu0_csc", name)
+
+
 def main():
     out_dir = HERE
+    if sys.argv[1:] == ["ilu0_csc"]:        # only these fixtures
+        return write_ilu0_csc(out_dir)
     # ---- SpTRSV, lower, CSR and CSC -------------------------------------
     for name, tri in triangular_cases().items():
         out = {}
@@ -192,19 +229,7 @@ def main():
     print("wrote matrix_market_cases")
 
     # ---- ILU0 CSR ---------------------------------------------------------
-    ilu_inputs = {"lap3d_g4": gen.laplacian3d_ilu0(4, seed=5)[0]}
-    rnd = sp.random(90, 90, density=0.08, random_state=6, format="csr")
-    rnd = rnd + rnd.T + sp.identity(90) * 4.0
-    rnd = sp.csr_matrix(rnd)
-    rnd.sort_indices()
-    ilu_inputs["random_n90"] = rnd
-    nodiag = sp.csr_matrix(rnd.copy())
-    nodiag = nodiag.tolil()
-    nodiag[5, 5] = 0.0
-    nodiag = sp.csr_matrix(nodiag)
-    nodiag.eliminate_zeros()
-    nodiag.sort_indices()
-    ilu_inputs["missing_diag_n90"] = nodiag
+    ilu_inputs = ilu0_inputs()
     for name, mat in ilu_inputs.items():
         data = mat.data.astype(np.float64)
         indices = mat.indices.astype(np.int32)
@@ -218,6 +243,8 @@ def main():
         out["factored"] = ilu0_csr(data.copy(), indices, indptr)
         np.savez_compressed(os.path.join(out_dir, f"ilu0_{name}.npz"), **out)
         print("wrote ilu0", name)
+
+    write_ilu0_csc(out_dir)
 
     # ---- supernodal solve ------------------------------------------------
     source = open(os.path.join(REF, "benchmark", "sptrsv_supernodal.py")).read()
