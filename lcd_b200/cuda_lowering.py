@@ -117,6 +117,36 @@ for i in range(n):
                         A_data[j_ptr] = A_data[j_ptr] - l_ik * u_kj
                         break
 """),
+    "ilu0_csc": (dict(A_data="val", A_indices="idx", A_indptr="ptr", n="n"), """
+for k in range(n):
+    col_start = A_indptr[k]
+    col_end = A_indptr[k + 1]
+    diag_val = 0.0
+    for dptr in range(col_start, col_end):
+        if A_indices[dptr] == k:
+            diag_val = A_data[dptr]
+            break
+    for i_ptr in range(col_start, col_end):
+        i = A_indices[i_ptr]
+        if i <= k:
+            continue
+        if diag_val != 0.0:
+            A_data[i_ptr] = A_data[i_ptr] / diag_val
+            l_ik = A_data[i_ptr]
+            for j in range(k + 1, n):
+                j_start = A_indptr[j]
+                j_end = A_indptr[j + 1]
+                u_kj = 0.0
+                for kj_ptr in range(j_start, j_end):
+                    if A_indices[kj_ptr] == k:
+                        u_kj = A_data[kj_ptr]
+                        break
+                if u_kj != 0.0:
+                    for ij_ptr in range(j_start, j_end):
+                        if A_indices[ij_ptr] == i:
+                            A_data[ij_ptr] = A_data[ij_ptr] - l_ik * u_kj
+                            break
+"""),
     "gauss_seidel_simple_csr": (dict(Ap="ptr", Ai="idx", Ax="val", D="diagonal", b="rhs", x="out", n="n"), """
 for i in range(n):
     x[i] = b[i]
@@ -138,7 +168,7 @@ for i in range(n):
 }
 # name of the inner loop a thread map may refer to, per operator
 _THREAD_LOOPS = {"sptrsv_csr_lower": "j", "sptrsv_csc_lower": "j", "sptrsv_csr_upper": "j",
-                 "sptrsv_csc_upper": "j", "ilu0_csr": "j_ptr", "gauss_seidel_simple_csr": "j",
+                 "sptrsv_csc_upper": "j", "ilu0_csr": "j_ptr", "ilu0_csc": "i_ptr", "gauss_seidel_simple_csr": "j",
                  "gauss_seidel_full_csr": "j"}
 GAUSS_SEIDEL_OPERATORS = ("gauss_seidel_simple_csr", "gauss_seidel_full_csr")
 # native entry point serving (operator, execution mode)
@@ -149,6 +179,9 @@ _ENTRY_POINTS = {
     ("sptrsv_csc", "wavefront"): "lcd_sptrsv_wavefront",
     ("ilu0_csr", "sync_free"): "lcd_spilu0_csr",
     ("ilu0_csr", "wavefront"): "lcd_spilu0_csr",
+    # the column loop updates the same entries in the same order: row kernel on the row-ordered view
+    ("ilu0_csc", "sync_free"): "lcd_spilu0_csr",
+    ("ilu0_csc", "wavefront"): "lcd_spilu0_csr",
     # a sweep is a lower-triangular solve on the diagonal-last rows lcd_gs_layout/lcd_gs_values make
     ("gauss_seidel_simple_csr", "sync_free"): "lcd_sptrsv_csr_syncfree",
     ("gauss_seidel_simple_csr", "wavefront"): "lcd_sptrsv_wavefront",
@@ -312,7 +345,7 @@ def recognise_operator(code, loop_iterator):
     if match is None:
         raise CUDALoweringError(
             "The loop nest over %r is not one of the operators served by the native kernels "
-            "(SpTRSV CSR/CSC lower/upper, SpILU0 CSR, Gauss-Seidel CSR sweeps); lcd_b200 does not interpret or "
+            "(SpTRSV CSR/CSC lower/upper, SpILU0 CSR/CSC, Gauss-Seidel CSR sweeps); lcd_b200 does not interpret or "
             "fall back to the CPU." % loop_iterator)
     operator, by_canonical, thread_canonical = match
     roles = {}

@@ -53,6 +53,10 @@ CHAIN_CAPABLE_OPERATORS = ("sptrsv_csr", "gauss_seidel_simple_csr", "gauss_seide
 _DAG_OPERATORS = {("sptrsv_csr", False): "csr_lower", ("sptrsv_csr", True): "csr_upper",
                   ("sptrsv_csc", False): "csc_lower", ("sptrsv_csc", True): "csc_upper",
                   ("ilu0_csr", False): "ilu0_csr",
+                  # the column loop is served through the row-ordered view of the pattern: its
+                  # DAG is the row loop's DAG on that view (the reference's inspector orders all
+                  # columns one after the other for this loop nest, a superset of these edges)
+                  ("ilu0_csc", False): "ilu0_csr",
                   ("gauss_seidel_simple_csr", False): "csr_lower_rows",
                   ("gauss_seidel_full_csr", False): "csr_lower_rows"}
 
@@ -166,8 +170,11 @@ def parallel(**kwargs):
 
         def device_dag(values, structure):
             from . import ops
-            return ops.dag_build(dag_operator, structure[roles["ptr"]], structure[roles["idx"]],
-                                 n=node_count(values, structure))
+            ptr, idx = structure[roles["ptr"]], structure[roles["idx"]]
+            if operator == "ilu0_csc":
+                view = ops.csc_row_view(ptr, idx)
+                ptr, idx = view.Ap, view.Ai
+            return ops.dag_build(dag_operator, ptr, idx, n=node_count(values, structure))
 
         def build_dag(*args, **call_kwargs):
             """(successor lists, dep_count) -- or wavefront lists when the fixed mode is
@@ -210,7 +217,7 @@ def parallel(**kwargs):
                     flops_per_iteration=2, thread_trip_counts=trips,
                     # measured on B200: the ILU0 sync-free kernel pays about 8x the SpTRSV
                     # hand-off (acquire/release flags plus the row update before the release)
-                    sync_free_penalty=8.0 if operator == "ilu0_csr" else 1.0,
+                    sync_free_penalty=8.0 if operator in ("ilu0_csr", "ilu0_csc") else 1.0,
                     chain_capable=operator in CHAIN_CAPABLE_OPERATORS)
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)

@@ -8,10 +8,11 @@ decorated operators of those files (same loop nests, decorated with
 the largest deviation from the sequential result.
 
     python -m lcd_b200.demos sptrsv       matrix.mtx [--max-n 128] [--storage csr|csc|both]
-    python -m lcd_b200.demos spilu0       matrix.mtx [--execution-mode wavefront|sync_free]
+    python -m lcd_b200.demos spilu0       matrix.mtx [--execution-mode wavefront|sync_free] [--storage csr|csc|both]
     python -m lcd_b200.demos gauss-seidel matrix.mtx [--variant simple|full|both] [--iterations 2]
 
-ILU0 in CSC form (``compiler/demo/spilu0.py:50-82``) has no native kernel and is not offered.
+ILU0 in CSC form (``compiler/demo/spilu0.py:50-82``) runs on the row kernels through the
+row-ordered view of the pattern (same updates in the same order: bit-identical values).
 """
 
 from __future__ import annotations
@@ -79,6 +80,45 @@ def ilu0_csr(A_data, A_indices, A_indptr):
     return A_data
 
 
+def ilu0_csc(A_data, A_indices, A_indptr):
+    n = len(A_indptr) - 1
+    for k in range(n):
+        col_start = A_indptr[k]
+        col_end = A_indptr[k + 1]
+        diag_val = 0.0
+        for dptr in range(col_start, col_end):
+            if A_indices[dptr] == k:
+                diag_val = A_data[dptr]
+                break
+        for i_ptr in range(col_start, col_end):
+            i = A_indices[i_ptr]
+            if i <= k:
+                continue
+            if diag_val != 0.0:
+                A_data[i_ptr] = A_data[i_ptr] / diag_val
+                l_ik = A_data[i_ptr]
+                for j in range(k + 1, n):
+                    j_start = A_indptr[j]
+                    j_end = A_indptr[j + 1]
+                    u_kj = 0.0
+                    for kj_ptr in range(j_start, j_end):
+                        if A_indices[kj_ptr] == k:
+                            u_kj = A_data[kj_ptr]
+                            break
+                    if u_kj != 0.0:
+                        for ij_ptr in range(j_start, j_end):
+                            if A_indices[ij_ptr] == i:
+                                A_data[ij_ptr] = A_data[ij_ptr] - l_ik * u_kj
+                                break
+    return A_data
+
+
+def compile_ilu0_csc(execution_mode="wavefront", threads_per_block=128):
+    """CSC ILU0 with the requested executor settings, as ``compiler/demo/spilu0.py:101-108``."""
+    return parallel(block_map="k", function_props=PROPS_ILU0, execution_mode=execution_mode,
+                    threads_per_block=threads_per_block)(ilu0_csc)
+
+
 def compile_ilu0_csr(execution_mode="wavefront", threads_per_block=128, thread_unroll=None):
     """CSR ILU0 with the requested executor settings (the unroll factor is scheduled unless
     given), as ``compiler/demo/spilu0.py:85-99``."""
@@ -140,19 +180,26 @@ def run_sptrsv(matrix_path, max_size=DEFAULT_MAX_N, storage="both"):
 
 
 def run_spilu0(matrix_path, max_size=DEFAULT_MAX_N, execution_mode="wavefront",
-               threads_per_block=128, thread_unroll=None):
-    """In-place ILU(0) of the regularised matrix (CSR) against the sequential loop."""
-    matrix = sp.csr_matrix(load_matrix_market(matrix_path, max_size))
-    matrix.sort_indices()
-    indptr, indices, data = _arrays(matrix)
-    factor = compile_ilu0_csr(execution_mode, threads_per_block, thread_unroll)
-    result = factor(data.copy(), indices, indptr)
-    error = float(np.max(np.abs(result - ilu0_csr(data.copy(), indices, indptr))))
-    schedule = factor.current_schedule
-    print(f"ILU0 CSR: n={matrix.shape[0]}, nnz={matrix.nnz}, mode={schedule.execution_mode}, "
-          f"threads={schedule.threads_per_block}, unroll={schedule.thread_unroll}, "
-          f"max_abs_error={error:.3e}")
-    return {"csr": result}
+               threads_per_block=128, thread_unroll=None, storage="csr"):
+    """In-place ILU(0) of the regularised matrix (CSR and/or CSC storage) against the sequential
+    loops."""
+    source = load_matrix_market(matrix_path, max_size)
+    results = {}
+    for name in (("csr", "csc") if storage == "both" else (storage,)):
+        matrix = sp.csr_matrix(source) if name == "csr" else sp.csc_matrix(source)
+        matrix.sort_indices()
+        indptr, indices, data = _arrays(matrix)
+        if name == "csr":
+            factor, loop = compile_ilu0_csr(execution_mode, threads_per_block, thread_unroll), ilu0_csr
+        else:
+            factor, loop = compile_ilu0_csc(execution_mode, threads_per_block), ilu0_csc
+        results[name] = factor(data.copy(), indices, indptr)
+        error = float(np.max(np.abs(results[name] - loop(data.copy(), indices, indptr))))
+        schedule = factor.current_schedule
+        print(f"ILU0 {name.upper()}: n={matrix.shape[0]}, nnz={matrix.nnz}, mode={schedule.execution_mode}, "
+              f"threads={schedule.threads_per_block}, unroll={schedule.thread_unroll}, "
+              f"max_abs_error={error:.3e}")
+    return results
 
 
 def run_gauss_seidel(matrix_path, max_size=DEFAULT_MAX_N, variant="both", iterations=2):
@@ -191,6 +238,7 @@ def main(argv=None):
             sub.add_argument("--execution-mode", choices=("wavefront", "sync_free"), default="wavefront")
             sub.add_argument("--threads-per-block", type=int, default=128)
             sub.add_argument("--thread-unroll", type=int, choices=(1, 2, 4, 8))
+            sub.add_argument("--storage", choices=("csr", "csc", "both"), default="csr")
         else:
             sub.add_argument("--variant", choices=("simple", "full", "both"), default="both")
             sub.add_argument("--iterations", type=int, default=2)
@@ -203,7 +251,7 @@ def main(argv=None):
         if args.threads_per_block <= 0:
             parser.error("--threads-per-block must be positive")
         return run_spilu0(args.matrix, args.max_n, args.execution_mode, args.threads_per_block,
-                          args.thread_unroll)
+                          args.thread_unroll, args.storage)
     if args.iterations <= 0:
         parser.error("--iterations must be positive")
     return run_gauss_seidel(args.matrix, args.max_n, args.variant, args.iterations)

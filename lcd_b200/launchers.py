@@ -229,13 +229,31 @@ def bind(lowering):
             ops.spilu0_csr(Ap, Ai, Ax, pos, mode="wavefront", wavefronts=nodes,
                            wavefront_ptr_host=ptr_host, lanes=lanes)
 
+    def ilu0_csc(*args, _hints=None):
+        # the column loop applies the row loop's updates in the row loop's order: gather the
+        # values into row order, factor with the row kernel, scatter back (the row-ordered view
+        # of the pattern is kept with the plan)
+        v = split(args)
+        Ap, Ai, Ax = matrix(v)
+        cache = (_hints or {}).setdefault("cache", {})
+        view = cache.get("csc_row_view")
+        if view is None or view.Ap.device != Ap.device:
+            view = cache["csc_row_view"] = ops.csc_row_view(Ap, Ai)
+        if lowering.execution_mode == "sync_free":
+            ops.spilu0_csc(Ap, Ai, Ax, view, mode="sync_free")
+        else:
+            nodes, _, ptr_host = wavefront_arrays(v)
+            ops.spilu0_csc(Ap, Ai, Ax, view, mode="wavefront", wavefronts=nodes,
+                           wavefront_ptr_host=ptr_host)
+
     launcher = {"sptrsv_csr": sptrsv_csr, "sptrsv_csc": sptrsv_csc, "ilu0_csr": ilu0_csr,
+                "ilu0_csc": ilu0_csc,
                 "gauss_seidel_simple_csr": gauss_seidel, "gauss_seidel_full_csr": gauss_seidel}.get(
         lowering.operator)
     if launcher is None:
         raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
     launcher.__name__ = lowering.launcher_name
-    launcher.accepts_hints = launcher in (sptrsv_csr, gauss_seidel)
+    launcher.accepts_hints = launcher in (sptrsv_csr, gauss_seidel, ilu0_csc)
 
     def kernel(*args, **kwargs):
         raise CUDALoweringError(

@@ -186,3 +186,41 @@ def not_served(Ap, Ai, Ax, b, n):
     for i in range(n):
         x[i] = b[i] * 2.0
     return x
+
+
+def ilu0_csc(A_data, A_indices, A_indptr):
+    n = len(A_indptr) - 1
+    for k in range(n):
+        col_start = A_indptr[k]
+        col_end = A_indptr[k + 1]
+        diag_val = 0.0
+        for dptr in range(col_start, col_end):
+            if A_indices[dptr] == k:
+                diag_val = A_data[dptr]
+                break
+        for i_ptr in range(col_start, col_end):
+            i = A_indices[i_ptr]
+            if i <= k:
+                continue
+            if diag_val != 0.0:
+                A_data[i_ptr] = A_data[i_ptr] / diag_val
+                l_ik = A_data[i_ptr]
+                for j in range(k + 1, n):
+                    j_start = A_indptr[j]
+                    j_end = A_indptr[j + 1]
+                    u_kj = 0.0
+                    for kj_ptr in range(j_start, j_end):
+                        if A_indices[kj_ptr] == k:
+                            u_kj = A_data[kj_ptr]
+                            break
+                    if u_kj != 0.0:
+                        for ij_ptr in range(j_start, j_end):
+                            if A_indices[ij_ptr] == i:
+                                A_data[ij_ptr] = A_data[ij_ptr] - l_ik * u_kj
+                                break
+    return A_data
+
+
+def compile_ilu0_csc(execution_mode="wavefront", threads_per_block=128):
+    """As compiler/demo/spilu0.py:101-108 (no thread map: the column loop has none)."""
+    return parallel(block_map="k", function_props=PROPS_ILU, execution_mode=execution_mode, threads_per_block=threads_per_block)(ilu0_csc)

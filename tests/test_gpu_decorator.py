@@ -204,14 +204,19 @@ def test_demos_on_a_matrix_market_file(cuda, tmp_path, capsys):
     np.testing.assert_allclose(solves["csc"], solves["csr"], rtol=1e-10, atol=1e-12)
     assert demos.run_sptrsv(path, 128, "csr")["csr"].shape == (128,)          # leading principal sample
     for mode in ("wavefront", "sync_free"):
-        demos.run_spilu0(path, 0, mode)
+        factors = demos.run_spilu0(path, 0, mode, storage="both")
+        # the same matrix factored by rows and by columns: the same values, entry by entry
+        n = 300
+        by_rows = sp.csr_matrix((factors["csr"], *_pattern(path, "csr")), shape=(n, n))
+        by_cols = sp.csc_matrix((factors["csc"], *_pattern(path, "csc")), shape=(n, n))
+        assert (by_rows != sp.csr_matrix(by_cols)).nnz == 0
     sweeps = demos.run_gauss_seidel(path, 0, "both", 2)
     np.testing.assert_allclose(sweeps["simple"], np.linspace(1.0, 2.0, 300), rtol=1e-10, atol=1e-12)
     np.testing.assert_allclose(sweeps["full"], sweeps["simple"], rtol=1e-10, atol=1e-12)
     demos.main(["gauss-seidel", str(path), "--max-n", "64", "--variant", "full", "--iterations", "3"])
     printed = capsys.readouterr().out
     errors = [float(line.rsplit("=", 1)[1]) for line in printed.splitlines() if "max_abs_error" in line]
-    assert len(errors) == 8 and max(errors) <= 1e-12
+    assert len(errors) == 10 and max(errors) <= 1e-12
     with pytest.raises(SystemExit):
         demos.main(["sptrsv", str(path), "--max-n", "-1"])
 
@@ -249,6 +254,28 @@ def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch
     grid = gen.laplacian2d_tril(64, seed=0)
     od.csr_warp_syncfree(*grid.csr_arrays(), grid.b, grid.n)
     assert calls["solve"] == 3
+
+
+def _pattern(path, storage):
+    from lcd_b200.matrix_market import load_matrix_market
+    matrix = load_matrix_market(path, 0)
+    matrix = sp.csr_matrix(matrix) if storage == "csr" else sp.csc_matrix(matrix)
+    matrix.sort_indices()
+    return matrix.indices, matrix.indptr
+
+
+@pytest.mark.parametrize("mode", ["wavefront", "sync_free"])
+@pytest.mark.parametrize("name", golden_names("csc_ilu0_"))
+def test_decorated_ilu0_on_csc_storage_is_bit_identical(cuda, name, mode):
+    """The column loop of compiler/demo/spilu0.py:50-82 through the decorator."""
+    import ops_decorated as od
+    g = golden(name)
+    op = od.compile_ilu0_csc(mode, 128)
+    out = op(g["data"].copy(), g["indices"], g["indptr"])
+    np.testing.assert_array_equal(out, g["factored"])
+    np.testing.assert_array_equal(out, od.ilu0_csc(g["data"].copy(), g["indices"], g["indptr"]))
+    again = op(g["data"].copy(), g["indices"], g["indptr"])     # cached plan and row view
+    np.testing.assert_array_equal(again, g["factored"])
 
 
 def test_decorated_chain_solve_follows_a_streamed_upload(cuda, oracle, monkeypatch):
