@@ -46,9 +46,13 @@ enum {
     LCD_OP_ILU0_CSR = 2,  /* full rows, sorted     (compiler/demo/spilu0.py:21-47)  */
     LCD_OP_CSR_UPPER = 3, /* rows, diagonal first, visited last to first            */
     LCD_OP_CSC_UPPER = 4, /* cols, diagonal last,  visited last to first            */
-    LCD_OP_CSR_LOWER_ROWS = 5 /* rows, every stored entry left of the diagonal is an operand,
+    LCD_OP_CSR_LOWER_ROWS = 5, /* rows, every stored entry left of the diagonal is an operand,
                                  the diagonal is stored anywhere or kept apart
                                  (compiler/demo/gauss_seidel.py:18-41); DAG build only */
+    LCD_OP_CSR_UPPER_ROWS = 6  /* full rows visited last to first, every stored entry right of
+                                 the diagonal is an operand: the backward solve on the U part of
+                                 an ILU0 factor kept in place (benchmark/spilu0_benchmark.py:
+                                 166-190 splits it off instead); DAG build only */
 };
 
 /* Flags of the CSR solvers. */
@@ -275,13 +279,93 @@ int lcd_sptrsv_wavefront_multi(int32_t n, int64_t nnz, int32_t nrhs, const int32
                                int32_t n_levels, int32_t *status_dev, int32_t timeout_ms,
                                void *stream, int *status_host);
 
+/*
+ * Sync-free CSR solve that hands its rows out in a caller-given topological order, for one or
+ * many right-hand sides (row-major n x nrhs blocks, nrhs <= 64, leading dimension ld >= nrhs in
+ * doubles; nrhs = 1 with ld = 1 is the plain vector solve).  `order` lists node ids (for an upper
+ * solve v = n - 1 - row) so that every operand of a row stands before the row: the level
+ * sets `wavefronts` of lcd_dag_build are such an order, and so is 0..n-1.  Level order keeps
+ * thousands of independent rows in flight on grid-like matrices where index order leaves one
+ * grid line; unlike the level-synchronous kernels below nothing waits for a whole level - a
+ * row waits for its own operands only - so there is neither a grid barrier nor a launch per
+ * level.  Serves the SpTRSV-CSR loop nest (compiler/demo/sptrsv.py:26-34) and, on ILU0
+ * factors (LCD_SOLVE_OF_FULL), the forward / backward solves of
+ * benchmark/spilu0_benchmark.py:166-190; the reference's closest counterpart is the
+ * persistent warp-task launcher, compiler/cuda_lowering.py:1070-1119, which also walks
+ * `task_nodes` in level order.
+ *   task_records  16 n + 2048 bytes of scratch, 16-byte aligned (the tail holds the ticket
+ *               counters, cleared by every call): one record per task {row, first entry,
+ *               entry count, diagonal position}, written by a first pass over (order, Ap,
+ *               diag_pos) unless records_ready != 0, which reuses what an earlier call with the
+ *               same Ap, diag_pos, flags and order left there (order may then be NULL).
+ *   row_flags   NULL: X is pre-filled with a reserved NaN pattern and consumers poll the
+ *               operands themselves (one extra write pass over X);
+ *               n ints of scratch: producers release a flag per row instead (no pass over X,
+ *               two L2 round trips per hand-off instead of one).  Zeroed by the call.
+ *   window_rows upper bound on the rows in flight (0: as many as the device holds).  Rows far
+ *               ahead of the frontier only poll; about four average levels is a good window.
+ *   flags       LCD_SOLVE_UPPER / OF_FULL / UNIT_DIAG (not EXACT: operands are consumed in
+ *               chunks of four as they arrive).
+ * An `order` that lacks a node ends in LCD_ERR_TIMEOUT (bounded waits), never in a hang.
+ */
+int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap,
+                           const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
+                           const double *B, double *X, int64_t ld, int flags,
+                           const int32_t *order, int32_t *task_records, int records_ready,
+                           int32_t *row_flags, int64_t window_rows, int32_t *status_dev,
+                           int32_t timeout_ms, void *stream, int *status_host);
+
+/*
+ * Solves small enough for one thread block (a few hundred thousand rows at most): CSR (pull)
+ * and CSC (push, compiler/demo/sptrsv.py:37-43) triangular solves whose cost is the hand-off
+ * between levels, not bandwidth.  One block walks the level sets with a block barrier per
+ * level and keeps the recent part of x (CSR) or the accumulators of the coming positions
+ * (CSC) in shared memory; nothing spins.  Replaces, for such sizes, the generated wavefront
+ * launchers (compiler/cuda_lowering.py:855-1016: a launch plus a device synchronisation per
+ * level) and the push kernel (:2031-2059).
+ *   lcd_small_plan_measure / lcd_small_plan_fill   once per pattern: `pos` (n ints) receives the
+ *       place of every node in `order` (= wavefronts of lcd_dag_build for the same op);
+ *       info_host[0] = longest row / column without its diagonal, [1] = widest level.  The fill
+ *       writes an ELL image of the matrix in level order with `entries` >= info_host[0] slots
+ *       per task (entries <= lcd_small_max_entries()): ell_pc / ell_src [entries * n] = place
+ *       of the operand (CSR) or target (CSC) and index of its value in Ax, -1 for padding;
+ *       row_of[n], diag_src[n].  *far_host = entries whose other end lies more than half the
+ *       shared-memory ring away (served through global memory).  Errors through status_dev:
+ *       LCD_ERR_INDEX_RANGE, LCD_ERR_BAD_POINTERS, LCD_ERR_CYCLE (order not topological).
+ *       info_dev: 4 ints of device scratch.
+ *   lcd_sptrsv_small   every solve: gathers values, right-hand side and reciprocal diagonals
+ *       into level order (a parallel pass) and walks the levels.  scratch:
+ *       lcd_small_scratch_bytes(n, entries) bytes, 256-byte aligned.  Asynchronous on `stream`;
+ *       it has no device-side waits and reports nothing (the plan calls validated the input).
+ *   op: LCD_OP_CSR_LOWER / CSR_UPPER / CSC_LOWER / CSC_UPPER; flags: LCD_SOLVE_OF_FULL /
+ *   UNIT_DIAG for the CSR ops.
+ */
+int lcd_small_max_entries(void);
+int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
+                           const int32_t *diag_pos, const int32_t *order,
+                           const int32_t *wavefront_ptr_dev, int32_t n_levels, int32_t *pos,
+                           int32_t *info_dev, int32_t *status_dev, void *stream, int32_t *info_host);
+int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
+                        const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
+                        const int32_t *pos, int32_t entries, int32_t *ell_pc, int32_t *ell_src,
+                        int32_t *row_of, int32_t *diag_src, int32_t *info_dev, int32_t *status_dev,
+                        void *stream, int32_t *far_host);
+int lcd_small_scratch_bytes(int32_t n, int32_t entries, int64_t *bytes);
+int lcd_sptrsv_small(int csc, int32_t n, int32_t entries, const double *Ax, const double *b, double *x,
+                     const int32_t *ell_pc, const int32_t *ell_src, const int32_t *row_of,
+                     const int32_t *diag_src, const int32_t *wavefront_ptr_dev, int32_t n_levels,
+                     int32_t max_width, int32_t has_far, void *scratch, int64_t scratch_bytes,
+                     void *stream);
+
 /* ---- SpILU0 (CSR, in place) -------------------------------------------------- */
 /*
  * In-place ILU(0) of a CSR matrix with sorted rows; arithmetic identical to the
  * sequential loop nest of compiler/demo/spilu0.py:21-47 (pivots in ascending
  * order, unfused multiply/subtract).  Replaces the nested-thread-map kernel of
  * compiler/cuda_lowering.py:1572-1989.  mode: 0 = sync-free (per-row done flags in
- * `done`, n ints, zeroed by the call), 1 = per-level launches over wavefronts.
+ * `done`, n ints, zeroed by the call), 1 = per-level launches over wavefronts,
+ * 2 = sync-free with the rows handed out in the order of `wavefronts` (needs `done` and
+ * `wavefronts`; one launch, rows of a level run side by side, no barrier between levels).
  */
 int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, double *Ax,
                    const int32_t *diag_pos, int mode, int32_t *done,
@@ -395,6 +479,19 @@ int lcd_sptrsv_csr_syncfree_part(int32_t n, int64_t nnz, const int32_t *Ap, cons
                                  int32_t n_ranks, int threads_per_block, int32_t *status_dev,
                                  int32_t timeout_ms, void *stream, int *status_host);
 
+/* The same partition with each rank's rows handed out in the order of the global level sets
+ * (lcd_sptrsv_csr_ordered's kernel): order_local lists this rank's n_local nodes in that order;
+ * task_records: 16 n_local + 2048 bytes of scratch (records_ready as for lcd_sptrsv_csr_ordered).
+ * Operands that may come from a peer are polled with system-scope loads.  x must have been
+ * filled and all ranks synchronised as for lcd_sptrsv_csr_syncfree_part.  flags: LCD_SOLVE_UPPER. */
+int lcd_sptrsv_csr_ordered_part(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                const double *Ax, const double *b, double *x, int flags,
+                                const int32_t *order_local, int32_t n_local, int32_t *task_records,
+                                int records_ready, const unsigned char *need_mask,
+                                double *const *peer_x, int32_t n_ranks, int64_t window_rows,
+                                int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                int *status_host);
+
 /* Scheduling knobs of the one-lane-per-row sync-free kernel (process-wide).  They
  * change waiting behaviour only, never results.  The reference's counterpart is the
  * schedule search of compiler/scheduler.py:172-303 (block size / unroll / protocol). */
@@ -405,8 +502,12 @@ enum {
     LCD_TUNE_ROW_VARIANT = 3,     /* 0: thread-per-row kernel, 1: generic lane-group kernel */
     LCD_TUNE_STAGE_PERCENT = 4,   /* shared-memory staging of a chunk's matrix entries, in percent
                                      of the average chunk size (0 = read entries from global) */
-    LCD_TUNE_CHAIN_CLUSTER = 5    /* blocks per cluster of the chain solver: 0 = as many as the device
+    LCD_TUNE_CHAIN_CLUSTER = 5,   /* blocks per cluster of the chain solver: 0 = as many as the device
                                      hosts (up to 8), 1 = plain blocks, 2 / 4 / 8 = at most that */
+    LCD_TUNE_ORDERED_PAUSE_NS = 6, /* lcd_sptrsv_csr_ordered: longest pause of a warp between two
+                                     unsuccessful polls (0 = never pause; default 256) */
+    LCD_TUNE_SMALL_THREADS = 7    /* lcd_sptrsv_small: threads of the one block, 256 / 512 / 1024
+                                     (0 = 512 while no level is wider than that, else 1024) */
 };
 int lcd_set_tuning(int key, int value);
 /* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,

@@ -16,12 +16,13 @@ LIB_PATH = os.path.join(_HERE, "liblcd_b200.so")
 # LCD_* codes of include/lcd_b200.h
 OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
     ERR_BAD_POINTERS, ERR_INDEX_RANGE, ERR_CYCLE, ERR_MISSING_DIAGONAL, ERR_TOO_LARGE = range(11)
-OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER, OP_CSR_LOWER_ROWS = range(6)
+(OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER, OP_CSR_LOWER_ROWS,
+ OP_CSR_UPPER_ROWS) = range(7)
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
 WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
 (TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT,
- TUNE_CHAIN_CLUSTER) = range(6)
+ TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS) = range(8)
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -81,6 +82,17 @@ _SIGNATURES = {
     "lcd_sptrsv_wavefront_multi": (c_int, [c_int32, c_int64, c_int32, _P, _P, _P, _P, _P, _P, c_int64,
                                            c_int, _P, _P, c_int32, _P, c_int32, _P,
                                            ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_csr_ordered": (c_int, [c_int32, c_int64, c_int32, _P, _P, _P, _P, _P, _P, c_int64,
+                                       c_int, _P, _P, c_int, _P, c_int64, _P, c_int32, _P,
+                                       ctypes.POINTER(c_int)]),
+    "lcd_small_max_entries": (c_int, []),
+    "lcd_small_plan_measure": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, c_int32, _P,
+                                       _P, _P, _P, ctypes.POINTER(c_int32 * 4)]),
+    "lcd_small_plan_fill": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, _P, c_int32,
+                                    _P, _P, _P, _P, _P, _P, _P, ctypes.POINTER(c_int32)]),
+    "lcd_small_scratch_bytes": (c_int, [c_int32, c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_sptrsv_small": (c_int, [c_int, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P, c_int32,
+                                 c_int32, c_int32, _P, c_int64, _P]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_spilu0_csr_static": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, c_int32, _P,
@@ -98,6 +110,9 @@ _SIGNATURES = {
     "lcd_sptrsv_csr_syncfree_part": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, c_int, c_int32,
                                              c_int32, _P, ctypes.POINTER(c_void_p), c_int32, c_int,
                                              _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_sptrsv_csr_ordered_part": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, c_int, _P, c_int32,
+                                            _P, c_int, _P, ctypes.POINTER(c_void_p), c_int32, c_int64,
+                                            _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_set_tuning": (c_int, [c_int, c_int]),
     "lcd_debug_set_trace": (c_int, [_P]),
     "lcd_checksum_i32": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_uint64 * 2), _P]),

@@ -41,6 +41,8 @@ inline unsigned long long timeout_ns(int32_t timeout_ms) {
 int sm_count();
 void set_debug_trace(long long *p);
 int set_chain_cluster_limit(int blocks);  // LCD_TUNE_CHAIN_CLUSTER
+int set_ordered_pause(int ns);           // LCD_TUNE_ORDERED_PAUSE_NS
+int set_small_threads(int threads);      // LCD_TUNE_SMALL_THREADS
 long long *debug_trace();  // profiling aid set by lcd_debug_set_trace (NULL = off)
 
 #ifdef __CUDACC__
@@ -56,6 +58,12 @@ __device__ __forceinline__ unsigned long long global_timer() {
 __device__ __forceinline__ double ld_relaxed_f64(const double *p) {
     double v;
     asm volatile("ld.relaxed.gpu.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+// system scope: the value may have been stored by another GPU through a peer mapping
+__device__ __forceinline__ double ld_relaxed_sys_f64(const double *p) {
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ void st_relaxed_f64(double *p, double v) {

@@ -227,7 +227,8 @@ __device__ __forceinline__ bool src_major(int op) {
 // Returns an LCD_* code for malformed input.
 template <typename F>
 __device__ __forceinline__ int visit_edges(const EdgeRule &q, int v, F f) {
-    const bool upper = q.op == LCD_OP_CSR_UPPER || q.op == LCD_OP_CSC_UPPER;
+    const bool upper = q.op == LCD_OP_CSR_UPPER || q.op == LCD_OP_CSC_UPPER ||
+                       q.op == LCD_OP_CSR_UPPER_ROWS;
     const int i = upper ? q.n - 1 - v : v;
     const int s = q.ptr[i], e = q.ptr[i + 1];
     if (s < 0 || e < s || (long long)e > q.nnz) return LCD_ERR_BAD_POINTERS;
@@ -246,7 +247,8 @@ __device__ __forceinline__ int visit_edges(const EdgeRule &q, int v, F f) {
                 if (c >= i) return rc;
                 f(c, i);
                 break;
-            case LCD_OP_CSR_UPPER: if (c > i) f(q.n - 1 - c, v); break;
+            case LCD_OP_CSR_UPPER:
+            case LCD_OP_CSR_UPPER_ROWS: if (c > i) f(q.n - 1 - c, v); break;
             default: if (c < i) f(v, q.n - 1 - c); break;  // LCD_OP_CSC_UPPER
         }
     }
@@ -509,7 +511,7 @@ static inline int grid_for(long long m, int threads) {
 using namespace lcd;
 
 extern "C" int lcd_dag_workspace_bytes(int op, int32_t n, int64_t nnz, int64_t *bytes) {
-    if (op < 0 || op > LCD_OP_CSR_LOWER_ROWS || n < 0 || nnz < 0 || !bytes)
+    if (op < 0 || op > LCD_OP_CSR_UPPER_ROWS || n < 0 || nnz < 0 || !bytes)
         return LCD_ERR_INVALID_ARGUMENT;
     Bump b{nullptr, 0};
     b.take<int32_t>(LCD_STATUS_WORDS);
@@ -524,7 +526,7 @@ extern "C" int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_
                              int32_t *level, int32_t *wavefronts, int32_t *wavefront_ptr,
                              int32_t *n_levels_host, void *workspace, int64_t workspace_bytes,
                              int32_t timeout_ms, void *stream) {
-    if (op < 0 || op > LCD_OP_CSR_LOWER_ROWS || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
+    if (op < 0 || op > LCD_OP_CSR_UPPER_ROWS || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
         return LCD_ERR_INVALID_ARGUMENT;
     *n_edges_host = 0;
     *n_levels_host = 0;

@@ -12,6 +12,9 @@
 // pivot without blocking (one poll per loop trip), so groups that share a warp
 // never wait on each other inside a convergence region.
 // Wavefront mode: one launch per level over the same row code.
+// Ordered mode: the sync-free kernel with rows handed out in the order of the level sets
+// instead of by index: one launch, no barrier between levels, and the rows of a level -
+// independent of each other - are resident together.
 #include "common.cuh"
 
 namespace lcd {
@@ -35,6 +38,12 @@ template <int G>
 __device__ __forceinline__ void apply_pivot(const Ilu0Params &p, int i, int row_start, int row_end,
                                             int kp, int k, int lane, unsigned gmask) {
     const int dk = __ldg(p.dpos + k);
+    const int ks = __ldg(p.Ap + k), ke = __ldg(p.Ap + k + 1);
+    // group-uniform checks: the pivot row's segment is searched below and its diagonal read
+    if (ks < 0 || ke < ks || (long long)ke > p.nnz || (long long)dk >= p.nnz) {
+        if (lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, k);
+        return;
+    }
     double diag = 0.0;
     if (dk >= 0) diag = ld_relaxed_f64(p.Ax + dk);
     if (diag == 0.0) return;  // group-uniform: every lane read the same value
@@ -45,7 +54,6 @@ __device__ __forceinline__ void apply_pivot(const Ilu0Params &p, int i, int row_
         p.Ax[kp] = lik;
     }
     if (G > 1) lik = __shfl_sync(gmask, lik, owner, G);
-    const int ks = __ldg(p.Ap + k), ke = __ldg(p.Ap + k + 1);
     // first own position after kp
     int jp = kp + 1 + ((lane - (kp + 1 - row_start)) % G + G) % G;
     for (; jp < row_end; jp += G) {
@@ -67,14 +75,25 @@ __global__ void __launch_bounds__(TPB) ilu0_syncfree_kernel(const Ilu0Params p) 
     if (threadIdx.x == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
     __syncthreads();
     const int local = threadIdx.x / G, lane = threadIdx.x % G;
-    const int i = s_chunk * R + local;
-    if (i >= p.n) return;
+    const int task = s_chunk * R + local;
+    if (task >= p.n) return;
+    // rows in index order, or in the order of the level sets (any topological order): a row
+    // then waits for rows of earlier tickets only, and rows of one level run side by side
+    int i = task;
+    if (p.wavefronts) {
+        i = __ldg(p.wavefronts + task);
+        if ((unsigned)i >= (unsigned)p.n) {
+            if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, task);
+            return;
+        }
+    }
     const unsigned gmask =
         G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
     const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
     bool bad = s < 0 || e < s || (long long)e > p.nnz;
     if (bad && lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
     int kp = s;
+    unsigned pause = 0;
     Deadline dl;
     dl.start(p.budget_ns);
     for (;;) {
@@ -99,8 +118,13 @@ __global__ void __launch_bounds__(TPB) ilu0_syncfree_kernel(const Ilu0Params p) 
             if (ready == 1) {
                 apply_pivot<G>(p, i, s, e, kp, k, lane, gmask);
                 ++kp;
+                pause = 0;
             } else if (ready == 2) {
                 bad = true;
+            } else {
+                // rows far behind the frontier stop competing for L2 with the polls that matter
+                pause = pause ? min(pause * 2, 1024u) : 32u;
+                __nanosleep(pause);
             }
         } else {
             // all stores of the group happen before the flag becomes visible
@@ -121,7 +145,10 @@ __global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int
     const int t = wave_start + gtid / G, lane = gtid % G;
     if (t >= wave_end) return;
     const int i = __ldg(p.wavefronts + t);
-    if ((unsigned)i >= (unsigned)p.n) return;
+    if ((unsigned)i >= (unsigned)p.n) {
+        if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, t);
+        return;
+    }
     const unsigned gmask =
         G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
     const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
@@ -140,7 +167,7 @@ __global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int
 template <int G>
 static cudaError_t launch_ilu0(const Ilu0Params &p, int mode, const int32_t *wptr_host,
                                int n_levels, cudaStream_t st) {
-    if (mode == 0) {
+    if (mode == 0 || mode == 2) {
         constexpr int TPB = 256, R = TPB / G;
         ilu0_syncfree_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
     } else {
@@ -163,11 +190,12 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
                               const int32_t *wavefronts, const int32_t *wavefront_ptr_host,
                               int32_t n_levels, int lanes_per_row, int32_t *status_dev,
                               int32_t timeout_ms, void *stream, int *status_host) {
-    if (n < 0 || nnz < 0 || !status_dev || (mode != 0 && mode != 1)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n < 0 || nnz < 0 || !status_dev || mode < 0 || mode > 2) return LCD_ERR_INVALID_ARGUMENT;
     if (n > 0 && (!Ap || !Ai || !Ax || !diag_pos)) return LCD_ERR_INVALID_ARGUMENT;
-    if (n > 0 && mode == 0 && !done) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && mode != 1 && !done) return LCD_ERR_INVALID_ARGUMENT;
     if (n > 0 && mode == 1 && (!wavefronts || !wavefront_ptr_host || n_levels < 0))
         return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && mode == 2 && !wavefronts) return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;
     int G = lanes_per_row;
     if (G <= 0) {
@@ -177,8 +205,8 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
     int rc = reset_status(status_dev, st);
     if (rc) return rc;
     if (n > 0) {
-        if (mode == 0) LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
-        Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, wavefronts, status_dev,
+        if (mode != 1) LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
+        Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, mode == 0 ? nullptr : wavefronts, status_dev,
                      timeout_ns(timeout_ms)};
         cudaError_t e;
         switch (G) {

@@ -1,0 +1,424 @@
+// Sync-free CSR triangular solves that take their rows in a caller-given topological
+// order (sm_100a), for one or many right-hand sides.
+//
+// Why an order.  The index-ordered sync-free kernels hand rows out by ascending index,
+// which is a valid topological order of a triangular matrix but a poor one for grid-like
+// matrices: the rows resident at one time then form a thin slab whose parallelism is one
+// grid line.  The level sets of lcd_dag_build list the rows level by level; handing rows
+// out in that order keeps whole levels of independent rows in flight, and - unlike the
+// level-synchronous kernels - nothing ever waits for a whole level: a row waits for
+// exactly its own operands (point-to-point), so there is no grid barrier and no launch
+// per level.
+//
+// Scheduling.  Persistent warps draw tasks from ticket counters, 32 / W consecutive tasks
+// per draw: groups of W lanes (W * KR >= nrhs, lane l of a group owns the right-hand sides
+// l, l + W, ...) take one row each, so no row ever queues behind another row of its own
+// warp.  A task only waits for tasks with smaller numbers, all of which belong to warps
+// that are running or finished: every wait terminates.
+//
+// No pointer chasing on the dependence chain.  A first pass turns (order, Ap, diag_pos)
+// into one 16-byte record per task {row, first entry, entry count, diagonal position}
+// (structure only: reusable while the pattern and the order stay).  The solve kernel is a
+// three-stage software pipeline per warp: while batch k is solved, the records of batch
+// k + 2 and the entries, diagonal and right-hand side of batch k + 1 are already in
+// flight; each stage's addresses come from loads issued a whole batch earlier.  What
+// remains on the chain of a row is: poll its operands, multiply-add, publish.
+//
+// Waiting.  All groups of a warp make one non-blocking attempt per trip and the trip ends
+// in a warp-wide vote, so no lane spins inside a branch (rows of one warp may depend on
+// each other).  A warp none of whose groups progressed sleeps before the next trip, with
+// an exponentially growing pause: rows far behind the frontier then stop competing for L2
+// with the polls that matter.  Every wait is bounded (status block, LCD_ERR_TIMEOUT).
+//
+// Hand-off.  Two forms: (a) X pre-filled with the reserved NaN pattern, consumers poll
+// the operand elements themselves (one L2 round trip per hop; costs one extra write pass
+// over X); (b) a per-row flag array: producers store their elements, then one lane
+// releases the row's flag; consumers poll the flag, fence, and read (two round trips per
+// hop, no pass over X).
+#include "common.cuh"
+
+namespace lcd {
+
+constexpr int kOrdThreads = 256;
+constexpr int kOrdWarps = kOrdThreads / 32;
+constexpr int kStage = 4;          // entries of a row tried per trip
+constexpr int kCounterStride = 64;  // ints between two ticket counters
+static int g_ordered_pause_ns = 256;  // longest pause between two polls of a waiting warp
+
+struct __align__(16) TaskMeta {
+    int row;  // matrix row, -1: nothing to do (an error was raised)
+    int lo;   // first off-diagonal entry
+    int cnt;  // number of off-diagonal entries
+    int d;    // position of the diagonal, -1: implicit unit diagonal
+};
+
+struct OrderedParams {
+    CsrSolveParams m;
+    const TaskMeta *__restrict__ meta;
+    int *row_flags;  // form (b): n ints, zero on entry; NULL: form (a)
+    int n_tasks;
+    unsigned max_pause_ns;
+    int *counters;   // kOrdWarps ticket counters, kCounterStride ints apart, zero on entry
+};
+
+int set_ordered_pause(int ns) {
+    if (ns < 0 || ns > 100000) return LCD_ERR_INVALID_ARGUMENT;
+    g_ordered_pause_ns = ns;
+    return LCD_OK;
+}
+
+__global__ void __launch_bounds__(256)
+ordered_meta_kernel(const CsrSolveParams p, const int *__restrict__ order, int n_tasks, TaskMeta *meta) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_tasks) return;
+    TaskMeta mt{-1, 0, 0, -1};
+    const int node = __ldg(order + t);
+    if ((unsigned)node >= (unsigned)p.n) {
+        raise_error(p.status, LCD_ERR_INDEX_RANGE, t);
+    } else {
+        const int r = (p.flags & LCD_SOLVE_UPPER) ? p.n - 1 - node : node;
+        int lo = 0, hi = 0, d = -1;
+        if (!csr_row_range(p, r, lo, hi, d))
+            raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
+                                                               : LCD_ERR_BAD_POINTERS, r);
+        else
+            mt = TaskMeta{r, lo, hi - lo, d};
+    }
+    meta[t] = mt;
+}
+
+// SYS: block-row partition across GPUs - operands may arrive from a peer (system-scope polls)
+// and a published value is also stored into the x arrays of the ranks that need it.
+template <int W, int KR, bool FLAGS, bool SYS = false>
+__global__ void __launch_bounds__(kOrdThreads) csr_ordered_kernel(const OrderedParams q) {
+    const CsrSolveParams &p = q.m;
+    constexpr int G = 32 / W;
+    constexpr unsigned kFull = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int g = lane / W, gl = lane % W;
+    const unsigned gmask = W == 32 ? kFull : (((1u << W) - 1u) << (g * W));
+    const bool upper = p.flags & LCD_SOLVE_UPPER;
+    const TaskMeta none{-1, 0, 0, -1};
+
+    // Tickets.  A draw hands out one batch of G tasks.  One counter for the whole grid would be
+    // the bottleneck (atomics on one address serialise: a million per millisecond), and a
+    // ticket that covers several consecutive batches would queue rows of one level behind each
+    // other in one warp.  So the batches are dealt round-robin to kOrdWarps streams with a
+    // counter each (256 bytes apart), and warp w of every block serves stream w: batch
+    // 8 q + w for the q-th draw.  Every running block serves every stream, so the earliest
+    // unfinished batch always belongs to a warp that is running or will draw it next.
+    int *counter = q.counters + (threadIdx.x >> 5) * kCounterStride;
+    const int stream = threadIdx.x >> 5;
+    int tk_pending = 0;
+    if (lane == 0) tk_pending = atomicAdd(counter, 1);
+    auto draw = [&]() {
+        // (the draw for the batch after this one is issued now and read at the next call)
+        const int ticket = __shfl_sync(kFull, tk_pending, 0);
+        if (lane == 0) tk_pending = atomicAdd(counter, 1);
+        const long long first = ((long long)ticket * kOrdWarps + stream) * G;
+        return first < q.n_tasks ? (int)first : q.n_tasks;
+    };
+    auto load_meta = [&](int t0) {
+        const int t = t0 + g;
+        return t < q.n_tasks ? __ldg(reinterpret_cast<const int4 *>(q.meta + t)) : make_int4(-1, 0, 0, -1);
+    };
+    // stage 2 registers: entries, diagonal and right-hand side of the group's next row
+    int nx_c[kStage];
+    double nx_v[kStage], nx_d, nx_b[KR];
+    auto load_row = [&](const int4 &mt) {
+        nx_d = 1.0;
+#pragma unroll
+        for (int i = 0; i < kStage; ++i) { nx_c[i] = 0; nx_v[i] = 0.0; }
+#pragma unroll
+        for (int c = 0; c < KR; ++c) nx_b[c] = 0.0;
+        if (mt.x >= 0) {
+#pragma unroll
+            for (int i = 0; i < kStage; ++i) {
+                if (i < mt.z) { nx_c[i] = __ldg(p.Ai + mt.y + i); nx_v[i] = __ldg(p.Ax + mt.y + i); }
+            }
+            if (mt.w >= 0) nx_d = __ldg(p.Ax + mt.w);
+#pragma unroll
+            for (int c = 0; c < KR; ++c) {
+                const int col = gl + W * c;
+                if (col < p.nrhs) nx_b[c] = __ldg(p.b + (long long)mt.x * p.ld + col);
+            }
+        }
+    };
+
+    // prologue: fill the pipeline
+    int tA = draw(), tB = draw(), tC = draw();
+    int4 mA = load_meta(tA), mB = load_meta(tB);
+    (void)none;
+    load_row(mA);
+
+    while (tA < q.n_tasks) {
+        // ---- rotate: the prefetched row becomes the current one ----
+        const int r = mA.x, lo = mA.y, cnt = mA.z;
+        int cidx[kStage];
+        double cval[kStage], acc[KR];
+#pragma unroll
+        for (int i = 0; i < kStage; ++i) { cidx[i] = nx_c[i]; cval[i] = nx_v[i]; }
+#pragma unroll
+        for (int c = 0; c < KR; ++c) acc[c] = nx_b[c];
+        const double rinv = 1.0 / nx_d;
+        // ---- issue the next stages: records of batch C, data of batch B, a ticket ----
+        const int4 mC = load_meta(tC);
+        load_row(mB);
+
+        // ---- solve the group's row of batch A ----
+        bool done = r < 0, failed = false, chunk_loaded = true, checked = false;
+        int e = 0;
+        unsigned pause = 0;
+        Deadline dl;
+        dl.start(p.budget_ns);
+        for (;;) {
+            bool progressed = false;
+            if (!done) {
+                if (e < cnt) {
+                    const int m = min(kStage, cnt - e);
+                    if (!chunk_loaded) {
+#pragma unroll
+                        for (int i = 0; i < kStage; ++i) {
+                            if (i < m) { cidx[i] = __ldg(p.Ai + lo + e + i); cval[i] = __ldg(p.Ax + lo + e + i); }
+                        }
+                        chunk_loaded = true;
+                        checked = false;
+                    }
+                    if (!checked) {
+#pragma unroll
+                        for (int i = 0; i < kStage; ++i) {
+                            if (i < m) {
+                                const int c = cidx[i];
+                                const bool ok = (unsigned)c < (unsigned)p.n && (upper ? c > r : c < r);
+                                if (!ok) {   // not an earlier row: nothing to wait for
+                                    if (gl == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                                    failed = true;
+                                }
+                            }
+                        }
+                        checked = true;
+                    }
+                    if (failed) {
+                        e = cnt;
+                    } else {
+                        double xv[kStage][KR];
+                        bool ready = true;
+                        if (FLAGS) {
+#pragma unroll
+                            for (int i = 0; i < kStage; ++i)
+                                if (i < m) ready = ready && ld_relaxed_s32(q.row_flags + cidx[i]) != 0;
+                            ready = __all_sync(gmask, ready) != 0;
+                            if (ready) {
+                                acquire_fence();
+#pragma unroll
+                                for (int i = 0; i < kStage; ++i) {
+#pragma unroll
+                                    for (int c = 0; c < KR; ++c) {
+                                        const int col = gl + W * c;
+                                        xv[i][c] = (i < m && col < p.nrhs)
+                                                       ? __ldcg(p.x + (long long)cidx[i] * p.ld + col) : 0.0;
+                                    }
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < kStage; ++i) {
+#pragma unroll
+                                for (int c = 0; c < KR; ++c) {
+                                    const int col = gl + W * c;
+                                    xv[i][c] = 0.0;
+                                    if (i < m && col < p.nrhs) {
+                                        const double *src = p.x + (long long)cidx[i] * p.ld + col;
+                                        xv[i][c] = SYS ? ld_relaxed_sys_f64(src) : ld_relaxed_f64(src);
+                                        ready = ready && !is_pending(xv[i][c]);
+                                    }
+                                }
+                            }
+                            ready = __all_sync(gmask, ready) != 0;
+                        }
+                        if (ready) {
+#pragma unroll
+                            for (int i = 0; i < kStage; ++i) {
+                                if (i < m) {
+#pragma unroll
+                                    for (int c = 0; c < KR; ++c) acc[c] = fma(-cval[i], xv[i][c], acc[c]);
+                                }
+                            }
+                            e += m;
+                            chunk_loaded = false;
+                            progressed = true;
+                        } else {
+                            const bool give_up = dl.tick(p.status, r);
+                            if (__any_sync(gmask, give_up)) { failed = true; e = cnt; }
+                        }
+                    }
+                }
+                if (e >= cnt) {
+                    // publish in the trip that consumed the last operand
+                    const double nanv = __longlong_as_double(kCanonicalNaN);
+#pragma unroll
+                    for (int c = 0; c < KR; ++c) {
+                        const int col = gl + W * c;
+                        if (col < p.nrhs) {
+                            const double v = failed ? nanv : acc[c] * rinv;
+                            if (FLAGS) __stcg(p.x + (long long)r * p.ld + col, v);
+                            else st_relaxed_f64(p.x + (long long)r * p.ld + col, publishable(v));
+                            if (SYS && p.need_mask) {   // rows of other GPUs wait for it in their own memory
+                                unsigned mk = p.need_mask[r];
+                                while (mk) {
+                                    const int peer = __ffs(mk) - 1;
+                                    mk &= mk - 1;
+                                    st_relaxed_sys_f64(p.peers[peer] + (long long)r * p.ld + col, publishable(v));
+                                }
+                            }
+                        }
+                    }
+                    if (FLAGS) {
+                        __syncwarp(gmask);   // the group's stores are ordered before the release
+                        if (gl == 0) st_release_s32(q.row_flags + r, 1);
+                    }
+                    done = true;
+                    progressed = true;
+                }
+            }
+            if (__all_sync(kFull, done)) break;
+            if (__any_sync(kFull, progressed)) {
+                pause = 0;
+            } else {
+                pause = pause ? min(pause * 2, q.max_pause_ns) : 32u;
+                if (q.max_pause_ns) __nanosleep(pause);
+            }
+        }
+        mA = mB;
+        mB = mC;
+        tA = tB;
+        tB = tC;
+        tC = draw();
+    }
+}
+
+template <int W, int KR, bool FLAGS, bool SYS = false>
+static int launch_ordered_t(const OrderedParams &q, long long window_rows, cudaStream_t st) {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int v = 0;
+        LCD_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, csr_ordered_kernel<W, KR, FLAGS, SYS>,
+                                                                  kOrdThreads, 0));
+        if (v < 1) return LCD_ERR_CUDA;
+        per_sm = v;
+    }
+    constexpr int rows_per_block = kOrdWarps * (32 / W);
+    long long grid = (long long)per_sm * sm_count();
+    const long long useful = ((long long)q.n_tasks + rows_per_block - 1) / rows_per_block;
+    if (grid > useful) grid = useful;
+    if (window_rows > 0) {
+        const long long want = (window_rows + rows_per_block - 1) / rows_per_block;
+        if (grid > want) grid = want;
+    }
+    if (grid < 1) grid = 1;
+    csr_ordered_kernel<W, KR, FLAGS, SYS><<<(unsigned)grid, kOrdThreads, 0, st>>>(q);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+template <int W, int KR>
+static int launch_ordered(const OrderedParams &q, long long window_rows, cudaStream_t st) {
+    return q.row_flags ? launch_ordered_t<W, KR, true>(q, window_rows, st)
+                       : launch_ordered_t<W, KR, false>(q, window_rows, st);
+}
+
+}  // namespace lcd
+
+using namespace lcd;
+
+extern "C" int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *Ap,
+                                      const int32_t *Ai, const double *Ax, const int32_t *diag_pos,
+                                      const double *B, double *X, int64_t ld, int flags,
+                                      const int32_t *order, int32_t *task_records, int records_ready,
+                                      int32_t *row_flags, int64_t window_rows, int32_t *status_dev,
+                                      int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || nrhs < 1 || nrhs > 64 || ld < nrhs || !status_dev || window_rows < 0)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (flags & LCD_SOLVE_EXACT) return LCD_ERR_INVALID_ARGUMENT;  // operands are taken as they arrive
+    if ((flags & LCD_SOLVE_OF_FULL) && !diag_pos) return LCD_ERR_INVALID_ARGUMENT;
+    if ((flags & LCD_SOLVE_UNIT_DIAG) && !(flags & LCD_SOLVE_OF_FULL)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !B || !X || X == B || !task_records || (nnz > 0 && (!Ai || !Ax))))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && !records_ready && !order) return LCD_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)task_records & 15) != 0) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0) {
+        if (row_flags) LCD_CUDA_TRY(cudaMemsetAsync(row_flags, 0, (size_t)n * sizeof(int32_t), st));
+        else LCD_CUDA_TRY(cudaMemsetAsync(X, 0xFF, (size_t)n * (size_t)ld * sizeof(double), st));
+        OrderedParams q;
+        q.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, diag_pos, B, X, flags, nrhs, ld, status_dev,
+                             timeout_ns(timeout_ms), nullptr, 0, n, nullptr, {nullptr}};
+        q.meta = reinterpret_cast<const TaskMeta *>(task_records);
+        q.row_flags = row_flags;
+        q.n_tasks = n;
+        q.max_pause_ns = (unsigned)g_ordered_pause_ns;
+        q.counters = task_records + 4 * (size_t)n;
+        LCD_CUDA_TRY(cudaMemsetAsync(q.counters, 0, kOrdWarps * kCounterStride * sizeof(int32_t), st));
+        if (!records_ready) {
+            ordered_meta_kernel<<<(n + 255) / 256, 256, 0, st>>>(
+                q.m, order, n, reinterpret_cast<TaskMeta *>(task_records));
+            LCD_CUDA_TRY(cudaGetLastError());
+        }
+        if (nrhs == 1) rc = launch_ordered<1, 1>(q, window_rows, st);
+        else if (nrhs <= 2) rc = launch_ordered<2, 1>(q, window_rows, st);
+        else if (nrhs <= 4) rc = launch_ordered<4, 1>(q, window_rows, st);
+        else if (nrhs <= 8) rc = launch_ordered<8, 1>(q, window_rows, st);
+        else if (nrhs <= 16) rc = launch_ordered<8, 2>(q, window_rows, st);
+        else if (nrhs <= 32) rc = launch_ordered<16, 2>(q, window_rows, st);
+        else rc = launch_ordered<32, 2>(q, window_rows, st);
+        if (rc) return rc;
+    }
+    return finish(status_dev, st, status_host);
+}
+
+// Block-row partition of one solve across the GPUs of a node, rows in level order: this rank
+// solves the nodes listed in `order_local` (its block of rows, in the order of the global level
+// sets) and publishes what other ranks need into their x arrays (plain peer stores).
+extern "C" int lcd_sptrsv_csr_ordered_part(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                           const double *Ax, const double *b, double *x, int flags,
+                                           const int32_t *order_local, int32_t n_local,
+                                           int32_t *task_records, int records_ready,
+                                           const unsigned char *need_mask, double *const *peer_x,
+                                           int32_t n_ranks, int64_t window_rows, int32_t *status_dev,
+                                           int32_t timeout_ms, void *stream, int *status_host) {
+    if (n < 0 || nnz < 0 || n_local < 0 || n_local > n || !status_dev || window_rows < 0 || n_ranks < 1 ||
+        n_ranks > 8)
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (flags & ~LCD_SOLVE_UPPER) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !Ai || !Ax || !b || !x || x == b || !task_records)) return LCD_ERR_INVALID_ARGUMENT;
+    if (n_local > 0 && !records_ready && !order_local) return LCD_ERR_INVALID_ARGUMENT;
+    if (need_mask && !peer_x) return LCD_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)task_records & 15) != 0) return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n_local > 0) {
+        // x is NOT filled here: every rank fills its x with the reserved pattern and all ranks
+        // synchronise on the host before the first rank is allowed to publish
+        OrderedParams q;
+        q.m = CsrSolveParams{n, nnz, Ap, Ai, Ax, nullptr, b, x, flags, 1, 1, status_dev,
+                             timeout_ns(timeout_ms), nullptr, 0, n, need_mask, {nullptr}};
+        for (int k = 0; k < n_ranks && peer_x; ++k) q.m.peers[k] = peer_x[k];
+        q.meta = reinterpret_cast<const TaskMeta *>(task_records);
+        q.row_flags = nullptr;
+        q.n_tasks = n_local;
+        q.max_pause_ns = (unsigned)g_ordered_pause_ns;
+        q.counters = task_records + 4 * (size_t)n_local;
+        LCD_CUDA_TRY(cudaMemsetAsync(q.counters, 0, kOrdWarps * kCounterStride * sizeof(int32_t), st));
+        if (!records_ready) {
+            ordered_meta_kernel<<<(n_local + 255) / 256, 256, 0, st>>>(
+                q.m, order_local, n_local, reinterpret_cast<TaskMeta *>(task_records));
+            LCD_CUDA_TRY(cudaGetLastError());
+        }
+        rc = launch_ordered_t<1, 1, false, true>(q, window_rows, st);
+        if (rc) return rc;
+    }
+    return finish(status_dev, st, status_host);
+}

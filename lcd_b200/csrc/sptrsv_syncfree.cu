@@ -583,6 +583,8 @@ extern "C" int lcd_set_tuning(int key, int value) {
         case LCD_TUNE_ROW_VARIANT: g_row_tuning.variant = value; break;
         case LCD_TUNE_STAGE_PERCENT: g_row_tuning.stage_percent = value; break;
         case LCD_TUNE_CHAIN_CLUSTER: return set_chain_cluster_limit(value);
+        case LCD_TUNE_ORDERED_PAUSE_NS: return set_ordered_pause(value);
+        case LCD_TUNE_SMALL_THREADS: return set_small_threads(value);
         default: return LCD_ERR_INVALID_ARGUMENT;
     }
     return LCD_OK;

@@ -222,7 +222,7 @@ def parallel(**kwargs):
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
             return SchedulePlan(schedule=schedule, execution_data=data, features=features,
-                                rows=dag.n, levels=dag.n_levels)
+                                rows=dag.n, levels=dag.n_levels, dag=dag)
 
         def plan_for(values, structure):
             from . import ops
@@ -272,7 +272,7 @@ def parallel(**kwargs):
                 lowering=lowering, argument_values=launch_values,
                 execution_data=_fresh_counters(plan.execution_data),
                 function_globals=function.__globals__, cuda_module=module.namespace["cuda"])
-            prepared.hints = {"rows": plan.rows, "levels": plan.levels,
+            prepared.hints = {"rows": plan.rows, "levels": plan.levels, "dag": plan.dag,
                               "arch": getattr(scheduler, "_arch_constants", None),
                               "cache": launch_caches.setdefault(id(plan), {})}
             return lowering, module, prepared

@@ -30,7 +30,8 @@ import numpy as np
 from . import ops
 from .cuda_lowering import CUDALoweringError, PUSH_DEPENDENCE
 from .cuda_runtime import as_tensor
-from .scheduler import chain_solver_preferred
+from .scheduler import (chain_solver_preferred, ordered_solver_preferred,
+                        small_solver_preferred)
 
 # Launch policy of the wavefront entry point: the cooperative single-launch walk
 # unless the level count is small enough for per-level launches to be cheaper.
@@ -92,6 +93,33 @@ def bind(lowering):
             return nodes, ptr_dev, ptr_host, tasks
         return nodes, ptr_dev, ptr_host
 
+    def small_plan_for(op_name, Ap, Ai, hints):
+        """The one-block solver's plan for this pattern (kept with the schedule plan), or None
+        when the matrix is not small, has rows it does not serve, or is better off elsewhere."""
+        dag, cache = hints.get("dag"), hints.setdefault("cache", {})
+        if dag is None or "small_plan" in cache:
+            return cache.get("small_plan")
+        plan = None
+        n, nnz = Ap.numel() - 1, Ai.numel()
+        if ops.SmallPlan.serves(n, nnz) and small_solver_preferred(n, nnz, dag.n_levels):
+            try:
+                plan = ops.SmallPlan(op_name, Ap, Ai, dag)
+            except ops.NativeError as error:
+                if error.code != ops.nat.ERR_TOO_LARGE:
+                    raise
+        cache["small_plan"] = plan
+        return plan
+
+    def ordered_plan_for(Ap, Ai, hints):
+        dag, cache = hints.get("dag"), hints.setdefault("cache", {})
+        if dag is None or "ordered_plan" in cache:
+            return cache.get("ordered_plan")
+        plan = None
+        if ordered_solver_preferred(Ap.numel() - 1, dag.n_levels, average_row(Ap, Ai)):
+            plan = ops.OrderedPlan(dag.wavefronts, dag.n_levels)
+        cache["ordered_plan"] = plan
+        return plan
+
     def chain_solve(Ap, Ai, Ax, b, x, cache):
         # the block tiles depend on the values (the structure is fixed per plan): they are
         # rebuilt unless the value array has the contents they were built from (position-keyed
@@ -137,16 +165,29 @@ def bind(lowering):
 
     def csr_solve(Ap, Ai, Ax, b, x, v, hints):
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
+        op_name = "csr_upper" if lowering.upper else "csr_lower"
         if lowering.execution_mode == "sync_free":
             if chain_solver_preferred(hints.get("rows", 0), hints.get("levels", 0),
                                       hints.get("arch")):
                 chain_solve(Ap, Ai, Ax, b, x, hints.setdefault("cache", {}))
+                return
+            small = small_plan_for(op_name, Ap, Ai, hints)
+            if small is not None:
+                ops.sptrsv_small(small, Ax, b, x)
+                return
+            ordered = ordered_plan_for(Ap, Ai, hints) if lanes == 1 else None
+            if ordered is not None:
+                ops.sptrsv_csr_ordered(Ap, Ai, Ax, b, ordered, x, upper=lowering.upper)
             else:
                 ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper, lanes=lanes)
         else:
             nodes, ptr_dev, ptr_host, tasks = wavefront_arrays(v, serves_tasks=True)
+            small = small_plan_for(op_name, Ap, Ai, hints) if tasks is None else None
+            if small is not None:          # the same level walk, inside one thread block
+                ops.sptrsv_small(small, Ax, b, x)
+                return
             mode = "per_level" if len(ptr_host) - 1 <= PER_LEVEL_MAX_LEVELS else "cooperative"
-            ops.sptrsv_wavefront("csr_upper" if lowering.upper else "csr_lower", Ap, Ai, Ax, b,
+            ops.sptrsv_wavefront(op_name, Ap, Ai, Ax, b,
                                  nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes, task_ptr=tasks)
 
     def sptrsv_csr(*args, _hints=None):
@@ -195,12 +236,20 @@ def bind(lowering):
         for _ in range(host_trip_count(v)):
             csr_solve(layout.Ap, layout.Ai, values, b, x, v, hints)
 
-    def sptrsv_csc(*args):
+    def sptrsv_csc(*args, _hints=None):
         v = split(args)
+        hints = _hints or {}
         Ap, Ai, Ax = matrix(v)
         b = as_tensor(v[roles["rhs"]], torch.float64)
         x = as_tensor(v[roles["out"]], torch.float64)
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))
+        band_chains = "task_ptr" in v and len(v["task_ptr"]) - 1 != len(v["task_nodes"])
+        small = None if band_chains else small_plan_for(
+            "csc_upper" if lowering.upper else "csc_lower", Ap, Ai, hints)
+        if small is not None:
+            # push into shared-memory accumulators, level by level inside one thread block
+            ops.sptrsv_small(small, Ax, b, x)
+            return
         if lowering.execution_mode == "sync_free":
             if lowering.dependence_protocol == PUSH_DEPENDENCE:
                 # push protocol: the counters already hold edge multiplicities
@@ -253,7 +302,7 @@ def bind(lowering):
     if launcher is None:
         raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
     launcher.__name__ = lowering.launcher_name
-    launcher.accepts_hints = launcher in (sptrsv_csr, gauss_seidel, ilu0_csc)
+    launcher.accepts_hints = launcher in (sptrsv_csr, sptrsv_csc, gauss_seidel, ilu0_csc)
 
     def kernel(*args, **kwargs):
         raise CUDALoweringError(

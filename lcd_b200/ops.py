@@ -18,7 +18,8 @@ from ._native import NativeError, check, ptr
 
 OPS = {"csr_lower": nat.OP_CSR_LOWER, "csc_lower": nat.OP_CSC_LOWER,
        "ilu0_csr": nat.OP_ILU0_CSR, "csr_upper": nat.OP_CSR_UPPER,
-       "csc_upper": nat.OP_CSC_UPPER, "csr_lower_rows": nat.OP_CSR_LOWER_ROWS}
+       "csc_upper": nat.OP_CSC_UPPER, "csr_lower_rows": nat.OP_CSR_LOWER_ROWS,
+       "csr_upper_rows": nat.OP_CSR_UPPER_ROWS}
 
 
 def _op_code(op):
@@ -290,6 +291,138 @@ def sptrsv_wavefront_multi(Ap, Ai, Ax, B, wavefronts, wavefront_ptr, X=None, *, 
     return X
 
 
+class OrderedPlan:
+    """Per-task records of an ordered solve (structure only): reusable while the pattern, the
+    flags and the order stay.  ``levels`` (when known) sizes the window of rows in flight."""
+
+    def __init__(self, order, levels=0):
+        _require(order, torch.int32, "order")
+        self.order = order
+        self.levels = int(levels)
+        self.records = torch.empty(order.numel() * 4 + 512, dtype=torch.int32, device=order.device)
+        self.key = None          # (Ap, diag_pos, flags) the records were built for
+
+    def window(self, nrhs):
+        n = self.order.numel()
+        if self.levels <= 0:
+            return 0
+        # about four average levels, never fewer rows than keep every SM busy
+        lanes = 1 if nrhs == 1 else (2 if nrhs <= 2 else 4 if nrhs <= 4 else 8 if nrhs <= 16
+                                     else 16 if nrhs <= 32 else 32)
+        floor = 148 * 8 * (32 // lanes)
+        return max(4 * n // self.levels, floor)
+
+
+def sptrsv_csr_ordered(Ap, Ai, Ax, B, order, X=None, *, upper=False, unit_diag=False,
+                       diag_pos=None, row_flags=None, use_flags=False, window_rows=None,
+                       status=None, timeout_ms=0, sync=True):
+    """Sync-free CSR solve with rows handed out in ``order``: node ids in a topological order
+    (``dag_build(...).wavefronts``), or an ``OrderedPlan`` around it that keeps the per-task
+    records between calls.  ``B``: a vector of n doubles or a row-major ``n x nrhs`` block
+    (nrhs <= 64).  ``use_flags``: per-row ready flags instead of the NaN pre-fill of X;
+    ``row_flags`` is the scratch for them (n int32)."""
+    _require(B, torch.float64, "B")
+    plan = order if isinstance(order, OrderedPlan) else OrderedPlan(order)
+    n = Ap.numel() - 1
+    if B.dim() == 1:
+        nrhs = 1
+        if B.numel() != n:
+            raise ValueError("B must hold n doubles")
+    elif B.dim() == 2 and B.shape[0] == n:
+        nrhs = B.shape[1]
+    else:
+        raise ValueError("B must be a vector of n doubles or a row-major n x nrhs tensor")
+    if plan.order.numel() != n:
+        raise ValueError("order must list every node once")
+    X = torch.empty_like(B) if X is None else X
+    status = new_status(B.device) if status is None else status
+    use_flags = use_flags or row_flags is not None
+    if use_flags and row_flags is None:
+        row_flags = torch.empty(max(n, 1), dtype=torch.int32, device=B.device)
+    flags = _solve_flags(upper, unit_diag, diag_pos is not None, False)
+    key = (Ap.data_ptr(), diag_pos.data_ptr() if diag_pos is not None else 0, flags, n)
+    ready = plan.key == key
+    window = plan.window(nrhs) if window_rows is None else int(window_rows)
+    host = ctypes.c_int(0)
+    rc = nat.load().lcd_sptrsv_csr_ordered(
+        n, Ai.numel(), nrhs, ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(B), ptr(X), nrhs, flags,
+        ptr(plan.order), ptr(plan.records), 1 if ready else 0, ptr(row_flags) if use_flags else None,
+        window, ptr(status), int(timeout_ms), _stream(), ctypes.byref(host) if sync else None)
+    plan.key = None
+    check(rc, "lcd_sptrsv_csr_ordered")
+    plan.key = key
+    return X
+
+
+class SmallPlan:
+    """Level-ordered ELL image of a small triangular matrix (structure only, built on the
+    device) and the per-solve scratch of the one-block solver."""
+
+    def __init__(self, op, Ap, Ai, dag, *, diag_pos=None, unit_diag=False):
+        op = _op_code(op)
+        _require(Ap, torch.int32, "Ap")
+        _require(Ai, torch.int32, "Ai")
+        lib = nat.load()
+        dev = Ap.device
+        n = Ap.numel() - 1
+        self.op, self.n = op, n
+        self.csc = op in (nat.OP_CSC_LOWER, nat.OP_CSC_UPPER)
+        flags = _solve_flags(False, unit_diag, diag_pos is not None, False)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.wavefront_ptr = dag.wavefront_ptr
+        self.n_levels = dag.n_levels
+        pos = torch.empty(max(n, 1), **i32)
+        info_dev = torch.zeros(4, **i32)
+        status = new_status(dev)
+        info = (ctypes.c_int32 * 4)()
+        check(lib.lcd_small_plan_measure(op, flags, n, Ai.numel(), ptr(Ap), ptr(diag_pos),
+                                         ptr(dag.wavefronts), ptr(dag.wavefront_ptr), dag.n_levels,
+                                         ptr(pos), ptr(info_dev), ptr(status), _stream(),
+                                         ctypes.byref(info)), "lcd_small_plan_measure")
+        longest, self.max_width = int(info[0]), int(info[1])
+        if longest > lib.lcd_small_max_entries():
+            raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
+                              f"a row holds {longest} off-diagonal entries; the one-block solver "
+                              f"serves up to {lib.lcd_small_max_entries()}")
+        self.entries = 2 if longest <= 2 else (4 if longest <= 4 else 8)
+        m = max(n, 1)
+        self.ell_pc = torch.empty(self.entries * m, **i32)
+        self.ell_src = torch.empty(self.entries * m, **i32)
+        self.row_of = torch.empty(m, **i32)
+        self.diag_src = torch.empty(m, **i32)
+        far = ctypes.c_int32(0)
+        check(lib.lcd_small_plan_fill(op, flags, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(diag_pos),
+                                      ptr(dag.wavefronts), ptr(pos), self.entries, ptr(self.ell_pc),
+                                      ptr(self.ell_src), ptr(self.row_of), ptr(self.diag_src),
+                                      ptr(info_dev), ptr(status), _stream(), ctypes.byref(far)),
+              "lcd_small_plan_fill")
+        self.far = int(far.value)
+        need = ctypes.c_int64(0)
+        check(lib.lcd_small_scratch_bytes(n, self.entries, ctypes.byref(need)), "lcd_small_scratch_bytes")
+        self.scratch = torch.empty(need.value, dtype=torch.uint8, device=dev)
+
+    @staticmethod
+    def serves(n, nnz):
+        """Cheap size test before a plan is attempted."""
+        return 0 < n <= SMALL_MAX_ROWS and nnz - n <= nat.load().lcd_small_max_entries() * n
+
+
+SMALL_MAX_ROWS = 1 << 18
+
+
+def sptrsv_small(plan, Ax, b, x=None):
+    """One-block level walk of a ``SmallPlan`` (asynchronous on the current stream)."""
+    _require(Ax, torch.float64, "Ax")
+    _require(b, torch.float64, "b")
+    x = torch.empty_like(b) if x is None else x
+    check(nat.load().lcd_sptrsv_small(1 if plan.csc else 0, plan.n, plan.entries, ptr(Ax), ptr(b),
+                                      ptr(x), ptr(plan.ell_pc), ptr(plan.ell_src), ptr(plan.row_of),
+                                      ptr(plan.diag_src), ptr(plan.wavefront_ptr), plan.n_levels,
+                                      plan.max_width, 1 if plan.far else 0, ptr(plan.scratch),
+                                      plan.scratch.numel(), _stream()), "lcd_sptrsv_small")
+    return x
+
+
 def transpose(src, rows, cols, out=None):
     """out[c, r] = src[r, c] for a row-major rows x cols block."""
     out = torch.empty(cols, rows, dtype=torch.float64, device=src.device) if out is None else out
@@ -361,7 +494,9 @@ def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr
 
 def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
                wavefront_ptr_host=None, done=None, lanes=0, status=None, timeout_ms=0, sync=True):
-    """In-place ILU(0) of a sorted CSR matrix; returns Ax."""
+    """In-place ILU(0) of a sorted CSR matrix; returns Ax.  ``mode``: "sync_free" (rows by
+    index), "ordered" (sync-free, rows in the order of ``wavefronts``) or "wavefront" (a launch
+    per level)."""
     _require(Ax, torch.float64, "Ax")
     _require(diag_pos, torch.int32, "diag_pos")
     n = Ap.numel() - 1
@@ -371,6 +506,14 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
         done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
         rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 0,
                                        ptr(done), None, None, 0, int(lanes), ptr(status),
+                                       int(timeout_ms), _stream(),
+                                       ctypes.byref(host) if sync else None)
+    elif mode == "ordered":
+        # sync-free, rows handed out in the order of the level sets
+        _require(wavefronts, torch.int32, "wavefronts")
+        done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 2,
+                                       ptr(done), ptr(wavefronts), None, 0, int(lanes), ptr(status),
                                        int(timeout_ms), _stream(),
                                        ctypes.byref(host) if sync else None)
     else:

@@ -140,6 +140,7 @@ class SchedulePlan:
     features: WorkloadFeatures | None = None
     rows: int = 0
     levels: int = 0
+    dag: object = None      # device arrays of the inspector (level sets for the launchers)
 
 
 def normalize_execution_mode(execution_mode):
@@ -301,6 +302,30 @@ def chain_solver_preferred(rows, levels, arch=None):
         return False
     polling_s = levels * arch.handoff_s + rows * arch.syncfree_row_s
     return rows * arch.chain_row_s < polling_s
+
+
+# Measured on B200: a level costs the one-block solver about 0.2 us (block barrier, operands in
+# shared memory) and one SM streams its packed arrays at about 60 GB/s; a hand-off through L2
+# (polling kernels, grid barriers) costs about 1 us per level whatever the kernel.
+SMALL_LEVEL_S = 0.2e-6
+SMALL_STREAM_BYTES_PER_S = 60e9
+L2_HANDOFF_S = 1.0e-6
+ORDERED_MIN_AVERAGE_WIDTH = 64
+
+
+def small_solver_preferred(rows, entries, levels):
+    """True when one thread block walking the levels is expected to beat the kernels that hand
+    values over through L2: few rows, many levels."""
+    if rows <= 0 or levels <= 0:
+        return False
+    small_s = levels * SMALL_LEVEL_S + (12.0 * entries + 32.0 * rows) / SMALL_STREAM_BYTES_PER_S
+    return small_s < levels * L2_HANDOFF_S + 10e-6
+
+
+def ordered_solver_preferred(rows, levels, average_row):
+    """True when the level-ordered sync-free kernel (one lane per row, rows of a level side by
+    side) is expected to beat the index-ordered one: wide levels, short rows."""
+    return levels > 0 and rows / levels >= ORDERED_MIN_AVERAGE_WIDTH and average_row <= 24
 
 
 def _schedule_rank(schedule):

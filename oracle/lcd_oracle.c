@@ -29,7 +29,8 @@
 #include <string.h>
 
 enum { ORC_CSR_LOWER = 0, ORC_CSC_LOWER = 1, ORC_ILU0_CSR = 2,
-       ORC_CSR_UPPER = 3, ORC_CSC_UPPER = 4, ORC_CSR_LOWER_ROWS = 5 };
+       ORC_CSR_UPPER = 3, ORC_CSC_UPPER = 4, ORC_CSR_LOWER_ROWS = 5,
+       ORC_CSR_UPPER_ROWS = 6 };
 
 /* ---- edge enumeration ------------------------------------------------- */
 /* Calls emit(src,dst) for every edge instance of the operator's rule, in the
@@ -67,6 +68,14 @@ static void enumerate_edges(int kind, int32_t n, const int32_t *ptr,
                 if (idx[j] >= i) break;
                 emit(e, idx[j], i);
             }
+        } else if (kind == ORC_CSR_UPPER_ROWS) {
+            /* full rows visited last to first (the reversed-index loop over the U part of a
+             * factor kept in place): an entry right of the diagonal is a flow dependence.  No
+             * loop nest of the reference states this rule; it is "ORC_CSR_UPPER on the upper
+             * triangle of the matrix" and is checked against exactly that. */
+            int32_t i = n - 1 - v;
+            for (int32_t j = ptr[i]; j < ptr[i + 1]; ++j)
+                if (idx[j] > i) emit(e, n - 1 - idx[j], v);
         } else if (kind == ORC_CSR_UPPER) {
             int32_t i = n - 1 - v;          /* row, diagonal first */
             for (int32_t j = ptr[i] + 1; j < ptr[i + 1]; ++j)

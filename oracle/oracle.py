@@ -18,9 +18,10 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liblcd_oracle.so")
 
-CSR_LOWER, CSC_LOWER, ILU0_CSR, CSR_UPPER, CSC_UPPER, CSR_LOWER_ROWS = range(6)
+CSR_LOWER, CSC_LOWER, ILU0_CSR, CSR_UPPER, CSC_UPPER, CSR_LOWER_ROWS, CSR_UPPER_ROWS = range(7)
 KINDS = {"csr_lower": CSR_LOWER, "csc_lower": CSC_LOWER, "ilu0_csr": ILU0_CSR,
-         "csr_upper": CSR_UPPER, "csc_upper": CSC_UPPER, "csr_lower_rows": CSR_LOWER_ROWS}
+         "csr_upper": CSR_UPPER, "csc_upper": CSC_UPPER, "csr_lower_rows": CSR_LOWER_ROWS,
+         "csr_upper_rows": CSR_UPPER_ROWS}
 
 
 def build(force=False):

@@ -1,0 +1,277 @@
+"""Parity of the level-ordered sync-free kernels (through the C ABI) with the CPU oracle:
+triangular solves with one and many right-hand sides in both hand-off forms, ILU0 with rows
+handed out in level order (bit-identical to the sequential loop), the solves on ILU0 factors
+kept in place, and the DAG rule for the U part of a full matrix."""
+import numpy as np
+import pytest
+import scipy.sparse as sp
+
+from conftest import golden, golden_names
+
+pytestmark = pytest.mark.gpu
+
+RESIDUAL_TOL = 1e-12     # relative residual ||Lx - b|| / ||b||, fp64
+
+
+def dev(a, dtype, device):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=dtype)).to(device)
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+def csr_residual(Ap, Ai, Ax, x, b):
+    n = len(Ap) - 1
+    A = sp.csr_matrix((Ax, Ai, Ap), shape=(n, n))
+    return float(np.linalg.norm(A @ x - b) / np.linalg.norm(b))
+
+
+def test_upper_rows_dag_rule(cuda, oracle):
+    """Edge rule "entries right of the diagonal of a full row" = the upper-triangular rule on
+    the upper triangle of the same matrix (all arrays element-wise)."""
+    from lcd_b200 import generators as gen, ops
+    mat, _ = gen.laplacian3d_ilu0(9, seed=3)
+    rng = np.random.default_rng(5)
+    R = sp.random(700, 700, 0.01, random_state=rng, format="csr") + sp.identity(700, format="csr")
+    R.sort_indices()
+    for A in (mat, R):
+        A = sp.csr_matrix(A)
+        A.sort_indices()
+        Ap, Ai = A.indptr.astype(np.int32), A.indices.astype(np.int32)
+        d = ops.dag_build("csr_upper_rows", dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda))
+        ref = oracle.dag_build("csr_upper_rows", Ap, Ai)
+        U = sp.triu(A, 0, format="csr")
+        U.sort_indices()
+        tri = oracle.dag_build("csr_upper", U.indptr.astype(np.int32), U.indices.astype(np.int32))
+        for name in ("dep_count", "dag_ptr", "dag_index", "level", "wavefronts", "wavefront_ptr"):
+            np.testing.assert_array_equal(host(getattr(d, name)), getattr(ref, name))
+            np.testing.assert_array_equal(getattr(ref, name), getattr(tri, name))
+
+
+@pytest.mark.parametrize("use_flags", [False, True])
+@pytest.mark.parametrize("nrhs", [1, 2, 3, 8, 13, 16, 31, 32, 33, 64])
+def test_ordered_solve_lower_grid(cuda, oracle, nrhs, use_flags):
+    from lcd_b200 import generators as gen, ops
+    tri = gen.laplacian3d_tril(19, seed=1, nrhs=nrhs)
+    Ap, Ai, Ax = tri.csr_arrays()
+    B = np.ascontiguousarray(tri.b).reshape(tri.n, nrhs)
+    dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+    dag = ops.dag_build("csr_lower", dAp, dAi)
+    X = host(ops.sptrsv_csr_ordered(dAp, dAi, dev(Ax, np.float64, cuda), dev(B, np.float64, cuda),
+                                    dag.wavefronts, use_flags=use_flags))
+    for q in range(nrhs):
+        want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, np.ascontiguousarray(B[:, q]))
+        np.testing.assert_allclose(X[:, q], want, rtol=1e-10, atol=1e-12)
+        assert csr_residual(Ap, Ai, Ax, X[:, q], B[:, q]) <= RESIDUAL_TOL
+
+
+@pytest.mark.parametrize("use_flags", [False, True])
+def test_ordered_solve_vector_forms_and_orders(cuda, oracle, use_flags):
+    """A plain vector (nrhs = 1, one-dimensional tensors); rows longer than one staged chunk;
+    narrow levels (rows of one batch depend on each other); index order as the order; upper."""
+    import torch
+    from lcd_b200 import generators as gen, ops
+    lower = gen.random_band_lower(6000, seed=4, mean_degree=11.0, band=50)
+    for tri, upper in ((lower, False), (gen.upper_from_lower(lower), True)):
+        Ap, Ai, Ax = tri.csr_arrays()
+        b = np.random.default_rng(9).uniform(-1, 1, tri.n)
+        dAp, dAi, dAx, db = (dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda),
+                             dev(Ax, np.float64, cuda), dev(b, np.float64, cuda))
+        dag = ops.dag_build("csr_upper" if upper else "csr_lower", dAp, dAi)
+        want = (oracle.sptrsv_csr_upper if upper else oracle.sptrsv_csr_lower)(Ap, Ai, Ax, b)
+        by_index = torch.arange(tri.n, dtype=torch.int32, device=cuda)
+        for order in (dag.wavefronts, by_index, ops.OrderedPlan(dag.wavefronts, dag.n_levels)):
+            x = host(ops.sptrsv_csr_ordered(dAp, dAi, dAx, db, order, upper=upper, use_flags=use_flags))
+            if isinstance(order, ops.OrderedPlan):        # second call reuses the task records
+                x = host(ops.sptrsv_csr_ordered(dAp, dAi, dAx, db, order, upper=upper,
+                                                use_flags=use_flags, window_rows=64))
+            assert x.shape == (tri.n,)
+            np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+            assert csr_residual(Ap, Ai, Ax, x, b) <= RESIDUAL_TOL
+
+
+def test_ordered_solve_config1_matrix_and_empty(cuda, oracle):
+    import torch
+    from lcd_b200 import generators as gen, ops
+    tri = gen.laplacian2d_tril(256, seed=0)              # the 65,536-row grid of the first configuration
+    Ap, Ai, Ax = tri.csr_arrays()
+    dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+    dag = ops.dag_build("csr_lower", dAp, dAi)
+    x = host(ops.sptrsv_csr_ordered(dAp, dAi, dev(Ax, np.float64, cuda), dev(tri.b, np.float64, cuda),
+                                    dag.wavefronts))
+    assert csr_residual(Ap, Ai, Ax, x, tri.b) <= RESIDUAL_TOL
+    np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b), rtol=1e-10, atol=1e-12)
+    # n = 0
+    e32 = torch.zeros(1, dtype=torch.int32, device=cuda)
+    empty = ops.sptrsv_csr_ordered(e32, torch.zeros(0, dtype=torch.int32, device=cuda),
+                                   torch.zeros(0, dtype=torch.float64, device=cuda),
+                                   torch.zeros(0, dtype=torch.float64, device=cuda),
+                                   torch.zeros(0, dtype=torch.int32, device=cuda))
+    assert empty.numel() == 0
+
+
+def test_ordered_solve_reports_bad_orders_without_hanging(cuda):
+    """An order that lacks a node, an entry on the wrong side of the diagonal and a node id
+    outside the matrix: the bounded waits / the checks report, the context stays usable."""
+    import torch
+    from lcd_b200 import _native as nat, generators as gen, ops
+    tri = gen.laplacian2d_tril(12, seed=0)
+    Ap, Ai, Ax = tri.csr_arrays()
+    dAp, dAi, dAx, db = (dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda),
+                         dev(tri.b, np.float64, cuda))
+    order = np.arange(tri.n, dtype=np.int32)
+    order[5] = 4                                          # row 5 is never solved: row 6 waits in vain
+    with pytest.raises(nat.NativeError) as err:
+        ops.sptrsv_csr_ordered(dAp, dAi, dAx, db, dev(order, np.int32, cuda), timeout_ms=200)
+    assert err.value.code == nat.ERR_TIMEOUT
+    bad = Ai.copy()
+    bad[Ap[5]] = 7                                        # row 5 names a later row
+    with pytest.raises(nat.NativeError) as err:
+        ops.sptrsv_csr_ordered(dAp, dev(bad, np.int32, cuda), dAx, db,
+                               torch.arange(tri.n, dtype=torch.int32, device=cuda), timeout_ms=200)
+    assert err.value.code == nat.ERR_INDEX_RANGE
+    order[:] = np.arange(tri.n)
+    order[3] = tri.n + 5                                  # a node id outside the matrix
+    with pytest.raises(nat.NativeError) as err:
+        ops.sptrsv_csr_ordered(dAp, dAi, dAx, db, dev(order, np.int32, cuda), timeout_ms=200)
+    assert err.value.code == nat.ERR_INDEX_RANGE
+    x = host(ops.sptrsv_csr_ordered(dAp, dAi, dAx, db, torch.arange(tri.n, dtype=torch.int32, device=cuda)))
+    assert csr_residual(Ap, Ai, Ax, x, tri.b) <= RESIDUAL_TOL
+
+
+@pytest.mark.parametrize("name", golden_names("ilu0_"))
+def test_ilu0_ordered_is_bit_identical_to_reference(cuda, name):
+    from lcd_b200 import ops
+    g = golden(name)
+    Ap, Ai = dev(g["indptr"], np.int32, cuda), dev(g["indices"], np.int32, cuda)
+    pos = ops.diag_positions(Ap, Ai)
+    d = ops.dag_build("ilu0_csr", Ap, Ai)
+    for lanes in (1, 2, 4, 8, 16, 32):
+        out = ops.spilu0_csr(Ap, Ai, dev(g["data"], np.float64, cuda), pos, mode="ordered",
+                             wavefronts=d.wavefronts, lanes=lanes)
+        np.testing.assert_array_equal(host(out), g["factored"])
+
+
+def test_ilu0_ordered_then_ordered_solves_on_the_factors(cuda, oracle):
+    from lcd_b200 import generators as gen, ops
+    mat, b = gen.laplacian3d_ilu0(26, seed=0)
+    Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+    pos = ops.diag_positions(dAp, dAi)
+    lower = ops.dag_build("ilu0_csr", dAp, dAi)          # operands of the L solve = pivots of ILU0
+    upper = ops.dag_build("csr_upper_rows", dAp, dAi)
+    fac = ops.spilu0_csr(dAp, dAi, dev(Ax, np.float64, cuda), pos, mode="ordered",
+                         wavefronts=lower.wavefronts)
+    want = oracle.ilu0_csr(Ap, Ai, Ax, fast=True)
+    np.testing.assert_array_equal(host(fac), want)
+    hp = host(pos)
+    for nrhs in (1, 6):
+        B = np.random.default_rng(nrhs).uniform(-1, 1, (len(b), nrhs))
+        dB = dev(B if nrhs > 1 else B[:, 0], np.float64, cuda)
+        Y = ops.sptrsv_csr_ordered(dAp, dAi, fac, dB, lower.wavefronts, diag_pos=pos, unit_diag=True)
+        X = host(ops.sptrsv_csr_ordered(dAp, dAi, fac, Y, upper.wavefronts, diag_pos=pos, upper=True))
+        X = X.reshape(len(b), nrhs)
+        for q in range(nrhs):
+            y_ref = oracle.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, np.ascontiguousarray(B[:, q]))
+            x_ref = oracle.sptrsv_upper_of_full(Ap, Ai, want, hp, y_ref)
+            np.testing.assert_allclose(X[:, q], x_ref, rtol=1e-10, atol=1e-12)
+
+
+def test_ilu0_reports_corrupted_pointers(cuda):
+    """A pivot row whose pointers are not monotone is reported, not searched."""
+    from lcd_b200 import _native as nat, generators as gen, ops
+    mat, _ = gen.laplacian3d_ilu0(6, seed=0)
+    Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    pos = ops.diag_positions(dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda))
+    bad = Ap.copy()
+    bad[41] = len(Ai) + 1000                              # row 40 ends / row 41 starts past the arrays
+    for mode in ("sync_free", "ordered"):
+        d = ops.dag_build("ilu0_csr", dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda))
+        with pytest.raises(nat.NativeError) as err:
+            ops.spilu0_csr(dev(bad, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda),
+                           pos, mode=mode, wavefronts=d.wavefronts, timeout_ms=300)
+        assert err.value.code in (nat.ERR_BAD_POINTERS, nat.ERR_INDEX_RANGE)
+
+
+# ------------------------------------------------------------- one-block solver ----
+def _small_case(kind, cuda):
+    from lcd_b200 import generators as gen
+    if kind == "lap2d":
+        return gen.laplacian2d_tril(40, seed=2)
+    if kind == "lap3d":
+        return gen.laplacian3d_tril(13, seed=2)
+    if kind == "band":              # narrow levels, rows of up to 8 entries, operands far back
+        return gen.random_band_lower(3000, seed=6, mean_degree=3.0, band=9)
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("kind", ["lap2d", "lap3d", "band"])
+@pytest.mark.parametrize("op", ["csr_lower", "csr_upper", "csc_lower", "csc_upper"])
+def test_small_solver_all_forms(cuda, oracle, kind, op):
+    from lcd_b200 import _native as nat, generators as gen, ops
+    tri = _small_case(kind, cuda)
+    upper = op.endswith("upper")
+    if upper:
+        tri = gen.upper_from_lower(tri)
+    b = np.random.default_rng(11).uniform(-1, 1, tri.n)
+    Ap, Ai, Ax = tri.csc_arrays() if op.startswith("csc") else tri.csr_arrays()
+    dAp, dAi, dAx, db = (dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda),
+                         dev(b, np.float64, cuda))
+    dag = ops.dag_build(op, dAp, dAi)
+    try:
+        plan = ops.SmallPlan(op, dAp, dAi, dag)
+    except nat.NativeError as error:                    # a row longer than the solver serves
+        assert error.code == nat.ERR_TOO_LARGE and kind == "band"
+        return
+    want = getattr(oracle, "sptrsv_" + op)(Ap, Ai, Ax, b)
+    for _ in range(2):                                  # the ring and the scratch are reused
+        x = host(ops.sptrsv_small(plan, dAx, db))
+        np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    A = sp.csc_matrix((Ax, Ai, Ap), shape=(tri.n, tri.n)) if op.startswith("csc") else \
+        sp.csr_matrix((Ax, Ai, Ap), shape=(tri.n, tri.n))
+    assert float(np.linalg.norm(A @ x - b) / np.linalg.norm(b)) <= RESIDUAL_TOL
+
+
+def test_small_solver_config1_csc_and_far_operands(cuda, oracle):
+    """The 65,536-row grid of the first configuration in CSC form against SciPy and the oracle;
+    then a matrix with operands 10,000 rows back (far outside the shared-memory
+    ring) in a chain of 20,000 levels (level offsets staged in several pieces)."""
+    from scipy.sparse.linalg import spsolve_triangular
+    from lcd_b200 import generators as gen, ops
+    tri = gen.laplacian2d_tril(256, seed=0)
+    for fmt in ("csc", "csr"):
+        Ap, Ai, Ax = tri.csc_arrays() if fmt == "csc" else tri.csr_arrays()
+        dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+        dag = ops.dag_build(fmt + "_lower", dAp, dAi)
+        plan = ops.SmallPlan(fmt + "_lower", dAp, dAi, dag)
+        assert plan.entries == 2 and plan.far == 0 and plan.max_width == 256
+        x = host(ops.sptrsv_small(plan, dev(Ax, np.float64, cuda), dev(tri.b, np.float64, cuda)))
+        want = getattr(oracle, f"sptrsv_{fmt}_lower")(Ap, Ai, Ax, tri.b)
+        np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    A = sp.csr_matrix((Ax, Ai, Ap), shape=(tri.n, tri.n))
+    np.testing.assert_allclose(x, spsolve_triangular(A, tri.b, lower=True), rtol=1e-10, atol=1e-12)
+    assert float(np.linalg.norm(A @ x - tri.b) / np.linalg.norm(tri.b)) <= RESIDUAL_TOL
+    # chain with long-range operands: row i holds columns i - 10000 and i - 1 and the diagonal
+    n = 20000
+    i = np.arange(n)
+    rows = np.concatenate([i[1:], i[10000:], i])
+    cols = np.concatenate([i[1:] - 1, i[10000:] - 10000, i])
+    rng = np.random.default_rng(3)
+    vals = np.concatenate([rng.uniform(-0.3, 0.3, n - 1), rng.uniform(-0.3, 0.3, n - 10000),
+                           2.0 + rng.uniform(0, 1, n)])
+    L = sp.csr_matrix((vals, (rows, cols)), shape=(n, n))
+    L.sort_indices()
+    b = rng.uniform(-1, 1, n)
+    for fmt in ("csr", "csc"):
+        M = L if fmt == "csr" else sp.csc_matrix(L)
+        M.sort_indices()
+        Ap, Ai, Ax = M.indptr.astype(np.int32), M.indices.astype(np.int32), M.data
+        dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+        dag = ops.dag_build(fmt + "_lower", dAp, dAi)
+        plan = ops.SmallPlan(fmt + "_lower", dAp, dAi, dag)
+        assert dag.n_levels == n and plan.far > 0
+        x = host(ops.sptrsv_small(plan, dev(Ax, np.float64, cuda), dev(b, np.float64, cuda)))
+        np.testing.assert_allclose(x, getattr(oracle, f"sptrsv_{fmt}_lower")(Ap, Ai, Ax, b),
+                                   rtol=1e-10, atol=1e-12)
