@@ -12,6 +12,14 @@ SpTRSV GFLOP/s with the reference's formula (n + 2 nnz) / t
 the matrix and solves its own right-hand side (multi-RHS sharding by column,
 no data-path collective, weak scaling).
 
+The same JSON line carries, under "configs", one record per other configuration of the
+path: on one GPU the CSC demo on the 256 x 256 grid, ILU0 on the 128^3 grid with the two
+solves on its factors, the supernodal solve with 1,048,576 rows and 64 right-hand sides on
+the 192^3 grid; on N > 1 GPUs the 64 right-hand sides split by column over the ranks and
+one solve on the 256^3 grid partitioned by block rows (both strong scaling).  Each record
+holds its time, its fraction of the measured copy bandwidth, a parity figure against the
+CPU restatement and (one GPU) that restatement's time on one host core.
+
 Prints ONE JSON line (rank 0).  ``--impl reference`` times the CPU restatement of
 the reference's sequential loop on the host cores instead.
 """
@@ -43,12 +51,15 @@ WORKLOADS = {
 }
 # side workloads (other configurations of the path); they print their own JSON line
 SIDE_WORKLOADS = {
+    "csc_lap2d_g256": ("csc", 256),
     "ilu0_lap3d_g128": ("ilu0", 128),
     "ilu0_lap3d_g64": ("ilu0", 64),
     "supernodal_n1048576": ("supernodal", 1_048_576),
     "supernodal_n131072": ("supernodal", 131_072),
     "multirhs_lap3d_g192": ("multirhs", 192),
     "multirhs_lap3d_g96": ("multirhs", 96),
+    "partition_lap3d_g256": ("partition", 256),
+    "partition_lap3d_g128": ("partition", 128),
 }
 DEFAULT_WORKLOAD = "sptrsv_random_n4194304"
 
@@ -356,6 +367,15 @@ def run_native(args):
             "effective_gbs": world * achieved, "residual": residual,
         }
         line.update(extras)
+    # the other configurations of the path (all ranks take part: the multi-GPU ones hold
+    # collectives); their records travel in the same JSON line
+    configs = None
+    if not args.kernel_only and not args.skip_configs:
+        del dAp, dAi, dAx, db, x
+        torch.cuda.empty_cache()
+        configs = other_configurations(args, rank, world)
+    if rank == 0:
+        line["configs"] = configs
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -376,7 +396,11 @@ def measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier):
     other = Ax.copy()
     other[-1] = np.nextafter(other[-1], np.inf)
     values = [pinned[2], torch.from_numpy(other).pin_memory().numpy()]
-    warm = [op(pinned[0], pinned[1], values[k], pinned[3], n) for k in range(2)]   # builds and caches the plan
+    torch.cuda.synchronize()
+    t_cold = time.perf_counter()
+    warm = [op(pinned[0], pinned[1], values[0], pinned[3], n)]    # first call: inspector + plan + solve
+    cold_ms = (time.perf_counter() - t_cold) * 1e3
+    warm.append(op(pinned[0], pinned[1], values[1], pinned[3], n))
     del warm                                    # (two page-locked result buffers exist afterwards)
     steps = max(2, min(args.steps, 5))
     torch.cuda.synchronize()
@@ -403,7 +427,7 @@ def measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier):
     del copies
     return {"value": world * flops(n, nnz) / per_call / 1e9, "unit": UNIT,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(out.nbytes),
-            "ms_per_call": per_call * 1e3, "calls": steps,
+            "ms_per_call": per_call * 1e3, "calls": steps, "first_call_ms": cold_ms,
             "h2d_copy_alone_ms": h2d_ms, "h2d_gb_per_s": h2d / h2d_ms / 1e6,
             "ms_each_call": [round((b - a) * 1e3, 2) for a, b in zip(marks, marks[1:])],
             "values_change_every_call": True,
@@ -480,144 +504,365 @@ def _host_time(fn, min_seconds=2.0, min_count=2):
     return (time.perf_counter() - t0) / count, count
 
 
-def run_side_workload(args):
-    """ILU0, supernodal and multi-RHS configurations: one JSON line each with the
-    kernel time, the effective bandwidth against the measured copy peak, the parity
-    check and the CPU restatement timed on one host core."""
+def _sptrsv_csc(Ap, Ai, Ax, b, n):
+    x = np.zeros(n)
+    for i in range(n):
+        x[i] = (b[i] - x[i]) / Ax[Ap[i]]
+        for j in range(Ap[i] + 1, Ap[i + 1]):
+            x[Ai[j]] += Ax[j] * x[i]
+    return x
+
+
+def _roofline(nbytes, ms, peak, ranks=1):
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak * ranks, "unit": "GB/s",
+            "frac": achieved / (peak * ranks)}
+
+
+def _context():
+    """(rank, local_rank, world, device) of this process; the process group is initialised by the
+    caller."""
     import torch
-    import torch.distributed as dist
-    from lcd_b200 import generators as gen, ops
-    from oracle import oracle as cpu
-    kind, size = SIDE_WORKLOADS[args.workload]
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    return rank, local_rank, world, torch.device("cuda", local_rank)
+
+
+def _max_over_ranks(value, world, dev):
+    if world == 1:
+        return float(value)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- configuration 1: the sptrsv_csc demo on the 256 x 256 grid -------------------------
+def config_csc_lap2d(args, size=256):
+    """Lower triangle of the 2-D 5-point Laplacian, CSC, through the decorated operator
+    (compiler/demo/sptrsv.py:35-43 of the reference) and through the C ABI."""
+    import torch
+    from scipy.sparse.linalg import spsolve_triangular
+    import scipy.sparse as sp
+    from lcd_b200 import generators as gen, ops
+    from lcd_b200.decorator import parallel
+    from oracle import oracle as cpu
+    _, _, _, dev = _context()
+    peak, _ = measured_peak_gbs()
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    tri = gen.laplacian2d_tril(size, seed=0)
+    Cp, Ci, Cx = tri.csc_arrays()
+    n, nnz = tri.n, tri.nnz
+    dCp, dCi, dCx, db = up(Cp), up(Ci), up(Cx), up(tri.b)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dag = ops.dag_build("csc_lower", dCp, dCi)
+    plan = ops.SmallPlan("csc_lower", dCp, dCi, dag)
+    torch.cuda.synchronize()
+    inspect_ms = (time.perf_counter() - t0) * 1e3
+    x = torch.empty_like(db)
+    ms = float(np.median(_time_steps(lambda: ops.sptrsv_small(plan, dCx, db, x), 50, 10)))
+    got = x.cpu().numpy()
+    want = cpu.sptrsv_csc_lower(Cp, Ci, Cx, tri.b)
+    A = sp.csc_matrix((Cx, Ci, Cp), shape=(n, n))
+    residual = float(np.linalg.norm(A @ got - tri.b) / np.linalg.norm(tri.b))
+    t0 = time.perf_counter()
+    xs = spsolve_triangular(sp.csr_matrix(A), tri.b, lower=True)
+    scipy_ms = (time.perf_counter() - t0) * 1e3
+    # end to end: the decorated operator with page-locked host arrays
+    op = parallel(block_map="i", thread_map="j",
+                  function_props={"Ap": ["monotonically_increasing"], "Ai": [],
+                                  ("Ap", "Ai"): ["triangularity"]})(_sptrsv_csc)
+    pinned = [torch.from_numpy(a).pin_memory().numpy() for a in (Cp, Ci, Cx, tri.b)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out = op(pinned[0], pinned[1], pinned[2], pinned[3], n)
+    cold_ms = (time.perf_counter() - t0) * 1e3
+    for _ in range(3):
+        out = op(pinned[0], pinned[1], pinned[2], pinned[3], n)
+    calls = 30
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        out = op(pinned[0], pinned[1], pinned[2], pinned[3], n)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / calls
+    e2e_residual = float(np.linalg.norm(A @ out - tri.b) / np.linalg.norm(tri.b))
+    cpu_s, count = _host_time(lambda: cpu.sptrsv_csc_lower(Cp, Ci, Cx, tri.b), min_seconds=1.0)
+    nbytes = algorithmic_bytes(n, nnz)
+    return {"workload": f"sptrsv_csc_lap2d_g{size}", "format": "csc_lower", "n": n, "nnz": nnz,
+            "levels": dag.n_levels, "kernel": "sptrsv_small_kernel (one thread block)",
+            "ms": ms, "gflops": flops(n, nnz) / (ms * 1e-3) / 1e9,
+            "inspector_ms": inspect_ms, "roofline": _roofline(nbytes, ms, peak),
+            "latency_bound_note": f"{dag.n_levels} levels x one block barrier",
+            "parity": {"relative_residual": residual,
+                       "max_abs_diff_vs_oracle": float(np.max(np.abs(got - want))),
+                       "max_abs_diff_vs_scipy": float(np.max(np.abs(got - xs))),
+                       "tolerance": 1e-12, "ok": bool(residual <= 1e-12)},
+            "e2e": {"ms_per_call": e2e_ms, "first_call_ms": cold_ms, "calls": calls,
+                    "gflops": flops(n, nnz) / (e2e_ms * 1e-3) / 1e9,
+                    "h2d_bytes_per_step": int(sum(a.nbytes for a in pinned)),
+                    "d2h_bytes_per_step": int(out.nbytes), "relative_residual": e2e_residual,
+                    "api": "lcd_b200.decorator.parallel(block_map='i', thread_map='j', "
+                           "function_props=...)(sptrsv_csc)(Ap, Ai, Ax, b, n)",
+                    "schedule": str(getattr(op.current_schedule, "execution_mode", None))},
+            "cpu_baseline": {"value": flops(n, nnz) / cpu_s / 1e9, "unit": "GFLOP/s", "ms": cpu_s * 1e3,
+                             "cores": 1, "kind": "port", "sample": f"{count} full solves",
+                             "scipy_spsolve_triangular_ms": scipy_ms}}
+
+
+# ---- configuration 3: ILU0 on the 3-D grid, then the two solves on the factors ----------
+def config_ilu0(args, size=128):
+    import torch
+    from lcd_b200 import generators as gen, ops
+    from oracle import oracle as cpu
+    _, _, _, dev = _context()
+    peak, _ = measured_peak_gbs()
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    mat, b = gen.laplacian3d_ilu0(size, seed=0)
+    Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    n, nnz = len(Ap) - 1, len(Ai)
+    dAp, dAi, dA0, db = up(Ap), up(Ai), up(Ax), up(b)
+    work = dA0.clone()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pos = ops.diag_positions(dAp, dAi)
+    dag = ops.dag_build("ilu0_csr", dAp, dAi)
+    back = ops.dag_build("csr_upper_rows", dAp, dAi)
+    torch.cuda.synchronize()
+    inspect_ms = (time.perf_counter() - t0) * 1e3
+    done = torch.empty(n, dtype=torch.int32, device=dev)
+    status = ops.new_status(dev)
+    y, x = torch.empty_like(db), torch.empty_like(db)
+    steps = max(3, min(args.steps, 10))
+    copy_ms = float(np.median(_time_steps(lambda: work.copy_(dA0), steps, 2)))
+    results = {}
+    for mode in ("sync_free", "ordered", "wavefront"):
+        def step():
+            work.copy_(dA0)
+            ops.spilu0_csr(dAp, dAi, work, pos, mode=mode, wavefronts=dag.wavefronts,
+                           wavefront_ptr_host=dag.wavefront_ptr_host, done=done,
+                           status=status, sync=False)
+        ms = _time_steps(step, steps, 2)
+        results[mode] = float(np.median(ms)) - copy_ms   # the restore of A is not part of ILU0
+        if ops.read_status(status)[0] != 0:
+            raise RuntimeError(f"ILU0 ({mode}) reported an error")
+    want = cpu.ilu0_csr(Ap, Ai, Ax, fast=True)
+    identical = bool(np.array_equal(work.cpu().numpy(), want))
+    forward = ops.OrderedPlan(dag.wavefronts, dag.n_levels)
+    backward = ops.OrderedPlan(back.wavefronts, back.n_levels)
+    fwd = _time_steps(lambda: ops.sptrsv_csr_ordered(dAp, dAi, work, db, forward, y, diag_pos=pos,
+                                                     unit_diag=True, status=status, sync=False), steps, 2)
+    bwd = _time_steps(lambda: ops.sptrsv_csr_ordered(dAp, dAi, work, y, backward, x, diag_pos=pos,
+                                                     upper=True, status=status, sync=False), steps, 2)
+    hp = pos.cpu().numpy()
+    x_ref = cpu.sptrsv_upper_of_full(Ap, Ai, want, hp, cpu.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, b))
+    err = float(np.max(np.abs(x.cpu().numpy() - x_ref)) / np.max(np.abs(x_ref)))
+    cpu_s, count = _host_time(lambda: cpu.ilu0_csr(Ap, Ai, Ax, fast=True))
+    solve_s, _ = _host_time(lambda: cpu.sptrsv_upper_of_full(
+        Ap, Ai, want, hp, cpu.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, b)), min_seconds=1.0)
+    nbytes = 20 * nnz + 4 * (n + 1) + 4 * n
+    best_mode = min(results, key=results.get)
+    best = results[best_mode]
+    tri_nnz = (nnz + n) // 2
+    return {"workload": f"ilu0_lap3d_g{size}", "metric": "spilu0_ms_per_factorization", "n": n, "nnz": nnz,
+            "levels": dag.n_levels, "ms": best, "mode": best_mode, "ms_by_mode": results,
+            "gflops_2nnz": 2 * nnz / (best * 1e-3) / 1e9, "inspector_ms": inspect_ms,
+            "roofline": _roofline(nbytes, best, peak),
+            "forward_solve_ms": float(np.median(fwd)), "backward_solve_ms": float(np.median(bwd)),
+            "solve_kernel": "csr_ordered_kernel on the factors in place (unit lower / upper)",
+            "solve_roofline": _roofline(2 * algorithmic_bytes(n, tri_nnz),
+                                        float(np.median(fwd)) + float(np.median(bwd)), peak),
+            "parity": {"factor_bit_identical_to_sequential": identical,
+                       "solve_max_rel_error": err, "tolerance": 1e-10,
+                       "ok": bool(identical and err <= 1e-10)},
+            "cpu_baseline": {"value": cpu_s * 1e3, "unit": "ms", "cores": 1, "kind": "port",
+                             "sample": f"{count} full factorisations",
+                             "forward_plus_backward_ms": solve_s * 1e3}}
+
+
+# ---- configuration 4: supernodal solve ----------------------------------------------------
+def config_supernodal(args, size=1_048_576):
+    import torch
+    from lcd_b200 import generators as gen, ops, supernodal
+    from oracle import oracle as cpu
+    _, _, _, dev = _context()
+    peak, _ = measured_peak_gbs()
+    t0 = time.time()
+    s = gen.supernodal_random(size, seed=0)
+    log(f"[bench] generated supernodal n={size} in {time.time() - t0:.1f}s "
+        f"({s.Lx.nbytes / 1e9:.2f} GB of panels, {s.n_super} supernodes)")
+    t0 = time.perf_counter()
+    plan = supernodal.analyse(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.col_to_super, device=dev)
+    torch.cuda.synchronize()
+    analyse_ms = (time.perf_counter() - t0) * 1e3
+    db = torch.from_numpy(np.ascontiguousarray(s.b)).to(dev)
+    x = torch.empty_like(db)
+    steps = max(3, min(args.steps, 10))
+    ms = _time_steps(lambda: supernodal.solve(plan, db, x, sync=False), steps, 2)
+    best = float(np.median(ms))
+    code = ops.read_status(plan.status)[0]
+    xs = x.cpu().numpy()
+    cpu_s, count = _host_time(lambda: cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b),
+                              min_seconds=3.0, min_count=1)
+    want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
+    err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
+    return {"workload": f"supernodal_n{size}", "n": size, "n_super": plan.n_super, "tasks": plan.n_tasks,
+            "panel_gb": plan.panel_values * 8 / 1e9, "ms": best,
+            "gflops": plan.flops / (best * 1e-3) / 1e9, "analyse_and_upload_ms": analyse_ms,
+            "status": code, "roofline": _roofline(plan.algorithmic_bytes, best, peak),
+            "parity": {"max_rel_error_vs_sequential": err, "tolerance": 1e-10,
+                       "ok": bool(code == 0 and err <= 1e-10)},
+            "cpu_baseline": {"value": plan.flops / cpu_s / 1e9, "unit": "GFLOP/s", "ms": cpu_s * 1e3,
+                             "cores": 1, "kind": "port", "sample": f"{count} full solves"}}
+
+
+# ---- configuration 5a: 64 right-hand sides, sharded by column over the ranks ----------------
+def config_multirhs(args, size=192, nrhs=64):
+    """Strong scaling: the 64 columns are split over the ranks (matrix replicated, no data-path
+    collective); the time is the slowest rank's, device-timed."""
+    import torch
+    from lcd_b200 import generators as gen
+    from lcd_b200.multigpu import ShardedMultiRHS
+    from oracle import oracle as cpu
+    rank, _, world, dev = _context()
+    peak, _ = measured_peak_gbs()
+    tri = gen.laplacian3d_tril(size, seed=0)
+    Ap, Ai, Ax = tri.csr_arrays()
+    n, nnz = tri.n, tri.nnz
+    solver = ShardedMultiRHS(Ap, Ai, Ax, device=dev)
+    start, stop = solver.shard(nrhs)
+    k = stop - start
+    # every rank draws the same block and keeps its columns, row-major (what the kernels read)
+    rng = np.random.default_rng([0, 7])
+    full = rng.uniform(-1.0, 1.0, (n, nrhs)) if n * nrhs <= (1 << 27) else None
+    if full is None:                      # large: draw this rank's columns only, column by column
+        cols = [np.random.default_rng([0, 7, q]).uniform(-1.0, 1.0, n) for q in range(start, stop)]
+        local = np.ascontiguousarray(np.stack(cols, axis=1))
+    else:
+        local = np.ascontiguousarray(full[:, start:stop])
+    B = torch.from_numpy(local).to(dev)
+    out = [None]
+    steps = max(3, min(args.steps, 10))
+
+    def step():
+        out[0] = solver.solve(B, layout="rows")
+    ms = _time_steps(step, steps, 3)
+    per = _max_over_ranks(np.median(ms), world, dev)
+    X = out[0].cpu().numpy()
+    checks = sorted({0, k - 1})
+    err = 0.0
+    for q in checks:
+        want = cpu.sptrsv_csr_lower(Ap, Ai, Ax, np.ascontiguousarray(local[:, q]))
+        err = max(err, float(np.max(np.abs(X[:, q] - want)) / np.max(np.abs(want))))
+    err = _max_over_ranks(err, world, dev)
+    # the column-major interface (two transpositions around the kernel), this rank's shard
+    cm = torch.from_numpy(np.ascontiguousarray(local.T)).to(dev)
+    cm_ms = _max_over_ranks(np.median(_time_steps(lambda: solver.solve(cm), 3, 1)), world, dev)
+    nbytes = world * (12 * nnz + 4 * (n + 1)) + 16 * n * nrhs
+    record = {"workload": f"multirhs_lap3d_g{size}", "n": n, "nnz": nnz, "nrhs": nrhs, "n_gpus": world,
+              "rhs_per_gpu": k, "scaling": "strong", "ms": per,
+              "gflops": nrhs * flops(n, nnz) / (per * 1e-3) / 1e9,
+              "column_major_interface_ms": cm_ms,
+              "roofline": _roofline(nbytes, per, peak, world),
+              "parity": {"max_rel_error_checked_columns": err, "columns_checked_per_rank": len(checks),
+                         "tolerance": 1e-10, "ok": bool(err <= 1e-10)}}
+    if rank == 0 and world == 1:
+        cpu_s, count = _host_time(lambda: cpu.sptrsv_csr_lower(Ap, Ai, Ax, local[:, 0].copy()), min_seconds=2.0)
+        record["cpu_baseline"] = {"value": flops(n, nnz) / cpu_s / 1e9, "unit": "GFLOP/s", "cores": 1,
+                                  "kind": "port", "ms_per_rhs": cpu_s * 1e3,
+                                  "sample": f"{count} single right-hand-side solves"}
+    return record
+
+
+# ---- configuration 5b: one solve partitioned by block rows over the ranks --------------------
+def config_partition(args, size=256):
+    """The 3-D grid matrix cut into contiguous row blocks, one per GPU; cross-block operands are
+    plain peer stores over NVLink, the final x is gathered with NCCL.  Times the whole call
+    (fill of x, two barriers, kernel, gather), slowest rank, device-timed."""
+    import torch
+    from lcd_b200 import generators as gen
+    from lcd_b200.multigpu import PartitionedSolve
+    from oracle import oracle as cpu
+    rank, _, world, dev = _context()
+    peak, _ = measured_peak_gbs()
+    tri = gen.laplacian3d_tril(size, seed=0)
+    Ap, Ai, Ax = tri.csr_arrays()
+    n, nnz = tri.n, tri.nnz
+    solver = PartitionedSolve(Ap, Ai, Ax)
+    b = torch.from_numpy(tri.b).to(dev)
+    out = [None]
+
+    def step():
+        out[0] = solver.solve(b, gather=True)
+    ms = _time_steps(step, max(3, min(args.steps, 5)), 2)
+    per = _max_over_ranks(np.median(ms), world, dev)
+
+    def local_only():
+        out[0] = solver.solve(b, gather=False)
+    local_ms = _max_over_ranks(np.median(_time_steps(local_only, 3, 1)), world, dev)
+    step()
+    x = out[0].cpu().numpy()
+    residual = cpu.relative_residual_csr(Ap, Ai, Ax, x, tri.b) if rank == 0 else 0.0
+    residual = _max_over_ranks(residual, world, dev)
+    levels = solver.levels
+    solver.close()
+    return {"workload": f"partition_lap3d_g{size}", "n": n, "nnz": nnz, "n_gpus": world, "levels": levels,
+            "scaling": "strong", "ms": per, "ms_without_gather": local_ms,
+            "gflops": flops(n, nnz) / (per * 1e-3) / 1e9,
+            "roofline": _roofline(algorithmic_bytes(n, nnz), per, peak, world),
+            "cut_planes": world - 1,
+            "parity": {"relative_residual": residual, "tolerance": 1e-12, "ok": bool(residual <= 1e-12)}}
+
+
+CONFIG_RUNNERS = {"ilu0": config_ilu0, "supernodal": config_supernodal, "multirhs": config_multirhs,
+                  "csc": config_csc_lap2d, "partition": config_partition}
+
+
+def other_configurations(args, rank, world):
+    """The configurations next to the headline one.  One GPU: the CSC demo, ILU0 with its two
+    solves, the supernodal solve and the 64 right-hand sides.  Several GPUs: the 64 right-hand
+    sides split by column and one large solve partitioned by block rows."""
+    import torch
+    if world == 1:
+        plan = [("cfg1_csc_lap2d_g256", "csc", 256), ("cfg3_ilu0_lap3d_g128", "ilu0", 128),
+                ("cfg4_supernodal_n1048576", "supernodal", 1_048_576),
+                ("cfg5a_multirhs_lap3d_g192", "multirhs", 192)]
+    else:
+        plan = [("cfg5a_multirhs_lap3d_g192", "multirhs", 192),
+                ("cfg5b_partition_lap3d_g256", "partition", 256)]
+    out = {}
+    for name, kind, size in plan:
+        t0 = time.time()
+        try:
+            out[name] = CONFIG_RUNNERS[kind](args, size)
+            out[name]["bench_seconds"] = round(time.time() - t0, 1)
+        except Exception as error:          # the headline line must still be printed
+            if world > 1:
+                raise                       # (a rank that stops alone would hang the others)
+            out[name] = {"error": f"{type(error).__name__}: {error}"}
+        torch.cuda.empty_cache()
+        if rank == 0:
+            log(f"[bench] {name}: {time.time() - t0:.1f}s")
+    return out
+
+
+def run_side_workload(args):
+    """One of the other configurations alone (smaller sizes for profiling runs): prints its
+    record as one JSON line."""
+    import torch
+    import torch.distributed as dist
+    kind, size = SIDE_WORKLOADS[args.workload]
+    rank, local_rank, world, dev = _context()
     torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     peak, peak_kind = measured_peak_gbs()
-    line = {"workload": args.workload, "n_gpus": world, "steps": args.steps, "dtype": "f64",
-            "data": "synthetic", "peak_gbs": peak, "peak_kind": peak_kind}
-    if kind == "ilu0":
-        mat, b = gen.laplacian3d_ilu0(size, seed=0)
-        Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
-        n, nnz = len(Ap) - 1, len(Ai)
-        dAp, dAi, dA0, db = up(Ap), up(Ai), up(Ax), up(b)
-        work = dA0.clone()
-        pos = ops.diag_positions(dAp, dAi)
-        dag = ops.dag_build("ilu0_csr", dAp, dAi)
-        done = torch.empty(n, dtype=torch.int32, device=dev)
-        status = ops.new_status(dev)
-        y, x = torch.empty_like(db), torch.empty_like(db)
-        results = {}
-        copy_ms = float(np.median(_time_steps(lambda: work.copy_(dA0), args.steps, 2)))
-        for mode in ("sync_free", "wavefront"):
-            def step():
-                work.copy_(dA0)
-                ops.spilu0_csr(dAp, dAi, work, pos, mode=mode, wavefronts=dag.wavefronts,
-                               wavefront_ptr_host=dag.wavefront_ptr_host, done=done,
-                               status=status, sync=False)
-            ms = _time_steps(step, args.steps, args.warmup)
-            results[mode] = float(np.median(ms)) - copy_ms   # the restore of A is not part of ILU0
-        want = cpu.ilu0_csr(Ap, Ai, Ax, fast=True)
-        line["bit_identical_to_sequential"] = bool(np.array_equal(work.cpu().numpy(), want))
-        fwd = _time_steps(lambda: ops.sptrsv_csr_syncfree(dAp, dAi, work, db, y, diag_pos=pos,
-                                                          unit_diag=True, status=status, sync=False),
-                          args.steps, args.warmup)
-        bwd = _time_steps(lambda: ops.sptrsv_csr_syncfree(dAp, dAi, work, y, x, diag_pos=pos,
-                                                          upper=True, status=status, sync=False),
-                          args.steps, args.warmup)
-        hp = pos.cpu().numpy()
-        x_ref = cpu.sptrsv_upper_of_full(Ap, Ai, want, hp,
-                                         cpu.sptrsv_unit_lower_of_full(Ap, Ai, want, hp, b))
-        err = float(np.max(np.abs(x.cpu().numpy() - x_ref)) / np.max(np.abs(x_ref)))
-        cpu_s, count = _host_time(lambda: cpu.ilu0_csr(Ap, Ai, Ax, fast=True))
-        bytes_ilu = 20 * nnz + 4 * (n + 1) + 4 * n
-        best = min(results.values())
-        line.update({"metric": "spilu0_ms_per_factorization", "unit": "ms", "higher_is_better": False,
-                     "value": best, "sync_free_ms": results["sync_free"],
-                     "wavefront_ms": results["wavefront"], "n": n, "nnz": nnz,
-                     "levels": dag.n_levels, "gflops_2nnz": 2 * nnz / (best * 1e-3) / 1e9,
-                     "forward_solve_ms": float(np.median(fwd)),
-                     "backward_solve_ms": float(np.median(bwd)), "solve_max_rel_error": err,
-                     "roofline": {"bound": "hbm", "achieved": bytes_ilu / (best * 1e-3) / 1e9,
-                                  "peak": peak, "unit": "GB/s",
-                                  "frac": bytes_ilu / (best * 1e-3) / 1e9 / peak},
-                     "cpu_baseline": {"value": cpu_s * 1e3, "unit": "ms", "cores": 1, "kind": "port",
-                                      "sample": f"{count} full factorisations"}})
-    elif kind == "supernodal":
-        from lcd_b200 import supernodal
-        t0 = time.time()
-        s = gen.supernodal_random(size, seed=0)
-        log(f"[bench] generated {args.workload} in {time.time() - t0:.1f}s "
-            f"({s.Lx.nbytes / 1e9:.2f} GB of panels, {s.n_super} supernodes)")
-        plan = supernodal.analyse(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.col_to_super, device=dev)
-        db = up(s.b)
-        x = torch.empty_like(db)
-        ms = _time_steps(lambda: supernodal.solve(plan, db, x, sync=False), args.steps, args.warmup)
-        best = float(np.median(ms))
-        code = ops.read_status(plan.status)[0]
-        xs = x.cpu().numpy()
-        check_n = min(size, 131_072)
-        if size <= 131_072:
-            want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
-            err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
-        else:
-            err = None
-        cpu_s, count = _host_time(lambda: cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b),
-                                  min_seconds=5.0, min_count=1)
-        if err is None:
-            want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
-            err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
-        nbytes = plan.algorithmic_bytes
-        line.update({"metric": "supernodal_sptrsv_gflops", "unit": "GFLOP/s", "higher_is_better": True,
-                     "value": plan.flops / (best * 1e-3) / 1e9, "ms_per_step": best,
-                     "n": size, "n_super": plan.n_super, "tasks": plan.n_tasks,
-                     "panel_gb": plan.panel_values * 8 / 1e9, "status": code,
-                     "max_rel_error_vs_sequential": err,
-                     "roofline": {"bound": "hbm", "achieved": nbytes / (best * 1e-3) / 1e9,
-                                  "peak": peak, "unit": "GB/s",
-                                  "frac": nbytes / (best * 1e-3) / 1e9 / peak},
-                     "cpu_baseline": {"value": plan.flops / cpu_s / 1e9, "unit": "GFLOP/s", "cores": 1,
-                                      "kind": "port", "sample": f"{count} full solves, {cpu_s * 1e3:.0f} ms each"}})
-    else:  # multi-RHS, sharded by column over the ranks
-        from lcd_b200.multigpu import ShardedMultiRHS
-        nrhs = 64
-        tri = gen.laplacian3d_tril(size, seed=0)
-        Ap, Ai, Ax = tri.csr_arrays()
-        n, nnz = tri.n, tri.nnz
-        solver = ShardedMultiRHS(Ap, Ai, Ax, device=dev)
-        start, stop = solver.shard(nrhs)
-        k = stop - start
-        rng = np.random.default_rng([0, 7])
-        B = torch.from_numpy(rng.uniform(-1.0, 1.0, (k, n))).to(dev)       # this rank's columns
-        out = [None]
-        def step():
-            out[0] = solver.solve(B)
-        ms = _time_steps(step, args.steps, args.warmup)
-        total_ms = float(np.sum(ms))
-        if world > 1:
-            t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            total_ms = float(t.item())
-        per = total_ms / args.steps
-        X = out[0].cpu().numpy()
-        col = 0
-        want = cpu.sptrsv_csr_lower(Ap, Ai, Ax, B[col].cpu().numpy())
-        err = float(np.max(np.abs(X[col] - want)) / np.max(np.abs(want)))
-        nbytes = world * (12 * nnz + 4 * (n + 1)) + 16 * n * nrhs
-        cpu_s, count = _host_time(lambda: cpu.sptrsv_csr_lower(Ap, Ai, Ax, want), min_seconds=2.0)
-        line.update({"metric": "multirhs_sptrsv_gflops", "unit": "GFLOP/s", "higher_is_better": True,
-                     "scaling": "strong", "value": nrhs * flops(n, nnz) / (per * 1e-3) / 1e9,
-                     "ms_per_step": per, "n": n, "nnz": nnz, "nrhs": nrhs, "rhs_per_gpu": k,
-                     "max_rel_error_col0": err,
-                     "roofline": {"bound": "hbm", "achieved": nbytes / (per * 1e-3) / 1e9,
-                                  "peak": peak * world, "unit": "GB/s",
-                                  "frac": nbytes / (per * 1e-3) / 1e9 / (peak * world)},
-                     "cpu_baseline": {"value": flops(n, nnz) / cpu_s / 1e9, "unit": "GFLOP/s", "cores": 1,
-                                      "kind": "port", "sample": f"{count} single-RHS solves"}})
+    line = {"data": "synthetic", "dtype": "f64", "steps": args.steps, "peak_gbs": peak,
+            "peak_kind": peak_kind}
+    line.update(CONFIG_RUNNERS[kind](args, size))
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -640,6 +885,8 @@ def main():
                         help="sync-free kernel: polling rows, block-recurrence chain, or by level count")
     parser.add_argument("--kernel-only", action="store_true",
                         help="time the kernel only (profiling runs): no e2e, CPU baseline, extras")
+    parser.add_argument("--skip-configs", action="store_true",
+                        help="headline configuration only: skip the records of the other configurations")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "native" else args.warmup
     if args.workload in SIDE_WORKLOADS:

@@ -172,9 +172,18 @@ int lcd_sptrsv_csr_syncfree(int32_t n, int64_t nnz, const int32_t *Ap, const int
  * dependent levels.
  *   workspace: lcd_chain_workspace_bytes(n) bytes (56 KiB per 64 rows), 16-byte aligned.
  *   flags: LCD_SOLVE_UPPER / OF_FULL / UNIT_DIAG as for lcd_sptrsv_csr_syncfree.
- * Explicit inverses are safe for diagonally dominant blocks; for other matrices prefer
- * lcd_sptrsv_csr_syncfree.
+ * Explicit inverses are safe for well-conditioned diagonal blocks only: multiplying by an
+ * inverse loses about log10(cond) digits that substitution keeps.  The preparation therefore
+ * records a growth figure - the largest |entry| of any tile times the largest |diagonal
+ * entry| of its rows, maximised over all blocks: about 1 for diagonally dominant matrices,
+ * astronomically large for blocks whose inverse grows along the substitution (inf for
+ * non-finite tiles).  lcd_chain_growth reads it back (it synchronises the stream); callers
+ * compare it with LCD_CHAIN_MAX_GROWTH and solve with lcd_sptrsv_csr_syncfree when it is
+ * larger (the decorator's launcher does).  The word lives behind the tiles in the workspace.
  */
+#define LCD_CHAIN_MAX_GROWTH 100.0
+int lcd_chain_growth(int32_t n, const void *workspace, int64_t workspace_bytes, void *stream,
+                     double *growth_host);
 int lcd_chain_workspace_bytes(int32_t n, int64_t *bytes);
 /* Diagnostic: blocks per thread-block cluster of the last lcd_sptrsv_csr_chain launch of this
  * process (8 where the device hosts such clusters, else 1; 0 before the first launch). */
@@ -442,10 +451,15 @@ int lcd_sptrsv_supernodal(int32_t n, int32_t n_super, int32_t n_tasks,
  * inv[inv_ptr[s] ..); inv_ptr[s] = sum of w_t^2 over t < s (n_super + 1 entries, device).
  * With them the solve multiplies by the inverse - independent loads and multiply-adds -
  * instead of substituting through w dependent steps; with inv_ptr == NULL it substitutes.
+ * growth_dev (optional, one double in device memory): receives the largest value over all
+ * supernodes of (largest |entry| of the inverse) x (largest |diagonal entry| of the block);
+ * about 1 for diagonally dominant blocks.  Multiplying by an explicit inverse loses about
+ * log10 of that figure in digits, which substitution keeps: above LCD_CHAIN_MAX_GROWTH solve
+ * with inv_ptr == NULL instead (lcd_b200.supernodal.analyse does).
  */
 int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
                            const int64_t *Lp, const double *Lx, const int64_t *inv_ptr,
-                           double *inv, void *stream);
+                           double *inv, double *growth_dev, void *stream);
 
 /* ---- block-row partition of one solve across the GPUs of a node ---------------- */
 /*

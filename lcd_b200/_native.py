@@ -21,6 +21,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
 WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
+CHAIN_MAX_GROWTH = 100.0        # LCD_CHAIN_MAX_GROWTH
 (TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT,
  TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS) = range(8)
 
@@ -57,6 +58,7 @@ _SIGNATURES = {
                               _P, c_int64, _P, _P, ctypes.POINTER(c_int)]),
     "lcd_gs_values": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P]),
     "lcd_chain_workspace_bytes": (c_int, [c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_chain_growth": (c_int, [c_int32, _P, c_int64, _P, ctypes.POINTER(c_double)]),
     "lcd_chain_cluster_size": (c_int, []),
     "lcd_chain_prepare": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, c_int64, _P]),
     "lcd_sptrsv_csr_chain": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, _P, c_int64,
@@ -101,7 +103,7 @@ _SIGNATURES = {
     "lcd_supernodal_strip_rows": (c_int, []),
     "lcd_sptrsv_supernodal": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
                                       _P, _P, _P, _P, _P, _P, c_int32, _P, ctypes.POINTER(c_int)]),
-    "lcd_supernodal_prepare": (c_int, [c_int32, _P, _P, _P, _P, _P, _P, _P]),
+    "lcd_supernodal_prepare": (c_int, [c_int32, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lcd_peer_alloc": (c_int, [c_int64, ctypes.POINTER(c_void_p), ctypes.c_char_p]),
     "lcd_peer_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_void_p)]),
     "lcd_peer_close": (c_int, [_P]),

@@ -166,6 +166,24 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int pair_b
         __syncwarp();
     }
     __syncthreads();
+    // Growth of the explicit inverses: (largest entry of any tile) x (largest diagonal entry of
+    // the half), about 1 for diagonally dominant blocks and huge for blocks whose inverse
+    // grows along the substitution (then multiplying by it loses digits that substitution
+    // keeps).  The maximum over all blocks goes to the word behind the tiles; NaN counts as inf.
+    double *growth_word = ws + (long long)((p.n + 63) / 64) * kPairDoubles;
+    double tile_max = 0.0;
+    auto absmax = [](double m, double v) {
+        v = fabs(v);
+        return (v != v) ? (double)INFINITY : (v > m ? v : m);
+    };
+    for (int k = 0; k < 32; ++k) tile_max = absmax(tile_max, T[swz(k, lane)]);
+    // (diag holds the reciprocal of the row's diagonal entry)
+    double diag_max = absmax(0.0, 1.0 / diag);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        tile_max = absmax(tile_max, __shfl_xor_sync(kFullMask, tile_max, off));
+        diag_max = absmax(diag_max, __shfl_xor_sync(kFullMask, diag_max, off));
+    }
     // Output layouts.  Inverse tiles (M11, M21, M22): element (r, k) at k * 32 + r, so that lane
     // r of a warp applying them loads its row coalesced.  T tiles: elements (r, 2q), (r, 2q + 1)
     // side by side at (q * 32 + r) * 2, so that lane r of a main warp reads its row from shared
@@ -198,6 +216,13 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int pair_b
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[j] = fma(-v, X[swz(k, c0 + j)], acc[j]);
         }
+        double prod_max = 0.0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) prod_max = absmax(prod_max, acc[j]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            prod_max = absmax(prod_max, __shfl_xor_sync(kFullMask, prod_max, off));
+        tile_max = absmax(tile_max, prod_max);
         if (prod == 0) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) out[kTileDoubles + (c0 + j) * 32 + lane] = acc[j];
@@ -206,6 +231,12 @@ chain_prepare_kernel(const CsrSolveParams p, double *__restrict__ ws, int pair_b
 #pragma unroll
             for (int j = 0; j < 16; j += 2) o[((c0 + j) / 2) * 32 + lane] = make_double2(acc[j], acc[j + 1]);
         }
+    }
+    if (lane == 0) {
+        // non-negative doubles order like their bit patterns (inf above every finite value)
+        const double growth = tile_max * diag_max;
+        atomicMax(reinterpret_cast<unsigned long long *>(growth_word),
+                  (unsigned long long)__double_as_longlong(growth != growth ? (double)INFINITY : growth));
     }
 }
 
@@ -1294,9 +1325,25 @@ extern "C" int lcd_chain_prepare_rows(int32_t n, int64_t nnz, const int32_t *Ap,
     // the attribute belongs to the current device's copy of the function
     LCD_CUDA_TRY(cudaFuncSetAttribute(chain_prepare_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kPrepSmemBytes));
+    if (row_begin == 0)   // the growth word behind the tiles restarts with the first range
+        LCD_CUDA_TRY(cudaMemsetAsync(static_cast<double *>(workspace) + ((int64_t)n + 63) / 64 * kPairDoubles,
+                                     0, sizeof(double), (cudaStream_t)stream));
     chain_prepare_kernel<<<pair_end - pair_begin, kPrepThreads, kPrepSmemBytes, (cudaStream_t)stream>>>(
         p, static_cast<double *>(workspace), pair_begin, pair_end);
     LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
+extern "C" int lcd_chain_growth(int32_t n, const void *workspace, int64_t workspace_bytes, void *stream,
+                                double *growth_host) {
+    if (n < 0 || !workspace || !growth_host) return LCD_ERR_INVALID_ARGUMENT;
+    int64_t need = 0;
+    lcd_chain_workspace_bytes(n, &need);
+    if (workspace_bytes < need) return LCD_ERR_WORKSPACE;
+    LCD_CUDA_TRY(cudaMemcpyAsync(growth_host,
+                                 static_cast<const double *>(workspace) + ((int64_t)n + 63) / 64 * kPairDoubles,
+                                 sizeof(double), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    LCD_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
     return LCD_OK;
 }
 

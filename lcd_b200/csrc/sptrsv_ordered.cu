@@ -19,10 +19,15 @@
 // No pointer chasing on the dependence chain.  A first pass turns (order, Ap, diag_pos)
 // into one 16-byte record per task {row, first entry, entry count, diagonal position}
 // (structure only: reusable while the pattern and the order stay).  The solve kernel is a
-// three-stage software pipeline per warp: while batch k is solved, the records of batch
-// k + 2 and the entries, diagonal and right-hand side of batch k + 1 are already in
-// flight; each stage's addresses come from loads issued a whole batch earlier.  What
-// remains on the chain of a row is: poll its operands, multiply-add, publish.
+// software pipeline per warp, staged in shared memory by asynchronous copies (cp.async,
+// one commit group per batch): while batch k is solved, the records of batch k + 2 and
+// the entries, diagonal and right-hand side of batch k + 1 are in flight, each stage's
+// addresses coming from copies that landed a batch earlier.  Staging in shared memory
+// instead of registers keeps the kernel at 64 registers, i.e. 32 warps per SM:
+// the solve is bound by memory latency, so resident warps are what fills HBM.  A warp holds
+// no more than these three batches: a task queued behind others in one warp waits for them,
+// which costs hand-offs when levels are narrow.  What remains on the chain of a row is:
+// poll its operands, multiply-add, publish.
 //
 // Waiting.  All groups of a warp make one non-blocking attempt per trip and the trip ends
 // in a warp-wide vote, so no lane spins inside a branch (rows of one warp may depend on
@@ -87,10 +92,49 @@ ordered_meta_kernel(const CsrSolveParams p, const int *__restrict__ order, int n
     meta[t] = mt;
 }
 
+// ---- asynchronous copies into shared memory (cp.async, completion by commit groups) ----
+__device__ __forceinline__ unsigned smem_address(const void *p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void cp_async_4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_address(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_address(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_address(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kMetaRing = 4;  // batches whose records are kept in shared memory
+constexpr int kDataRing = 2;  // batches whose entries / right-hand sides are kept there
+constexpr int kTicketDraws = 1;  // places of its stream a warp takes per draw (more = deeper queue per warp)
+
+struct __align__(16) RowData {   // 64 bytes
+    int col[kStage];
+    double val[kStage];
+    double diag;
+    double pad;
+};
+
+template <int W, int KR>
+struct WarpStage {
+    static constexpr int G = 32 / W;
+    int4 meta[kMetaRing][G];
+    RowData row[kDataRing][G];
+    double rhs[kDataRing][KR][32];
+};
+
 // SYS: block-row partition across GPUs - operands may arrive from a peer (system-scope polls)
 // and a published value is also stored into the x arrays of the ranks that need it.
 template <int W, int KR, bool FLAGS, bool SYS = false>
-__global__ void __launch_bounds__(kOrdThreads) csr_ordered_kernel(const OrderedParams q) {
+__global__ void __launch_bounds__(kOrdThreads, 4) csr_ordered_kernel(const OrderedParams q) {
+    extern __shared__ __align__(16) unsigned char ordered_smem[];
     const CsrSolveParams &p = q.m;
     constexpr int G = 32 / W;
     constexpr unsigned kFull = 0xffffffffu;
@@ -98,74 +142,96 @@ __global__ void __launch_bounds__(kOrdThreads) csr_ordered_kernel(const OrderedP
     const int g = lane / W, gl = lane % W;
     const unsigned gmask = W == 32 ? kFull : (((1u << W) - 1u) << (g * W));
     const bool upper = p.flags & LCD_SOLVE_UPPER;
-    const TaskMeta none{-1, 0, 0, -1};
+    WarpStage<W, KR> &stage = reinterpret_cast<WarpStage<W, KR> *>(ordered_smem)[threadIdx.x >> 5];
 
-    // Tickets.  A draw hands out one batch of G tasks.  One counter for the whole grid would be
-    // the bottleneck (atomics on one address serialise: a million per millisecond), and a
-    // ticket that covers several consecutive batches would queue rows of one level behind each
-    // other in one warp.  So the batches are dealt round-robin to kOrdWarps streams with a
-    // counter each (256 bytes apart), and warp w of every block serves stream w: batch
-    // 8 q + w for the q-th draw.  Every running block serves every stream, so the earliest
-    // unfinished batch always belongs to a warp that is running or will draw it next.
+    // Tickets.  One counter for the whole grid would be the bottleneck (atomics on one
+    // address serialise), and a ticket that covers consecutive batches would queue rows of one
+    // level behind each other in one warp.  So the batches (G tasks each) are dealt round-robin
+    // to kOrdWarps streams with a counter each (256 bytes apart), warp w of every block serves
+    // stream w, and a draw takes kTicketDraws places of the stream: batches 8 (q + j) + w.
+    // Every running block serves every stream, so the earliest unfinished batch always belongs
+    // to a warp that is running or will draw it next.
     int *counter = q.counters + (threadIdx.x >> 5) * kCounterStride;
     const int stream = threadIdx.x >> 5;
-    int tk_pending = 0;
-    if (lane == 0) tk_pending = atomicAdd(counter, 1);
+    int tk_base = 0, tk_pos = kTicketDraws, tk_pending = 0;
+    if (lane == 0) tk_pending = atomicAdd(counter, kTicketDraws);
     auto draw = [&]() {
-        // (the draw for the batch after this one is issued now and read at the next call)
-        const int ticket = __shfl_sync(kFull, tk_pending, 0);
-        if (lane == 0) tk_pending = atomicAdd(counter, 1);
-        const long long first = ((long long)ticket * kOrdWarps + stream) * G;
+        if (tk_pos == kTicketDraws) {
+            // (the following draw is issued now and read kTicketDraws batches later)
+            tk_base = __shfl_sync(kFull, tk_pending, 0);
+            if (lane == 0) tk_pending = atomicAdd(counter, kTicketDraws);
+            tk_pos = 0;
+        }
+        const long long first = ((long long)(tk_base + tk_pos++) * kOrdWarps + stream) * G;
         return first < q.n_tasks ? (int)first : q.n_tasks;
     };
-    auto load_meta = [&](int t0) {
-        const int t = t0 + g;
-        return t < q.n_tasks ? __ldg(reinterpret_cast<const int4 *>(q.meta + t)) : make_int4(-1, 0, 0, -1);
+    // stage 1: the records of batch `seq` (first task t0) on their way to shared memory
+    auto fetch_meta = [&](int seq, int t0) {
+        if (gl == 0) {
+            int4 *dst = &stage.meta[seq & (kMetaRing - 1)][g];
+            if (t0 + g < q.n_tasks) cp_async_16(dst, q.meta + t0 + g);
+            else *dst = make_int4(-1, 0, 0, -1);
+        }
     };
-    // stage 2 registers: entries, diagonal and right-hand side of the group's next row
-    int nx_c[kStage];
-    double nx_v[kStage], nx_d, nx_b[KR];
-    auto load_row = [&](const int4 &mt) {
-        nx_d = 1.0;
-#pragma unroll
-        for (int i = 0; i < kStage; ++i) { nx_c[i] = 0; nx_v[i] = 0.0; }
-#pragma unroll
-        for (int c = 0; c < KR; ++c) nx_b[c] = 0.0;
+    // stage 2: entries, diagonal and right-hand side of batch `seq`, whose records have arrived
+    auto fetch_data = [&](int seq) {
+        const int4 mt = stage.meta[seq & (kMetaRing - 1)][g];
+        RowData &rd = stage.row[seq & (kDataRing - 1)][g];
         if (mt.x >= 0) {
-#pragma unroll
-            for (int i = 0; i < kStage; ++i) {
-                if (i < mt.z) { nx_c[i] = __ldg(p.Ai + mt.y + i); nx_v[i] = __ldg(p.Ax + mt.y + i); }
+            for (int k = gl; k < kStage; k += W) {
+                if (k < mt.z) {
+                    cp_async_4(&rd.col[k], p.Ai + mt.y + k);
+                    cp_async_8(&rd.val[k], p.Ax + mt.y + k);
+                }
             }
-            if (mt.w >= 0) nx_d = __ldg(p.Ax + mt.w);
+            if (gl == 0) {
+                if (mt.w >= 0) cp_async_8(&rd.diag, p.Ax + mt.w);
+                else rd.diag = 1.0;
+            }
 #pragma unroll
             for (int c = 0; c < KR; ++c) {
                 const int col = gl + W * c;
-                if (col < p.nrhs) nx_b[c] = __ldg(p.b + (long long)mt.x * p.ld + col);
+                if (col < p.nrhs)
+                    cp_async_8(&stage.rhs[seq & (kDataRing - 1)][c][lane], p.b + (long long)mt.x * p.ld + col);
             }
         }
     };
 
-    // prologue: fill the pipeline
-    int tA = draw(), tB = draw(), tC = draw();
-    int4 mA = load_meta(tA), mB = load_meta(tB);
-    (void)none;
-    load_row(mA);
+    // prologue: records of the first two batches, then the data of the first
+    int tb[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) tb[k] = draw();
+    fetch_meta(0, tb[0]);
+    fetch_meta(1, tb[1]);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    fetch_data(0);
+    cp_async_commit();
 
-    while (tA < q.n_tasks) {
-        // ---- rotate: the prefetched row becomes the current one ----
-        const int r = mA.x, lo = mA.y, cnt = mA.z;
+    for (int seq = 0; tb[0] < q.n_tasks; ++seq) {
+        // group seq - 1 = {records of batch seq + 1, data of batch seq} has landed
+        cp_async_wait<0>();
+        __syncwarp();
+        // ---- issue group seq: records of batch seq + 2, data of batch seq + 1 ----
+        fetch_meta(seq + 2, tb[2]);
+        fetch_data(seq + 1);
+        cp_async_commit();
+
+        // ---- solve the group's row of batch seq ----
+        const int4 mt = stage.meta[seq & (kMetaRing - 1)][g];
+        const RowData &rd = stage.row[seq & (kDataRing - 1)][g];
+        const int r = mt.x, lo = mt.y, cnt = mt.z;
         int cidx[kStage];
         double cval[kStage], acc[KR];
+        double rinv = 1.0;
+        if (r >= 0) {
 #pragma unroll
-        for (int i = 0; i < kStage; ++i) { cidx[i] = nx_c[i]; cval[i] = nx_v[i]; }
+            for (int i = 0; i < kStage; ++i) { cidx[i] = rd.col[i]; cval[i] = rd.val[i]; }
 #pragma unroll
-        for (int c = 0; c < KR; ++c) acc[c] = nx_b[c];
-        const double rinv = 1.0 / nx_d;
-        // ---- issue the next stages: records of batch C, data of batch B, a ticket ----
-        const int4 mC = load_meta(tC);
-        load_row(mB);
-
-        // ---- solve the group's row of batch A ----
+            for (int c = 0; c < KR; ++c) acc[c] = stage.rhs[seq & (kDataRing - 1)][c][lane];
+            rinv = 1.0 / rd.diag;
+        }
         bool done = r < 0, failed = false, chunk_loaded = true, checked = false;
         int e = 0;
         unsigned pause = 0;
@@ -289,21 +355,24 @@ __global__ void __launch_bounds__(kOrdThreads) csr_ordered_kernel(const OrderedP
                 if (q.max_pause_ns) __nanosleep(pause);
             }
         }
-        mA = mB;
-        mB = mC;
-        tA = tB;
-        tB = tC;
-        tC = draw();
+        tb[0] = tb[1];
+        tb[1] = tb[2];
+        tb[2] = draw();
     }
+    cp_async_wait<0>();   // nothing of this warp is in flight when the block leaves
 }
 
 template <int W, int KR, bool FLAGS, bool SYS = false>
 static int launch_ordered_t(const OrderedParams &q, long long window_rows, cudaStream_t st) {
     static int per_sm = 0;
+    const size_t smem = sizeof(WarpStage<W, KR>) * kOrdWarps;
     if (per_sm == 0) {
+        if (smem > 48 * 1024)
+            LCD_CUDA_TRY(cudaFuncSetAttribute(csr_ordered_kernel<W, KR, FLAGS, SYS>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         int v = 0;
         LCD_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, csr_ordered_kernel<W, KR, FLAGS, SYS>,
-                                                                  kOrdThreads, 0));
+                                                                  kOrdThreads, smem));
         if (v < 1) return LCD_ERR_CUDA;
         per_sm = v;
     }
@@ -316,7 +385,7 @@ static int launch_ordered_t(const OrderedParams &q, long long window_rows, cudaS
         if (grid > want) grid = want;
     }
     if (grid < 1) grid = 1;
-    csr_ordered_kernel<W, KR, FLAGS, SYS><<<(unsigned)grid, kOrdThreads, 0, st>>>(q);
+    csr_ordered_kernel<W, KR, FLAGS, SYS><<<(unsigned)grid, kOrdThreads, smem, st>>>(q);
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }

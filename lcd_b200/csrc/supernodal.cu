@@ -263,13 +263,21 @@ __global__ void __launch_bounds__(kSnThreads, 4) supernodal_kernel(const Superno
 __global__ void __launch_bounds__(128)
 supernodal_inverse_kernel(int n_super, const int *__restrict__ sn, const int *__restrict__ Lip,
                           const long long *__restrict__ Lp, const double *__restrict__ Lx,
-                          const long long *__restrict__ inv_ptr, double *inv) {
+                          const long long *__restrict__ inv_ptr, double *inv,
+                          unsigned long long *growth) {
     const int s = blockIdx.x;
     if (s >= n_super) return;
     const int c0 = sn[s], w = sn[s + 1] - c0;
     const int len = Lip[s + 1] - Lip[s];
     const double *M = Lx + Lp[c0];
     double *out = inv + inv_ptr[s];
+    // growth of the explicit inverse: largest |entry| of the inverse times largest |diagonal
+    // entry| of the block (about 1 for diagonally dominant blocks; NaN counts as inf)
+    double inv_max = 0.0, diag_max = 0.0;
+    auto absmax = [](double m, double v) {
+        v = fabs(v);
+        return (v != v) ? (double)INFINITY : (v > m ? v : m);
+    };
     for (int c = threadIdx.x; c < w; c += blockDim.x) {
         double *col = out + (long long)c * w;
         for (int r = 0; r < c; ++r) col[r] = 0.0;
@@ -277,6 +285,21 @@ supernodal_inverse_kernel(int n_super, const int *__restrict__ sn, const int *__
             double acc = (r == c) ? 1.0 : 0.0;
             for (int k = c; k < r; ++k) acc = fma(-M[(long long)k * len + r], col[k], acc);
             col[r] = acc / M[(long long)r * len + r];
+            inv_max = absmax(inv_max, col[r]);
+        }
+        diag_max = absmax(diag_max, M[(long long)c * len + c]);
+    }
+    if (growth) {
+        __shared__ unsigned long long s_inv, s_diag;
+        if (threadIdx.x == 0) { s_inv = 0ull; s_diag = 0ull; }
+        __syncthreads();
+        // non-negative doubles order like their bit patterns
+        atomicMax(&s_inv, (unsigned long long)__double_as_longlong(inv_max));
+        atomicMax(&s_diag, (unsigned long long)__double_as_longlong(diag_max));
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const double g = __longlong_as_double((long long)s_inv) * __longlong_as_double((long long)s_diag);
+            atomicMax(growth, (unsigned long long)__double_as_longlong(g != g ? (double)INFINITY : g));
         }
     }
 }
@@ -312,13 +335,15 @@ extern "C" int lcd_supernodal_pending(int32_t n_super, const int32_t *sn, const 
 
 extern "C" int lcd_supernodal_prepare(int32_t n_super, const int32_t *sn, const int32_t *Lip,
                                       const int64_t *Lp, const double *Lx, const int64_t *inv_ptr,
-                                      double *inv, void *stream) {
+                                      double *inv, double *growth_dev, void *stream) {
     if (n_super < 0 || (n_super > 0 && (!sn || !Lip || !Lp || !Lx || !inv_ptr || !inv)))
         return LCD_ERR_INVALID_ARGUMENT;
+    if (growth_dev) LCD_CUDA_TRY(cudaMemsetAsync(growth_dev, 0, sizeof(double), (cudaStream_t)stream));
     if (n_super == 0) return LCD_OK;
     supernodal_inverse_kernel<<<n_super, 128, 0, (cudaStream_t)stream>>>(
         n_super, sn, Lip, reinterpret_cast<const long long *>(Lp), Lx,
-        reinterpret_cast<const long long *>(inv_ptr), inv);
+        reinterpret_cast<const long long *>(inv_ptr), inv,
+        reinterpret_cast<unsigned long long *>(growth_dev));
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }

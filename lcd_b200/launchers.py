@@ -133,7 +133,12 @@ def bind(lowering):
         if cache.get("chain_values") != stamp:
             ops.chain_prepare(Ap, Ai, Ax, workspace, upper=lowering.upper)
             cache["chain_values"] = stamp
-        ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
+            # explicit block inverses are only as accurate as the blocks are well conditioned
+            cache["chain_stable"] = ops.chain_growth(workspace, n) <= ops.CHAIN_MAX_GROWTH
+        if cache["chain_stable"]:
+            ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
+        else:           # substitution (still on the GPU): slower on such matrices, but stable
+            ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper)
 
     def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache):
         # The value array is still being uploaded, piece by piece (pieces: elements uploaded
@@ -162,6 +167,9 @@ def bind(lowering):
             ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, status=status, rows=(begin, end),
                                  sync=end == n)
             begin = end
+        if ops.chain_growth(workspace, n) > ops.CHAIN_MAX_GROWTH:
+            # the block inverses grew: solve again by substitution (the whole array has arrived)
+            ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper)
 
     def csr_solve(Ap, Ai, Ax, b, x, v, hints):
         lanes = _lanes_from_schedule(lowering, average_row(Ap, Ai))

@@ -31,47 +31,91 @@ def column_shard(nrhs, world, rank):
     return start, start + base + (1 if rank < extra else 0)
 
 
-# Levels at least this wide (on average) are solved level by level: every gather is a
-# coalesced row of the right-hand-side block and nothing waits inside a level.  Narrower
-# level structures are dependence chains and go to the sync-free kernel.
-WAVEFRONT_MIN_AVERAGE_WIDTH = 256
+# Levels at least this wide (on average) are solved with the level-ordered sync-free kernel:
+# rows of a level run side by side and every gather is a coalesced row of the right-hand-side
+# block.  Narrower level structures are dependence chains and go to the index-ordered kernel,
+# whose chunks hand values over through shared memory.
+ORDERED_MIN_AVERAGE_WIDTH = 256
+# Measured on B200 (192^3 grid, 64 right-hand sides on one GPU): point-to-point kernel 4.7 ms,
+# level-synchronous kernel (a grid barrier per level) 5.0 ms; with fewer right-hand sides per
+# GPU the barrier per level dominates (8 columns: 1.9 ms against 4.5 ms).  The barrier kernel
+# is kept for blocks wider than this many columns, i.e. for none at the current limit of 64.
+BARRIER_FROM_RHS = 64
 _level_sets = {}
 
 
 def _levels_for(matrix, upper):
-    """Level sets of a device matrix, built once per matrix object."""
+    """(level sets, ordered plan) of a device matrix, built once per matrix object."""
     from . import ops
     Ap, Ai, _ = matrix
     key = (Ap.data_ptr(), Ai.data_ptr(), Ap.numel(), Ai.numel(), bool(upper))
-    dag = _level_sets.get(key)
-    if dag is None:
+    entry = _level_sets.get(key)
+    if entry is None:
         if len(_level_sets) >= 8:
             _level_sets.pop(next(iter(_level_sets)))
-        dag = _level_sets[key] = ops.dag_build("csr_upper" if upper else "csr_lower", Ap, Ai)
-    return dag
+        dag = ops.dag_build("csr_upper" if upper else "csr_lower", Ap, Ai)
+        entry = _level_sets[key] = (dag, ops.OrderedPlan(dag.wavefronts, dag.n_levels))
+    return entry
 
 
-def _native_local_solve(matrix, block, upper=False):
-    """Solve for a column-major shard (k columns of length n, device tensor of shape
-    (k, n)) with a multi-RHS kernel chosen from the level width; same layout out."""
-    import torch
+def _solve_rows(matrix, rows_major, upper, out=None):
+    """Solve for a row-major n x k block (k <= 64) with the kernel the level width asks for."""
     from . import ops
     Ap, Ai, Ax = matrix
+    n = rows_major.shape[0]
+    dag, plan = _levels_for(matrix, upper)
+    if dag.n_levels > 0 and n / dag.n_levels >= ORDERED_MIN_AVERAGE_WIDTH:
+        if rows_major.shape[1] > BARRIER_FROM_RHS:
+            return ops.sptrsv_wavefront_multi(Ap, Ai, Ax, rows_major, dag.wavefronts,
+                                              dag.wavefront_ptr, out, upper=upper)
+        return ops.sptrsv_csr_ordered(Ap, Ai, Ax, rows_major, plan, out, upper=upper)
+    return ops.sptrsv_csr_syncfree_multi(Ap, Ai, Ax, rows_major, out, upper=upper)
+
+
+def _native_local_solve(matrix, block, upper=False, layout="columns"):
+    """Solve for this rank's shard on the GPU.  ``layout="columns"``: the shard is column-major
+    (k columns of length n, a device tensor of shape (k, n)) and is transposed into the
+    row-major blocks the kernels read, 64 columns at a time, and back; ``layout="rows"``: the
+    shard already is a row-major n x k block (k <= 64) and goes to the kernel as it is."""
+    import torch
+    from . import ops
+    if layout == "rows":
+        n, k = block.shape
+        if k > MAX_RHS_PER_LAUNCH:
+            raise ValueError(f"a row-major shard holds at most {MAX_RHS_PER_LAUNCH} columns")
+        return _solve_rows(matrix, block, upper)
     k, n = block.shape
     out = torch.empty_like(block)
-    dag = _levels_for(matrix, upper)
-    wide = dag.n_levels > 0 and n / dag.n_levels >= WAVEFRONT_MIN_AVERAGE_WIDTH
     for first in range(0, k, MAX_RHS_PER_LAUNCH):
         last = min(first + MAX_RHS_PER_LAUNCH, k)
         cols = last - first
         rows_major = ops.transpose(block[first:last].contiguous(), cols, n).view(n, cols)
-        if wide:
-            solved = ops.sptrsv_wavefront_multi(Ap, Ai, Ax, rows_major, dag.wavefronts,
-                                                dag.wavefront_ptr, upper=upper)
-        else:
-            solved = ops.sptrsv_csr_syncfree_multi(Ap, Ai, Ax, rows_major, upper=upper)
+        solved = _solve_rows(matrix, rows_major, upper)
         ops.transpose(solved, n, cols, out=out[first:last])
     return out
+
+
+def agree_on_status(dist, group, code, device):
+    """MAX of the ranks' status codes (0 = fine): every rank learns that some rank failed
+    before anybody raises, so no rank is left alone in a later collective."""
+    import torch
+    word = torch.tensor([int(code)], dtype=torch.int32, device=device)
+    dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group)
+    return int(word.item())
+
+
+class RemoteRankError(RuntimeError):
+    """Another rank of the process group reported an error in the step all ranks just did."""
+
+    def __init__(self, code, where):
+        self.code = int(code)
+        super().__init__(f"{where}: a rank of the process group failed with status {code}")
+
+
+def _local_status(error):
+    """Status code of an exception raised by a local solver (native codes are positive)."""
+    code = getattr(error, "code", None)
+    return int(code) if isinstance(code, int) and code > 0 else 255
 
 
 class ShardedMultiRHS:
@@ -102,11 +146,17 @@ class ShardedMultiRHS:
     def shard(self, nrhs):
         return column_shard(nrhs, self.world, self.rank)
 
-    def solve(self, B, gather=False):
+    def solve(self, B, gather=False, layout="columns", agree=None):
         """``B``: the full column-major ``n x nrhs`` block (host array, every rank
-        passes the same) or this rank's shard as a ``(k, n)`` tensor.  Returns the
-        local shard ``(k, n)``; with ``gather=True`` the full ``(nrhs, n)`` block on
-        every rank (row q = solution for right-hand side q)."""
+        passes the same) or this rank's shard as a device tensor: ``(k, n)``
+        (``layout="columns"``) or a row-major ``(n, k)`` block with k <= 64
+        (``layout="rows"``, no transposition).  Returns the local shard in the layout it
+        came in; with ``gather=True`` the full ``(nrhs, n)`` block on every rank (row q =
+        solution for right-hand side q).
+
+        ``agree`` (default: whenever a collective follows, i.e. with ``gather``): the ranks
+        exchange their status before anybody raises, so that an error on one rank raises on
+        all of them instead of leaving the others alone in the gather."""
         import torch
         if isinstance(B, np.ndarray):
             if B.ndim != 2 or B.shape[0] != self.n:
@@ -114,14 +164,31 @@ class ShardedMultiRHS:
             nrhs = B.shape[1]
             start, stop = self.shard(nrhs)
             local = torch.from_numpy(np.ascontiguousarray(B[:, start:stop].T)).to(self.device)
+            layout = "columns"
         else:
             local, nrhs = B, None
-        solved = self.local_solver(self.matrix, local, self.upper)
-        if not gather:
-            return solved
-        if nrhs is None:
+        if gather and nrhs is None:
             raise ValueError("gather=True needs the full block to know every shard size")
-        if self.world == 1:
+        agree = (gather and self.world > 1) if agree is None else (agree and self.world > 1)
+        failure, solved = None, None
+        try:
+            if layout == "columns":
+                solved = self.local_solver(self.matrix, local, self.upper)
+            else:
+                solved = self.local_solver(self.matrix, local, self.upper, layout)
+        except Exception as error:      # keep the code: the other ranks have to hear of it
+            if not agree:
+                raise
+            failure = error
+        if agree:
+            status = agree_on_status(self.dist, self.group,
+                                     _local_status(failure) if failure is not None else 0,
+                                     self.device)
+            if failure is not None:
+                raise failure
+            if status:
+                raise RemoteRankError(status, "ShardedMultiRHS.solve")
+        if not gather or self.world == 1:
             return solved
         # shards may differ by one column: pad to the widest so that every rank
         # contributes a tensor of the same shape, then drop the padding
@@ -181,14 +248,15 @@ class PartitionedSolve:
     """One triangular solve (CSR, lower or upper) split into contiguous block rows,
     one per GPU.  Cross-partition operands travel as plain 8-byte peer stores into the
     consumer's own x array; there is no collective on the data path (the optional
-    final gather uses NCCL)."""
+    final gather uses NCCL).
 
-    def __init__(self, Ap, Ai, Ax, upper=False, group=None, threads=0):
-        import ctypes
+    ``local_solver(rank, bounds, b) -> (status, block)`` replaces the GPU part (tests of the
+    partition / agreement / gather logic on CPU ranks); no device memory is touched then."""
+
+    def __init__(self, Ap, Ai, Ax, upper=False, group=None, threads=0, ordered=None,
+                 local_solver=None, device=None):
         import torch
         import torch.distributed as dist
-        from . import _native as nat
-        from .ops import _stream, new_status
         if not dist.is_initialized():
             raise RuntimeError("PartitionedSolve needs an initialised process group")
         self.dist, self.group = dist, group
@@ -196,11 +264,19 @@ class PartitionedSolve:
         if self.world > 8:
             raise ValueError("at most 8 ranks (one node)")
         self.upper, self.threads = upper, threads
+        self.n = len(Ap) - 1
+        self.bounds = row_partition(self.n, self.world)
+        self.local_solver = local_solver
+        self.buffer = self.order_local = self.records = None
+        if local_solver is not None:
+            self.device = torch.device("cpu" if device is None else device)
+            return
+        import ctypes
+        from . import _native as nat, ops
+        from .ops import _stream, new_status
         dev = torch.device("cuda", torch.cuda.current_device())
         up = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dtype=dt)).to(dev)
         self.Ap, self.Ai, self.Ax = up(Ap, np.int32), up(Ai, np.int32), up(Ax, np.float64)
-        self.n = len(Ap) - 1
-        self.bounds = row_partition(self.n, self.world)
         self.status = new_status(dev)
         self.device = dev
         lib = nat.load()
@@ -220,13 +296,24 @@ class PartitionedSolve:
         for q, handle in enumerate(handles):
             self.peer_ptrs[q] = self.buffer.ptr if q == self.rank else self.buffer.open_peer(handle)
         self.x = torch.as_tensor(self.buffer, device=dev)
+        # rows of this rank in the order of the global level sets (wide levels: rows of a level
+        # run side by side; the index-ordered kernel keeps one grid line in flight)
+        dag = ops.dag_build("csr_upper" if upper else "csr_lower", self.Ap, self.Ai)
+        self.levels = dag.n_levels
+        wide = dag.n_levels > 0 and self.n / dag.n_levels >= ORDERED_MIN_AVERAGE_WIDTH
+        if wide if ordered is None else ordered:
+            t0, t1 = int(self.bounds[self.rank]), int(self.bounds[self.rank + 1])
+            nodes = dag.wavefronts
+            self.order_local = nodes[(nodes >= t0) & (nodes < t1)].contiguous()
+            self.records = torch.empty(self.order_local.numel() * 4 + 512, dtype=torch.int32, device=dev)
+            self.records_ready = False
+            self.window = max(4 * self.n // max(dag.n_levels, 1) // self.world, 148 * 8 * 32)
+        del dag
         torch.cuda.synchronize()
         dist.barrier(group=group)
 
-    def solve(self, b, gather=True, timeout_ms=0):
-        """``b``: full right-hand side (host array or device tensor, same on every
-        rank).  Returns x: the full vector on every rank (``gather=True``) or this
-        rank's block."""
+    def _solve_on_gpu(self, b, timeout_ms):
+        """(status, this rank's block of x); the status is returned, not raised."""
         import ctypes
         import torch
         from . import _native as nat, ops
@@ -238,16 +325,45 @@ class PartitionedSolve:
         self.dist.barrier(group=self.group)       # nobody publishes into an unfilled array
         host = ctypes.c_int(0)
         t0, t1 = int(self.bounds[self.rank]), int(self.bounds[self.rank + 1])
-        rc = self._lib.lcd_sptrsv_csr_syncfree_part(
-            self.n, self.Ai.numel(), nat.ptr(self.Ap), nat.ptr(self.Ai), nat.ptr(self.Ax),
-            nat.ptr(b_dev), nat.ptr(self.x), nat.SOLVE_UPPER if self.upper else 0, t0, t1,
-            nat.ptr(self.need) if self.world > 1 else None, self.peer_ptrs, self.world,
-            int(self.threads), nat.ptr(self.status), int(timeout_ms), _stream(),
-            ctypes.byref(host))
-        nat.check(rc, "lcd_sptrsv_csr_syncfree_part")
+        flags = nat.SOLVE_UPPER if self.upper else 0
+        need = nat.ptr(self.need) if self.world > 1 else None
+        if self.order_local is not None:
+            rc = self._lib.lcd_sptrsv_csr_ordered_part(
+                self.n, self.Ai.numel(), nat.ptr(self.Ap), nat.ptr(self.Ai), nat.ptr(self.Ax),
+                nat.ptr(b_dev), nat.ptr(self.x), flags, nat.ptr(self.order_local),
+                self.order_local.numel(), nat.ptr(self.records), 1 if self.records_ready else 0,
+                need, self.peer_ptrs, self.world, int(self.window), nat.ptr(self.status),
+                int(timeout_ms), _stream(), ctypes.byref(host))
+            self.records_ready = rc == 0
+        else:
+            rc = self._lib.lcd_sptrsv_csr_syncfree_part(
+                self.n, self.Ai.numel(), nat.ptr(self.Ap), nat.ptr(self.Ai), nat.ptr(self.Ax),
+                nat.ptr(b_dev), nat.ptr(self.x), flags, t0, t1, need, self.peer_ptrs, self.world,
+                int(self.threads), nat.ptr(self.status), int(timeout_ms), _stream(),
+                ctypes.byref(host))
         lo, hi = (self.n - t1, self.n - t0) if self.upper else (t0, t1)
-        mine = self.x[lo:hi].clone()
+        return rc, self.x[lo:hi].clone()
+
+    def solve(self, b, gather=True, timeout_ms=0):
+        """``b``: full right-hand side (host array or device tensor, same on every
+        rank).  Returns x: the full vector on every rank (``gather=True``) or this
+        rank's block.
+
+        The closing barrier runs whatever the local outcome was, and the ranks agree on the
+        status before anybody raises: an error is per rank (a bad row in one block), and a
+        rank that raised early would leave the others alone in the barrier and the gather."""
+        import torch
+        if self.local_solver is not None:
+            rc, mine = self.local_solver(self.rank, self.bounds, b)
+        else:
+            rc, mine = self._solve_on_gpu(b, timeout_ms)
         self.dist.barrier(group=self.group)       # peers may still be reading / writing x
+        status = agree_on_status(self.dist, self.group, rc, self.device) if self.world > 1 else rc
+        if rc:
+            from ._native import check
+            check(rc, "PartitionedSolve.solve")
+        if status:
+            raise RemoteRankError(status, "PartitionedSolve.solve")
         if not gather or self.world == 1:
             return mine
         widest = int(np.max(np.diff(self.bounds)))
@@ -261,8 +377,11 @@ class PartitionedSolve:
         return torch.cat(blocks)
 
     def close(self):
+        if self.buffer is None:
+            return
         import torch
         torch.cuda.synchronize()
         self.dist.barrier(group=self.group)
         self.x = None
         self.buffer.release()
+        self.buffer = None

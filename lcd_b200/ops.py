@@ -205,6 +205,18 @@ def chain_prepare(Ap, Ai, Ax, workspace, *, upper=False, unit_diag=False, diag_p
     return workspace
 
 
+def chain_growth(workspace, n):
+    """Growth figure of the block inverses in ``workspace`` (synchronises the stream): compare
+    with ``CHAIN_MAX_GROWTH``; above it the chain solver loses accuracy that substitution keeps."""
+    out = ctypes.c_double(0.0)
+    check(nat.load().lcd_chain_growth(int(n), ptr(workspace), workspace.numel() * 8, _stream(),
+                                      ctypes.byref(out)), "lcd_chain_growth")
+    return float(out.value)
+
+
+CHAIN_MAX_GROWTH = nat.CHAIN_MAX_GROWTH
+
+
 def sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, unit_diag=False,
                      diag_pos=None, status=None, timeout_ms=0, sync=True, rows=None):
     """Block-recurrence chain solve (for matrices whose levels hold only a few rows).

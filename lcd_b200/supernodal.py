@@ -52,6 +52,8 @@ class SupernodalPlan:
     flops: float
     block_inverses: torch.Tensor | None = None      # inverse diagonal blocks, column-major
     inverse_ptr: torch.Tensor | None = None         # int64 start of each supernode's inverse
+    inverse_growth: float = 0.0    # max |inverse entry| x max |diagonal| over the supernodes (the
+                                   # inverses are dropped when it exceeds the stability bound)
 
     @property
     def algorithmic_bytes(self):
@@ -149,21 +151,29 @@ def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda", inver
     panel_values = int((width * length).sum())
     flops = float((width * width + 2 * width * (length - width)).sum())
     inv = inv_ptr = None
+    inverse_growth = 0.0
     if invert_triangles and n_super:
         starts = np.zeros(n_super + 1, dtype=np.int64)
         np.cumsum(width * width, out=starts[1:])
         inv_ptr = up(starts, np.int64)
         inv = torch.empty(int(starts[-1]), dtype=torch.float64, device=dev)
+        growth = torch.zeros(1, dtype=torch.float64, device=dev)
         check(nat.load().lcd_supernodal_prepare(n_super, ptr(t_sn), ptr(t_Lip), ptr(t_Lp), ptr(t_Lx),
-                                                ptr(inv_ptr), ptr(inv), _stream()),
+                                                ptr(inv_ptr), ptr(inv), ptr(growth), _stream()),
               "lcd_supernodal_prepare")
+        inverse_growth = float(growth.item())
+        if not inverse_growth <= nat.CHAIN_MAX_GROWTH:
+            # ill-conditioned diagonal blocks: substitution keeps the digits an explicit
+            # inverse would lose
+            inv = inv_ptr = None
     return SupernodalPlan(
         n=n, n_super=n_super, n_tasks=int(first[-1]), sn=t_sn, Lip=t_Lip, Li=t_Li, Lp=t_Lp,
         Lx=t_Lx, col_to_super=t_cts, task_super=up(task_super, np.int32),
         task_strip=up(task_strip, np.int32), initial_pending=pending,
         pending=torch.empty_like(pending),
         solved=torch.empty(max(n, 1), dtype=torch.float64, device=dev), status=new_status(dev),
-        panel_values=panel_values, flops=flops, block_inverses=inv, inverse_ptr=inv_ptr)
+        panel_values=panel_values, flops=flops, block_inverses=inv, inverse_ptr=inv_ptr,
+        inverse_growth=inverse_growth)
 
 
 def solve(plan: SupernodalPlan, b, x=None, timeout_ms=0, sync=True):

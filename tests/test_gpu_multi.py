@@ -24,11 +24,12 @@ def _partition_worker(rank, world, port, out_dir):
     for name, tri in (("lap3d", gen.laplacian3d_tril(40, seed=0)),
                       ("band", gen.random_band_lower(100_000, seed=3, mean_degree=12.0, band=64))):
         Ap, Ai, Ax = tri.csr_arrays()
-        solver = PartitionedSolve(Ap, Ai, Ax)
-        for _ in range(2):                       # the peer buffers are reusable
-            x = solver.solve(tri.b, gather=True)
-        results[name] = x.cpu().numpy()
-        solver.close()
+        for ordered in (True, False):            # rows in level order / in index order
+            solver = PartitionedSolve(Ap, Ai, Ax, ordered=ordered)
+            for _ in range(2):                   # the peer buffers and task records are reusable
+                x = solver.solve(tri.b, gather=True)
+            results[name + ("" if ordered else "_by_index")] = x.cpu().numpy()
+            solver.close()
         up = gen.upper_from_lower(tri)
         Up, Ui, Ux = up.csr_arrays()
         solver = PartitionedSolve(Up, Ui, Ux, upper=True)
@@ -36,7 +37,11 @@ def _partition_worker(rank, world, port, out_dir):
         solver.close()
     tri = gen.laplacian3d_tril(24, seed=1, nrhs=13)
     Ap, Ai, Ax = tri.csr_arrays()
-    results["multirhs"] = ShardedMultiRHS(Ap, Ai, Ax).solve(np.asarray(tri.b), gather=True).cpu().numpy()
+    sharded = ShardedMultiRHS(Ap, Ai, Ax)
+    results["multirhs"] = sharded.solve(np.asarray(tri.b), gather=True).cpu().numpy()
+    start, stop = sharded.shard(13)              # the same shard as a row-major block, no transposes
+    rows_major = torch.from_numpy(np.ascontiguousarray(np.asarray(tri.b)[:, start:stop])).cuda()
+    results["multirhs_rows"] = sharded.solve(rows_major, layout="rows").cpu().numpy()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **results)
     dist.barrier()
     dist.destroy_process_group()
@@ -55,7 +60,7 @@ def test_partitioned_and_sharded_solves_on_two_gpus(cuda, oracle, tmp_path):
     for name, tri in (("lap3d", gen.laplacian3d_tril(40, seed=0)),
                       ("band", gen.random_band_lower(100_000, seed=3, mean_degree=12.0, band=64))):
         Ap, Ai, Ax = tri.csr_arrays()
-        want[name] = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+        want[name] = want[name + "_by_index"] = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
         up = gen.upper_from_lower(tri)
         Up, Ui, Ux = up.csr_arrays()
         want[name + "_upper"] = oracle.sptrsv_csr_upper(Up, Ui, Ux, up.b)
@@ -63,7 +68,10 @@ def test_partitioned_and_sharded_solves_on_two_gpus(cuda, oracle, tmp_path):
     Ap, Ai, Ax = tri.csr_arrays()
     want["multirhs"] = np.stack([oracle.sptrsv_csr_lower(Ap, Ai, Ax, np.ascontiguousarray(tri.b[:, q]))
                                  for q in range(13)])
+    from lcd_b200.multigpu import column_shard
     for rank in range(world):
         got = np.load(tmp_path / f"rank{rank}.npz")
         for name, ref in want.items():
             np.testing.assert_allclose(got[name], ref, rtol=1e-10, atol=1e-12, err_msg=f"{name} rank {rank}")
+        start, stop = column_shard(13, world, rank)
+        np.testing.assert_allclose(got["multirhs_rows"], want["multirhs"][start:stop].T, rtol=1e-10, atol=1e-12)

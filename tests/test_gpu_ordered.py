@@ -275,3 +275,34 @@ def test_small_solver_config1_csc_and_far_operands(cuda, oracle):
         x = host(ops.sptrsv_small(plan, dev(Ax, np.float64, cuda), dev(b, np.float64, cuda)))
         np.testing.assert_allclose(x, getattr(oracle, f"sptrsv_{fmt}_lower")(Ap, Ai, Ax, b),
                                    rtol=1e-10, atol=1e-12)
+
+
+def test_partition_need_mask_matches_numpy(cuda):
+    """need_mask[c] has bit q set exactly when a row owned by rank q stores an off-diagonal entry
+    in a column c produced by another rank (lower and upper, node ids reversed for upper)."""
+    import ctypes
+    import torch
+    from lcd_b200 import _native as nat, generators as gen
+    from lcd_b200.multigpu import row_partition
+    lower = gen.random_band_lower(5000, seed=8, mean_degree=7.0, band=300)
+    for tri, upper in ((lower, False), (gen.upper_from_lower(lower), True)):
+        Ap, Ai, _ = tri.csr_arrays()
+        n = tri.n
+        for parts in (2, 3, 8):
+            bounds = row_partition(n, parts)
+            want = np.zeros(n, dtype=np.uint8)
+            owner_of = np.searchsorted(bounds, np.arange(n), side="right") - 1   # by node id
+            for r in range(n):
+                node = n - 1 - r if upper else r
+                lo, hi = (Ap[r] + 1, Ap[r + 1]) if upper else (Ap[r], Ap[r + 1] - 1)
+                for c in Ai[lo:hi]:
+                    node_c = n - 1 - c if upper else c
+                    if node_c < bounds[owner_of[node]]:
+                        want[c] |= 1 << owner_of[node]
+            need = torch.zeros((n + 3) // 4 * 4, dtype=torch.uint8, device=cuda)
+            dAp, dAi, dbounds = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(bounds, np.int32, cuda)
+            rc = nat.load().lcd_partition_need_mask(
+                n, nat.ptr(dAp), nat.ptr(dAi), nat.SOLVE_UPPER if upper else 0, nat.ptr(dbounds), parts,
+                nat.ptr(need), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert rc == 0
+            np.testing.assert_array_equal(host(need)[:n], want)
