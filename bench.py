@@ -539,6 +539,27 @@ def _max_over_ranks(value, world, dev):
     return float(t.item())
 
 
+def numba_cuda_reference():
+    """The reference's own Numba-CUDA path (wavefront variant of the sptrsv_csc demo) timed on
+    this box by ``baseline/numba_wavefront.py`` in a child process: the unmodified reference from
+    ``baseline/_ref`` (git-ignored; placed there by ``baseline/install_reference.py`` where the
+    reference checkout exists).  Returns its JSON record, or the reason it could not run."""
+    import tempfile
+    script = os.path.join(ROOT, "baseline", "numba_wavefront.py")
+    try:
+        with tempfile.TemporaryDirectory() as scratch:      # the reference writes smt_file.smt2 into the cwd
+            done = subprocess.run([sys.executable, script], cwd=scratch, capture_output=True, text=True,
+                                  timeout=300)
+        lines = [line for line in done.stdout.splitlines() if line.startswith("{")]
+        if not lines:
+            return {"unavailable": ("no result: " + (done.stderr.strip().splitlines() or ["?"])[-1])[:300]}
+        return json.loads(lines[-1])
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the child process did not finish within 300 s"}
+    except Exception as error:
+        return {"unavailable": f"{type(error).__name__}: {error}"[:300]}
+
+
 # ---- configuration 1: the sptrsv_csc demo on the 256 x 256 grid -------------------------
 def config_csc_lap2d(args, size=256):
     """Lower triangle of the 2-D 5-point Laplacian, CSC, through the decorated operator
@@ -592,7 +613,9 @@ def config_csc_lap2d(args, size=256):
     e2e_residual = float(np.linalg.norm(A @ out - tri.b) / np.linalg.norm(tri.b))
     cpu_s, count = _host_time(lambda: cpu.sptrsv_csc_lower(Cp, Ci, Cx, tri.b), min_seconds=1.0)
     nbytes = algorithmic_bytes(n, nnz)
+    reference_gpu = numba_cuda_reference() if size == 256 else {"unavailable": "timed on the 256 x 256 grid only"}
     return {"workload": f"sptrsv_csc_lap2d_g{size}", "format": "csc_lower", "n": n, "nnz": nnz,
+            "numba_cuda_wavefront_ms": reference_gpu.get("ms"), "numba_cuda_reference": reference_gpu,
             "levels": dag.n_levels, "kernel": "sptrsv_small_kernel (one thread block)",
             "ms": ms, "gflops": flops(n, nnz) / (ms * 1e-3) / 1e9,
             "inspector_ms": inspect_ms, "roofline": _roofline(nbytes, ms, peak),
@@ -668,6 +691,10 @@ def config_ilu0(args, size=128):
     best = results[best_mode]
     tri_nnz = (nnz + n) // 2
     return {"workload": f"ilu0_lap3d_g{size}", "metric": "spilu0_ms_per_factorization", "n": n, "nnz": nnz,
+            "numba_cuda_wavefront_ms": None,
+            "numba_cuda_reference": {"unavailable": "not run: the reference's inspector is interpreted "
+                                     "Python over sets of edges and needs minutes and gigabytes at "
+                                     f"{n} rows before its first launch"},
             "levels": dag.n_levels, "ms": best, "mode": best_mode, "ms_by_mode": results,
             "gflops_2nnz": 2 * nnz / (best * 1e-3) / 1e9, "inspector_ms": inspect_ms,
             "roofline": _roofline(nbytes, best, peak),
@@ -791,6 +818,30 @@ def config_partition(args, size=256):
     tri = gen.laplacian3d_tril(size, seed=0)
     Ap, Ai, Ax = tri.csr_arrays()
     n, nnz = tri.n, tri.nnz
+    if world == 1:
+        # the one-GPU point of the curve: the same kernel on the whole matrix, no partition
+        from lcd_b200 import ops
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        dAp, dAi, dAx, db = up(Ap), up(Ai), up(Ax), up(tri.b)
+        t0 = time.perf_counter()
+        dag = ops.dag_build("csr_lower", dAp, dAi)
+        torch.cuda.synchronize()
+        inspect_ms = (time.perf_counter() - t0) * 1e3
+        plan = ops.OrderedPlan(dag.wavefronts, dag.n_levels)
+        x = torch.empty_like(db)
+        status = ops.new_status(dev)
+        ms = float(np.median(_time_steps(lambda: ops.sptrsv_csr_ordered(
+            dAp, dAi, dAx, db, plan, x, status=status, sync=False), max(3, min(args.steps, 10)), 3)))
+        residual = cpu.relative_residual_csr(Ap, Ai, Ax, x.cpu().numpy(), tri.b)
+        cpu_s, count = _host_time(lambda: cpu.sptrsv_csr_lower(Ap, Ai, Ax, tri.b), min_seconds=1.0)
+        return {"workload": f"partition_lap3d_g{size}", "n": n, "nnz": nnz, "n_gpus": 1,
+                "levels": dag.n_levels, "scaling": "strong", "ms": ms, "inspector_ms": inspect_ms,
+                "kernel": "csr_ordered_kernel (whole matrix on one GPU)",
+                "gflops": flops(n, nnz) / (ms * 1e-3) / 1e9,
+                "roofline": _roofline(algorithmic_bytes(n, nnz), ms, peak), "cut_planes": 0,
+                "parity": {"relative_residual": residual, "tolerance": 1e-12, "ok": bool(residual <= 1e-12)},
+                "cpu_baseline": {"value": flops(n, nnz) / cpu_s / 1e9, "unit": "GFLOP/s", "ms": cpu_s * 1e3,
+                                 "cores": 1, "kind": "port", "sample": f"{count} full solves"}}
     solver = PartitionedSolve(Ap, Ai, Ax)
     b = torch.from_numpy(tri.b).to(dev)
     out = [None]
@@ -829,7 +880,8 @@ def other_configurations(args, rank, world):
     if world == 1:
         plan = [("cfg1_csc_lap2d_g256", "csc", 256), ("cfg3_ilu0_lap3d_g128", "ilu0", 128),
                 ("cfg4_supernodal_n1048576", "supernodal", 1_048_576),
-                ("cfg5a_multirhs_lap3d_g192", "multirhs", 192)]
+                ("cfg5a_multirhs_lap3d_g192", "multirhs", 192),
+                ("cfg5b_partition_lap3d_g256", "partition", 256)]
     else:
         plan = [("cfg5a_multirhs_lap3d_g192", "multirhs", 192),
                 ("cfg5b_partition_lap3d_g256", "partition", 256)]

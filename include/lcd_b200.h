@@ -34,7 +34,9 @@ enum {
     LCD_ERR_INDEX_RANGE = 7,      /* an index lies outside [0, n) or on the wrong side of the diagonal */
     LCD_ERR_CYCLE = 8,            /* the dependence graph is not acyclic */
     LCD_ERR_MISSING_DIAGONAL = 9, /* a row needs a diagonal entry that is not stored */
-    LCD_ERR_TOO_LARGE = 10        /* a size exceeds a documented limit */
+    LCD_ERR_TOO_LARGE = 10,       /* a size exceeds a documented limit */
+    LCD_ERR_LEVEL_CAP = 11        /* internal to lcd_dag_build_capped: the level propagation reached the
+                                     requested cap (reported as a negative level count, not returned) */
 };
 
 /* Operators: which edge rule the inspector applies.  The numbering is shared by
@@ -98,12 +100,44 @@ int lcd_read_status(const int32_t *status_dev, void *stream, int32_t *node);
  * `timeout_ms` bounds the level propagation's device-side waits (0 = default).
  */
 int lcd_dag_workspace_bytes(int op, int32_t n, int64_t nnz, int64_t *bytes);
+/*
+ * The same build with a bound on the level propagation.  The propagation is the one sequential
+ * part of the inspector (one hand-off per level); a caller that only has to know whether the DAG
+ * is deep - the launcher of the sync-free CSR solve chooses the block-recurrence chain solver
+ * from that alone and never reads the level sets - passes level_cap > 0: as soon as a node reaches
+ * level `level_cap` the propagation stops, *n_levels_host receives -level_cap, and level,
+ * wavefronts and wavefront_ptr are left unfinished (dep_count, edge_count, dag_ptr and dag_index
+ * are complete).  A DAG with at most level_cap levels is built in full, as by lcd_dag_build
+ * (= level_cap 0).
+ */
+int lcd_dag_build_capped(int op, int32_t n, const int32_t *ptr, const int32_t *idx, int64_t nnz,
+                         int32_t *dep_count, int32_t *edge_count, int32_t *dag_ptr,
+                         int32_t *dag_index, int64_t *n_edges_host, int32_t *level,
+                         int32_t *wavefronts, int32_t *wavefront_ptr, int32_t *n_levels_host,
+                         int32_t level_cap, void *workspace, int64_t workspace_bytes,
+                         int32_t timeout_ms, void *stream);
 int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_t *idx, int64_t nnz,
                   int32_t *dep_count, int32_t *edge_count, int32_t *dag_ptr,
                   int32_t *dag_index, int64_t *n_edges_host, int32_t *level,
                   int32_t *wavefronts, int32_t *wavefront_ptr, int32_t *n_levels_host,
                   void *workspace, int64_t workspace_bytes, int32_t timeout_ms,
                   void *stream);
+
+/*
+ * Band chains: the tasks of the reference's warp executor with band_width > 1
+ * (compiler/dag_preprocessing.py:258-298, _band_chains).  Inside every band of band_width
+ * consecutive levels, nodes connected by DAG edges form one task; tasks are listed by their
+ * first node in level order, nodes inside a task in level order - element-wise what the
+ * reference's union-find over Python lists returns.  Inputs are device arrays of lcd_dag_build.
+ *   task_nodes[n], task_ptr[n + 1] (first *n_tasks_host + 1 entries valid),
+ *   band_ptr[ceil(n_levels / band_width) + 1]  - all device arrays.
+ * The call synchronises `stream`.
+ */
+int lcd_band_chains_workspace_bytes(int32_t n, int64_t *bytes);
+int lcd_band_chains(int32_t n, const int32_t *dag_ptr, const int32_t *dag_index, const int32_t *level,
+                    const int32_t *wavefronts, const int32_t *wavefront_ptr_dev, int32_t n_levels,
+                    int32_t band_width, int32_t *task_nodes, int32_t *task_ptr, int32_t *band_ptr,
+                    int32_t *n_tasks_host, void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
  * Rows of a Gauss-Seidel sweep over a lower-triangular matrix -> the diagonal-last rows the
@@ -520,8 +554,11 @@ enum {
                                      hosts (up to 8), 1 = plain blocks, 2 / 4 / 8 = at most that */
     LCD_TUNE_ORDERED_PAUSE_NS = 6, /* lcd_sptrsv_csr_ordered: longest pause of a warp between two
                                      unsuccessful polls (0 = never pause; default 256) */
-    LCD_TUNE_SMALL_THREADS = 7    /* lcd_sptrsv_small: threads of the one block, 256 / 512 / 1024
+    LCD_TUNE_SMALL_THREADS = 7,   /* lcd_sptrsv_small: threads of the one block, 256 / 512 / 1024
                                      (0 = 512 while no level is wider than that, else 1024) */
+    LCD_TUNE_ILU0_LOOKAHEAD = 8   /* lcd_spilu0_csr sync-free modes: 1 (default) = pattern look-ups
+                                     for the next pivots before their flags are polled, own entries
+                                     in registers; 0 = search while the pivot is held.  Same result. */
 };
 int lcd_set_tuning(int key, int value);
 /* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,

@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_HERE, "liblcd_b200.so")
 
 # LCD_* codes of include/lcd_b200.h
 OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
-    ERR_BAD_POINTERS, ERR_INDEX_RANGE, ERR_CYCLE, ERR_MISSING_DIAGONAL, ERR_TOO_LARGE = range(11)
+    ERR_BAD_POINTERS, ERR_INDEX_RANGE, ERR_CYCLE, ERR_MISSING_DIAGONAL, ERR_TOO_LARGE, \
+    ERR_LEVEL_CAP = range(12)
 (OP_CSR_LOWER, OP_CSC_LOWER, OP_ILU0_CSR, OP_CSR_UPPER, OP_CSC_UPPER, OP_CSR_LOWER_ROWS,
  OP_CSR_UPPER_ROWS) = range(7)
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
@@ -23,7 +24,7 @@ WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
 CHAIN_MAX_GROWTH = 100.0        # LCD_CHAIN_MAX_GROWTH
 (TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT,
- TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS) = range(8)
+ TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS, TUNE_ILU0_LOOKAHEAD) = range(9)
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -50,6 +51,12 @@ _SIGNATURES = {
     "lcd_dag_build": (c_int, [c_int, c_int32, _P, _P, c_int64, _P, _P, _P, _P,
                               ctypes.POINTER(c_int64), _P, _P, _P, ctypes.POINTER(c_int32),
                               _P, c_int64, c_int32, _P]),
+    "lcd_band_chains_workspace_bytes": (c_int, [c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_band_chains": (c_int, [c_int32, _P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, _P,
+                                ctypes.POINTER(c_int32), _P, c_int64, _P]),
+    "lcd_dag_build_capped": (c_int, [c_int, c_int32, _P, _P, c_int64, _P, _P, _P, _P,
+                                     ctypes.POINTER(c_int64), _P, _P, _P, ctypes.POINTER(c_int32),
+                                     c_int32, _P, c_int64, c_int32, _P]),
     "lcd_diag_positions": (c_int, [c_int32, _P, _P, c_int64, _P, _P, _P, ctypes.POINTER(c_int)]),
     "lcd_sptrsv_csr_syncfree": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, c_int,
                                         c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),

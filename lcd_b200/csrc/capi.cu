@@ -116,6 +116,7 @@ extern "C" const char *lcd_error_string(int code) {
         case LCD_ERR_CYCLE: return "dependence graph is not acyclic";
         case LCD_ERR_MISSING_DIAGONAL: return "a required diagonal entry is not stored";
         case LCD_ERR_TOO_LARGE: return "size exceeds a documented limit";
+        case LCD_ERR_LEVEL_CAP: return "level propagation stopped at the requested cap";
         default: return "unknown lcd_b200 error";
     }
 }

@@ -43,6 +43,7 @@ void set_debug_trace(long long *p);
 int set_chain_cluster_limit(int blocks);  // LCD_TUNE_CHAIN_CLUSTER
 int set_ordered_pause(int ns);           // LCD_TUNE_ORDERED_PAUSE_NS
 int set_small_threads(int threads);      // LCD_TUNE_SMALL_THREADS
+int set_ilu0_lookahead(int on);          // LCD_TUNE_ILU0_LOOKAHEAD
 long long *debug_trace();  // profiling aid set by lcd_debug_set_trace (NULL = off)
 
 #ifdef __CUDACC__

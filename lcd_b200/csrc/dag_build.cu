@@ -308,7 +308,7 @@ constexpr int kLevelThreads = 512;
 
 __global__ void __launch_bounds__(kLevelThreads)
 level_kernel(int n, const int *__restrict__ pred_ptr, const unsigned *__restrict__ pred,
-             int *level, int *max_level, int32_t *status, unsigned long long budget_ns) {
+             int *level, int *max_level, int32_t *status, unsigned long long budget_ns, int cap) {
     __shared__ int sl[kLevelThreads];
     __shared__ int s_chunk;
     __shared__ int s_max;
@@ -344,6 +344,9 @@ level_kernel(int n, const int *__restrict__ pred_ptr, const unsigned *__restrict
                     }
                 }
             } else {
+                // a caller that only asks "are there at least `cap` levels?" gets its answer
+                // here: the status word stops every other waiter within a few polls
+                if (cap > 0 && lvl >= cap) raise_error(status, LCD_ERR_LEVEL_CAP, v);
                 asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(level + v), "r"(lvl) : "memory");
                 slv[tid] = lvl;
                 atomicMax(&s_max, lvl);
@@ -500,6 +503,84 @@ __global__ void gs_scatter_kernel(long long nnz, const int *__restrict__ perm,
     if (j < nnz && perm[j] >= 0) Ax_out[perm[j]] = Ax[j];
 }
 
+// ---- band chains ---------------------------------------------------------------------
+// Tasks of the reference's warp executor with band_width > 1: inside every band of band_width
+// consecutive levels the nodes that are connected by DAG edges form one task (a chain solved
+// by one lane group), tasks ordered by their first node in level order, nodes inside a task
+// in level order.  Connected components by lock-free union-find over positions in the level
+// order (the smaller position becomes the root, so a component's label is the position of
+// its first node), then one stable sort by label.
+__device__ __forceinline__ int chain_find(int *parent, int v) {
+    int p = parent[v];
+    while (p != v) {            // path halving
+        const int gp = parent[p];
+        if (gp != p) parent[v] = gp;
+        v = p;
+        p = gp;
+    }
+    return v;
+}
+
+__global__ void chain_init_kernel(int n, const int *__restrict__ wavefronts, int *pos, int *parent,
+                                  int32_t *status) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    parent[t] = t;
+    const int v = wavefronts[t];
+    if ((unsigned)v >= (unsigned)n) raise_error(status, LCD_ERR_INDEX_RANGE, t);
+    else pos[v] = t;
+}
+
+__global__ void chain_union_kernel(int n, const int *__restrict__ dag_ptr, const int *__restrict__ dag_index,
+                                   const int *__restrict__ level, const int *__restrict__ pos,
+                                   int band_width, int *parent) {
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= n) return;
+    const int band = level[u] / band_width;
+    for (int e = dag_ptr[u]; e < dag_ptr[u + 1]; ++e) {
+        const int w = dag_index[e];
+        if ((unsigned)w >= (unsigned)n || level[w] / band_width != band) continue;
+        int a = pos[u], b = pos[w];
+        for (;;) {              // hook the larger root under the smaller one
+            a = chain_find(parent, a);
+            b = chain_find(parent, b);
+            if (a == b) break;
+            if (a < b) { const int t = a; a = b; b = t; }
+            if (atomicCAS(parent + a, a, b) == a) break;
+        }
+    }
+}
+
+__global__ void chain_label_kernel(int n, const int *__restrict__ wavefronts, int *parent,
+                                   unsigned *keys, unsigned *vals) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    int r = t;
+    while (parent[r] != r) r = parent[r];
+    keys[t] = (unsigned)r;
+    vals[t] = (unsigned)wavefronts[t];
+}
+
+__global__ void chain_heads_kernel(int n, const unsigned *__restrict__ keys, int *head) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) head[t] = (t == 0 || keys[t] != keys[t - 1]) ? 1 : 0;
+}
+
+__global__ void chain_emit_kernel(int n, const unsigned *__restrict__ vals, const int *__restrict__ headscan,
+                                  const int *__restrict__ wavefront_ptr, int n_levels, int band_width,
+                                  int *task_nodes, int *task_ptr, int *band_ptr) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int n_bands = (n_levels + band_width - 1) / band_width;
+    if (t <= n_bands) {
+        const int first_level = t * band_width < n_levels ? t * band_width : n_levels;
+        band_ptr[t] = headscan[wavefront_ptr[first_level]];   // tasks that start before the band
+    }
+    if (t >= n) return;
+    task_nodes[t] = (int)vals[t];
+    if (headscan[t + 1] != headscan[t]) task_ptr[headscan[t]] = t;
+    if (t == n - 1) task_ptr[headscan[n]] = n;
+}
+
 static inline int grid_for(long long m, int threads) {
     long long g = (m + threads - 1) / threads;
     const long long cap = 148ll * 32;
@@ -526,7 +607,19 @@ extern "C" int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_
                              int32_t *level, int32_t *wavefronts, int32_t *wavefront_ptr,
                              int32_t *n_levels_host, void *workspace, int64_t workspace_bytes,
                              int32_t timeout_ms, void *stream) {
-    if (op < 0 || op > LCD_OP_CSR_UPPER_ROWS || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host)
+    return lcd_dag_build_capped(op, n, ptr, idx, nnz, dep_count, edge_count, dag_ptr, dag_index,
+                                n_edges_host, level, wavefronts, wavefront_ptr, n_levels_host, 0,
+                                workspace, workspace_bytes, timeout_ms, stream);
+}
+
+extern "C" int lcd_dag_build_capped(int op, int32_t n, const int32_t *ptr, const int32_t *idx,
+                                    int64_t nnz, int32_t *dep_count, int32_t *edge_count,
+                                    int32_t *dag_ptr, int32_t *dag_index, int64_t *n_edges_host,
+                                    int32_t *level, int32_t *wavefronts, int32_t *wavefront_ptr,
+                                    int32_t *n_levels_host, int32_t level_cap, void *workspace,
+                                    int64_t workspace_bytes, int32_t timeout_ms, void *stream) {
+    if (op < 0 || op > LCD_OP_CSR_UPPER_ROWS || n < 0 || nnz < 0 || !n_edges_host || !n_levels_host ||
+        level_cap < 0)
         return LCD_ERR_INVALID_ARGUMENT;
     *n_edges_host = 0;
     *n_levels_host = 0;
@@ -603,12 +696,17 @@ extern "C" int lcd_dag_build(int op, int32_t n, const int32_t *ptr, const int32_
     rc = reset_status(status, st);
     if (rc) return rc;
     level_kernel<<<(n + kLevelThreads - 1) / kLevelThreads, kLevelThreads, 0, st>>>(
-        n, s.pred_ptr, pred, level, s.max_level, status, timeout_ns(timeout_ms));
+        n, s.pred_ptr, pred, level, s.max_level, status, timeout_ns(timeout_ms), level_cap);
     LCD_CUDA_TRY(cudaGetLastError());
     int max_level = -1;
     LCD_CUDA_TRY(cudaMemcpyAsync(&max_level, s.max_level, sizeof max_level, cudaMemcpyDeviceToHost, st));
     LCD_CUDA_TRY(cudaStreamSynchronize(st));
     rc = lcd_read_status(status, st, nullptr);
+    if (rc == LCD_ERR_LEVEL_CAP) {
+        // at least level_cap + 1 levels: the level arrays stay unfinished, everything else is built
+        *n_levels_host = -level_cap;
+        return LCD_OK;
+    }
     if (rc) return rc;
     const int n_levels = max_level + 1;
     *n_levels_host = n_levels;
@@ -700,5 +798,66 @@ extern "C" int lcd_gs_values(int32_t n, int64_t nnz, const int32_t *Ap_out, cons
         gs_scatter_kernel<<<(unsigned)((nnz + 255) / 256), 256, 0, st>>>(nnz, perm, Ax, Ax_out);
         LCD_CUDA_TRY(cudaGetLastError());
     }
+    return LCD_OK;
+}
+
+extern "C" int lcd_band_chains_workspace_bytes(int32_t n, int64_t *bytes) {
+    if (n < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
+    Bump b{nullptr, 0};
+    b.take<int32_t>(LCD_STATUS_WORDS);
+    plan_scratch(b, n, n);
+    *bytes = (int64_t)b.used + 256;
+    return LCD_OK;
+}
+
+extern "C" int lcd_band_chains(int32_t n, const int32_t *dag_ptr, const int32_t *dag_index,
+                               const int32_t *level, const int32_t *wavefronts,
+                               const int32_t *wavefront_ptr_dev, int32_t n_levels, int32_t band_width,
+                               int32_t *task_nodes, int32_t *task_ptr, int32_t *band_ptr,
+                               int32_t *n_tasks_host, void *workspace, int64_t workspace_bytes,
+                               void *stream) {
+    if (n < 0 || n_levels < 0 || band_width < 1 || !n_tasks_host) return LCD_ERR_INVALID_ARGUMENT;
+    *n_tasks_host = 0;
+    if (!task_ptr || !band_ptr || !workspace) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!dag_ptr || !dag_index || !level || !wavefronts || !wavefront_ptr_dev || !task_nodes))
+        return LCD_ERR_INVALID_ARGUMENT;
+    int64_t need = 0;
+    lcd_band_chains_workspace_bytes(n, &need);
+    if (workspace_bytes < need) return LCD_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (n == 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(task_ptr, 0, sizeof(int32_t), st));
+        LCD_CUDA_TRY(cudaMemsetAsync(band_ptr, 0, sizeof(int32_t), st));
+        LCD_CUDA_TRY(cudaStreamSynchronize(st));
+        return LCD_OK;
+    }
+    Bump bump{reinterpret_cast<char *>(workspace), 0};
+    int32_t *status = bump.take<int32_t>(LCD_STATUS_WORDS);
+    DagScratch s = plan_scratch(bump, n, n);
+    int rc = reset_status(status, st);
+    if (rc) return rc;
+    const int nblk = (n + 255) / 256;
+    int *pos = s.cnt, *parent = s.pred_ptr;
+    chain_init_kernel<<<nblk, 256, 0, st>>>(n, wavefronts, pos, parent, status);
+    chain_union_kernel<<<nblk, 256, 0, st>>>(n, dag_ptr, dag_index, level, pos, band_width, parent);
+    chain_label_kernel<<<nblk, 256, 0, st>>>(n, wavefronts, parent, s.k0, s.v0);
+    LCD_CUDA_TRY(cudaGetLastError());
+    bool in_first = true;
+    LCD_CUDA_TRY(radix_sort_pairs(s.k0, s.v0, s.k1, s.v1, n, bits_for(n > 1 ? n - 1 : 1), s.sort, st,
+                                  &in_first));
+    const unsigned *keys = in_first ? s.k0 : s.k1, *vals = in_first ? s.v0 : s.v1;
+    chain_heads_kernel<<<nblk, 256, 0, st>>>(n, keys, s.flags);
+    LCD_CUDA_TRY(exclusive_scan(s.flags, n, s.flags, s.scan_sums, s.scan_total, st));
+    const int n_bands = (n_levels + band_width - 1) / band_width;
+    const int m = n > n_bands + 1 ? n : n_bands + 1;
+    chain_emit_kernel<<<(m + 255) / 256, 256, 0, st>>>(n, vals, s.flags, wavefront_ptr_dev, n_levels,
+                                                       band_width, task_nodes, task_ptr, band_ptr);
+    LCD_CUDA_TRY(cudaGetLastError());
+    long long total = 0;
+    LCD_CUDA_TRY(cudaMemcpyAsync(&total, s.scan_total, sizeof total, cudaMemcpyDeviceToHost, st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    rc = lcd_read_status(status, st, nullptr);
+    if (rc) return rc;
+    *n_tasks_host = (int32_t)total;
     return LCD_OK;
 }

@@ -138,6 +138,194 @@ __global__ void __launch_bounds__(TPB) ilu0_syncfree_kernel(const Ilu0Params p) 
     }
 }
 
+// ---- the same factorisation with the structure work taken off the dependence chain ----
+// What a row has to wait for are VALUES of its pivot rows; WHERE those values sit (the pivot
+// row's pointers, its diagonal position, the entry of the pivot row under each entry of this
+// row) follows from the pattern alone.  The kernel above searches while it holds the pivot;
+// this one looks everything up for the next four pivots before it polls their flags, keeps
+// the row's own entries in registers (two per lane; longer rows keep the rest in memory), polls
+// the four flags together and fetches the values of all pivots that are ready with one round
+// of independent loads.  Per row the chain shrinks from about eight dependent loads per
+// pivot to two round trips per group of pivots.  Operations on every entry are the same and
+// in the same order (pivots ascending, unfused multiply / subtract), so the result is still
+// bit-identical to the sequential loop.
+constexpr int kIluOwn = 2;     // entries of the row a lane keeps in registers
+constexpr int kIluPivots = 4;  // pivots looked up and polled together
+
+template <int G, int TPB>
+__global__ void __launch_bounds__(TPB) ilu0_lookahead_kernel(const Ilu0Params p) {
+    constexpr int R = TPB / G;
+    __shared__ int s_chunk;
+    if (threadIdx.x == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    __syncthreads();
+    const int local = threadIdx.x / G, lane = threadIdx.x % G;
+    const int task = s_chunk * R + local;
+    if (task >= p.n) return;
+    int i = task;
+    if (p.wavefronts) {
+        i = __ldg(p.wavefronts + task);
+        if ((unsigned)i >= (unsigned)p.n) {
+            if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, task);
+            return;
+        }
+    }
+    const unsigned gmask =
+        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+    const int s = __ldg(p.Ap + i), e = __ldg(p.Ap + i + 1);
+    bool bad = s < 0 || e < s || (long long)e > p.nnz;
+    if (bad && lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
+    // the lane's own entries of row i: positions s + lane + o * G
+    int col[kIluOwn];
+    double val[kIluOwn];
+#pragma unroll
+    for (int o = 0; o < kIluOwn; ++o) {
+        const int jp = s + lane + o * G;
+        col[o] = -1;
+        val[o] = 0.0;
+        if (!bad && jp < e) { col[o] = __ldg(p.Ai + jp); val[o] = p.Ax[jp]; }
+    }
+    const int spill = s + kIluOwn * G;   // entries from here on stay in memory (long rows)
+    int kp = s;
+    unsigned pause = 0;
+    Deadline dl;
+    dl.start(p.budget_ns);
+    while (!bad) {
+        // ---- look up the next pivots (pattern only, nothing to wait for) ----
+        int pk[kIluPivots], pks[kIluPivots], pke[kIluPivots], pd[kIluPivots];
+        int match[kIluPivots][kIluOwn];
+        int npiv = 0;
+#pragma unroll
+        for (int q = 0; q < kIluPivots; ++q) {
+            pk[q] = -1; pks[q] = 0; pke[q] = 0; pd[q] = -1;
+            if (npiv == q && kp + q < e) {
+                const int k = __ldg(p.Ai + kp + q);
+                if (k < 0 || k >= p.n) {
+                    if (lane == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, i);
+                    bad = true;
+                } else if (k < i) {
+                    pk[q] = k;
+                    npiv = q + 1;
+                }
+            }
+        }
+        if (bad || npiv == 0) break;
+#pragma unroll
+        for (int q = 0; q < kIluPivots; ++q) {
+            if (q < npiv) {
+                pks[q] = __ldg(p.Ap + pk[q]);
+                pke[q] = __ldg(p.Ap + pk[q] + 1);
+                pd[q] = __ldg(p.dpos + pk[q]);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kIluPivots; ++q) {
+            if (q < npiv && (pks[q] < 0 || pke[q] < pks[q] || (long long)pke[q] > p.nnz ||
+                             (long long)pd[q] >= p.nnz)) {
+                if (lane == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, pk[q]);
+                bad = true;
+            }
+        }
+        if (bad) break;
+#pragma unroll
+        for (int q = 0; q < kIluPivots; ++q) {
+#pragma unroll
+            for (int o = 0; o < kIluOwn; ++o) {
+                match[q][o] = -1;
+                const int jp = s + lane + o * G;
+                if (q < npiv && jp < e && jp > kp + q) {
+                    int lo = pks[q], hi = pke[q];   // leftmost entry of the pivot row that is >= col
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (__ldg(p.Ai + mid) < col[o]) lo = mid + 1; else hi = mid;
+                    }
+                    if (lo < pke[q] && __ldg(p.Ai + lo) == col[o]) match[q][o] = lo;
+                }
+            }
+        }
+        // ---- wait for the pivots in order, as many at a time as are ready ----
+        int applied = 0;
+        unsigned ready_mask = 0;
+        while (applied < npiv && !bad) {
+            int verdict = 0;   // 2 = give up
+            if (lane == 0) {
+                unsigned fresh = 0;
+#pragma unroll
+                for (int q = 0; q < kIluPivots; ++q)
+                    if (q >= applied && q < npiv && !(ready_mask >> q & 1u) &&
+                        ld_relaxed_s32(p.done + pk[q]) != 0)
+                        fresh |= 1u << q;
+                if (fresh) { acquire_fence(); ready_mask |= fresh; }
+                if (!(ready_mask >> applied & 1u) && dl.tick(p.status, i)) verdict = 2;
+            }
+            if (G > 1) {
+                ready_mask = __shfl_sync(gmask, ready_mask, 0, G);
+                verdict = __shfl_sync(gmask, verdict, 0, G);
+            }
+            if (verdict == 2) { bad = true; break; }
+            int upto = applied;
+            while (upto < npiv && (ready_mask >> upto & 1u)) ++upto;
+            if (upto == applied) {
+                // rows far behind the frontier stop competing for L2 with the polls that matter
+                pause = pause ? min(pause * 2, 1024u) : 32u;
+                __nanosleep(pause);
+                continue;
+            }
+            pause = 0;
+            // one round of independent loads: diagonals and matched entries of the ready pivots
+            double dg[kIluPivots], u[kIluPivots][kIluOwn];
+#pragma unroll
+            for (int q = 0; q < kIluPivots; ++q) {
+                dg[q] = 0.0;
+                const bool on = q >= applied && q < upto;
+                if (on && pd[q] >= 0) dg[q] = ld_relaxed_f64(p.Ax + pd[q]);
+#pragma unroll
+                for (int o = 0; o < kIluOwn; ++o)
+                    u[q][o] = (on && match[q][o] >= 0) ? ld_relaxed_f64(p.Ax + match[q][o]) : 0.0;
+            }
+#pragma unroll
+            for (int q = 0; q < kIluPivots; ++q) {
+                if (q < applied || q >= upto || dg[q] == 0.0) continue;   // (group-uniform)
+                const int rel = kp + q - s, owner = rel % G, slot = rel / G;
+                double lik = 0.0;
+                if (lane == owner) {
+                    if (slot == 0) { lik = val[0] / dg[q]; val[0] = lik; }
+                    else if (slot == 1) { lik = val[1] / dg[q]; val[1] = lik; }
+                    else { lik = p.Ax[kp + q] / dg[q]; p.Ax[kp + q] = lik; }
+                }
+                if (G > 1) lik = __shfl_sync(gmask, lik, owner, G);
+#pragma unroll
+                for (int o = 0; o < kIluOwn; ++o)
+                    if (match[q][o] >= 0) val[o] = __dsub_rn(val[o], __dmul_rn(lik, u[q][o]));
+                // entries of a long row that live in memory: searched while the pivot is held
+                for (int jp = spill + lane; jp < e; jp += G) {
+                    if (jp <= kp + q) continue;
+                    const int j = __ldg(p.Ai + jp);
+                    int lo = pks[q], hi = pke[q];
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (__ldg(p.Ai + mid) < j) lo = mid + 1; else hi = mid;
+                    }
+                    if (lo < pke[q] && __ldg(p.Ai + lo) == j)
+                        p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ld_relaxed_f64(p.Ax + lo)));
+                }
+            }
+            applied = upto;
+        }
+        kp += npiv;
+        if (npiv < kIluPivots) break;   // the next entry is the diagonal or right of it
+    }
+    // the row's entries go back to memory, then the flag: all stores of the group happen
+    // before the flag becomes visible (also after an error, so that nobody waits for this row)
+#pragma unroll
+    for (int o = 0; o < kIluOwn; ++o) {
+        const int jp = s + lane + o * G;
+        if (col[o] >= 0 && jp < e) p.Ax[jp] = val[o];
+    }
+    // (the release store is cumulative over what the group's lanes wrote before the barrier)
+    __syncwarp(gmask);
+    if (lane == 0) st_release_s32(p.done + i, 1);
+}
+
 template <int G>
 __global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int wave_start,
                                                         int wave_end) {
@@ -164,12 +352,21 @@ __global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int
     }
 }
 
+static int g_ilu0_lookahead = 1;   // LCD_TUNE_ILU0_LOOKAHEAD
+int set_ilu0_lookahead(int on) {
+    g_ilu0_lookahead = on ? 1 : 0;
+    return LCD_OK;
+}
+
 template <int G>
 static cudaError_t launch_ilu0(const Ilu0Params &p, int mode, const int32_t *wptr_host,
                                int n_levels, cudaStream_t st) {
     if (mode == 0 || mode == 2) {
         constexpr int TPB = 256, R = TPB / G;
-        ilu0_syncfree_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
+        if (g_ilu0_lookahead)
+            ilu0_lookahead_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
+        else
+            ilu0_syncfree_kernel<G, TPB><<<(p.n + R - 1) / R, TPB, 0, st>>>(p);
     } else {
         for (int l = 0; l < n_levels; ++l) {
             const int ws = wptr_host[l], we = wptr_host[l + 1];

@@ -41,30 +41,30 @@ class CUDAModuleCompilationError(Exception):
 
 
 # Page-locked result buffers.  Allocating one costs about 12 ms per 32 MB, so a few are kept
-# and handed out again - but only once nothing else refers to their memory any more (the
-# array returned to the caller, and every view of it, holds a reference to the storage).
+# and handed out again - but only once the array that was returned to the caller is gone: the
+# pool keeps a weak reference to that array, and every view or tensor made from it keeps it
+# alive (a view's ``base`` is the array), so a dead reference means nobody can still read it.
 _PINNED_BLOCKS = {}
 _PINNED_BLOCKS_PER_SHAPE = 4
 
 
-def _storage_users(tensor):
+def _pinned_result(shape, dtype):
+    """(page-locked tensor, its NumPy array) for a result of this shape; the array is what the
+    caller receives."""
+    import weakref
     import torch
-    return torch._C._storage_Use_Count(tensor.untyped_storage()._cdata)
-
-
-def _pinned_block(shape, dtype):
-    import torch
-    try:
-        blocks = _PINNED_BLOCKS.setdefault((shape, dtype), [])
-        for block, idle_count in blocks:
-            if _storage_users(block) == idle_count:
-                return block
-        block = torch.empty(shape, dtype=dtype, pin_memory=True)
-        if len(blocks) < _PINNED_BLOCKS_PER_SHAPE:
-            blocks.append((block, _storage_users(block)))
-        return block
-    except AttributeError:      # no way to tell whether a block is still in use: never reuse
-        return torch.empty(shape, dtype=dtype, pin_memory=True)
+    blocks = _PINNED_BLOCKS.setdefault((shape, dtype), [])
+    for entry in blocks:
+        block, alive = entry
+        if alive() is None:
+            array = block.numpy()
+            entry[1] = weakref.ref(array)
+            return block, array
+    block = torch.empty(shape, dtype=dtype, pin_memory=True)
+    array = block.numpy()
+    if len(blocks) < _PINNED_BLOCKS_PER_SHAPE:
+        blocks.append([block, weakref.ref(array)])
+    return block, array
 
 
 # Page-locked host arrays of at least twice this size are uploaded in pieces (a quarter of this
@@ -119,14 +119,61 @@ class DeviceArray:
     def copy_to_host(self):
         # through page-locked memory: a copy into a fresh pageable array runs at a few GB/s
         # (33 MB took 15 ms)
-        if self.tensor.numel() * self.tensor.element_size() < (1 << 20):
+        if self.tensor.numel() * self.tensor.element_size() < (1 << 16):
             return self.tensor.cpu().numpy()
-        host = _pinned_block(tuple(self.tensor.shape), self.tensor.dtype)
+        host, array = _pinned_result(tuple(self.tensor.shape), self.tensor.dtype)
         host.copy_(self.tensor)
-        return host.numpy()
+        return array
 
     def __len__(self):
         return self._tensor.shape[0]
+
+
+class LazyDeviceArray(DeviceArray):
+    """A device array that is only computed when somebody reads it (executor arrays that the
+    chosen kernel does not use, e.g. the level order next to a solver that ignores levels)."""
+
+    def __init__(self, make, length):
+        self._make, self._made, self._length = make, None, int(length)
+        self.arrival = None
+
+    @property
+    def _tensor(self):
+        if self._made is None:
+            self._made = self._make()
+        return self._made
+
+    @property
+    def shape(self):
+        return (self._length,)
+
+    def __len__(self):
+        return self._length
+
+
+class LazyHostArray:
+    """Host counterpart: turns into a NumPy array on first use (``np.asarray`` and friends)."""
+
+    def __init__(self, make):
+        self._make, self._made = make, None
+
+    def _array(self):
+        if self._made is None:
+            self._made = np.asarray(self._make())
+        return self._made
+
+    def __array__(self, dtype=None, copy=None):
+        array = self._array()
+        return array if dtype is None else array.astype(dtype, copy=False)
+
+    def __len__(self):
+        return len(self._array())
+
+    def __getitem__(self, item):
+        return self._array()[item]
+
+    def copy(self):
+        return self._array().copy()
 
 
 class TorchCUDA:
@@ -306,14 +353,28 @@ def execute_cuda_call(compiled_module, lowering, prepared_arguments, function_gl
     return _evaluate_host_epilogue(lowering, results, function_globals or {})
 
 
+_CODE_CACHE = {}
+
+
+def _compiled(statements, build, filename):
+    """Code object for a list of AST statements, compiled once (keyed by the list object, which
+    belongs to a lowering that lives as long as its decorated function)."""
+    entry = _CODE_CACHE.get(id(statements))
+    if entry is None or entry[0] is not statements:
+        if len(_CODE_CACHE) > 256:
+            _CODE_CACHE.clear()
+        entry = _CODE_CACHE[id(statements)] = (statements, compile(build(), filename=filename, mode="exec"))
+    return entry[1]
+
+
 def _evaluate_host_prelude(lowering, argument_values, function_globals):
     if not lowering.host_prelude:
         return {}
     namespace = dict(function_globals)
     namespace.update(argument_values)
-    module = ast.fix_missing_locations(
-        ast.Module(body=deepcopy(lowering.host_prelude), type_ignores=[]))
-    exec(compile(module, filename="<cuda-host-prelude>", mode="exec"), namespace, namespace)
+    code = _compiled(lowering.host_prelude, lambda: ast.fix_missing_locations(
+        ast.Module(body=deepcopy(lowering.host_prelude), type_ignores=[])), "<cuda-host-prelude>")
+    exec(code, namespace, namespace)
     missing = [name for name in lowering.lifted_variables if name not in namespace]
     if missing:
         raise CUDARuntimePreparationError(
@@ -327,15 +388,17 @@ def _evaluate_host_epilogue(lowering, result_values, function_globals):
         return None
     namespace = dict(function_globals)
     namespace.update(result_values)
-    helper = ast.FunctionDef(
-        name="_lcd_host_epilogue",
-        args=ast.arguments(posonlyargs=[], args=[], kwonlyargs=[], kw_defaults=[], defaults=[]),
-        body=deepcopy(lowering.host_epilogue), decorator_list=[], returns=None,
-        type_comment=None)
-    if hasattr(helper, "type_params"):
-        helper.type_params = []
-    module = ast.fix_missing_locations(ast.Module(body=[helper], type_ignores=[]))
-    exec(compile(module, filename="<cuda-host-epilogue>", mode="exec"), namespace, namespace)
+
+    def build():
+        helper = ast.FunctionDef(
+            name="_lcd_host_epilogue",
+            args=ast.arguments(posonlyargs=[], args=[], kwonlyargs=[], kw_defaults=[], defaults=[]),
+            body=deepcopy(lowering.host_epilogue), decorator_list=[], returns=None,
+            type_comment=None)
+        if hasattr(helper, "type_params"):
+            helper.type_params = []
+        return ast.fix_missing_locations(ast.Module(body=[helper], type_ignores=[]))
+    exec(_compiled(lowering.host_epilogue, build, "<cuda-host-epilogue>"), namespace, namespace)
     try:
         return namespace["_lcd_host_epilogue"]()
     finally:
@@ -344,7 +407,29 @@ def _evaluate_host_epilogue(lowering, result_values, function_globals):
         namespace.clear()
 
 
+_NAME_CACHE = {}
+
+
+def _cached_names(kind, statements, compute):
+    """Name lists of a statement list, walked once (keyed like the compiled code above)."""
+    key = (kind, id(statements))
+    entry = _NAME_CACHE.get(key)
+    if entry is None or entry[0] is not statements:
+        if len(_NAME_CACHE) > 512:
+            _NAME_CACHE.clear()
+        entry = _NAME_CACHE[key] = (statements, tuple(compute(statements)))
+    return list(entry[1])
+
+
 def _returned_names(statements):
+    return _cached_names("returned", statements, _walk_returned_names)
+
+
+def _stored_names(statements):
+    return _cached_names("stored", statements, _walk_stored_names)
+
+
+def _walk_returned_names(statements):
     names = []
     for statement in statements:
         for node in ast.walk(statement):
@@ -356,7 +441,7 @@ def _returned_names(statements):
     return names
 
 
-def _stored_names(statements):
+def _walk_stored_names(statements):
     names = []
     for statement in statements:
         for node in ast.walk(statement):

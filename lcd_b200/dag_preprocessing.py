@@ -65,7 +65,9 @@ class WarpTaskExecutionData:
 
 
 def _is_device_dag(value):
-    return hasattr(value, "dag_ptr") and hasattr(value, "wavefront_ptr") and hasattr(value, "level")
+    # (asked of the class: reading the level arrays of a capped device DAG would build them)
+    kind = type(value)
+    return hasattr(value, "dag_ptr") and hasattr(kind, "wavefront_ptr") and hasattr(kind, "level")
 
 
 def preprocess_dag_output(dag_successors, scheduling_data, execution_mode):
@@ -197,16 +199,21 @@ def preprocess_warp_tasks(dag_successors, wavefront_list=None, band_width=1, edg
     if _is_device_dag(dag_successors):
         dag = dag_successors
         if band_width != 1:
-            dag_ptr = dag.dag_ptr.cpu().numpy()
-            dag_index = dag.dag_index.cpu().numpy()
-            nodes = dag.wavefronts.cpu().numpy()
-            task_nodes, task_ptr, band_ptr = _band_chains(nodes, dag.wavefront_ptr_host, dag_ptr,
-                                                          dag_index, band_width)
+            from . import ops
+            task_nodes, task_ptr, band_ptr = ops.band_chains(dag, band_width)
+            band_ptr = band_ptr.cpu().numpy()          # band offsets stay on the host
         else:
             import torch
-            task_nodes = dag.wavefronts
-            task_ptr = torch.arange(dag.n + 1, dtype=torch.int32, device=dag.wavefronts.device)
-            band_ptr = dag.wavefront_ptr_host.copy()
+            task_ptr = torch.arange(dag.n + 1, dtype=torch.int32, device=dag.dep_count.device)
+            if getattr(dag, "capped", False):
+                # a deep DAG whose level sets were not built (the chain solver reads none): the
+                # level order is computed only if somebody asks for it
+                from .cuda_runtime import LazyDeviceArray, LazyHostArray
+                task_nodes = LazyDeviceArray(lambda: dag.wavefronts, dag.n)
+                band_ptr = LazyHostArray(lambda: dag.wavefront_ptr_host.copy())
+            else:
+                task_nodes = dag.wavefronts
+                band_ptr = dag.wavefront_ptr_host.copy()
         count = dag.dep_count if edge_count is None else edge_count
         return WarpTaskExecutionData(task_nodes=task_nodes, task_ptr=task_ptr, band_ptr=band_ptr,
                                      dep_count=count.clone(), initial_dep_count=count,
@@ -234,36 +241,35 @@ def preprocess_warp_tasks(dag_successors, wavefront_list=None, band_width=1, edg
 
 
 def _band_chains(nodes, level_ptr, dag_ptr, dag_index, band_width):
-    """Connected components (in order of first appearance) of each band of levels."""
+    """Tasks for ``band_width`` > 1 from host arrays (the list form of the API): inside every band
+    of ``band_width`` levels, the connected components of the DAG edges that stay in the band,
+    listed by their first node in level order.  SciPy's connected-components labelling does the
+    grouping; components are then ranked by the position of their first node."""
+    from scipy.sparse import coo_matrix
+    from scipy.sparse.csgraph import connected_components
+    nodes = np.asarray(nodes, dtype=np.int64)
+    level_ptr = np.asarray(level_ptr, dtype=np.int64)
+    n = len(nodes)
     level_count = len(level_ptr) - 1
-    task_nodes, task_ptr, band_ptr = [], [0], [0]
-    for first in range(0, level_count, band_width):
-        last = min(first + band_width, level_count)
-        band = [int(v) for v in nodes[level_ptr[first]:level_ptr[last]]]
-        position_of = {node: position for position, node in enumerate(band)}
-        parent = list(range(len(band)))
-
-        def find(position):
-            root = position
-            while parent[root] != root:
-                root = parent[root]
-            while parent[position] != root:
-                parent[position], position = root, parent[position]
-            return root
-
-        for position, node in enumerate(band):
-            for successor in dag_index[dag_ptr[node]:dag_ptr[node + 1]]:
-                other = position_of.get(int(successor))
-                if other is not None:
-                    a, b = find(position), find(other)
-                    if a != b:
-                        parent[b] = a
-        chains = {}
-        for position, node in enumerate(band):
-            chains.setdefault(find(position), []).append(node)
-        for chain in chains.values():
-            task_nodes.extend(chain)
-            task_ptr.append(len(task_nodes))
-        band_ptr.append(len(task_ptr) - 1)
-    return (np.asarray(task_nodes, dtype=np.int32), np.asarray(task_ptr, dtype=np.int32),
-            np.asarray(band_ptr, dtype=np.int32))
+    n_bands = -(-level_count // band_width) if level_count else 0
+    if n == 0:
+        return (np.zeros(0, np.int32), np.zeros(1, np.int32), np.zeros(n_bands + 1, np.int32))
+    position = np.empty(n, dtype=np.int64)
+    position[nodes] = np.arange(n)
+    level_of_position = np.repeat(np.arange(level_count), np.diff(level_ptr))
+    band_of_node = (level_of_position // band_width)[position]
+    source = np.repeat(np.arange(n), np.diff(np.asarray(dag_ptr, dtype=np.int64)))
+    target = np.asarray(dag_index, dtype=np.int64)
+    inside = band_of_node[source] == band_of_node[target]
+    graph = coo_matrix((np.ones(int(inside.sum()), dtype=np.int8),
+                        (position[source[inside]], position[target[inside]])), shape=(n, n))
+    _, component = connected_components(graph, directed=False)
+    first = np.full(component.max() + 1, n, dtype=np.int64)
+    np.minimum.at(first, component, np.arange(n))
+    label = first[component]                       # position of the component's first node
+    order = np.argsort(label, kind="stable")
+    heads = np.flatnonzero(np.r_[True, label[order][1:] != label[order][:-1]])
+    task_ptr = np.r_[heads, n]
+    band_first = level_ptr[np.minimum(np.arange(n_bands + 1) * band_width, level_count)]
+    band_ptr = np.searchsorted(heads, band_first, side="left")
+    return (nodes[order].astype(np.int32), task_ptr.astype(np.int32), band_ptr.astype(np.int32))

@@ -168,13 +168,23 @@ def parallel(**kwargs):
             n = values.get(roles.get("n"))
             return int(n) if n is not None else structure[roles["ptr"]].numel() - 1
 
-        def device_dag(values, structure):
+        def device_dag(values, structure, may_cap=False):
             from . import ops
+            from .scheduler import FALLBACK_ARCH_CONSTANTS
             ptr, idx = structure[roles["ptr"]], structure[roles["idx"]]
             if operator == "ilu0_csc":
                 view = ops.csc_row_view(ptr, idx)
                 ptr, idx = view.Ap, view.Ai
-            return ops.dag_build(dag_operator, ptr, idx, n=node_count(values, structure))
+            n = node_count(values, structure)
+            # A sync-free CSR solve on a deep DAG goes to the chain solver, which reads no level
+            # sets: stop the level propagation (one hand-off per level, the slow part of the
+            # inspector on such matrices) once the DAG is known to be deep enough for that choice.
+            cap = 0
+            if (may_cap and operator in CHAIN_CAPABLE_OPERATORS and band_width == 1
+                    and n >= FALLBACK_ARCH_CONSTANTS.chain_min_rows
+                    and (fixed_schedule is None or fixed_schedule.execution_mode == SYNC_FREE)):
+                cap = max(n // 64, 1)
+            return ops.dag_build(dag_operator, ptr, idx, n=n, level_cap=cap)
 
         def build_dag(*args, **call_kwargs):
             """(successor lists, dep_count) -- or wavefront lists when the fixed mode is
@@ -205,7 +215,7 @@ def parallel(**kwargs):
             lookup_arguments = dict(values)
             lookup_arguments.update(structure)
             lookups = materialize_structural_lookups(structural_lookups, lookup_arguments)
-            dag = device_dag(values, structure)
+            dag = device_dag(values, structure, may_cap=True)
             features = None
             schedule = fixed_schedule
             if schedule is None:
@@ -222,13 +232,13 @@ def parallel(**kwargs):
                 schedule = scheduler.schedule(features, schedule_space)
             data = attach_auxiliary_values(execution_data_for(schedule, dag), lookups)
             return SchedulePlan(schedule=schedule, execution_data=data, features=features,
-                                rows=dag.n, levels=dag.n_levels, dag=dag)
+                                rows=dag.n, levels=dag.levels_at_least, dag=dag)
 
         def plan_for(values, structure):
             from . import ops
-            fingerprint = tuple(
-                (name,) + ops.fingerprint(structure[name]) for name in structure_names
-            ) + (node_count(values, structure),)
+            prints = ops.fingerprints([structure[name] for name in structure_names])
+            fingerprint = tuple((name,) + found for name, found in zip(structure_names, prints)) + (
+                node_count(values, structure),)
             plan = schedule_plans.get(fingerprint)
             if plan is None:
                 plan = create_schedule_plan(values, structure)
@@ -270,7 +280,7 @@ def parallel(**kwargs):
                     launch_values[name] = DeviceArray(tensor)
             prepared = prepare_cuda_arguments(
                 lowering=lowering, argument_values=launch_values,
-                execution_data=_fresh_counters(plan.execution_data),
+                execution_data=plan.execution_data,      # (a launcher that consumes counters copies them)
                 function_globals=function.__globals__, cuda_module=module.namespace["cuda"])
             prepared.hints = {"rows": plan.rows, "levels": plan.levels, "dag": plan.dag,
                               "arch": getattr(scheduler, "_arch_constants", None),
@@ -309,13 +319,3 @@ def parallel(**kwargs):
         return wrapper
 
     return decorator
-
-
-def _fresh_counters(execution_data):
-    """The kernels consume ``dep_count``; every call gets its own copy of the
-    pristine counters (the reference re-uploads them per call)."""
-    from dataclasses import replace
-    initial = getattr(execution_data, "initial_dep_count", None)
-    if initial is None or not hasattr(initial, "clone"):
-        return execution_data
-    return replace(execution_data, dep_count=initial.clone())

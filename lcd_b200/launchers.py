@@ -97,7 +97,7 @@ def bind(lowering):
         """The one-block solver's plan for this pattern (kept with the schedule plan), or None
         when the matrix is not small, has rows it does not serve, or is better off elsewhere."""
         dag, cache = hints.get("dag"), hints.setdefault("cache", {})
-        if dag is None or "small_plan" in cache:
+        if dag is None or dag.capped or "small_plan" in cache:    # (capped: deep, level sets not built)
             return cache.get("small_plan")
         plan = None
         n, nnz = Ap.numel() - 1, Ai.numel()
@@ -112,7 +112,7 @@ def bind(lowering):
 
     def ordered_plan_for(Ap, Ai, hints):
         dag, cache = hints.get("dag"), hints.setdefault("cache", {})
-        if dag is None or "ordered_plan" in cache:
+        if dag is None or dag.capped or "ordered_plan" in cache:
             return cache.get("ordered_plan")
         plan = None
         if ordered_solver_preferred(Ap.numel() - 1, dag.n_levels, average_row(Ap, Ai)):
@@ -260,8 +260,9 @@ def bind(lowering):
             return
         if lowering.execution_mode == "sync_free":
             if lowering.dependence_protocol == PUSH_DEPENDENCE:
-                # push protocol: the counters already hold edge multiplicities
-                dep = as_tensor(v["dep_count"], torch.int32)
+                # push protocol: the counters already hold edge multiplicities; the kernel
+                # consumes them, the plan keeps the pristine ones
+                dep = as_tensor(v["dep_count"], torch.int32).clone()
             else:
                 # counter protocol counts distinct predecessors; the push kernel
                 # decrements once per stored entry, so recount on the device
@@ -273,14 +274,20 @@ def bind(lowering):
             ops.sptrsv_wavefront("csc_upper" if lowering.upper else "csc_lower", Ap, Ai, Ax, b,
                                  nodes, ptr_dev, ptr_host, x, mode=mode, lanes=lanes, task_ptr=tasks)
 
-    def ilu0_csr(*args):
+    def ilu0_csr(*args, _hints=None):
         v = split(args)
         Ap, Ai, Ax = matrix(v)
         lookup = [name for name in names if name.startswith("_lcd_lookup_position_")]
         pos = as_tensor(v[lookup[0]], torch.int32) if lookup else ops.diag_positions(Ap, Ai)
         lanes = 0 if lowering.thread_loop_iterator is not None else 1
+        dag = (_hints or {}).get("dag")
         if lowering.execution_mode == "sync_free":
-            ops.spilu0_csr(Ap, Ai, Ax, pos, mode="sync_free", lanes=lanes)
+            if dag is not None and dag.n_levels > 0 and dag.n / dag.n_levels >= 8:
+                # rows in the order of the level sets: the rows of a level run side by side
+                # (by index, a grid matrix keeps one grid line in flight)
+                ops.spilu0_csr(Ap, Ai, Ax, pos, mode="ordered", wavefronts=dag.wavefronts, lanes=lanes)
+            else:
+                ops.spilu0_csr(Ap, Ai, Ax, pos, mode="sync_free", lanes=lanes)
         else:
             nodes, _, ptr_host = wavefront_arrays(v)
             ops.spilu0_csr(Ap, Ai, Ax, pos, mode="wavefront", wavefronts=nodes,
@@ -296,8 +303,12 @@ def bind(lowering):
         view = cache.get("csc_row_view")
         if view is None or view.Ap.device != Ap.device:
             view = cache["csc_row_view"] = ops.csc_row_view(Ap, Ai)
+        dag = (_hints or {}).get("dag")
         if lowering.execution_mode == "sync_free":
-            ops.spilu0_csc(Ap, Ai, Ax, view, mode="sync_free")
+            if dag is not None and dag.n_levels > 0 and dag.n / dag.n_levels >= 8:
+                ops.spilu0_csc(Ap, Ai, Ax, view, mode="ordered", wavefronts=dag.wavefronts)
+            else:
+                ops.spilu0_csc(Ap, Ai, Ax, view, mode="sync_free")
         else:
             nodes, _, ptr_host = wavefront_arrays(v)
             ops.spilu0_csc(Ap, Ai, Ax, view, mode="wavefront", wavefronts=nodes,
@@ -310,7 +321,7 @@ def bind(lowering):
     if launcher is None:
         raise CUDALoweringError(f"no native kernel for operator {lowering.operator!r}")
     launcher.__name__ = lowering.launcher_name
-    launcher.accepts_hints = launcher in (sptrsv_csr, sptrsv_csc, gauss_seidel, ilu0_csc)
+    launcher.accepts_hints = launcher in (sptrsv_csr, sptrsv_csc, gauss_seidel, ilu0_csr, ilu0_csc)
 
     def kernel(*args, **kwargs):
         raise CUDALoweringError(

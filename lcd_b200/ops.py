@@ -26,7 +26,14 @@ def _op_code(op):
     return OPS[op] if isinstance(op, str) else int(op)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream():
+    """Handle of the current CUDA stream (the raw-handle getter when this torch has it:
+    ``torch.cuda.current_stream()`` builds a Stream object per call)."""
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(torch.cuda.current_device()))
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
@@ -54,22 +61,44 @@ def to_device(array, dtype=None, device="cuda"):
     return torch.from_numpy(a).to(device, non_blocking=False)
 
 
-@dataclass
 class DeviceDag:
-    """Outputs of the on-device DAG build (all int32 device tensors)."""
+    """Outputs of the on-device DAG build (all int32 device tensors).
 
-    n: int
-    op: int
-    dep_count: torch.Tensor
-    edge_count: torch.Tensor
-    dag_ptr: torch.Tensor
-    dag_index: torch.Tensor
-    level: torch.Tensor
-    wavefronts: torch.Tensor
-    wavefront_ptr: torch.Tensor
-    n_edges: int
-    n_levels: int
-    _wavefront_ptr_host: np.ndarray | None = None
+    Built with a level cap that was reached (``capped``), the level arrays - ``level``,
+    ``wavefronts``, ``wavefront_ptr``, ``n_levels`` - are not there yet; reading one of them runs
+    the full build once.  ``levels_at_least`` is a lower bound that never triggers that."""
+
+    def __init__(self, n, op, dep_count, edge_count, dag_ptr, dag_index, n_edges, level, wavefronts,
+                 wavefront_ptr, n_levels, capped_at=0, complete=None):
+        self.n, self.op = n, op
+        self.dep_count, self.edge_count = dep_count, edge_count
+        self.dag_ptr, self.dag_index, self.n_edges = dag_ptr, dag_index, n_edges
+        self._level, self._wavefronts, self._wavefront_ptr = level, wavefronts, wavefront_ptr
+        self._n_levels = n_levels
+        self._wavefront_ptr_host = None
+        self.capped_at = int(capped_at)
+        self._complete = complete
+
+    @property
+    def capped(self):
+        return self.capped_at > 0
+
+    @property
+    def levels_at_least(self):
+        return self.capped_at + 1 if self.capped else self._n_levels
+
+    def _levels(self):
+        if self.capped:
+            full = self._complete()
+            self._level, self._wavefronts = full._level, full._wavefronts
+            self._wavefront_ptr, self._n_levels = full._wavefront_ptr, full._n_levels
+            self.capped_at, self._complete = 0, None
+        return self
+
+    level = property(lambda self: self._levels()._level)
+    wavefronts = property(lambda self: self._levels()._wavefronts)
+    wavefront_ptr = property(lambda self: self._levels()._wavefront_ptr)
+    n_levels = property(lambda self: self._levels()._n_levels)
 
     @property
     def wavefront_ptr_host(self):
@@ -78,8 +107,10 @@ class DeviceDag:
         return self._wavefront_ptr_host
 
 
-def dag_build(op, ptr_t, idx_t, n=None, timeout_ms=0):
-    """Dependence DAG, level sets and topological order of one operator."""
+def dag_build(op, ptr_t, idx_t, n=None, timeout_ms=0, level_cap=0):
+    """Dependence DAG, level sets and topological order of one operator.  ``level_cap`` > 0 stops
+    the level propagation (the sequential part) once a node reaches that level: the result then
+    is ``capped`` and completes itself when its level arrays are read."""
     op = _op_code(op)
     _require(ptr_t, torch.int32, "ptr")
     _require(idx_t, torch.int32, "idx")
@@ -100,14 +131,40 @@ def dag_build(op, ptr_t, idx_t, n=None, timeout_ms=0):
     wptr = torch.empty(n + 1, **i32)
     n_edges = ctypes.c_int64(0)
     n_levels = ctypes.c_int32(0)
-    rc = lib.lcd_dag_build(op, n, ptr(ptr_t), ptr(idx_t), nnz, ptr(dep), ptr(edge), ptr(dag_ptr),
-                           ptr(dag_index), ctypes.byref(n_edges), ptr(level), ptr(waves),
-                           ptr(wptr), ctypes.byref(n_levels), ptr(ws), need.value,
-                           int(timeout_ms), _stream())
+    rc = lib.lcd_dag_build_capped(op, n, ptr(ptr_t), ptr(idx_t), nnz, ptr(dep), ptr(edge), ptr(dag_ptr),
+                                  ptr(dag_index), ctypes.byref(n_edges), ptr(level), ptr(waves),
+                                  ptr(wptr), ctypes.byref(n_levels), int(level_cap), ptr(ws), need.value,
+                                  int(timeout_ms), _stream())
     check(rc, "lcd_dag_build")
     del ws
-    return DeviceDag(n, op, dep, edge, dag_ptr, dag_index[:n_edges.value], level, waves,
-                     wptr[:n_levels.value + 1], n_edges.value, n_levels.value)
+    if n_levels.value < 0:          # the cap was reached: level arrays on demand
+        return DeviceDag(n, op, dep, edge, dag_ptr, dag_index[:n_edges.value], n_edges.value, None, None,
+                         None, 0, capped_at=-n_levels.value,
+                         complete=lambda: dag_build(op, ptr_t, idx_t, n=n, timeout_ms=timeout_ms))
+    return DeviceDag(n, op, dep, edge, dag_ptr, dag_index[:n_edges.value], n_edges.value, level, waves,
+                     wptr[:n_levels.value + 1], n_levels.value)
+
+
+def band_chains(dag, band_width):
+    """(task_nodes, task_ptr, band_ptr) of the warp executor's tasks for ``band_width`` > 1:
+    int32 device tensors, element-wise the reference's ``_band_chains``."""
+    lib = nat.load()
+    n, dev = dag.n, dag.wavefronts.device
+    need = ctypes.c_int64(0)
+    check(lib.lcd_band_chains_workspace_bytes(n, ctypes.byref(need)), "lcd_band_chains_workspace_bytes")
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    n_bands = (dag.n_levels + band_width - 1) // band_width
+    task_nodes = torch.empty(max(n, 1), **i32)
+    task_ptr = torch.empty(n + 1, **i32)
+    band_ptr = torch.empty(n_bands + 1, **i32)
+    n_tasks = ctypes.c_int32(0)
+    check(lib.lcd_band_chains(n, ptr(dag.dag_ptr), ptr(dag.dag_index), ptr(dag.level),
+                              ptr(dag.wavefronts), ptr(dag.wavefront_ptr), dag.n_levels,
+                              int(band_width), ptr(task_nodes), ptr(task_ptr), ptr(band_ptr),
+                              ctypes.byref(n_tasks), ptr(ws), need.value, _stream()),
+          "lcd_band_chains")
+    return task_nodes[:n], task_ptr[:n_tasks.value + 1], band_ptr
 
 
 def diag_positions(ptr_t, idx_t, status=None):
@@ -590,6 +647,30 @@ def spilu0_csc(Ap, Ai, Ax, view=None, *, mode="sync_free", wavefronts=None, wave
 
 
 _checksum_scratch = {}
+_FINGERPRINT_SLOTS = 8
+
+
+def fingerprints(tensors):
+    """Fingerprints of up to eight int32 device tensors with one synchronisation: the checksum
+    kernels are queued back to back and their results come back in one copy."""
+    tensors = list(tensors)
+    if not tensors:
+        return []
+    if len(tensors) > _FINGERPRINT_SLOTS:
+        return [fingerprint(t) for t in tensors]
+    device = tensors[0].device
+    key = (device, "batch")
+    scratch = _checksum_scratch.get(key)
+    if scratch is None:
+        scratch = _checksum_scratch[key] = torch.zeros(2 * _FINGERPRINT_SLOTS, dtype=torch.int64, device=device)
+    lib = nat.load()
+    for k, t in enumerate(tensors):
+        _require(t, torch.int32, "fingerprint input")
+        check(lib.lcd_checksum_i32(ptr(t), t.numel(), ctypes.c_void_p(scratch.data_ptr() + 16 * k), None,
+                                   _stream()), "lcd_checksum_i32")
+    words = scratch[:2 * len(tensors)].cpu().tolist()       # one copy, one synchronisation
+    mask = (1 << 64) - 1
+    return [(t.numel(), words[2 * k] & mask, words[2 * k + 1] & mask) for k, t in enumerate(tensors)]
 
 
 def fingerprint(t):

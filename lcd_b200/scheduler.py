@@ -372,8 +372,14 @@ def extract_workload_features(dag, wavefront_list, argument_values, function_pro
     """Features of one concrete input.  ``dag`` is either the reference's list of
     successor lists or a device DAG (then everything is read from its sizes)."""
     if hasattr(dag, "n_edges"):
-        rows, edges, levels = dag.n, dag.n_edges, dag.n_levels
-        widths = np.diff(dag.wavefront_ptr_host) if levels else np.zeros(0, dtype=np.int64)
+        if getattr(dag, "capped", False):
+            # deep DAG whose level sets were not built: a lower bound of the level count is all
+            # the cost model needs to send it to the sync-free schedules
+            rows, edges, levels = dag.n, dag.n_edges, dag.levels_at_least
+            widths = np.asarray([max(1, rows // max(levels, 1))], dtype=np.int64)
+        else:
+            rows, edges, levels = dag.n, dag.n_edges, dag.n_levels
+            widths = np.diff(dag.wavefront_ptr_host) if levels else np.zeros(0, dtype=np.int64)
     else:
         rows = len(dag)
         edges = sum(len(s) for s in dag)

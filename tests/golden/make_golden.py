@@ -109,10 +109,30 @@ def write_ilu0_csc(out_dir):
         print("wrote ilu0_csc", name)
 
 
+def write_band_chains(out_dir):
+    """Tasks of the warp executor with band_width > 1: the reference's preprocess_warp_tasks
+    (compiler/dag_preprocessing.py:207-298) on the successor lists and level sets of its own
+    inspector, for band widths 2, 3 and 5."""
+    out = {}
+    for name, tri in triangular_cases().items():
+        Ap, Ai, Ax = tri.csr_arrays()
+        with contextlib.redirect_stdout(_sink):
+            succ, dep = ref_ops.csr_warp_syncfree.build_dag(Ap, Ai, Ax, tri.b, tri.n)
+        waves = wavefronts_from_dag(succ, dep)
+        for width in (2, 3, 5):
+            data = preprocess_warp_tasks(succ, waves, band_width=width)
+            for field in ("task_nodes", "task_ptr", "band_ptr"):
+                out[f"{name}/w{width}/{field}"] = np.asarray(getattr(data, field))
+    np.savez_compressed(os.path.join(out_dir, "band_chains.npz"), **out)
+    print("wrote band chains", len(out))
+
+
 def main():
     out_dir = HERE
     if sys.argv[1:] == ["ilu0_csc"]:        # only these fixtures
         return write_ilu0_csc(out_dir)
+    if sys.argv[1:] == ["band_chains"]:
+        return write_band_chains(out_dir)
     # ---- SpTRSV, lower, CSR and CSC -------------------------------------
     for name, tri in triangular_cases().items():
         out = {}
@@ -245,6 +265,7 @@ def main():
         print("wrote ilu0", name)
 
     write_ilu0_csc(out_dir)
+    write_band_chains(out_dir)
 
     # ---- supernodal solve ------------------------------------------------
     source = open(os.path.join(REF, "benchmark", "sptrsv_supernodal.py")).read()

@@ -107,9 +107,10 @@ def test_decorated_band_chains(cuda, name):
     data = od.csr_warp_wavefront_band2.schedule_plan(*csr).execution_data
     succ, waves = od.simple_sptrsv_csr.build_dag(*csr)
     want = preprocess_warp_tasks(succ, waves, band_width=2)               # list form (host logic tests pin it)
-    np.testing.assert_array_equal(np.asarray(data.task_nodes), want.task_nodes)
-    np.testing.assert_array_equal(np.asarray(data.task_ptr), want.task_ptr)
-    np.testing.assert_array_equal(np.asarray(data.band_ptr), want.band_ptr)
+    to_host = lambda a: a.cpu().numpy() if hasattr(a, "cpu") else np.asarray(a)   # built on the device
+    np.testing.assert_array_equal(to_host(data.task_nodes), want.task_nodes)
+    np.testing.assert_array_equal(to_host(data.task_ptr), want.task_ptr)
+    np.testing.assert_array_equal(to_host(data.band_ptr), want.band_ptr)
     assert len(data.task_ptr) - 1 < n or len(waves) == n                  # chains do form
     x = od.csr_warp_wavefront_band2(*csr)
     np.testing.assert_allclose(x, g["x_csr"], rtol=1e-10, atol=1e-12)

@@ -306,3 +306,65 @@ def test_partition_need_mask_matches_numpy(cuda):
                 nat.ptr(need), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
             assert rc == 0
             np.testing.assert_array_equal(host(need)[:n], want)
+
+
+@pytest.mark.parametrize("name", ["lap2d_g8", "band_n300", "band_n600", "lap3d_g5"])
+def test_band_chains_on_device_match_reference_fixture(cuda, name):
+    """lcd_band_chains against the arrays the reference's preprocess_warp_tasks produced
+    (band widths 2, 3, 5), and on a larger grid against the list form."""
+    from lcd_b200 import ops
+    chains, g = golden("band_chains"), golden("sptrsv_" + name)
+    dag = ops.dag_build("csr_lower", dev(g["csr_Ap"], np.int32, cuda), dev(g["csr_Ai"], np.int32, cuda))
+    for width in (2, 3, 5):
+        nodes, task_ptr, band_ptr = ops.band_chains(dag, width)
+        np.testing.assert_array_equal(host(nodes), chains[f"{name}/w{width}/task_nodes"])
+        np.testing.assert_array_equal(host(task_ptr), chains[f"{name}/w{width}/task_ptr"])
+        np.testing.assert_array_equal(host(band_ptr), chains[f"{name}/w{width}/band_ptr"])
+
+
+def test_band_chains_on_device_larger(cuda, oracle):
+    from lcd_b200 import dag_preprocessing as dp, generators as gen, ops
+    for tri in (gen.laplacian2d_tril(70, seed=1), gen.random_band_lower(20_000, seed=5, mean_degree=5.0, band=30)):
+        Ap, Ai, _ = tri.csr_arrays()
+        dag = ops.dag_build("csr_lower", dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda))
+        ref = oracle.dag_build("csr_lower", Ap, Ai)
+        for width in (2, 4, 7, 1000):
+            want = dp._band_chains(ref.wavefronts, ref.wavefront_ptr, ref.dag_ptr, ref.dag_index, width)
+            got = ops.band_chains(dag, width)
+            for a, b in zip(got, want):
+                np.testing.assert_array_equal(host(a), b)
+
+
+def test_capped_dag_build_completes_on_demand(cuda, oracle):
+    """A level cap stops the propagation on a deep DAG (the other arrays are complete); reading a
+    level array finishes the build, element-wise as without a cap.  A shallow DAG is unaffected."""
+    from lcd_b200 import generators as gen, ops
+    deep = gen.random_band_lower(60_000, seed=1, mean_degree=15.0, band=64)
+    Ap, Ai, _ = deep.csr_arrays()
+    dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+    ref = oracle.dag_build("csr_lower", Ap, Ai)
+    levels = len(ref.wavefront_ptr) - 1
+    capped = ops.dag_build("csr_lower", dAp, dAi, level_cap=500)
+    assert levels > 501 and capped.capped and capped.levels_at_least == 501
+    np.testing.assert_array_equal(host(capped.dep_count), ref.dep_count)
+    np.testing.assert_array_equal(host(capped.dag_ptr), ref.dag_ptr)
+    np.testing.assert_array_equal(host(capped.dag_index), ref.dag_index)
+    assert capped.capped                                  # still: nothing asked for levels yet
+    np.testing.assert_array_equal(host(capped.wavefronts), ref.wavefronts)
+    assert not capped.capped and capped.n_levels == levels
+    np.testing.assert_array_equal(host(capped.level), ref.level)
+    np.testing.assert_array_equal(host(capped.wavefront_ptr), ref.wavefront_ptr)
+    shallow = gen.laplacian2d_tril(30, seed=0)
+    Sp, Si, _ = shallow.csr_arrays()
+    d = ops.dag_build("csr_lower", dev(Sp, np.int32, cuda), dev(Si, np.int32, cuda), level_cap=500)
+    assert not d.capped and d.n_levels == 59
+    # through the decorator: a deep matrix is solved without its level sets ever being built
+    import ops_decorated as od
+    big = gen.random_band_lower(40_000, seed=3, mean_degree=15.0, band=64)
+    Bp, Bi, Bx = big.csr_arrays()
+    x = od.csr_warp_syncfree(Bp, Bi, Bx, big.b, big.n)
+    assert csr_residual(Bp, Bi, Bx, x, big.b) <= RESIDUAL_TOL
+    plan = od.csr_warp_syncfree.schedule_plan(Bp, Bi, Bx, big.b, big.n)
+    assert plan.dag.capped and plan.levels == big.n // 64 + 1
+    waves = plan.execution_data.task_nodes                # asking for them builds them
+    np.testing.assert_array_equal(host(waves.tensor), oracle.dag_build("csr_lower", Bp, Bi).wavefronts)

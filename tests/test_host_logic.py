@@ -113,6 +113,22 @@ def test_band_chains_group_connected_nodes():
     np.testing.assert_array_equal(tasks.band_ptr, [0, 2, 3])
 
 
+@pytest.mark.parametrize("name", ["lap2d_g8", "band_n300", "band_n600", "lap3d_g5"])
+def test_band_chains_list_form_matches_reference_fixture(name):
+    """Band widths 2, 3 and 5 against what the reference's preprocess_warp_tasks returned for the
+    successor lists and level sets of its own inspector."""
+    from lcd_b200 import dag_preprocessing as dp
+    chains, g = golden("band_chains"), golden("sptrsv_" + name)
+    ptr, idx = g["csr_warp_syncfree/succ_ptr"], g["csr_warp_syncfree/succ_idx"]
+    succ = [idx[ptr[v]:ptr[v + 1]].tolist() for v in range(len(ptr) - 1)]
+    lp, li = g["levels_ptr"], g["levels_idx"]
+    waves = [li[lp[k]:lp[k + 1]].tolist() for k in range(len(lp) - 1)]
+    for width in (2, 3, 5):
+        data = dp.preprocess_warp_tasks(succ, waves, band_width=width)
+        for field in ("task_nodes", "task_ptr", "band_ptr"):
+            np.testing.assert_array_equal(getattr(data, field), chains[f"{name}/w{width}/{field}"])
+
+
 # ---- scheduler -----------------------------------------------------------------
 def test_schedule_space_matches_reference_rules():
     from lcd_b200 import scheduler as sc
@@ -396,14 +412,17 @@ def test_pinned_result_blocks_are_reused_only_when_released(monkeypatch):
     monkeypatch.setattr(torch, "empty", lambda *a, **k: plain_empty(
         *a, **{name: v for name, v in k.items() if name != "pin_memory"}))
     monkeypatch.setattr(rt, "_PINNED_BLOCKS", {})
-    first = rt._pinned_block((16,), torch.float64).numpy()
-    second = rt._pinned_block((16,), torch.float64).numpy()
+    first = rt._pinned_result((16,), torch.float64)[1]
+    second = rt._pinned_result((16,), torch.float64)[1]
     address = lambda array: array.__array_interface__["data"][0]
     assert address(first) != address(second)
     view = first[4:]
     del first
-    third = rt._pinned_block((16,), torch.float64).numpy()      # the view keeps the first block busy
+    third = rt._pinned_result((16,), torch.float64)[1]          # the view keeps the first block busy
     assert address(third) not in (address(view) - 32, address(second))
     released = address(view) - 32
     del view
-    assert address(rt._pinned_block((16,), torch.float64).numpy()) == released
+    assert address(rt._pinned_result((16,), torch.float64)[1]) == released
+    as_tensor = torch.from_numpy(second)                         # a tensor made from the array counts too
+    del second
+    assert address(rt._pinned_result((16,), torch.float64)[1]) != as_tensor.data_ptr()
