@@ -409,7 +409,12 @@ int lcd_sptrsv_small(int csc, int32_t n, int32_t entries, const double *Ax, cons
  * `done`, n ints, zeroed by the call), 1 = per-level launches over wavefronts,
  * 2 = sync-free with the rows handed out in the order of `wavefronts` (needs `done` and
  * `wavefronts`; one launch, rows of a level run side by side, no barrier between levels).
+ * LCD_ILU0_SKIP_STORED_ZEROS may be added to the mode: an explicitly stored zero of a pivot row
+ * then causes no update, which is what the column loop does (compiler/demo/spilu0.py:69-75:
+ * `if u_kj != 0.0`); the row loop (:36-44) updates with l_ik * 0.  The two differ only for
+ * non-finite multipliers and in the sign of zero.
  */
+#define LCD_ILU0_SKIP_STORED_ZEROS 8
 int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, double *Ax,
                    const int32_t *diag_pos, int mode, int32_t *done,
                    const int32_t *wavefronts, const int32_t *wavefront_ptr_host,
@@ -439,7 +444,7 @@ int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, const int32
                           int32_t timeout_ms, void *stream, int *status_host);
 /*
  * ILU0 on CSC storage (compiler/demo/spilu0.py:50-82, the right-looking column loop) is served by
- * the row kernels: the column form updates the same entries in the same order, so the values are
+ * the row kernels (mode + LCD_ILU0_SKIP_STORED_ZEROS): the column form updates the same entries in the same order, so the values are
  * gathered into row order through a position map (position[k] = place in the column-ordered
  * array of the k-th entry in row order; the host side builds it with the row pointers, column
  * indices and diagonal positions of the row-ordered view), factored with lcd_spilu0_csr and
@@ -566,6 +571,26 @@ int lcd_set_tuning(int key, int value);
  * of 512-row chunks: row stamps, per-chunk start times, wait counters and the helpers'
  * publication stamps) record SM cycle counters and timer values.  Pass NULL to switch it off again. */
 int lcd_debug_set_trace(long long *trace_dev);
+
+/*
+ * Machine constants for the scheduler's cost model, measured on the current device: replaces the
+ * micro-benchmarks of compiler/scheduler.py:714-775 (empty launches and an atomic kernel timed
+ * through Numba).  out_host receives LCD_CALIBRATION_VALUES doubles (LCD_CAL_* indices; a value that
+ * could not be measured stays 0).  workspace: at least 64 MiB of device memory, 256-byte aligned
+ * (the larger, the closer the copy figure is to the HBM rate).  Synchronises the stream; takes a
+ * few milliseconds.
+ */
+enum {
+    LCD_CAL_LAUNCH_S = 0,         /* one kernel launch in a back-to-back sequence */
+    LCD_CAL_L2_HANDOFF_S = 1,     /* one hand-off between two thread blocks through global memory */
+    LCD_CAL_SMEM_HANDOFF_S = 2,   /* one hand-off between two warps of a block through shared memory */
+    LCD_CAL_BLOCK_BARRIER_S = 3,  /* one __syncthreads() of 512 threads */
+    LCD_CAL_ATOMIC_S = 4,         /* one atomicAdd on an address every thread of the grid adds to */
+    LCD_CAL_GRID_BARRIER_S = 5,   /* one grid-wide barrier, one block of 512 threads per SM */
+    LCD_CAL_COPY_BYTES_PER_S = 6, /* device-to-device copy, read + write bytes */
+    LCD_CALIBRATION_VALUES = 8
+};
+int lcd_calibrate(void *workspace, int64_t workspace_bytes, void *stream, double *out_host);
 
 /* ---- small device utilities used by the host layer ---------------------------- */
 int lcd_fill_u64(uint64_t *dst, int64_t count, uint64_t value, void *stream);

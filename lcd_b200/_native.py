@@ -22,6 +22,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSORTED, \
 SOLVE_UPPER, SOLVE_UNIT_DIAG, SOLVE_OF_FULL, SOLVE_EXACT = 1, 2, 4, 8
 WAVEFRONT_PER_LEVEL, WAVEFRONT_COOPERATIVE = 0, 1
 STATUS_WORDS = 8
+ILU0_SKIP_STORED_ZEROS = 8      # LCD_ILU0_SKIP_STORED_ZEROS
 CHAIN_MAX_GROWTH = 100.0        # LCD_CHAIN_MAX_GROWTH
 (TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT,
  TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS, TUNE_ILU0_LOOKAHEAD) = range(9)
@@ -122,6 +123,7 @@ _SIGNATURES = {
     "lcd_sptrsv_csr_ordered_part": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, c_int, _P, c_int32,
                                             _P, c_int, _P, ctypes.POINTER(c_void_p), c_int32, c_int64,
                                             _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_calibrate": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_double * 8)]),
     "lcd_set_tuning": (c_int, [c_int, c_int]),
     "lcd_debug_set_trace": (c_int, [_P]),
     "lcd_checksum_i32": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_uint64 * 2), _P]),

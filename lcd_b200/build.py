@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB_PATH = os.path.join(HERE, "liblcd_b200.so")
 SOURCES = ("capi.cu", "dag_build.cu", "sptrsv_syncfree.cu", "sptrsv_chain.cu",
-           "sptrsv_wavefront.cu", "sptrsv_ordered.cu", "sptrsv_small.cu", "spilu0.cu", "supernodal.cu")
+           "sptrsv_wavefront.cu", "sptrsv_ordered.cu", "sptrsv_small.cu", "spilu0.cu", "supernodal.cu", "calibrate.cu")
 NVCC_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
               "-Xcompiler", "-fPIC", "-I" + INCLUDE, "-I" + CSRC)
 

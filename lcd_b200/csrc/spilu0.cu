@@ -30,6 +30,10 @@ struct Ilu0Params {
     const int *__restrict__ wavefronts;
     int32_t *status;
     unsigned long long budget_ns;
+    // column-loop semantics (compiler/demo/spilu0.py:69-75): an explicitly stored zero of the
+    // pivot row is treated like a missing entry - no update, so a non-finite multiplier does not
+    // turn the target into NaN and its sign of zero is kept
+    int skip_stored_zeros;
 };
 
 // Applies pivot row k (position kp in row i) with the lanes of one group.
@@ -63,8 +67,10 @@ __device__ __forceinline__ void apply_pivot(const Ilu0Params &p, int i, int row_
             const int mid = (lo + hi) >> 1;
             if (__ldg(p.Ai + mid) < j) lo = mid + 1; else hi = mid;
         }
-        if (lo < ke && __ldg(p.Ai + lo) == j)
-            p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ld_relaxed_f64(p.Ax + lo)));
+        if (lo < ke && __ldg(p.Ai + lo) == j) {
+            const double ukj = ld_relaxed_f64(p.Ax + lo);
+            if (!(p.skip_stored_zeros && ukj == 0.0)) p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ukj));
+        }
     }
 }
 
@@ -295,7 +301,8 @@ __global__ void __launch_bounds__(TPB) ilu0_lookahead_kernel(const Ilu0Params p)
                 if (G > 1) lik = __shfl_sync(gmask, lik, owner, G);
 #pragma unroll
                 for (int o = 0; o < kIluOwn; ++o)
-                    if (match[q][o] >= 0) val[o] = __dsub_rn(val[o], __dmul_rn(lik, u[q][o]));
+                    if (match[q][o] >= 0 && !(p.skip_stored_zeros && u[q][o] == 0.0))
+                        val[o] = __dsub_rn(val[o], __dmul_rn(lik, u[q][o]));
                 // entries of a long row that live in memory: searched while the pivot is held
                 for (int jp = spill + lane; jp < e; jp += G) {
                     if (jp <= kp + q) continue;
@@ -305,8 +312,11 @@ __global__ void __launch_bounds__(TPB) ilu0_lookahead_kernel(const Ilu0Params p)
                         const int mid = (lo + hi) >> 1;
                         if (__ldg(p.Ai + mid) < j) lo = mid + 1; else hi = mid;
                     }
-                    if (lo < pke[q] && __ldg(p.Ai + lo) == j)
-                        p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ld_relaxed_f64(p.Ax + lo)));
+                    if (lo < pke[q] && __ldg(p.Ai + lo) == j) {
+                        const double ukj = ld_relaxed_f64(p.Ax + lo);
+                        if (!(p.skip_stored_zeros && ukj == 0.0))
+                            p.Ax[jp] = __dsub_rn(p.Ax[jp], __dmul_rn(lik, ukj));
+                    }
                 }
             }
             applied = upto;
@@ -387,6 +397,8 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
                               const int32_t *wavefronts, const int32_t *wavefront_ptr_host,
                               int32_t n_levels, int lanes_per_row, int32_t *status_dev,
                               int32_t timeout_ms, void *stream, int *status_host) {
+    const int skip_stored_zeros = (mode & LCD_ILU0_SKIP_STORED_ZEROS) ? 1 : 0;
+    mode &= ~LCD_ILU0_SKIP_STORED_ZEROS;
     if (n < 0 || nnz < 0 || !status_dev || mode < 0 || mode > 2) return LCD_ERR_INVALID_ARGUMENT;
     if (n > 0 && (!Ap || !Ai || !Ax || !diag_pos)) return LCD_ERR_INVALID_ARGUMENT;
     if (n > 0 && mode != 1 && !done) return LCD_ERR_INVALID_ARGUMENT;
@@ -404,7 +416,7 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
     if (n > 0) {
         if (mode != 1) LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
         Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, mode == 0 ? nullptr : wavefronts, status_dev,
-                     timeout_ns(timeout_ms)};
+                     timeout_ns(timeout_ms), skip_stored_zeros};
         cudaError_t e;
         switch (G) {
             case 1: e = launch_ilu0<1>(p, mode, wavefront_ptr_host, n_levels, st); break;
@@ -482,7 +494,7 @@ extern "C" int lcd_spilu0_csr_static(int32_t n, int64_t nnz, const int32_t *Ap, 
     if (n > 0) {
         LCD_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)n * sizeof(int32_t), st));
         Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, done, nullptr, status_dev,
-                     timeout_ns(timeout_ms)};
+                     timeout_ns(timeout_ms), 0};
         cudaError_t e;
         switch (G) {
             case 1: e = launch_ilu0<1>(p, 0, nullptr, 0, st); break;

@@ -562,7 +562,8 @@ def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr
 
 
 def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
-               wavefront_ptr_host=None, done=None, lanes=0, status=None, timeout_ms=0, sync=True):
+               wavefront_ptr_host=None, done=None, lanes=0, status=None, timeout_ms=0, sync=True,
+               skip_stored_zeros=False):
     """In-place ILU(0) of a sorted CSR matrix; returns Ax.  ``mode``: "sync_free" (rows by
     index), "ordered" (sync-free, rows in the order of ``wavefronts``) or "wavefront" (a launch
     per level)."""
@@ -571,9 +572,10 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
     n = Ap.numel() - 1
     status = new_status(Ax.device) if status is None else status
     host = ctypes.c_int(0)
+    extra = nat.ILU0_SKIP_STORED_ZEROS if skip_stored_zeros else 0   # the column loop's rule
     if mode.replace("-", "_") == "sync_free":
         done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
-        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 0,
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 0 + extra,
                                        ptr(done), None, None, 0, int(lanes), ptr(status),
                                        int(timeout_ms), _stream(),
                                        ctypes.byref(host) if sync else None)
@@ -581,13 +583,13 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
         # sync-free, rows handed out in the order of the level sets
         _require(wavefronts, torch.int32, "wavefronts")
         done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
-        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 2,
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 2 + extra,
                                        ptr(done), ptr(wavefronts), None, 0, int(lanes), ptr(status),
                                        int(timeout_ms), _stream(),
                                        ctypes.byref(host) if sync else None)
     else:
         wph = np.ascontiguousarray(wavefront_ptr_host, dtype=np.int32)
-        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 1,
+        rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 1 + extra,
                                        None, ptr(wavefronts), wph.ctypes.data_as(ctypes.c_void_p),
                                        len(wph) - 1, int(lanes), ptr(status), int(timeout_ms),
                                        _stream(), ctypes.byref(host) if sync else None)
@@ -642,7 +644,8 @@ def spilu0_csc(Ap, Ai, Ax, view=None, *, mode="sync_free", wavefronts=None, wave
     view = csc_row_view(Ap, Ai) if view is None else view
     by_rows = permute(view.position, Ax)
     spilu0_csr(view.Ap, view.Ai, by_rows, view.diag_pos, mode=mode, wavefronts=wavefronts,
-               wavefront_ptr_host=wavefront_ptr_host, lanes=lanes, status=status, timeout_ms=timeout_ms)
+               wavefront_ptr_host=wavefront_ptr_host, lanes=lanes, status=status, timeout_ms=timeout_ms,
+               skip_stored_zeros=True)
     return permute(view.position, by_rows, Ax, scatter=True)
 
 

@@ -26,7 +26,7 @@ from __future__ import annotations
 
 import hashlib
 import itertools
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import numpy as np
 
@@ -337,18 +337,46 @@ def _schedule_rank(schedule):
             EXECUTION_MODES.index(schedule.execution_mode), schedule.dependence_protocol)
 
 
+_MEASURED_CONSTANTS = {}
+CALIBRATION_NAMES = ("launch_s", "l2_handoff_s", "shared_memory_handoff_s", "block_barrier_s",
+                     "contended_atomic_s", "grid_barrier_s", "copy_bytes_per_s")
+
+
+def calibrate(workspace_bytes=256 << 20):
+    """Raw figures of ``lcd_calibrate`` on the current device (a dict by CALIBRATION_NAMES)."""
+    import ctypes
+    import torch
+    from . import _native as nat
+    workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device="cuda")
+    out = (ctypes.c_double * 8)()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nat.check(nat.load().lcd_calibrate(nat.ptr(workspace), workspace.numel(), stream, ctypes.byref(out)),
+              "lcd_calibrate")
+    return {name: float(out[k]) for k, name in enumerate(CALIBRATION_NAMES)}
+
+
 def measure_arch_constants():
-    """Machine constants of the current device (bandwidth from its memory clock
-    and bus width when a GPU is present, else the B200 fallback)."""
+    """Machine constants of the current device, measured on it once per process and device
+    (``lcd_calibrate``: launch latency, hand-off through L2, contended atomic, grid barrier, copy
+    bandwidth), as the reference measures its own (compiler/scheduler.py:714-775).  Figures that
+    could not be measured keep the values observed on B200; without a GPU all of them do."""
     try:
         import torch
         if torch.cuda.is_available():
-            props = torch.cuda.get_device_properties(torch.cuda.current_device())
-            bandwidth = getattr(props, "memory_bus_width", 0) / 8 * \
-                getattr(props, "memory_clock_rate", 0) * 1e3 * 2
-            if bandwidth > 1e11:
-                return ArchConstants(3.0e-6, 2.0e-9, bandwidth, 1.5e9)
-    except Exception:  # pragma: no cover - no device
+            device = torch.cuda.current_device()
+            if device not in _MEASURED_CONSTANTS:
+                raw = calibrate()
+                pick = lambda name, default: raw[name] if raw.get(name, 0.0) > 0.0 else default
+                base = FALLBACK_ARCH_CONSTANTS
+                _MEASURED_CONSTANTS[device] = replace(
+                    base,
+                    launch_latency_s=pick("launch_s", base.launch_latency_s),
+                    atomic_cost_s=pick("contended_atomic_s", base.atomic_cost_s),
+                    memory_bandwidth_bytes_per_s=pick("copy_bytes_per_s", base.memory_bandwidth_bytes_per_s),
+                    barrier_s=pick("grid_barrier_s", base.barrier_s),
+                    handoff_s=pick("l2_handoff_s", base.handoff_s))
+            return _MEASURED_CONSTANTS[device]
+    except Exception:  # no device, or no library: the cost model still needs numbers
         pass
     return FALLBACK_ARCH_CONSTANTS
 
@@ -442,3 +470,10 @@ def inspection_fingerprint(values, content_names):
     shapes = tuple((name, value.dtype.str, value.shape)
                    for name, value in sorted(values.items()) if isinstance(value, np.ndarray))
     return content, shapes
+
+
+if __name__ == "__main__":          # python -m lcd_b200.scheduler --calibrate
+    import json
+    import sys
+    if "--calibrate" in sys.argv:
+        print(json.dumps({"raw": calibrate(), "arch_constants": measure_arch_constants().__dict__}, indent=1))

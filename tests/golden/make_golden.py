@@ -97,6 +97,22 @@ def write_ilu0_csc(out_dir):
     inputs = dict(ilu0_inputs())
     uns = sp.random(70, 70, density=0.1, random_state=8, format="csr") + sp.identity(70) * 3.0
     inputs["unsymmetric_n70"] = sp.csr_matrix(uns)
+    # explicitly stored zeros right of the diagonal (the column loop skips them: `if u_kj != 0.0`),
+    # among them a negative zero, and one huge sub-diagonal entry over a tiny pivot, so that a
+    # multiplier overflows to inf where a stored zero sits in the pivot row
+    zeros = sp.csr_matrix(sp.random(60, 60, density=0.12, random_state=11, format="csr")
+                          + sp.identity(60) * 3.0).tolil()
+    zeros[3, 3] = 1e-200
+    zeros[7, 3] = 1e200
+    zeros[3, 9] = 5.0
+    zeros[7, 9] = 2.0
+    zeros = sp.csr_matrix(zeros)
+    zeros.sort_indices()
+    upper = np.flatnonzero(zeros.indices > np.repeat(np.arange(60), np.diff(zeros.indptr)))
+    zeros.data[upper[::3]] = 0.0
+    zeros.data[upper[1::9]] = -0.0
+    zeros.data[[p for p in range(zeros.indptr[3], zeros.indptr[4]) if zeros.indices[p] == 9]] = 0.0
+    inputs["stored_zeros_n60"] = zeros
     for name, mat in inputs.items():
         csc = sp.csc_matrix(mat)
         csc.sort_indices()

@@ -227,21 +227,26 @@ def test_csr_chain_solver_cluster_sizes(cuda, oracle):
     assert used[0] == 1
 
 
-@pytest.mark.parametrize("mode", ["sync_free", "wavefront"])
+@pytest.mark.parametrize("mode", ["sync_free", "wavefront", "ordered"])
 @pytest.mark.parametrize("name", golden_names("csc_ilu0_"))
 def test_ilu0_on_csc_storage_is_bit_identical(cuda, oracle, name, mode):
     """ILU0 of a matrix stored by columns: gathered into row order, factored by the row kernel,
-    scattered back - bit for bit the result of the reference's column loop."""
-    from lcd_b200 import ops
+    scattered back - bit for bit the result of the reference's column loop, stored zeros in pivot
+    rows (skipped by that loop), a negative zero and an infinite multiplier included."""
+    from lcd_b200 import _native as nat, ops
     g = golden(name)
     Ap, Ai = dev(g["indptr"], np.int32, cuda), dev(g["indices"], np.int32, cuda)
     view = ops.csc_row_view(Ap, Ai)
     kw = {}
-    if mode == "wavefront":
+    if mode != "sync_free":
         d = ops.dag_build("ilu0_csr", view.Ap, view.Ai)
         kw = dict(wavefronts=d.wavefronts, wavefront_ptr_host=host(d.wavefront_ptr))
-    out = ops.spilu0_csc(Ap, Ai, dev(g["data"], np.float64, cuda), view, mode=mode, **kw)
-    np.testing.assert_array_equal(host(out), g["factored"])
+    for lookahead in (1, 0):
+        nat.load().lcd_set_tuning(nat.TUNE_ILU0_LOOKAHEAD, lookahead)
+        out = host(ops.spilu0_csc(Ap, Ai, dev(g["data"], np.float64, cuda), view, mode=mode, **kw))
+        nat.load().lcd_set_tuning(nat.TUNE_ILU0_LOOKAHEAD, 1)
+        np.testing.assert_array_equal(out, g["factored"])
+        np.testing.assert_array_equal(out.view(np.int64), g["factored"].view(np.int64))   # signs of zero too
 
 
 def test_ilu0_on_csc_storage_larger(cuda, oracle):

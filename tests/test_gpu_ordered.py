@@ -368,3 +368,20 @@ def test_capped_dag_build_completes_on_demand(cuda, oracle):
     assert plan.dag.capped and plan.levels == big.n // 64 + 1
     waves = plan.execution_data.task_nodes                # asking for them builds them
     np.testing.assert_array_equal(host(waves.tensor), oracle.dag_build("csr_lower", Bp, Bi).wavefronts)
+
+
+def test_device_calibration_gives_plausible_constants(cuda):
+    """lcd_calibrate: every figure measured (positive), in the range a current GPU can have."""
+    from lcd_b200 import scheduler
+    raw = scheduler.calibrate(workspace_bytes=128 << 20)
+    assert set(raw) == set(scheduler.CALIBRATION_NAMES)
+    assert 0.5e-6 < raw["launch_s"] < 50e-6
+    assert 0.1e-6 < raw["l2_handoff_s"] < 20e-6
+    assert 5e-9 < raw["shared_memory_handoff_s"] < raw["l2_handoff_s"]
+    assert 5e-9 < raw["block_barrier_s"] < 5e-6
+    assert 1e-11 < raw["contended_atomic_s"] < 1e-6
+    assert 0.3e-6 < raw["grid_barrier_s"] < 100e-6
+    assert 0.2e12 < raw["copy_bytes_per_s"] < 20e12
+    arch = scheduler.measure_arch_constants()
+    assert arch.handoff_s == raw["l2_handoff_s"] or arch.handoff_s > 0      # cached per device
+    assert arch.memory_bandwidth_bytes_per_s > 0.2e12

@@ -16,10 +16,10 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _factor_static(lib, nat, Ap, Ai, Ax, pos, lanes=0):
+def _factor_static(lib, nat, Ap, Ai, Ax, pos, lanes=0, stream=None):
     import torch
     host = ctypes.c_int(-1)
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    stream = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
     rc = lib.lcd_spilu0_csr_static(Ap.numel() - 1, Ai.numel(), nat.ptr(Ap), nat.ptr(Ai),
                                    nat.ptr(Ax), nat.ptr(pos), lanes, 0, stream,
                                    ctypes.byref(host))
@@ -42,13 +42,28 @@ def test_static_scratch_ilu0_matches_the_allocating_entry_point(cuda):
         want = ops.spilu0_csr(Ap, Ai, values.clone(), pos, mode="sync_free").cpu().numpy()
         for call in range(2):                            # the array keeps the last call's contents
             work = values.clone()
+            torch.cuda.synchronize()
+            # torch's counter only sees torch's own allocator; the driver's free-memory figure
+            # also sees a cudaMalloc inside the library (from the second call on: the first one
+            # on a device may load the module and look up the array's address)
             before = torch.cuda.memory_allocated(cuda)
+            free_before = torch.cuda.mem_get_info(cuda)[0]
             rc, status = _factor_static(lib, nat, Ap, Ai, work, pos)
             assert (rc, status) == (0, 0), (call, rc, status)
             assert torch.cuda.memory_allocated(cuda) == before
+            if call:
+                assert torch.cuda.mem_get_info(cuda)[0] == free_before
             np.testing.assert_array_equal(work.cpu().numpy(), want)   # ILU0 parity is bit-exact
         work = values.clone()
         rc, status = _factor_static(lib, nat, Ap, Ai, work, pos, lanes=1)
+        assert (rc, status) == (0, 0)
+        np.testing.assert_array_equal(work.cpu().numpy(), want)
+        # on a stream of the caller's own (one call at a time: the calls share the array)
+        side = torch.cuda.Stream(device=cuda)
+        work = values.clone()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(side):
+            rc, status = _factor_static(lib, nat, Ap, Ai, work, pos, stream=side)
         assert (rc, status) == (0, 0)
         np.testing.assert_array_equal(work.cpu().numpy(), want)
 
