@@ -613,7 +613,11 @@ def config_csc_lap2d(args, size=256):
     e2e_residual = float(np.linalg.norm(A @ out - tri.b) / np.linalg.norm(tri.b))
     cpu_s, count = _host_time(lambda: cpu.sptrsv_csc_lower(Cp, Ci, Cx, tri.b), min_seconds=1.0)
     nbytes = algorithmic_bytes(n, nnz)
-    reference_gpu = numba_cuda_reference() if size == 256 else {"unavailable": "timed on the 256 x 256 grid only"}
+    if args.kernel_only:
+        reference_gpu = {"unavailable": "skipped (--kernel-only)"}
+    else:
+        reference_gpu = numba_cuda_reference() if size == 256 else {
+            "unavailable": "timed on the 256 x 256 grid only"}
     return {"workload": f"sptrsv_csc_lap2d_g{size}", "format": "csc_lower", "n": n, "nnz": nnz,
             "numba_cuda_wavefront_ms": reference_gpu.get("ms"), "numba_cuda_reference": reference_gpu,
             "levels": dag.n_levels, "kernel": "sptrsv_small_kernel (one thread block)",

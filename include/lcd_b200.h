@@ -359,46 +359,55 @@ int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *
                            int32_t timeout_ms, void *stream, int *status_host);
 
 /*
- * Solves small enough for one thread block (a few hundred thousand rows at most): CSR (pull)
- * and CSC (push, compiler/demo/sptrsv.py:37-43) triangular solves whose cost is the hand-off
- * between levels, not bandwidth.  One block walks the level sets with a block barrier per
- * level and keeps the recent part of x (CSR) or the accumulators of the coming positions
- * (CSC) in shared memory; nothing spins.  Replaces, for such sizes, the generated wavefront
- * launchers (compiler/cuda_lowering.py:855-1016: a launch plus a device synchronisation per
- * level) and the push kernel (:2031-2059).
+ * Solves small enough for one thread block (a few hundred thousand rows at most): CSR and CSC
+ * (compiler/demo/sptrsv.py:26-43) triangular solves whose cost is the hand-off between levels,
+ * not bandwidth.  One block walks the level sets with a block barrier per level and keeps the
+ * recent part of x in shared memory; nothing spins.  Replaces, for such sizes, the generated
+ * wavefront launchers (compiler/cuda_lowering.py:855-1016: a launch plus a device synchronisation
+ * per level) and the sync-free kernels (:1343-1410, push :2031-2059).  The CSC loop (push) is
+ * served by the same pull walk on the transposed structure - no atomics, results do not depend on
+ * timing.
+ *   Task slots: every level is padded to a multiple of 32 slots, so that the lanes of a warp
+ *       always work in the same level (the scoreboard of outstanding loads belongs to the warp).
+ *       slot_ptr[l] = first slot of level l (n_levels + 1 entries, a device array the caller
+ *       computes from wavefront_ptr: running sum of the level widths rounded up to 32);
+ *       n_slots = slot_ptr[n_levels].
  *   lcd_small_plan_measure / lcd_small_plan_fill   once per pattern: `pos` (n ints) receives the
- *       place of every node in `order` (= wavefronts of lcd_dag_build for the same op);
- *       info_host[0] = longest row / column without its diagonal, [1] = widest level.  The fill
- *       writes an ELL image of the matrix in level order with `entries` >= info_host[0] slots
- *       per task (entries <= lcd_small_max_entries()): ell_pc / ell_src [entries * n] = place
- *       of the operand (CSR) or target (CSC) and index of its value in Ax, -1 for padding;
- *       row_of[n], diag_src[n].  *far_host = entries whose other end lies more than half the
- *       shared-memory ring away (served through global memory).  Errors through status_dev:
- *       LCD_ERR_INDEX_RANGE, LCD_ERR_BAD_POINTERS, LCD_ERR_CYCLE (order not topological).
- *       info_dev: 4 ints of device scratch.
+ *       slot of every node (order, level, wavefront_ptr: wavefronts, level and wavefront_ptr of
+ *       lcd_dag_build for the same op); info_host[0] = most operands of one task (longest row
+ *       without its diagonal), [1] = widest level.  The fill writes one record per slot with
+ *       `entries` = 2, 4 or 8 >= info_host[0] operand slots (more operands than
+ *       lcd_small_max_entries(): not served): rec_pc / rec_src [n_slots * entries] = slot of the
+ *       operand and index of its value in Ax, -1 for padding; row_of[n_slots] (-1: padding
+ *       slot), diag_src[n_slots].  *far_host = operands more than half the shared-memory ring
+ *       back (read from global memory).  cursor: n_slots ints of scratch (CSC ops only).
+ *       Errors through status_dev: LCD_ERR_INDEX_RANGE, LCD_ERR_BAD_POINTERS, LCD_ERR_CYCLE
+ *       (order not topological).  info_dev: 4 ints of device scratch.
  *   lcd_sptrsv_small   every solve: gathers values, right-hand side and reciprocal diagonals
- *       into level order (a parallel pass) and walks the levels.  scratch:
- *       lcd_small_scratch_bytes(n, entries) bytes, 256-byte aligned.  Asynchronous on `stream`;
- *       it has no device-side waits and reports nothing (the plan calls validated the input).
+ *       into slot order (a parallel pass), walks the levels, and puts x back into matrix order
+ *       (a parallel pass).  scratch: lcd_small_scratch_bytes(n_slots, entries) bytes, 256-byte
+ *       aligned; rec_pc 16-byte aligned.  Asynchronous on `stream`; it has no device-side waits
+ *       and reports nothing (the plan calls validated the input).
  *   op: LCD_OP_CSR_LOWER / CSR_UPPER / CSC_LOWER / CSC_UPPER; flags: LCD_SOLVE_OF_FULL /
  *   UNIT_DIAG for the CSR ops.
  */
 int lcd_small_max_entries(void);
 int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
-                           const int32_t *diag_pos, const int32_t *order,
-                           const int32_t *wavefront_ptr_dev, int32_t n_levels, int32_t *pos,
-                           int32_t *info_dev, int32_t *status_dev, void *stream, int32_t *info_host);
+                           const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
+                           const int32_t *level, const int32_t *wavefront_ptr_dev,
+                           const int32_t *slot_ptr_dev, int32_t n_levels, int32_t n_slots, int32_t *pos,
+                           int32_t *cursor, int32_t *info_dev, int32_t *status_dev, void *stream,
+                           int32_t *info_host);
 int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
                         const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
-                        const int32_t *pos, int32_t entries, int32_t *ell_pc, int32_t *ell_src,
-                        int32_t *row_of, int32_t *diag_src, int32_t *info_dev, int32_t *status_dev,
-                        void *stream, int32_t *far_host);
-int lcd_small_scratch_bytes(int32_t n, int32_t entries, int64_t *bytes);
-int lcd_sptrsv_small(int csc, int32_t n, int32_t entries, const double *Ax, const double *b, double *x,
-                     const int32_t *ell_pc, const int32_t *ell_src, const int32_t *row_of,
-                     const int32_t *diag_src, const int32_t *wavefront_ptr_dev, int32_t n_levels,
-                     int32_t max_width, int32_t has_far, void *scratch, int64_t scratch_bytes,
-                     void *stream);
+                        const int32_t *pos, int32_t n_slots, int32_t entries, int32_t *rec_pc,
+                        int32_t *rec_src, int32_t *row_of, int32_t *diag_src, int32_t *cursor,
+                        int32_t *info_dev, int32_t *status_dev, void *stream, int32_t *far_host);
+int lcd_small_scratch_bytes(int32_t n_slots, int32_t entries, int64_t *bytes);
+int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *Ax, const double *b,
+                     double *x, const int32_t *rec_pc, const int32_t *rec_src, const int32_t *row_of,
+                     const int32_t *diag_src, const int32_t *slot_ptr_dev, int32_t n_levels,
+                     int32_t max_width, void *scratch, int64_t scratch_bytes, void *stream);
 
 /* ---- SpILU0 (CSR, in place) -------------------------------------------------- */
 /*

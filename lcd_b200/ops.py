@@ -424,8 +424,9 @@ def sptrsv_csr_ordered(Ap, Ai, Ax, B, order, X=None, *, upper=False, unit_diag=F
 
 
 class SmallPlan:
-    """Level-ordered ELL image of a small triangular matrix (structure only, built on the
-    device) and the per-solve scratch of the one-block solver."""
+    """Level-ordered task records of a small triangular matrix (structure only, built on the
+    device) and the per-solve scratch of the one-block solver.  Every level is padded to whole
+    warps of task slots."""
 
     def __init__(self, op, Ap, Ai, dag, *, diag_pos=None, unit_diag=False):
         op = _op_code(op)
@@ -435,39 +436,49 @@ class SmallPlan:
         dev = Ap.device
         n = Ap.numel() - 1
         self.op, self.n = op, n
-        self.csc = op in (nat.OP_CSC_LOWER, nat.OP_CSC_UPPER)
         flags = _solve_flags(False, unit_diag, diag_pos is not None, False)
         i32 = dict(dtype=torch.int32, device=dev)
-        self.wavefront_ptr = dag.wavefront_ptr
         self.n_levels = dag.n_levels
+        widths = np.diff(dag.wavefront_ptr_host.astype(np.int64))
+        slot_ptr = np.zeros(dag.n_levels + 1, dtype=np.int64)
+        np.cumsum((widths + 31) // 32 * 32, out=slot_ptr[1:])
+        self.n_slots = int(slot_ptr[-1])
+        if self.n_slots > SMALL_MAX_SLOTS:
+            raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
+                              f"{self.n_slots} task slots after padding every level to whole warps; "
+                              f"the one-block solver serves up to {SMALL_MAX_SLOTS}")
+        self.slot_ptr = torch.from_numpy(slot_ptr.astype(np.int32)).to(dev)
+        m = max(self.n_slots, 1)
         pos = torch.empty(max(n, 1), **i32)
+        cursor = torch.empty(m, **i32)
         info_dev = torch.zeros(4, **i32)
         status = new_status(dev)
         info = (ctypes.c_int32 * 4)()
-        check(lib.lcd_small_plan_measure(op, flags, n, Ai.numel(), ptr(Ap), ptr(diag_pos),
-                                         ptr(dag.wavefronts), ptr(dag.wavefront_ptr), dag.n_levels,
-                                         ptr(pos), ptr(info_dev), ptr(status), _stream(),
+        check(lib.lcd_small_plan_measure(op, flags, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(diag_pos),
+                                         ptr(dag.wavefronts), ptr(dag.level), ptr(dag.wavefront_ptr),
+                                         ptr(self.slot_ptr), dag.n_levels, self.n_slots, ptr(pos),
+                                         ptr(cursor), ptr(info_dev), ptr(status), _stream(),
                                          ctypes.byref(info)), "lcd_small_plan_measure")
         longest, self.max_width = int(info[0]), int(info[1])
         if longest > lib.lcd_small_max_entries():
             raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
-                              f"a row holds {longest} off-diagonal entries; the one-block solver "
+                              f"a task has {longest} operands; the one-block solver "
                               f"serves up to {lib.lcd_small_max_entries()}")
         self.entries = 2 if longest <= 2 else (4 if longest <= 4 else 8)
-        m = max(n, 1)
-        self.ell_pc = torch.empty(self.entries * m, **i32)
-        self.ell_src = torch.empty(self.entries * m, **i32)
+        self.rec_pc = torch.empty(self.entries * m, **i32)
+        self.rec_src = torch.empty(self.entries * m, **i32)
         self.row_of = torch.empty(m, **i32)
         self.diag_src = torch.empty(m, **i32)
         far = ctypes.c_int32(0)
         check(lib.lcd_small_plan_fill(op, flags, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(diag_pos),
-                                      ptr(dag.wavefronts), ptr(pos), self.entries, ptr(self.ell_pc),
-                                      ptr(self.ell_src), ptr(self.row_of), ptr(self.diag_src),
-                                      ptr(info_dev), ptr(status), _stream(), ctypes.byref(far)),
-              "lcd_small_plan_fill")
+                                      ptr(dag.wavefronts), ptr(pos), self.n_slots, self.entries,
+                                      ptr(self.rec_pc), ptr(self.rec_src), ptr(self.row_of),
+                                      ptr(self.diag_src), ptr(cursor), ptr(info_dev), ptr(status),
+                                      _stream(), ctypes.byref(far)), "lcd_small_plan_fill")
         self.far = int(far.value)
         need = ctypes.c_int64(0)
-        check(lib.lcd_small_scratch_bytes(n, self.entries, ctypes.byref(need)), "lcd_small_scratch_bytes")
+        check(lib.lcd_small_scratch_bytes(self.n_slots, self.entries, ctypes.byref(need)),
+              "lcd_small_scratch_bytes")
         self.scratch = torch.empty(need.value, dtype=torch.uint8, device=dev)
 
     @staticmethod
@@ -477,6 +488,7 @@ class SmallPlan:
 
 
 SMALL_MAX_ROWS = 1 << 18
+SMALL_MAX_SLOTS = 1 << 21
 
 
 def sptrsv_small(plan, Ax, b, x=None):
@@ -484,11 +496,11 @@ def sptrsv_small(plan, Ax, b, x=None):
     _require(Ax, torch.float64, "Ax")
     _require(b, torch.float64, "b")
     x = torch.empty_like(b) if x is None else x
-    check(nat.load().lcd_sptrsv_small(1 if plan.csc else 0, plan.n, plan.entries, ptr(Ax), ptr(b),
-                                      ptr(x), ptr(plan.ell_pc), ptr(plan.ell_src), ptr(plan.row_of),
-                                      ptr(plan.diag_src), ptr(plan.wavefront_ptr), plan.n_levels,
-                                      plan.max_width, 1 if plan.far else 0, ptr(plan.scratch),
-                                      plan.scratch.numel(), _stream()), "lcd_sptrsv_small")
+    check(nat.load().lcd_sptrsv_small(plan.n, plan.n_slots, plan.entries, ptr(Ax), ptr(b), ptr(x),
+                                      ptr(plan.rec_pc), ptr(plan.rec_src), ptr(plan.row_of),
+                                      ptr(plan.diag_src), ptr(plan.slot_ptr), plan.n_levels,
+                                      plan.max_width, ptr(plan.scratch), plan.scratch.numel(), _stream()),
+          "lcd_sptrsv_small")
     return x
 
 
