@@ -570,9 +570,13 @@ enum {
                                      unsuccessful polls (0 = never pause; default 256) */
     LCD_TUNE_SMALL_THREADS = 7,   /* lcd_sptrsv_small: threads of the one block, 256 / 512 / 1024
                                      (0 = 512 while no level is wider than that, else 1024) */
-    LCD_TUNE_ILU0_LOOKAHEAD = 8   /* lcd_spilu0_csr sync-free modes: 1 (default) = pattern look-ups
+    LCD_TUNE_ILU0_LOOKAHEAD = 8,  /* lcd_spilu0_csr sync-free modes: 1 (default) = pattern look-ups
                                      for the next pivots before their flags are polled, own entries
                                      in registers; 0 = search while the pivot is held.  Same result. */
+    LCD_TUNE_ORDERED_MIN_LANES = 9 /* lcd_sptrsv_csr_ordered: lanes per row at least: 1, 2 (default), 4
+                                     or 8 (with 2 a warp holds 16 rows, which measured twice as fast
+                                     as 32 rows per warp even with one right-hand side); a value
+                                     100 * W + KR picks the kernel variant outright (tuning runs) */
 };
 int lcd_set_tuning(int key, int value);
 /* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,

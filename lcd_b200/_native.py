@@ -25,7 +25,8 @@ STATUS_WORDS = 8
 ILU0_SKIP_STORED_ZEROS = 8      # LCD_ILU0_SKIP_STORED_ZEROS
 CHAIN_MAX_GROWTH = 100.0        # LCD_CHAIN_MAX_GROWTH
 (TUNE_SLEEP_LOCAL_NS, TUNE_SLEEP_GLOBAL_NS, TUNE_GAP_NS, TUNE_ROW_VARIANT, TUNE_STAGE_PERCENT,
- TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS, TUNE_ILU0_LOOKAHEAD) = range(9)
+ TUNE_CHAIN_CLUSTER, TUNE_ORDERED_PAUSE_NS, TUNE_SMALL_THREADS, TUNE_ILU0_LOOKAHEAD,
+ TUNE_ORDERED_MIN_LANES) = range(10)
 
 
 class NativeLibraryMissing(RuntimeError):

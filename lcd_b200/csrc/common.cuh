@@ -42,6 +42,7 @@ int sm_count();
 void set_debug_trace(long long *p);
 int set_chain_cluster_limit(int blocks);  // LCD_TUNE_CHAIN_CLUSTER
 int set_ordered_pause(int ns);           // LCD_TUNE_ORDERED_PAUSE_NS
+int set_ordered_min_lanes(int lanes);    // LCD_TUNE_ORDERED_MIN_LANES
 int set_small_threads(int threads);      // LCD_TUNE_SMALL_THREADS
 int set_ilu0_lookahead(int on);          // LCD_TUNE_ILU0_LOOKAHEAD
 long long *debug_trace();  // profiling aid set by lcd_debug_set_trace (NULL = off)

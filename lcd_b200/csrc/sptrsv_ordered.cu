@@ -49,6 +49,7 @@ constexpr int kOrdWarps = kOrdThreads / 32;
 constexpr int kStage = 4;          // entries of a row tried per trip
 constexpr int kCounterStride = 64;  // ints between two ticket counters
 static int g_ordered_pause_ns = 256;  // longest pause between two polls of a waiting warp
+static int g_ordered_min_lanes = 2;   // lanes per row at least (1 measured 2x slower than 2)
 
 struct __align__(16) TaskMeta {
     int row;  // matrix row, -1: nothing to do (an error was raised)
@@ -64,11 +65,18 @@ struct OrderedParams {
     int n_tasks;
     unsigned max_pause_ns;
     int *counters;   // kOrdWarps ticket counters, kCounterStride ints apart, zero on entry
+    long long *trace;  // profiling aid (lcd_debug_set_trace), 3n words: nanosecond timer when a row's
+                       // batch came up / when the row was published, and its number of waiting trips
 };
 
 int set_ordered_pause(int ns) {
     if (ns < 0 || ns > 100000) return LCD_ERR_INVALID_ARGUMENT;
     g_ordered_pause_ns = ns;
+    return LCD_OK;
+}
+int set_ordered_min_lanes(int lanes) {
+    if (lanes < 100 && lanes != 1 && lanes != 2 && lanes != 4 && lanes != 8) return LCD_ERR_INVALID_ARGUMENT;
+    g_ordered_min_lanes = lanes;
     return LCD_OK;
 }
 
@@ -134,6 +142,7 @@ struct WarpStage {
 // and a published value is also stored into the x arrays of the ranks that need it.
 template <int W, int KR, bool FLAGS, bool SYS = false>
 __global__ void __launch_bounds__(kOrdThreads, 4) csr_ordered_kernel(const OrderedParams q) {
+    constexpr int S = KR <= 2 ? kStage : (KR <= 4 ? 2 : 1);   // entries tried per trip (registers)
     extern __shared__ __align__(16) unsigned char ordered_smem[];
     const CsrSolveParams &p = q.m;
     constexpr int G = 32 / W;
@@ -219,138 +228,152 @@ __global__ void __launch_bounds__(kOrdThreads, 4) csr_ordered_kernel(const Order
         cp_async_commit();
 
         // ---- solve the group's row of batch seq ----
+        // Every lane runs every trip and every vote is a full-warp ballot read through the
+        // group's mask: a vote with one mask per group would be executed once per group, and the
+        // lanes would stay split behind it (measured with one lane per row: 32 serial copies of
+        // the trip, 500 warp instructions per trip instead of 50).
         const int4 mt = stage.meta[seq & (kMetaRing - 1)][g];
         const RowData &rd = stage.row[seq & (kDataRing - 1)][g];
         const int r = mt.x, lo = mt.y, cnt = mt.z;
-        int cidx[kStage];
-        double cval[kStage], acc[KR];
+        int cidx[S];
+        double cval[S], acc[KR];
         double rinv = 1.0;
-        if (r >= 0) {
+        bool active = r >= 0, failed = false;
+        int e = 0, m = 0;
+        // entries [e, e + m) are staged in cidx / cval; an entry that is not an earlier row fails the row
+        auto check_chunk = [&]() {
 #pragma unroll
-            for (int i = 0; i < kStage; ++i) { cidx[i] = rd.col[i]; cval[i] = rd.val[i]; }
+            for (int i = 0; i < S; ++i) {
+                if (i < m) {
+                    const int c = cidx[i];
+                    if (!((unsigned)c < (unsigned)p.n && (upper ? c > r : c < r))) failed = true;
+                }
+            }
+            if (failed) {
+                if (gl == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
+                m = 0;
+                e = cnt;
+            }
+        };
+        if (active) {
+#pragma unroll
+            for (int i = 0; i < S; ++i) { cidx[i] = rd.col[i]; cval[i] = rd.val[i]; }   // (S <= kStage)
 #pragma unroll
             for (int c = 0; c < KR; ++c) acc[c] = stage.rhs[seq & (kDataRing - 1)][c][lane];
             rinv = 1.0 / rd.diag;
+            m = min(S, cnt);
+            check_chunk();
+            if (q.trace && gl == 0) q.trace[r] = (long long)global_timer();
         }
-        bool done = r < 0, failed = false, chunk_loaded = true, checked = false;
-        int e = 0;
         unsigned pause = 0;
+        int trips = 0;
         Deadline dl;
         dl.start(p.budget_ns);
         for (;;) {
-            bool progressed = false;
-            if (!done) {
-                if (e < cnt) {
-                    const int m = min(kStage, cnt - e);
-                    if (!chunk_loaded) {
+            // -- poll: one non-blocking attempt at the staged entries --
+            double xv[S][KR];
+            bool ready = true;
+            if (FLAGS) {
 #pragma unroll
-                        for (int i = 0; i < kStage; ++i) {
-                            if (i < m) { cidx[i] = __ldg(p.Ai + lo + e + i); cval[i] = __ldg(p.Ax + lo + e + i); }
-                        }
-                        chunk_loaded = true;
-                        checked = false;
-                    }
-                    if (!checked) {
+                for (int i = 0; i < S; ++i)
+                    if (active && i < m) ready = ready && ld_relaxed_s32(q.row_flags + cidx[i]) != 0;
+            } else {
 #pragma unroll
-                        for (int i = 0; i < kStage; ++i) {
-                            if (i < m) {
-                                const int c = cidx[i];
-                                const bool ok = (unsigned)c < (unsigned)p.n && (upper ? c > r : c < r);
-                                if (!ok) {   // not an earlier row: nothing to wait for
-                                    if (gl == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, r);
-                                    failed = true;
-                                }
-                            }
-                        }
-                        checked = true;
-                    }
-                    if (failed) {
-                        e = cnt;
-                    } else {
-                        double xv[kStage][KR];
-                        bool ready = true;
-                        if (FLAGS) {
-#pragma unroll
-                            for (int i = 0; i < kStage; ++i)
-                                if (i < m) ready = ready && ld_relaxed_s32(q.row_flags + cidx[i]) != 0;
-                            ready = __all_sync(gmask, ready) != 0;
-                            if (ready) {
-                                acquire_fence();
-#pragma unroll
-                                for (int i = 0; i < kStage; ++i) {
-#pragma unroll
-                                    for (int c = 0; c < KR; ++c) {
-                                        const int col = gl + W * c;
-                                        xv[i][c] = (i < m && col < p.nrhs)
-                                                       ? __ldcg(p.x + (long long)cidx[i] * p.ld + col) : 0.0;
-                                    }
-                                }
-                            }
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < kStage; ++i) {
-#pragma unroll
-                                for (int c = 0; c < KR; ++c) {
-                                    const int col = gl + W * c;
-                                    xv[i][c] = 0.0;
-                                    if (i < m && col < p.nrhs) {
-                                        const double *src = p.x + (long long)cidx[i] * p.ld + col;
-                                        xv[i][c] = SYS ? ld_relaxed_sys_f64(src) : ld_relaxed_f64(src);
-                                        ready = ready && !is_pending(xv[i][c]);
-                                    }
-                                }
-                            }
-                            ready = __all_sync(gmask, ready) != 0;
-                        }
-                        if (ready) {
-#pragma unroll
-                            for (int i = 0; i < kStage; ++i) {
-                                if (i < m) {
-#pragma unroll
-                                    for (int c = 0; c < KR; ++c) acc[c] = fma(-cval[i], xv[i][c], acc[c]);
-                                }
-                            }
-                            e += m;
-                            chunk_loaded = false;
-                            progressed = true;
-                        } else {
-                            const bool give_up = dl.tick(p.status, r);
-                            if (__any_sync(gmask, give_up)) { failed = true; e = cnt; }
-                        }
-                    }
-                }
-                if (e >= cnt) {
-                    // publish in the trip that consumed the last operand
-                    const double nanv = __longlong_as_double(kCanonicalNaN);
+                for (int i = 0; i < S; ++i) {
 #pragma unroll
                     for (int c = 0; c < KR; ++c) {
                         const int col = gl + W * c;
-                        if (col < p.nrhs) {
-                            const double v = failed ? nanv : acc[c] * rinv;
-                            if (FLAGS) __stcg(p.x + (long long)r * p.ld + col, v);
-                            else st_relaxed_f64(p.x + (long long)r * p.ld + col, publishable(v));
-                            if (SYS && p.need_mask) {   // rows of other GPUs wait for it in their own memory
-                                unsigned mk = p.need_mask[r];
-                                while (mk) {
-                                    const int peer = __ffs(mk) - 1;
-                                    mk &= mk - 1;
-                                    st_relaxed_sys_f64(p.peers[peer] + (long long)r * p.ld + col, publishable(v));
-                                }
+                        xv[i][c] = 0.0;
+                        if (active && i < m && col < p.nrhs) {
+                            const double *src = p.x + (long long)cidx[i] * p.ld + col;
+                            xv[i][c] = SYS ? ld_relaxed_sys_f64(src) : ld_relaxed_f64(src);
+                            ready = ready && !is_pending(xv[i][c]);
+                        }
+                    }
+                }
+            }
+            if (W > 1) ready = (__ballot_sync(kFull, ready) & gmask) == gmask;
+            if (FLAGS) {
+                const bool take = active && ready;
+                if (take) acquire_fence();
+#pragma unroll
+                for (int i = 0; i < S; ++i) {
+#pragma unroll
+                    for (int c = 0; c < KR; ++c) {
+                        const int col = gl + W * c;
+                        xv[i][c] = (take && i < m && col < p.nrhs)
+                                       ? __ldcg(p.x + (long long)cidx[i] * p.ld + col) : 0.0;
+                    }
+                }
+            }
+            // -- consume, then publish in the trip that consumed the last operand --
+            const bool progressed = active && (ready || failed);
+            bool publish = false;
+            if (progressed) {
+#pragma unroll
+                for (int i = 0; i < S; ++i) {
+                    if (i < m) {
+#pragma unroll
+                        for (int c = 0; c < KR; ++c) acc[c] = fma(-cval[i], xv[i][c], acc[c]);
+                    }
+                }
+                e += m;
+                if (e < cnt) {      // rows longer than one staged chunk: fetch the next one
+                    m = min(S, cnt - e);
+#pragma unroll
+                    for (int i = 0; i < S; ++i) {
+                        if (i < m) {
+                            if (S < kStage && e + i < kStage) {   // still among the staged entries
+                                cidx[i] = rd.col[e + i];
+                                cval[i] = rd.val[e + i];
+                            } else {
+                                cidx[i] = __ldg(p.Ai + lo + e + i);
+                                cval[i] = __ldg(p.Ax + lo + e + i);
                             }
                         }
                     }
-                    if (FLAGS) {
-                        __syncwarp(gmask);   // the group's stores are ordered before the release
-                        if (gl == 0) st_release_s32(q.row_flags + r, 1);
+                    check_chunk();
+                }
+                publish = e >= cnt;
+            }
+            if (publish) {
+                const double nanv = __longlong_as_double(kCanonicalNaN);
+#pragma unroll
+                for (int c = 0; c < KR; ++c) {
+                    const int col = gl + W * c;
+                    if (col < p.nrhs) {
+                        const double v = failed ? nanv : acc[c] * rinv;
+                        if (FLAGS) __stcg(p.x + (long long)r * p.ld + col, v);
+                        else st_relaxed_f64(p.x + (long long)r * p.ld + col, publishable(v));
+                        if (SYS && p.need_mask) {   // rows of other GPUs wait for it in their own memory
+                            unsigned mk = p.need_mask[r];
+                            while (mk) {
+                                const int peer = __ffs(mk) - 1;
+                                mk &= mk - 1;
+                                st_relaxed_sys_f64(p.peers[peer] + (long long)r * p.ld + col, publishable(v));
+                            }
+                        }
                     }
-                    done = true;
-                    progressed = true;
+                }
+                active = false;
+                m = 0;
+                if (q.trace && gl == 0) {
+                    q.trace[p.n + r] = (long long)global_timer();
+                    q.trace[2ll * p.n + r] = trips;
                 }
             }
-            if (__all_sync(kFull, done)) break;
+            if (FLAGS) {
+                __syncwarp();   // the group's stores are ordered before the release of its flag
+                if (publish && gl == 0) st_release_s32(q.row_flags + r, 1);
+            }
+            ++trips;
+            const unsigned still = __ballot_sync(kFull, active);
+            if (still == 0) break;
             if (__any_sync(kFull, progressed)) {
                 pause = 0;
             } else {
+                // nobody moved: bounded wait (a raised error or the deadline fails the waiting rows)
+                if (__any_sync(kFull, active && dl.tick(p.status, r))) failed = active;
                 pause = pause ? min(pause * 2, q.max_pause_ns) : 32u;
                 if (q.max_pause_ns) __nanosleep(pause);
             }
@@ -429,19 +452,35 @@ extern "C" int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, cons
         q.n_tasks = n;
         q.max_pause_ns = (unsigned)g_ordered_pause_ns;
         q.counters = task_records + 4 * (size_t)n;
+        q.trace = debug_trace();
         LCD_CUDA_TRY(cudaMemsetAsync(q.counters, 0, kOrdWarps * kCounterStride * sizeof(int32_t), st));
         if (!records_ready) {
             ordered_meta_kernel<<<(n + 255) / 256, 256, 0, st>>>(
                 q.m, order, n, reinterpret_cast<TaskMeta *>(task_records));
             LCD_CUDA_TRY(cudaGetLastError());
         }
-        if (nrhs == 1) rc = launch_ordered<1, 1>(q, window_rows, st);
-        else if (nrhs <= 2) rc = launch_ordered<2, 1>(q, window_rows, st);
-        else if (nrhs <= 4) rc = launch_ordered<4, 1>(q, window_rows, st);
-        else if (nrhs <= 8) rc = launch_ordered<8, 1>(q, window_rows, st);
-        else if (nrhs <= 16) rc = launch_ordered<8, 2>(q, window_rows, st);
-        else if (nrhs <= 32) rc = launch_ordered<16, 2>(q, window_rows, st);
-        else rc = launch_ordered<32, 2>(q, window_rows, st);
+        // (lanes per row) x (right-hand sides per lane) >= nrhs.  Measured on 3-D grids (192^3): two
+        // to eight lanes per row are fastest whatever the number of right-hand sides up to eight
+        // (one lane per row, i.e. 32 rows per warp, is twice as slow even for one right-hand side:
+        // a warp moves on when its slowest row is done); beyond that the lanes take two, then four
+        // right-hand sides each.
+        int W, KR;
+        if (g_ordered_min_lanes >= 100) {        // explicit variant (tuning runs): 100 * W + KR
+            W = g_ordered_min_lanes / 100;
+            KR = g_ordered_min_lanes % 100;
+            if (W * KR < nrhs) return LCD_ERR_INVALID_ARGUMENT;
+        } else {
+            W = nrhs <= 2 ? 2 : (nrhs <= 4 ? 4 : (nrhs <= 32 ? 8 : 16));
+            KR = nrhs <= 8 ? 1 : (nrhs <= 16 ? 2 : 4);
+            if (KR == 1 && g_ordered_min_lanes > W) W = g_ordered_min_lanes;   // 4 or 8 lanes per row
+            if (nrhs == 1 && g_ordered_min_lanes == 1) W = 1;
+        }
+#define LCD_ORDERED_CASE(w, k) if (W == w && KR == k) rc = launch_ordered<w, k>(q, window_rows, st); else
+        LCD_ORDERED_CASE(1, 1) LCD_ORDERED_CASE(2, 1) LCD_ORDERED_CASE(4, 1) LCD_ORDERED_CASE(8, 1)
+        LCD_ORDERED_CASE(8, 2) LCD_ORDERED_CASE(16, 2) LCD_ORDERED_CASE(32, 2)
+        LCD_ORDERED_CASE(8, 4) LCD_ORDERED_CASE(16, 4)
+        rc = LCD_ERR_INVALID_ARGUMENT;
+#undef LCD_ORDERED_CASE
         if (rc) return rc;
     }
     return finish(status_dev, st, status_host);
@@ -480,13 +519,14 @@ extern "C" int lcd_sptrsv_csr_ordered_part(int32_t n, int64_t nnz, const int32_t
         q.n_tasks = n_local;
         q.max_pause_ns = (unsigned)g_ordered_pause_ns;
         q.counters = task_records + 4 * (size_t)n_local;
+        q.trace = nullptr;
         LCD_CUDA_TRY(cudaMemsetAsync(q.counters, 0, kOrdWarps * kCounterStride * sizeof(int32_t), st));
         if (!records_ready) {
             ordered_meta_kernel<<<(n_local + 255) / 256, 256, 0, st>>>(
                 q.m, order_local, n_local, reinterpret_cast<TaskMeta *>(task_records));
             LCD_CUDA_TRY(cudaGetLastError());
         }
-        rc = launch_ordered_t<1, 1, false, true>(q, window_rows, st);
+        rc = launch_ordered_t<2, 1, false, true>(q, window_rows, st);
         if (rc) return rc;
     }
     return finish(status_dev, st, status_host);

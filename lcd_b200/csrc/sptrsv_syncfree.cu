@@ -586,6 +586,7 @@ extern "C" int lcd_set_tuning(int key, int value) {
         case LCD_TUNE_ORDERED_PAUSE_NS: return set_ordered_pause(value);
         case LCD_TUNE_SMALL_THREADS: return set_small_threads(value);
         case LCD_TUNE_ILU0_LOOKAHEAD: return set_ilu0_lookahead(value);
+        case LCD_TUNE_ORDERED_MIN_LANES: return set_ordered_min_lanes(value);
         default: return LCD_ERR_INVALID_ARGUMENT;
     }
     return LCD_OK;

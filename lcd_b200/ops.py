@@ -376,8 +376,7 @@ class OrderedPlan:
         if self.levels <= 0:
             return 0
         # about four average levels, never fewer rows than keep every SM busy
-        lanes = 1 if nrhs == 1 else (2 if nrhs <= 2 else 4 if nrhs <= 4 else 8 if nrhs <= 16
-                                     else 16 if nrhs <= 32 else 32)
+        lanes = 2 if nrhs <= 2 else 4 if nrhs <= 4 else 8 if nrhs <= 32 else 16
         floor = 148 * 8 * (32 // lanes)
         return max(4 * n // self.levels, floor)
 
