@@ -666,12 +666,15 @@ def config_ilu0(args, size=128):
     steps = max(3, min(args.steps, 10))
     copy_ms = float(np.median(_time_steps(lambda: work.copy_(dA0), steps, 2)))
     results = {}
-    for mode in ("sync_free", "ordered", "wavefront"):
+    scratch = torch.empty_like(dA0)
+    max_row = int((dAp[1:] - dAp[:-1]).max())
+    for mode in ("sync_free", "ordered", "ordered_flags", "wavefront"):
         def step():
             work.copy_(dA0)
-            ops.spilu0_csr(dAp, dAi, work, pos, mode=mode, wavefronts=dag.wavefronts,
-                           wavefront_ptr_host=dag.wavefront_ptr_host, done=done,
-                           status=status, sync=False)
+            ops.spilu0_csr(dAp, dAi, work, pos, mode=mode.split("_flags")[0], wavefronts=dag.wavefronts,
+                           wavefront_ptr_host=dag.wavefront_ptr_host, done=done, status=status,
+                           sync=False, max_row=max_row,
+                           scratch=False if mode == "ordered_flags" else scratch)
         ms = _time_steps(step, steps, 2)
         results[mode] = float(np.median(ms)) - copy_ms   # the restore of A is not part of ILU0
         if ops.read_status(status)[0] != 0:

@@ -431,6 +431,23 @@ int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
                    void *stream, int *status_host);
 
 /*
+ * The same factorisation in one launch with rows handed out in `order` (the level sets of
+ * lcd_dag_build with LCD_OP_ILU0_CSR; NULL = by index) and the factor's entries as their own
+ * ready flags: the factor is built in `factor_scratch` (nnz doubles, pre-filled by the call with a
+ * reserved NaN pattern), a row polls exactly the entries of its pivot rows that it needs there
+ * and publishes its own with plain stores - no flags, no fences, one L2 round trip per
+ * dependence.  A is only read until the factor is complete and replaced by it at the end; after
+ * an error it is unchanged.  Bit-identical to lcd_spilu0_csr.  Rows must fit the lanes'
+ * registers (2 entries per lane, lanes_per_row = 4 / 8 / 16 / 32, 0 = from nnz / n): a longer row
+ * gives LCD_ERR_TOO_LARGE - use lcd_spilu0_csr (mode 2) then.  flags: 0 or
+ * LCD_ILU0_SKIP_STORED_ZEROS.  Replaces the same reference kernel (compiler/cuda_lowering.py:1572-1989).
+ */
+int lcd_spilu0_csr_ordered(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai, double *Ax,
+                           const int32_t *diag_pos, const int32_t *order, double *factor_scratch,
+                           int flags, int lanes_per_row, int32_t *status_dev, int32_t timeout_ms,
+                           void *stream, int *status_host);
+
+/*
  * ILU(0) for callers that cannot allocate.  No counterpart in the reference: it exists
  * for users of this library that call it where device memory cannot be requested (inside
  * a fixed memory pool, in a callback that runs while the allocator is held elsewhere, or

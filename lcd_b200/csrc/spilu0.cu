@@ -14,7 +14,9 @@
 // Wavefront mode: one launch per level over the same row code.
 // Ordered mode: the sync-free kernel with rows handed out in the order of the level sets
 // instead of by index: one launch, no barrier between levels, and the rows of a level -
-// independent of each other - are resident together.
+// independent of each other - are resident together.  lcd_spilu0_csr_ordered goes one step
+// further and drops the flags: the factor is written to a second array whose entries are
+// their own ready flags (ilu0_valueflag_kernel below).
 #include "common.cuh"
 
 namespace lcd {
@@ -336,6 +338,218 @@ __global__ void __launch_bounds__(TPB) ilu0_lookahead_kernel(const Ilu0Params p)
     if (lane == 0) st_release_s32(p.done + i, 1);
 }
 
+// ---- rows in level order, values as their own ready flags --------------------------------
+// The kernels above announce a finished row with a release store to done[row] and a consumer
+// follows its poll with an acquire fence: two fences and two round trips through L2 per hop.
+// Here the factor is written to a second array `out` that starts out filled with the reserved
+// NaN pattern (the trick of the triangular solves): a row reads its own entries from A, which
+// nobody modifies, polls exactly the entries of its pivot rows that it needs - the diagonal
+// u_kk and the matched u_kj - in `out`, and publishes its finished entries there with relaxed
+// stores.  No flags, no fences; one round trip per hop.  Arithmetic and its order are those of
+// the sequential loop (pivots ascending, unfused multiply / subtract): bit-identical.
+// All lanes of a warp run every trip and every vote is a full-warp ballot read through the
+// group's mask, as in the ordered triangular solve.  Rows longer than kIluOwn * G entries do
+// not fit the lanes' registers: the kernel reports LCD_ERR_TOO_LARGE before it touches anything
+// (the caller then uses the flag-based kernel; A is still intact).
+// P pivots are looked up and polled together: three measured faster than four (fewer loads and
+// votes per trip; 1.17 against 1.32 ms on the 128^3 grid) and than two; three blocks of 256
+// threads per SM (77 registers) faster than four with spills and than two.
+constexpr int kIluTripPivots = 3;
+template <int G, int P, int BPS>
+__global__ void __launch_bounds__(256, BPS) ilu0_valueflag_kernel(const Ilu0Params p, double *out) {
+    constexpr int R = 256 / G;
+    constexpr unsigned kFull = 0xffffffffu;
+    __shared__ int s_chunk;
+    if (threadIdx.x == 0) s_chunk = atomicAdd(&p.status[kStatusTicket], 1);
+    __syncthreads();
+    const int local = threadIdx.x / G, gl = threadIdx.x % G;
+    const int lane32 = threadIdx.x & 31, gbase = lane32 & ~(G - 1);
+    const unsigned gmask = G == 32 ? kFull : (((1u << G) - 1u) << gbase);
+    const int task = s_chunk * R + local;
+    bool active = task < p.n;
+    int i = task;
+    if (active && p.wavefronts) {
+        i = __ldg(p.wavefronts + task);
+        if ((unsigned)i >= (unsigned)p.n) {
+            if (gl == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, task);
+            active = false;
+        }
+    }
+    int s = 0, e = 0;
+    if (active) {
+        s = __ldg(p.Ap + i);
+        e = __ldg(p.Ap + i + 1);
+        if (s < 0 || e < s || (long long)e > p.nnz) {
+            if (gl == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, i);
+            active = false;
+        } else if (e - s > kIluOwn * G) {
+            if (gl == 0) raise_error(p.status, LCD_ERR_TOO_LARGE, i);
+            active = false;
+        }
+    }
+    // the lane's own entries of row i: positions s + gl + o * G
+    int col[kIluOwn];
+    double val[kIluOwn];
+#pragma unroll
+    for (int o = 0; o < kIluOwn; ++o) {
+        const int jp = s + gl + o * G;
+        col[o] = -1;
+        val[o] = 0.0;
+        if (active && jp < e) { col[o] = __ldg(p.Ai + jp); val[o] = p.Ax[jp]; }
+    }
+    int kp = s;                 // position of the next pivot in row i
+    bool lookup = active;       // the next pivots have to be looked up
+    bool failed = false;
+    int pd[P], match[P][kIluOwn];
+    int npiv = 0, applied = 0;
+    bool more = false;
+    unsigned pause = 0;
+    Deadline dl;
+    dl.start(p.budget_ns);
+    for (;;) {
+        // ---- pattern only: the next pivots, their diagonals, the matches of the own entries ----
+        if (lookup) {
+            lookup = false;
+            npiv = 0;
+            applied = 0;
+            int pk[P], pks[P], pke[P];
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+                pk[q] = -1; pks[q] = 0; pke[q] = 0; pd[q] = -1;
+                if (npiv == q && kp + q < e && !failed) {
+                    const int k = __ldg(p.Ai + kp + q);
+                    if (k < 0 || k >= p.n) {
+                        if (gl == 0) raise_error(p.status, LCD_ERR_INDEX_RANGE, i);
+                        failed = true;
+                    } else if (k < i) {
+                        pk[q] = k;
+                        npiv = q + 1;
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+                if (q < npiv) {
+                    pks[q] = __ldg(p.Ap + pk[q]);
+                    pke[q] = __ldg(p.Ap + pk[q] + 1);
+                    pd[q] = __ldg(p.dpos + pk[q]);
+                    if (pks[q] < 0 || pke[q] < pks[q] || (long long)pke[q] > p.nnz ||
+                        (long long)pd[q] >= p.nnz) {
+                        if (gl == 0) raise_error(p.status, LCD_ERR_BAD_POINTERS, pk[q]);
+                        failed = true;
+                    }
+                }
+            }
+            if (failed) npiv = 0;
+            // a full chunk: is the entry behind it another pivot?
+            more = false;
+            if (npiv == P && kp + P < e) {
+                const int k = __ldg(p.Ai + kp + P);
+                more = k >= 0 && k < i;
+            }
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+#pragma unroll
+                for (int o = 0; o < kIluOwn; ++o) {
+                    match[q][o] = -1;
+                    const int jp = s + gl + o * G;
+                    if (q < npiv && jp < e && jp > kp + q) {
+                        int lo = pks[q], hi = pke[q];   // leftmost entry of the pivot row that is >= col
+                        while (lo < hi) {
+                            const int mid = (lo + hi) >> 1;
+                            if (__ldg(p.Ai + mid) < col[o]) lo = mid + 1; else hi = mid;
+                        }
+                        if (lo < pke[q] && __ldg(p.Ai + lo) == col[o]) match[q][o] = lo;
+                    }
+                }
+            }
+        }
+        // ---- one non-blocking look at everything the outstanding pivots need ----
+        double dg[P], u[P][kIluOwn];
+        unsigned mine = 0;     // bit q: this lane has all it needs of pivot q
+#pragma unroll
+        for (int q = 0; q < P; ++q) {
+            dg[q] = 0.0;
+            const bool on = active && q >= applied && q < npiv;
+            bool ok = true;
+            if (on && pd[q] >= 0) {
+                dg[q] = ld_relaxed_f64(out + pd[q]);
+                ok = !is_pending(dg[q]);
+            }
+#pragma unroll
+            for (int o = 0; o < kIluOwn; ++o) {
+                u[q][o] = 0.0;
+                if (on && match[q][o] >= 0) {
+                    u[q][o] = ld_relaxed_f64(out + match[q][o]);
+                    ok = ok && !is_pending(u[q][o]);
+                }
+            }
+            if (ok) mine |= 1u << q;
+        }
+        // pivots are applied in order: the ready prefix, the same for all lanes of the group
+        int upto = applied;
+#pragma unroll
+        for (int q = 0; q < P; ++q) {
+            const bool all = G == 1 ? (mine >> q & 1u) != 0
+                                    : (__ballot_sync(kFull, (mine >> q & 1u) != 0) & gmask) == gmask;
+            if (q == upto && q < npiv && all) ++upto;
+        }
+        const bool progressed = active && (upto > applied || npiv == 0 || failed);
+#pragma unroll
+        for (int q = 0; q < P; ++q) {
+            const bool on = active && q >= applied && q < upto && dg[q] != 0.0;   // (group-uniform)
+            const int rel = kp + q - s, owner = rel % G, slot = rel / G;
+            double lik = 0.0;
+            if (on && gl == owner) {
+                if (slot == 0) { lik = val[0] / dg[q]; val[0] = lik; }
+                else { lik = val[1] / dg[q]; val[1] = lik; }
+            }
+            if (G > 1) lik = __shfl_sync(kFull, lik, gbase + owner);
+            if (on) {
+#pragma unroll
+                for (int o = 0; o < kIluOwn; ++o)
+                    if (match[q][o] >= 0 && !(p.skip_stored_zeros && u[q][o] == 0.0))
+                        val[o] = __dsub_rn(val[o], __dmul_rn(lik, u[q][o]));
+            }
+        }
+        if (progressed) {
+            applied = upto;
+            if (failed || applied == npiv) {
+                if (more && !failed) {   // more pivots in the row
+                    kp += npiv;
+                    lookup = true;
+                } else {
+                    // the row is finished: its entries become visible one by one, each its own flag
+                    const double nanv = __longlong_as_double(kCanonicalNaN);
+#pragma unroll
+                    for (int o = 0; o < kIluOwn; ++o) {
+                        const int jp = s + gl + o * G;
+                        if (jp < e) st_relaxed_f64(out + jp, failed ? nanv : publishable(val[o]));
+                    }
+                    active = false;
+                }
+            }
+        }
+        if (__ballot_sync(kFull, active) == 0) break;
+        if (__any_sync(kFull, progressed)) {
+            pause = 0;
+        } else {
+            if (__any_sync(kFull, active && dl.tick(p.status, i))) failed = active;
+            pause = pause ? min(pause * 2, 256u) : 32u;
+            __nanosleep(pause);
+        }
+    }
+}
+
+// Copies the finished factor over A unless the factorisation reported an error.
+__global__ void __launch_bounds__(256) ilu0_commit_kernel(const int32_t *status, const double *__restrict__ out,
+                                                          double *Ax, long long nnz) {
+    if (status[kStatusCode] != 0) return;
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < nnz;
+         j += (long long)gridDim.x * blockDim.x)
+        Ax[j] = out[j];
+}
+
 template <int G>
 __global__ void __launch_bounds__(256) ilu0_level_kernel(const Ilu0Params p, int wave_start,
                                                         int wave_end) {
@@ -428,6 +642,44 @@ extern "C" int lcd_spilu0_csr(int32_t n, int64_t nnz, const int32_t *Ap, const i
             default: return LCD_ERR_INVALID_ARGUMENT;
         }
         LCD_CUDA_TRY(e);
+    }
+    return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_spilu0_csr_ordered(int32_t n, int64_t nnz, const int32_t *Ap, const int32_t *Ai,
+                                      double *Ax, const int32_t *diag_pos, const int32_t *order,
+                                      double *factor_scratch, int flags, int lanes_per_row,
+                                      int32_t *status_dev, int32_t timeout_ms, void *stream,
+                                      int *status_host) {
+    if (n < 0 || nnz < 0 || !status_dev || (flags & ~LCD_ILU0_SKIP_STORED_ZEROS))
+        return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Ap || !Ai || !diag_pos || (nnz > 0 && (!Ax || !factor_scratch || factor_scratch == Ax))))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int G = lanes_per_row;
+    if (G <= 0) {
+        const double avg = n > 0 ? (double)nnz / n : 0.0;
+        G = avg <= 7 ? 4 : (avg <= 15 ? 8 : (avg <= 31 ? 16 : 32));
+    }
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (n > 0 && nnz > 0) {
+        rc = lcd_fill_u64(reinterpret_cast<uint64_t *>(factor_scratch), nnz, kPendingBits, st);
+        if (rc) return rc;
+        Ilu0Params p{n, nnz, Ap, Ai, Ax, diag_pos, nullptr, order, status_dev, timeout_ns(timeout_ms),
+                     (flags & LCD_ILU0_SKIP_STORED_ZEROS) ? 1 : 0};
+        switch (G) {
+            case 4: ilu0_valueflag_kernel<4, kIluTripPivots, 3><<<(n + 63) / 64, 256, 0, st>>>(p, factor_scratch); break;
+            case 8: ilu0_valueflag_kernel<8, kIluTripPivots, 3><<<(n + 31) / 32, 256, 0, st>>>(p, factor_scratch); break;
+            case 16: ilu0_valueflag_kernel<16, kIluTripPivots, 3><<<(n + 15) / 16, 256, 0, st>>>(p, factor_scratch); break;
+            case 32: ilu0_valueflag_kernel<32, kIluTripPivots, 3><<<(n + 7) / 8, 256, 0, st>>>(p, factor_scratch); break;
+            default: return LCD_ERR_INVALID_ARGUMENT;
+        }
+        LCD_CUDA_TRY(cudaGetLastError());
+        // A is replaced only when the factor is complete: after an error (a row too long for the
+        // lanes' registers, bad pointers, a wait that ran out) the caller still holds A
+        ilu0_commit_kernel<<<sm_count() * 8, 256, 0, st>>>(status_dev, factor_scratch, Ax, nnz);
+        LCD_CUDA_TRY(cudaGetLastError());
     }
     return finish(status_dev, st, status_host);
 }

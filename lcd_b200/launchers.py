@@ -285,7 +285,14 @@ def bind(lowering):
             if dag is not None and dag.n_levels > 0 and dag.n / dag.n_levels >= 8:
                 # rows in the order of the level sets: the rows of a level run side by side
                 # (by index, a grid matrix keeps one grid line in flight)
-                ops.spilu0_csr(Ap, Ai, Ax, pos, mode="ordered", wavefronts=dag.wavefronts, lanes=lanes)
+                cache = (_hints or {}).get("cache", {})
+                if "ilu0_max_row" not in cache:            # once per pattern: picks the lanes per row
+                    cache["ilu0_max_row"] = int((Ap[1:] - Ap[:-1]).max()) if Ap.numel() > 1 else 0
+                if cache.get("ilu0_scratch") is None or cache["ilu0_scratch"].numel() < Ai.numel():
+                    cache["ilu0_scratch"] = torch.empty(max(Ai.numel(), 1), dtype=torch.float64,
+                                                        device=Ax.device)
+                ops.spilu0_csr(Ap, Ai, Ax, pos, mode="ordered", wavefronts=dag.wavefronts, lanes=lanes,
+                               max_row=cache["ilu0_max_row"], scratch=cache["ilu0_scratch"])
             else:
                 ops.spilu0_csr(Ap, Ai, Ax, pos, mode="sync_free", lanes=lanes)
         else:

@@ -574,10 +574,14 @@ def sptrsv_wavefront(op, Ap, Ai, Ax, b, wavefronts, wavefront_ptr, wavefront_ptr
 
 def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
                wavefront_ptr_host=None, done=None, lanes=0, status=None, timeout_ms=0, sync=True,
-               skip_stored_zeros=False):
+               skip_stored_zeros=False, scratch=None, max_row=None):
     """In-place ILU(0) of a sorted CSR matrix; returns Ax.  ``mode``: "sync_free" (rows by
     index), "ordered" (sync-free, rows in the order of ``wavefronts``) or "wavefront" (a launch
-    per level)."""
+    per level).  ``scratch`` (ordered mode): nnz doubles for the kernel that uses the factor's
+    entries as their own ready flags, allocated when None; False selects the flag-based kernel.
+    ``max_row`` (longest row, when the caller knows it) picks the lanes per row and skips that
+    kernel for rows of more than 64 entries; without it and without ``sync`` a row too long for
+    the kernel shows up in ``status`` (A unchanged)."""
     _require(Ax, torch.float64, "Ax")
     _require(diag_pos, torch.int32, "diag_pos")
     n = Ap.numel() - 1
@@ -593,6 +597,21 @@ def spilu0_csr(Ap, Ai, Ax, diag_pos, *, mode="sync_free", wavefronts=None,
     elif mode == "ordered":
         # sync-free, rows handed out in the order of the level sets
         _require(wavefronts, torch.int32, "wavefronts")
+        if (max_row is not None and max_row > 64) or lanes in (1, 2):
+            scratch = False
+        if scratch is not False:
+            # the factor's entries as their own ready flags (rows must fit the lanes' registers)
+            if max_row is not None and not lanes:
+                lanes = 4 if max_row <= 8 else 8 if max_row <= 16 else 16 if max_row <= 32 else 32
+            if scratch is None or scratch.numel() < Ai.numel():
+                scratch = torch.empty(max(Ai.numel(), 1), dtype=torch.float64, device=Ax.device)
+            rc = nat.load().lcd_spilu0_csr_ordered(
+                n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), ptr(wavefronts), ptr(scratch),
+                extra, int(lanes), ptr(status), int(timeout_ms), _stream(),
+                ctypes.byref(host) if sync else None)
+            if rc != nat.ERR_TOO_LARGE and not (sync and host.value == nat.ERR_TOO_LARGE):
+                check(rc, "lcd_spilu0_csr_ordered")
+                return Ax
         done = torch.empty(n, dtype=torch.int32, device=Ax.device) if done is None else done
         rc = nat.load().lcd_spilu0_csr(n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(Ax), ptr(diag_pos), 2 + extra,
                                        ptr(done), ptr(wavefronts), None, 0, int(lanes), ptr(status),

@@ -179,6 +179,50 @@ def test_ilu0_ordered_then_ordered_solves_on_the_factors(cuda, oracle):
             np.testing.assert_allclose(X[:, q], x_ref, rtol=1e-10, atol=1e-12)
 
 
+def test_ilu0_value_flag_kernel_matches_flag_kernel_and_falls_back(cuda, oracle):
+    """Ordered ILU0 with the factor's entries as their own ready flags: same bits as the
+    flag-based kernel and the sequential loop; a row too long for the lanes' registers is
+    reported with A untouched, and the wrapper then takes the flag-based kernel."""
+    import torch
+    from lcd_b200 import _native as nat, generators as gen, ops
+    mat, _ = gen.laplacian3d_ilu0(21, seed=2)
+    Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    dAp, dAi = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda)
+    pos = ops.diag_positions(dAp, dAi)
+    d = ops.dag_build("ilu0_csr", dAp, dAi)
+    want = oracle.ilu0_csr(Ap, Ai, Ax, fast=True)
+    scratch = torch.empty(len(Ai), dtype=torch.float64, device=cuda)
+    for lanes in (0, 4, 8, 16, 32):
+        got = ops.spilu0_csr(dAp, dAi, dev(Ax, np.float64, cuda), pos, mode="ordered",
+                             wavefronts=d.wavefronts, lanes=lanes, scratch=scratch, max_row=7)
+        np.testing.assert_array_equal(host(got), want)
+    flagged = ops.spilu0_csr(dAp, dAi, dev(Ax, np.float64, cuda), pos, mode="ordered",
+                             wavefronts=d.wavefronts, scratch=False)
+    np.testing.assert_array_equal(host(flagged), want)
+    # a dense-ish banded matrix: rows of up to 81 entries do not fit 2 x 32 registers
+    rng = np.random.default_rng(3)
+    n = 400
+    B = sp.diags([rng.uniform(0.01, 0.1, n - abs(k)) for k in range(-40, 41)], list(range(-40, 41)),
+                 format="csr") + 10.0 * sp.identity(n, format="csr")
+    B = sp.csr_matrix(B)
+    B.sort_indices()
+    Bp, Bi, Bx = B.indptr.astype(np.int32), B.indices.astype(np.int32), B.data.copy()
+    dBp, dBi = dev(Bp, np.int32, cuda), dev(Bi, np.int32, cuda)
+    bpos = ops.diag_positions(dBp, dBi)
+    bd = ops.dag_build("ilu0_csr", dBp, dBi)
+    work = dev(Bx, np.float64, cuda)
+    status = ops.new_status(cuda)
+    factor = torch.empty(len(Bi), dtype=torch.float64, device=cuda)
+    rc = nat.load().lcd_spilu0_csr_ordered(
+        n, len(Bi), nat.ptr(dBp), nat.ptr(dBi), nat.ptr(work), nat.ptr(bpos), nat.ptr(bd.wavefronts),
+        nat.ptr(factor), 0, 32, nat.ptr(status), 500, None, None)
+    assert rc == nat.OK
+    assert ops.read_status(status)[0] == nat.ERR_TOO_LARGE
+    np.testing.assert_array_equal(host(work), Bx)            # A is only replaced by a complete factor
+    got = ops.spilu0_csr(dBp, dBi, work, bpos, mode="ordered", wavefronts=bd.wavefronts)
+    np.testing.assert_array_equal(host(got), oracle.ilu0_csr(Bp, Bi, Bx, fast=True))
+
+
 def test_ilu0_reports_corrupted_pointers(cuda):
     """A pivot row whose pointers are not monotone is reported, not searched."""
     from lcd_b200 import _native as nat, generators as gen, ops
