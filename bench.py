@@ -60,6 +60,8 @@ SIDE_WORKLOADS = {
     "multirhs_lap3d_g96": ("multirhs", 96),
     "partition_lap3d_g256": ("partition", 256),
     "partition_lap3d_g128": ("partition", 128),
+    "literal_kernels_lap3d_g96": ("literal", 96),
+    "literal_kernels_lap3d_g48": ("literal", 48),
 }
 DEFAULT_WORKLOAD = "sptrsv_random_n4194304"
 
@@ -261,6 +263,16 @@ def run_native(args):
     dag_build_ms = (time.perf_counter() - t0) * 1e3
     levels, dag_edges = dag.n_levels, dag.n_edges
     del dag
+    # what the decorated call runs first: the build stops the level propagation as soon as a row
+    # passes rows / 64 levels (enough to pick the chain solver); the level sets are completed
+    # only if something asks for them
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    capped = ops.dag_build("csr_lower", dAp, dAi, level_cap=max(n // 64, 1))
+    torch.cuda.synchronize()
+    dag_build_capped_ms = (time.perf_counter() - t0) * 1e3
+    level_cap_hit = bool(capped.capped)
+    del capped
     solver = args.solver
     if solver == "auto":
         solver = "chain" if chain_solver_preferred(n, levels) else "row"
@@ -323,7 +335,8 @@ def run_native(args):
     if not args.kernel_only:
         e2e = measure_e2e(args, Ap, Ai, Ax, b, n, nnz, world, dev, barrier)
 
-    extras = {"dag_build_ms": dag_build_ms, "levels": levels, "dag_edges": dag_edges}
+    extras = {"dag_build_ms": dag_build_ms, "dag_build_capped_ms": dag_build_capped_ms,
+              "level_cap_hit": level_cap_hit, "levels": levels, "dag_edges": dag_edges}
     if rank == 0 and solver == "chain":
         # the two kernels of a step apart (events around each)
         extras["prepare_ms"] = float(np.mean(_time_steps(
@@ -354,7 +367,8 @@ def run_native(args):
                        "threads_per_block": threads or 1024, "rhs_per_gpu": 1,
                        "l2_policy": "inputs (%.2f GB) exceed the 126 MB L2" % (
                            algorithmic_bytes(n, nnz) / 1e9)},
-            "e2e": e2e, "gpu_launches": args.steps * launches_per_step,
+            "e2e": e2e, "e2e_cold_ms": (e2e or {}).get("first_call_ms"),
+            "gpu_launches": args.steps * launches_per_step,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": (TRAFFIC_BYTES_PER_ROW[kernel_name] * n
@@ -875,7 +889,102 @@ def config_partition(args, size=256):
             "parity": {"relative_residual": residual, "tolerance": 1e-12, "ok": bool(residual <= 1e-12)}}
 
 
-CONFIG_RUNNERS = {"ilu0": config_ilu0, "supernodal": config_supernodal, "multirhs": config_multirhs,
+# ---- the literal counterparts of the reference's generated kernels, one small grid ------------
+def config_literal_kernels(args, size=96):
+    """Every kernel that mirrors one of the reference's generated variants directly (index-ordered
+    polling with one and with several lanes per row, the push kernel on CSC storage, per-level
+    and cooperative wavefront kernels, the multi-right-hand-side polling and wavefront kernels,
+    ILU0 by index / per level), once each on the 3-D grid, checked against the CPU port.  The
+    launcher prefers the level-ordered kernels over all of these on such a matrix; the record
+    says by how much."""
+    import torch
+    import scipy.sparse as sp
+    from lcd_b200 import generators as gen, ops
+    from oracle import oracle as cpu
+    _, _, _, dev = _context()
+    up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    tri = gen.laplacian3d_tril(size, seed=0)
+    Ap, Ai, Ax = tri.csr_arrays()
+    Cp, Ci, Cx = tri.csc_arrays()
+    n, nnz = tri.n, tri.nnz
+    dAp, dAi, dAx, db = up(Ap), up(Ai), up(Ax), up(tri.b)
+    dCp, dCi, dCx = up(Cp), up(Ci), up(Cx)
+    status = ops.new_status(dev)
+    want = cpu.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+    dag = ops.dag_build("csr_lower", dAp, dAi)
+    cdag = ops.dag_build("csc_lower", dCp, dCi)
+    x = torch.empty_like(db)
+    reps = max(2, min(args.steps, 5))
+    out = {}
+
+    def timed(name, fn, result=None, reference=None):
+        ms = float(np.median(_time_steps(fn, reps, 1)))
+        rec = {"ms": ms}
+        if result is not None:
+            got = result().cpu().numpy()
+            ref = want if reference is None else reference
+            rec["max_rel_error"] = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
+        if ops.read_status(status)[0] != 0:
+            rec["status"] = int(ops.read_status(status)[0])
+        out[name] = rec
+
+    timed("csr_syncfree_row_kernel", lambda: ops.sptrsv_csr_syncfree(
+        dAp, dAi, dAx, db, x, lanes=1, status=status, sync=False), lambda: x)
+    timed("csr_syncfree_kernel<4>", lambda: ops.sptrsv_csr_syncfree(
+        dAp, dAi, dAx, db, x, lanes=4, status=status, sync=False), lambda: x)
+    counts = ops.csc_edge_count(dCp, dCi)
+    timed("csc_syncfree_kernel", lambda: ops.sptrsv_csc_syncfree(
+        dCp, dCi, dCx, db, counts.clone(), x, status=status, sync=False), lambda: x)
+    timed("wavefront_coop_kernel", lambda: ops.sptrsv_wavefront(
+        "csr_lower", dAp, dAi, dAx, db, dag.wavefronts, dag.wavefront_ptr, None, x,
+        mode="cooperative", status=status, sync=False), lambda: x)
+    timed("wavefront_level_kernel (a launch per level)", lambda: ops.sptrsv_wavefront(
+        "csr_lower", dAp, dAi, dAx, db, dag.wavefronts, dag.wavefront_ptr, dag.wavefront_ptr_host, x,
+        mode="per_level", status=status, sync=False), lambda: x)
+    timed("csc wavefront_coop_kernel", lambda: ops.sptrsv_wavefront(
+        "csc_lower", dCp, dCi, dCx, db, cdag.wavefronts, cdag.wavefront_ptr, None, x,
+        mode="cooperative", status=status, sync=False), lambda: x)
+    plan = ops.OrderedPlan(dag.wavefronts, dag.n_levels)
+    timed("csr_ordered_kernel (what the launcher uses)", lambda: ops.sptrsv_csr_ordered(
+        dAp, dAi, dAx, db, plan, x, status=status, sync=False), lambda: x)
+    # eight right-hand sides
+    B = np.random.default_rng(3).uniform(-1, 1, (n, 8))
+    dB = up(B)
+    X = torch.empty_like(dB)
+    want8 = cpu.sptrsv_csr_lower(Ap, Ai, Ax, np.ascontiguousarray(B[:, 5]))
+    timed("csr_syncfree_multi_kernel (8 rhs)", lambda: ops.sptrsv_csr_syncfree_multi(
+        dAp, dAi, dAx, dB, X, status=status, sync=False), lambda: X[:, 5], want8)
+    timed("wavefront_multi_coop_kernel (8 rhs)", lambda: ops.sptrsv_wavefront_multi(
+        dAp, dAi, dAx, dB, dag.wavefronts, dag.wavefront_ptr, X, status=status, sync=False),
+        lambda: X[:, 5], want8)
+    timed("csr_ordered_kernel (8 rhs)", lambda: ops.sptrsv_csr_ordered(
+        dAp, dAi, dAx, dB, plan, X, status=status, sync=False), lambda: X[:, 5], want8)
+    # ILU0 by index and per level on the matching full matrix
+    mat, _ = gen.laplacian3d_ilu0(size, seed=0)
+    Fp, Fi, Fx = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    dFp, dFi, dF0 = up(Fp), up(Fi), up(Fx)
+    work = dF0.clone()
+    pos = ops.diag_positions(dFp, dFi)
+    fdag = ops.dag_build("ilu0_csr", dFp, dFi)
+    fwant = cpu.ilu0_csr(Fp, Fi, Fx, fast=True)
+    done = torch.empty(len(Fp) - 1, dtype=torch.int32, device=dev)
+    for name, kw in (("ilu0_lookahead_kernel by index", dict(mode="sync_free")),
+                     ("ilu0_level_kernel (a launch per level)", dict(mode="wavefront")),
+                     ("ilu0_lookahead_kernel in level order", dict(mode="ordered", scratch=False)),
+                     ("ilu0_valueflag_kernel (what the launcher uses)", dict(mode="ordered"))):
+        def step():
+            work.copy_(dF0)
+            ops.spilu0_csr(dFp, dFi, work, pos, wavefronts=fdag.wavefronts,
+                           wavefront_ptr_host=fdag.wavefront_ptr_host, done=done, status=status,
+                           sync=False, max_row=7, **kw)
+        ms = float(np.median(_time_steps(step, reps, 1)))
+        out[name] = {"ms_with_restore_of_A": ms,
+                     "bit_identical": bool(np.array_equal(work.cpu().numpy(), fwant))}
+    return {"workload": f"literal_kernels_lap3d_g{size}", "n": n, "nnz": nnz, "levels": dag.n_levels,
+            "kernels": out}
+
+
+CONFIG_RUNNERS = {"literal": config_literal_kernels, "ilu0": config_ilu0, "supernodal": config_supernodal, "multirhs": config_multirhs,
                   "csc": config_csc_lap2d, "partition": config_partition}
 
 
@@ -947,6 +1056,11 @@ def main():
     parser.add_argument("--skip-configs", action="store_true",
                         help="headline configuration only: skip the records of the other configurations")
     args = parser.parse_args()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # the data path uses plain peer stores and NCCL only for gathers and small reductions:
+        # no in-switch reduction is needed, and a rank that stops with an error must not leave
+        # memory bound to an NVLink multicast object
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     args.warmup = max(args.warmup, 3) if args.impl == "native" else args.warmup
     if args.workload in SIDE_WORKLOADS:
         run_side_workload(args)

@@ -23,7 +23,7 @@
 // one commit group per batch): while batch k is solved, the records of batch k + 2 and
 // the entries, diagonal and right-hand side of batch k + 1 are in flight, each stage's
 // addresses coming from copies that landed a batch earlier.  Staging in shared memory
-// instead of registers keeps the kernel at 64 registers, i.e. 32 warps per SM:
+// instead of registers keeps the kernel at 64 registers (KR <= 2), i.e. 32 warps per SM:
 // the solve is bound by memory latency, so resident warps are what fills HBM.  A warp holds
 // no more than these three batches: a task queued behind others in one warp waits for them,
 // which costs hand-offs when levels are narrow.  What remains on the chain of a row is:
@@ -31,9 +31,18 @@
 //
 // Waiting.  All groups of a warp make one non-blocking attempt per trip and the trip ends
 // in a warp-wide vote, so no lane spins inside a branch (rows of one warp may depend on
-// each other).  A warp none of whose groups progressed sleeps before the next trip, with
-// an exponentially growing pause: rows far behind the frontier then stop competing for L2
-// with the polls that matter.  Every wait is bounded (status block, LCD_ERR_TIMEOUT).
+// each other).  Every lane runs every trip, and a group's vote is a full-warp ballot read
+// through the group's mask: a vote instruction with one mask per group is executed once per
+// group and leaves the groups split behind it (measured: 500 warp instructions per trip
+// instead of 50, 3.4 us per hand-off instead of 1.9).  A warp none of whose groups progressed
+// sleeps before the next trip, with an exponentially growing pause: rows far behind the
+// frontier then stop competing for L2 with the polls that matter.  Every wait is bounded
+// (status block, LCD_ERR_TIMEOUT).
+//
+// Rows per warp.  A warp moves on when its slowest row is done, so few rows per warp are
+// better than many: with one right-hand side two lanes per row (16 rows per warp, the second
+// lane idle) take half the time of one lane per row.  With many right-hand sides a lane takes
+// four of them (KR = 4, three entries of a row per trip, 74 registers, three blocks per SM).
 //
 // Hand-off.  Two forms: (a) X pre-filled with the reserved NaN pattern, consumers poll
 // the operand elements themselves (one L2 round trip per hop; costs one extra write pass
@@ -141,8 +150,8 @@ struct WarpStage {
 // SYS: block-row partition across GPUs - operands may arrive from a peer (system-scope polls)
 // and a published value is also stored into the x arrays of the ranks that need it.
 template <int W, int KR, bool FLAGS, bool SYS = false>
-__global__ void __launch_bounds__(kOrdThreads, 4) csr_ordered_kernel(const OrderedParams q) {
-    constexpr int S = KR <= 2 ? kStage : (KR <= 4 ? 2 : 1);   // entries tried per trip (registers)
+__global__ void __launch_bounds__(kOrdThreads, KR >= 4 ? 3 : 4) csr_ordered_kernel(const OrderedParams q) {
+    constexpr int S = KR <= 2 ? kStage : (KR <= 4 ? 3 : 1);   // entries tried per trip (registers)
     extern __shared__ __align__(16) unsigned char ordered_smem[];
     const CsrSolveParams &p = q.m;
     constexpr int G = 32 / W;
@@ -459,11 +468,12 @@ extern "C" int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, cons
                 q.m, order, n, reinterpret_cast<TaskMeta *>(task_records));
             LCD_CUDA_TRY(cudaGetLastError());
         }
-        // (lanes per row) x (right-hand sides per lane) >= nrhs.  Measured on 3-D grids (192^3): two
-        // to eight lanes per row are fastest whatever the number of right-hand sides up to eight
-        // (one lane per row, i.e. 32 rows per warp, is twice as slow even for one right-hand side:
-        // a warp moves on when its slowest row is done); beyond that the lanes take two, then four
-        // right-hand sides each.
+        // (lanes per row) x (right-hand sides per lane) >= nrhs.  Measured on a 3-D grid (192^3):
+        // with one lane per row (32 rows per warp) a solve takes twice as long as with two, even
+        // for one right-hand side (a warp moves on when its slowest row is done); two to eight
+        // lanes per row are fastest up to eight right-hand sides; beyond that four right-hand
+        // sides per lane (three entries per trip, three blocks per SM) beat two: 1.8 / 2.3 / 3.3 ms
+        // for 16 / 32 / 64 right-hand sides against 2.0 / 2.8 / 4.7.
         int W, KR;
         if (g_ordered_min_lanes >= 100) {        // explicit variant (tuning runs): 100 * W + KR
             W = g_ordered_min_lanes / 100;
@@ -471,7 +481,7 @@ extern "C" int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, cons
             if (W * KR < nrhs) return LCD_ERR_INVALID_ARGUMENT;
         } else {
             W = nrhs <= 2 ? 2 : (nrhs <= 4 ? 4 : (nrhs <= 32 ? 8 : 16));
-            KR = nrhs <= 8 ? 1 : (nrhs <= 16 ? 2 : 4);
+            KR = nrhs <= 8 ? 1 : 4;
             if (KR == 1 && g_ordered_min_lanes > W) W = g_ordered_min_lanes;   // 4 or 8 lanes per row
             if (nrhs == 1 && g_ordered_min_lanes == 1) W = 1;
         }
