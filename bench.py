@@ -280,10 +280,12 @@ def run_native(args):
         workspace = ops.chain_workspace(n, dev)
 
         def step():
-            # numeric preparation (block tiles from the values) and solve, both timed
-            ops.chain_prepare(dAp, dAi, dAx, workspace)
-            ops.sptrsv_csr_chain(dAp, dAi, dAx, db, workspace, x, status=status, sync=False)
-        kernel_name, launches_per_step = "csr_chain_kernel", 2
+            # numeric preparation (block tiles from the values) and solve, both timed: the
+            # preparation runs range by range on a second stream, the solve of a range follows
+            # its own tiles (what the decorated call does when the values have changed)
+            ops.chain_prepare_and_solve(dAp, dAi, dAx, db, workspace, x, status=status, sync=False)
+        kernel_name = "csr_chain_kernel"
+        launches_per_step = 2 * (len(ops.chain_pipeline_bounds(n)) - 1)
     else:
         def step():
             ops.sptrsv_csr_syncfree(dAp, dAi, dAx, db, x, lanes=lanes, threads=threads,
@@ -361,7 +363,8 @@ def run_native(args):
             "data": "synthetic",
             "config": {"workload": args.workload, "n": n, "nnz": nnz, "format": "csr_lower",
                        "mode": "sync_free", "solver": solver,
-                       "step": ("lcd_chain_prepare + lcd_sptrsv_csr_chain" if solver == "chain"
+                       "step": ("lcd_chain_prepare_rows + lcd_sptrsv_csr_chain_rows, 16 row ranges, "
+                                "preparation on a second stream" if solver == "chain"
                                 else "lcd_sptrsv_csr_syncfree"),
                        "lanes_per_row": lanes or "auto",
                        "threads_per_block": threads or 1024, "rhs_per_gpu": 1,

@@ -131,10 +131,14 @@ def bind(lowering):
             cache.pop("chain_values", None)
         stamp = ops.fingerprint(Ax.view(torch.int32))
         if cache.get("chain_values") != stamp:
-            ops.chain_prepare(Ap, Ai, Ax, workspace, upper=lowering.upper)
+            # new values: preparation and solve pipelined over row ranges (the preparation is
+            # throughput work on a second stream, the solve runs on one SM at a time)
+            ops.chain_prepare_and_solve(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
             cache["chain_values"] = stamp
             # explicit block inverses are only as accurate as the blocks are well conditioned
             cache["chain_stable"] = ops.chain_growth(workspace, n) <= ops.CHAIN_MAX_GROWTH
+            if cache["chain_stable"]:
+                return
         if cache["chain_stable"]:
             ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=lowering.upper)
         else:           # substitution (still on the GPU): slower on such matrices, but stable

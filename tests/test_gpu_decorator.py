@@ -230,10 +230,22 @@ def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch
     from lcd_b200 import generators as gen, ops
     tri = gen.random_band_lower(65_536, seed=3)
     Ap, Ai, Ax = tri.csr_arrays()
+    # "prepare": preparation + solve pipelined over row ranges (new values); "solve": a solve in
+    # one piece on tiles that are kept
     calls = {"prepare": 0, "solve": 0}
-    real_prepare, real_solve = ops.chain_prepare, ops.sptrsv_csr_chain
-    monkeypatch.setattr(ops, "chain_prepare", lambda *a, **k: (calls.__setitem__("prepare", calls["prepare"] + 1), real_prepare(*a, **k))[1])
-    monkeypatch.setattr(ops, "sptrsv_csr_chain", lambda *a, **k: (calls.__setitem__("solve", calls["solve"] + 1), real_solve(*a, **k))[1])
+    real_pipeline, real_solve = ops.chain_prepare_and_solve, ops.sptrsv_csr_chain
+
+    def counted_pipeline(*a, **k):
+        calls["prepare"] += 1
+        calls["solve"] += 1
+        return real_pipeline(*a, **k)
+
+    def counted_solve(*a, **k):
+        if k.get("rows") is None:
+            calls["solve"] += 1
+        return real_solve(*a, **k)
+    monkeypatch.setattr(ops, "chain_prepare_and_solve", counted_pipeline)
+    monkeypatch.setattr(ops, "sptrsv_csr_chain", counted_solve)
     plan = od.csr_warp_syncfree.schedule_plan(Ap, Ai, Ax, tri.b, tri.n)
     assert plan.rows == tri.n and plan.rows / plan.levels < 64
     want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)

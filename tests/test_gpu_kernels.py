@@ -308,6 +308,27 @@ def test_csr_chain_solver_in_row_ranges(cuda, oracle):
     assert err.value.code == ERR_INVALID_ARGUMENT
 
 
+def test_csr_chain_prepare_and_solve_pipelined(cuda, oracle):
+    """Preparation on a second stream, range by range, with the solve of a range behind its
+    own tiles: same result as the two steps one after the other, for every number of pieces."""
+    import torch
+    from lcd_b200 import generators as gen, ops
+    for upper in (False, True):
+        tri = gen.random_band_lower(70_000, seed=21, mean_degree=15.0, band=64)
+        if upper:
+            tri = gen.upper_from_lower(tri)
+        Ap, Ai, Ax = tri.csr_arrays()
+        want = (oracle.sptrsv_csr_upper if upper else oracle.sptrsv_csr_lower)(Ap, Ai, Ax, tri.b)
+        dAp, dAi, dAx = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda)
+        db = dev(tri.b, np.float64, cuda)
+        ws = ops.chain_workspace(tri.n, cuda)
+        for pieces in (1, 2, 5, 8, 1000):
+            ws.zero_()
+            x = ops.chain_prepare_and_solve(dAp, dAi, dAx, db, ws, upper=upper, pieces=pieces)
+            np.testing.assert_allclose(host(x), want, rtol=1e-10, atol=1e-12)
+            assert ops.chain_growth(ws, tri.n) <= ops.CHAIN_MAX_GROWTH
+
+
 def test_csr_chain_solver_on_ilu_factors_and_errors(cuda, oracle):
     from lcd_b200 import generators as gen, ops
     from lcd_b200._native import ERR_INDEX_RANGE, ERR_WORKSPACE, NativeError
