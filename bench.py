@@ -108,7 +108,7 @@ def algorithmic_bytes(n, nnz):
 # DRAM traffic per row of the dominant kernel (dram__bytes_read.sum + dram__bytes_write.sum of one
 # ncu capture at 1,048,576 rows divided by the rows; both kernels' traffic grows in proportion to
 # the rows, so a launch on n rows is charged n times this; see profiles/)
-TRAFFIC_BYTES_PER_ROW = {"csr_chain_kernel": 1.233e9 / 1048576, "csr_syncfree_row_kernel": 227.3e6 / 1048576}
+TRAFFIC_BYTES_PER_ROW = {"csr_chain_kernel": 1.2314e9 / 1048576, "csr_syncfree_row_kernel": 227.3e6 / 1048576}
 
 
 def flops(n, nnz):
