@@ -760,7 +760,29 @@ def config_supernodal(args, size=1_048_576):
                               min_seconds=3.0, min_count=1)
     want = cpu.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b)
     err = float(np.max(np.abs(xs - want)) / np.max(np.abs(want)))
+    conversion = None
+    if size <= 131_072:
+        # the layout built on the device from the same matrix stored by columns
+        # (convert_csc_to_supernodal of the reference), then solved from the converted arrays
+        L = s.to_csc()
+        L.sort_indices()
+        up = lambda a, t: torch.from_numpy(np.ascontiguousarray(a, dtype=t)).to(dev)
+        dCp, dCi, dCx = up(L.indptr, np.int32), up(L.indices, np.int32), up(L.data, np.float64)
+        supernodal.from_csc(dCp, dCi, dCx, device=dev)          # warm-up (allocations)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layout = supernodal.from_csc(dCp, dCi, dCx, device=dev)
+        torch.cuda.synchronize()
+        convert_ms = (time.perf_counter() - t0) * 1e3
+        plan2 = supernodal.analyse(layout.sn, layout.Lip, layout.Li, layout.Lp, layout.Lx,
+                                   layout.col_to_super, device=dev)
+        x2 = supernodal.solve(plan2, db).cpu().numpy()
+        conversion = {"csc_nnz": int(L.nnz), "ms": convert_ms, "n_super": layout.n_super,
+                      "max_width": layout.max_width, "panel_values": int(layout.Lx.numel()),
+                      "solve_max_rel_error": float(np.max(np.abs(x2 - want)) / np.max(np.abs(want)))}
+        del plan2, layout, dCp, dCi, dCx
     return {"workload": f"supernodal_n{size}", "n": size, "n_super": plan.n_super, "tasks": plan.n_tasks,
+            "csc_to_supernodal": conversion,
             "panel_gb": plan.panel_values * 8 / 1e9, "ms": best,
             "gflops": plan.flops / (best * 1e-3) / 1e9, "analyse_and_upload_ms": analyse_ms,
             "status": code, "roofline": _roofline(plan.algorithmic_bytes, best, peak),

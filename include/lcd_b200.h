@@ -409,6 +409,33 @@ int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *
                      const int32_t *diag_src, const int32_t *slot_ptr_dev, int32_t n_levels,
                      int32_t max_width, void *scratch, int64_t scratch_bytes, void *stream);
 
+/* ---- CSC -> supernodal layout ------------------------------------------------------ */
+/*
+ * Supernodal layout of a lower-triangular matrix stored by columns (sorted rows): replaces
+ * detect_supernodes + convert_csc_to_supernodal (utils/symbolic_cholesky_csc.py:883-921,
+ * 950-1021).  Column j + 1 joins column j's supernode when the symmetric difference of their row
+ * patterns has at most relaxation + 1 elements; the row structure of a supernode (Li[Lip[s] ..
+ * Lip[s+1])) is the sorted union of its columns' patterns; column j holds one value per row of
+ * that union at Lx[Lp[j] ..] (zero where it stores none).  Two calls because the sizes of Li and
+ * Lx depend on the pattern:
+ *   lcd_supernodal_layout - structure: col_to_super (n), super_begin (n + 1 ints, the first
+ *     n_super + 1 meaningful), Lip (n + 1 ints, likewise), Li (nnz ints, the first Lip[n_super]
+ *     meaningful), Lp (n + 1 64-bit offsets).  summary_host[4] = {n_super, Lip[n_super], widest
+ *     supernode, Lp[n]}.  Synchronises the stream.
+ *   lcd_supernodal_fill - values: zeroes Lx[0 .. panel_values) and scatters Cx into it; repeat
+ *     when the values change.
+ * The arrays feed lcd_sptrsv_supernodal unchanged (sn = super_begin).
+ */
+int lcd_supernodal_layout_workspace_bytes(int32_t n, int64_t nnz, int64_t *bytes);
+int lcd_supernodal_layout(int32_t n, int64_t nnz, const int32_t *Cp, const int32_t *Ci,
+                          int32_t relaxation, int32_t *col_to_super, int32_t *super_begin,
+                          int32_t *Lip, int32_t *Li, int64_t *Lp, int64_t *summary_host,
+                          void *workspace, int64_t workspace_bytes, void *stream);
+int lcd_supernodal_fill(int32_t n, int64_t nnz, const int32_t *Cp, const int32_t *Ci,
+                        const double *Cx, const int32_t *col_to_super, const int32_t *Lip,
+                        const int32_t *Li, const int64_t *Lp, double *Lx, int64_t panel_values,
+                        int32_t *status_dev, void *stream, int *status_host);
+
 /* ---- SpILU0 (CSR, in place) -------------------------------------------------- */
 /*
  * In-place ILU(0) of a CSR matrix with sorted rows; arithmetic identical to the

@@ -106,6 +106,11 @@ _SIGNATURES = {
                                  c_int32, _P, c_int64, _P]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
+    "lcd_supernodal_layout_workspace_bytes": (c_int, [c_int32, c_int64, _P]),
+    "lcd_supernodal_layout": (c_int, [c_int32, c_int64, _P, _P, c_int32, _P, _P, _P, _P, _P, _P, _P,
+                                      c_int64, _P]),
+    "lcd_supernodal_fill": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, _P, _P, c_int64, _P, _P,
+                                    _P]),
     "lcd_spilu0_csr_ordered": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int, c_int, _P,
                                        c_int32, _P, _P]),
     "lcd_spilu0_csr_static": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, c_int32, _P,

@@ -861,3 +861,270 @@ extern "C" int lcd_band_chains(int32_t n, const int32_t *dag_ptr, const int32_t 
     *n_tasks_host = (int32_t)total;
     return LCD_OK;
 }
+
+// ---- CSC -> supernodal layout ------------------------------------------------------------
+// Counterpart of convert_csc_to_supernodal (utils/symbolic_cholesky_csc.py:883-1021 of the
+// reference, a triple Python loop over sets): column j + 1 joins column j's supernode when the
+// symmetric difference of their row patterns has at most relaxation + 1 elements; the row
+// structure of a supernode is the sorted union of its columns' patterns; every column stores one
+// value per row of that union.  Here: a two-pointer comparison per column pair, a scan for the
+// supernode numbers, a stable radix sort of (supernode, row) pairs + flag / scan / compact for
+// the unions, a 64-bit scan for the panel offsets, and a binary search per stored entry for the
+// values.  Columns must be sorted (what the reference's set logic does not need, SciPy delivers).
+namespace lcd {
+
+__device__ __forceinline__ int column_of_entry(const int *__restrict__ Cp, int n, long long k) {
+    int lo = 0, hi = n;          // last column whose pointer is <= k
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if ((long long)Cp[mid] <= k) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+__global__ void sn_merge_kernel(int n, long long nnz, const int *__restrict__ Cp,
+                                const int *__restrict__ Ci, int relaxation, int *begin,
+                                int32_t *status) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const int s = Cp[j], e = Cp[j + 1];
+    if (s < 0 || e < s || (long long)e > nnz || (j == 0 && s != 0)) {
+        raise_error(status, LCD_ERR_BAD_POINTERS, j);
+        begin[j] = 1;
+        return;
+    }
+    for (int k = s; k < e; ++k) {
+        const int r = Ci[k];
+        if ((unsigned)r >= (unsigned)n) { raise_error(status, LCD_ERR_INDEX_RANGE, j); break; }
+        if (k > s && r <= Ci[k - 1]) { raise_error(status, LCD_ERR_UNSORTED, j); break; }
+    }
+    if (j == 0) { begin[0] = 1; return; }
+    const int ps = Cp[j - 1];
+    if (ps < 0 || ps > s) { begin[j] = 1; return; }   // (reported by the thread of column j - 1)
+    // symmetric difference of columns j - 1 and j, given up once it exceeds the allowance
+    int a = ps, b = s, differ = 0;
+    const int limit = relaxation + 1;
+    while (differ <= limit && (a < s || b < e)) {
+        if (a < s && b < e) {
+            const int ra = Ci[a], rb = Ci[b];
+            if (ra == rb) { ++a; ++b; }
+            else if (ra < rb) { ++a; ++differ; }
+            else { ++b; ++differ; }
+        } else {
+            differ += (s - a) + (e - b);
+            break;
+        }
+    }
+    begin[j] = differ > limit ? 1 : 0;
+}
+
+__global__ void sn_number_kernel(int n, const int *__restrict__ begin, const int *__restrict__ scan,
+                                 int *col_to_super, int *super_begin) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j > n) return;
+    if (j == n) { super_begin[scan[n]] = n; return; }
+    col_to_super[j] = scan[j + 1] - 1;
+    if (begin[j]) super_begin[scan[j]] = j;
+}
+
+__global__ void sn_pairs_kernel(int n, long long nnz, const int *__restrict__ Cp,
+                                const int *__restrict__ Ci, const int *__restrict__ col_to_super,
+                                unsigned *rows, unsigned *supers) {
+    for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
+         k += (long long)gridDim.x * blockDim.x) {
+        rows[k] = (unsigned)Ci[k];
+        supers[k] = (unsigned)col_to_super[column_of_entry(Cp, n, k)];
+    }
+}
+
+// (supers, rows) sorted by supernode, then row: heads of runs are the union's elements
+__global__ void sn_heads_kernel(long long m, const unsigned *__restrict__ supers,
+                                const unsigned *__restrict__ rows, int *head, int *count) {
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < m;
+         t += (long long)gridDim.x * blockDim.x) {
+        const bool first = t == 0 || supers[t] != supers[t - 1] || rows[t] != rows[t - 1];
+        head[t] = first ? 1 : 0;
+        if (first) atomicAdd(count + supers[t], 1);
+    }
+}
+
+__global__ void sn_rows_kernel(long long m, const unsigned *__restrict__ rows,
+                               const int *__restrict__ head, const int *__restrict__ headscan,
+                               int *Li) {
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < m;
+         t += (long long)gridDim.x * blockDim.x)
+        if (head[t]) Li[headscan[t]] = (int)rows[t];
+}
+
+// One block: 64-bit exclusive scan of width * length per supernode (panel offsets), widest
+// supernode, and the summary the host reads.
+__global__ void __launch_bounds__(1024)
+sn_panels_kernel(int n, const int *__restrict__ nsuper_dev, const int *__restrict__ super_begin,
+                 const int *__restrict__ Lip, long long *base, long long *summary) {
+    __shared__ long long part[1024];
+    __shared__ long long carry;
+    __shared__ int widest;
+    const int n_super = *nsuper_dev;
+    if (threadIdx.x == 0) { carry = 0; widest = 0; }
+    __syncthreads();
+    for (int s0 = 0; s0 < n_super; s0 += 1024) {
+        const int s = s0 + threadIdx.x;
+        long long size = 0;
+        if (s < n_super) {
+            const int width = super_begin[s + 1] - super_begin[s];
+            size = (long long)width * (Lip[s + 1] - Lip[s]);
+            atomicMax(&widest, width);
+        }
+        part[threadIdx.x] = size;
+        __syncthreads();
+        for (int off = 1; off < 1024; off <<= 1) {       // inclusive scan of the tile
+            const long long add = threadIdx.x >= off ? part[threadIdx.x - off] : 0;
+            __syncthreads();
+            part[threadIdx.x] += add;
+            __syncthreads();
+        }
+        if (s < n_super) base[s] = carry + part[threadIdx.x] - size;
+        __syncthreads();
+        if (threadIdx.x == 1023) carry += part[1023];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        base[n_super] = carry;
+        summary[0] = n_super;
+        summary[1] = Lip[n_super];
+        summary[2] = widest;
+        summary[3] = carry;
+    }
+}
+
+__global__ void sn_colptr_kernel(int n, const int *__restrict__ nsuper_dev,
+                                 const int *__restrict__ col_to_super, const int *__restrict__ super_begin,
+                                 const int *__restrict__ Lip, const long long *__restrict__ base,
+                                 long long *Lp) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j > n) return;
+    if (j == n) { Lp[n] = base[*nsuper_dev]; return; }
+    const int s = col_to_super[j];
+    Lp[j] = base[s] + (long long)(j - super_begin[s]) * (Lip[s + 1] - Lip[s]);
+}
+
+__global__ void sn_fill_kernel(int n, long long nnz, const int *__restrict__ Cp,
+                               const int *__restrict__ Ci, const double *__restrict__ Cx,
+                               const int *__restrict__ col_to_super, const int *__restrict__ Lip,
+                               const int *__restrict__ Li, const long long *__restrict__ Lp,
+                               double *Lx, int32_t *status) {
+    for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
+         k += (long long)gridDim.x * blockDim.x) {
+        const int j = column_of_entry(Cp, n, k);
+        const int s = col_to_super[j], row = Ci[k];
+        int lo = Lip[s], hi = Lip[s + 1];
+        const int end = hi;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (Li[mid] < row) lo = mid + 1; else hi = mid;
+        }
+        if (lo < end && Li[lo] == row) Lx[Lp[j] + (lo - Lip[s])] = Cx[k];
+        else raise_error(status, LCD_ERR_INDEX_RANGE, j);   // the layout belongs to another pattern
+    }
+}
+
+}  // namespace lcd
+
+extern "C" int lcd_supernodal_layout_workspace_bytes(int32_t n, int64_t nnz, int64_t *bytes) {
+    if (n < 0 || nnz < 0 || !bytes) return LCD_ERR_INVALID_ARGUMENT;
+    Bump b{nullptr, 0};
+    b.take<int32_t>(LCD_STATUS_WORDS);
+    plan_scratch(b, n, nnz);
+    b.take<long long>((size_t)n + 2);
+    b.take<long long>(8);
+    *bytes = (int64_t)b.used + 256;
+    return LCD_OK;
+}
+
+extern "C" int lcd_supernodal_layout(int32_t n, int64_t nnz, const int32_t *Cp, const int32_t *Ci,
+                                     int32_t relaxation, int32_t *col_to_super, int32_t *super_begin,
+                                     int32_t *Lip, int32_t *Li, int64_t *Lp, int64_t *summary_host,
+                                     void *workspace, int64_t workspace_bytes, void *stream) {
+    if (n < 0 || nnz < 0 || relaxation < 0 || !summary_host || !workspace) return LCD_ERR_INVALID_ARGUMENT;
+    if (!super_begin || !Lip || !Lp) return LCD_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (!Cp || !col_to_super || (nnz > 0 && (!Ci || !Li)))) return LCD_ERR_INVALID_ARGUMENT;
+    int64_t need = 0;
+    lcd_supernodal_layout_workspace_bytes(n, nnz, &need);
+    if (workspace_bytes < need) return LCD_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    for (int k = 0; k < 4; ++k) summary_host[k] = 0;
+    if (n == 0) {
+        LCD_CUDA_TRY(cudaMemsetAsync(super_begin, 0, sizeof(int32_t), st));
+        LCD_CUDA_TRY(cudaMemsetAsync(Lip, 0, sizeof(int32_t), st));
+        LCD_CUDA_TRY(cudaMemsetAsync(Lp, 0, sizeof(int64_t), st));
+        LCD_CUDA_TRY(cudaStreamSynchronize(st));
+        return LCD_OK;
+    }
+    Bump bump{reinterpret_cast<char *>(workspace), 0};
+    int32_t *status = bump.take<int32_t>(LCD_STATUS_WORDS);
+    DagScratch s = plan_scratch(bump, n, nnz);
+    long long *base = bump.take<long long>((size_t)n + 2);
+    long long *summary = bump.take<long long>(8);
+    int rc = reset_status(status, st);
+    if (rc) return rc;
+    const int nblk = (n + 1 + 255) / 256;
+    int *begin = s.cnt, *scan = s.pred_ptr, *count = s.out_degree;
+    sn_merge_kernel<<<nblk, 256, 0, st>>>(n, nnz, Cp, Ci, relaxation, begin, status);
+    LCD_CUDA_TRY(exclusive_scan(begin, n, scan, s.scan_sums, s.scan_total, st));
+    sn_number_kernel<<<nblk, 256, 0, st>>>(n, begin, scan, col_to_super, super_begin);
+    LCD_CUDA_TRY(cudaGetLastError());
+    rc = lcd_read_status(status, st, nullptr);    // malformed columns: nothing below may index with them
+    if (rc) return rc;
+    LCD_CUDA_TRY(cudaMemsetAsync(count, 0, ((size_t)n + 1) * sizeof(int), st));
+    if (nnz > 0) {
+        sn_pairs_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(n, nnz, Cp, Ci, col_to_super, s.k0, s.v0);
+        // by row, then (stable) by supernode
+        bool in_first = true;
+        LCD_CUDA_TRY(radix_sort_pairs(s.k0, s.v0, s.k1, s.v1, nnz, bits_for(n > 1 ? n - 1 : 1), s.sort,
+                                      st, &in_first));
+        unsigned *rows = in_first ? s.k0 : s.k1, *supers = in_first ? s.v0 : s.v1;
+        unsigned *rows_alt = in_first ? s.k1 : s.k0, *supers_alt = in_first ? s.v1 : s.v0;
+        LCD_CUDA_TRY(radix_sort_pairs(supers, rows, supers_alt, rows_alt, nnz,
+                                      bits_for(n > 1 ? n - 1 : 1), s.sort, st, &in_first));
+        const unsigned *sup = in_first ? supers : supers_alt, *row = in_first ? rows : rows_alt;
+        // (the heads go to the key buffer the sort left free, their scan to the flag array)
+        int *heads = reinterpret_cast<int *>(in_first ? supers_alt : supers);
+        sn_heads_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, sup, row, heads, count);
+        LCD_CUDA_TRY(exclusive_scan(heads, nnz, s.flags, s.scan_sums, s.scan_total, st));
+        sn_rows_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(nnz, row, heads, s.flags, Li);
+    }
+    // Lip = exclusive scan of the union sizes (entries past the last supernode repeat the total)
+    LCD_CUDA_TRY(exclusive_scan(count, n, Lip, s.scan_sums, s.scan_total, st));
+    sn_panels_kernel<<<1, 1024, 0, st>>>(n, scan + n, super_begin, Lip, base, summary);
+    sn_colptr_kernel<<<nblk, 256, 0, st>>>(n, scan + n, col_to_super, super_begin, Lip, base,
+                                           reinterpret_cast<long long *>(Lp));
+    LCD_CUDA_TRY(cudaGetLastError());
+    long long host[4] = {0, 0, 0, 0};
+    LCD_CUDA_TRY(cudaMemcpyAsync(host, summary, sizeof host, cudaMemcpyDeviceToHost, st));
+    LCD_CUDA_TRY(cudaStreamSynchronize(st));
+    rc = lcd_read_status(status, st, nullptr);
+    if (rc) return rc;
+    for (int k = 0; k < 4; ++k) summary_host[k] = host[k];
+    return LCD_OK;
+}
+
+extern "C" int lcd_supernodal_fill(int32_t n, int64_t nnz, const int32_t *Cp, const int32_t *Ci,
+                                   const double *Cx, const int32_t *col_to_super, const int32_t *Lip,
+                                   const int32_t *Li, const int64_t *Lp, double *Lx,
+                                   int64_t panel_values, int32_t *status_dev, void *stream,
+                                   int *status_host) {
+    if (n < 0 || nnz < 0 || panel_values < 0 || !status_dev) return LCD_ERR_INVALID_ARGUMENT;
+    if (nnz > 0 && (!Cp || !Ci || !Cx || !col_to_super || !Lip || !Li || !Lp || !Lx))
+        return LCD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (panel_values > 0) LCD_CUDA_TRY(cudaMemsetAsync(Lx, 0, (size_t)panel_values * sizeof(double), st));
+    if (nnz > 0) {
+        sn_fill_kernel<<<grid_for(nnz, 256), 256, 0, st>>>(n, nnz, Cp, Ci, Cx, col_to_super, Lip, Li,
+                                                          reinterpret_cast<const long long *>(Lp), Lx,
+                                                          status_dev);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    return finish(status_dev, st, status_host);
+}

@@ -133,7 +133,8 @@ def analyse(sn, Lip, Li, Lp, Lx, col_to_super=None, n=None, device="cuda", inver
 
     def up(a, dtype):
         if isinstance(a, torch.Tensor) and a.is_cuda:
-            return a.to(dtype).contiguous()
+            kind = {np.int32: torch.int32, np.int64: torch.int64, np.float64: torch.float64}[dtype]
+            return a.to(kind).contiguous()
         return torch.from_numpy(_host(a, dtype)).to(dev)
 
     t_sn, t_Lip = up(sn_h, np.int32), up(Lip_h, np.int32)
@@ -208,3 +209,68 @@ def sptrsv_csc_supernodal(sn_begin, col_to_sup, Lip, Li, Lp, Lx, x, flag_thread=
     out = solve(plan, xd).cpu().numpy()
     x[...] = out
     return x
+
+
+@dataclass
+class SupernodalLayout:
+    """Supernodal arrays of a CSC matrix as device tensors (the reference's ``Ls`` dictionary of
+    ``convert_csc_to_supernodal``: ``sn`` = 'supernodes', ``Li`` = 'i', ``Lip`` = 'ip', ``Lp`` =
+    'p' widened to int64, ``Lx`` = 'x')."""
+
+    n: int
+    n_super: int
+    max_width: int
+    sn: torch.Tensor
+    Lip: torch.Tensor
+    Li: torch.Tensor
+    Lp: torch.Tensor
+    Lx: torch.Tensor
+    col_to_super: torch.Tensor
+
+    def fill(self, Cp, Ci, Cx, status=None):
+        """New values of the same pattern into the same panels."""
+        status = new_status(Cx.device) if status is None else status
+        host = ctypes.c_int(0)
+        check(nat.load().lcd_supernodal_fill(
+            self.n, Ci.numel(), ptr(Cp), ptr(Ci), ptr(Cx), ptr(self.col_to_super), ptr(self.Lip),
+            ptr(self.Li), ptr(self.Lp), ptr(self.Lx), self.Lx.numel(), ptr(status), _stream(),
+            ctypes.byref(host)), "lcd_supernodal_fill")
+        return self
+
+
+def from_csc(Cp, Ci, Cx, relaxation=0, device="cuda"):
+    """Supernodal layout of a lower-triangular matrix stored by columns with sorted rows
+    (``convert_csc_to_supernodal(L, relaxation)`` of the reference,
+    utils/symbolic_cholesky_csc.py:950-1021), built on the device.  Arguments may be NumPy arrays
+    or device tensors; returns a ``SupernodalLayout`` whose fields feed ``analyse``."""
+    dev = torch.device(device)
+
+    def up(a, dtype):
+        if isinstance(a, torch.Tensor):
+            return a.to(device=dev, dtype=dtype).contiguous()
+        return torch.from_numpy(np.ascontiguousarray(a, dtype={torch.int32: np.int32,
+                                                               torch.float64: np.float64}[dtype])).to(dev)
+    Cp, Ci, Cx = up(Cp, torch.int32), up(Ci, torch.int32), up(Cx, torch.float64)
+    n, nnz = Cp.numel() - 1, Ci.numel()
+    if n < 0 or Cx.numel() != nnz:
+        raise SupernodalError("indptr, indices and data have inconsistent lengths")
+    need = ctypes.c_int64(0)
+    check(nat.load().lcd_supernodal_layout_workspace_bytes(n, nnz, ctypes.byref(need)),
+          "lcd_supernodal_layout_workspace_bytes")
+    workspace = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    col_to_super = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    begin = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    Lip = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    Li = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    Lp = torch.empty(n + 1, dtype=torch.int64, device=dev)
+    summary = (ctypes.c_int64 * 4)()
+    check(nat.load().lcd_supernodal_layout(
+        n, nnz, ptr(Cp), ptr(Ci), int(relaxation), ptr(col_to_super), ptr(begin), ptr(Lip), ptr(Li),
+        ptr(Lp), summary, ptr(workspace), workspace.numel(), _stream()), "lcd_supernodal_layout")
+    n_super, n_rows, max_width, panel_values = (int(v) for v in summary)
+    layout = SupernodalLayout(
+        n=n, n_super=n_super, max_width=max_width, sn=begin[:n_super + 1].clone(),
+        Lip=Lip[:n_super + 1].clone(), Li=Li[:n_rows].clone(), Lp=Lp,
+        Lx=torch.empty(max(panel_values, 1), dtype=torch.float64, device=dev)[:panel_values],
+        col_to_super=col_to_super[:n])
+    return layout.fill(Cp, Ci, Cx)

@@ -187,6 +187,45 @@ def sptrsv_supernodal(sn, Lip, Li, Lp, Lx, b):
     return x
 
 
+def csc_to_supernodal(indptr, indices, data, relaxation=0):
+    """Supernodal layout of a lower-triangular CSC matrix: restatement (NumPy, small inputs) of
+    the reference's converter, utils/symbolic_cholesky_csc.py:883-921 (column i joins column
+    i + 1 when the symmetric difference of their row patterns has at most relaxation + 1
+    elements) and :950-1021 (row structure of a supernode = sorted union of its columns'
+    patterns; every column stores a value per row of that union, zero where it has none).
+    Returns a dict with the reference's keys: x, i, ip, p, supernodes, col_to_super, nSuper,
+    max_width."""
+    indptr, indices = _i32(indptr), _i32(indices)
+    data = _f64(data)
+    n = len(indptr) - 1
+    pattern = [indices[indptr[j]:indptr[j + 1]] for j in range(n)]
+    begins = [0] if n else []
+    for j in range(n - 1):
+        differ = len(np.setxor1d(pattern[j], pattern[j + 1]))
+        if differ > relaxation + 1:
+            begins.append(j + 1)
+    supernodes = np.asarray(begins + [n], dtype=np.int32)
+    n_super = len(begins)
+    col_to_super = np.zeros(n, dtype=np.int32)
+    rows, ip, p = [], [0], [0]
+    for s in range(n_super):
+        first, last = supernodes[s], supernodes[s + 1]
+        col_to_super[first:last] = s
+        union = np.unique(np.concatenate([pattern[j] for j in range(first, last)]))
+        rows.append(union)
+        ip.append(ip[-1] + len(union))
+        for _ in range(first, last):
+            p.append(p[-1] + len(union))
+    x = np.zeros(p[-1], dtype=np.float64)
+    for j in range(n):
+        union = rows[col_to_super[j]]
+        x[p[j] + np.searchsorted(union, pattern[j])] = data[indptr[j]:indptr[j + 1]]
+    return {"x": x, "i": np.concatenate(rows).astype(np.int32) if rows else np.zeros(0, np.int32),
+            "ip": np.asarray(ip, dtype=np.int32), "p": np.asarray(p, dtype=np.int64),
+            "supernodes": supernodes, "col_to_super": col_to_super, "nSuper": n_super,
+            "max_width": int(np.max(np.diff(supernodes))) if n_super else 0}
+
+
 def relative_residual_csr(Ap, Ai, Ax, x, b):
     """||A x - b||_2 / ||b||_2 for a CSR matrix that stores its diagonal."""
     Ap, Ai, Ax, x, b = _i32(Ap), _i32(Ai), _f64(Ax), _f64(x), _f64(b)

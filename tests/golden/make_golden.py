@@ -143,8 +143,55 @@ def write_band_chains(out_dir):
     print("wrote band chains", len(out))
 
 
+def supernodal_conversion_cases():
+    """Lower-triangular CSC matrices (sorted columns, diagonal stored) for the converter."""
+    rng = np.random.default_rng(17)
+    cases = {}
+    # Cholesky factor of the 2-D Laplacian on a 9 x 9 grid: real fill, nested column patterns
+    g = 9
+    T = sp.diags([-1.0, 4.0, -1.0], [-1, 0, 1], shape=(g, g))
+    A = (sp.kron(sp.identity(g), T) + sp.kron(sp.diags([-1.0, -1.0], [-1, 1], shape=(g, g)),
+                                               sp.identity(g))).toarray()
+    L = np.linalg.cholesky(A)
+    L[np.abs(L) < 1e-14] = 0.0
+    cases["chol_lap2d_g9"] = sp.csc_matrix(np.tril(L))
+    # the generator's supernodal matrices, taken back to CSC
+    cases["generated_n200"] = gen.supernodal_random(n=200, seed=8, widths=(2, 3, 4, 8),
+                                                    min_targets=1, max_targets=4).to_csc()
+    # random lower triangle: hardly any column pairs merge
+    R = sp.tril(sp.random(150, 150, 0.05, random_state=rng, format="csc"), -1) + sp.identity(150)
+    cases["random_n150"] = sp.csc_matrix(R)
+    cases["diagonal_n40"] = sp.csc_matrix(sp.identity(40) * 2.0)
+    cases["dense_n24"] = sp.csc_matrix(np.tril(rng.uniform(0.5, 1.5, (24, 24))))
+    for m in cases.values():
+        m.sort_indices()
+    return cases
+
+
+def write_supernodal_conversion(out_dir):
+    """convert_csc_to_supernodal (utils/symbolic_cholesky_csc.py:883-1021) of the reference on
+    small matrices, relaxation 0, 1 and 3: supernode partition, row structure, column pointers,
+    panel values."""
+    out = {}
+    for name, L in supernodal_conversion_cases().items():
+        out[f"{name}/indptr"] = L.indptr.astype(np.int32)
+        out[f"{name}/indices"] = L.indices.astype(np.int32)
+        out[f"{name}/data"] = L.data.astype(np.float64)
+        for relaxation in (0, 1, 3):
+            with contextlib.redirect_stdout(_sink):
+                Ls = convert_csc_to_supernodal(L, relaxation=relaxation)
+            for field in ("x", "i", "ip", "p", "supernodes", "col_to_super"):
+                out[f"{name}/r{relaxation}/{field}"] = np.asarray(Ls[field])
+            out[f"{name}/r{relaxation}/nSuper"] = np.int64(Ls["nSuper"])
+            out[f"{name}/r{relaxation}/max_width"] = np.int64(Ls["max_width"])
+    np.savez_compressed(os.path.join(out_dir, "csc_to_supernodal.npz"), **out)
+    print("wrote csc_to_supernodal", len(out))
+
+
 def main():
     out_dir = HERE
+    if sys.argv[1:] == ["csc_to_supernodal"]:
+        return write_supernodal_conversion(out_dir)
     if sys.argv[1:] == ["ilu0_csc"]:        # only these fixtures
         return write_ilu0_csc(out_dir)
     if sys.argv[1:] == ["band_chains"]:
@@ -282,6 +329,7 @@ def main():
 
     write_ilu0_csc(out_dir)
     write_band_chains(out_dir)
+    write_supernodal_conversion(out_dir)
 
     # ---- supernodal solve ------------------------------------------------
     source = open(os.path.join(REF, "benchmark", "sptrsv_supernodal.py")).read()

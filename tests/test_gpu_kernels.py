@@ -599,6 +599,57 @@ def test_supernodal_medium(cuda, oracle):
     np.testing.assert_allclose(x, oracle.sptrsv_supernodal(s.sn, s.Lip, s.Li, s.Lp, s.Lx, s.b), rtol=1e-9, atol=1e-12)
 
 
+@pytest.mark.parametrize("relaxation", [0, 1, 3])
+def test_csc_to_supernodal_matches_reference_converter(cuda, relaxation):
+    """The device converter against what the reference's convert_csc_to_supernodal returned
+    (utils/symbolic_cholesky_csc.py:950-1021): every array element-wise, values bit-exact."""
+    import os
+    from lcd_b200 import supernodal
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "csc_to_supernodal.npz"))
+    for name in sorted({k.split("/")[0] for k in g.files}):
+        got = supernodal.from_csc(g[f"{name}/indptr"], g[f"{name}/indices"], g[f"{name}/data"],
+                                  relaxation=relaxation, device=cuda)
+        ref = {f: g[f"{name}/r{relaxation}/{f}"] for f in ("x", "i", "ip", "p", "supernodes", "col_to_super")}
+        np.testing.assert_array_equal(host(got.sn), ref["supernodes"], err_msg=name)
+        np.testing.assert_array_equal(host(got.col_to_super), ref["col_to_super"], err_msg=name)
+        np.testing.assert_array_equal(host(got.Lip), ref["ip"], err_msg=name)
+        np.testing.assert_array_equal(host(got.Li), ref["i"], err_msg=name)
+        np.testing.assert_array_equal(host(got.Lp), ref["p"], err_msg=name)
+        np.testing.assert_array_equal(host(got.Lx), ref["x"], err_msg=name)
+        assert got.n_super == int(g[f"{name}/r{relaxation}/nSuper"])
+        assert got.max_width == int(g[f"{name}/r{relaxation}/max_width"])
+
+
+def test_csc_to_supernodal_medium_then_solve(cuda, oracle):
+    """A 20,000-column matrix: layout equal to the CPU restatement, then analysed and solved
+    from the converted arrays; new values into the same panels; malformed input is reported."""
+    import torch
+    from lcd_b200 import _native as nat, generators as gen, supernodal
+    s = gen.supernodal_random(n=20_000, seed=11, widths=(8, 16, 32, 64), min_targets=3, max_targets=9)
+    L = s.to_csc()
+    L.sort_indices()
+    Cp, Ci, Cx = L.indptr.astype(np.int32), L.indices.astype(np.int32), L.data
+    for relaxation in (0, 2):
+        got = supernodal.from_csc(Cp, Ci, Cx, relaxation=relaxation, device=cuda)
+        ref = oracle.csc_to_supernodal(Cp, Ci, Cx, relaxation)
+        for mine, field in ((got.sn, "supernodes"), (got.col_to_super, "col_to_super"), (got.Lip, "ip"),
+                            (got.Li, "i"), (got.Lp, "p"), (got.Lx, "x")):
+            np.testing.assert_array_equal(host(mine), ref[field], err_msg=field)
+        plan = supernodal.analyse(got.sn, got.Lip, got.Li, got.Lp, got.Lx, got.col_to_super)
+        x = host(supernodal.solve(plan, dev(s.b, np.float64, cuda)))
+        np.testing.assert_allclose(x, oracle.sptrsv_csc_lower(Cp, Ci, Cx, s.b), rtol=1e-9, atol=1e-12)
+    got.fill(dev(Cp, np.int32, cuda), dev(Ci, np.int32, cuda), dev(2.0 * Cx, np.float64, cuda))
+    np.testing.assert_array_equal(host(got.Lx), 2.0 * ref["x"])
+    empty = supernodal.from_csc(np.zeros(1, np.int32), np.zeros(0, np.int32), np.zeros(0), device=cuda)
+    assert empty.n_super == 0 and empty.Lx.numel() == 0
+    shuffled = Ci.copy()
+    col = int(np.argmax(np.diff(Cp) >= 3))
+    shuffled[Cp[col]:Cp[col] + 2] = shuffled[Cp[col]:Cp[col] + 2][::-1]
+    with pytest.raises(nat.NativeError) as err:
+        supernodal.from_csc(Cp, shuffled, Cx, device=cuda)
+    assert err.value.code == nat.ERR_UNSORTED
+
+
 # ------------------------------------------------- failure detection ----
 def test_waits_are_bounded_and_errors_reported(cuda):
     """Faults are made on the host (bad counters / bad indices); the kernels give

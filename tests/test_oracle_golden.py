@@ -1,4 +1,5 @@
 """The CPU oracle against fixtures produced by the reference's own pipeline."""
+import os
 import numpy as np
 import pytest
 
@@ -154,3 +155,23 @@ def test_reference_unit_test_vectors(oracle):
     np.testing.assert_array_equal(pos, [0, -1, 4])
     _, rc = oracle.diag_positions([0, 2], [1, 0])
     assert rc == 2  # unsorted segment -> StructuralLookupError in the reference
+
+
+def _conversion_cases():
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "csc_to_supernodal.npz"))
+    names = sorted({k.split("/")[0] for k in g.files})
+    return g, names
+
+
+@pytest.mark.parametrize("relaxation", [0, 1, 3])
+def test_csc_to_supernodal_matches_reference_converter(oracle, relaxation):
+    """The restated converter against what utils/symbolic_cholesky_csc.py:950-1021 returned."""
+    g, names = _conversion_cases()
+    for name in names:
+        got = oracle.csc_to_supernodal(g[f"{name}/indptr"], g[f"{name}/indices"], g[f"{name}/data"],
+                                       relaxation)
+        for field in ("i", "ip", "p", "supernodes", "col_to_super"):
+            np.testing.assert_array_equal(got[field], g[f"{name}/r{relaxation}/{field}"], err_msg=f"{name} {field}")
+        np.testing.assert_array_equal(got["x"], g[f"{name}/r{relaxation}/x"])
+        assert got["nSuper"] == int(g[f"{name}/r{relaxation}/nSuper"])
+        assert got["max_width"] == int(g[f"{name}/r{relaxation}/max_width"])
