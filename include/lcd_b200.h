@@ -645,7 +645,11 @@ enum {
     LCD_CAL_ATOMIC_S = 4,         /* one atomicAdd on an address every thread of the grid adds to */
     LCD_CAL_GRID_BARRIER_S = 5,   /* one grid-wide barrier, one block of 512 threads per SM */
     LCD_CAL_COPY_BYTES_PER_S = 6, /* device-to-device copy, read + write bytes */
-    LCD_CALIBRATION_VALUES = 8
+    LCD_CAL_L2_LOAD_S = 7,        /* one dependent ld.relaxed.gpu that hits L2 (mean of 4096 over 32 MB;
+                                     SM clock taken at its nominal rate) */
+    LCD_CAL_L2_LOAD_P10_S = 8,    /* ... its 10th percentile (lines homed near the SM) */
+    LCD_CAL_L2_LOAD_P90_S = 9,    /* ... its 90th percentile (lines homed on the other die) */
+    LCD_CALIBRATION_VALUES = 10
 };
 int lcd_calibrate(void *workspace, int64_t workspace_bytes, void *stream, double *out_host);
 

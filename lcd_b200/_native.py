@@ -131,7 +131,7 @@ _SIGNATURES = {
     "lcd_sptrsv_csr_ordered_part": (c_int, [c_int32, c_int64, _P, _P, _P, _P, _P, c_int, _P, c_int32,
                                             _P, c_int, _P, ctypes.POINTER(c_void_p), c_int32, c_int64,
                                             _P, c_int32, _P, ctypes.POINTER(c_int)]),
-    "lcd_calibrate": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_double * 8)]),
+    "lcd_calibrate": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_double * 16)]),
     "lcd_set_tuning": (c_int, [c_int, c_int]),
     "lcd_debug_set_trace": (c_int, [_P]),
     "lcd_checksum_i32": (c_int, [_P, c_int64, _P, ctypes.POINTER(c_uint64 * 2), _P]),

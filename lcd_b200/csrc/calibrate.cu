@@ -4,6 +4,8 @@
 // atomic on one contended address, and the copy bandwidth.  Counterpart of the reference's
 // measure_arch_constants (compiler/scheduler.py:714-775), which times empty launches and an
 // atomic kernel with Numba.  Every wait in here is bounded.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace lcd {
@@ -77,6 +79,30 @@ __global__ void calib_gridbar_kernel(unsigned long long *counter, int rounds, un
         if (aborted(status)) return;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *elapsed_ns = global_timer() - t0;
+}
+
+// Dependent loads through L2: a chain of kChaseSteps addresses 128 bytes apart spread over 32 MB
+// (resident in L2 after the first walk), each loaded with ld.relaxed.gpu as the polls are.
+constexpr int kChaseSteps = 4096;
+constexpr int kChaseSlots = 1 << 18;       // x 128 B = 32 MB
+__global__ void calib_chase_init_kernel(unsigned long long *buf) {
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (unsigned)kChaseSlots)
+        buf[(size_t)i * 16] = (i * 1664525u + 1013904223u) & (unsigned)(kChaseSlots - 1);
+}
+__global__ void calib_chase_kernel(const unsigned long long *buf, int passes, unsigned *cycles) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (int pass = 0; pass < passes; ++pass) {
+        unsigned long long at = 0;
+        for (int k = 0; k < kChaseSteps; ++k) {
+            const long long t0 = clock64();
+            unsigned long long next;
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(next) : "l"(buf + at * 16) : "memory");
+            at = next;
+            const long long t1 = clock64() + (long long)(at >> 40);   // (waits for the value)
+            if (pass == passes - 1) cycles[k] = (unsigned)(t1 - t0);
+        }
+    }
 }
 
 __global__ void calib_copy_kernel(const double4 *__restrict__ src, double4 *__restrict__ dst, long long count) {
@@ -167,6 +193,28 @@ extern "C" int lcd_calibrate(void *workspace, int64_t workspace_bytes, void *str
         if (cudaEventSynchronize(e1) != cudaSuccess) return fail(LCD_ERR_CUDA);
         cudaEventElapsedTime(&ms, e0, e1);
         out_host[LCD_CAL_COPY_BYTES_PER_S] = 3.0 * 2.0 * (double)half / (ms * 1e-3);
+    }
+    // 7. latency of a dependent L2 load (what one poll of a waiting row costs)
+    if (workspace_bytes >= (40ll << 20)) {
+        unsigned long long *buf = reinterpret_cast<unsigned long long *>(static_cast<char *>(workspace) + 8192);
+        unsigned *cycles = reinterpret_cast<unsigned *>(static_cast<char *>(workspace) + (36ll << 20));
+        calib_chase_init_kernel<<<kChaseSlots / 256, 256, 0, st>>>(buf);
+        calib_chase_kernel<<<1, 32, 0, st>>>(buf, 2, cycles);
+        static unsigned host_cycles[kChaseSteps];
+        int clock_khz = 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, dev);
+        if (cudaMemcpyAsync(host_cycles, cycles, sizeof host_cycles, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+            cudaStreamSynchronize(st) == cudaSuccess && clock_khz > 0) {
+            std::sort(host_cycles, host_cycles + kChaseSteps);
+            double sum = 0.0;
+            for (int k = 0; k < kChaseSteps; ++k) sum += host_cycles[k];
+            const double to_s = 1.0 / (clock_khz * 1e3);
+            out_host[LCD_CAL_L2_LOAD_S] = sum / kChaseSteps * to_s;
+            out_host[LCD_CAL_L2_LOAD_P10_S] = host_cycles[kChaseSteps / 10] * to_s;
+            out_host[LCD_CAL_L2_LOAD_P90_S] = host_cycles[kChaseSteps * 9 / 10] * to_s;
+        }
     }
     if (cudaGetLastError() != cudaSuccess) return fail(LCD_ERR_CUDA);
     return fail(LCD_OK);

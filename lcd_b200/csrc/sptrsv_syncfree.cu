@@ -31,16 +31,20 @@ __global__ void __launch_bounds__(TPB, MINB) csr_syncfree_kernel(const CsrSolveP
     const int local = tid / G;
     const int lane = tid % G;
     const int task = row0 + local;
-    if (task >= p.n) return;
+    // (no early return: every lane of a warp takes part in the votes below)
+    bool done = task >= p.n;
     const bool upper = p.flags & LCD_SOLVE_UPPER;
     const bool exact = p.flags & LCD_SOLVE_EXACT;
     const int r = upper ? p.n - 1 - task : task;
+    constexpr unsigned kFull = 0xffffffffu;
     const unsigned gmask =
-        G == 32 ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
+        G == 32 ? kFull : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
 
     int lo = 0, hi = 0, d = -1;
     bool failed = false;
-    if (!csr_row_range(p, r, lo, hi, d)) {
+    if (done) {
+        // a group past the last row: nothing to do
+    } else if (!csr_row_range(p, r, lo, hi, d)) {
         if (lane == 0)
             raise_error(p.status, (p.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL
                                                                : LCD_ERR_BAD_POINTERS, r);
@@ -49,7 +53,7 @@ __global__ void __launch_bounds__(TPB, MINB) csr_syncfree_kernel(const CsrSolveP
         d = -1;
     }
     double acc = 0.0, dv = 1.0, rinv = 1.0;
-    if (lane == 0) {
+    if (lane == 0 && !done) {
         acc = __ldg(p.b + r);
         if (d >= 0) dv = __ldg(p.Ax + d);
         if (!exact) rinv = 1.0 / dv;  // off the critical path: computed before any wait
@@ -81,22 +85,37 @@ __global__ void __launch_bounds__(TPB, MINB) csr_syncfree_kernel(const CsrSolveP
                 }
             }
         }
-        const bool group_done = (G == 1) ? !have : (__all_sync(gmask, !have) != 0);
-        if (group_done) {
+        // Votes are full-warp ballots read through the group's mask, and the reduction runs in
+        // a warp-uniform branch: a vote or shuffle with one member mask per group is executed
+        // once per group and leaves the groups split (measured: branch_resolving as the top
+        // stall of this kernel).
+        bool group_done;
+        if (G == 1) {
+            group_done = !done && !have;
+        } else {
+            const unsigned idle = __ballot_sync(kFull, done || !have);
+            group_done = !done && (idle & gmask) == gmask;
+        }
+        if (G == 1 ? group_done : __any_sync(kFull, group_done)) {
+            double sum = acc;
             if (G > 1) {
 #pragma unroll
-                for (int off = G / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(gmask, acc, off, G);
-                failed = __any_sync(gmask, failed) != 0;
+                for (int off = G / 2; off > 0; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off, G);
+                const unsigned bad = __ballot_sync(kFull, failed);
+                if (group_done) failed = (bad & gmask) != 0;
             }
-            if (lane == 0) {
-                double val = (d < 0) ? acc : (exact ? acc / dv : acc * rinv);
-                if (failed) val = __longlong_as_double(kCanonicalNaN);
-                val = publishable(val);
-                st_relaxed_f64(p.x + r, val);
-                sxv[local] = val;
+            if (group_done) {
+                if (lane == 0) {
+                    double val = (d < 0) ? sum : (exact ? sum / dv : sum * rinv);
+                    if (failed) val = __longlong_as_double(kCanonicalNaN);
+                    val = publishable(val);
+                    st_relaxed_f64(p.x + r, val);
+                    sxv[local] = val;
+                }
+                done = true;
             }
-            break;
         }
+        if (G == 1 ? done : __all_sync(kFull, done)) break;
     }
 }
 

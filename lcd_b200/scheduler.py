@@ -339,7 +339,8 @@ def _schedule_rank(schedule):
 
 _MEASURED_CONSTANTS = {}
 CALIBRATION_NAMES = ("launch_s", "l2_handoff_s", "shared_memory_handoff_s", "block_barrier_s",
-                     "contended_atomic_s", "grid_barrier_s", "copy_bytes_per_s")
+                     "contended_atomic_s", "grid_barrier_s", "copy_bytes_per_s", "l2_load_s",
+                     "l2_load_p10_s", "l2_load_p90_s")
 
 
 def calibrate(workspace_bytes=256 << 20):
@@ -348,7 +349,7 @@ def calibrate(workspace_bytes=256 << 20):
     import torch
     from . import _native as nat
     workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device="cuda")
-    out = (ctypes.c_double * 8)()
+    out = (ctypes.c_double * 16)()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     nat.check(nat.load().lcd_calibrate(nat.ptr(workspace), workspace.numel(), stream, ctypes.byref(out)),
               "lcd_calibrate")
