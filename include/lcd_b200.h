@@ -359,55 +359,79 @@ int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *
                            int32_t timeout_ms, void *stream, int *status_host);
 
 /*
- * Solves small enough for one thread block (a few hundred thousand rows at most): CSR and CSC
- * (compiler/demo/sptrsv.py:26-43) triangular solves whose cost is the hand-off between levels,
- * not bandwidth.  One block walks the level sets with a block barrier per level and keeps the
- * recent part of x in shared memory; nothing spins.  Replaces, for such sizes, the generated
- * wavefront launchers (compiler/cuda_lowering.py:855-1016: a launch plus a device synchronisation
- * per level) and the sync-free kernels (:1343-1410, push :2031-2059).  The CSC loop (push) is
- * served by the same pull walk on the transposed structure - no atomics, results do not depend on
- * timing.
- *   Task slots: every level is padded to a multiple of 32 slots, so that the lanes of a warp
- *       always work in the same level (the scoreboard of outstanding loads belongs to the warp).
- *       slot_ptr[l] = first slot of level l (n_levels + 1 entries, a device array the caller
- *       computes from wavefront_ptr: running sum of the level widths rounded up to 32);
- *       n_slots = slot_ptr[n_levels].
+ * Level walks with the hand-off in shared memory: CSR and CSC (compiler/demo/sptrsv.py:26-43)
+ * triangular solves whose cost is the hand-off between levels, not bandwidth.
+ *   blocks = 1: solves small enough for one thread block (a few hundred thousand rows at most).
+ *       One block walks the level sets with a block barrier per level and keeps the recent part
+ *       of x in shared memory; nothing spins.
+ *   blocks > 1 (at most one per SM; cooperative launch): block b owns the nodes
+ *       [n b / blocks, n (b + 1) / blocks) and walks its tasks of every level.  Operands of the
+ *       own block come from shared memory behind the block barrier; operands another block owns
+ *       are requested a turn ahead and, if still missing, polled in the position-ordered x in
+ *       global memory (pre-filled with the reserved NaN pattern; bounded waits, LCD_ERR_TIMEOUT).
+ *       The operands of a triangular solve have smaller node numbers, i.e. they belong to the
+ *       same or an earlier block: the blocks form a pipeline that pays one hand-off through L2
+ *       per block, not per level.
+ * Replaces the generated wavefront launchers (compiler/cuda_lowering.py:855-1016: a launch plus a
+ * device synchronisation per level) and the sync-free kernels (:1343-1410, push :2031-2059).  The
+ * CSC loop (push) is served by the same pull walk on the transposed structure - no atomics,
+ * results do not depend on timing.
+ *   Task slots: every slice of a level is padded to a multiple of 32 slots, so that the lanes of
+ *       a warp always work in the same level (the scoreboard of outstanding loads belongs to the
+ *       warp).  Slots are numbered block by block.  Within a level the tasks are sorted by node,
+ *       so a block's tasks of a level are consecutive: lcd_small_level_cuts writes
+ *       cuts[b * n_levels + l] = tasks of level l that belong to blocks < b (blocks x n_levels
+ *       ints).  From them the caller computes slot_ptr[b * (n_levels + 1) + l] = first slot of
+ *       block b's tasks of level l (running sum, block by block, of the slice sizes rounded up to
+ *       32; entry n_levels of block b = first slot of block b + 1; n_slots = the last entry).
+ *       One block: cuts may be NULL, slot_ptr has n_levels + 1 entries.
  *   lcd_small_plan_measure / lcd_small_plan_fill   once per pattern: `pos` (n ints) receives the
  *       slot of every node (order, level, wavefront_ptr: wavefronts, level and wavefront_ptr of
  *       lcd_dag_build for the same op); info_host[0] = most operands of one task (longest row
- *       without its diagonal), [1] = widest level.  The fill writes one record per slot with
+ *       without its diagonal), [1] = widest slice.  The fill writes one record per slot with
  *       `entries` = 2, 4 or 8 >= info_host[0] operand slots (more operands than
  *       lcd_small_max_entries(): not served): rec_pc / rec_src [n_slots * entries] = slot of the
  *       operand and index of its value in Ax, -1 for padding; row_of[n_slots] (-1: padding
- *       slot), diag_src[n_slots].  *far_host = operands more than half the shared-memory ring
- *       back (read from global memory).  cursor: n_slots ints of scratch (CSC ops only).
- *       Errors through status_dev: LCD_ERR_INDEX_RANGE, LCD_ERR_BAD_POINTERS, LCD_ERR_CYCLE
- *       (order not topological).  info_dev: 4 ints of device scratch.
- *   lcd_sptrsv_small   every solve: gathers values, right-hand side and reciprocal diagonals
- *       into slot order (a parallel pass), walks the levels, and puts x back into matrix order
- *       (a parallel pass).  scratch: lcd_small_scratch_bytes(n_slots, entries) bytes, 256-byte
- *       aligned; rec_pc 16-byte aligned.  Asynchronous on `stream`; it has no device-side waits
- *       and reports nothing (the plan calls validated the input).
+ *       slot), diag_src[n_slots].  *far_host = operands of the own block more than half the
+ *       shared-memory ring back (read from global memory).  cursor: n_slots ints of scratch (CSC
+ *       ops only).  Errors through status_dev: LCD_ERR_INDEX_RANGE, LCD_ERR_BAD_POINTERS,
+ *       LCD_ERR_CYCLE (an operand that is not in an earlier level).  info_dev: 4 ints of scratch.
+ *   lcd_sptrsv_small   every solve: walks the levels.  With gather_values != 0 the call first
+ *       gathers the coefficients and reciprocal diagonals into slot order in `scratch` (a
+ *       parallel pass: needed on the first call and whenever Ax has changed; with 0 the values of
+ *       the previous call stay - the usual case of one matrix and many right-hand sides).  A
+ *       task's record is fetched two turns before the task runs, its right-hand side one turn
+ *       before, straight from b; x is written by position into `scratch` (what the operands
+ *       read) and in matrix order into x.  scratch: lcd_small_scratch_bytes(n_slots, entries)
+ *       bytes, 256-byte aligned; rec_pc 16-byte aligned.  Asynchronous on `stream` unless
+ *       status_host is given.
+ *       LCD_ERR_TOO_LARGE: more blocks than the device can keep resident.
  *   op: LCD_OP_CSR_LOWER / CSR_UPPER / CSC_LOWER / CSC_UPPER; flags: LCD_SOLVE_OF_FULL /
  *   UNIT_DIAG for the CSR ops.
  */
 int lcd_small_max_entries(void);
+int lcd_small_level_cuts(int32_t n, int32_t blocks, int32_t n_levels, const int32_t *order,
+                         const int32_t *wavefront_ptr_dev, int32_t *cuts_dev, void *stream);
 int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
                            const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
                            const int32_t *level, const int32_t *wavefront_ptr_dev,
-                           const int32_t *slot_ptr_dev, int32_t n_levels, int32_t n_slots, int32_t *pos,
-                           int32_t *cursor, int32_t *info_dev, int32_t *status_dev, void *stream,
-                           int32_t *info_host);
+                           const int32_t *slot_ptr_dev, const int32_t *cuts_dev, int32_t n_levels,
+                           int32_t blocks, int32_t n_slots, int32_t *pos, int32_t *cursor,
+                           int32_t *info_dev, int32_t *status_dev, void *stream, int32_t *info_host);
 int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
                         const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
-                        const int32_t *pos, int32_t n_slots, int32_t entries, int32_t *rec_pc,
-                        int32_t *rec_src, int32_t *row_of, int32_t *diag_src, int32_t *cursor,
-                        int32_t *info_dev, int32_t *status_dev, void *stream, int32_t *far_host);
+                        const int32_t *level, const int32_t *slot_ptr_dev, int32_t n_levels,
+                        int32_t blocks, const int32_t *pos, int32_t n_slots, int32_t entries,
+                        int32_t *rec_pc, int32_t *rec_src, int32_t *row_of, int32_t *diag_src,
+                        int32_t *cursor, int32_t *info_dev, int32_t *status_dev, void *stream,
+                        int32_t *far_host);
 int lcd_small_scratch_bytes(int32_t n_slots, int32_t entries, int64_t *bytes);
 int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *Ax, const double *b,
                      double *x, const int32_t *rec_pc, const int32_t *rec_src, const int32_t *row_of,
                      const int32_t *diag_src, const int32_t *slot_ptr_dev, int32_t n_levels,
-                     int32_t max_width, void *scratch, int64_t scratch_bytes, void *stream);
+                     int32_t blocks, int32_t max_width, int32_t gather_values, void *scratch,
+                     int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms, void *stream,
+                     int *status_host);
 
 /* ---- CSC -> supernodal layout ------------------------------------------------------ */
 /*

@@ -97,13 +97,16 @@ _SIGNATURES = {
                                        c_int, _P, _P, c_int, _P, c_int64, _P, c_int32, _P,
                                        ctypes.POINTER(c_int)]),
     "lcd_small_max_entries": (c_int, []),
-    "lcd_small_plan_measure": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, _P, c_int32,
-                                       c_int32, _P, _P, _P, _P, _P, ctypes.POINTER(c_int32 * 4)]),
-    "lcd_small_plan_fill": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, _P, c_int32, c_int32,
-                                    _P, _P, _P, _P, _P, _P, _P, _P, ctypes.POINTER(c_int32)]),
+    "lcd_small_level_cuts": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P]),
+    "lcd_small_plan_measure": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       c_int32, c_int32, c_int32, _P, _P, _P, _P, _P,
+                                       ctypes.POINTER(c_int32 * 4)]),
+    "lcd_small_plan_fill": (c_int, [c_int, c_int, c_int32, c_int64, _P, _P, _P, _P, _P, _P, c_int32, c_int32,
+                                    _P, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P,
+                                    ctypes.POINTER(c_int32)]),
     "lcd_small_scratch_bytes": (c_int, [c_int32, c_int32, ctypes.POINTER(c_int64)]),
     "lcd_sptrsv_small": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P, c_int32,
-                                 c_int32, _P, c_int64, _P]),
+                                 c_int32, c_int32, c_int32, _P, c_int64, _P, c_int32, _P, _P]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_supernodal_layout_workspace_bytes": (c_int, [c_int32, c_int64, _P]),

@@ -12,10 +12,11 @@
 //   * no pointer chasing, few instructions on the critical path.  The block's time per level
 //     is the instruction latency of the warps that own the level's rows, so everything a task
 //     needs sits in two records whose addresses follow from t alone: {values of its entries,
-//     right-hand side, reciprocal diagonal} (doubles, gathered per solve by a fully parallel
-//     pass) and {positions of its operands} (ints, per pattern), fetched with 128-bit loads
-//     two turns (several levels) before the task's level comes up.  x is stored by position
-//     (coalesced); a last parallel pass puts it back into matrix order.
+//     reciprocal diagonal} (doubles, gathered by a fully parallel pass whenever the matrix
+//     values change) and {positions of its operands} (ints, per pattern), fetched with 128-bit
+//     loads two turns (several levels) before the task's level comes up; the right-hand side
+//     follows one turn ahead, straight from b.  x is stored by position (coalesced, what the
+//     operands read) and into matrix order (a scattered store nobody waits for).
 //   * whole warps per level.  The scoreboard that tracks outstanding loads belongs to the warp,
 //     not the lane: if lanes of one warp had their turns in consecutive levels, the lanes of
 //     level l + 1 would wait for the prefetches the lanes of level l had just issued into the
@@ -46,11 +47,16 @@ struct SmallLayout {
 
 struct SmallSolveParams {
     SmallLayout lay;
-    const int *__restrict__ wptr;
+    const int *__restrict__ wptr;        // slot table: first slot of (block, level), blocks x (n_levels + 1)
     int n_levels;
-    int max_width;
-    const double *__restrict__ rec_val;  // [n * (E + 2)]: values, right-hand side, reciprocal diagonal
-    double *xp;                          // [n] x by position
+    int max_width;                       // widest slice of a level in slots
+    int blocks;                          // thread blocks that share the walk (1: the one-block solver)
+    int32_t *status;                     // bounded waits for operands of other blocks
+    unsigned long long budget_ns;
+    const double *__restrict__ rec_val;  // [n * (E + 2)]: coefficients, (unused), reciprocal diagonal
+    const double *__restrict__ b;        // right-hand side, matrix order
+    double *x;                           // result, matrix order
+    double *xp;                          // [n] x by position (what the walk's operands read)
     long long *trace;                    // profiling aid (lcd_debug_set_trace): SM cycle counter after
                                          // every level's barrier [n_levels], then, for the tasks of
                                          // thread 0, at the start / after the stores / at the end [3 each]
@@ -87,12 +93,36 @@ __device__ __forceinline__ bool small_range(const SmallOp &q, int v, int &i, int
 }
 
 // pass 1: place of every node in the order, widest level, longest row (CSR)
+// Shared walk: block b owns the nodes [n * b / blocks, n * (b + 1) / blocks).  The operands of a
+// triangular solve have smaller node numbers, so they belong to the same or an earlier block: the
+// dependences between blocks all point one way, and the blocks form a pipeline instead of
+// meeting at every level.  Within a level the tasks are sorted by node, so a block's tasks of a
+// level are consecutive: cuts[b * n_levels + l] = tasks of level l that belong to blocks < b.
+__device__ __forceinline__ int block_of_node(int v, int n, int blocks) {
+    return (int)((((long long)v + 1) * blocks - 1) / n);
+}
+
+__global__ void small_cuts_kernel(int n, int blocks, int n_levels, const int *__restrict__ order,
+                                  const int *__restrict__ wptr, int *cuts) {
+    const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (id >= (long long)blocks * n_levels) return;
+    const int b = (int)(id / n_levels), l = (int)(id % n_levels);
+    const int first = (int)((long long)n * b / blocks);      // the block's first node
+    int lo = wptr[l], hi = wptr[l + 1];
+    const int start = lo;
+    while (lo < hi) {                                         // first task of the level with node >= first
+        const int mid = (lo + hi) >> 1;
+        if (order[mid] < first) lo = mid + 1; else hi = mid;
+    }
+    cuts[id] = lo - start;
+}
+
 __global__ void small_measure_kernel(const SmallOp q, const int *__restrict__ order,
                                      const int *__restrict__ level, const int *__restrict__ wptr,
-                                     const int *__restrict__ slot_ptr, int n_levels, int *pos,
-                                     int *info, int32_t *status) {
+                                     const int *__restrict__ slot_ptr, const int *__restrict__ cuts,
+                                     int n_levels, int blocks, int *pos, int *info, int32_t *status) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t < n_levels) atomicMax(info + 1, wptr[t + 1] - wptr[t]);
+    if (t < n_levels && blocks == 1) atomicMax(info + 1, wptr[t + 1] - wptr[t]);   // widest level
     if (t >= q.n) return;
     const int v = order[t];
     if ((unsigned)v >= (unsigned)q.n) { raise_error(status, LCD_ERR_INDEX_RANGE, t); return; }
@@ -101,7 +131,14 @@ __global__ void small_measure_kernel(const SmallOp q, const int *__restrict__ or
         raise_error(status, LCD_ERR_INDEX_RANGE, t);     // order and levels do not belong together
         return;
     }
-    pos[v] = slot_ptr[l] + (t - wptr[l]);    // the level's first slot is a multiple of 32
+    {   // the first slot of every (block, level) is a multiple of 32
+        const int o = t - wptr[l];
+        const int b = blocks > 1 ? block_of_node(v, q.n, blocks) : 0;
+        const int before = blocks > 1 ? cuts[(size_t)b * n_levels + l] : 0;
+        if (o < before) { raise_error(status, LCD_ERR_UNSORTED, t); return; }   // level not sorted by node
+        pos[v] = slot_ptr[(size_t)b * (n_levels + 1) + l] + (o - before);
+        if (blocks > 1) atomicMax(info + 1, o - before + 1);                     // widest slice
+    }
     int i, lo, hi, d;
     if (!small_range(q, v, i, lo, hi, d)) {
         raise_error(status, (q.flags & LCD_SOLVE_OF_FULL) ? LCD_ERR_MISSING_DIAGONAL : LCD_ERR_BAD_POINTERS, i);
@@ -131,11 +168,25 @@ __global__ void small_count_rows_kernel(const SmallOp q, const int *__restrict__
     }
 }
 
+// Block that owns slot g: block b's slots are [table[b * stride], table[(b + 1) * stride]) with
+// stride = n_levels + 1 (the last block ends at n_slots).
+__device__ __forceinline__ int block_of_slot(const int *__restrict__ table, int blocks, int stride, int g) {
+    int lo = 0, hi = blocks;          // last block whose first slot is <= g
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (table[(size_t)mid * stride] <= g) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
 __global__ void small_fill_kernel(const SmallOp q, const int *__restrict__ order,
-                                  const int *__restrict__ pos, int E, int *rec_pc, int *rec_src,
-                                  int *row_of, int *diag_src, int *cursor, int *info, int32_t *status) {
+                                  const int *__restrict__ pos, const int *__restrict__ level,
+                                  const int *__restrict__ slot_ptr, int n_levels, int blocks, int E,
+                                  int *rec_pc, int *rec_src, int *row_of, int *diag_src, int *cursor,
+                                  int *info, int32_t *status) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= q.n) return;
+    const int stride = n_levels + 1;
     const bool upper = small_is_upper(q.op);
     const bool csc = small_is_csc(q.op);
     const int v = order[t];
@@ -155,13 +206,19 @@ __global__ void small_fill_kernel(const SmallOp q, const int *__restrict__ order
                 if (!side) {
                     raise_error(status, LCD_ERR_INDEX_RANGE, i);
                 } else {
-                    const int other = pos[upper ? q.n - 1 - c : c];
-                    // ... and stands before the task in the order
-                    if (other < 0 || other >= slot) raise_error(status, LCD_ERR_CYCLE, i);
+                    const int node = upper ? q.n - 1 - c : c;
+                    const int other = pos[node];
+                    // ... and stands in an earlier level
+                    if (other < 0 || level[node] >= level[v]) raise_error(status, LCD_ERR_CYCLE, i);
                     else {
                         pc = other;
                         src = lo + e;
-                        if (slot - other > kRing / 2) atomicAdd(info + 2, 1);
+                        // an operand of the own block beyond the shared-memory window is read
+                        // from global memory (counted: the caller reports it)
+                        if (slot - other > kRing / 2 &&
+                            block_of_slot(slot_ptr, blocks, stride, other) ==
+                                block_of_slot(slot_ptr, blocks, stride, slot))
+                            atomicAdd(info + 2, 1);
                     }
                 }
             }
@@ -176,13 +233,16 @@ __global__ void small_fill_kernel(const SmallOp q, const int *__restrict__ order
         const int r = q.Ai[j];
         const bool side = (unsigned)r < (unsigned)q.n && (upper ? r < i : r > i);
         if (!side) continue;                         // reported by the counting pass
-        const int target = pos[upper ? q.n - 1 - r : r];
-        if (target <= slot) { raise_error(status, LCD_ERR_CYCLE, i); continue; }
+        const int node = upper ? q.n - 1 - r : r;
+        const int target = pos[node];
+        if (target < 0 || level[node] <= level[v]) { raise_error(status, LCD_ERR_CYCLE, i); continue; }
         const int k = atomicAdd(cursor + target, 1);
         if (k >= E) continue;                        // cannot happen: E covers the longest row
         rec_pc[(size_t)target * E + k] = slot;
         rec_src[(size_t)target * E + k] = j;
-        if (target - slot > kRing / 2) atomicAdd(info + 2, 1);
+        if (target - slot > kRing / 2 &&
+            block_of_slot(slot_ptr, blocks, stride, target) == block_of_slot(slot_ptr, blocks, stride, slot))
+            atomicAdd(info + 2, 1);
     }
 }
 
@@ -209,9 +269,10 @@ __global__ void small_sort_slots_kernel(int n, int E, int upper, const int *__re
     }
 }
 
-// ---- per solve ------------------------------------------------------------------------
-__global__ void small_pack_kernel(const SmallLayout lay, const double *__restrict__ Ax,
-                                  const double *__restrict__ b, double *rec_val) {
+// ---- per value set --------------------------------------------------------------------
+// Coefficients and reciprocal diagonals into slot order (fully parallel; repeated only when the
+// matrix values change - the right-hand side is read in place by the walk).
+__global__ void small_pack_kernel(const SmallLayout lay, const double *__restrict__ Ax, double *rec_val) {
     const int E = lay.entries, stride = gridDim.x * blockDim.x;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < lay.n; t += stride) {
         double *rec = rec_val + (size_t)t * (E + 2);
@@ -221,29 +282,53 @@ __global__ void small_pack_kernel(const SmallLayout lay, const double *__restric
         }
         const int row = lay.row_of[t];
         const int d = lay.diag_src[t];
-        rec[E] = row >= 0 ? b[row] : 0.0;            // (padding slots solve to 0 and go nowhere)
-        rec[E + 1] = row < 0 ? 0.0 : (d >= 0 ? 1.0 / Ax[d] : 1.0);
+        rec[E] = 0.0;
+        rec[E + 1] = row < 0 ? 0.0 : (d >= 0 ? 1.0 / Ax[d] : 1.0);   // (padding slots solve to 0)
     }
 }
 
-// The walk stores x by position (coalesced); this pass puts it back into matrix order.
-__global__ void small_unpack_kernel(int n, const int *__restrict__ row_of, const double *__restrict__ xp,
-                                    double *__restrict__ x) {
-    const int stride = gridDim.x * blockDim.x;
-    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
-        if (row_of[t] >= 0) x[row_of[t]] = xp[t];
-}
-
-template <int E>
+// ---- per solve ------------------------------------------------------------------------
+template <int E, bool SHARED>
 struct SmallTask {
     double val[E];
     double bb, dinv;
-    int pc[E];
+    int pc[E];                   // slots of the operands (-1: none)
+    int row;                     // matrix row of the task (-1: padding slot)
+    double rx[SHARED ? E : 1];   // shared walk: operands of other blocks, fetched a turn ahead
+                                 // (the pending pattern: not yet there)
 };
 
+// Shared walk: the operands of task `t` (slot relative to `base`) that other blocks own are
+// requested one turn before the task runs - a load from L2 costs about as much as two levels of
+// the walk, and a block that trails its neighbours by a few levels finds them there already.
 template <int E>
-__device__ __forceinline__ void small_load(SmallTask<E> &q, const SmallSolveParams &p, int t) {
-    if (t < p.lay.n) {
+__device__ __forceinline__ void small_peek(SmallTask<E, true> &q, const SmallSolveParams &p, int base,
+                                           int count, int t) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        q.rx[e] = __longlong_as_double((long long)kPendingBits);
+        if (t < count) {
+            const int pc = q.pc[e];
+            if (pc >= 0 && (unsigned)(pc - base) >= (unsigned)t) q.rx[e] = ld_relaxed_f64(p.xp + pc);
+        }
+    }
+}
+
+// Second stage of a task's prefetch, one turn before it runs: its record (coefficients, operand
+// slots, row) was requested a turn earlier; now the right-hand side, straight from b in matrix
+// order - no gathering pass per solve.
+template <int E, bool SHARED>
+__device__ __forceinline__ void small_values(SmallTask<E, SHARED> &q, const SmallSolveParams &p, int count,
+                                             int t) {
+    q.bb = (t < count && q.row >= 0) ? __ldg(p.b + q.row) : 0.0;
+}
+
+// t: slot relative to the block's first slot `base`; count: slots of the block
+template <int E, bool SHARED>
+__device__ __forceinline__ void small_load(SmallTask<E, SHARED> &q, const SmallSolveParams &p, int base,
+                                           int count, int t) {
+    if (t < count) {
+        t += base;
         // two records per task, 16-byte aligned (E + 2 and E are even): 128-bit loads
         const double2 *rv = reinterpret_cast<const double2 *>(p.rec_val + (size_t)t * (E + 2));
 #pragma unroll
@@ -252,9 +337,8 @@ __device__ __forceinline__ void small_load(SmallTask<E> &q, const SmallSolvePara
             q.val[2 * k] = v.x;
             q.val[2 * k + 1] = v.y;
         }
-        const double2 tail = __ldg(rv + E / 2);
-        q.bb = tail.x;
-        q.dinv = tail.y;
+        q.dinv = __ldg(rv + E / 2).y;
+        q.row = __ldg(p.lay.row_of + t);
         if (E == 2) {
             const int2 c = __ldg(reinterpret_cast<const int2 *>(p.lay.rec_pc + (size_t)t * E));
             q.pc[0] = c.x;
@@ -267,58 +351,112 @@ __device__ __forceinline__ void small_load(SmallTask<E> &q, const SmallSolvePara
                 q.pc[4 * k] = c.x; q.pc[4 * k + 1] = c.y; q.pc[4 * k + 2] = c.z; q.pc[4 * k + 3] = c.w;
             }
         }
+    } else {
+        q.row = -1;
     }
 }
 
-template <int E, int T, int DEPTH>
+// With blocks > 1 (cooperative launch: all blocks are resident) block b walks its slice of every
+// level.  Operands of the own block are handed over through the shared-memory ring behind the
+// block barrier, as in the one-block form; operands that another block owns are polled in the
+// position-ordered x in global memory, which starts out filled with the reserved NaN pattern.
+// Rows of a level do not depend on each other, so a thread may spin on such an operand without
+// holding up anything but its own block's barrier.  Because operands lie in earlier levels, and
+// for a triangular matrix mostly in slices with smaller numbers, the blocks fall into a pipeline:
+// block b trails block b - 1 by one hand-off through L2, once - not once per level.
+template <int E, int T, int DEPTH, bool SHARED>
 __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolveParams p) {
     extern __shared__ __align__(16) double ring[];  // kRing doubles
     __shared__ int s_wptr[kWptrChunk + 1];
     const int tid = threadIdx.x;
     const bool use_ring = p.max_width <= kRing / 2;
+    constexpr bool shared_walk = SHARED;
+    const int *table = p.wptr + (size_t)blockIdx.x * (p.n_levels + 1);
+    const int base = __ldg(table);                         // the block's first slot
+    const int count = __ldg(table + p.n_levels) - base;    // ... and how many it has
+    double *xp = p.xp + base;
     // two register sets used in turn: a set is reloaded right after its task and not touched
     // again until two turns later, so its loads have several levels to arrive
-    SmallTask<E> q0, q1;
+    SmallTask<E, SHARED> q0, q1;
     int t = tid;
     int phase = 0;
-    small_load(q0, p, t);
-    if (DEPTH > 1) small_load(q1, p, t + T);
+    small_load(q0, p, base, count, t);
+    if (DEPTH > 1) small_load(q1, p, base, count, t + T);
+    small_values(q0, p, count, t);
+    if (DEPTH > 1) small_values(q1, p, count, t + T);
+    if (SHARED) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            q0.rx[e] = __longlong_as_double((long long)kPendingBits);
+            q1.rx[e] = q0.rx[e];
+        }
+    }
     int traced = 0;
-    auto run = [&](SmallTask<E> &c) {
-        if (p.trace && tid == 0) p.trace[p.n_levels + 3 * traced] = clock64();
+    auto run = [&](SmallTask<E, SHARED> &c, SmallTask<E, SHARED> &next) {
+        if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[p.n_levels + 3 * traced] = clock64();
         double acc = c.bb;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             const int pc = c.pc[e];
             if (pc >= 0) {
-                const double xv = (use_ring && t - pc <= kRing / 2) ? ring[pc & (kRing - 1)]
-                                                                    : *(volatile const double *)(p.xp + pc);
+                const int rel = pc - base;
+                double xv;
+                if ((unsigned)rel < (unsigned)t) {        // a slot of this block (earlier level)
+                    xv = (use_ring && t - rel <= kRing / 2) ? ring[rel & (kRing - 1)]
+                                                            : *(volatile const double *)(xp + rel);
+                } else if (!SHARED) {
+                    xv = __longlong_as_double(kCanonicalNaN);   // (cannot happen: one block owns all)
+                } else {                                  // another block's: fetched a turn ago,
+                    xv = c.rx[e];                         // else wait for it (bounded)
+                    if (is_pending(xv)) {
+                        Deadline dl;
+                        dl.start(p.budget_ns);
+                        for (;;) {
+                            xv = ld_relaxed_f64(p.xp + pc);
+                            if (!is_pending(xv)) break;
+                            if (dl.tick(p.status, pc)) { xv = __longlong_as_double(kCanonicalNaN); break; }
+                        }
+                    }
+                }
                 acc = fma(-c.val[e], xv, acc);
             }
         }
         const double xi = acc * c.dinv;
         ring[t & (kRing - 1)] = xi;
-        p.xp[t] = xi;                      // consecutive tasks, consecutive addresses (a plain store:
-                                           // the block barrier orders it for the block's own readers)
-        if (p.trace && tid == 0) p.trace[p.n_levels + 3 * traced + 1] = clock64();
-        small_load(c, p, t + DEPTH * T);
+        // consecutive tasks, consecutive addresses.  One block: a plain store (the block barrier
+        // orders it for the block's own readers); shared walk: other blocks poll it
+        if (shared_walk) st_relaxed_f64(xp + t, publishable(xi));
+        else xp[t] = xi;
+        if (c.row >= 0) p.x[c.row] = xi;   // the result in matrix order (nobody reads it here)
+        if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[p.n_levels + 3 * traced + 1] = clock64();
+        small_load(c, p, base, count, t + DEPTH * T);
         t += T;
-        if (p.trace && tid == 0) p.trace[p.n_levels + 3 * traced++ + 2] = clock64();
+        if constexpr (DEPTH > 1) {
+            small_values(next, p, count, t);         // next turn's task: its record is there by now
+            if constexpr (SHARED) small_peek(next, p, base, count, t);
+        } else {
+            small_values(c, p, count, t);            // (one register set: waits for the record just loaded)
+        }
+        if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[p.n_levels + 3 * traced++ + 2] = clock64();
     };
-    for (int base = 0; base < p.n_levels; base += kWptrChunk) {
-        const int count = min(kWptrChunk, p.n_levels - base);
+    for (int first = 0; first < p.n_levels; first += kWptrChunk) {
+        const int levels = min(kWptrChunk, p.n_levels - first);
         __syncthreads();  // the previous chunk of offsets is no longer read
-        for (int k = tid; k <= count; k += T) s_wptr[k] = __ldg(p.wptr + base + k);
+        for (int k = tid; k <= levels; k += T) s_wptr[k] = __ldg(table + first + k) - base;
         __syncthreads();
-        for (int l = 0; l < count; ++l) {
+        for (int l = 0; l < levels; ++l) {
             const int we = s_wptr[l + 1];
             while (t < we) {
-                if (DEPTH == 1 || phase == 0) run(q0);
-                else run(q1);
+                if (DEPTH == 1 || phase == 0) run(q0, q1);
+                else run(q1, q0);
                 phase ^= 1;
             }
             __syncthreads();
-            if (p.trace && tid == 0) p.trace[base + l] = clock64();
+            if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[first + l] = clock64();
+            if (SHARED && p.trace && tid == 0) {     // EXPERIMENT: level times of three blocks
+                const int which = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x / 2 ? 1 : (blockIdx.x == gridDim.x - 1 ? 2 : -1));
+                if (which >= 0) p.trace[(8ll + which) * p.n_levels + first + l] = (long long)global_timer();
+            }
         }
     }
 }
@@ -328,11 +466,26 @@ static int launch_small_t(const SmallSolveParams &p, cudaStream_t st) {
     static bool configured = false;
     const int smem = kRing * (int)sizeof(double);
     if (!configured) {
-        LCD_CUDA_TRY(cudaFuncSetAttribute(sptrsv_small_kernel<E, T, DEPTH>,
+        LCD_CUDA_TRY(cudaFuncSetAttribute(sptrsv_small_kernel<E, T, DEPTH, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        LCD_CUDA_TRY(cudaFuncSetAttribute(sptrsv_small_kernel<E, T, DEPTH, true>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         configured = true;
     }
-    sptrsv_small_kernel<E, T, DEPTH><<<1, T, smem, st>>>(p);
+    if (p.blocks <= 1) {
+        sptrsv_small_kernel<E, T, DEPTH, false><<<1, T, smem, st>>>(p);
+    } else {
+        // blocks wait for each other: they must all be resident (cooperative launch, one per SM)
+        static int per_sm = -1;
+        if (per_sm < 0)
+            LCD_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &per_sm, sptrsv_small_kernel<E, T, DEPTH, true>, T, smem));
+        if ((long long)per_sm * sm_count() < p.blocks) return LCD_ERR_TOO_LARGE;
+        SmallSolveParams q = p;
+        void *args[] = {(void *)&q};
+        LCD_CUDA_TRY(cudaLaunchCooperativeKernel((void *)sptrsv_small_kernel<E, T, DEPTH, true>, dim3((unsigned)p.blocks),
+                                                 dim3(T), args, (size_t)smem, st));
+    }
     LCD_CUDA_TRY(cudaGetLastError());
     return LCD_OK;
 }
@@ -366,14 +519,27 @@ using namespace lcd;
 
 extern "C" int lcd_small_max_entries(void) { return kSmallMaxEntries; }
 
+extern "C" int lcd_small_level_cuts(int32_t n, int32_t blocks, int32_t n_levels, const int32_t *order,
+                                    const int32_t *wavefront_ptr_dev, int32_t *cuts_dev, void *stream) {
+    if (n < 0 || blocks < 1 || blocks > 1024 || n_levels < 0) return LCD_ERR_INVALID_ARGUMENT;
+    if (n == 0 || n_levels == 0) return LCD_OK;
+    if (!order || !wavefront_ptr_dev || !cuts_dev) return LCD_ERR_INVALID_ARGUMENT;
+    const long long m = (long long)blocks * n_levels;
+    small_cuts_kernel<<<(unsigned)((m + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        n, blocks, n_levels, order, wavefront_ptr_dev, cuts_dev);
+    LCD_CUDA_TRY(cudaGetLastError());
+    return LCD_OK;
+}
+
 extern "C" int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
                                       const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
                                       const int32_t *level, const int32_t *wavefront_ptr_dev,
-                                      const int32_t *slot_ptr_dev, int32_t n_levels, int32_t n_slots,
-                                      int32_t *pos, int32_t *cursor, int32_t *info_dev,
+                                      const int32_t *slot_ptr_dev, const int32_t *cuts_dev,
+                                      int32_t n_levels, int32_t blocks, int32_t n_slots, int32_t *pos,
+                                      int32_t *cursor, int32_t *info_dev,
                                       int32_t *status_dev, void *stream, int32_t *info_host) {
     if (n < 0 || nnz < 0 || n_levels < 0 || n_slots < n || !info_dev || !status_dev || !info_host ||
-        !small_op_ok(op))
+        !small_op_ok(op) || blocks < 1 || blocks > 1024 || (blocks > 1 && !cuts_dev))
         return LCD_ERR_INVALID_ARGUMENT;
     const bool csc = op == LCD_OP_CSC_LOWER || op == LCD_OP_CSC_UPPER;
     if (csc && (flags & (LCD_SOLVE_OF_FULL | LCD_SOLVE_UNIT_DIAG))) return LCD_ERR_INVALID_ARGUMENT;
@@ -391,7 +557,8 @@ extern "C" int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz,
         const SmallOp q{op, flags & (LCD_SOLVE_OF_FULL | LCD_SOLVE_UNIT_DIAG), n, nnz, Ap, Ai, diag_pos};
         const int m = n > n_levels ? n : n_levels;
         small_measure_kernel<<<(m + 255) / 256, 256, 0, st>>>(q, order, level, wavefront_ptr_dev, slot_ptr_dev,
-                                                              n_levels, pos, info_dev, status_dev);
+                                                              cuts_dev, n_levels, blocks, pos, info_dev,
+                                                              status_dev);
         if (csc) {
             LCD_CUDA_TRY(cudaMemsetAsync(cursor, 0, (size_t)n_slots * sizeof(int32_t), st));
             small_count_rows_kernel<<<(n + 255) / 256, 256, 0, st>>>(q, order, pos, cursor, info_dev,
@@ -406,15 +573,17 @@ extern "C" int lcd_small_plan_measure(int op, int flags, int32_t n, int64_t nnz,
 
 extern "C" int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, const int32_t *Ap,
                                    const int32_t *Ai, const int32_t *diag_pos, const int32_t *order,
-                                   const int32_t *pos, int32_t n_slots, int32_t entries, int32_t *rec_pc,
+                                   const int32_t *level, const int32_t *slot_ptr_dev, int32_t n_levels,
+                                   int32_t blocks, const int32_t *pos, int32_t n_slots, int32_t entries,
+                                   int32_t *rec_pc,
                                    int32_t *rec_src, int32_t *row_of, int32_t *diag_src,
                                    int32_t *cursor, int32_t *info_dev, int32_t *status_dev,
                                    void *stream, int32_t *far_host) {
     if (n < 0 || nnz < 0 || n_slots < n || (entries != 2 && entries != 4 && entries != 8) || !info_dev ||
-        !status_dev || !far_host || !small_op_ok(op))
+        !status_dev || !far_host || !small_op_ok(op) || blocks < 1 || blocks > 1024 || n_levels < 0)
         return LCD_ERR_INVALID_ARGUMENT;
     const bool csc = op == LCD_OP_CSC_LOWER || op == LCD_OP_CSC_UPPER;
-    if (n > 0 && (!Ap || (nnz > 0 && !Ai) || !order || !pos || !rec_pc || !rec_src || !row_of || !diag_src ||
+    if (n > 0 && (!Ap || (nnz > 0 && !Ai) || !order || !level || !slot_ptr_dev || !pos || !rec_pc || !rec_src || !row_of || !diag_src ||
                   (csc && !cursor)))
         return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;
@@ -429,8 +598,9 @@ extern "C" int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, co
         LCD_CUDA_TRY(cudaMemsetAsync(row_of, 0xFF, (size_t)n_slots * sizeof(int32_t), st));
         LCD_CUDA_TRY(cudaMemsetAsync(diag_src, 0xFF, (size_t)n_slots * sizeof(int32_t), st));
         if (csc) LCD_CUDA_TRY(cudaMemsetAsync(cursor, 0, (size_t)n_slots * sizeof(int32_t), st));
-        small_fill_kernel<<<(n + 255) / 256, 256, 0, st>>>(q, order, pos, entries, rec_pc, rec_src, row_of,
-                                                           diag_src, cursor, info_dev, status_dev);
+        small_fill_kernel<<<(n + 255) / 256, 256, 0, st>>>(q, order, pos, level, slot_ptr_dev, n_levels, blocks,
+                                                           entries, rec_pc, rec_src, row_of, diag_src, cursor,
+                                                           info_dev, status_dev);
         if (csc)
             small_sort_slots_kernel<<<(n_slots + 255) / 256, 256, 0, st>>>(
                 n_slots, entries, op == LCD_OP_CSC_UPPER ? 1 : 0, row_of, rec_pc, rec_src);
@@ -451,11 +621,17 @@ extern "C" int lcd_small_scratch_bytes(int32_t n_slots, int32_t entries, int64_t
 extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *Ax,
                                 const double *b, double *x, const int32_t *rec_pc, const int32_t *rec_src,
                                 const int32_t *row_of, const int32_t *diag_src,
-                                const int32_t *slot_ptr_dev, int32_t n_levels, int32_t max_width,
-                                void *scratch, int64_t scratch_bytes, void *stream) {
-    if (n < 0 || n_slots < n || n_levels < 0 || (entries != 2 && entries != 4 && entries != 8))
+                                const int32_t *slot_ptr_dev, int32_t n_levels, int32_t blocks,
+                                int32_t max_width, int32_t gather_values, void *scratch,
+                                int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms,
+                                void *stream, int *status_host) {
+    if (n < 0 || n_slots < n || n_levels < 0 || (entries != 2 && entries != 4 && entries != 8) ||
+        blocks < 1 || blocks > 1024 || !status_dev)
         return LCD_ERR_INVALID_ARGUMENT;
-    if (n == 0) return LCD_OK;
+    if (n == 0) {
+        const int rc0 = reset_status(status_dev, (cudaStream_t)stream);
+        return rc0 ? rc0 : finish(status_dev, (cudaStream_t)stream, status_host);
+    }
     if (!Ax || !b || !x || x == b || !rec_pc || !rec_src || !row_of || !diag_src || !slot_ptr_dev || !scratch)
         return LCD_ERR_INVALID_ARGUMENT;
     int64_t need = 0;
@@ -468,17 +644,23 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
     base += align256((size_t)n_slots * (entries + 2) * 8);
     double *xp = reinterpret_cast<double *>(base);
     const SmallLayout lay{n_slots, entries, rec_pc, rec_src, row_of, diag_src};
-    const int blocks = (n_slots + 255) / 256 < 148 * 8 ? (n_slots + 255) / 256 : 148 * 8;
-    small_pack_kernel<<<blocks, 256, 0, st>>>(lay, Ax, b, rec_val);
-    LCD_CUDA_TRY(cudaGetLastError());
-    // (the widest level in slots: rounded up to whole warps)
-    const SmallSolveParams p{lay, slot_ptr_dev, n_levels, (max_width + 31) & ~31, rec_val, xp, debug_trace()};
-    int rc;
+    int rc = reset_status(status_dev, st);
+    if (rc) return rc;
+    if (gather_values) {
+        const int grid = (n_slots + 255) / 256 < sm_count() * 8 ? (n_slots + 255) / 256 : sm_count() * 8;
+        small_pack_kernel<<<grid, 256, 0, st>>>(lay, Ax, rec_val);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
+    if (blocks > 1) {   // blocks poll each other's results: the value is its own ready flag
+        rc = lcd_fill_u64(reinterpret_cast<uint64_t *>(xp), n_slots, kPendingBits, st);
+        if (rc) return rc;
+    }
+    // (the widest slice in slots: rounded up to whole warps)
+    const SmallSolveParams p{lay, slot_ptr_dev, n_levels, (max_width + 31) & ~31, blocks, status_dev,
+                             timeout_ns(timeout_ms), rec_val, b, x, xp, debug_trace()};
     if (entries == 2) rc = launch_small_e<2>(p, st);
     else if (entries == 4) rc = launch_small_e<4>(p, st);
     else rc = launch_small_e<8>(p, st);
     if (rc) return rc;
-    small_unpack_kernel<<<blocks, 256, 0, st>>>(n_slots, row_of, xp, x);
-    LCD_CUDA_TRY(cudaGetLastError());
-    return LCD_OK;
+    return finish(status_dev, st, status_host);
 }

@@ -110,6 +110,31 @@ def bind(lowering):
         cache["small_plan"] = plan
         return plan
 
+    def walk_plan_for(op_name, Ap, Ai, hints):
+        """Plan of the level walk shared by many blocks (wide levels, short rows), or None."""
+        dag, cache = hints.get("dag"), hints.setdefault("cache", {})
+        if dag is None or dag.capped or "walk_plan" in cache:
+            return cache.get("walk_plan")
+        plan = None
+        n, nnz = Ap.numel() - 1, Ai.numel()
+        blocks = ops.sliced_blocks(n, dag.n_levels) if dag.n_levels > 0 else 1
+        if blocks >= 8 and nnz - n <= ops.nat.load().lcd_small_max_entries() * n:
+            try:
+                plan = ops.SmallPlan(op_name, Ap, Ai, dag, blocks=blocks)
+            except ops.NativeError as error:
+                if error.code != ops.nat.ERR_TOO_LARGE:
+                    raise
+        cache["walk_plan"] = plan
+        return plan
+
+    def walk_solve(plan, Ax, b, x, cache):
+        # the coefficients are gathered into slot order again only when the value array has other
+        # contents than at the last solve (device checksum, as for the chain solver's tiles)
+        stamp = ops.fingerprint(Ax.view(torch.int32))
+        same = cache.get("walk_values") == stamp
+        ops.sptrsv_small(plan, Ax, b, x, same_values=same, sync=True)
+        cache["walk_values"] = stamp
+
     def ordered_plan_for(Ap, Ai, hints):
         dag, cache = hints.get("dag"), hints.setdefault("cache", {})
         if dag is None or dag.capped or "ordered_plan" in cache:
@@ -186,6 +211,10 @@ def bind(lowering):
             small = small_plan_for(op_name, Ap, Ai, hints)
             if small is not None:
                 ops.sptrsv_small(small, Ax, b, x)
+                return
+            walk = walk_plan_for(op_name, Ap, Ai, hints) if lanes == 1 else None
+            if walk is not None:
+                walk_solve(walk, Ax, b, x, hints.setdefault("cache", {}))
                 return
             ordered = ordered_plan_for(Ap, Ai, hints) if lanes == 1 else None
             if ordered is not None:

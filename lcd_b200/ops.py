@@ -478,11 +478,14 @@ def sptrsv_csr_ordered(Ap, Ai, Ax, B, order, X=None, *, upper=False, unit_diag=F
 
 
 class SmallPlan:
-    """Level-ordered task records of a small triangular matrix (structure only, built on the
-    device) and the per-solve scratch of the one-block solver.  Every level is padded to whole
-    warps of task slots."""
+    """Level-ordered task records of a triangular matrix (structure only, built on the device)
+    and the per-solve scratch of the level walk with shared-memory hand-off.  ``blocks`` = 1:
+    the one-block solver for small systems.  ``blocks`` > 1: the nodes are cut into that many
+    ranges and one thread block walks the tasks of each range level by level (at most one block
+    per SM; ``blocks`` = 0 picks a number from the average level width).  A block's tasks of a
+    level are padded to whole warps of task slots."""
 
-    def __init__(self, op, Ap, Ai, dag, *, diag_pos=None, unit_diag=False):
+    def __init__(self, op, Ap, Ai, dag, *, diag_pos=None, unit_diag=False, blocks=1):
         op = _op_code(op)
         _require(Ap, torch.int32, "Ap")
         _require(Ai, torch.int32, "Ai")
@@ -492,31 +495,56 @@ class SmallPlan:
         self.op, self.n = op, n
         flags = _solve_flags(False, unit_diag, diag_pos is not None, False)
         i32 = dict(dtype=torch.int32, device=dev)
-        self.n_levels = dag.n_levels
+        self.n_levels = levels = dag.n_levels
         widths = np.diff(dag.wavefront_ptr_host.astype(np.int64))
-        slot_ptr = np.zeros(dag.n_levels + 1, dtype=np.int64)
-        np.cumsum((widths + 31) // 32 * 32, out=slot_ptr[1:])
-        self.n_slots = int(slot_ptr[-1])
-        if self.n_slots > SMALL_MAX_SLOTS:
+        if blocks == 0:
+            blocks = sliced_blocks(n, levels, dev)
+        self.blocks = blocks = max(1, int(blocks))
+        if blocks * (levels + 1) > SLICED_MAX_TABLE:
             raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
-                              f"{self.n_slots} task slots after padding every level to whole warps; "
-                              f"the one-block solver serves up to {SMALL_MAX_SLOTS}")
-        self.slot_ptr = torch.from_numpy(slot_ptr.astype(np.int32)).to(dev)
+                              f"{blocks} blocks x {levels} levels: slot table too large")
+        # slot table: block b owns the nodes [n b / blocks, n (b + 1) / blocks); its tasks of a
+        # level are consecutive in the level's (node-sorted) task list; every such slice is padded
+        # to whole warps and the slots are numbered block by block
+        if blocks > 1:
+            self.cuts = torch.empty(blocks * max(levels, 1), **i32)
+            check(lib.lcd_small_level_cuts(n, blocks, levels, ptr(dag.wavefronts), ptr(dag.wavefront_ptr),
+                                           ptr(self.cuts), _stream()), "lcd_small_level_cuts")
+            cuts = np.empty((blocks + 1, levels), dtype=np.int64)
+            cuts[:blocks] = self.cuts.cpu().numpy().reshape(blocks, levels)
+            cuts[blocks] = widths
+        else:
+            self.cuts = None
+            cuts = np.stack([np.zeros(levels, dtype=np.int64), widths])
+        padded = (np.diff(cuts, axis=0) + 31) // 32 * 32              # blocks x levels
+        local = np.zeros((blocks, levels + 1), dtype=np.int64)
+        np.cumsum(padded, axis=1, out=local[:, 1:])
+        base = np.zeros(blocks + 1, dtype=np.int64)
+        np.cumsum(local[:, -1], out=base[1:])
+        table = local + base[:-1, None]
+        self.n_slots = int(base[-1])
+        limit = SMALL_MAX_SLOTS if blocks == 1 else SLICED_MAX_SLOTS
+        if self.n_slots > limit:
+            raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
+                              f"{self.n_slots} task slots after padding to whole warps; "
+                              f"the level walk serves up to {limit}")
+        self.slot_ptr = torch.from_numpy(np.ascontiguousarray(table.astype(np.int32)).reshape(-1)).to(dev)
         m = max(self.n_slots, 1)
         pos = torch.empty(max(n, 1), **i32)
         cursor = torch.empty(m, **i32)
         info_dev = torch.zeros(4, **i32)
-        status = new_status(dev)
+        self.status = status = new_status(dev)
         info = (ctypes.c_int32 * 4)()
         check(lib.lcd_small_plan_measure(op, flags, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(diag_pos),
                                          ptr(dag.wavefronts), ptr(dag.level), ptr(dag.wavefront_ptr),
-                                         ptr(self.slot_ptr), dag.n_levels, self.n_slots, ptr(pos),
+                                         ptr(self.slot_ptr), ptr(self.cuts), levels, blocks, self.n_slots,
+                                         ptr(pos),
                                          ptr(cursor), ptr(info_dev), ptr(status), _stream(),
                                          ctypes.byref(info)), "lcd_small_plan_measure")
         longest, self.max_width = int(info[0]), int(info[1])
         if longest > lib.lcd_small_max_entries():
             raise NativeError(nat.ERR_TOO_LARGE, "SmallPlan",
-                              f"a task has {longest} operands; the one-block solver "
+                              f"a task has {longest} operands; the level walk "
                               f"serves up to {lib.lcd_small_max_entries()}")
         self.entries = 2 if longest <= 2 else (4 if longest <= 4 else 8)
         self.rec_pc = torch.empty(self.entries * m, **i32)
@@ -525,7 +553,8 @@ class SmallPlan:
         self.diag_src = torch.empty(m, **i32)
         far = ctypes.c_int32(0)
         check(lib.lcd_small_plan_fill(op, flags, n, Ai.numel(), ptr(Ap), ptr(Ai), ptr(diag_pos),
-                                      ptr(dag.wavefronts), ptr(pos), self.n_slots, self.entries,
+                                      ptr(dag.wavefronts), ptr(dag.level), ptr(self.slot_ptr), levels,
+                                      blocks, ptr(pos), self.n_slots, self.entries,
                                       ptr(self.rec_pc), ptr(self.rec_src), ptr(self.row_of),
                                       ptr(self.diag_src), ptr(cursor), ptr(info_dev), ptr(status),
                                       _stream(), ctypes.byref(far)), "lcd_small_plan_fill")
@@ -537,23 +566,41 @@ class SmallPlan:
 
     @staticmethod
     def serves(n, nnz):
-        """Cheap size test before a plan is attempted."""
+        """Cheap size test before a one-block plan is attempted."""
         return 0 < n <= SMALL_MAX_ROWS and nnz - n <= nat.load().lcd_small_max_entries() * n
 
 
 SMALL_MAX_ROWS = 1 << 18
 SMALL_MAX_SLOTS = 1 << 21
+SLICED_MAX_SLOTS = 1 << 27         # slots x 8 operand entries stay below 2^31
+SLICED_MAX_TABLE = 1 << 24         # blocks x (levels + 1) entries of the slot table
+SLICED_ROWS_PER_SLICE = 64         # average tasks of a slice of a level worth a block of its own
 
 
-def sptrsv_small(plan, Ax, b, x=None):
-    """One-block level walk of a ``SmallPlan`` (asynchronous on the current stream)."""
+def sliced_blocks(n, levels, device=None):
+    """Thread blocks for the shared level walk: one per SM at most, and no more than give every
+    block about 64 tasks of an average level."""
+    count = ctypes.c_int(0)
+    check(nat.load().lcd_device_sm_count(ctypes.byref(count)), "lcd_device_sm_count")
+    return int(max(1, min(count.value, n // max(levels, 1) // SLICED_ROWS_PER_SLICE)))
+
+
+def sptrsv_small(plan, Ax, b, x=None, *, status=None, timeout_ms=0, sync=False, same_values=False):
+    """Level walk of a ``SmallPlan`` (asynchronous on the current stream unless ``sync``).
+    ``same_values``: Ax holds what the previous solve with this plan had (one matrix, many
+    right-hand sides) - its coefficients are not gathered into slot order again."""
     _require(Ax, torch.float64, "Ax")
     _require(b, torch.float64, "b")
     x = torch.empty_like(b) if x is None else x
+    status = plan.status if status is None else status
+    host = ctypes.c_int(0)
     check(nat.load().lcd_sptrsv_small(plan.n, plan.n_slots, plan.entries, ptr(Ax), ptr(b), ptr(x),
                                       ptr(plan.rec_pc), ptr(plan.rec_src), ptr(plan.row_of),
-                                      ptr(plan.diag_src), ptr(plan.slot_ptr), plan.n_levels,
-                                      plan.max_width, ptr(plan.scratch), plan.scratch.numel(), _stream()),
+                                      ptr(plan.diag_src), ptr(plan.slot_ptr), plan.n_levels, plan.blocks,
+                                      plan.max_width, 0 if same_values else 1, ptr(plan.scratch),
+                                      plan.scratch.numel(),
+                                      ptr(status), int(timeout_ms), _stream(),
+                                      ctypes.byref(host) if sync else None),
           "lcd_sptrsv_small")
     return x
 

@@ -321,6 +321,91 @@ def test_small_solver_config1_csc_and_far_operands(cuda, oracle):
                                    rtol=1e-10, atol=1e-12)
 
 
+@pytest.mark.parametrize("blocks", [2, 7, 40, 148])
+@pytest.mark.parametrize("op", ["csr_lower", "csr_upper", "csc_lower", "csc_upper"])
+def test_level_walk_shared_by_many_blocks(cuda, oracle, op, blocks):
+    """The level walk cut into node ranges, one thread block each: operands of the own range
+    through shared memory, the others polled in global memory.  Same results as the one-block
+    form bit for bit (the operands of a task are taken in the same order); repeated solves keep
+    the gathered coefficients; levels narrower than the number of blocks leave blocks idle."""
+    from lcd_b200 import generators as gen, ops
+    tri = gen.laplacian3d_tril(17, seed=4)
+    if op.endswith("upper"):
+        tri = gen.upper_from_lower(tri)
+    b = np.random.default_rng(5).uniform(-1, 1, tri.n)
+    Ap, Ai, Ax = tri.csc_arrays() if op.startswith("csc") else tri.csr_arrays()
+    dAp, dAi, dAx, db = (dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda),
+                         dev(b, np.float64, cuda))
+    dag = ops.dag_build(op, dAp, dAi)
+    one = host(ops.sptrsv_small(ops.SmallPlan(op, dAp, dAi, dag), dAx, db, sync=True))
+    plan = ops.SmallPlan(op, dAp, dAi, dag, blocks=blocks)
+    assert plan.blocks == blocks and plan.n_slots >= tri.n
+    x = host(ops.sptrsv_small(plan, dAx, db, sync=True))
+    np.testing.assert_array_equal(x, one)
+    np.testing.assert_allclose(x, getattr(oracle, "sptrsv_" + op)(Ap, Ai, Ax, b), rtol=1e-10, atol=1e-12)
+    b2 = np.random.default_rng(6).uniform(-1, 1, tri.n)
+    x2 = host(ops.sptrsv_small(plan, dAx, dev(b2, np.float64, cuda), sync=True, same_values=True))
+    np.testing.assert_allclose(x2, getattr(oracle, "sptrsv_" + op)(Ap, Ai, Ax, b2), rtol=1e-10, atol=1e-12)
+    scaled = 3.0 * Ax                                    # new values: gathered again
+    x3 = host(ops.sptrsv_small(plan, dev(scaled, np.float64, cuda), db, sync=True))
+    np.testing.assert_allclose(x3, getattr(oracle, "sptrsv_" + op)(Ap, Ai, scaled, b), rtol=1e-10, atol=1e-12)
+
+
+def test_level_walk_on_factors_random_patterns_and_bad_input(cuda, oracle):
+    """Unit-lower / upper solves on ILU0 factors kept in place; a random band matrix whose
+    operands reach far back and into other blocks' ranges; an order that is no level order is
+    reported by the plan, not walked."""
+    import torch
+    from lcd_b200 import _native as nat, generators as gen, ops
+    mat, b = gen.laplacian3d_ilu0(14, seed=0)
+    Ap, Ai, Ax = mat.indptr.astype(np.int32), mat.indices.astype(np.int32), mat.data
+    fac = oracle.ilu0_csr(Ap, Ai, Ax, fast=True)
+    dAp, dAi, dF, db = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(fac, np.float64, cuda), dev(b, np.float64, cuda)
+    pos = ops.diag_positions(dAp, dAi)
+    lower = ops.dag_build("ilu0_csr", dAp, dAi)
+    upper = ops.dag_build("csr_upper_rows", dAp, dAi)
+    hp = host(pos)
+    y_ref = oracle.sptrsv_unit_lower_of_full(Ap, Ai, fac, hp, b)
+    x_ref = oracle.sptrsv_upper_of_full(Ap, Ai, fac, hp, y_ref)
+    for blocks in (1, 5, 33):
+        pl = ops.SmallPlan("csr_lower", dAp, dAi, lower, diag_pos=pos, unit_diag=True, blocks=blocks)
+        pu = ops.SmallPlan("csr_upper", dAp, dAi, upper, diag_pos=pos, blocks=blocks)
+        y = ops.sptrsv_small(pl, dF, db, sync=True)
+        x = host(ops.sptrsv_small(pu, dF, y, sync=True))
+        np.testing.assert_allclose(host(y), y_ref, rtol=1e-10, atol=1e-12)
+        np.testing.assert_allclose(x, x_ref, rtol=1e-10, atol=1e-12)
+    band = gen.random_band_lower(30_000, seed=12, mean_degree=4.0, band=2000)
+    Bp, Bi, Bx = band.csr_arrays()
+    dBp, dBi = dev(Bp, np.int32, cuda), dev(Bi, np.int32, cuda)
+    bdag = ops.dag_build("csr_lower", dBp, dBi)
+    want = oracle.sptrsv_csr_lower(Bp, Bi, Bx, band.b)
+    for blocks in (3, 20):
+        try:
+            plan = ops.SmallPlan("csr_lower", dBp, dBi, bdag, blocks=blocks)
+        except nat.NativeError as error:                  # a row with more than eight operands
+            assert error.code == nat.ERR_TOO_LARGE
+            break
+        x = host(ops.sptrsv_small(plan, dev(Bx, np.float64, cuda), dev(band.b, np.float64, cuda), sync=True))
+        np.testing.assert_allclose(x, want, rtol=1e-10, atol=1e-12)
+    # levels that do not belong to the matrix: an operand in the same level as its task
+    tri = gen.laplacian2d_tril(20, seed=0)
+    Tp, Ti, _ = tri.csr_arrays()
+    dTp, dTi = dev(Tp, np.int32, cuda), dev(Ti, np.int32, cuda)
+    good = ops.dag_build("csr_lower", dTp, dTi)
+
+    class Flat:                                           # every node in one level
+        n_levels = 1
+        wavefronts = torch.arange(tri.n, dtype=torch.int32, device=cuda)
+        level = torch.zeros(tri.n, dtype=torch.int32, device=cuda)
+        wavefront_ptr = torch.tensor([0, tri.n], dtype=torch.int32, device=cuda)
+        wavefront_ptr_host = np.array([0, tri.n], dtype=np.int32)
+    for blocks in (1, 4):
+        with pytest.raises(nat.NativeError) as err:
+            ops.SmallPlan("csr_lower", dTp, dTi, Flat, blocks=blocks)
+        assert err.value.code == nat.ERR_CYCLE
+    assert good.n_levels > 1
+
+
 def test_partition_need_mask_matches_numpy(cuda):
     """need_mask[c] has bit q set exactly when a row owned by rank q stores an off-diagonal entry
     in a column c produced by another rank (lower and upper, node ids reversed for upper)."""
