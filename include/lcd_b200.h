@@ -650,7 +650,11 @@ int lcd_set_tuning(int key, int value);
 /* Profiling aid (no reference counterpart): with a non-NULL device array of 64-bit words,
  * the one-lane-per-row solver (n words) and the chain solver (2 n + 29 C words, C the number
  * of 512-row chunks: row stamps, per-chunk start times, wait counters and the helpers'
- * publication stamps) record SM cycle counters and timer values.  Pass NULL to switch it off again. */
+ * publication stamps) record SM cycle counters and timer values; the ordered solve (3 n words:
+ * timer when a row's batch came up, when the row was published, its waiting trips) and the level
+ * walk (12 n_levels + 4096 words: cycle counter after every level and around the first thread's
+ * tasks; shared walk: timer after every level of the first, middle and last block) likewise.
+ * Pass NULL to switch it off again. */
 int lcd_debug_set_trace(long long *trace_dev);
 
 /*

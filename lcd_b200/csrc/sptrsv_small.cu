@@ -272,7 +272,9 @@ __global__ void small_sort_slots_kernel(int n, int E, int upper, const int *__re
 // ---- per value set --------------------------------------------------------------------
 // Coefficients and reciprocal diagonals into slot order (fully parallel; repeated only when the
 // matrix values change - the right-hand side is read in place by the walk).
-__global__ void small_pack_kernel(const SmallLayout lay, const double *__restrict__ Ax, double *rec_val) {
+// (one block: the right-hand side travels in the record too, b != NULL, and the pass runs per solve)
+__global__ void small_pack_kernel(const SmallLayout lay, const double *__restrict__ Ax,
+                                  const double *__restrict__ b, double *rec_val) {
     const int E = lay.entries, stride = gridDim.x * blockDim.x;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < lay.n; t += stride) {
         double *rec = rec_val + (size_t)t * (E + 2);
@@ -282,9 +284,17 @@ __global__ void small_pack_kernel(const SmallLayout lay, const double *__restric
         }
         const int row = lay.row_of[t];
         const int d = lay.diag_src[t];
-        rec[E] = 0.0;
+        rec[E] = (b && row >= 0) ? b[row] : 0.0;
         rec[E + 1] = row < 0 ? 0.0 : (d >= 0 ? 1.0 / Ax[d] : 1.0);   // (padding slots solve to 0)
     }
+}
+
+// One block: the walk stores x by position only; this pass puts it into matrix order.
+__global__ void small_unpack_kernel(int n, const int *__restrict__ row_of, const double *__restrict__ xp,
+                                    double *__restrict__ x) {
+    const int stride = gridDim.x * blockDim.x;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
+        if (row_of[t] >= 0) x[row_of[t]] = xp[t];
 }
 
 // ---- per solve ------------------------------------------------------------------------
@@ -293,7 +303,7 @@ struct SmallTask {
     double val[E];
     double bb, dinv;
     int pc[E];                   // slots of the operands (-1: none)
-    int row;                     // matrix row of the task (-1: padding slot)
+    int row;                     // shared walk: matrix row of the task (-1: padding slot)
     double rx[SHARED ? E : 1];   // shared walk: operands of other blocks, fetched a turn ahead
                                  // (the pending pattern: not yet there)
 };
@@ -337,8 +347,10 @@ __device__ __forceinline__ void small_load(SmallTask<E, SHARED> &q, const SmallS
             q.val[2 * k] = v.x;
             q.val[2 * k + 1] = v.y;
         }
-        q.dinv = __ldg(rv + E / 2).y;
-        q.row = __ldg(p.lay.row_of + t);
+        const double2 tail = __ldg(rv + E / 2);
+        q.dinv = tail.y;
+        if (SHARED) q.row = __ldg(p.lay.row_of + t);
+        else q.bb = tail.x;               // one block: the right-hand side came with the record
         if (E == 2) {
             const int2 c = __ldg(reinterpret_cast<const int2 *>(p.lay.rec_pc + (size_t)t * E));
             q.pc[0] = c.x;
@@ -382,8 +394,10 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
     int phase = 0;
     small_load(q0, p, base, count, t);
     if (DEPTH > 1) small_load(q1, p, base, count, t + T);
-    small_values(q0, p, count, t);
-    if (DEPTH > 1) small_values(q1, p, count, t + T);
+    if (SHARED) {
+        small_values(q0, p, count, t);
+        if (DEPTH > 1) small_values(q1, p, count, t + T);
+    }
     if (SHARED) {
 #pragma unroll
         for (int e = 0; e < E; ++e) {
@@ -401,7 +415,7 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
             if (pc >= 0) {
                 const int rel = pc - base;
                 double xv;
-                if ((unsigned)rel < (unsigned)t) {        // a slot of this block (earlier level)
+                if (!SHARED || (unsigned)rel < (unsigned)t) {   // a slot of this block (earlier level)
                     xv = (use_ring && t - rel <= kRing / 2) ? ring[rel & (kRing - 1)]
                                                             : *(volatile const double *)(xp + rel);
                 } else if (!SHARED) {
@@ -427,14 +441,14 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
         // orders it for the block's own readers); shared walk: other blocks poll it
         if (shared_walk) st_relaxed_f64(xp + t, publishable(xi));
         else xp[t] = xi;
-        if (c.row >= 0) p.x[c.row] = xi;   // the result in matrix order (nobody reads it here)
+        if (SHARED && c.row >= 0) p.x[c.row] = xi;   // the result in matrix order (nobody reads it here)
         if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[p.n_levels + 3 * traced + 1] = clock64();
         small_load(c, p, base, count, t + DEPTH * T);
         t += T;
-        if constexpr (DEPTH > 1) {
+        if constexpr (SHARED && DEPTH > 1) {
             small_values(next, p, count, t);         // next turn's task: its record is there by now
-            if constexpr (SHARED) small_peek(next, p, base, count, t);
-        } else {
+            small_peek(next, p, base, count, t);
+        } else if constexpr (SHARED) {
             small_values(c, p, count, t);            // (one register set: waits for the record just loaded)
         }
         if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[p.n_levels + 3 * traced++ + 2] = clock64();
@@ -453,7 +467,8 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
             }
             __syncthreads();
             if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[first + l] = clock64();
-            if (SHARED && p.trace && tid == 0) {     // EXPERIMENT: level times of three blocks
+            if (SHARED && p.trace && tid == 0) {     // shared walk: timer after every level of the first,
+                                                     // the middle and the last block [8..11) x n_levels
                 const int which = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x / 2 ? 1 : (blockIdx.x == gridDim.x - 1 ? 2 : -1));
                 if (which >= 0) p.trace[(8ll + which) * p.n_levels + first + l] = (long long)global_timer();
             }
@@ -646,9 +661,11 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
     const SmallLayout lay{n_slots, entries, rec_pc, rec_src, row_of, diag_src};
     int rc = reset_status(status_dev, st);
     if (rc) return rc;
-    if (gather_values) {
-        const int grid = (n_slots + 255) / 256 < sm_count() * 8 ? (n_slots + 255) / 256 : sm_count() * 8;
-        small_pack_kernel<<<grid, 256, 0, st>>>(lay, Ax, rec_val);
+    const int grid = (n_slots + 255) / 256 < sm_count() * 8 ? (n_slots + 255) / 256 : sm_count() * 8;
+    if (blocks == 1 || gather_values) {
+        // one block: coefficients and right-hand side per solve (small systems: a few microseconds);
+        // shared walk: coefficients only, and only when asked - it reads b in place
+        small_pack_kernel<<<grid, 256, 0, st>>>(lay, Ax, blocks == 1 ? b : nullptr, rec_val);
         LCD_CUDA_TRY(cudaGetLastError());
     }
     if (blocks > 1) {   // blocks poll each other's results: the value is its own ready flag
@@ -662,5 +679,9 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
     else if (entries == 4) rc = launch_small_e<4>(p, st);
     else rc = launch_small_e<8>(p, st);
     if (rc) return rc;
+    if (blocks == 1) {
+        small_unpack_kernel<<<grid, 256, 0, st>>>(n_slots, row_of, xp, x);
+        LCD_CUDA_TRY(cudaGetLastError());
+    }
     return finish(status_dev, st, status_host);
 }

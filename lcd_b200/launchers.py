@@ -182,8 +182,10 @@ def bind(lowering):
         cache.pop("chain_values", None)
         ends = torch.tensor([end for end, _ in pieces], dtype=Ap.dtype, device=Ap.device)
         # rows [0, r) are complete once Ap[r] entries are there
-        complete = (torch.searchsorted(Ap, ends, right=True) - 1).clamp(0, n)
-        complete = (complete // ops.CHAIN_SOLVE_ROWS * ops.CHAIN_SOLVE_ROWS).tolist()
+        # (the few numbers are finished on the host: every torch operator used here for the first
+        # time in a process costs tens of milliseconds of module loading)
+        found = torch.searchsorted(Ap, ends, right=True).tolist()
+        complete = [min(max(r - 1, 0), n) // ops.CHAIN_SOLVE_ROWS * ops.CHAIN_SOLVE_ROWS for r in found]
         complete[-1] = n
         status = ops.new_status(Ax.device)
         stream = torch.cuda.current_stream()
