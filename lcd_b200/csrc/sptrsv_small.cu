@@ -277,15 +277,17 @@ __global__ void small_pack_kernel(const SmallLayout lay, const double *__restric
                                   const double *__restrict__ b, double *rec_val) {
     const int E = lay.entries, stride = gridDim.x * blockDim.x;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < lay.n; t += stride) {
-        double *rec = rec_val + (size_t)t * (E + 2);
-        for (int e = 0; e < E; ++e) {
-            const int s = lay.rec_src[(size_t)t * E + e];
-            rec[e] = s >= 0 ? Ax[s] : 0.0;
+        // (records are 16-byte aligned and E is even: pairs of indices in, pairs of doubles out)
+        const int2 *src = reinterpret_cast<const int2 *>(lay.rec_src + (size_t)t * E);
+        double2 *rec = reinterpret_cast<double2 *>(rec_val + (size_t)t * (E + 2));
+        for (int e = 0; e < E / 2; ++e) {
+            const int2 s = __ldg(src + e);
+            rec[e] = make_double2(s.x >= 0 ? Ax[s.x] : 0.0, s.y >= 0 ? Ax[s.y] : 0.0);
         }
         const int row = lay.row_of[t];
         const int d = lay.diag_src[t];
-        rec[E] = (b && row >= 0) ? b[row] : 0.0;
-        rec[E + 1] = row < 0 ? 0.0 : (d >= 0 ? 1.0 / Ax[d] : 1.0);   // (padding slots solve to 0)
+        rec[E / 2] = make_double2((b && row >= 0) ? b[row] : 0.0,
+                                  row < 0 ? 0.0 : (d >= 0 ? 1.0 / Ax[d] : 1.0));   // (padding slots solve to 0)
     }
 }
 
