@@ -268,6 +268,36 @@ def test_decorated_narrow_levels_take_the_chain_solver(cuda, oracle, monkeypatch
     assert calls["solve"] == 3
 
 
+def test_decorated_wide_levels_take_the_shared_level_walk(cuda, oracle, monkeypatch):
+    """A 3-D grid with hundreds of rows per level through the decorator: the sync-free launcher
+    walks the levels with one thread block per node range; the coefficients are gathered into
+    slot order on the first call and again only when the values change."""
+    import ops_decorated as od
+    from lcd_b200 import generators as gen, ops
+    tri = gen.laplacian3d_tril(48, seed=2)
+    Ap, Ai, Ax = tri.csr_arrays()
+    seen = []
+    real = ops.sptrsv_small
+
+    def counted(plan, *a, **k):
+        seen.append((plan.blocks, bool(k.get("same_values"))))
+        return real(plan, *a, **k)
+    monkeypatch.setattr(ops, "sptrsv_small", counted)
+    for op in (od.csr_warp_syncfree, od.csr_plain_syncfree):
+        seen.clear()
+        x = op(Ap, Ai, Ax, tri.b, tri.n)
+        np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b), rtol=1e-10, atol=1e-12)
+        assert oracle.relative_residual_csr(Ap, Ai, Ax, x, tri.b) <= 1e-12
+        b2 = tri.b[::-1].copy()
+        x2 = op(Ap, Ai, Ax, b2, tri.n)                                     # same matrix, new right-hand side
+        np.testing.assert_allclose(x2, oracle.sptrsv_csr_lower(Ap, Ai, Ax, b2), rtol=1e-10, atol=1e-12)
+        Ax3 = Ax * 1.5
+        x3 = op(Ap, Ai, Ax3, tri.b, tri.n)                                 # new values: gathered again
+        np.testing.assert_allclose(x3, oracle.sptrsv_csr_lower(Ap, Ai, Ax3, tri.b), rtol=1e-10, atol=1e-12)
+        assert [same for _, same in seen] == [False, True, False]
+        assert all(blocks >= 8 for blocks, _ in seen)
+
+
 def _pattern(path, storage):
     from lcd_b200.matrix_market import load_matrix_market
     matrix = load_matrix_market(path, 0)
