@@ -386,8 +386,9 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
     const bool use_ring = p.max_width <= kRing / 2;
     constexpr bool shared_walk = SHARED;
     const int *table = p.wptr + (size_t)blockIdx.x * (p.n_levels + 1);
-    const int base = __ldg(table);                         // the block's first slot
-    const int count = __ldg(table + p.n_levels) - base;    // ... and how many it has
+    // the block's first slot and how many it has (one block: all of them, known without a look)
+    const int base = SHARED ? __ldg(table) : 0;
+    const int count = SHARED ? __ldg(table + p.n_levels) - base : p.lay.n;
     double *xp = p.xp + base;
     // two register sets used in turn: a set is reloaded right after its task and not touched
     // again until two turns later, so its loads have several levels to arrive
