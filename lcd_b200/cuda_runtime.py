@@ -188,25 +188,42 @@ class TorchCUDA:
         if not (pinned and host.dim() == 1 and
                 host.numel() * host.element_size() >= 2 * STREAMED_UPLOAD_BYTES):
             return DeviceArray(host.to("cuda", non_blocking=pinned))
-        device = torch.empty(host.shape, dtype=host.dtype, device="cuda")
+        return TorchCUDA.to_device_together([array])[0]
+
+    @staticmethod
+    def to_device_together(arrays):
+        """Streamed upload of page-locked 1-D arrays of one length (the column indices and the
+        values of a sparse matrix): every array is cut at the same element positions and the
+        pieces are issued in turn, so that after the k-th piece of the last array the first
+        ``end_k`` elements of all of them are on the device.  One ``DeviceArray`` per array,
+        each with its own list of (elements uploaded so far, event)."""
+        import torch
+        hosts = [torch.from_numpy(np.ascontiguousarray(a)) for a in arrays]
+        count = hosts[0].numel()
+        if any(h.dim() != 1 or h.numel() != count or not h.is_pinned() for h in hosts):
+            raise CUDARuntimePreparationError(
+                "arrays uploaded together must be page-locked, one-dimensional and of one length")
+        devices = [torch.empty(h.shape, dtype=h.dtype, device="cuda") for h in hosts]
         copies = _copy_stream()
-        copies.wait_stream(torch.cuda.current_stream())   # the block may just have been in use there
-        device.record_stream(copies)
-        step = STREAMED_UPLOAD_BYTES // host.element_size()
-        arrival = []
+        copies.wait_stream(torch.cuda.current_stream())   # the blocks may just have been in use there
+        for device in devices:
+            device.record_stream(copies)
+        step = STREAMED_UPLOAD_BYTES // max(h.element_size() for h in hosts)
+        arrivals = [[] for _ in hosts]
         with torch.cuda.stream(copies):
             start, piece = 0, step // 4
-            while start < host.numel():
+            while start < count:
                 # (a short first piece: whoever follows the pieces starts early; then doubling:
                 # the link is faster than any consumer here, and fewer pieces mean fewer launches)
-                end = min(host.numel(), start + piece)
+                end = min(count, start + piece)
                 piece *= 2
-                device[start:end].copy_(host[start:end], non_blocking=True)
-                event = torch.cuda.Event()
-                event.record(copies)
-                arrival.append((end, event))
+                for host, device, arrival in zip(hosts, devices, arrivals):
+                    device[start:end].copy_(host[start:end], non_blocking=True)
+                    event = torch.cuda.Event()
+                    event.record(copies)
+                    arrival.append((end, event))
                 start = end
-        return DeviceArray(device, arrival)
+        return [DeviceArray(device, arrival) for device, arrival in zip(devices, arrivals)]
 
     @staticmethod
     def synchronize():
@@ -255,6 +272,7 @@ class CUDAPreparedArguments:
     host_values: dict
     lifted_variables: tuple
     hints: dict = field(default_factory=dict)   # what the inspector learnt (rows, levels, ...)
+    verify: object = None   # set when the call started under a predicted plan: () -> plan was right
 
     @property
     def launcher_arguments(self):
@@ -536,11 +554,14 @@ def _is_cuda_array(value):
     return isinstance(value, DeviceArray) or hasattr(value, "__cuda_array_interface__")
 
 
-def start_large_uploads(values, skip=()):
+def start_large_uploads(values, skip=(), together=()):
     """Begin the upload of the page-locked arrays among ``values`` (a dict, changed in place) if
     one of them is large enough to be streamed in pieces, so that the transfer overlaps the host
     work that follows.  Smaller arrays go first: the launcher that follows the pieces needs
-    them complete.  Everything else stays as it is."""
+    them complete.  The arrays named in ``together`` (one length, e.g. a matrix's column
+    indices and values) go last and travel side by side, cut at the same element positions,
+    so that a consumer that follows the pieces has whole rows early.  Everything else stays as
+    it is."""
     import torch
     pinned = [(value.nbytes, name) for name, value in values.items()
               if name not in skip and isinstance(value, np.ndarray) and value.ndim == 1
@@ -548,5 +569,12 @@ def start_large_uploads(values, skip=()):
               and torch.from_numpy(value).is_pinned()]
     if not pinned or max(pinned)[0] < 2 * STREAMED_UPLOAD_BYTES:
         return
+    side_by_side = [name for name in together if any(name == found for _, found in pinned)]
+    if len(side_by_side) < 2:
+        side_by_side = []
     for _, name in sorted(pinned):
-        values[name] = TorchCUDA.to_device(values[name])
+        if name not in side_by_side:
+            values[name] = TorchCUDA.to_device(values[name])
+    if side_by_side:
+        arrays = TorchCUDA.to_device_together([values[name] for name in side_by_side])
+        values.update(zip(side_by_side, arrays))

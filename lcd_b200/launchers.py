@@ -169,10 +169,11 @@ def bind(lowering):
         else:           # substitution (still on the GPU): slower on such matrices, but stable
             ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper)
 
-    def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache):
+    def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache, index_pieces=None):
         # The value array is still being uploaded, piece by piece (pieces: elements uploaded
-        # so far and the event that says so).  The chain solver consumes the matrix front to
-        # back, so tiles are prepared and rows solved as far as the values have arrived: the
+        # so far and the event that says so; index_pieces: the same for the column indices when
+        # they travel beside the values).  The chain solver consumes the matrix front to
+        # back, so tiles are prepared and rows solved as far as the entries have arrived: the
         # solve overlaps the upload instead of following it.  (No look at the tile cache: its
         # key needs the whole array, and the preparation hides under the upload anyway.)
         n = Ap.numel() - 1
@@ -189,14 +190,31 @@ def bind(lowering):
         complete[-1] = n
         status = ops.new_status(Ax.device)
         stream = torch.cuda.current_stream()
+        # as in ops.chain_prepare_and_solve: the tiles of a range are prepared on a second
+        # stream (behind the upload of its entries), the range is solved on this stream behind
+        # its tiles; a large piece is cut into ranges so that its preparation runs beside the
+        # solve of the rows before it
+        side = ops.side_stream(Ax.device)
+        side.wait_stream(stream)
+        step = ops.chain_pipeline_bounds(n)[1]
         begin = 0
-        for (_, event), end in zip(pieces, complete):
-            stream.wait_event(event)
+        for (entries, event), end in zip(pieces, complete):
             if end <= begin and end != n:
                 continue
-            ops.chain_prepare(Ap, Ai, Ax, workspace, rows=(begin, end))
-            ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, status=status, rows=(begin, end),
-                                 sync=end == n)
+            side.wait_event(event)
+            if index_pieces:   # the first piece of the indices that covers these entries
+                side.wait_event(next(e for upto, e in index_pieces if upto >= entries))
+            cuts = list(range(begin, end, step)) + [end]
+            tiles = []
+            with torch.cuda.stream(side):
+                for lo, hi in zip(cuts[:-1], cuts[1:]):
+                    ops.chain_prepare(Ap, Ai, Ax, workspace, rows=(lo, hi))
+                    tiles.append(torch.cuda.Event())
+                    tiles[-1].record(side)
+            for lo, hi, prepared in zip(cuts[:-1], cuts[1:], tiles):
+                stream.wait_event(prepared)
+                ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, status=status, rows=(lo, hi),
+                                     sync=hi == n)
             begin = end
         if ops.chain_growth(workspace, n) > ops.CHAIN_MAX_GROWTH:
             # the block inverses grew: solve again by substitution (the whole array has arrived)
@@ -241,9 +259,13 @@ def bind(lowering):
                 getattr(values, "arrival", None) and values._tensor.dtype == torch.float64 and
                 chain_solver_preferred(hints.get("rows", 0), hints.get("levels", 0), hints.get("arch"))):
             Ax, pieces = values.take_arrival()
-            chain_solve_streamed(as_tensor(v[roles["ptr"]], torch.int32), as_tensor(v[roles["idx"]], torch.int32),
+            indices, index_pieces = v[roles["idx"]], None
+            if getattr(indices, "arrival", None) and indices._tensor.dtype == torch.int32:
+                indices, index_pieces = indices.take_arrival()
+            chain_solve_streamed(as_tensor(v[roles["ptr"]], torch.int32), as_tensor(indices, torch.int32),
                                  Ax, pieces, as_tensor(v[roles["rhs"]], torch.float64),
-                                 as_tensor(v[roles["out"]], torch.float64), hints.setdefault("cache", {}))
+                                 as_tensor(v[roles["out"]], torch.float64), hints.setdefault("cache", {}),
+                                 index_pieces)
             return
         Ap, Ai, Ax = matrix(v)
         b = as_tensor(v[roles["rhs"]], torch.float64)

@@ -379,6 +379,16 @@ def chain_pipeline_bounds(n, pieces=None):
     return list(range(0, n, step)) + [n]
 
 
+def side_stream(device):
+    """The second stream of a device, for throughput work that runs beside a latency-bound
+    kernel on the current stream."""
+    key = torch.device(device).index
+    side = _side_streams.get(key)
+    if side is None:
+        side = _side_streams[key] = torch.cuda.Stream(device=device, priority=0)
+    return side
+
+
 def chain_prepare_and_solve(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, unit_diag=False,
                             diag_pos=None, status=None, timeout_ms=0, sync=True, pieces=None):
     """Numeric preparation and solve of the chain solver as one pipelined step.  The solve runs
@@ -394,10 +404,7 @@ def chain_prepare_and_solve(Ap, Ai, Ax, b, workspace, x=None, *, upper=False, un
         return sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, upper=upper, unit_diag=unit_diag,
                                 diag_pos=diag_pos, status=status, timeout_ms=timeout_ms, sync=sync)
     main = torch.cuda.current_stream(b.device)
-    key = b.device.index
-    side = _side_streams.get(key)
-    if side is None:
-        side = _side_streams[key] = torch.cuda.Stream(device=b.device, priority=0)
+    side = side_stream(b.device)
     side.wait_stream(main)                      # the inputs are complete
     ready = []
     with torch.cuda.stream(side):

@@ -353,6 +353,52 @@ def test_decorated_chain_solve_follows_a_streamed_upload(cuda, oracle, monkeypat
     np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(gp, gi, gx, grid.b), rtol=1e-10, atol=1e-12)
 
 
+def test_decorated_chain_solve_starts_under_the_previous_plan(cuda, oracle, monkeypatch):
+    """A call whose page-locked arrays have the lengths of the previous call's starts under that
+    call's plan, with the column indices uploaded side by side with the values; the structure
+    fingerprint is compared after the launch, and a call with another structure is run again
+    under its own plan."""
+    import torch
+    import ops_decorated as od
+    import lcd_b200.cuda_runtime as rt
+    from lcd_b200 import generators as gen, ops
+    monkeypatch.setattr(rt, "STREAMED_UPLOAD_BYTES", 1 << 19)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+    tri = gen.random_band_lower(65_536, seed=5)
+    Ap, Ai, Ax = (pin(a) for a in tri.csr_arrays())
+    op = od.csr_warp_syncfree
+    want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
+    np.testing.assert_allclose(op(Ap, Ai, Ax, tri.b, tri.n), want, rtol=1e-10, atol=1e-12)
+    together, plans = [], []
+    real_together = rt.TorchCUDA.to_device_together
+    monkeypatch.setattr(rt.TorchCUDA, "to_device_together",
+                        staticmethod(lambda arrays: (together.append(len(arrays)), real_together(arrays))[1]))
+    real_dag = ops.dag_build
+    monkeypatch.setattr(ops, "dag_build", lambda *a, **k: (plans.append(1), real_dag(*a, **k))[1])
+    # same structure, new values: one side-by-side upload of indices and values, no new plan
+    Ax2 = pin(Ax * 1.25)
+    x = op(Ap, Ai, Ax2, tri.b, tri.n)
+    np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax2, tri.b), rtol=1e-10, atol=1e-12)
+    assert 2 in together and not plans
+    # another structure of the same lengths
+    Ai3 = Ai.copy()
+    for r in range(40_000, 40_100):
+        lo = Ap[r]                                # (the row's first column moves one to the left)
+        if Ap[r + 1] - 1 - lo >= 1 and Ai3[lo] > 0:
+            Ai3[lo] -= 1
+    assert not np.array_equal(Ai3, Ai)
+    Ai3 = pin(Ai3)
+    together.clear()
+    x = op(Ap, Ai3, Ax, tri.b, tri.n)
+    np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai3, Ax, tri.b), rtol=1e-10, atol=1e-12)
+    assert 2 in together and plans                # predicted, found different, planned afresh
+    # and back: the first structure's plan is still cached, the prediction (now the third
+    # structure's plan) is wrong again
+    plans.clear()
+    np.testing.assert_allclose(op(Ap, Ai, Ax, tri.b, tri.n), want, rtol=1e-10, atol=1e-12)
+    assert not plans
+
+
 @pytest.mark.parametrize("mode", ["wavefront", "sync_free"])
 @pytest.mark.parametrize("name", golden_names("ilu0_"))
 def test_decorated_ilu0_is_bit_identical(cuda, name, mode):
