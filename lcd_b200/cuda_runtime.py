@@ -74,12 +74,12 @@ STREAMED_UPLOAD_BYTES = 64 << 20
 _COPY_STREAMS = {}
 
 
-def _copy_stream():
+def _copy_stream(kind="upload"):
     import torch
-    device = torch.cuda.current_device()
-    if device not in _COPY_STREAMS:
-        _COPY_STREAMS[device] = torch.cuda.Stream(device=device)
-    return _COPY_STREAMS[device]
+    key = (torch.cuda.current_device(), kind)
+    if key not in _COPY_STREAMS:
+        _COPY_STREAMS[key] = torch.cuda.Stream(device=key[0])
+    return _COPY_STREAMS[key]
 
 
 class DeviceArray:
@@ -90,6 +90,8 @@ class DeviceArray:
     still in flight.  Reading ``tensor`` makes the current stream wait for the whole upload; a
     launcher that wants to follow the pieces takes the list with ``take_arrival()`` and waits
     for the events itself."""
+
+    _early = None     # [page-locked tensor, its array, rows already on their way] of download_rows
 
     def __init__(self, tensor, arrival=None):
         self._tensor = tensor
@@ -119,11 +121,45 @@ class DeviceArray:
     def copy_to_host(self):
         # through page-locked memory: a copy into a fresh pageable array runs at a few GB/s
         # (33 MB took 15 ms)
+        if self._early is not None:
+            # a launcher that produces the array front to back has sent most of it already
+            (host, array, upto), self._early = self._early, None
+            _copy_stream("download").synchronize()
+            if upto < self._tensor.shape[0]:
+                host[upto:].copy_(self.tensor[upto:])
+            return array
         if self.tensor.numel() * self.tensor.element_size() < (1 << 16):
             return self.tensor.cpu().numpy()
         host, array = _pinned_result(tuple(self.tensor.shape), self.tensor.dtype)
         host.copy_(self.tensor)
         return array
+
+    def download_rows(self, begin, end):
+        """Start the copy of rows [begin, end) to the page-locked array that ``copy_to_host()``
+        will return, behind the work queued on the current stream so far.  For launchers that
+        finish their result front to back (ranges must follow one another from row 0; anything
+        else is ignored and copied at the end)."""
+        import torch
+        if self._early is None:
+            if begin != 0:
+                return
+            host, array = _pinned_result(tuple(self._tensor.shape), self._tensor.dtype)
+            self._early = [host, array, 0]
+        host, _, upto = self._early
+        if begin != upto or end <= begin:
+            return
+        stream = _copy_stream("download")
+        stream.wait_stream(torch.cuda.current_stream())
+        self._tensor.record_stream(stream)
+        with torch.cuda.stream(stream):
+            host[begin:end].copy_(self._tensor[begin:end], non_blocking=True)
+        self._early[2] = end
+
+    def forget_downloads(self):
+        """The rows sent so far are stale (the launcher computes the result again)."""
+        if self._early is not None:
+            _copy_stream("download").synchronize()
+            self._early = None
 
     def __len__(self):
         return self._tensor.shape[0]
@@ -191,12 +227,41 @@ class TorchCUDA:
         return TorchCUDA.to_device_together([array])[0]
 
     @staticmethod
-    def to_device_together(arrays):
+    def to_device_split(array, head):
+        """Upload the first ``head`` elements of a page-locked 1-D array now; the returned
+        ``finish()`` queues the rest (call it once, after whatever should travel in between).
+        The ``DeviceArray`` carries both pieces in its arrival list."""
+        import torch
+        host = torch.from_numpy(np.ascontiguousarray(array))
+        device = torch.empty(host.shape, dtype=host.dtype, device="cuda")
+        copies = _copy_stream()
+        copies.wait_stream(torch.cuda.current_stream())
+        device.record_stream(copies)
+        arrival = []
+
+        def piece(start, end):
+            with torch.cuda.stream(copies):
+                device[start:end].copy_(host[start:end], non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(copies)
+            arrival.append((end, event))
+
+        head = max(1, min(int(head), host.numel()))
+        piece(0, head)
+        if head == host.numel():
+            return DeviceArray(device, arrival), lambda: None
+        # (the list is complete before anybody can read it: finish() runs inside the same
+        # start_large_uploads call)
+        return DeviceArray(device, arrival), lambda: piece(head, host.numel())
+
+    @staticmethod
+    def to_device_together(arrays, after_first=None):
         """Streamed upload of page-locked 1-D arrays of one length (the column indices and the
         values of a sparse matrix): every array is cut at the same element positions and the
         pieces are issued in turn, so that after the k-th piece of the last array the first
         ``end_k`` elements of all of them are on the device.  One ``DeviceArray`` per array,
-        each with its own list of (elements uploaded so far, event)."""
+        each with its own list of (elements uploaded so far, event).  ``after_first()`` is called
+        when the first pieces have been queued (for a copy that may wait until then)."""
         import torch
         hosts = [torch.from_numpy(np.ascontiguousarray(a)) for a in arrays]
         count = hosts[0].numel()
@@ -222,6 +287,8 @@ class TorchCUDA:
                     event = torch.cuda.Event()
                     event.record(copies)
                     arrival.append((end, event))
+                if start == 0 and after_first is not None:
+                    after_first()           # (queues on the same copy stream)
                 start = end
         return [DeviceArray(device, arrival) for device, arrival in zip(devices, arrivals)]
 
@@ -554,13 +621,15 @@ def _is_cuda_array(value):
     return isinstance(value, DeviceArray) or hasattr(value, "__cuda_array_interface__")
 
 
-def start_large_uploads(values, skip=(), together=()):
+def start_large_uploads(values, skip=(), together=(), late=()):
     """Begin the upload of the page-locked arrays among ``values`` (a dict, changed in place) if
     one of them is large enough to be streamed in pieces, so that the transfer overlaps the host
     work that follows.  Smaller arrays go first: the launcher that follows the pieces needs
     them complete.  The arrays named in ``together`` (one length, e.g. a matrix's column
     indices and values) go last and travel side by side, cut at the same element positions,
-    so that a consumer that follows the pieces has whole rows early.  Everything else stays as
+    so that a consumer that follows the pieces has whole rows early; of the arrays named in
+    ``late`` (a right-hand side that the same consumer reads front to back) only the first
+    sixteenth goes before them, the rest behind their first pieces.  Everything else stays as
     it is."""
     import torch
     pinned = [(value.nbytes, name) for name, value in values.items()
@@ -572,9 +641,16 @@ def start_large_uploads(values, skip=(), together=()):
     side_by_side = [name for name in together if any(name == found for _, found in pinned)]
     if len(side_by_side) < 2:
         side_by_side = []
-    for _, name in sorted(pinned):
-        if name not in side_by_side:
+    finish = []
+    for nbytes, name in sorted(pinned):
+        if name in side_by_side:
+            continue
+        if side_by_side and name in late and nbytes >= STREAMED_UPLOAD_BYTES // 8:
+            values[name], rest = TorchCUDA.to_device_split(values[name], len(values[name]) // 16)
+            finish.append(rest)
+        else:
             values[name] = TorchCUDA.to_device(values[name])
     if side_by_side:
-        arrays = TorchCUDA.to_device_together([values[name] for name in side_by_side])
+        arrays = TorchCUDA.to_device_together([values[name] for name in side_by_side],
+                                              after_first=lambda: [rest() for rest in finish])
         values.update(zip(side_by_side, arrays))

@@ -306,7 +306,7 @@ def parallel(**kwargs):
                 pointers = roles["ptr"]
                 structure = {pointers: torch.from_numpy(values[pointers]).to("cuda", non_blocking=True)}
                 start_large_uploads(launch_values, skip=structure,
-                                    together=(roles["idx"], roles["val"]))
+                                    together=(roles["idx"], roles["val"]), late=(roles["rhs"],))
                 indices = launch_values[roles["idx"]]
                 expected = last_plan[0]
                 arrived = indices.arrival[-1][1]

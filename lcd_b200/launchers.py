@@ -169,10 +169,12 @@ def bind(lowering):
         else:           # substitution (still on the GPU): slower on such matrices, but stable
             ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper)
 
-    def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache, index_pieces=None):
+    def chain_solve_streamed(Ap, Ai, Ax, pieces, b, x, cache, index_pieces=None, rhs_pieces=None,
+                             result=None):
         # The value array is still being uploaded, piece by piece (pieces: elements uploaded
-        # so far and the event that says so; index_pieces: the same for the column indices when
-        # they travel beside the values).  The chain solver consumes the matrix front to
+        # so far and the event that says so; index_pieces, rhs_pieces: the same for the column
+        # indices when they travel beside the values and for a right-hand side sent in two parts;
+        # result: the device array object of x, which can send finished rows to the host early).  The chain solver consumes the matrix front to
         # back, so tiles are prepared and rows solved as far as the entries have arrived: the
         # solve overlaps the upload instead of following it.  (No look at the tile cache: its
         # key needs the whole array, and the preparation hides under the upload anyway.)
@@ -213,11 +215,17 @@ def bind(lowering):
                     tiles[-1].record(side)
             for lo, hi, prepared in zip(cuts[:-1], cuts[1:], tiles):
                 stream.wait_event(prepared)
+                if rhs_pieces:
+                    stream.wait_event(next(e for upto, e in rhs_pieces if upto >= hi))
                 ops.sptrsv_csr_chain(Ap, Ai, Ax, b, workspace, x, status=status, rows=(lo, hi),
                                      sync=hi == n)
+                if result is not None:
+                    result.download_rows(lo, hi)
             begin = end
         if ops.chain_growth(workspace, n) > ops.CHAIN_MAX_GROWTH:
             # the block inverses grew: solve again by substitution (the whole array has arrived)
+            if result is not None:
+                result.forget_downloads()
             ops.sptrsv_csr_syncfree(Ap, Ai, Ax, b, x, upper=lowering.upper)
 
     def csr_solve(Ap, Ai, Ax, b, x, v, hints):
@@ -262,10 +270,15 @@ def bind(lowering):
             indices, index_pieces = v[roles["idx"]], None
             if getattr(indices, "arrival", None) and indices._tensor.dtype == torch.int32:
                 indices, index_pieces = indices.take_arrival()
+            rhs, rhs_pieces = v[roles["rhs"]], None
+            if getattr(rhs, "arrival", None) and rhs._tensor.dtype == torch.float64:
+                rhs, rhs_pieces = rhs.take_arrival()
+            result, x = v[roles["out"]], as_tensor(v[roles["out"]], torch.float64)
+            if not (hasattr(result, "download_rows") and result._tensor.data_ptr() == x.data_ptr()):
+                result = None
             chain_solve_streamed(as_tensor(v[roles["ptr"]], torch.int32), as_tensor(indices, torch.int32),
-                                 Ax, pieces, as_tensor(v[roles["rhs"]], torch.float64),
-                                 as_tensor(v[roles["out"]], torch.float64), hints.setdefault("cache", {}),
-                                 index_pieces)
+                                 Ax, pieces, as_tensor(rhs, torch.float64), x,
+                                 hints.setdefault("cache", {}), index_pieces, rhs_pieces, result)
             return
         Ap, Ai, Ax = matrix(v)
         b = as_tensor(v[roles["rhs"]], torch.float64)

@@ -364,7 +364,7 @@ def test_decorated_chain_solve_starts_under_the_previous_plan(cuda, oracle, monk
     from lcd_b200 import generators as gen, ops
     monkeypatch.setattr(rt, "STREAMED_UPLOAD_BYTES", 1 << 19)
     pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
-    tri = gen.random_band_lower(65_536, seed=5)
+    tri = gen.random_band_lower(262_144, seed=5)      # (a right-hand side of 2 MB)
     Ap, Ai, Ax = (pin(a) for a in tri.csr_arrays())
     op = od.csr_warp_syncfree
     want = oracle.sptrsv_csr_lower(Ap, Ai, Ax, tri.b)
@@ -372,7 +372,7 @@ def test_decorated_chain_solve_starts_under_the_previous_plan(cuda, oracle, monk
     together, plans = [], []
     real_together = rt.TorchCUDA.to_device_together
     monkeypatch.setattr(rt.TorchCUDA, "to_device_together",
-                        staticmethod(lambda arrays: (together.append(len(arrays)), real_together(arrays))[1]))
+                        staticmethod(lambda arrays, **kw: (together.append(len(arrays)), real_together(arrays, **kw))[1]))
     real_dag = ops.dag_build
     monkeypatch.setattr(ops, "dag_build", lambda *a, **k: (plans.append(1), real_dag(*a, **k))[1])
     # same structure, new values: one side-by-side upload of indices and values, no new plan
@@ -380,6 +380,20 @@ def test_decorated_chain_solve_starts_under_the_previous_plan(cuda, oracle, monk
     x = op(Ap, Ai, Ax2, tri.b, tri.n)
     np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax2, tri.b), rtol=1e-10, atol=1e-12)
     assert 2 in together and not plans
+    # the right-hand side went in two parts around the first pieces of the matrix, and the result
+    # came back range by range
+    sent = []
+    real_split = rt.TorchCUDA.to_device_split
+    monkeypatch.setattr(rt.TorchCUDA, "to_device_split",
+                        staticmethod(lambda array, head: (sent.append(head), real_split(array, head))[1]))
+    early = []
+    real_rows = rt.DeviceArray.download_rows
+    monkeypatch.setattr(rt.DeviceArray, "download_rows",
+                        lambda self, lo, hi: (early.append((lo, hi)), real_rows(self, lo, hi))[1])
+    b2 = pin(tri.b * 0.5)
+    x = op(Ap, Ai, Ax2, b2, tri.n)
+    np.testing.assert_allclose(x, oracle.sptrsv_csr_lower(Ap, Ai, Ax2, b2), rtol=1e-10, atol=1e-12)
+    assert sent == [tri.n // 16] and early and early[0][0] == 0 and early[-1][1] == tri.n
     # another structure of the same lengths
     Ai3 = Ai.copy()
     for r in range(40_000, 40_100):
