@@ -406,6 +406,14 @@ int lcd_sptrsv_csr_ordered(int32_t n, int64_t nnz, int32_t nrhs, const int32_t *
  *       bytes, 256-byte aligned; rec_pc 16-byte aligned.  Asynchronous on `stream` unless
  *       status_host is given.
  *       LCD_ERR_TOO_LARGE: more blocks than the device can keep resident.
+ *   lcd_sptrsv_small_multi   the same walk for nrhs = 1, 2, 4, 8 or 16 right-hand sides (no
+ *       reference counterpart; the reference's launchers take one): b and x are row-major
+ *       n x nrhs blocks with leading dimension ld (doubles), blocks > 1 for nrhs > 1.  The walk
+ *       runs on nrhs interleaved copies of the pattern - task s * nrhs + r is slot s for
+ *       right-hand side r and reads slot s's record - so a level's hand-off is still one block
+ *       barrier plus the polls of operands that other blocks own.  scratch:
+ *       lcd_small_scratch_bytes_multi bytes.  LCD_ERR_TOO_LARGE also when n_slots * nrhs or
+ *       n * ld does not fit 31 bits.
  *   op: LCD_OP_CSR_LOWER / CSR_UPPER / CSC_LOWER / CSC_UPPER; flags: LCD_SOLVE_OF_FULL /
  *   UNIT_DIAG for the CSR ops.
  */
@@ -432,6 +440,14 @@ int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *
                      int32_t blocks, int32_t max_width, int32_t gather_values, void *scratch,
                      int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms, void *stream,
                      int *status_host);
+int lcd_small_scratch_bytes_multi(int32_t n_slots, int32_t entries, int32_t nrhs, int64_t *bytes);
+int lcd_sptrsv_small_multi(int32_t n, int32_t n_slots, int32_t entries, const double *Ax,
+                           const double *b, double *x, int32_t nrhs, int64_t ld,
+                           const int32_t *rec_pc, const int32_t *rec_src, const int32_t *row_of,
+                           const int32_t *diag_src, const int32_t *slot_ptr_dev, int32_t n_levels,
+                           int32_t blocks, int32_t max_width, int32_t gather_values, void *scratch,
+                           int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms,
+                           void *stream, int *status_host);
 
 /* ---- CSC -> supernodal layout ------------------------------------------------------ */
 /*

@@ -107,6 +107,10 @@ _SIGNATURES = {
     "lcd_small_scratch_bytes": (c_int, [c_int32, c_int32, ctypes.POINTER(c_int64)]),
     "lcd_sptrsv_small": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P, _P, _P, _P, c_int32,
                                  c_int32, c_int32, c_int32, _P, c_int64, _P, c_int32, _P, _P]),
+    "lcd_small_scratch_bytes_multi": (c_int, [c_int32, c_int32, c_int32, ctypes.POINTER(c_int64)]),
+    "lcd_sptrsv_small_multi": (c_int, [c_int32, c_int32, c_int32, _P, _P, _P, c_int32, c_int64, _P, _P, _P, _P,
+                                       _P, c_int32, c_int32, c_int32, c_int32, _P, c_int64, _P, c_int32,
+                                       _P, _P]),
     "lcd_spilu0_csr": (c_int, [c_int32, c_int64, _P, _P, _P, _P, c_int, _P, _P, _P, c_int32,
                                c_int, _P, c_int32, _P, ctypes.POINTER(c_int)]),
     "lcd_supernodal_layout_workspace_bytes": (c_int, [c_int32, c_int64, _P]),

@@ -60,6 +60,12 @@ struct SmallSolveParams {
     long long *trace;                    // profiling aid (lcd_debug_set_trace): SM cycle counter after
                                          // every level's barrier [n_levels], then, for the tasks of
                                          // thread 0, at the start / after the stores / at the end [3 each]
+    // Shared walk with R = 1 << rshift right-hand sides (row-major n x R blocks with leading
+    // dimension ld): the walk runs on R interleaved copies of the pattern.  Copy r of slot s is
+    // the task s * R + r; it reads the record of slot s, operand slots pc * R + r, and element r
+    // of its row of b and x.  Everything below (ring, x by position, level table) counts tasks.
+    int rshift;
+    int ld;
 };
 
 // ---- per pattern -------------------------------------------------------------------
@@ -305,7 +311,7 @@ struct SmallTask {
     double val[E];
     double bb, dinv;
     int pc[E];                   // slots of the operands (-1: none)
-    int row;                     // shared walk: matrix row of the task (-1: padding slot)
+    int row;                     // shared walk: the task's element of b and x (-1: padding slot)
     double rx[SHARED ? E : 1];   // shared walk: operands of other blocks, fetched a turn ahead
                                  // (the pending pattern: not yet there)
 };
@@ -341,6 +347,9 @@ __device__ __forceinline__ void small_load(SmallTask<E, SHARED> &q, const SmallS
                                            int count, int t) {
     if (t < count) {
         t += base;
+        const int copy = SHARED ? t & ((1 << p.rshift) - 1) : 0;   // which right-hand side
+        const int copies = SHARED ? 1 << p.rshift : 1;
+        if (SHARED) t >>= p.rshift;                                // the slot whose record this is
         // two records per task, 16-byte aligned (E + 2 and E are even): 128-bit loads
         const double2 *rv = reinterpret_cast<const double2 *>(p.rec_val + (size_t)t * (E + 2));
 #pragma unroll
@@ -351,18 +360,25 @@ __device__ __forceinline__ void small_load(SmallTask<E, SHARED> &q, const SmallS
         }
         const double2 tail = __ldg(rv + E / 2);
         q.dinv = tail.y;
-        if (SHARED) q.row = __ldg(p.lay.row_of + t);
-        else q.bb = tail.x;               // one block: the right-hand side came with the record
+        if (SHARED) {
+            const int row = __ldg(p.lay.row_of + t);
+            q.row = row >= 0 ? row * p.ld + copy : -1;   // (element of b and x, not the row)
+        } else {
+            q.bb = tail.x;                // one block: the right-hand side came with the record
+        }
         if (E == 2) {
             const int2 c = __ldg(reinterpret_cast<const int2 *>(p.lay.rec_pc + (size_t)t * E));
-            q.pc[0] = c.x;
-            q.pc[1] = c.y;
+            q.pc[0] = c.x * copies + copy;   // (-1, no operand, stays negative)
+            q.pc[1] = c.y * copies + copy;
         } else {
             const int4 *rc = reinterpret_cast<const int4 *>(p.lay.rec_pc + (size_t)t * E);
 #pragma unroll
             for (int k = 0; k < E / 4; ++k) {
                 const int4 c = __ldg(rc + k);
-                q.pc[4 * k] = c.x; q.pc[4 * k + 1] = c.y; q.pc[4 * k + 2] = c.z; q.pc[4 * k + 3] = c.w;
+                q.pc[4 * k] = c.x * copies + copy;
+                q.pc[4 * k + 1] = c.y * copies + copy;
+                q.pc[4 * k + 2] = c.z * copies + copy;
+                q.pc[4 * k + 3] = c.w * copies + copy;
             }
         }
     } else {
@@ -383,12 +399,13 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
     extern __shared__ __align__(16) double ring[];  // kRing doubles
     __shared__ int s_wptr[kWptrChunk + 1];
     const int tid = threadIdx.x;
-    const bool use_ring = p.max_width <= kRing / 2;
+    const bool use_ring = p.max_width <= kRing / 2;   // (max_width counts tasks)
     constexpr bool shared_walk = SHARED;
     const int *table = p.wptr + (size_t)blockIdx.x * (p.n_levels + 1);
     // the block's first slot and how many it has (one block: all of them, known without a look)
-    const int base = SHARED ? __ldg(table) : 0;
-    const int count = SHARED ? __ldg(table + p.n_levels) - base : p.lay.n;
+    const int rshift = SHARED ? p.rshift : 0;
+    const int base = SHARED ? __ldg(table) << rshift : 0;
+    const int count = SHARED ? (__ldg(table + p.n_levels) << rshift) - base : p.lay.n;
     double *xp = p.xp + base;
     // two register sets used in turn: a set is reloaded right after its task and not touched
     // again until two turns later, so its loads have several levels to arrive
@@ -459,7 +476,7 @@ __global__ void __launch_bounds__(T, 1) sptrsv_small_kernel(const SmallSolvePara
     for (int first = 0; first < p.n_levels; first += kWptrChunk) {
         const int levels = min(kWptrChunk, p.n_levels - first);
         __syncthreads();  // the previous chunk of offsets is no longer read
-        for (int k = tid; k <= levels; k += T) s_wptr[k] = __ldg(table + first + k) - base;
+        for (int k = tid; k <= levels; k += T) s_wptr[k] = (__ldg(table + first + k) << rshift) - base;
         __syncthreads();
         for (int l = 0; l < levels; ++l) {
             const int we = s_wptr[l + 1];
@@ -629,23 +646,33 @@ extern "C" int lcd_small_plan_fill(int op, int flags, int32_t n, int64_t nnz, co
     return finish(status_dev, st, &host);
 }
 
-extern "C" int lcd_small_scratch_bytes(int32_t n_slots, int32_t entries, int64_t *bytes) {
-    if (n_slots < 0 || (entries != 2 && entries != 4 && entries != 8) || !bytes) return LCD_ERR_INVALID_ARGUMENT;
+extern "C" int lcd_small_scratch_bytes_multi(int32_t n_slots, int32_t entries, int32_t nrhs, int64_t *bytes) {
+    if (n_slots < 0 || (entries != 2 && entries != 4 && entries != 8) || !bytes || nrhs < 1 || nrhs > 16 ||
+        (nrhs & (nrhs - 1)) != 0)
+        return LCD_ERR_INVALID_ARGUMENT;
     const size_t m = (size_t)(n_slots > 0 ? n_slots : 1);
-    *bytes = (int64_t)(align256(m * (entries + 2) * 8) + align256(m * 8) + 256);
+    *bytes = (int64_t)(align256(m * (entries + 2) * 8) + align256(m * nrhs * 8) + 256);
     return LCD_OK;
 }
 
-extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *Ax,
-                                const double *b, double *x, const int32_t *rec_pc, const int32_t *rec_src,
-                                const int32_t *row_of, const int32_t *diag_src,
-                                const int32_t *slot_ptr_dev, int32_t n_levels, int32_t blocks,
-                                int32_t max_width, int32_t gather_values, void *scratch,
-                                int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms,
-                                void *stream, int *status_host) {
+extern "C" int lcd_small_scratch_bytes(int32_t n_slots, int32_t entries, int64_t *bytes) {
+    return lcd_small_scratch_bytes_multi(n_slots, entries, 1, bytes);
+}
+
+extern "C" int lcd_sptrsv_small_multi(int32_t n, int32_t n_slots, int32_t entries, const double *Ax,
+                                      const double *b, double *x, int32_t nrhs, int64_t ld,
+                                      const int32_t *rec_pc, const int32_t *rec_src,
+                                      const int32_t *row_of, const int32_t *diag_src,
+                                      const int32_t *slot_ptr_dev, int32_t n_levels, int32_t blocks,
+                                      int32_t max_width, int32_t gather_values, void *scratch,
+                                      int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms,
+                                      void *stream, int *status_host) {
     if (n < 0 || n_slots < n || n_levels < 0 || (entries != 2 && entries != 4 && entries != 8) ||
-        blocks < 1 || blocks > 1024 || !status_dev)
+        blocks < 1 || blocks > 1024 || !status_dev || nrhs < 1 || nrhs > 16 || (nrhs & (nrhs - 1)) != 0 ||
+        ld < nrhs || (nrhs > 1 && blocks == 1))
         return LCD_ERR_INVALID_ARGUMENT;
+    // tasks and elements of b and x are counted in 32-bit integers
+    if ((long long)n_slots * nrhs > 0x7fffffffll || (long long)n * ld > 0x7fffffffll) return LCD_ERR_TOO_LARGE;
     if (n == 0) {
         const int rc0 = reset_status(status_dev, (cudaStream_t)stream);
         return rc0 ? rc0 : finish(status_dev, (cudaStream_t)stream, status_host);
@@ -653,7 +680,7 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
     if (!Ax || !b || !x || x == b || !rec_pc || !rec_src || !row_of || !diag_src || !slot_ptr_dev || !scratch)
         return LCD_ERR_INVALID_ARGUMENT;
     int64_t need = 0;
-    lcd_small_scratch_bytes(n_slots, entries, &need);
+    lcd_small_scratch_bytes_multi(n_slots, entries, nrhs, &need);
     if (scratch_bytes < need) return LCD_ERR_WORKSPACE;
     if (((uintptr_t)scratch & 255) != 0 || ((uintptr_t)rec_pc & 15) != 0) return LCD_ERR_INVALID_ARGUMENT;
     cudaStream_t st = (cudaStream_t)stream;
@@ -672,12 +699,14 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
         LCD_CUDA_TRY(cudaGetLastError());
     }
     if (blocks > 1) {   // blocks poll each other's results: the value is its own ready flag
-        rc = lcd_fill_u64(reinterpret_cast<uint64_t *>(xp), n_slots, kPendingBits, st);
+        rc = lcd_fill_u64(reinterpret_cast<uint64_t *>(xp), (int64_t)n_slots * nrhs, kPendingBits, st);
         if (rc) return rc;
     }
-    // (the widest slice in slots: rounded up to whole warps)
-    const SmallSolveParams p{lay, slot_ptr_dev, n_levels, (max_width + 31) & ~31, blocks, status_dev,
-                             timeout_ns(timeout_ms), rec_val, b, x, xp, debug_trace()};
+    int rshift = 0;
+    while ((1 << rshift) < nrhs) ++rshift;
+    // (the widest slice in tasks: slots rounded up to whole warps, times the right-hand sides)
+    const SmallSolveParams p{lay, slot_ptr_dev, n_levels, ((max_width + 31) & ~31) << rshift, blocks, status_dev,
+                             timeout_ns(timeout_ms), rec_val, b, x, xp, debug_trace(), rshift, (int)ld};
     if (entries == 2) rc = launch_small_e<2>(p, st);
     else if (entries == 4) rc = launch_small_e<4>(p, st);
     else rc = launch_small_e<8>(p, st);
@@ -687,4 +716,16 @@ extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, con
         LCD_CUDA_TRY(cudaGetLastError());
     }
     return finish(status_dev, st, status_host);
+}
+
+extern "C" int lcd_sptrsv_small(int32_t n, int32_t n_slots, int32_t entries, const double *Ax,
+                                const double *b, double *x, const int32_t *rec_pc, const int32_t *rec_src,
+                                const int32_t *row_of, const int32_t *diag_src,
+                                const int32_t *slot_ptr_dev, int32_t n_levels, int32_t blocks,
+                                int32_t max_width, int32_t gather_values, void *scratch,
+                                int64_t scratch_bytes, int32_t *status_dev, int32_t timeout_ms,
+                                void *stream, int *status_host) {
+    return lcd_sptrsv_small_multi(n, n_slots, entries, Ax, b, x, 1, 1, rec_pc, rec_src, row_of, diag_src,
+                                  slot_ptr_dev, n_levels, blocks, max_width, gather_values, scratch,
+                                  scratch_bytes, status_dev, timeout_ms, stream, status_host);
 }

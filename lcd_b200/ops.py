@@ -566,10 +566,21 @@ class SmallPlan:
                                       ptr(self.diag_src), ptr(cursor), ptr(info_dev), ptr(status),
                                       _stream(), ctypes.byref(far)), "lcd_small_plan_fill")
         self.far = int(far.value)
-        need = ctypes.c_int64(0)
-        check(lib.lcd_small_scratch_bytes(self.n_slots, self.entries, ctypes.byref(need)),
-              "lcd_small_scratch_bytes")
-        self.scratch = torch.empty(need.value, dtype=torch.uint8, device=dev)
+        self.scratch, self.scratch_rhs = None, 0
+        self.scratch_for(1)
+
+    def scratch_for(self, nrhs):
+        """Scratch of the solve (coefficients in slot order, x by position) for ``nrhs``
+        right-hand sides; growing it loses the gathered coefficients."""
+        if nrhs > self.scratch_rhs:
+            need = ctypes.c_int64(0)
+            check(nat.load().lcd_small_scratch_bytes_multi(self.n_slots, self.entries, nrhs,
+                                                           ctypes.byref(need)),
+                  "lcd_small_scratch_bytes_multi")
+            self.scratch = torch.empty(need.value, dtype=torch.uint8, device=self.slot_ptr.device)
+            self.scratch_rhs = nrhs
+            self.gathered = False
+        return self.scratch
 
     @staticmethod
     def serves(n, nnz):
@@ -592,23 +603,43 @@ def sliced_blocks(n, levels, device=None):
     return int(max(1, min(count.value, n // max(levels, 1) // SLICED_ROWS_PER_SLICE)))
 
 
+SMALL_MAX_RHS = 16
+
+
 def sptrsv_small(plan, Ax, b, x=None, *, status=None, timeout_ms=0, sync=False, same_values=False):
     """Level walk of a ``SmallPlan`` (asynchronous on the current stream unless ``sync``).
+    ``b``: one right-hand side, or - for a plan with several blocks - a row-major ``n x k`` block
+    with k = 1, 2, 4, 8 or 16 (the walk then runs on k interleaved copies of the pattern).
     ``same_values``: Ax holds what the previous solve with this plan had (one matrix, many
     right-hand sides) - its coefficients are not gathered into slot order again."""
     _require(Ax, torch.float64, "Ax")
-    _require(b, torch.float64, "b")
-    x = torch.empty_like(b) if x is None else x
+    if b.dim() == 1:
+        _require(b, torch.float64, "b")
+        x = torch.empty_like(b) if x is None else x
+        nrhs, ld = 1, 1
+    else:
+        # a row-major block, or columns [c0, c1) of one (leading dimension = its row stride)
+        x = torch.empty(b.shape, dtype=b.dtype, device=b.device) if x is None else x
+        for name, t in (("b", b), ("x", x)):
+            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float64 and t.dim() == 2
+                    and t.stride(1) == 1 and t.stride(0) >= t.shape[1]):
+                raise TypeError(f"{name} must be a row-major float64 CUDA block of right-hand sides")
+        if x.shape != b.shape or x.stride() != b.stride():
+            raise ValueError("x must have the shape and leading dimension of b")
+        nrhs, ld = int(b.shape[1]), int(b.stride(0))
     status = plan.status if status is None else status
     host = ctypes.c_int(0)
-    check(nat.load().lcd_sptrsv_small(plan.n, plan.n_slots, plan.entries, ptr(Ax), ptr(b), ptr(x),
-                                      ptr(plan.rec_pc), ptr(plan.rec_src), ptr(plan.row_of),
-                                      ptr(plan.diag_src), ptr(plan.slot_ptr), plan.n_levels, plan.blocks,
-                                      plan.max_width, 0 if same_values else 1, ptr(plan.scratch),
-                                      plan.scratch.numel(),
-                                      ptr(status), int(timeout_ms), _stream(),
-                                      ctypes.byref(host) if sync else None),
-          "lcd_sptrsv_small")
+    scratch = plan.scratch_for(nrhs)
+    gather = not (same_values and plan.gathered)
+    check(nat.load().lcd_sptrsv_small_multi(plan.n, plan.n_slots, plan.entries, ptr(Ax), ptr(b), ptr(x),
+                                            nrhs, ld, ptr(plan.rec_pc), ptr(plan.rec_src),
+                                            ptr(plan.row_of), ptr(plan.diag_src), ptr(plan.slot_ptr),
+                                            plan.n_levels, plan.blocks, plan.max_width,
+                                            1 if gather else 0, ptr(scratch), scratch.numel(),
+                                            ptr(status), int(timeout_ms), _stream(),
+                                            ctypes.byref(host) if sync else None),
+          "lcd_sptrsv_small_multi")
+    plan.gathered = True
     return x
 
 

@@ -351,6 +351,41 @@ def test_level_walk_shared_by_many_blocks(cuda, oracle, op, blocks):
     np.testing.assert_allclose(x3, getattr(oracle, "sptrsv_" + op)(Ap, Ai, scaled, b), rtol=1e-10, atol=1e-12)
 
 
+@pytest.mark.parametrize("op", ["csr_lower", "csr_upper", "csc_lower"])
+def test_level_walk_with_a_block_of_right_hand_sides(cuda, oracle, op):
+    """The shared walk on k interleaved copies of the pattern: a row-major n x k block of
+    right-hand sides (k = 2, 4, 8, 16, also as a view with a larger leading dimension) gives,
+    column by column, exactly what the walk gives for that column alone."""
+    import torch
+    from lcd_b200 import _native as nat, generators as gen, ops
+    tri = gen.laplacian3d_tril(15, seed=2)
+    if op.endswith("upper"):
+        tri = gen.upper_from_lower(tri)
+    Ap, Ai, Ax = tri.csc_arrays() if op.startswith("csc") else tri.csr_arrays()
+    dAp, dAi, dAx = dev(Ap, np.int32, cuda), dev(Ai, np.int32, cuda), dev(Ax, np.float64, cuda)
+    dag = ops.dag_build(op, dAp, dAi)
+    plan = ops.SmallPlan(op, dAp, dAi, dag, blocks=7)
+    B = np.random.default_rng(8).uniform(-1, 1, (tri.n, 16))
+    dB = dev(B, np.float64, cuda)
+    alone = np.stack([host(ops.sptrsv_small(plan, dAx, dB[:, q].contiguous(), sync=True)) for q in range(16)], axis=1)
+    np.testing.assert_allclose(alone[:, 3], getattr(oracle, "sptrsv_" + op)(Ap, Ai, Ax, B[:, 3].copy()),
+                               rtol=1e-10, atol=1e-12)
+    for k in (16, 8, 4, 2):
+        X = host(ops.sptrsv_small(plan, dAx, dB[:, :k].contiguous(), sync=True, same_values=True))
+        np.testing.assert_array_equal(X, alone[:, :k])
+    # a view into a wider block: leading dimension 16, four columns
+    out = torch.zeros_like(dB)
+    ops.sptrsv_small(plan, dAx, dB[:, 4:8], out[:, 4:8], sync=True)
+    np.testing.assert_array_equal(host(out)[:, 4:8], alone[:, 4:8])
+    assert not host(out)[:, :4].any() and not host(out)[:, 8:].any()
+    with pytest.raises(ops.NativeError) as bad:          # three columns: not served
+        ops.sptrsv_small(plan, dAx, dB[:, :3].contiguous(), sync=True)
+    assert bad.value.code == nat.ERR_INVALID_ARGUMENT
+    one_block = ops.SmallPlan(op, dAp, dAi, dag)
+    with pytest.raises(ops.NativeError):                 # the one-block form takes one right-hand side
+        ops.sptrsv_small(one_block, dAx, dB[:, :2].contiguous(), sync=True)
+
+
 def test_level_walk_on_factors_random_patterns_and_bad_input(cuda, oracle):
     """Unit-lower / upper solves on ILU0 factors kept in place; a random band matrix whose
     operands reach far back and into other blocks' ranges; an order that is no level order is
