@@ -138,16 +138,28 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            self.rows.append((time.perf_counter(), [c.strip() for c in line.split(",")]))
+
+    def mark(self):
+        """The timed region starts now: samples from here on are the ones reported."""
+        self.marked = time.perf_counter()
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.15)
         self.proc.terminate()
+        marked = getattr(self, "marked", 0.0)
+        rows = [row for t, row in self.rows if t >= marked]
+        note = None
+        if not rows and self.rows:
+            # the timed region was shorter than the sampling period: the last samples of the
+            # warm-up steps (the same work, directly before) stand in
+            rows = [row for _, row in self.rows[-3:]]
+            note = "sampled during the warm-up steps directly before the timed region"
         sm, smax, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for row in self.rows:
+        for row in rows:
             try:
                 sm.append(float(row[1]))
                 smax.append(float(row[2]))
@@ -156,9 +168,12 @@ class ClockSampler:
             for name, cell in zip(names, row[5:9]):
                 if cell.lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None, "samples": len(sm),
-                "reasons": sorted(reasons)}
+        out = {"sm_mhz": float(np.median(sm)) if sm else None,
+               "sm_max_mhz": max(smax) if smax else None, "samples": len(sm),
+               "reasons": sorted(reasons)}
+        if note:
+            out["note"] = note
+        return out
 
 
 # ----------------------------------------------------------- reference arm ----
@@ -302,15 +317,18 @@ def run_native(args):
     if not residual <= 1e-12:
         raise RuntimeError(f"relative residual {residual:.3e} exceeds 1e-12")
 
+    # (the sampler is started before the warm-up steps: nvidia-smi needs a few hundred
+    # milliseconds before its first line, more than a short timed region lasts)
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier()
-    sampler = ClockSampler(local_rank)
-    if rank == 0:
-        sampler.start()
     events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     torch.cuda.synchronize()
+    sampler.mark()
     events[0].record()
     for k in range(args.steps):
         step()
