@@ -69,7 +69,7 @@ def test_decorated_solve_falls_back_to_substitution_on_graded_blocks(cuda):
     n = 40_960
     L, b, _ = graded_chain(n, seed=1)
     Ap, Ai, Ax = L.indptr.astype(np.int32), L.indices.astype(np.int32), L.data
-    for _ in range(2):                                    # second call: cached plan and verdict
+    for _ in range(2):                                    # second call: cached plan and growth figure
         x = csr_warp_syncfree(Ap, Ai, Ax, b, n)
         assert np.linalg.norm(L @ x - b) / np.linalg.norm(b) <= RESIDUAL_TOL
     tri = gen.random_band_lower(40_000, seed=2, mean_degree=15.0, band=64)   # well conditioned: chain solver
