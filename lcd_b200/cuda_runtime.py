@@ -542,7 +542,12 @@ def _zeros_like_count(count_array, length=None, device_like=None):
         import torch
         if isinstance(count_array, torch.Tensor):
             n = count_array.numel() if length is None else length
-            return torch.zeros(n, dtype=torch.int32, device=count_array.device)
+            device = count_array.device
+            if device.type == "cuda":
+                # made when a launcher reads it (the native kernels that poll operands instead
+                # of counting never do: two allocations and fills less per call)
+                return LazyDeviceArray(lambda: torch.zeros(n, dtype=torch.int32, device=device), n)
+            return torch.zeros(n, dtype=torch.int32, device=device)
     except ImportError:  # pragma: no cover
         pass
     n = len(count_array) if length is None else length
@@ -617,8 +622,17 @@ def _prepare_value(value, cuda_module):
 
 
 def _is_cuda_array(value):
-    # (a DeviceArray first: asking it for the interface would wait for an upload in flight)
-    return isinstance(value, DeviceArray) or hasattr(value, "__cuda_array_interface__")
+    # (a DeviceArray first: asking it for the interface would wait for an upload in flight;
+    # host arrays and scalars next, and a torch tensor by its own flag: torch builds the whole
+    # interface dictionary for every look at the attribute, 4 us a time)
+    if isinstance(value, DeviceArray):
+        return True
+    if value is None or isinstance(value, (np.ndarray, np.generic, int, float, list, tuple)):
+        return False
+    is_cuda = getattr(value, "is_cuda", None)
+    if isinstance(is_cuda, bool):
+        return is_cuda
+    return hasattr(value, "__cuda_array_interface__")
 
 
 def start_large_uploads(values, skip=(), together=(), late=()):
